@@ -1,0 +1,283 @@
+// Python bindings of the sm_100a kernels: tensor validation, then a launch on
+// the current CUDA stream (so every op is capturable in a CUDA graph).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "kernels/launchers.h"
+
+namespace {
+
+using torch::Tensor;
+
+#define CHECK_CUDA(t) TORCH_CHECK((t).is_cuda(), #t " must be a CUDA tensor")
+#define CHECK_DTYPE(t, d) TORCH_CHECK((t).scalar_type() == (d), #t " has dtype ", (t).scalar_type(), ", expected ", (d))
+#define CHECK_LAST_CONTIG(t) TORCH_CHECK((t).stride(-1) == 1, #t " must be contiguous in its last dimension")
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+// One int32 error word per device, zero-initialised; kernels record the first
+// failure (bounded-wait timeout, bad index) here instead of trapping.
+Tensor& error_word_ref(int device) {
+  static std::vector<Tensor> words(64);
+  if (!words[device].defined()) {
+    c10::cuda::CUDAGuard g(device);
+    words[device] = torch::zeros({1}, torch::dtype(torch::kInt32).device(torch::kCUDA, device));
+  }
+  return words[device];
+}
+int* err_ptr(const Tensor& like) { return error_word_ref(like.get_device()).data_ptr<int>(); }
+
+Tensor error_word(int64_t device) { return error_word_ref(int(device)); }
+
+template <typename T>
+T* ptr(const Tensor& t) { return reinterpret_cast<T*>(t.data_ptr()); }
+template <typename T>
+const T* cptr(const Tensor& t) { return reinterpret_cast<const T*>(t.data_ptr()); }
+
+// ------------------------------------------------------------------ GEMMs
+void fp8_gemm(const Tensor& a_q, const Tensor& a_s_t, const Tensor& w, const Tensor& w_s, Tensor& out,
+              const c10::optional<Tensor>& residual) {
+  CHECK_CUDA(a_q); CHECK_CUDA(w); CHECK_CUDA(out);
+  CHECK_DTYPE(a_q, torch::kFloat8_e4m3fn); CHECK_DTYPE(w, torch::kFloat8_e4m3fn);
+  CHECK_DTYPE(a_s_t, torch::kFloat32); CHECK_DTYPE(w_s, torch::kFloat32); CHECK_DTYPE(out, torch::kBFloat16);
+  TORCH_CHECK(a_q.dim() == 2 && w.dim() == 2 && a_q.size(1) == w.size(1), "fp8_gemm: [M,K] x [N,K]");
+  CHECK_LAST_CONTIG(a_q); CHECK_LAST_CONTIG(w); CHECK_LAST_CONTIG(out);
+  TORCH_CHECK(w_s.is_contiguous() && a_s_t.stride(1) == 1, "fp8_gemm: scale layouts");
+  const int M = a_q.size(0), N = w.size(0), K = a_q.size(1);
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "fp8_gemm: out shape");
+  TORCH_CHECK(a_s_t.size(0) == (K + 127) / 128 && a_s_t.size(1) >= M, "fp8_gemm: activation scales [K/128, >=M]");
+  TORCH_CHECK(w_s.size(0) == (N + 127) / 128 && w_s.size(1) == (K + 127) / 128, "fp8_gemm: weight scales");
+  c10::cuda::CUDAGuard g(a_q.device());
+  b200::FP8GemmArgs a{};
+  a.A = cptr<uint8_t>(a_q); a.B = cptr<uint8_t>(w); a.sfa = cptr<float>(a_s_t); a.sfb = cptr<float>(w_s);
+  a.out = ptr<__nv_bfloat16>(out);
+  a.residual = nullptr; a.ldr = 0;
+  if (residual && residual->defined()) {
+    CHECK_DTYPE((*residual), torch::kBFloat16);
+    TORCH_CHECK(residual->size(0) == M && residual->size(1) == N && residual->stride(1) == 1, "fp8_gemm: residual");
+    a.residual = cptr<__nv_bfloat16>(*residual); a.ldr = residual->stride(0);
+  }
+  a.M = M; a.N = N; a.K = K; a.lda = a_q.stride(0); a.ldb = w.stride(0);
+  a.lda_s = a_s_t.stride(0); a.ldo = out.stride(0); a.err = err_ptr(a_q);
+  b200::launch_fp8_gemm(a, stream());
+}
+
+// out_g[m, n] = sum_k A_g[m, k] * B_g[n, k]; strides in elements.
+void bf16_gemm(const Tensor& A, int64_t a_off, int64_t lda, int64_t a_batch, const Tensor& B, int64_t b_off,
+               int64_t ldb, int64_t b_batch, Tensor& out, int64_t o_off, int64_t ldo, int64_t o_batch,
+               int64_t M, int64_t N, int64_t K, int64_t batch) {
+  CHECK_CUDA(A); CHECK_CUDA(B); CHECK_CUDA(out);
+  CHECK_DTYPE(A, torch::kBFloat16); CHECK_DTYPE(B, torch::kBFloat16);
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 || out.scalar_type() == torch::kFloat32, "bf16_gemm: out dtype");
+  auto span_ok = [](const Tensor& t, int64_t off, int64_t rows, int64_t ld, int64_t bs, int64_t nb, int64_t cols) {
+    const int64_t last = off + (nb - 1) * bs + (rows - 1) * ld + cols;
+    return off >= 0 && last <= t.numel() && t.is_contiguous();
+  };
+  TORCH_CHECK(span_ok(A, a_off, M, lda, a_batch, batch, K), "bf16_gemm: A view out of bounds");
+  TORCH_CHECK(span_ok(B, b_off, N, ldb, b_batch, batch, K), "bf16_gemm: B view out of bounds");
+  TORCH_CHECK(span_ok(out, o_off, M, ldo, o_batch, batch, N), "bf16_gemm: out view out of bounds");
+  c10::cuda::CUDAGuard g(A.device());
+  b200::BF16GemmArgs a{};
+  a.A = cptr<__nv_bfloat16>(A) + a_off; a.B = cptr<__nv_bfloat16>(B) + b_off;
+  const bool f32 = out.scalar_type() == torch::kFloat32;
+  a.out = f32 ? static_cast<void*>(ptr<float>(out) + o_off) : static_cast<void*>(ptr<__nv_bfloat16>(out) + o_off);
+  a.out_fp32 = f32; a.M = M; a.N = N; a.K = K; a.batch = batch;
+  a.lda = lda; a.a_batch = a_batch; a.ldb = ldb; a.b_batch = b_batch; a.ldo = ldo; a.o_batch = o_batch;
+  a.err = err_ptr(A);
+  b200::launch_bf16_gemm(a, stream());
+}
+
+// ------------------------------------------------------------- elementwise
+void rms_norm(const Tensor& x, const c10::optional<Tensor>& residual, const Tensor& weight, double eps,
+              const c10::optional<Tensor>& out, const c10::optional<Tensor>& out_sum,
+              const c10::optional<Tensor>& q, const c10::optional<Tensor>& sfa_t) {
+  CHECK_CUDA(x); CHECK_DTYPE(x, torch::kBFloat16); CHECK_DTYPE(weight, torch::kFloat32);
+  CHECK_LAST_CONTIG(x);
+  TORCH_CHECK(x.dim() == 2 && weight.numel() == x.size(1) && weight.is_contiguous(), "rms_norm shapes");
+  c10::cuda::CUDAGuard g(x.device());
+  b200::NormArgs a{};
+  a.x = cptr<__nv_bfloat16>(x); a.ldx = x.stride(0); a.weight = cptr<float>(weight);
+  a.rows = x.size(0); a.D = x.size(1); a.eps = float(eps);
+  if (residual && residual->defined()) {
+    TORCH_CHECK(out_sum && out_sum->defined(), "rms_norm: residual needs out_sum");
+    a.residual = cptr<__nv_bfloat16>(*residual); a.ldr = residual->stride(0);
+    a.out_sum = ptr<__nv_bfloat16>(*out_sum); a.lds = out_sum->stride(0);
+  }
+  if (out && out->defined()) { a.out = ptr<__nv_bfloat16>(*out); a.ldo = out->stride(0); }
+  if (q && q->defined()) {
+    CHECK_DTYPE((*q), torch::kFloat8_e4m3fn);
+    TORCH_CHECK(sfa_t && sfa_t->defined() && sfa_t->size(0) == x.size(1) / 128 && sfa_t->size(1) >= x.size(0), "rms_norm: sfa_t");
+    a.q = ptr<uint8_t>(*q); a.ldq = q->stride(0); a.sfa_t = ptr<float>(*sfa_t); a.lda_s = sfa_t->stride(0);
+  }
+  b200::launch_rms_norm(a, stream());
+}
+
+void quant_act(const Tensor& x, Tensor& q, Tensor& sfa_t) {
+  CHECK_CUDA(x); CHECK_DTYPE(x, torch::kBFloat16); CHECK_DTYPE(q, torch::kFloat8_e4m3fn); CHECK_DTYPE(sfa_t, torch::kFloat32);
+  CHECK_LAST_CONTIG(x); CHECK_LAST_CONTIG(q);
+  TORCH_CHECK(sfa_t.size(0) == x.size(1) / 128 && sfa_t.size(1) >= x.size(0) && sfa_t.stride(1) == 1, "quant_act: sfa_t");
+  c10::cuda::CUDAGuard g(x.device());
+  b200::launch_quant_act(cptr<__nv_bfloat16>(x), x.stride(0), x.size(0), x.size(1), ptr<uint8_t>(q), q.stride(0),
+                         ptr<float>(sfa_t), sfa_t.stride(0), stream());
+}
+
+void silu_mul_quant(const Tensor& packed, const c10::optional<Tensor>& h, const c10::optional<Tensor>& q,
+                    const c10::optional<Tensor>& sfa_t) {
+  CHECK_CUDA(packed); CHECK_DTYPE(packed, torch::kBFloat16); CHECK_LAST_CONTIG(packed);
+  const int rows = packed.size(0), I = packed.size(1) / 2;
+  c10::cuda::CUDAGuard g(packed.device());
+  __nv_bfloat16* hp = nullptr;
+  if (h && h->defined()) { TORCH_CHECK(h->is_contiguous() && h->size(1) == I, "silu: h"); hp = ptr<__nv_bfloat16>(*h); }
+  uint8_t* qp = nullptr; float* sp = nullptr; int lda_s = 0;
+  if (q && q->defined()) {
+    TORCH_CHECK(q->is_contiguous() && q->size(1) == I && sfa_t && sfa_t->defined(), "silu: q");
+    qp = ptr<uint8_t>(*q); sp = ptr<float>(*sfa_t); lda_s = sfa_t->stride(0);
+  }
+  b200::launch_silu_mul_quant(cptr<__nv_bfloat16>(packed), packed.stride(0), rows, I, hp, qp, sp, lda_s, stream());
+}
+
+void mla_q_rope(const Tensor& q, int64_t ldq, int64_t T, int64_t H, int64_t nope, int64_t rope, const Tensor& freqs,
+                const Tensor& positions, Tensor& out, int64_t ldo_tok, int64_t ldo_head, int64_t out_offset) {
+  CHECK_CUDA(q); CHECK_DTYPE(q, torch::kBFloat16); CHECK_DTYPE(out, torch::kBFloat16);
+  c10::cuda::CUDAGuard g(q.device());
+  b200::launch_mla_q_rope(cptr<__nv_bfloat16>(q), ldq, T, H, nope, rope, cptr<float>(freqs), cptr<float>(positions),
+                          ptr<__nv_bfloat16>(out), ldo_tok, ldo_head, out_offset, stream());
+}
+
+void kv_finish(const Tensor& kv, int64_t L, int64_t R, const Tensor& norm_w, double eps, const Tensor& freqs,
+               const Tensor& positions, Tensor& out, const c10::optional<Tensor>& dst_row) {
+  CHECK_CUDA(kv); CHECK_DTYPE(kv, torch::kBFloat16); CHECK_DTYPE(out, torch::kBFloat16); CHECK_LAST_CONTIG(kv);
+  c10::cuda::CUDAGuard g(kv.device());
+  const int64_t* dr = nullptr;
+  if (dst_row && dst_row->defined()) { CHECK_DTYPE((*dst_row), torch::kInt64); dr = cptr<int64_t>(*dst_row); }
+  b200::launch_kv_finish(cptr<__nv_bfloat16>(kv), kv.stride(0), kv.size(0), L, R, cptr<float>(norm_w), float(eps),
+                         cptr<float>(freqs), cptr<float>(positions), ptr<__nv_bfloat16>(out), out.stride(0), dr, stream());
+}
+
+void index_k(const Tensor& k, int64_t R, const Tensor& ln_w, const Tensor& ln_b, double eps, const Tensor& freqs,
+             const Tensor& positions, Tensor& k_q, Tensor& k_scale) {
+  CHECK_CUDA(k); CHECK_DTYPE(k, torch::kBFloat16); CHECK_DTYPE(k_q, torch::kFloat8_e4m3fn); CHECK_LAST_CONTIG(k);
+  c10::cuda::CUDAGuard g(k.device());
+  b200::launch_index_k(cptr<__nv_bfloat16>(k), k.stride(0), k.size(0), k.size(1), R, cptr<float>(ln_w), cptr<float>(ln_b),
+                       float(eps), cptr<float>(freqs), cptr<float>(positions), ptr<uint8_t>(k_q), ptr<float>(k_scale), stream());
+}
+
+void index_q(const Tensor& q, int64_t ldq, int64_t T, int64_t H, int64_t D, int64_t R, const Tensor& freqs,
+             const Tensor& positions, Tensor& q_q, Tensor& q_scale, const Tensor& w_raw, double head_scale,
+             Tensor& weights) {
+  CHECK_CUDA(q); CHECK_DTYPE(q, torch::kBFloat16); CHECK_DTYPE(q_q, torch::kFloat8_e4m3fn);
+  c10::cuda::CUDAGuard g(q.device());
+  b200::launch_index_q(cptr<__nv_bfloat16>(q), ldq, T, H, D, R, cptr<float>(freqs), cptr<float>(positions),
+                       ptr<uint8_t>(q_q), ptr<float>(q_scale), cptr<float>(w_raw), float(head_scale),
+                       ptr<float>(weights), stream());
+}
+
+void linear_f32(const Tensor& x, const Tensor& W, Tensor& out) {
+  CHECK_CUDA(x); CHECK_DTYPE(x, torch::kBFloat16); CHECK_DTYPE(W, torch::kFloat32); CHECK_DTYPE(out, torch::kFloat32);
+  CHECK_LAST_CONTIG(x); TORCH_CHECK(W.is_contiguous() && out.is_contiguous(), "linear_f32 layout");
+  c10::cuda::CUDAGuard g(x.device());
+  b200::launch_linear_f32(cptr<__nv_bfloat16>(x), x.stride(0), cptr<float>(W), x.size(0), W.size(0), W.size(1),
+                          ptr<float>(out), stream());
+}
+
+void embed(const Tensor& ids, const Tensor& table, Tensor& out) {
+  CHECK_CUDA(ids); CHECK_DTYPE(ids, torch::kInt64); CHECK_DTYPE(table, torch::kBFloat16); CHECK_DTYPE(out, torch::kBFloat16);
+  TORCH_CHECK(table.is_contiguous() && out.is_contiguous() && ids.is_contiguous(), "embed layout");
+  c10::cuda::CUDAGuard g(ids.device());
+  b200::launch_embed(cptr<int64_t>(ids), ids.numel(), cptr<__nv_bfloat16>(table), table.size(0), table.size(1),
+                     ptr<__nv_bfloat16>(out), err_ptr(ids), stream());
+}
+
+// ------------------------------------------------------------- indexer
+void indexer_logits(const Tensor& q, const Tensor& k, const Tensor& w, const Tensor& kscale, Tensor& logits,
+                    int64_t query_start) {
+  CHECK_CUDA(q); CHECK_DTYPE(q, torch::kFloat8_e4m3fn); CHECK_DTYPE(k, torch::kFloat8_e4m3fn);
+  CHECK_DTYPE(w, torch::kFloat32); CHECK_DTYPE(kscale, torch::kFloat32); CHECK_DTYPE(logits, torch::kFloat32);
+  TORCH_CHECK(q.dim() == 3 && q.size(1) == 64 && q.size(2) == 128 && q.is_contiguous(), "indexer: q [Q,64,128]");
+  TORCH_CHECK(k.dim() == 2 && k.size(1) == 128 && k.is_contiguous(), "indexer: k [N,128]");
+  TORCH_CHECK(w.is_contiguous() && w.size(0) == q.size(0) && w.size(1) == 64, "indexer: w [Q,64]");
+  TORCH_CHECK(kscale.numel() >= k.size(0), "indexer: kscale");
+  TORCH_CHECK(logits.size(0) >= q.size(0) && logits.size(1) >= k.size(0) && logits.stride(1) == 1, "indexer: logits");
+  TORCH_CHECK(query_start >= 0 && query_start + q.size(0) <= k.size(0), "indexer: query_start");
+  c10::cuda::CUDAGuard g(q.device());
+  b200::IndexerArgs a{};
+  a.q = cptr<uint8_t>(q); a.k = cptr<uint8_t>(k); a.w = cptr<float>(w); a.kscale = cptr<float>(kscale);
+  a.logits = ptr<float>(logits); a.ldl = logits.stride(0); a.Q = q.size(0); a.N = k.size(0);
+  a.query_start = query_start; a.n_cols = logits.size(1); a.err = err_ptr(q);
+  b200::launch_indexer_logits(a, stream());
+}
+
+void topk(const Tensor& scores, int64_t N, int64_t k, int64_t causal_start, Tensor& values, Tensor& ids) {
+  CHECK_CUDA(scores); CHECK_DTYPE(scores, torch::kFloat32); CHECK_DTYPE(values, torch::kFloat32);
+  CHECK_DTYPE(ids, torch::kInt32); CHECK_LAST_CONTIG(scores);
+  TORCH_CHECK(values.is_contiguous() && ids.is_contiguous() && values.size(1) == k && ids.size(1) == k, "topk outputs");
+  TORCH_CHECK(N <= scores.size(1), "topk: N exceeds scores width");
+  c10::cuda::CUDAGuard g(scores.device());
+  b200::launch_topk_causal(cptr<float>(scores), scores.stride(0), scores.size(0), N, k, causal_start,
+                           ptr<float>(values), ptr<int>(ids), stream());
+}
+
+// ------------------------------------------------------------- attention
+void sparse_mla(const Tensor& q, const Tensor& kv, const Tensor& ids, double scale, Tensor& out,
+                const c10::optional<Tensor>& lse, int64_t splits, const c10::optional<Tensor>& scratch) {
+  CHECK_CUDA(q); CHECK_DTYPE(q, torch::kBFloat16); CHECK_DTYPE(kv, torch::kBFloat16); CHECK_DTYPE(ids, torch::kInt32);
+  CHECK_DTYPE(out, torch::kBFloat16);
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 576 && q.is_contiguous(), "sparse_mla: q [T,H,576]");
+  TORCH_CHECK(kv.dim() == 2 && kv.size(1) == 576 && kv.is_contiguous(), "sparse_mla: kv [P,576]");
+  TORCH_CHECK(ids.dim() == 2 && ids.size(0) == q.size(0) && ids.is_contiguous(), "sparse_mla: ids [T,K]");
+  TORCH_CHECK(out.is_contiguous() && out.size(0) == q.size(0) && out.size(1) == q.size(1) && out.size(2) == 512, "sparse_mla: out");
+  c10::cuda::CUDAGuard g(q.device());
+  b200::MLAArgs a{};
+  a.q = cptr<__nv_bfloat16>(q); a.kv = cptr<__nv_bfloat16>(kv); a.ids = cptr<int>(ids);
+  a.out = ptr<__nv_bfloat16>(out); a.lse = (lse && lse->defined()) ? ptr<float>(*lse) : nullptr;
+  a.T = q.size(0); a.H = q.size(1); a.K = ids.size(1); a.P = kv.size(0); a.scale = float(scale); a.err = err_ptr(q);
+  float* sp = nullptr;
+  if (splits > 1) {
+    TORCH_CHECK(scratch && scratch->defined() && scratch->scalar_type() == torch::kFloat32, "sparse_mla: scratch");
+    TORCH_CHECK(size_t(scratch->numel()) * 4 >= b200::sparse_mla_scratch_bytes(a.T, a.H, splits), "sparse_mla: scratch too small");
+    sp = ptr<float>(*scratch);
+  }
+  b200::launch_sparse_mla_split(a, int(splits), sp, stream());
+}
+
+int64_t sparse_mla_scratch_bytes(int64_t T, int64_t H, int64_t splits) {
+  return int64_t(b200::sparse_mla_scratch_bytes(T, H, splits));
+}
+
+// ------------------------------------------------------------ transfer
+void gather_rows(const Tensor& host, Tensor& records, const Tensor& host_ids, const Tensor& slots, int64_t n,
+                 const c10::optional<Tensor>& device_count) {
+  TORCH_CHECK(host.is_pinned(), "gather_rows: host must be pinned");
+  CHECK_CUDA(records); CHECK_DTYPE(host_ids, torch::kInt64); CHECK_DTYPE(slots, torch::kInt64);
+  TORCH_CHECK(host.is_contiguous() && records.is_contiguous() && host.stride(0) * host.element_size() == records.stride(0) * records.element_size(),
+              "gather_rows: matching contiguous rows");
+  c10::cuda::CUDAGuard g(records.device());
+  const int row_bytes = records.stride(0) * records.element_size();
+  b200::launch_gather_rows(cptr<uint8_t>(host), ptr<uint8_t>(records), cptr<int64_t>(host_ids), cptr<int64_t>(slots),
+                           int(n), (device_count && device_count->defined()) ? cptr<int>(*device_count) : nullptr,
+                           row_bytes, host.size(0), records.size(0), err_ptr(records), stream());
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels of the B200 DeepSeek-V3.2 DSA framework";
+  m.def("error_word", &error_word);
+  m.def("fp8_gemm", &fp8_gemm);
+  m.def("bf16_gemm", &bf16_gemm);
+  m.def("rms_norm", &rms_norm);
+  m.def("quant_act", &quant_act);
+  m.def("silu_mul_quant", &silu_mul_quant);
+  m.def("mla_q_rope", &mla_q_rope);
+  m.def("kv_finish", &kv_finish);
+  m.def("index_k", &index_k);
+  m.def("index_q", &index_q);
+  m.def("linear_f32", &linear_f32);
+  m.def("embed", &embed);
+  m.def("indexer_logits", &indexer_logits);
+  m.def("topk", &topk);
+  m.def("sparse_mla", &sparse_mla);
+  m.def("sparse_mla_scratch_bytes", &sparse_mla_scratch_bytes);
+  m.def("gather_rows", &gather_rows);
+}

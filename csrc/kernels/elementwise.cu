@@ -1,0 +1,483 @@
+// Memory-bound sm_100a kernels: RMSNorm (+residual, +fused FP8 quantisation),
+// 1x128 activation quantisation, SiLU*up (+quant), the MLA / indexer RoPE and
+// quantisation epilogues, the FP32 indexer head-weight projection and the
+// embedding gather.  Rows are processed with 16-byte vector accesses; all
+// reductions are FP32.
+//
+// Reference math: models/deepseek_v32/nonmatrix.py:21-93 (norms, SiLU),
+// models/deepseek_v32/projections.py:182-257 (projection epilogues),
+// operators/deepseek_v32/indexer/quantization.py:12-24 (UE8M0 quantisation),
+// operators/deepseek_v32/linear/fp8.py:63-70 (1x128 activation scales).
+#include "../common/ptx.cuh"
+#include "launchers.h"
+
+namespace b200 {
+namespace {
+
+constexpr float kFp8Max = 448.f;
+
+// Round a positive finite FP32 scale up to a power of two by clearing the
+// mantissa after adding (2^23 - 1): the exponent-only (UE8M0) convention.
+__device__ __forceinline__ float ue8m0_ceil(float s) {
+  const uint32_t bits = __float_as_uint(s);
+  if (bits >= 0x7F800000u) return s;  // inf / nan pass through
+  return __uint_as_float((bits + 0x007FFFFFu) & 0x7F800000u);
+}
+
+__device__ __forceinline__ uint8_t to_e4m3(float v) {
+  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+}
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) t += red[i];
+  return t;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Quantise 128 values held as 4 per lane across one warp (lane owns
+// elements [4*lane, 4*lane+4)).  Returns the scale.
+__device__ __forceinline__ float quant_group_warp(const float (&v)[4], uint8_t* dst) {
+  float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+  amax = fmaxf(warp_max(amax), 1e-4f);
+  const float scale = ue8m0_ceil(__fdiv_rn(amax, kFp8Max));
+  const float inv = __frcp_rn(scale);  // exact: scale is a power of two
+  uint32_t packed = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float x = fminf(fmaxf(v[i] * inv, -kFp8Max), kFp8Max);
+    packed |= static_cast<uint32_t>(to_e4m3(x)) << (8 * i);
+  }
+  reinterpret_cast<uint32_t*>(dst)[threadIdx.x % 32] = packed;
+  return scale;
+}
+
+// ------------------------------------------------------------------ RMSNorm
+// One CTA of 256 threads per row; each thread handles 8-element chunks.
+constexpr int kNormThreads = 256;
+constexpr int kNormMaxChunks = 4;  // D <= 256 * 8 * 4 = 8192
+
+__global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(NormArgs a) {
+  __shared__ float red[kNormThreads / 32];
+  __shared__ alignas(16) __nv_bfloat16 srow[8192];
+  const int row = blockIdx.x;
+  const __nv_bfloat16* x = a.x + row * a.ldx;
+  const __nv_bfloat16* r = a.residual ? a.residual + row * a.ldr : nullptr;
+  const int nchunk = a.D / 8;
+  float v[kNormMaxChunks][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kNormMaxChunks; ++c) {
+    const int idx = threadIdx.x + c * kNormThreads;
+    if (idx < nchunk) {
+      uint4 xv = *reinterpret_cast<const uint4*>(x + idx * 8);
+      const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        v[c][2 * t] = bf16_lo(xw[t]);
+        v[c][2 * t + 1] = bf16_hi(xw[t]);
+      }
+      if (r) {
+        uint4 rv = *reinterpret_cast<const uint4*>(r + idx * 8);
+        const uint32_t* rw = reinterpret_cast<const uint32_t*>(&rv);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          v[c][2 * t] += bf16_lo(rw[t]);
+          v[c][2 * t + 1] += bf16_hi(rw[t]);
+        }
+        uint4 sv;
+        uint32_t* sw = reinterpret_cast<uint32_t*>(&sv);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) sw[t] = pack_bf16(v[c][2 * t], v[c][2 * t + 1]);
+        *reinterpret_cast<uint4*>(a.out_sum + row * a.lds + idx * 8) = sv;
+      }
+#pragma unroll
+      for (int t = 0; t < 8; ++t) ss += v[c][t] * v[c][t];
+    }
+  }
+  const float total = block_sum<kNormThreads>(ss, red);
+  const float inv = rsqrtf(total / a.D + a.eps);
+#pragma unroll
+  for (int c = 0; c < kNormMaxChunks; ++c) {
+    const int idx = threadIdx.x + c * kNormThreads;
+    if (idx < nchunk) {
+      const float4 w0 = *reinterpret_cast<const float4*>(a.weight + idx * 8);
+      const float4 w1 = *reinterpret_cast<const float4*>(a.weight + idx * 8 + 4);
+      const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      uint4 ov;
+      uint32_t* ow = reinterpret_cast<uint32_t*>(&ov);
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        ow[t] = pack_bf16(v[c][2 * t] * inv * w[2 * t], v[c][2 * t + 1] * inv * w[2 * t + 1]);
+      if (a.out) *reinterpret_cast<uint4*>(a.out + row * a.ldo + idx * 8) = ov;
+      if (a.q) *reinterpret_cast<uint4*>(srow + idx * 8) = ov;
+    }
+  }
+  if (a.q) {
+    __syncthreads();
+    // 1x128 groups: one warp per group, 4 elements per lane.
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    for (int g = warp; g < a.D / 128; g += kNormThreads / 32) {
+      const __nv_bfloat16* src = srow + g * 128 + lane * 4;
+      float f[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) f[t] = __bfloat162float(src[t]);
+      const float sc = quant_group_warp(f, a.q + row * a.ldq + g * 128);
+      if (lane == 0) a.sfa_t[static_cast<int64_t>(g) * a.lda_s + row] = sc;
+    }
+  }
+}
+
+// ----------------------------------------------------------- quant_act
+// One warp per 128-wide group.
+__global__ void quant_act_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int rows,
+                                 int D, uint8_t* __restrict__ q, int64_t ldq,
+                                 float* __restrict__ sfa_t, int lda_s) {
+  const int groups = D / 128;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (gw >= rows * groups) return;
+  const int row = gw / groups, g = gw % groups;
+  const __nv_bfloat16* src = x + row * ldx + g * 128 + lane * 4;
+  const uint2 raw = *reinterpret_cast<const uint2*>(src);
+  float f[4] = {bf16_lo(raw.x), bf16_hi(raw.x), bf16_lo(raw.y), bf16_hi(raw.y)};
+  const float sc = quant_group_warp(f, q + row * ldq + g * 128);
+  if (lane == 0) sfa_t[static_cast<int64_t>(g) * lda_s + row] = sc;
+}
+
+// ------------------------------------------------------------ silu * up
+__global__ void silu_mul_quant_kernel(const __nv_bfloat16* __restrict__ packed, int64_t ldp,
+                                      int rows, int I, __nv_bfloat16* __restrict__ h,
+                                      uint8_t* __restrict__ q, float* __restrict__ sfa_t,
+                                      int lda_s) {
+  const int groups = I / 128;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (gw >= rows * groups) return;
+  const int row = gw / groups, g = gw % groups;
+  const __nv_bfloat16* gp = packed + row * ldp + g * 128 + lane * 4;
+  const __nv_bfloat16* up = gp + I;
+  const uint2 gr = *reinterpret_cast<const uint2*>(gp);
+  const uint2 ur = *reinterpret_cast<const uint2*>(up);
+  const float gv[4] = {bf16_lo(gr.x), bf16_hi(gr.x), bf16_lo(gr.y), bf16_hi(gr.y)};
+  const float uv[4] = {bf16_lo(ur.x), bf16_hi(ur.x), bf16_lo(ur.y), bf16_hi(ur.y)};
+  float f[4];
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const float s = gv[t] / (1.f + __expf(-gv[t]));
+    f[t] = __bfloat162float(__float2bfloat16_rn(s * uv[t]));
+  }
+  if (h) {
+    uint2 o;
+    o.x = pack_bf16(f[0], f[1]);
+    o.y = pack_bf16(f[2], f[3]);
+    *reinterpret_cast<uint2*>(h + static_cast<int64_t>(row) * I + g * 128 + lane * 4) = o;
+  }
+  if (q) {
+    const float sc = quant_group_warp(f, q + static_cast<int64_t>(row) * I + g * 128);
+    if (lane == 0) sfa_t[static_cast<int64_t>(g) * lda_s + row] = sc;
+  }
+}
+
+// ----------------------------------------------------------------- RoPE
+__device__ __forceinline__ void rope_angle(const float* freqs, const float* positions, int t, int i,
+                                           float& c, float& s) {
+  const float ang = positions[t] * freqs[i];
+  sincosf(ang, &s, &c);
+}
+
+// One thread per (t, h, pair).  Interleaved pairs (2i, 2i+1).
+__global__ void mla_q_rope_kernel(const __nv_bfloat16* __restrict__ q, int64_t ldq, int T, int H,
+                                  int nope, int rope, const float* __restrict__ freqs,
+                                  const float* __restrict__ positions,
+                                  __nv_bfloat16* __restrict__ out, int64_t ldo_tok,
+                                  int64_t ldo_head, int out_offset) {
+  const int half = rope / 2;
+  const int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
+  if (idx >= int64_t(T) * H * half) return;
+  const int i = idx % half;
+  const int h = (idx / half) % H;
+  const int t = idx / (int64_t(half) * H);
+  const __nv_bfloat16* src = q + t * ldq + int64_t(h) * (nope + rope) + nope;
+  const float a = __bfloat162float(src[2 * i]);
+  const float b = __bfloat162float(src[2 * i + 1]);
+  float c, s;
+  rope_angle(freqs, positions, t, i, c, s);
+  __nv_bfloat16* dst = out + t * ldo_tok + h * ldo_head + out_offset;
+  dst[2 * i] = __float2bfloat16_rn(a * c - b * s);
+  dst[2 * i + 1] = __float2bfloat16_rn(b * c + a * s);
+}
+
+// One CTA (128 threads) per token: RMSNorm of the latent, interleaved RoPE of k_pe.
+__global__ void kv_finish_kernel(const __nv_bfloat16* __restrict__ kv, int64_t ldkv, int T, int L,
+                                 int R, const float* __restrict__ norm_w, float eps,
+                                 const float* __restrict__ freqs,
+                                 const float* __restrict__ positions,
+                                 __nv_bfloat16* __restrict__ out, int64_t ldo,
+                                 const int64_t* __restrict__ dst_row) {
+  __shared__ float red[4];
+  const int t = blockIdx.x;
+  const __nv_bfloat16* src = kv + t * ldkv;
+  __nv_bfloat16* dst = out + (dst_row ? dst_row[t] : int64_t(t)) * ldo;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < L; i += blockDim.x) {
+    const float v = __bfloat162float(src[i]);
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < blockDim.x / 32; ++i) tot += red[i];
+  const float inv = rsqrtf(tot / L + eps);
+  for (int i = threadIdx.x; i < L; i += blockDim.x)
+    dst[i] = __float2bfloat16_rn(__bfloat162float(src[i]) * inv * norm_w[i]);
+  for (int i = threadIdx.x; i < R / 2; i += blockDim.x) {
+    const float a = __bfloat162float(src[L + 2 * i]);
+    const float b = __bfloat162float(src[L + 2 * i + 1]);
+    float c, s;
+    rope_angle(freqs, positions, t, i, c, s);
+    dst[L + 2 * i] = __float2bfloat16_rn(a * c - b * s);
+    dst[L + 2 * i + 1] = __float2bfloat16_rn(b * c + a * s);
+  }
+}
+
+// One warp per token (D = 128: 4 elements per lane).
+__global__ void index_k_kernel(const __nv_bfloat16* __restrict__ k, int64_t ldk, int T, int D,
+                               int R, const float* __restrict__ ln_w,
+                               const float* __restrict__ ln_b, float eps,
+                               const float* __restrict__ freqs,
+                               const float* __restrict__ positions, uint8_t* __restrict__ k_q,
+                               float* __restrict__ k_scale) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (t >= T) return;
+  __shared__ float buf[8][128];
+  float* row = buf[threadIdx.x / 32];
+  const __nv_bfloat16* src = k + t * ldk;
+  float v[4];
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    v[j] = __bfloat162float(src[lane * 4 + j]);
+    sum += v[j];
+  }
+  const float mean = warp_sum(sum) / D;
+  float var = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) var += (v[j] - mean) * (v[j] - mean);
+  var = warp_sum(var) / D;
+  const float inv = rsqrtf(var + eps);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = lane * 4 + j;
+    row[c] = __bfloat162float(__float2bfloat16_rn((v[j] - mean) * inv * ln_w[c] + ln_b[c]));
+  }
+  __syncwarp();
+  // split-half RoPE on [0, R): pair (i, i + R/2)
+  float out[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = lane * 4 + j;
+    if (c < R) {
+      const int half = R / 2;
+      const int i = c < half ? c : c - half;
+      float cs, sn;
+      rope_angle(freqs, positions, t, i, cs, sn);
+      const float a = row[i], b = row[i + half];
+      out[j] = c < half ? a * cs - b * sn : b * cs + a * sn;
+      out[j] = __bfloat162float(__float2bfloat16_rn(out[j]));
+    } else {
+      out[j] = row[c];
+    }
+  }
+  const float sc = quant_group_warp(out, k_q + int64_t(t) * D);
+  if (lane == 0) k_scale[t] = sc;
+}
+
+// One warp per (t, h).
+__global__ void index_q_kernel(const __nv_bfloat16* __restrict__ q, int64_t ldq, int T, int H,
+                               int D, int R, const float* __restrict__ freqs,
+                               const float* __restrict__ positions, uint8_t* __restrict__ q_q,
+                               float* __restrict__ q_scale, const float* __restrict__ w_raw,
+                               float head_scale, float* __restrict__ weights) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (gw >= T * H) return;
+  const int t = gw / H, h = gw % H;
+  const __nv_bfloat16* src = q + t * ldq + int64_t(h) * D;
+  const int half = R / 2;
+  float out[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = lane * 4 + j;
+    if (c < R) {
+      const int i = c < half ? c : c - half;
+      float cs, sn;
+      rope_angle(freqs, positions, t, i, cs, sn);
+      const float a = __bfloat162float(src[i]), b = __bfloat162float(src[i + half]);
+      out[j] = __bfloat162float(__float2bfloat16_rn(c < half ? a * cs - b * sn : b * cs + a * sn));
+    } else {
+      out[j] = __bfloat162float(src[c]);
+    }
+  }
+  const float sc = quant_group_warp(out, q_q + (int64_t(t) * H + h) * D);
+  if (lane == 0) {
+    q_scale[t * H + h] = sc;
+    weights[t * H + h] = w_raw[t * H + h] * head_scale * sc;
+  }
+}
+
+// ------------------------------------------------- FP32 head-weight linear
+// out[t, h] = sum_k x[t, k] * W[h, k]; tile 16 tokens x 64 heads, K chunks of 64.
+__global__ void __launch_bounds__(256) linear_f32_kernel(const __nv_bfloat16* __restrict__ x,
+                                                         int64_t ldx, const float* __restrict__ W,
+                                                         int T, int H, int K,
+                                                         float* __restrict__ out) {
+  __shared__ float xs[16][65];
+  __shared__ float ws[64][65];
+  const int t0 = blockIdx.x * 16, h0 = blockIdx.y * 64;
+  const int tx = threadIdx.x % 64, ty = threadIdx.x / 64;  // ty in [0,4)
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k0 = 0; k0 < K; k0 += 64) {
+    for (int i = threadIdx.x; i < 16 * 64; i += 256) {
+      const int r = i / 64, c = i % 64;
+      xs[r][c] = (t0 + r < T && k0 + c < K) ? __bfloat162float(x[(t0 + r) * ldx + k0 + c]) : 0.f;
+    }
+    for (int i = threadIdx.x; i < 64 * 64; i += 256) {
+      const int r = i / 64, c = i % 64;
+      ws[r][c] = (h0 + r < H && k0 + c < K) ? W[int64_t(h0 + r) * K + k0 + c] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int c = 0; c < 64; ++c) {
+      const float wv = ws[tx][c];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] = fmaf(xs[ty * 4 + j][c], wv, acc[j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int t = t0 + ty * 4 + j, h = h0 + tx;
+    if (t < T && h < H) out[int64_t(t) * H + h] = acc[j];
+  }
+}
+
+// ----------------------------------------------------------------- embed
+__global__ void embed_kernel(const int64_t* __restrict__ ids, int T,
+                             const __nv_bfloat16* __restrict__ table, int64_t vocab, int D,
+                             __nv_bfloat16* __restrict__ out, int* err) {
+  const int t = blockIdx.x;
+  int64_t id = ids[t];
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0) record_error(err, kErrBadIndex);
+    id = 0;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(table + id * D);
+  uint4* dst = reinterpret_cast<uint4*>(out + int64_t(t) * D);
+  for (int i = threadIdx.x; i < D / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+}  // namespace
+
+void launch_rms_norm(const NormArgs& a, cudaStream_t stream) {
+  if (a.rows <= 0) return;
+  if (a.D % 128 || a.D > 8192) throw std::invalid_argument("rms_norm: D must be a multiple of 128 and <= 8192");
+  rms_norm_kernel<<<a.rows, kNormThreads, 0, stream>>>(a);
+  cuda_check(cudaGetLastError(), "rms_norm launch");
+}
+
+void launch_quant_act(const __nv_bfloat16* x, int64_t ldx, int rows, int D, uint8_t* q,
+                      int64_t ldq, float* sfa_t, int lda_s, cudaStream_t stream) {
+  if (rows <= 0) return;
+  if (D % 128) throw std::invalid_argument("quant_act: D must be a multiple of 128");
+  const int64_t warps = int64_t(rows) * (D / 128);
+  quant_act_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(x, ldx, rows, D, q, ldq, sfa_t, lda_s);
+  cuda_check(cudaGetLastError(), "quant_act launch");
+}
+
+void launch_silu_mul_quant(const __nv_bfloat16* packed, int64_t ldp, int rows, int I,
+                           __nv_bfloat16* h, uint8_t* q, float* sfa_t, int lda_s,
+                           cudaStream_t stream) {
+  if (rows <= 0) return;
+  if (I % 128) throw std::invalid_argument("silu_mul: I must be a multiple of 128");
+  const int64_t warps = int64_t(rows) * (I / 128);
+  silu_mul_quant_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(packed, ldp, rows, I, h, q, sfa_t, lda_s);
+  cuda_check(cudaGetLastError(), "silu_mul launch");
+}
+
+void launch_mla_q_rope(const __nv_bfloat16* q, int64_t ldq, int T, int H, int nope, int rope,
+                       const float* freqs, const float* positions, __nv_bfloat16* out,
+                       int64_t ldo_tok, int64_t ldo_head, int out_offset, cudaStream_t stream) {
+  const int64_t n = int64_t(T) * H * (rope / 2);
+  if (n <= 0) return;
+  mla_q_rope_kernel<<<(n + 255) / 256, 256, 0, stream>>>(q, ldq, T, H, nope, rope, freqs, positions,
+                                                          out, ldo_tok, ldo_head, out_offset);
+  cuda_check(cudaGetLastError(), "mla_q_rope launch");
+}
+
+void launch_kv_finish(const __nv_bfloat16* kv, int64_t ldkv, int T, int L, int R,
+                      const float* norm_w, float eps, const float* freqs,
+                      const float* positions, __nv_bfloat16* out, int64_t ldo,
+                      const int64_t* dst_row, cudaStream_t stream) {
+  if (T <= 0) return;
+  kv_finish_kernel<<<T, 128, 0, stream>>>(kv, ldkv, T, L, R, norm_w, eps, freqs, positions, out, ldo, dst_row);
+  cuda_check(cudaGetLastError(), "kv_finish launch");
+}
+
+void launch_index_k(const __nv_bfloat16* k, int64_t ldk, int T, int D, int R,
+                    const float* ln_w, const float* ln_b, float eps, const float* freqs,
+                    const float* positions, uint8_t* k_q, float* k_scale, cudaStream_t stream) {
+  if (T <= 0) return;
+  if (D != 128) throw std::invalid_argument("index_k: head dim must be 128");
+  index_k_kernel<<<(T + 7) / 8, 256, 0, stream>>>(k, ldk, T, D, R, ln_w, ln_b, eps, freqs, positions, k_q, k_scale);
+  cuda_check(cudaGetLastError(), "index_k launch");
+}
+
+void launch_index_q(const __nv_bfloat16* q, int64_t ldq, int T, int H, int D, int R,
+                    const float* freqs, const float* positions, uint8_t* q_q, float* q_scale,
+                    const float* w_raw, float head_scale, float* weights, cudaStream_t stream) {
+  if (T <= 0) return;
+  if (D != 128) throw std::invalid_argument("index_q: head dim must be 128");
+  const int64_t warps = int64_t(T) * H;
+  index_q_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(q, ldq, T, H, D, R, freqs, positions, q_q, q_scale, w_raw, head_scale, weights);
+  cuda_check(cudaGetLastError(), "index_q launch");
+}
+
+void launch_linear_f32(const __nv_bfloat16* x, int64_t ldx, const float* W, int T, int H, int K,
+                       float* out, cudaStream_t stream) {
+  if (T <= 0) return;
+  dim3 grid((T + 15) / 16, (H + 63) / 64);
+  linear_f32_kernel<<<grid, 256, 0, stream>>>(x, ldx, W, T, H, K, out);
+  cuda_check(cudaGetLastError(), "linear_f32 launch");
+}
+
+void launch_embed(const int64_t* ids, int T, const __nv_bfloat16* table, int64_t vocab, int D,
+                  __nv_bfloat16* out, int* err, cudaStream_t stream) {
+  if (T <= 0) return;
+  if (D % 8) throw std::invalid_argument("embed: D must be a multiple of 8");
+  embed_kernel<<<T, 256, 0, stream>>>(ids, T, table, vocab, D, out, err);
+  cuda_check(cudaGetLastError(), "embed launch");
+}
+
+}  // namespace b200

@@ -1,0 +1,259 @@
+// DSA lightning-indexer logits on the sm_100a tensor core.
+//
+//   logits[q, t] = kscale[t] * sum_h relu(Q[q, h, :] . K[t, :]) * w[q, h]
+//
+// Q: E4M3 [Q, 64, 128], K: E4M3 [N, 128], w: FP32 [Q, 64] (model head weight
+// x query scale), kscale: FP32 [N].  Column t of row q is computed only while
+// t <= query_start + q (causal); masked columns inside a computed tile get
+// -inf, columns past a row's last tile are left untouched (consumers read each
+// row up to its causal end).  Reference: the SM90 WGMMA kernel
+// operators/deepseek_v32/indexer/csrc/echo_logits.cuh:48-590 and DeepGEMM
+// fp8_mqa_logits as called at operators/deepseek_v32/indexer/echo.py:386-393.
+//
+// Mapping: one tcgen05.mma kind::f8f6f4 with M = 128 keys (A = K tile from
+// shared memory), N = 4 queries x 64 heads = 256 (B = the 4 queries' Q rows),
+// K = 128 -> a 128x256 FP32 accumulator in TMEM.  Both operands are naturally
+// K-major 128-byte rows, so TMA writes them with the 128-byte swizzle and the
+// MMA reads them unchanged.  Two accumulators (512 TMEM columns) let the 8
+// epilogue warps reduce tile i while the tensor core computes tile i+1.
+//
+// Work unit = (query block of 4, chunk of key tiles); persistent CTAs walk the
+// units chunk-major so concurrently running CTAs share K tiles through L2.
+#include "../common/ptx.cuh"
+#include "launchers.h"
+
+namespace b200 {
+namespace {
+
+constexpr int kHeads = 64;
+constexpr int kDim = 128;
+constexpr int QB = 4;                 // queries per unit
+constexpr int BKV = 128;              // keys per tile
+constexpr int NQ = QB * kHeads;       // 256 MMA columns
+constexpr int kStages = 8;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + kEpiWarps * 32;
+
+struct Smem {
+  alignas(1024) uint8_t q[2][NQ * kDim];         // 2 x 32 KB
+  alignas(1024) uint8_t k[kStages][BKV * kDim];  // 8 x 16 KB
+  uint64_t q_full[2], q_empty[2];
+  uint64_t k_full[kStages], k_empty[kStages];
+  uint64_t tmem_full[2], tmem_empty[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+struct Schedule {
+  int Q, N, query_start, num_qb, num_tiles_total, chunk_tiles, num_chunks;
+  __device__ __forceinline__ int units() const { return num_qb * num_chunks; }
+  // Returns false when the unit lies entirely past the query block's causal end.
+  __device__ __forceinline__ bool unit(int u, int& qb, int& t0, int& t1) const {
+    qb = u % num_qb;
+    const int chunk = u / num_qb;
+    const int q_last = min(Q - 1, qb * QB + QB - 1);
+    const int end = min(N, query_start + q_last + 1);  // exclusive visible end of the block
+    const int tiles = (end + BKV - 1) / BKV;
+    t0 = chunk * chunk_tiles;
+    t1 = min(tiles, t0 + chunk_tiles);
+    return t0 < t1;
+  }
+};
+
+__global__ void __maxnreg__(200)
+    indexer_kernel(const __grid_constant__ CUtensorMap tma_q,
+                   const __grid_constant__ CUtensorMap tma_k, const float* __restrict__ w,
+                   const float* __restrict__ kscale, float* __restrict__ logits, int64_t ldl,
+                   Schedule sch, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  auto& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.q_full[i], 1);
+      mbar_init(&s.q_empty[i], 1);
+      mbar_init(&s.tmem_full[i], 1);
+      mbar_init(&s.tmem_empty[i], kEpiWarps);
+    }
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&s.k_full[i], 1);
+      mbar_init(&s.k_empty[i], 1);
+    }
+    s.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&s.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  volatile int* abort_flag = &s.abort_flag;
+  const int units = sch.units();
+
+  if (warp == 0) {
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t ucount = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        int qb, t0, t1;
+        if (!sch.unit(u, qb, t0, t1)) continue;
+        const uint32_t qbuf = ucount & 1, qpar = (ucount >> 1) & 1;
+        ++ucount;
+        if (!mbar_wait(&s.q_empty[qbuf], qpar ^ 1, err, kErrTimeoutSmemEmpty, abort_flag)) break;
+        mbar_arrive_expect_tx(&s.q_full[qbuf], NQ * kDim);
+        tma_load_2d(s.q[qbuf], &tma_q, &s.q_full[qbuf], 0, qb * QB * kHeads);
+        for (int t = t0; t < t1; ++t) {
+          if (!mbar_wait(&s.k_empty[stage], phase ^ 1, err, kErrTimeoutSmemEmpty, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&s.k_full[stage], BKV * kDim);
+          tma_load_2d(s.k[stage], &tma_k, &s.k_full[stage], 0, t * BKV);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      const uint32_t idesc = umma_idesc(BKV, NQ, 0, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t ucount = 0, tcount = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        int qb, t0, t1;
+        if (!sch.unit(u, qb, t0, t1)) continue;
+        const uint32_t qbuf = ucount & 1, qpar = (ucount >> 1) & 1;
+        ++ucount;
+        if (!mbar_wait(&s.q_full[qbuf], qpar, err, kErrTimeoutTmaFull, abort_flag)) break;
+        tc_fence_after();
+        const uint64_t bdesc = umma_desc_sw128(smem_u32(s.q[qbuf]));
+        for (int t = t0; t < t1; ++t, ++tcount) {
+          const uint32_t buf = tcount & 1, bpar = (tcount >> 1) & 1;
+          if (!mbar_wait(&s.tmem_empty[buf], bpar ^ 1, err, kErrTimeoutTmemEmpty, abort_flag) ||
+              !mbar_wait(&s.k_full[stage], phase, err, kErrTimeoutTmaFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = umma_desc_sw128(smem_u32(s.k[stage]));
+#pragma unroll
+          for (int k = 0; k < kDim / 32; ++k)
+            mma_f8_ss(tmem + buf * NQ, adesc + (k * 32 >> 4), bdesc + (k * 32 >> 4), idesc, k > 0);
+          mma_commit(&s.k_empty[stage]);
+          mma_commit(&s.tmem_full[buf]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) mma_commit(&s.q_empty[qbuf]);
+      }
+    }
+  } else {
+    const int ew = warp - 2;             // 0..7
+    const int quad = warp & 3;           // TMEM lane quadrant
+    const int half = ew / 4;             // which 2 of the 4 queries
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    const int key_in_tile = quad * 32 + lane;
+    uint32_t tcount = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      int qb, t0, t1;
+      if (!sch.unit(u, qb, t0, t1)) continue;
+      float wreg[2][kHeads];
+      int qidx[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        qidx[j] = qb * QB + half * 2 + j;
+        const int qc = min(qidx[j], sch.Q - 1);
+#pragma unroll
+        for (int h = 0; h < kHeads; ++h) wreg[j][h] = __ldg(w + int64_t(qc) * kHeads + h);
+      }
+      for (int t = t0; t < t1; ++t, ++tcount) {
+        const uint32_t buf = tcount & 1, bpar = (tcount >> 1) & 1;
+        const int key = t * BKV + key_in_tile;
+        const float ks = key < sch.N ? __ldg(kscale + key) : 0.f;
+        if (!mbar_wait(&s.tmem_full[buf], bpar, err, kErrTimeoutTmemFull, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float out[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          float acc = 0.f;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tmem + lane_addr + buf * NQ + (half * 2 + j) * kHeads + c * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int h = 0; h < 32; ++h) acc = fmaf(fmaxf(__uint_as_float(r[h]), 0.f), wreg[j][c * 32 + h], acc);
+          }
+          out[j] = acc * ks;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.tmem_empty[buf]);
+        if (key < sch.N) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            if (qidx[j] < sch.Q) {
+              const bool visible = key <= sch.query_start + qidx[j];
+              logits[int64_t(qidx[j]) * ldl + key] = visible ? out[j] : -INFINITY;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
+void launch_indexer_logits(const IndexerArgs& a, cudaStream_t stream) {
+  if (a.Q <= 0 || a.N <= 0) return;
+  const CUtensorMap tq = make_tma_2d(a.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, int64_t(a.Q) * kHeads,
+                                     kDim, kDim, kDim, NQ);
+  const CUtensorMap tk = make_tma_2d(a.k, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.N, kDim, kDim, kDim, BKV);
+  Schedule sch;
+  sch.Q = a.Q;
+  sch.N = a.N;
+  sch.query_start = a.query_start;
+  sch.num_qb = (a.Q + QB - 1) / QB;
+  const int end = std::min(a.N, a.query_start + a.Q);
+  sch.num_tiles_total = (end + BKV - 1) / BKV;
+  // Enough units to fill every SM about twice, at most 16 tiles per unit.
+  const int sms = sm_count();
+  int64_t work = int64_t(sch.num_qb) * sch.num_tiles_total;
+  int chunk = int(std::max<int64_t>(1, std::min<int64_t>(16, work / (2 * sms))));
+  sch.chunk_tiles = chunk;
+  sch.num_chunks = (sch.num_tiles_total + chunk - 1) / chunk;
+  const int units = sch.num_qb * sch.num_chunks;
+  const int grid = std::min(units, sms);
+  const size_t smem = sizeof(Smem) + 1024;
+  cuda_check(cudaFuncSetAttribute(indexer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+             "indexer smem attribute");
+  indexer_kernel<<<grid, kThreads, smem, stream>>>(tq, tk, a.w, a.kscale, a.logits, a.ldl, sch, a.err);
+  cuda_check(cudaGetLastError(), "indexer launch");
+}
+
+}  // namespace b200

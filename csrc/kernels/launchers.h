@@ -1,0 +1,155 @@
+// Launch entry points of the sm_100a kernels.  These .cu files include only
+// CUDA headers; csrc/bindings.cpp validates torch tensors and calls them.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "../common/host.h"
+
+namespace b200 {
+
+// ---------------------------------------------------------------- GEMMs
+struct FP8GemmArgs {
+  const uint8_t* A;  // E4M3 [M, K], row pitch lda bytes
+  const uint8_t* B;  // E4M3 [N, K], row pitch ldb bytes
+  const float* sfa;  // [ceil(K/128), lda_s]  per-row 1x128 activation scales (transposed)
+  const float* sfb;  // [ceil(N/128), ceil(K/128)] weight block scales
+  __nv_bfloat16* out;
+  const __nv_bfloat16* residual;  // optional, added in FP32
+  int M, N, K;
+  int64_t lda, ldb;
+  int lda_s, ldo, ldr;
+  int* err;
+};
+void launch_fp8_gemm(const FP8GemmArgs& a, cudaStream_t stream);
+
+// Batched BF16 GEMM: for g in [0, batch): out_g[m, n] = sum_k A_g[m, k] * B_g[n, k].
+// A_g row m starts at A + g*a_batch + m*lda (elements), B likewise; out_g at
+// out + g*o_batch + m*ldo.  FP32 accumulate; output bf16 or fp32.
+struct BF16GemmArgs {
+  const __nv_bfloat16* A;
+  const __nv_bfloat16* B;
+  void* out;
+  bool out_fp32;
+  int M, N, K, batch;
+  int64_t lda, a_batch, ldb, b_batch, ldo, o_batch;
+  int* err;
+};
+void launch_bf16_gemm(const BF16GemmArgs& a, cudaStream_t stream);
+
+// ---------------------------------------------------------- elementwise
+// RMSNorm over rows of width D (FP32 weight).  With residual: the FP32 sum
+// x + residual is normalised unrounded and also written rounded (out_sum).
+// With q != nullptr the normalised BF16 row is also quantised 1x128 (UE8M0)
+// into q [rows, D] / sfa_t [D/128, lda_s].
+struct NormArgs {
+  const __nv_bfloat16* x;
+  int64_t ldx;
+  const __nv_bfloat16* residual;
+  int64_t ldr;
+  const float* weight;
+  __nv_bfloat16* out;
+  int64_t ldo;
+  __nv_bfloat16* out_sum;
+  int64_t lds;
+  uint8_t* q;
+  int64_t ldq;
+  float* sfa_t;
+  int lda_s;
+  int rows, D;
+  float eps;
+};
+void launch_rms_norm(const NormArgs& a, cudaStream_t stream);
+
+void launch_quant_act(const __nv_bfloat16* x, int64_t ldx, int rows, int D, uint8_t* q,
+                      int64_t ldq, float* sfa_t, int lda_s, cudaStream_t stream);
+
+// h = silu(gate) * up rounded to BF16, then 1x128 quantised (for the down GEMM).
+// gate = packed[:, :I], up = packed[:, I:2I].
+void launch_silu_mul_quant(const __nv_bfloat16* packed, int64_t ldp, int rows, int I,
+                           __nv_bfloat16* h, uint8_t* q, float* sfa_t, int lda_s,
+                           cudaStream_t stream);
+
+// MLA query RoPE: projected_q[t, h, 512 + i] = rope_interleaved(q[t, h*192 + 128 + i]).
+void launch_mla_q_rope(const __nv_bfloat16* q, int64_t ldq, int T, int H, int nope, int rope,
+                       const float* freqs, const float* positions, __nv_bfloat16* out,
+                       int64_t ldo_tok, int64_t ldo_head, int out_offset, cudaStream_t stream);
+
+// KV record: out[t, 0:L] = rmsnorm(kv[t, 0:L]) (FP32 weight), out[t, L:L+R] = rope(kv[t, L:]).
+// Rows go to out + dst_row[t] * ldo when dst_row is given, else out + t*ldo.
+void launch_kv_finish(const __nv_bfloat16* kv, int64_t ldkv, int T, int L, int R,
+                      const float* norm_w, float eps, const float* freqs,
+                      const float* positions, __nv_bfloat16* out, int64_t ldo,
+                      const int64_t* dst_row, cudaStream_t stream);
+
+// Indexer key: k = bf16(layernorm(x) * w + b); rope split-half on the first R
+// dims; quantise the 128-d row (UE8M0) -> k_q [t], k_scale [t].
+void launch_index_k(const __nv_bfloat16* k, int64_t ldk, int T, int D, int R,
+                    const float* ln_w, const float* ln_b, float eps, const float* freqs,
+                    const float* positions, uint8_t* k_q, float* k_scale, cudaStream_t stream);
+
+// Indexer query: rope split-half + per-(t,h) quantisation; weights[t,h] =
+// raw[t,h] * head_scale * q_scale[t,h].
+void launch_index_q(const __nv_bfloat16* q, int64_t ldq, int T, int H, int D, int R,
+                    const float* freqs, const float* positions, uint8_t* q_q, float* q_scale,
+                    const float* w_raw, float head_scale, float* weights, cudaStream_t stream);
+
+// FP32 x[T, K] (bf16 input) @ W[H, K]^T -> out fp32 [T, H].
+void launch_linear_f32(const __nv_bfloat16* x, int64_t ldx, const float* W, int T, int H, int K,
+                       float* out, cudaStream_t stream);
+
+void launch_embed(const int64_t* ids, int T, const __nv_bfloat16* table, int64_t vocab, int D,
+                  __nv_bfloat16* out, int* err, cudaStream_t stream);
+
+// ------------------------------------------------------------- indexer
+// logits[q, t] = kscale[t] * sum_h relu(Q[q,h,:] . K[t,:]) * w[q,h]; -inf for
+// t > query_start + q (and t >= N).  Q: E4M3 [Q, H=64, 128]; K: E4M3 [N, 128].
+struct IndexerArgs {
+  const uint8_t* q;
+  const uint8_t* k;
+  const float* w;
+  const float* kscale;
+  float* logits;
+  int64_t ldl;
+  int Q, N, query_start, n_cols;
+  int* err;
+};
+void launch_indexer_logits(const IndexerArgs& a, cudaStream_t stream);
+
+// -------------------------------------------------------------- top-k
+// Exact descending top-k per row of FP32 scores [R, N] (row pitch ld), ties to
+// the smaller index, -1 ids for non-finite values.  k <= 2048.
+void launch_topk(const float* scores, int64_t ld, int R, int N, int k, float* values, int* ids,
+                 cudaStream_t stream);
+// Same, with row r reading only columns [0, min(N, causal_start + r + 1)).
+void launch_topk_causal(const float* scores, int64_t ld, int R, int N, int k, int causal_start,
+                        float* values, int* ids, cudaStream_t stream);
+
+// --------------------------------------------------------------- sparse MLA
+struct MLAArgs {
+  const __nv_bfloat16* q;   // [T, H, 576]
+  const __nv_bfloat16* kv;  // [P, 576]
+  const int* ids;           // [T, K]  (-1 / >= P = padding)
+  __nv_bfloat16* out;       // [T, H, 512]
+  float* lse;               // optional [T, H]
+  int T, H, K, P;
+  float scale;
+  int* err;
+};
+void launch_sparse_mla(const MLAArgs& a, cudaStream_t stream);
+// Split-K variant: `splits` CTAs per (token, head block) write FP32 partials
+// and LSE into `scratch` (sparse_mla_scratch_bytes) and a combine kernel merges.
+size_t sparse_mla_scratch_bytes(int T, int H, int splits);
+void launch_sparse_mla_split(const MLAArgs& a, int splits, float* scratch, cudaStream_t stream);
+
+// ----------------------------------------------------------- KV transfer
+// records[slots[i]] = host[host_ids[i]] for i < n (width bytes per row), SM
+// gather from host-mapped pinned memory; count may live on the device.
+void launch_gather_rows(const uint8_t* host, uint8_t* records, const int64_t* host_ids,
+                        const int64_t* slots, int n, const int* device_count, int row_bytes,
+                        int64_t host_rows, int64_t pool_rows, int* err, cudaStream_t stream);
+
+}  // namespace b200

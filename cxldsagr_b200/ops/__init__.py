@@ -1,0 +1,248 @@
+"""Operator API: sm_100a kernels for CUDA tensors, FP32 oracles for CPU tensors.
+
+Each function accepts tensors on either device.  CUDA inputs always run the
+native kernels of ``csrc/`` (no silent PyTorch fallback); CPU inputs run the
+restated reference math of :mod:`.reference`.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import reference
+from .native import check_errors, error_word, lib  # noqa: F401
+
+FP8 = torch.float8_e4m3fn
+
+
+def _cuda(t: torch.Tensor) -> bool:
+    return t.is_cuda
+
+
+# ------------------------------------------------------------------- norms
+def rms_norm(x, weight, eps, *, out=None):
+    if not _cuda(x):
+        return reference.rms_norm(x, weight, eps)
+    x2 = x.reshape(-1, x.shape[-1])
+    out = torch.empty_like(x2) if out is None else out
+    lib().rms_norm(x2, None, weight.float().contiguous(), eps, out, None, None, None)
+    return out.reshape(x.shape)
+
+
+def residual_rms_norm(x, residual, weight, eps):
+    """(rmsnorm(x + residual), x + residual rounded); residual None -> (rmsnorm(x), x)."""
+    if not _cuda(x):
+        return reference.residual_rms_norm(x, residual, weight, eps)
+    if residual is None:
+        return rms_norm(x, weight, eps), x
+    out, summed = torch.empty_like(x), torch.empty_like(x)
+    lib().rms_norm(x, residual, weight.float().contiguous(), eps, out, summed, None, None)
+    return out, summed
+
+
+def norm_quant(x, residual, weight, eps, *, want_out=True):
+    """Fused (residual) RMSNorm + 1x128 FP8 quantisation of the normalised rows.
+
+    Returns (normed bf16 or None, summed bf16 (or x), q fp8 [M,D], scales_t fp32 [D/128, M]).
+    """
+    M, D = x.shape
+    if not _cuda(x):
+        normed, summed = reference.residual_rms_norm(x, residual, weight, eps)
+        q, s = reference.quantize_act(normed)
+        return normed, summed, q, s.t().contiguous()
+    out = torch.empty_like(x) if want_out else None
+    summed = torch.empty_like(x) if residual is not None else x
+    q = torch.empty((M, D), dtype=FP8, device=x.device)
+    s_t = torch.empty((D // 128, M), dtype=torch.float32, device=x.device)
+    lib().rms_norm(x, residual, weight, eps, out, summed if residual is not None else None, q, s_t)
+    return out, summed, q, s_t
+
+
+# ---------------------------------------------------------------- quant
+def quantize_act(x):
+    """1x128 UE8M0 quantisation -> (fp8 [M,K], scales_t fp32 [K/128, M])."""
+    if not _cuda(x):
+        q, s = reference.quantize_act(x)
+        return q, s.t().contiguous()
+    M, K = x.shape
+    q = torch.empty((M, K), dtype=FP8, device=x.device)
+    s_t = torch.empty((K // 128, M), dtype=torch.float32, device=x.device)
+    lib().quant_act(x, q, s_t)
+    return q, s_t
+
+
+def quantize_index(x, scale_fmt="ue8m0"):
+    return reference.quantize_index(x, scale_fmt)
+
+
+# ----------------------------------------------------------------- gemms
+def fp8_gemm(q, s_t, weight, w_scales, *, out=None, residual=None):
+    """BF16 [M,N] = dequant(q, s_t) @ dequant(weight, w_scales)^T (+ residual)."""
+    if not _cuda(q):
+        a = reference.dequantize_act(q, s_t.t())
+        res = a @ reference.dequantize_weight(weight, w_scales).T
+        if residual is not None:
+            res = res + residual.float()
+        return res.to(torch.bfloat16)
+    M, N = q.shape[0], weight.shape[0]
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=q.device) if out is None else out
+    lib().fp8_gemm(q, s_t, weight, w_scales, out, residual)
+    return out
+
+
+def fp8_linear(x, weight, w_scales, *, out=None, residual=None):
+    """Checkpoint FP8 linear: quantise x 1x128 (UE8M0), block-scaled GEMM -> BF16."""
+    x2 = x.reshape(-1, x.shape[-1])
+    if not _cuda(x):
+        res = reference.fp8_linear(x2, weight, w_scales)
+        if residual is not None:
+            res = (res.float() + residual.float()).bfloat16()
+        return res.reshape(*x.shape[:-1], weight.shape[0])
+    q, s_t = quantize_act(x2.contiguous())
+    return fp8_gemm(q, s_t, weight, w_scales, out=out, residual=residual).reshape(*x.shape[:-1], weight.shape[0])
+
+
+def linear(x, weight, scales=None):
+    """FP8-block (``scales`` given) or BF16 linear -> BF16."""
+    if scales is not None:
+        return fp8_linear(x, weight, scales)
+    if not _cuda(x):
+        return reference.linear(x, weight)
+    x2 = x.reshape(-1, x.shape[-1]).contiguous()
+    M, K = x2.shape
+    N = weight.shape[0]
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    lib().bf16_gemm(x2, 0, K, 0, weight.contiguous(), 0, K, 0, out, 0, N, 0, M, N, K, 1)
+    return out.reshape(*x.shape[:-1], N)
+
+
+def bmm_nt(a, b, out=None, *, out_dtype=torch.bfloat16):
+    """Batched out[g] = a[g] @ b[g]^T for a [G,M,K], b [G,N,K] (contiguous views)."""
+    if not _cuda(a):
+        return torch.bmm(a.float(), b.float().transpose(1, 2)).to(out_dtype)
+    G, M, K = a.shape
+    N = b.shape[1]
+    a, b = a.contiguous(), b.contiguous()
+    out = torch.empty((G, M, N), dtype=out_dtype, device=a.device) if out is None else out
+    lib().bf16_gemm(a, 0, K, M * K, b, 0, K, N * K, out, 0, N, M * N, M, N, K, G)
+    return out
+
+
+def linear_f32(x, weight):
+    """FP32 x @ weight^T with a BF16 x and an FP32 weight -> FP32."""
+    if not _cuda(x):
+        return x.float() @ weight.float().T
+    out = torch.empty((x.shape[0], weight.shape[0]), dtype=torch.float32, device=x.device)
+    lib().linear_f32(x.contiguous(), weight.contiguous(), out)
+    return out
+
+
+def silu_mul(gate, up):
+    if not _cuda(gate):
+        return reference.silu_mul(gate, up)
+    packed = torch.cat((gate, up), -1).contiguous()
+    h = torch.empty_like(gate)
+    lib().silu_mul_quant(packed, h, None, None)
+    return h
+
+
+def silu_mul_quant(packed):
+    """packed [M, 2I] (gate|up) -> (h bf16 [M,I], q fp8 [M,I], scales_t [I/128, M])."""
+    M, I2 = packed.shape
+    I = I2 // 2
+    if not _cuda(packed):
+        h = reference.silu_mul(packed[:, :I], packed[:, I:])
+        q, s = reference.quantize_act(h)
+        return h, q, s.t().contiguous()
+    h = torch.empty((M, I), dtype=torch.bfloat16, device=packed.device)
+    q = torch.empty((M, I), dtype=FP8, device=packed.device)
+    s_t = torch.empty((I // 128, M), dtype=torch.float32, device=packed.device)
+    lib().silu_mul_quant(packed, h, q, s_t)
+    return h, q, s_t
+
+
+# --------------------------------------------------------------- indexer
+def indexer_logits(q, k, weights, kscale, query_start: int, *, out=None):
+    """Causal FP32 logits [Q, N] (masked columns -inf)."""
+    if not _cuda(q):
+        return reference.indexer_logits(q, k, weights, kscale, query_start)
+    Q, N = q.shape[0], k.shape[0]
+    if out is None:
+        out = torch.full((Q, N), -torch.inf, dtype=torch.float32, device=q.device)
+    lib().indexer_logits(q, k, weights, kscale, out, query_start)
+    return out
+
+
+def exact_topk(scores, k: int, *, causal_start: int | None = None, n: int | None = None):
+    """Descending top-k (ties -> smaller index), -1 ids for non-finite/empty slots.
+
+    ``causal_start`` restricts row r to columns [0, causal_start + r + 1).
+    Output width is min(k, n) like the reference selection API.
+    """
+    n = scores.shape[1] if n is None else n
+    count = min(k, n)
+    if not _cuda(scores):
+        s = scores[:, :n]
+        if causal_start is not None:
+            rows = torch.arange(s.shape[0])[:, None]
+            cols = torch.arange(n)[None, :]
+            s = s.masked_fill(cols > causal_start + rows, -torch.inf)
+        return reference.exact_topk(s, count)
+    R = scores.shape[0]
+    values = torch.empty((R, count), dtype=torch.float32, device=scores.device)
+    ids = torch.empty((R, count), dtype=torch.int32, device=scores.device)
+    lib().topk(scores, n, count, -1 if causal_start is None else causal_start, values, ids)
+    return values, ids
+
+
+# ------------------------------------------------------------- attention
+def sparse_mla(q, kv, ids, scale, *, splits: int = 1, return_lse: bool = False):
+    """Sparse MLA: q [T,H,576], kv [P,576], ids [T,K] -> [T,H,512] (BF16)."""
+    if not _cuda(q):
+        if return_lse:
+            o, lse = reference.sparse_mla_lse(q, kv, ids, scale)
+            return o.to(q.dtype), lse
+        return reference.sparse_mla(q, kv, ids, scale)
+    T, H, _ = q.shape
+    out = torch.empty((T, H, 512), dtype=torch.bfloat16, device=q.device)
+    lse = torch.empty((T, H), dtype=torch.float32, device=q.device) if return_lse else None
+    scratch = None
+    if splits > 1:
+        nbytes = lib().sparse_mla_scratch_bytes(T, H, splits)
+        scratch = torch.empty(nbytes // 4, dtype=torch.float32, device=q.device)
+    lib().sparse_mla(q.contiguous(), kv, ids.contiguous(), float(scale), out, lse, splits, scratch)
+    return (out, lse) if return_lse else out
+
+
+def sparse_mla_decode(q, kv, ids, scale, splits: int = 16):
+    """Single-query decode: split the selection over ``splits`` CTAs and LSE-merge."""
+    return sparse_mla(q, kv, ids, scale, splits=splits)
+
+
+# -------------------------------------------------------------- transfer
+def gather_host_records(host, records, host_ids, slots, *, device_count=None):
+    """records[slots[i]] = host[host_ids[i]] (SM gather from pinned host memory on CUDA)."""
+    if not records.is_cuda:
+        records[slots.long()] = host[host_ids.long()].to(records.dtype)
+        return records
+    n = host_ids.numel()
+    if n:
+        lib().gather_rows(host, records, host_ids.long().contiguous(), slots.long().contiguous(), n, device_count)
+    return records
+
+
+def embed(ids, table):
+    if not table.is_cuda:
+        return table[ids.long()].bfloat16()
+    out = torch.empty((ids.numel(), table.shape[1]), dtype=torch.bfloat16, device=table.device)
+    lib().embed(ids.long().contiguous(), table, out)
+    return out
+
+
+route_experts = reference.route_experts
+
+
+def attention_scale_log2(scale: float) -> float:
+    return scale * math.log2(math.e)

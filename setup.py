@@ -1,0 +1,35 @@
+"""Build the sm_100a extension in-tree: ``python setup.py build_ext --inplace``.
+
+Only ``-gencode arch=compute_100a,code=sm_100a`` is emitted (torch skips its
+own arch list when an explicit -gencode flag is present).
+"""
+
+import glob
+import os
+
+from setuptools import setup
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "--expt-relaxed-constexpr",
+    "-Xptxas=-warn-spills",
+]
+SOURCES = ["csrc/bindings.cpp"] + sorted(glob.glob("csrc/kernels/*.cu"))
+
+setup(
+    name="cxldsagr_b200",
+    version="0.1.0",
+    packages=[],
+    ext_modules=[
+        CUDAExtension(
+            name="cxldsagr_b200._C",
+            sources=SOURCES,
+            include_dirs=[os.path.join(ROOT, "csrc")],
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+        )
+    ],
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+)

@@ -1,0 +1,235 @@
+"""Numerics of every sm_100a kernel against the plain-PyTorch FP32 oracle."""
+
+import math
+
+import pytest
+import torch
+
+from cxldsagr_b200 import ops
+from cxldsagr_b200.checkpoint import quantize_weight_blocks
+from cxldsagr_b200.config import v32_config
+from cxldsagr_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).abs().max() / b.abs().max().clamp_min(1e-6)).item()
+
+
+@pytest.fixture(autouse=True)
+def _check_device_errors():
+    yield
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+        ops.check_errors(DEV)
+
+
+# ------------------------------------------------------------------ norms
+@pytest.mark.parametrize("rows,D", [(1, 7168), (37, 1536), (130, 512)])
+def test_rms_norm(rows, D):
+    torch.manual_seed(0)
+    x = torch.randn(rows, D, device=DEV).bfloat16()
+    r = torch.randn(rows, D, device=DEV).bfloat16()
+    w = torch.rand(D, device=DEV) + 0.5
+    got = ops.rms_norm(x, w, 1e-6)
+    want = ref.rms_norm(x.cpu(), w.cpu(), 1e-6)
+    assert rel_err(got.cpu(), want) < 1e-2
+    n, s = ops.residual_rms_norm(x, r, w, 1e-6)
+    wn, ws = ref.residual_rms_norm(x.cpu(), r.cpu(), w.cpu(), 1e-6)
+    assert torch.equal(s.cpu(), ws)
+    assert rel_err(n.cpu(), wn) < 1e-2
+
+
+def test_norm_quant_matches_quantize():
+    torch.manual_seed(1)
+    x = torch.randn(64, 7168, device=DEV).bfloat16()
+    w = torch.rand(7168, device=DEV) + 0.5
+    n, _, q, s_t = ops.norm_quant(x, None, w, 1e-6)
+    q2, s2 = ops.quantize_act(n)
+    assert torch.equal(q.view(torch.uint8), q2.view(torch.uint8))
+    assert torch.equal(s_t, s2)
+
+
+@pytest.mark.parametrize("M,K", [(1, 128), (33, 7168), (256, 18432)])
+def test_quant_act_bitwise(M, K):
+    torch.manual_seed(2)
+    x = (torch.randn(M, K, device=DEV) * 3).bfloat16()
+    q, s_t = ops.quantize_act(x)
+    rq, rs = ref.quantize_act(x.cpu())
+    assert torch.equal(s_t.cpu(), rs.t())
+    assert torch.equal(q.cpu().view(torch.uint8), rq.view(torch.uint8))
+
+
+def test_silu_mul_quant():
+    torch.manual_seed(3)
+    packed = torch.randn(17, 2 * 2048, device=DEV).bfloat16()
+    h, q, s_t = ops.silu_mul_quant(packed)
+    rh = ref.silu_mul(packed[:, :2048].cpu(), packed[:, 2048:].cpu())
+    assert rel_err(h.cpu(), rh) < 1e-2
+    rq, rs = ref.quantize_act(h.cpu())
+    assert torch.equal(s_t.cpu(), rs.t())
+
+
+# ------------------------------------------------------------------ gemms
+@pytest.mark.parametrize("M,N,K", [(1, 576, 7168), (128, 1536, 7168), (200, 7168, 2048), (1024, 2240, 7168), (77, 130, 256)])
+def test_fp8_gemm(M, N, K):
+    torch.manual_seed(4)
+    x = torch.randn(M, K, device=DEV).bfloat16()
+    w, s = quantize_weight_blocks(torch.randn(N, K, device=DEV) * 0.02, pow2_scales=False)
+    got = ops.fp8_linear(x, w, s)
+    want = ref.fp8_linear(x.cpu(), w.cpu(), s.cpu())
+    assert rel_err(got.cpu(), want) < 2e-2
+
+
+def test_fp8_gemm_residual():
+    torch.manual_seed(5)
+    x = torch.randn(130, 1024, device=DEV).bfloat16()
+    res = torch.randn(130, 384, device=DEV).bfloat16()
+    w, s = quantize_weight_blocks(torch.randn(384, 1024, device=DEV) * 0.05)
+    got = ops.fp8_linear(x, w, s, residual=res)
+    want = ref.fp8_linear(x.cpu(), w.cpu(), s.cpu()).float() + res.cpu().float()
+    assert rel_err(got.cpu(), want) < 2e-2
+
+
+@pytest.mark.parametrize("G,M,N,K", [(1, 1, 1000, 7168), (4, 130, 512, 128), (3, 64, 128, 512)])
+def test_bf16_bmm(G, M, N, K):
+    torch.manual_seed(6)
+    a = torch.randn(G, M, K, device=DEV).bfloat16()
+    b = torch.randn(G, N, K, device=DEV).bfloat16()
+    got = ops.bmm_nt(a, b, out_dtype=torch.float32)
+    want = torch.bmm(a.float().cpu(), b.float().cpu().transpose(1, 2))
+    assert rel_err(got.cpu(), want) < 1e-3
+
+
+# ------------------------------------------------------------- indexer
+@pytest.mark.parametrize("Q,N,start", [(1, 700, 699), (7, 300, 200), (64, 4096, 4032), (130, 2000, 0)])
+def test_indexer_logits(Q, N, start):
+    torch.manual_seed(7)
+    N = max(N, start + Q)
+    q = (torch.randn(Q, 64, 128, device=DEV) * 2).to(torch.float8_e4m3fn)
+    k = (torch.randn(N, 128, device=DEV) * 2).to(torch.float8_e4m3fn)
+    w = torch.randn(Q, 64, device=DEV)
+    ks = torch.rand(N, device=DEV) + 0.1
+    got = ops.indexer_logits(q, k, w, ks, start)
+    want = ref.indexer_logits(q.cpu(), k.cpu(), w.cpu(), ks.cpu(), start)
+    fin = torch.isfinite(want)
+    assert torch.equal(torch.isfinite(got.cpu()), fin)
+    assert rel_err(got.cpu()[fin], want[fin]) < 1e-4
+
+
+# ----------------------------------------------------------------- topk
+@pytest.mark.parametrize("R,N,k", [(3, 100, 64), (5, 5000, 2048), (2, 70000, 2048), (4, 1500, 2048)])
+def test_topk(R, N, k):
+    torch.manual_seed(8)
+    s = torch.randn(R, N, device=DEV)
+    v, i = ops.exact_topk(s, k)
+    rv, ri = ref.exact_topk(s.cpu(), k)
+    assert torch.equal(i.cpu(), ri)
+    assert torch.equal(v.cpu(), rv)
+
+
+def test_topk_ties_and_causal():
+    torch.manual_seed(9)
+    s = torch.randint(0, 5, (6, 3000), device=DEV).float()
+    v, i = ops.exact_topk(s, 2048, causal_start=1000)
+    rows = torch.arange(6)[:, None]
+    cols = torch.arange(3000)[None, :]
+    masked = s.cpu().masked_fill(cols > 1000 + rows, -torch.inf)
+    rv, ri = ref.exact_topk(masked, 2048)
+    assert torch.equal(i.cpu(), ri)
+
+
+# ------------------------------------------------------------ sparse MLA
+@pytest.mark.parametrize("T,K,P,splits", [(2, 2048, 5000, 1), (3, 256, 300, 1), (1, 2048, 9000, 16), (5, 100, 64, 4)])
+def test_sparse_mla(T, K, P, splits):
+    torch.manual_seed(10)
+    H = 128
+    q = (torch.randn(T, H, 576, device=DEV) * 0.5).bfloat16()
+    kv = (torch.randn(P, 576, device=DEV) * 0.5).bfloat16()
+    ids = torch.randint(0, P, (T, K), device=DEV, dtype=torch.int32)
+    ids[:, -7:] = -1
+    ids[0, :3] = P + 5  # out of range = padding
+    scale = v32_config().attention_scale
+    got, lse = ops.sparse_mla(q, kv, ids, scale, splits=splits, return_lse=True)
+    want, wlse = ref.sparse_mla_lse(q.cpu(), kv.cpu(), ids.cpu(), scale)
+    assert rel_err(got.cpu(), want) < 2e-2
+    assert torch.allclose(lse.cpu(), wlse, atol=2e-2, rtol=1e-3)
+
+
+def test_sparse_mla_all_padding_is_zero():
+    q = torch.randn(2, 128, 576, device=DEV).bfloat16()
+    kv = torch.randn(10, 576, device=DEV).bfloat16()
+    ids = torch.full((2, 64), -1, dtype=torch.int32, device=DEV)
+    out = ops.sparse_mla(q, kv, ids, 0.1)
+    assert torch.count_nonzero(out) == 0
+
+
+# ---------------------------------------------------------- elementwise
+def test_projection_epilogues():
+    torch.manual_seed(11)
+    cfg = v32_config(3)
+    T = 19
+    freqs = ref.rotary_frequencies(cfg).to(DEV)
+    pos = torch.arange(100, 100 + T, device=DEV).float()
+    angles = (pos[:, None] * freqs[None, :]).cpu()
+    L = ops.lib()
+    # MLA q rope
+    q = torch.randn(T, 128 * 192, device=DEV).bfloat16()
+    out = torch.zeros(T, 128, 576, device=DEV).bfloat16()
+    L.mla_q_rope(q, q.stride(0), T, 128, 128, 64, freqs, pos, out, 128 * 576, 576, 512)
+    want = ref.apply_rope(q.cpu().reshape(T, 128, 192)[..., 128:], angles, interleaved=True)
+    assert rel_err(out[..., 512:].cpu(), want) < 1e-2
+    # kv finish
+    kv = torch.randn(T, 576, device=DEV).bfloat16()
+    nw = torch.rand(512, device=DEV) + 0.5
+    rec = torch.empty(T, 576, device=DEV).bfloat16()
+    L.kv_finish(kv, 512, 64, nw, 1e-6, freqs, pos, rec, None)
+    lat = ref.rms_norm(kv.cpu()[:, :512], nw.cpu(), 1e-6)
+    pe = ref.apply_rope(kv.cpu()[:, 512:], angles, interleaved=True)
+    assert rel_err(rec[:, :512].cpu(), lat) < 1e-2 and rel_err(rec[:, 512:].cpu(), pe) < 1e-2
+    # index k
+    k = torch.randn(T, 128, device=DEV).bfloat16()
+    lw, lb = torch.rand(128, device=DEV) + 0.5, torch.randn(128, device=DEV) * 0.1
+    kq = torch.empty(T, 128, device=DEV, dtype=torch.float8_e4m3fn)
+    ksc = torch.empty(T, device=DEV)
+    L.index_k(k, 64, lw, lb, 1e-6, freqs, pos, kq, ksc)
+    kk = ref.layer_norm(k.cpu(), lw.cpu(), lb.cpu(), 1e-6).bfloat16()
+    kk = ref.apply_rope(kk, angles, interleaved=False)
+    rq, rs = ref.quantize_index(kk)
+    assert torch.allclose(ksc.cpu(), rs[:, 0])
+    assert rel_err(kq.cpu().float() * ksc.cpu()[:, None], rq.float() * rs) < 0.07  # one e4m3 step
+    # index q
+    iq = torch.randn(T, 64 * 128, device=DEV).bfloat16()
+    wraw = torch.randn(T, 64, device=DEV)
+    qq = torch.empty(T, 64, 128, device=DEV, dtype=torch.float8_e4m3fn)
+    qs = torch.empty(T, 64, device=DEV)
+    wts = torch.empty(T, 64, device=DEV)
+    L.index_q(iq, iq.stride(0), T, 64, 128, 64, freqs, pos, qq, qs, wraw, 0.125, wts)
+    rq2 = ref.apply_rope(iq.cpu().reshape(T, 64, 128), angles, interleaved=False)
+    _, rqs = ref.quantize_index(rq2)
+    assert torch.allclose(qs.cpu(), rqs[..., 0])
+    assert torch.allclose(wts.cpu(), wraw.cpu() * 0.125 * rqs[..., 0])
+
+
+def test_linear_f32_and_embed():
+    torch.manual_seed(12)
+    x = torch.randn(40, 7168, device=DEV).bfloat16()
+    W = torch.randn(64, 7168, device=DEV)
+    got = ops.linear_f32(x, W)
+    want = x.cpu().float() @ W.cpu().T
+    assert rel_err(got.cpu(), want) < 1e-5
+    table = torch.randn(1000, 256, device=DEV).bfloat16()
+    ids = torch.tensor([5, 0, 999, 17], device=DEV)
+    assert torch.equal(ops.embed(ids, table), table[ids])
+
+
+def test_gather_rows_from_pinned_host():
+    host = torch.randn(256, 576).bfloat16().pin_memory()
+    records = torch.zeros(65, 576, device=DEV).bfloat16()
+    hid = torch.tensor([3, 100, 255, 7], device=DEV)
+    slots = torch.tensor([1, 64, 2, 30], device=DEV)
+    ops.gather_host_records(host, records, hid, slots)
+    assert torch.equal(records[slots].cpu(), host[hid.cpu()])
