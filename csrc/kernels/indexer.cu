@@ -40,6 +40,7 @@ struct Smem {
   uint64_t q_full[2], q_empty[2];
   uint64_t k_full[kStages], k_empty[kStages];
   uint64_t tmem_full[2], tmem_empty[2];
+  alignas(16) float w[kEpiWarps][2][kHeads];  // per-warp head weights of its 2 queries
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -60,7 +61,7 @@ struct Schedule {
   }
 };
 
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(kThreads, 1)
     indexer_kernel(const __grid_constant__ CUtensorMap tma_q,
                    const __grid_constant__ CUtensorMap tma_k, const float* __restrict__ w,
                    const float* __restrict__ kscale, float* __restrict__ logits, int64_t ldl,
@@ -171,15 +172,19 @@ __global__ void __maxnreg__(200)
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
       int qb, t0, t1;
       if (!sch.unit(u, qb, t0, t1)) continue;
-      float wreg[2][kHeads];
+      // Each warp stages its own 2 queries' head weights (private slice:
+      // only __syncwarp ordering is needed, no cross-warp barrier).
+      __syncwarp();
+#pragma unroll
+      for (int e = lane; e < 2 * kHeads; e += 32) {
+        const int j = e / kHeads, h = e % kHeads;
+        const int qc = min(qb * QB + half * 2 + j, sch.Q - 1);
+        s.w[ew][j][h] = __ldg(w + int64_t(qc) * kHeads + h);
+      }
+      __syncwarp();
       int qidx[2];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        qidx[j] = qb * QB + half * 2 + j;
-        const int qc = min(qidx[j], sch.Q - 1);
-#pragma unroll
-        for (int h = 0; h < kHeads; ++h) wreg[j][h] = __ldg(w + int64_t(qc) * kHeads + h);
-      }
+      for (int j = 0; j < 2; ++j) qidx[j] = qb * QB + half * 2 + j;
       for (int t = t0; t < t1; ++t, ++tcount) {
         const uint32_t buf = tcount & 1, bpar = (tcount >> 1) & 1;
         const int key = t * BKV + key_in_tile;
@@ -193,13 +198,20 @@ __global__ void __maxnreg__(200)
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           float acc = 0.f;
+          const float4* wv = reinterpret_cast<const float4*>(s.w[ew][j]);
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             uint32_t r[32];
             tmem_ld32(tmem + lane_addr + buf * NQ + (half * 2 + j) * kHeads + c * 32, r);
             tmem_wait_ld();
 #pragma unroll
-            for (int h = 0; h < 32; ++h) acc = fmaf(fmaxf(__uint_as_float(r[h]), 0.f), wreg[j][c * 32 + h], acc);
+            for (int h4 = 0; h4 < 8; ++h4) {
+              const float4 ww = wv[c * 8 + h4];
+              acc = fmaf(fmaxf(__uint_as_float(r[4 * h4 + 0]), 0.f), ww.x, acc);
+              acc = fmaf(fmaxf(__uint_as_float(r[4 * h4 + 1]), 0.f), ww.y, acc);
+              acc = fmaf(fmaxf(__uint_as_float(r[4 * h4 + 2]), 0.f), ww.z, acc);
+              acc = fmaf(fmaxf(__uint_as_float(r[4 * h4 + 3]), 0.f), ww.w, acc);
+            }
           }
           out[j] = acc * ks;
         }
