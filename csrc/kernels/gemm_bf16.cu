@@ -37,7 +37,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bf16_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                      const __grid_constant__ CUtensorMap tma_b, void* __restrict__ out,
                      int out_fp32, int64_t ldo, int64_t o_batch, int M, int N, int K, int batch,
-                     int* err) {
+                     int a_batch_inner, int b_batch_inner, int* err) {
   extern __shared__ uint8_t smem_raw[];
   auto& s = *reinterpret_cast<Smem<BN, STAGES>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -85,8 +85,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&s.full[stage], (BM + BN) * 128);
-          tma_load_3d(s.a[stage], &tma_a, &s.full[stage], kb * BKE, m0, g);
-          tma_load_3d(s.b[stage], &tma_b, &s.full[stage], kb * BKE, n0, g);
+          // Tensor-map dims are ordered by increasing stride: (k, m, g) or (k, g, m).
+          if (a_batch_inner) tma_load_3d(s.a[stage], &tma_a, &s.full[stage], kb * BKE, g, m0);
+          else tma_load_3d(s.a[stage], &tma_a, &s.full[stage], kb * BKE, m0, g);
+          if (b_batch_inner) tma_load_3d(s.b[stage], &tma_b, &s.full[stage], kb * BKE, g, n0);
+          else tma_load_3d(s.b[stage], &tma_b, &s.full[stage], kb * BKE, n0, g);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -202,12 +205,18 @@ void launch_bf16_gemm(const BF16GemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0 || a.batch <= 0) return;
   constexpr int BN = 128, STAGES = 6;
   if ((a.K * 2) % 16) throw std::invalid_argument("bf16 gemm: K must be a multiple of 8");
-  const CUtensorMap ta = make_tma_3d(a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.K, a.M, a.batch,
-                                     a.lda * 2, (a.batch > 1 ? a.a_batch : a.M * a.lda) * 2, BKE,
-                                     BM, 1);
-  const CUtensorMap tb = make_tma_3d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.K, a.N, a.batch,
-                                     a.ldb * 2, (a.batch > 1 ? a.b_batch : a.N * a.ldb) * 2, BKE,
-                                     BN, 1);
+  // A box of 1 along the batch dim and 128 rows along M / N lands as a
+  // 128-row x 128-byte tile whichever order the two outer dims have.
+  const int64_t a_bs = a.batch > 1 ? a.a_batch : int64_t(a.M) * a.lda;
+  const int64_t b_bs = a.batch > 1 ? a.b_batch : int64_t(a.N) * a.ldb;
+  const bool a_inner = a.batch > 1 && a_bs < a.lda;
+  const bool b_inner = a.batch > 1 && b_bs < a.ldb;
+  const CUtensorMap ta = a_inner
+      ? make_tma_3d(a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.K, a.batch, a.M, a_bs * 2, a.lda * 2, BKE, 1, BM)
+      : make_tma_3d(a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.K, a.M, a.batch, a.lda * 2, a_bs * 2, BKE, BM, 1);
+  const CUtensorMap tb = b_inner
+      ? make_tma_3d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.K, a.batch, a.N, b_bs * 2, a.ldb * 2, BKE, 1, BN)
+      : make_tma_3d(a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.K, a.N, a.batch, a.ldb * 2, b_bs * 2, BKE, BN, 1);
   const int64_t tiles = int64_t((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN) * a.batch;
   const int grid = int(std::min<int64_t>(tiles, sm_count()));
   const size_t smem = sizeof(Smem<BN, STAGES>) + 1024;
@@ -215,7 +224,7 @@ void launch_bf16_gemm(const BF16GemmArgs& a, cudaStream_t stream) {
   cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
              "bf16 gemm smem attribute");
   kern<<<grid, kThreads, smem, stream>>>(ta, tb, a.out, a.out_fp32 ? 1 : 0, a.ldo, a.o_batch, a.M,
-                                         a.N, a.K, a.batch, a.err);
+                                         a.N, a.K, a.batch, a_inner ? 1 : 0, b_inner ? 1 : 0, a.err);
   cuda_check(cudaGetLastError(), "bf16 gemm launch");
 }
 

@@ -1,0 +1,165 @@
+"""One layer of DSA attention: projections -> indexer -> exact top-k -> KV
+append / recall -> sparse MLA -> value expansion -> o_proj.
+
+Reference pipeline: ``models/deepseek_v32/attention.py:276-425`` (runner) and
+``models/deepseek_v32/projections.py:182-293`` (projections).  Differences of
+the B200 design: the q_a / kv_a / indexer-wk linears run as one FP8 GEMM on
+the quantised normed input, q_b and indexer wq_b as another; the KV record is
+written by the projection epilogue straight into its pool row; the indexer
+reads the resident FP8 key cache through TMA and the selection feeds the MLA
+kernel without a host round trip in the resident (``hbm``) method.
+
+Cache methods (``CacheConfig.method``):
+* ``hbm``            resident main KV (logical row = physical row);
+* ``serial_sparse``  finite HBM pool + pinned DRAM; exact recall after top-k;
+* ``echo``           as serial_sparse, plus a prefetch of the subset of the
+                     coming top-k that the coarse logit histogram proves, issued
+                     on a copy stream while the exact top-k runs;
+* ``dense_prefetch`` whole-history copy-engine DMA into the pool (one layer
+                     ahead), then attention on resident rows.
+"""
+
+from __future__ import annotations
+
+from contextlib import nullcontext
+
+import torch
+
+from ... import ops
+from ...cache.sparse_token_cache import SparseTokenCache, WorkingSetTooLarge
+from ...contracts import TokenSelection
+from .weights import AttentionWeights
+
+
+class AttentionRunner:
+    def __init__(self, cfg, weights: AttentionWeights, cache: SparseTokenCache, *, method: str = "hbm",
+                 index_capacity: int | None = None):
+        self.cfg = cfg
+        self.w = weights
+        self.cache = cache
+        self.method = method
+        self.device = cache.device
+        cap = index_capacity or (cache.capacity + cache.candidate_slots)
+        self.index_keys = torch.zeros((cap, cfg.index_head_dim), dtype=torch.float8_e4m3fn, device=self.device)
+        self.index_scales = torch.zeros(cap, dtype=torch.float32, device=self.device)
+        # offset[0]: prefill mean hint, offset[1]: decode EMA of the kth score.
+        self.offset = torch.zeros(16, dtype=torch.float32, device=self.device)
+        self.last_indices = None
+        self.head_scale = cfg.index_n_heads ** -0.5 * cfg.index_head_dim ** -0.5
+        (self.qa0, self.qa_n), (self.kv0, self.kv_n), (self.ik0, self.ik_n) = weights.spans_a
+        (self.qb0, self.qb_n), (self.iq0, self.iq_n) = weights.spans_b
+
+    # ------------------------------------------------------------- projection
+    def project(self, normed, quantized, pos: int, positions, freqs):
+        cfg, w = self.cfg, self.w
+        T = normed.shape[0]
+        H, nope, rope, L = cfg.n_heads, cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.kv_lora_rank
+        a = w.fused_a(normed, quantized=quantized)
+        qa = a[:, self.qa0:self.qa0 + self.qa_n]
+        kv = a[:, self.kv0:self.kv0 + self.kv_n]
+        ik = a[:, self.ik0:self.ik0 + self.ik_n]
+        qa_normed, _, qr8, qrs = ops.norm_quant(qa, None, w.q_norm, cfg.norm_eps, want_out=w.fused_b.scales is None)
+        b = w.fused_b(qa_normed, quantized=(qr8, qrs))
+        q_proj = torch.empty((T, H, cfg.qk_head_dim), dtype=torch.bfloat16, device=normed.device)
+        ops.mla_absorb(b, H, nope, rope, w.wk_b_t, q_proj)
+        ops.mla_q_rope(b, H, nope, rope, freqs, positions, q_proj, L)
+        # KV record straight into its cache row.
+        rows = self.cache.destination_rows(T)
+        ops.kv_finish(kv, L, rope, w.kv_norm, cfg.norm_eps, freqs, positions, self.cache.records, rows)
+        self.cache.finish_append(rows)
+        # Indexer key into the resident FP8 key cache.
+        ops.index_k(ik, rope, w.index_norm_w, w.index_norm_b, cfg.norm_eps, freqs, positions,
+                    self.index_keys[pos:pos + T], self.index_scales[pos:pos + T])
+        w_raw = ops.linear_f32(normed, w.index_head)
+        iq = b[:, self.iq0:self.iq0 + self.iq_n]
+        q_idx, weights = ops.index_q(iq, cfg.index_n_heads, cfg.index_head_dim, rope, freqs, positions,
+                                     w_raw, self.head_scale)
+        return q_proj, q_idx, weights
+
+    # ---------------------------------------------------------------- forward
+    def forward(self, normed, quantized, pos: int, positions, freqs, *, scope=None, logits_buf=None):
+        scope = scope or (lambda _name: nullcontext())
+        cfg = self.cfg
+        T = normed.shape[0]
+        end = pos + T
+        with self.cache.operation():
+            with scope("attention_projection"):
+                q_proj, q_idx, weights = self.project(normed, quantized, pos, positions, freqs)
+            with scope("indexer"):
+                if logits_buf is not None and logits_buf.shape[0] >= T and logits_buf.shape[1] >= end:
+                    logits = logits_buf[:T]
+                else:
+                    logits = torch.empty((T, max(4, (end + 3) // 4 * 4)), dtype=torch.float32, device=normed.device)
+                if logits.is_cuda:
+                    ops.lib().indexer_logits(q_idx, self.index_keys[:end], weights, self.index_scales[:end], logits, pos)
+                else:
+                    logits = ops.indexer_logits(q_idx, self.index_keys[:end], weights, self.index_scales[:end], pos)
+            if self.method == "echo" and self.cache.offload and pos > 0:
+                with scope("indexer_prefetch"):
+                    self._predictive_prefetch(logits, pos, end)
+            with scope("exact_topk"):
+                values, ids = ops.exact_topk(logits, cfg.index_topk, causal_start=pos, n=end)
+            if self.method == "echo" and self.cache.offload:
+                with scope("prefetch_hint"):
+                    self._update_hints(logits, values, pos, end)
+            self.last_indices = ids
+            with scope("sparse_mla"):
+                attn = self._consume(q_proj, ids)
+        with scope("attention_output"):
+            v = ops.mla_expand(attn, self.w.wv_b)
+            return self.w.wo(v.reshape(T, -1))
+
+    def _consume(self, q, ids):
+        if not self.cache.offload:
+            return ops.sparse_mla(q, self.cache.records, ids, self.cfg.attention_scale, value_dim=self.cfg.kv_lora_rank)
+        try:
+            physical = self.cache.ensure(ids)
+        except WorkingSetTooLarge:
+            if len(q) == 1:
+                raise ValueError("the pool must fit one query's exact selection") from None
+            self.cache.stats.capacity_splits += 1
+            mid = len(q) // 2
+            return torch.cat((self._consume(q[:mid], ids[:mid]), self._consume(q[mid:], ids[mid:])))
+        return ops.sparse_mla(q, self.cache.records, physical, self.cfg.attention_scale, value_dim=self.cfg.kv_lora_rank)
+
+    # ------------------------------------------------------------ echo method
+    def _predictive_prefetch(self, logits, pos, end):
+        """Prefetch the provable part of the coming top-k (coarse histogram threshold).
+
+        For each query, bucket ``logit - offset[0]`` into 256 monotone bins; the
+        bin holding the k-th element is the threshold; history tokens in strictly
+        higher bins are certainly selected and are recalled now (reference
+        predictor: operators/deepseek_v32/indexer/csrc/echo_logits.cuh:500-584).
+        Budget: min(8192, P - Q) records.
+        """
+        k = self.cfg.index_topk
+        hist_end = min(pos, self.cache.length)
+        if hist_end <= k:
+            return
+        rows = logits[:, :hist_end] - self.offset[0]
+        key = _order_bins(rows)
+        counts = torch.zeros((rows.shape[0], 257), dtype=torch.int64, device=rows.device)
+        counts.scatter_add_(1, key.long(), torch.ones_like(key, dtype=torch.int64))
+        above = counts.flip(1).cumsum(1).flip(1)  # elements in bins >= b
+        thr = (above[:, 1:] > k).sum(1)            # first bin with <= k elements above it
+        pred = key > thr[:, None]
+        budget = min(8192, self.cache.slots - logits.shape[0])
+        cand = torch.nonzero(pred.any(0)).flatten()
+        if budget > 0 and cand.numel():
+            self.cache.prefetch(cand, limit=budget)
+
+    def _update_hints(self, logits, values, pos, end):
+        self.offset[0] = ops.reference.prefetch_hint(logits[:, :end])
+        if logits.shape[0] == 1 and end >= 32768:
+            self.offset[1] = ops.reference.decode_hint(self.offset[1], values[0, -1])
+
+    def reset(self):
+        self.cache.reset()
+        self.offset.zero_()
+
+
+def _order_bins(x: torch.Tensor) -> torch.Tensor:
+    """256 monotone bins of FP16-ordered values (upper 8 bits of an order-preserving key)."""
+    h = x.clamp(-65504, 65504).half().view(torch.int16).int()
+    key = torch.where(h < 0, (~h) & 0xFFFF, h | 0x8000)
+    return (key >> 8).clamp(0, 255) + 1

@@ -1,0 +1,339 @@
+"""DeepSeek-V3.2 model: embedding -> DSA blocks -> final norm -> last-token LM head.
+
+Reference: ``models/deepseek_v32/model.py:63-980`` (model + transactional
+forward), ``layers.py:215-344`` (block), ``layers.py:54-212`` (MLP / MoE).
+
+One forward call is one cache *step* for every layer: ``begin_step`` on all
+layer caches, the tokens run through the blocks in chunks of ``chunk_size``
+(prefill) and the step is committed only when every chunk succeeded;
+otherwise every layer rolls back and all cleanup errors are collected in one
+``BaseExceptionGroup`` (reference: ``model.py:778-814``).  A *transient*
+forward (candidate tokens of a GR request) writes KV only to the pool's GPU
+tail rows and is always discarded afterwards.
+
+The extend step can be captured once into a CUDA graph (:meth:`capture_extend`)
+and replayed per request, like the reference's full extend graph
+(``models/deepseek_v32/execution/extend_graph.py``).
+"""
+
+from __future__ import annotations
+
+from contextlib import nullcontext
+from dataclasses import dataclass
+
+import torch
+
+from ... import ops
+from ...cache.sparse_token_cache import SparseTokenCache
+from ...cache.sparse_token_pool import SharedSparseTokenPool
+from ...config import CacheConfig, ModelConfig
+from .attention import AttentionRunner
+from .weights import MLPWeights, MoEWeights, load_attention, load_mlp, load_moe
+
+
+class DenseMLP:
+    def __init__(self, w: MLPWeights):
+        self.w = w
+
+    def __call__(self, normed, quantized):
+        packed = self.w.gate_up(normed, quantized=quantized)
+        h, q, s_t = ops.silu_mul_quant(packed)
+        return self.w.down(h, quantized=(q, s_t))
+
+
+class MoE:
+    """Routed experts (sigmoid group-limited top-k) plus the shared expert.
+
+    Single-GPU path: tokens are grouped per expert and each expert runs the
+    FP8 GEMM kernels on its contiguous slice.  The expert-parallel fused
+    dispatch/combine lives in :mod:`cxldsagr_b200.parallel.ep`.
+    """
+
+    def __init__(self, cfg: ModelConfig, w: MoEWeights):
+        self.cfg, self.w = cfg, w
+        self.shared = DenseMLP(w.shared) if w.shared is not None else None
+
+    def __call__(self, normed, quantized):
+        cfg, w = self.cfg, self.w
+        ids, weights = ops.route_experts(normed, w.gate, w.bias, cfg)
+        out = torch.zeros(normed.shape, dtype=torch.float32, device=normed.device)
+        flat = ids.reshape(-1)
+        order = torch.argsort(flat, stable=True)
+        counts = torch.bincount(flat, minlength=cfg.n_routed_experts).tolist()
+        token = order // cfg.num_experts_per_tok
+        start = 0
+        I = cfg.moe_intermediate_size
+        for e, n in enumerate(counts):
+            if n == 0:
+                continue
+            sel = order[start:start + n]
+            start += n
+            j = e - w.experts.start
+            if not 0 <= j < len(w.experts):
+                continue
+            rows = token[start - n:start]
+            x = normed[rows]
+            if w.s_gate_up is not None:
+                packed = ops.fp8_linear(x, w.w_gate_up[j], w.s_gate_up[j])
+                h, q, s_t = ops.silu_mul_quant(packed)
+                y = ops.fp8_gemm(q, s_t, w.w_down[j], w.s_down[j])
+            else:
+                packed = ops.linear(x, w.w_gate_up[j])
+                h = ops.silu_mul(packed[:, :I], packed[:, I:])
+                y = ops.linear(h, w.w_down[j])
+            wt = weights.reshape(-1)[sel]
+            out.index_add_(0, rows, y.float() * wt[:, None])
+        if self.shared is not None:
+            out += self.shared(normed, quantized).float()
+        return out.bfloat16()
+
+
+class Block:
+    def __init__(self, cfg: ModelConfig, layer: int, attention: AttentionRunner, mlp, post_norm):
+        self.cfg, self.layer = cfg, layer
+        self.attention = attention
+        self.mlp = mlp
+        self.post_norm = post_norm
+
+    def forward(self, hidden, residual, pos, positions, freqs, *, scope=None, logits_buf=None):
+        cfg = self.cfg
+        scope = scope or (lambda _n: nullcontext())
+        with scope("input_residual_norm"):
+            normed, summed, q8, s8 = ops.norm_quant(hidden, residual, self.attention.w.input_norm, cfg.norm_eps)
+        attn = self.attention.forward(normed, (q8, s8), pos, positions, freqs, scope=scope, logits_buf=logits_buf)
+        with scope("post_attention_residual_norm"):
+            normed2, out_res, q2, s2 = ops.norm_quant(summed, attn, self.post_norm, cfg.norm_eps)
+        with scope("moe" if isinstance(self.mlp, MoE) else "dense_mlp"):
+            out = self.mlp(normed2, (q2, s2))
+        return out, out_res
+
+
+@dataclass
+class ForwardResult:
+    logits: torch.Tensor      # fp32 [1, vocab] of the last token
+    start: int
+    length: int
+
+
+class DeepSeekV32Model:
+    """A contiguous range of DeepSeek-V3.2 layers with embedding, final norm and LM head.
+
+    ``source`` provides checkpoint tensors (:class:`CheckpointReader` or
+    :class:`StateDictSource`).  ``cache`` chooses the KV method and sizes;
+    offload methods share one :class:`SharedSparseTokenPool` across layers.
+    """
+
+    def __init__(self, cfg: ModelConfig, source, *, device="cuda", cache: CacheConfig | None = None,
+                 layers=None, pool: SharedSparseTokenPool | None = None, scope=None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.cache_cfg = cache or CacheConfig(capacity=4096)
+        self.layer_ids = list(range(cfg.num_hidden_layers) if layers is None else layers)
+        self.scope = scope
+        cc = self.cache_cfg
+        dev = self.device
+        self.embed_table = source.get_tensor("model.embed_tokens.weight").to(dev, torch.bfloat16).contiguous()
+        self.final_norm = source.get_tensor("model.norm.weight").to(dev, torch.float32).contiguous()
+        self.lm_head = source.get_tensor("lm_head.weight").to(dev, torch.bfloat16).contiguous()
+        self.freqs = ops.reference.rotary_frequencies(cfg, device=dev)
+        width = cfg.qk_head_dim
+        self.pool = pool
+        self.session = None
+        if cc.offload and pool is None:
+            P = cc.pool_tokens or min(cc.capacity, 65536)
+            host = cc.host_tokens or cc.capacity
+            host = (host + 63) // 64 * 64
+            self.pool = SharedSparseTokenPool(host, width, len(self.layer_ids), P, device=dev,
+                                              candidate_slots=cc.candidate_tokens)
+        if cc.offload:
+            self.session = self.pool.allocate_session(cc.capacity)
+        self.blocks: list[Block] = []
+        for i, layer in enumerate(self.layer_ids):
+            if cc.offload:
+                kv_cache = self.session.layer(i)
+            else:
+                kv_cache = SparseTokenCache(cc.capacity, width, device=dev, candidate_slots=cc.candidate_tokens)
+            attn_w = load_attention(source, cfg, layer, device=dev)
+            runner = AttentionRunner(cfg, attn_w, kv_cache, method=cc.method,
+                                     index_capacity=cc.capacity + cc.candidate_tokens)
+            if cfg.is_moe_layer(layer):
+                mlp = MoE(cfg, load_moe(source, cfg, layer, device=dev))
+            else:
+                mlp = DenseMLP(load_mlp(source, cfg, f"model.layers.{layer}.mlp", device=dev))
+            post = source.get_tensor(f"model.layers.{layer}.post_attention_layernorm.weight").to(dev, torch.float32)
+            self.blocks.append(Block(cfg, layer, runner, mlp, post.contiguous()))
+        self.length = 0
+        self._logits_buf = None
+        self.poisoned = False
+
+    # -------------------------------------------------------------- helpers
+    @property
+    def caches(self):
+        return [b.attention.cache for b in self.blocks]
+
+    def _scope(self):
+        return self.scope or (lambda _n: nullcontext())
+
+    def _ensure_logits_buf(self, rows, cols):
+        if not self.device.type == "cuda":
+            return None
+        cols = (cols + 3) // 4 * 4
+        buf = self._logits_buf
+        if buf is None or buf.shape[0] < rows or buf.shape[1] < cols:
+            cap_cols = max(cols, (self.cache_cfg.capacity + self.cache_cfg.candidate_tokens + 3) // 4 * 4)
+            buf = torch.empty((max(rows, self.cache_cfg.chunk_size), cap_cols), dtype=torch.float32, device=self.device)
+            self._logits_buf = buf
+        return buf
+
+    # ------------------------------------------------------------- forward
+    def _body(self, ids: torch.Tensor, start: int, chunk: int):
+        cfg = self.cfg
+        scope = self._scope()
+        T = ids.numel()
+        out_h, out_r = None, None
+        for c0 in range(0, T, chunk):
+            c1 = min(T, c0 + chunk)
+            pos = start + c0
+            positions = torch.arange(pos, start + c1, device=self.device, dtype=torch.float32)
+            with scope("embedding"):
+                hidden = ops.embed(ids[c0:c1], self.embed_table)
+            residual = None
+            logits_buf = self._ensure_logits_buf(c1 - c0, start + c1)
+            for block in self.blocks:
+                hidden, residual = block.forward(hidden, residual, pos, positions, self.freqs,
+                                                 scope=scope, logits_buf=logits_buf)
+            out_h, out_r = hidden, residual
+        with scope("final_norm_lm_head"):
+            last, _ = ops.residual_rms_norm(out_h[-1:], out_r[-1:], self.final_norm, cfg.norm_eps)
+            logits = ops.linear(last, self.lm_head).float() if not self.device.type == "cuda" else self._lm_head(last)
+        return logits
+
+    def _lm_head(self, last):
+        out = torch.empty((last.shape[0], self.lm_head.shape[0]), dtype=torch.float32, device=self.device)
+        V, D = self.lm_head.shape
+        ops.lib().bf16_gemm(last.contiguous(), 0, D, 0, self.lm_head, 0, D, 0, out, 0, V, 0, last.shape[0], V, D, 1)
+        return out
+
+    def forward(self, ids, *, transient: bool = False, chunk_size: int | None = None, commit: bool = True):
+        """Run ``ids`` after the committed history; returns last-token logits.
+
+        ``transient``: candidate tokens (GR); their KV lives only in the GPU
+        tail rows and is discarded (history length unchanged).
+        """
+        if self.poisoned:
+            raise RuntimeError("model is poisoned after a failed cleanup")
+        ids = ids.to(self.device).reshape(-1)
+        T = ids.numel()
+        if T == 0:
+            raise ValueError("empty token batch")
+        start = self.length
+        for c in self.caches:
+            (c.begin_transient if transient else c.begin_step)(T)
+        chunk = chunk_size or self.cache_cfg.chunk_size
+        if transient and any(c.offload for c in self.caches):
+            chunk = T  # candidate rows are one batch
+        try:
+            logits = self._body(ids, start, chunk)
+        except BaseException as primary:
+            errors = []
+            for c in self.caches:
+                try:
+                    c.rollback()
+                except BaseException as exc:  # noqa: BLE001 - keep every cleanup failure
+                    errors.append(exc)
+            if errors:
+                self.poisoned = True
+                raise BaseExceptionGroup("forward and cache rollback failed", [primary, *errors]) from None
+            raise
+        if transient:
+            for c in self.caches:
+                c.discard_transient()
+        elif commit:
+            for c in self.caches:
+                c.commit()
+            self.length = start + T
+        return ForwardResult(logits, start, T)
+
+    prefill = forward
+
+    def extend(self, ids, **kw):
+        return self.forward(ids, **kw)
+
+    def candidate(self, ids):
+        return self.forward(ids, transient=True)
+
+    def truncate(self, length: int):
+        for c in self.caches:
+            c.truncate(length)
+        self.length = length
+
+    def reset(self):
+        for b in self.blocks:
+            b.attention.reset()
+        self.length = 0
+
+    # --------------------------------------------------------- CUDA graph
+    def capture_extend(self, T: int, *, warmup: int = 2) -> "ExtendGraph":
+        """Capture a T-token extend at the current history length into a CUDA graph."""
+        return ExtendGraph(self, T, warmup=warmup)
+
+
+class ExtendGraph:
+    """One CUDA graph for a whole T-token extend step of the resident (hbm) method.
+
+    Each replay re-opens the cache step on the host (cheap bookkeeping), copies
+    the token ids into the static input and launches the graph; the caller
+    commits with :meth:`commit` or discards with :meth:`rollback`.
+    """
+
+    def __init__(self, model: DeepSeekV32Model, T: int, *, warmup: int = 2):
+        if model.cache_cfg.offload:
+            raise ValueError("graph capture covers the resident (hbm) cache method")
+        self.model, self.T = model, T
+        self.start = model.length
+        dev = model.device
+        self.static_ids = torch.zeros(T, dtype=torch.int64, device=dev)
+        model._ensure_logits_buf(T, self.start + T)
+        stream = torch.cuda.Stream(device=dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                model.forward(self.static_ids, commit=False)
+                self._rewind()
+        torch.cuda.current_stream(dev).wait_stream(stream)
+        self.graph = torch.cuda.CUDAGraph()
+        for c in model.caches:
+            c.begin_step(T)
+        from ...ops.native import launch_count
+
+        n0 = launch_count()
+        with torch.cuda.graph(self.graph, stream=stream):
+            self.static_logits = model._body(self.static_ids, self.start, T)
+        self.launches_per_replay = launch_count() - n0
+        model._graph_launches = self.launches_per_replay
+        self._rewind()
+
+    def _rewind(self):
+        for c in self.model.caches:
+            c._step_end = None
+            c.written = c.length = self.start
+        self.model.length = self.start
+
+    def replay(self, ids: torch.Tensor):
+        m = self.model
+        if m.length != self.start:
+            raise RuntimeError("extend graph was captured at another history length")
+        self.static_ids.copy_(ids.reshape(-1), non_blocking=True)
+        for c in m.caches:
+            c.begin_step(self.T)
+            c.written = self.start + self.T
+        self.graph.replay()
+        return self.static_logits
+
+    def commit(self):
+        for c in self.model.caches:
+            c.commit()
+        self.model.length = self.start + self.T
+
+    def rollback(self):
+        self._rewind()

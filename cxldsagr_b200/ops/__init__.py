@@ -198,13 +198,15 @@ def exact_topk(scores, k: int, *, causal_start: int | None = None, n: int | None
 
 
 # ------------------------------------------------------------- attention
-def sparse_mla(q, kv, ids, scale, *, splits: int = 1, return_lse: bool = False):
+def sparse_mla(q, kv, ids, scale, *, splits: int = 1, return_lse: bool = False, value_dim: int = 512):
     """Sparse MLA: q [T,H,576], kv [P,576], ids [T,K] -> [T,H,512] (BF16)."""
     if not _cuda(q):
         if return_lse:
-            o, lse = reference.sparse_mla_lse(q, kv, ids, scale)
+            o, lse = reference.sparse_mla_lse(q, kv, ids, scale, value_dim)
             return o.to(q.dtype), lse
-        return reference.sparse_mla(q, kv, ids, scale)
+        return reference.sparse_mla(q, kv, ids, scale, value_dim)
+    if value_dim != 512 or q.shape[-1] != 576:
+        raise ValueError("the sm_100a sparse MLA kernel covers the V3.2 shape (576 / 512)")
     T, H, _ = q.shape
     out = torch.empty((T, H, 512), dtype=torch.bfloat16, device=q.device)
     lse = torch.empty((T, H), dtype=torch.float32, device=q.device) if return_lse else None
@@ -246,3 +248,80 @@ route_experts = reference.route_experts
 
 def attention_scale_log2(scale: float) -> float:
     return scale * math.log2(math.e)
+
+
+# ------------------------------------------------- projection epilogues
+def _angles(freqs, positions):
+    return positions.float()[:, None] * freqs[None, :].float()
+
+
+def mla_q_rope(b, H, nope, rope, freqs, positions, q_proj, latent):
+    """q_proj[:, h, latent:] = interleaved-RoPE(b[:, h*(nope+rope)+nope : ...])."""
+    T = q_proj.shape[0]
+    if not _cuda(b):
+        qpe = b[:, : H * (nope + rope)].reshape(T, H, nope + rope)[..., nope:]
+        q_proj[..., latent:] = reference.apply_rope(qpe, _angles(freqs, positions), interleaved=True)
+        return
+    lib().mla_q_rope(b, b.stride(0), T, H, nope, rope, freqs, positions, q_proj, q_proj.stride(0), q_proj.stride(1), latent)
+
+
+def kv_finish(kv, L, R, norm_w, eps, freqs, positions, records, rows):
+    """records[rows] = [rmsnorm(kv[:, :L]) || interleaved-RoPE(kv[:, L:L+R])]."""
+    if not _cuda(kv):
+        lat = reference.rms_norm(kv[:, :L], norm_w, eps)
+        pe = reference.apply_rope(kv[:, L:L + R], _angles(freqs, positions), interleaved=True)
+        records[rows.long()] = torch.cat((lat, pe), -1).to(records.dtype)
+        return
+    lib().kv_finish(kv, L, R, norm_w, eps, freqs, positions, records, rows.long())
+
+
+def index_k(ik, R, ln_w, ln_b, eps, freqs, positions, k_out, s_out):
+    """Indexer key: LayerNorm(+bias) -> BF16 -> split-half RoPE -> UE8M0 FP8 (into k_out/s_out)."""
+    if not _cuda(ik):
+        k = reference.layer_norm(ik, ln_w, ln_b, eps).bfloat16()
+        k = reference.apply_rope(k, _angles(freqs, positions), interleaved=False)
+        q, s = reference.quantize_index(k)
+        k_out.copy_(q)
+        s_out.copy_(s[:, 0])
+        return
+    lib().index_k(ik, R, ln_w, ln_b, eps, freqs, positions, k_out, s_out)
+
+
+def index_q(iq, heads, dim, R, freqs, positions, w_raw, head_scale):
+    """Indexer query: split-half RoPE + per-head UE8M0 FP8; weights = raw * head_scale * q_scale."""
+    T = iq.shape[0]
+    if not _cuda(iq):
+        q = reference.apply_rope(iq[:, : heads * dim].reshape(T, heads, dim), _angles(freqs, positions), interleaved=False)
+        qq, qs = reference.quantize_index(q)
+        return qq, (w_raw * head_scale * qs[..., 0]).contiguous()
+    qq = torch.empty((T, heads, dim), dtype=FP8, device=iq.device)
+    qs = torch.empty((T, heads), dtype=torch.float32, device=iq.device)
+    w = torch.empty((T, heads), dtype=torch.float32, device=iq.device)
+    lib().index_q(iq, iq.stride(0), T, heads, dim, R, freqs, positions, qq, qs, w_raw.contiguous(), head_scale, w)
+    return qq, w
+
+
+def mla_absorb(b, H, nope, rope, wk_b_t, q_proj):
+    """q_proj[:, h, :L] = b_nope[:, h] @ wk_b_t[h]^T  (W_UK absorption, BF16 GEMM per head)."""
+    T = q_proj.shape[0]
+    L = wk_b_t.shape[1]
+    if not _cuda(b):
+        qn = b[:, : H * (nope + rope)].reshape(T, H, nope + rope)[..., :nope].float()
+        q_proj[..., :L] = torch.einsum("thn,hln->thl", qn, wk_b_t.float()).to(q_proj.dtype)
+        return
+    if not b.is_contiguous():
+        raise ValueError("absorb input must be the contiguous projection output")
+    lib().bf16_gemm(b, 0, b.stride(0), nope + rope, wk_b_t, 0, nope, L * nope,
+                    q_proj, 0, q_proj.stride(0), q_proj.stride(1), T, L, nope, H)
+
+
+def mla_expand(attn, wv_b):
+    """out[:, h] = attn[:, h] @ wv_b[h]^T : [T,H,L] x [H,V,L] -> [T,H,V] (BF16)."""
+    T, H, L = attn.shape
+    V = wv_b.shape[1]
+    if not _cuda(attn):
+        return torch.einsum("thl,hvl->thv", attn.float(), wv_b.float()).to(torch.bfloat16)
+    out = torch.empty((T, H, V), dtype=torch.bfloat16, device=attn.device)
+    attn = attn.contiguous()
+    lib().bf16_gemm(attn, 0, H * L, L, wv_b, 0, L, V * L, out, 0, H * V, V, T, V, L, H)
+    return out

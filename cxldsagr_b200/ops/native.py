@@ -16,6 +16,35 @@ class NativeUnavailable(RuntimeError):
     pass
 
 
+# Entry points that launch more than one kernel per call.
+_MULTI_LAUNCH = {"sparse_mla": lambda args: 2 if len(args) > 6 and int(args[6]) > 1 else 1}
+_NO_LAUNCH = {"error_word", "sparse_mla_scratch_bytes"}
+
+
+class _CountingLib:
+    """Proxy of the extension that counts kernel launches issued from Python.
+
+    ``launches`` counts every native kernel launch (a CUDA-graph replay
+    re-issues the launches recorded while it was captured).
+    """
+
+    def __init__(self, mod):
+        self._mod = mod
+        self.launches = 0
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if name in _NO_LAUNCH or not callable(fn):
+            return fn
+        multi = _MULTI_LAUNCH.get(name)
+
+        def call(*args):
+            self.launches += multi(args) if multi else 1
+            return fn(*args)
+
+        return call
+
+
 @functools.cache
 def lib():
     try:
@@ -24,7 +53,11 @@ def lib():
         raise NativeUnavailable(
             "the sm_100a extension is not built; run `python setup.py build_ext --inplace`"
         ) from exc
-    return _C
+    return _CountingLib(_C)
+
+
+def launch_count() -> int:
+    return lib().launches
 
 
 def available() -> bool:
