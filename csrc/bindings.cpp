@@ -152,7 +152,8 @@ void kv_finish(const Tensor& kv, int64_t L, int64_t R, const Tensor& norm_w, dou
   const int64_t* dr = nullptr;
   if (dst_row && dst_row->defined()) { CHECK_DTYPE((*dst_row), torch::kInt64); dr = cptr<int64_t>(*dst_row); }
   b200::launch_kv_finish(cptr<__nv_bfloat16>(kv), kv.stride(0), kv.size(0), L, R, cptr<float>(norm_w), float(eps),
-                         cptr<float>(freqs), cptr<float>(positions), ptr<__nv_bfloat16>(out), out.stride(0), dr, stream());
+                         cptr<float>(freqs), cptr<float>(positions), ptr<__nv_bfloat16>(out), out.stride(0), dr,
+                         out.size(0), err_ptr(kv), stream());
 }
 
 void index_k(const Tensor& k, int64_t R, const Tensor& ln_w, const Tensor& ln_b, double eps, const Tensor& freqs,
@@ -215,7 +216,7 @@ void topk(const Tensor& scores, int64_t N, int64_t k, int64_t causal_start, Tens
   TORCH_CHECK(N <= scores.size(1), "topk: N exceeds scores width");
   c10::cuda::CUDAGuard g(scores.device());
   b200::launch_topk_causal(cptr<float>(scores), scores.stride(0), scores.size(0), N, k, causal_start,
-                           ptr<float>(values), ptr<int>(ids), stream());
+                           ptr<float>(values), ptr<int>(ids), err_ptr(scores), stream());
 }
 
 // ------------------------------------------------------------- attention

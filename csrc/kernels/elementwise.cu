@@ -233,11 +233,16 @@ __global__ void kv_finish_kernel(const __nv_bfloat16* __restrict__ kv, int64_t l
                                  const float* __restrict__ freqs,
                                  const float* __restrict__ positions,
                                  __nv_bfloat16* __restrict__ out, int64_t ldo,
-                                 const int64_t* __restrict__ dst_row) {
+                                 const int64_t* __restrict__ dst_row, int64_t out_rows, int* err) {
   __shared__ float red[4];
   const int t = blockIdx.x;
   const __nv_bfloat16* src = kv + t * ldkv;
-  __nv_bfloat16* dst = out + (dst_row ? dst_row[t] : int64_t(t)) * ldo;
+  const int64_t drow = dst_row ? dst_row[t] : int64_t(t);
+  if (drow < 0 || drow >= out_rows) {  // never write outside the record table
+    if (threadIdx.x == 0) record_error(err, kErrBadIndex);
+    return;
+  }
+  __nv_bfloat16* dst = out + drow * ldo;
   float ss = 0.f;
   for (int i = threadIdx.x; i < L; i += blockDim.x) {
     const float v = __bfloat162float(src[i]);
@@ -439,9 +444,10 @@ void launch_mla_q_rope(const __nv_bfloat16* q, int64_t ldq, int T, int H, int no
 void launch_kv_finish(const __nv_bfloat16* kv, int64_t ldkv, int T, int L, int R,
                       const float* norm_w, float eps, const float* freqs,
                       const float* positions, __nv_bfloat16* out, int64_t ldo,
-                      const int64_t* dst_row, cudaStream_t stream) {
+                      const int64_t* dst_row, int64_t out_rows, int* err, cudaStream_t stream) {
   if (T <= 0) return;
-  kv_finish_kernel<<<T, 128, 0, stream>>>(kv, ldkv, T, L, R, norm_w, eps, freqs, positions, out, ldo, dst_row);
+  kv_finish_kernel<<<T, 128, 0, stream>>>(kv, ldkv, T, L, R, norm_w, eps, freqs, positions, out, ldo, dst_row,
+                                          out_rows, err);
   cuda_check(cudaGetLastError(), "kv_finish launch");
 }
 

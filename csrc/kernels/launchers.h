@@ -83,7 +83,7 @@ void launch_mla_q_rope(const __nv_bfloat16* q, int64_t ldq, int T, int H, int no
 void launch_kv_finish(const __nv_bfloat16* kv, int64_t ldkv, int T, int L, int R,
                       const float* norm_w, float eps, const float* freqs,
                       const float* positions, __nv_bfloat16* out, int64_t ldo,
-                      const int64_t* dst_row, cudaStream_t stream);
+                      const int64_t* dst_row, int64_t out_rows, int* err, cudaStream_t stream);
 
 // Indexer key: k = bf16(layernorm(x) * w + b); rope split-half on the first R
 // dims; quantise the 128-d row (UE8M0) -> k_q [t], k_scale [t].
@@ -123,10 +123,10 @@ void launch_indexer_logits(const IndexerArgs& a, cudaStream_t stream);
 // Exact descending top-k per row of FP32 scores [R, N] (row pitch ld), ties to
 // the smaller index, -1 ids for non-finite values.  k <= 2048.
 void launch_topk(const float* scores, int64_t ld, int R, int N, int k, float* values, int* ids,
-                 cudaStream_t stream);
+                 int* err, cudaStream_t stream);
 // Same, with row r reading only columns [0, min(N, causal_start + r + 1)).
 void launch_topk_causal(const float* scores, int64_t ld, int R, int N, int k, int causal_start,
-                        float* values, int* ids, cudaStream_t stream);
+                        float* values, int* ids, int* err, cudaStream_t stream);
 
 // --------------------------------------------------------------- sparse MLA
 struct MLAArgs {

@@ -36,7 +36,7 @@ __device__ __forceinline__ float key_value(uint32_t k) {
 __global__ void __launch_bounds__(kThreads) topk_kernel(const float* __restrict__ scores, int64_t ld,
                                                         int N, int k, int causal_start,
                                                         float* __restrict__ values,
-                                                        int* __restrict__ ids) {
+                                                        int* __restrict__ ids, int* err) {
   __shared__ uint32_t hist[256];
   __shared__ uint64_t cand[kMaxK];
   __shared__ uint32_t s_prefix, s_krem, s_count, s_running;
@@ -54,6 +54,7 @@ __global__ void __launch_bounds__(kThreads) topk_kernel(const float* __restrict_
     s_count = 0;
     s_running = 0;
   }
+  __syncthreads();  // every path below reads or atomically updates these
   uint32_t prefix = 0;
   uint32_t krem = take;
   // --- radix select (skipped when every candidate is taken)
@@ -109,7 +110,8 @@ __global__ void __launch_bounds__(kThreads) topk_kernel(const float* __restrict_
     }
     if (gt) {
       const uint32_t pos = atomicAdd(&s_count, 1u);
-      cand[pos] = (uint64_t(key) << 32) | uint32_t(0xFFFFFFFFu - uint32_t(i));
+      if (pos < uint32_t(kMaxK)) cand[pos] = (uint64_t(key) << 32) | uint32_t(0xFFFFFFFFu - uint32_t(i));
+      else record_error(err, kErrBadIndex);
     }
     if (!take_all) {
       // ordered rank of `eq` flags within this chunk
@@ -122,7 +124,8 @@ __global__ void __launch_bounds__(kThreads) topk_kernel(const float* __restrict_
       before += __popc(ballot & ((1u << lane) - 1u));
       if (eq && before < krem) {
         const uint32_t pos = atomicAdd(&s_count, 1u);
-        cand[pos] = (uint64_t(key) << 32) | uint32_t(0xFFFFFFFFu - uint32_t(i));
+        if (pos < uint32_t(kMaxK)) cand[pos] = (uint64_t(key) << 32) | uint32_t(0xFFFFFFFFu - uint32_t(i));
+        else record_error(err, kErrBadIndex);
       }
       __syncthreads();
       if (threadIdx.x == 0) {
@@ -134,7 +137,7 @@ __global__ void __launch_bounds__(kThreads) topk_kernel(const float* __restrict_
     }
   }
   __syncthreads();
-  const int count = int(s_count);  // == take
+  const int count = min(int(s_count), kMaxK);  // == take
   int n2 = 1;
   while (n2 < count) n2 <<= 1;
   for (int i = count + threadIdx.x; i < n2; i += kThreads) cand[i] = 0ull;
@@ -174,15 +177,15 @@ __global__ void __launch_bounds__(kThreads) topk_kernel(const float* __restrict_
 }  // namespace
 
 void launch_topk(const float* scores, int64_t ld, int R, int N, int k, float* values, int* ids,
-                 cudaStream_t stream) {
-  launch_topk_causal(scores, ld, R, N, k, -1, values, ids, stream);
+                 int* err, cudaStream_t stream) {
+  launch_topk_causal(scores, ld, R, N, k, -1, values, ids, err, stream);
 }
 
 void launch_topk_causal(const float* scores, int64_t ld, int R, int N, int k, int causal_start,
-                        float* values, int* ids, cudaStream_t stream) {
+                        float* values, int* ids, int* err, cudaStream_t stream) {
   if (R <= 0) return;
   if (k < 1 || k > kMaxK) throw std::invalid_argument("topk: k must be in [1, 2048]");
-  topk_kernel<<<R, kThreads, 0, stream>>>(scores, ld, N, k, causal_start, values, ids);
+  topk_kernel<<<R, kThreads, 0, stream>>>(scores, ld, N, k, causal_start, values, ids, err);
   cuda_check(cudaGetLastError(), "topk launch");
 }
 
