@@ -44,6 +44,7 @@ def parse():
     p.add_argument("--layers", type=int, default=3)
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--e2e-steps", type=int, default=2)
+    p.add_argument("--profile", action="store_true", help="print a per-scope device-time breakdown to stderr")
     return p.parse_args()
 
 
@@ -129,6 +130,19 @@ def main():
         step()
     barrier()
     ops.check_errors(dev)
+    if args.profile:
+        from cxldsagr_b200.utils.tracing import EventScope
+
+        scope = EventScope(dev)
+        model.scope = scope
+        model.reset()
+        model.prefill(hist)
+        prefill_scopes = scope.summary()
+        scope.reset()
+        model.extend(ext)
+        extend_scopes = scope.summary()
+        model.scope = None
+        print(json.dumps({"profile_prefill": prefill_scopes, "profile_extend_eager": extend_scopes}), file=sys.stderr)
 
     launches0 = launch_count()
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]

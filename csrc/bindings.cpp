@@ -169,9 +169,10 @@ void index_q(const Tensor& q, int64_t ldq, int64_t T, int64_t H, int64_t D, int6
              Tensor& weights) {
   CHECK_CUDA(q); CHECK_DTYPE(q, torch::kBFloat16); CHECK_DTYPE(q_q, torch::kFloat8_e4m3fn);
   c10::cuda::CUDAGuard g(q.device());
+  TORCH_CHECK(w_raw.is_contiguous() && (w_raw.size(-1) == H || w_raw.size(-1) == 2 * H), "index_q: w_raw");
   b200::launch_index_q(cptr<__nv_bfloat16>(q), ldq, T, H, D, R, cptr<float>(freqs), cptr<float>(positions),
-                       ptr<uint8_t>(q_q), ptr<float>(q_scale), cptr<float>(w_raw), float(head_scale),
-                       ptr<float>(weights), stream());
+                       ptr<uint8_t>(q_q), ptr<float>(q_scale), cptr<float>(w_raw), w_raw.size(-1) == 2 * H ? 1 : 0,
+                       float(head_scale), ptr<float>(weights), stream());
 }
 
 void linear_f32(const Tensor& x, const Tensor& W, Tensor& out) {
@@ -221,7 +222,8 @@ void topk(const Tensor& scores, int64_t N, int64_t k, int64_t causal_start, Tens
 
 // ------------------------------------------------------------- attention
 void sparse_mla(const Tensor& q, const Tensor& kv, const Tensor& ids, double scale, Tensor& out,
-                const c10::optional<Tensor>& lse, int64_t splits, const c10::optional<Tensor>& scratch) {
+                const c10::optional<Tensor>& lse, int64_t splits, const c10::optional<Tensor>& scratch,
+                int64_t impl) {
   CHECK_CUDA(q); CHECK_DTYPE(q, torch::kBFloat16); CHECK_DTYPE(kv, torch::kBFloat16); CHECK_DTYPE(ids, torch::kInt32);
   CHECK_DTYPE(out, torch::kBFloat16);
   TORCH_CHECK(q.dim() == 3 && q.size(2) == 576 && q.is_contiguous(), "sparse_mla: q [T,H,576]");
@@ -239,7 +241,8 @@ void sparse_mla(const Tensor& q, const Tensor& kv, const Tensor& ids, double sca
     TORCH_CHECK(size_t(scratch->numel()) * 4 >= b200::sparse_mla_scratch_bytes(a.T, a.H, splits), "sparse_mla: scratch too small");
     sp = ptr<float>(*scratch);
   }
-  b200::launch_sparse_mla_split(a, int(splits), sp, stream());
+  if (impl == 0 || impl >= 16) b200::launch_sparse_mla_tc(a, int(splits), sp, stream(), impl >= 16 ? int(impl - 16) : 0);
+  else b200::launch_sparse_mla_split(a, int(splits), sp, stream());
 }
 
 int64_t sparse_mla_scratch_bytes(int64_t T, int64_t H, int64_t splits) {

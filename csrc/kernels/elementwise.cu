@@ -324,7 +324,7 @@ __global__ void index_q_kernel(const __nv_bfloat16* __restrict__ q, int64_t ldq,
                                int D, int R, const float* __restrict__ freqs,
                                const float* __restrict__ positions, uint8_t* __restrict__ q_q,
                                float* __restrict__ q_scale, const float* __restrict__ w_raw,
-                               float head_scale, float* __restrict__ weights) {
+                               int w_split, float head_scale, float* __restrict__ weights) {
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (gw >= T * H) return;
@@ -348,7 +348,10 @@ __global__ void index_q_kernel(const __nv_bfloat16* __restrict__ q, int64_t ldq,
   const float sc = quant_group_warp(out, q_q + (int64_t(t) * H + h) * D);
   if (lane == 0) {
     q_scale[t * H + h] = sc;
-    weights[t * H + h] = w_raw[t * H + h] * head_scale * sc;
+    // w_raw row t holds H values, or 2H (hi || lo split-precision partials).
+    const float raw = w_split ? w_raw[int64_t(t) * 2 * H + h] + w_raw[int64_t(t) * 2 * H + H + h]
+                              : w_raw[int64_t(t) * H + h];
+    weights[t * H + h] = raw * head_scale * sc;
   }
 }
 
@@ -462,11 +465,11 @@ void launch_index_k(const __nv_bfloat16* k, int64_t ldk, int T, int D, int R,
 
 void launch_index_q(const __nv_bfloat16* q, int64_t ldq, int T, int H, int D, int R,
                     const float* freqs, const float* positions, uint8_t* q_q, float* q_scale,
-                    const float* w_raw, float head_scale, float* weights, cudaStream_t stream) {
+                    const float* w_raw, int w_split, float head_scale, float* weights, cudaStream_t stream) {
   if (T <= 0) return;
   if (D != 128) throw std::invalid_argument("index_q: head dim must be 128");
   const int64_t warps = int64_t(T) * H;
-  index_q_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(q, ldq, T, H, D, R, freqs, positions, q_q, q_scale, w_raw, head_scale, weights);
+  index_q_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(q, ldq, T, H, D, R, freqs, positions, q_q, q_scale, w_raw, w_split, head_scale, weights);
   cuda_check(cudaGetLastError(), "index_q launch");
 }
 

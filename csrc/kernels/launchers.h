@@ -92,10 +92,12 @@ void launch_index_k(const __nv_bfloat16* k, int64_t ldk, int T, int D, int R,
                     const float* positions, uint8_t* k_q, float* k_scale, cudaStream_t stream);
 
 // Indexer query: rope split-half + per-(t,h) quantisation; weights[t,h] =
-// raw[t,h] * head_scale * q_scale[t,h].
+// raw[t,h] * head_scale * q_scale[t,h], with raw = w_raw[t,h] or, when
+// w_split, w_raw[t,h] + w_raw[t,H+h] (BF16 hi/lo partials of an FP32 product).
 void launch_index_q(const __nv_bfloat16* q, int64_t ldq, int T, int H, int D, int R,
                     const float* freqs, const float* positions, uint8_t* q_q, float* q_scale,
-                    const float* w_raw, float head_scale, float* weights, cudaStream_t stream);
+                    const float* w_raw, int w_split, float head_scale, float* weights,
+                    cudaStream_t stream);
 
 // FP32 x[T, K] (bf16 input) @ W[H, K]^T -> out fp32 [T, H].
 void launch_linear_f32(const __nv_bfloat16* x, int64_t ldx, const float* W, int T, int H, int K,
@@ -144,6 +146,11 @@ void launch_sparse_mla(const MLAArgs& a, cudaStream_t stream);
 // and LSE into `scratch` (sparse_mla_scratch_bytes) and a combine kernel merges.
 size_t sparse_mla_scratch_bytes(int T, int H, int splits);
 void launch_sparse_mla_split(const MLAArgs& a, int splits, float* scratch, cudaStream_t stream);
+// tcgen05 version (2-CTA clusters exchanging partial S through DSMEM).
+void launch_sparse_mla_tc(const MLAArgs& a, int splits, float* scratch, cudaStream_t stream, int dbg = 0);
+// out[t,h,:] = sum_s exp(lse_s - lse) * part_o[s,t,h,:]; lse = logsumexp_s lse_s.
+void launch_mla_combine(const float* part_o, const float* part_lse, int splits, int T, int H,
+                        __nv_bfloat16* out, float* lse, cudaStream_t stream);
 
 // ----------------------------------------------------------- KV transfer
 // records[slots[i]] = host[host_ids[i]] for i < n (width bytes per row), SM

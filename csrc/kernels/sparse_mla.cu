@@ -321,10 +321,13 @@ void launch_sparse_mla_split(const MLAArgs& a, int splits, float* scratch, cudaS
   sparse_mla_kernel<<<grid, kThreads, smem, stream>>>(a.q, a.kv, a.ids, a.T, a.H, a.K, a.P, scale_log2,
                                                        splits, a.out, part_o, part_lse, a.lse);
   cuda_check(cudaGetLastError(), "sparse_mla launch");
-  if (splits > 1) {
-    mla_combine_kernel<<<a.T * a.H, 128, 0, stream>>>(part_o, part_lse, splits, a.T, a.H, a.out, a.lse);
-    cuda_check(cudaGetLastError(), "mla_combine launch");
-  }
+  if (splits > 1) launch_mla_combine(part_o, part_lse, splits, a.T, a.H, a.out, a.lse, stream);
+}
+
+void launch_mla_combine(const float* part_o, const float* part_lse, int splits, int T, int H,
+                        __nv_bfloat16* out, float* lse, cudaStream_t stream) {
+  mla_combine_kernel<<<T * H, 128, 0, stream>>>(part_o, part_lse, splits, T, H, out, lse);
+  cuda_check(cudaGetLastError(), "mla_combine launch");
 }
 
 void launch_sparse_mla(const MLAArgs& a, cudaStream_t stream) { launch_sparse_mla_split(a, 1, nullptr, stream); }

@@ -1,0 +1,140 @@
+"""Per-operator microbenchmarks on one GPU (CUDA-event timing, warm-up,
+inputs larger than L2 or an explicit L2 flush between iterations).
+
+    python -m cxldsagr_b200.evaluation.kernel_bench --op sparse_mla --T 256
+    python -m cxldsagr_b200.evaluation.kernel_bench --op all
+
+Counterpart of the reference's operator observation harness
+(experiments/deepseek_v32_observation): each op reports device time per call,
+achieved FLOP/s or bytes/s and the fraction of the measured peaks in
+MEASURED_PEAKS.json when present (fallback 6.65 TB/s, 1.59 PFLOP/s bf16).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+from .. import ops
+from ..checkpoint import quantize_weight_blocks
+
+_L2_FLUSH = None
+
+
+def _peaks():
+    path = os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def flush_l2(dev):
+    global _L2_FLUSH
+    if _L2_FLUSH is None:
+        _L2_FLUSH = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    _L2_FLUSH.zero_()
+
+
+def time_fn(fn, *, warmup=3, iters=10, flush=True, dev="cuda"):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(iters):
+        if flush:
+            flush_l2(dev)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        total += s.elapsed_time(e)
+    return total / iters
+
+
+def bench_sparse_mla(T=256, K=2048, P=65664, splits=1, impl=0, locality=0.0, **_):
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = (torch.randn(T, 128, 576, device=dev, generator=g) * 0.5).bfloat16()
+    kv = (torch.randn(P, 576, device=dev, generator=g) * 0.5).bfloat16()
+    ids = torch.randint(0, P, (T, K), device=dev, dtype=torch.int32, generator=g)
+    if locality > 0:  # a shared hot set, like correlated top-k of neighbouring queries
+        hot = torch.randint(0, P, (K,), device=dev, dtype=torch.int32, generator=g)
+        mask = torch.rand(T, K, device=dev, generator=g) < locality
+        ids = torch.where(mask, hot[None, :].expand(T, K), ids)
+    ms = time_fn(lambda: ops.sparse_mla(q, kv, ids, 0.1, splits=splits, impl=impl))
+    flops = 2.0 * T * 128 * K * (576 + 512)
+    gather = T * K * 1152.0
+    pk = _peaks()
+    return {"op": "sparse_mla", "T": T, "K": K, "P": P, "splits": splits, "impl": impl, "ms": ms,
+            "tflops": flops / ms / 1e9, "frac_bf16_peak": flops / ms / 1e9 / pk["bf16_tflops"],
+            "gather_gbs": gather / ms / 1e6, "peaks": pk["source"]}
+
+
+def bench_fp8_gemm(M=1024, N=36864, K=7168, **_):
+    dev = "cuda"
+    x = torch.randn(M, K, device=dev).bfloat16()
+    w, s = quantize_weight_blocks(torch.randn(N, K, device=dev) * 0.02)
+    q, s_t = ops.quantize_act(x)
+    out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    ms = time_fn(lambda: ops.fp8_gemm(q, s_t, w, s, out=out))
+    flops = 2.0 * M * N * K
+    return {"op": "fp8_gemm", "M": M, "N": N, "K": K, "ms": ms, "tflops": flops / ms / 1e9,
+            "bytes_gbs": (N * K + M * K + M * N * 2) / ms / 1e6}
+
+
+def bench_indexer(Q=1024, N=65536, **_):
+    dev = "cuda"
+    q = (torch.randn(Q, 64, 128, device=dev) * 2).to(torch.float8_e4m3fn)
+    k = (torch.randn(N, 128, device=dev) * 2).to(torch.float8_e4m3fn)
+    w = torch.randn(Q, 64, device=dev)
+    ks = torch.rand(N, device=dev)
+    out = torch.empty(Q, N, device=dev)
+    start = N - Q
+    ms = time_fn(lambda: ops.lib().indexer_logits(q, k, w, ks, out, start))
+    visible = Q * start + Q * (Q + 1) / 2
+    flops = 2.0 * 64 * 128 * visible
+    return {"op": "indexer_logits", "Q": Q, "N": N, "ms": ms, "tflops": flops / ms / 1e9}
+
+
+def bench_topk(R=1024, N=65536, k=2048, **_):
+    dev = "cuda"
+    s = torch.randn(R, N, device=dev)
+    ms = time_fn(lambda: ops.exact_topk(s, k))
+    return {"op": "topk", "R": R, "N": N, "k": k, "ms": ms, "read_gbs": R * N * 4 / ms / 1e6}
+
+
+OPS = {"sparse_mla": bench_sparse_mla, "fp8_gemm": bench_fp8_gemm, "indexer": bench_indexer, "topk": bench_topk}
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--op", default="all")
+    p.add_argument("--T", type=int, default=256)
+    p.add_argument("--K", type=int, default=2048)
+    p.add_argument("--P", type=int, default=65664)
+    p.add_argument("--splits", type=int, default=1)
+    p.add_argument("--impl", type=int, default=0)
+    p.add_argument("--locality", type=float, default=0.0)
+    p.add_argument("--M", type=int, default=1024)
+    p.add_argument("--N", type=int, default=36864)
+    p.add_argument("--Kdim", type=int, default=7168)
+    a = p.parse_args()
+    names = list(OPS) if a.op == "all" else a.op.split(",")
+    for name in names:
+        kw = dict(T=a.T, K=a.K, P=a.P, splits=a.splits, impl=a.impl, locality=a.locality)
+        if name == "fp8_gemm":
+            kw = dict(M=a.M, N=a.N, K=a.Kdim)
+        print(json.dumps(OPS[name](**kw)))
+    torch.cuda.synchronize()
+    ops.check_errors("cuda")
+
+
+if __name__ == "__main__":
+    main()

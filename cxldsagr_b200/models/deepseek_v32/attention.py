@@ -50,30 +50,40 @@ class AttentionRunner:
         (self.qb0, self.qb_n), (self.iq0, self.iq_n) = weights.spans_b
 
     # ------------------------------------------------------------- projection
-    def project(self, normed, quantized, pos: int, positions, freqs):
+    def project(self, normed, quantized, pos: int, positions, freqs, scope=None):
+        scope = scope or (lambda _name: nullcontext())
         cfg, w = self.cfg, self.w
         T = normed.shape[0]
         H, nope, rope, L = cfg.n_heads, cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.kv_lora_rank
-        a = w.fused_a(normed, quantized=quantized)
+        with scope("fused_a_gemm"):
+            a = w.fused_a(normed, quantized=quantized)
         qa = a[:, self.qa0:self.qa0 + self.qa_n]
         kv = a[:, self.kv0:self.kv0 + self.kv_n]
         ik = a[:, self.ik0:self.ik0 + self.ik_n]
-        qa_normed, _, qr8, qrs = ops.norm_quant(qa, None, w.q_norm, cfg.norm_eps, want_out=w.fused_b.scales is None)
-        b = w.fused_b(qa_normed, quantized=(qr8, qrs))
+        with scope("q_norm"):
+            qa_normed, _, qr8, qrs = ops.norm_quant(qa, None, w.q_norm, cfg.norm_eps, want_out=w.fused_b.scales is None)
+        with scope("fused_b_gemm"):
+            b = w.fused_b(qa_normed, quantized=(qr8, qrs))
         q_proj = torch.empty((T, H, cfg.qk_head_dim), dtype=torch.bfloat16, device=normed.device)
-        ops.mla_absorb(b, H, nope, rope, w.wk_b_t, q_proj)
-        ops.mla_q_rope(b, H, nope, rope, freqs, positions, q_proj, L)
+        with scope("absorb"):
+            ops.mla_absorb(b, H, nope, rope, w.wk_b_t, q_proj)
+        with scope("q_rope"):
+            ops.mla_q_rope(b, H, nope, rope, freqs, positions, q_proj, L)
         # KV record straight into its cache row.
-        rows = self.cache.destination_rows(T)
-        ops.kv_finish(kv, L, rope, w.kv_norm, cfg.norm_eps, freqs, positions, self.cache.records, rows)
-        self.cache.finish_append(rows)
+        with scope("kv_record"):
+            rows = self.cache.destination_rows(T)
+            ops.kv_finish(kv, L, rope, w.kv_norm, cfg.norm_eps, freqs, positions, self.cache.records, rows)
+            self.cache.finish_append(rows)
         # Indexer key into the resident FP8 key cache.
-        ops.index_k(ik, rope, w.index_norm_w, w.index_norm_b, cfg.norm_eps, freqs, positions,
-                    self.index_keys[pos:pos + T], self.index_scales[pos:pos + T])
-        w_raw = ops.linear_f32(normed, w.index_head)
+        with scope("index_k"):
+            ops.index_k(ik, rope, w.index_norm_w, w.index_norm_b, cfg.norm_eps, freqs, positions,
+                        self.index_keys[pos:pos + T], self.index_scales[pos:pos + T])
+        with scope("index_weights_f32"):
+            w_raw = ops.linear_split(normed, w.index_head_split) if normed.is_cuda else ops.linear_f32(normed, w.index_head)
         iq = b[:, self.iq0:self.iq0 + self.iq_n]
-        q_idx, weights = ops.index_q(iq, cfg.index_n_heads, cfg.index_head_dim, rope, freqs, positions,
-                                     w_raw, self.head_scale)
+        with scope("index_q"):
+            q_idx, weights = ops.index_q(iq, cfg.index_n_heads, cfg.index_head_dim, rope, freqs, positions,
+                                         w_raw, self.head_scale)
         return q_proj, q_idx, weights
 
     # ---------------------------------------------------------------- forward
@@ -84,7 +94,7 @@ class AttentionRunner:
         end = pos + T
         with self.cache.operation():
             with scope("attention_projection"):
-                q_proj, q_idx, weights = self.project(normed, quantized, pos, positions, freqs)
+                q_proj, q_idx, weights = self.project(normed, quantized, pos, positions, freqs, scope)
             with scope("indexer"):
                 if logits_buf is not None and logits_buf.shape[0] >= T and logits_buf.shape[1] >= end:
                     logits = logits_buf[:T]
@@ -106,8 +116,10 @@ class AttentionRunner:
             with scope("sparse_mla"):
                 attn = self._consume(q_proj, ids)
         with scope("attention_output"):
-            v = ops.mla_expand(attn, self.w.wv_b)
-            return self.w.wo(v.reshape(T, -1))
+            with scope("expand"):
+                v = ops.mla_expand(attn, self.w.wv_b)
+            with scope("o_proj"):
+                return self.w.wo(v.reshape(T, -1))
 
     def _consume(self, q, ids):
         if not self.cache.offload:

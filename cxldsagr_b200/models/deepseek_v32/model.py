@@ -35,10 +35,14 @@ class DenseMLP:
     def __init__(self, w: MLPWeights):
         self.w = w
 
-    def __call__(self, normed, quantized):
-        packed = self.w.gate_up(normed, quantized=quantized)
-        h, q, s_t = ops.silu_mul_quant(packed)
-        return self.w.down(h, quantized=(q, s_t))
+    def __call__(self, normed, quantized, scope=None):
+        scope = scope or (lambda _n: nullcontext())
+        with scope("gate_up_gemm"):
+            packed = self.w.gate_up(normed, quantized=quantized)
+        with scope("silu_mul_quant"):
+            h, q, s_t = ops.silu_mul_quant(packed)
+        with scope("down_gemm"):
+            return self.w.down(h, quantized=(q, s_t))
 
 
 class MoE:
@@ -104,7 +108,7 @@ class Block:
         with scope("post_attention_residual_norm"):
             normed2, out_res, q2, s2 = ops.norm_quant(summed, attn, self.post_norm, cfg.norm_eps)
         with scope("moe" if isinstance(self.mlp, MoE) else "dense_mlp"):
-            out = self.mlp(normed2, (q2, s2))
+            out = self.mlp(normed2, (q2, s2), scope) if isinstance(self.mlp, DenseMLP) else self.mlp(normed2, (q2, s2))
         return out, out_res
 
 

@@ -96,6 +96,7 @@ class AttentionWeights:
     index_norm_w: torch.Tensor     # fp32 [128]
     index_norm_b: torch.Tensor     # fp32 [128]
     index_head: torch.Tensor       # fp32 [64, D]
+    index_head_split: torch.Tensor  # bf16 [128, D]: hi || lo of index_head
     fused_a: Linear
     spans_a: list
     fused_b: Linear
@@ -148,7 +149,8 @@ def load_attention(source, cfg: ModelConfig, layer: int, *, device) -> Attention
         kv_norm=_f32(source, a + "kv_a_layernorm.weight", device),
         index_norm_w=_f32(source, a + "indexer.k_norm.weight", device),
         index_norm_b=_f32(source, a + "indexer.k_norm.bias", device),
-        index_head=_f32(source, a + "indexer.weights_proj.weight", device),
+        index_head=(ih := _f32(source, a + "indexer.weights_proj.weight", device)),
+        index_head_split=ops.split_bf16(ih),
         fused_a=fused_a,
         spans_a=spans_a,
         fused_b=fused_b,

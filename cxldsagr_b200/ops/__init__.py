@@ -131,11 +131,34 @@ def bmm_nt(a, b, out=None, *, out_dtype=torch.bfloat16):
 
 
 def linear_f32(x, weight):
-    """FP32 x @ weight^T with a BF16 x and an FP32 weight -> FP32."""
+    """FP32 x @ weight^T with a BF16 x and an FP32 weight -> FP32 (SIMT kernel)."""
     if not _cuda(x):
         return x.float() @ weight.float().T
     out = torch.empty((x.shape[0], weight.shape[0]), dtype=torch.float32, device=x.device)
     lib().linear_f32(x.contiguous(), weight.contiguous(), out)
+    return out
+
+
+def split_bf16(weight: torch.Tensor) -> torch.Tensor:
+    """[N, K] FP32 -> [2N, K] BF16 = [hi; lo] with hi + lo ~= weight (~16 mantissa bits)."""
+    hi = weight.float().bfloat16()
+    lo = (weight.float() - hi.float()).bfloat16()
+    return torch.cat((hi, lo)).contiguous()
+
+
+def linear_split(x, w_split):
+    """Tensor-core x @ [hi; lo]^T for a BF16 x -> FP32 [M, 2N] partials (hi || lo).
+
+    hi + lo reproduces an FP32 weight to ~2^-17 relative, so summing the two
+    halves (done by the consumer) matches an FP32 GEMV to FP32 accumulation noise.
+    """
+    if not _cuda(x):
+        return x.float() @ w_split.float().T
+    x2 = x.contiguous()
+    M, K = x2.shape
+    N = w_split.shape[0]
+    out = torch.empty((M, N), dtype=torch.float32, device=x.device)
+    lib().bf16_gemm(x2, 0, K, 0, w_split, 0, K, 0, out, 0, N, 0, M, N, K, 1)
     return out
 
 
@@ -198,7 +221,8 @@ def exact_topk(scores, k: int, *, causal_start: int | None = None, n: int | None
 
 
 # ------------------------------------------------------------- attention
-def sparse_mla(q, kv, ids, scale, *, splits: int = 1, return_lse: bool = False, value_dim: int = 512):
+def sparse_mla(q, kv, ids, scale, *, splits: int = 1, return_lse: bool = False, value_dim: int = 512,
+               impl: int = 0):
     """Sparse MLA: q [T,H,576], kv [P,576], ids [T,K] -> [T,H,512] (BF16)."""
     if not _cuda(q):
         if return_lse:
@@ -214,7 +238,7 @@ def sparse_mla(q, kv, ids, scale, *, splits: int = 1, return_lse: bool = False, 
     if splits > 1:
         nbytes = lib().sparse_mla_scratch_bytes(T, H, splits)
         scratch = torch.empty(nbytes // 4, dtype=torch.float32, device=q.device)
-    lib().sparse_mla(q.contiguous(), kv, ids.contiguous(), float(scale), out, lse, splits, scratch)
+    lib().sparse_mla(q.contiguous(), kv, ids.contiguous(), float(scale), out, lse, splits, scratch, impl)
     return (out, lse) if return_lse else out
 
 
@@ -288,8 +312,13 @@ def index_k(ik, R, ln_w, ln_b, eps, freqs, positions, k_out, s_out):
 
 
 def index_q(iq, heads, dim, R, freqs, positions, w_raw, head_scale):
-    """Indexer query: split-half RoPE + per-head UE8M0 FP8; weights = raw * head_scale * q_scale."""
+    """Indexer query: split-half RoPE + per-head UE8M0 FP8; weights = raw * head_scale * q_scale.
+
+    ``w_raw`` is [T, heads] or the [T, 2*heads] hi || lo partials of :func:`linear_split`.
+    """
     T = iq.shape[0]
+    if w_raw.shape[-1] == 2 * heads and not _cuda(iq):
+        w_raw = w_raw[:, :heads] + w_raw[:, heads:]
     if not _cuda(iq):
         q = reference.apply_rope(iq[:, : heads * dim].reshape(T, heads, dim), _angles(freqs, positions), interleaved=False)
         qq, qs = reference.quantize_index(q)

@@ -17,7 +17,7 @@ class NativeUnavailable(RuntimeError):
 
 
 # Entry points that launch more than one kernel per call.
-_MULTI_LAUNCH = {"sparse_mla": lambda args: 2 if len(args) > 6 and int(args[6]) > 1 else 1}
+_MULTI_LAUNCH = {"sparse_mla": lambda args: 2 if len(args) > 6 and int(args[6]) > 1 else 1}  # + LSE combine
 _NO_LAUNCH = {"error_word", "sparse_mla_scratch_bytes"}
 
 

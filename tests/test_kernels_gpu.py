@@ -143,8 +143,10 @@ def test_topk_ties_and_causal():
 
 
 # ------------------------------------------------------------ sparse MLA
-@pytest.mark.parametrize("T,K,P,splits", [(2, 2048, 5000, 1), (3, 256, 300, 1), (1, 2048, 9000, 16), (5, 100, 64, 4)])
-def test_sparse_mla(T, K, P, splits):
+@pytest.mark.parametrize("impl", [0, 1], ids=["tcgen05", "mma_sync"])
+@pytest.mark.parametrize("T,K,P,splits", [(2, 2048, 5000, 1), (3, 256, 300, 1), (1, 2048, 9000, 16), (5, 100, 64, 4),
+                                          (300, 2048, 70000, 1)])
+def test_sparse_mla(T, K, P, splits, impl):
     torch.manual_seed(10)
     H = 128
     q = (torch.randn(T, H, 576, device=DEV) * 0.5).bfloat16()
@@ -153,18 +155,38 @@ def test_sparse_mla(T, K, P, splits):
     ids[:, -7:] = -1
     ids[0, :3] = P + 5  # out of range = padding
     scale = v32_config().attention_scale
-    got, lse = ops.sparse_mla(q, kv, ids, scale, splits=splits, return_lse=True)
-    want, wlse = ref.sparse_mla_lse(q.cpu(), kv.cpu(), ids.cpu(), scale)
+    got, lse = ops.sparse_mla(q, kv, ids, scale, splits=splits, return_lse=True, impl=impl)
+    if T > 8:  # oracle on a subset of rows
+        rows = torch.tensor([0, 1, T // 2, T - 1])
+        want, wlse = ref.sparse_mla_lse(q[rows].cpu(), kv.cpu(), ids[rows].cpu(), scale)
+        got, lse = got[rows.to(DEV)], lse[rows.to(DEV)]
+    else:
+        want, wlse = ref.sparse_mla_lse(q.cpu(), kv.cpu(), ids.cpu(), scale)
     assert rel_err(got.cpu(), want) < 2e-2
     assert torch.allclose(lse.cpu(), wlse, atol=2e-2, rtol=1e-3)
 
 
-def test_sparse_mla_all_padding_is_zero():
+@pytest.mark.parametrize("impl", [0, 1])
+def test_sparse_mla_all_padding_is_zero(impl):
     q = torch.randn(2, 128, 576, device=DEV).bfloat16()
     kv = torch.randn(10, 576, device=DEV).bfloat16()
     ids = torch.full((2, 64), -1, dtype=torch.int32, device=DEV)
-    out = ops.sparse_mla(q, kv, ids, 0.1)
+    out = ops.sparse_mla(q, kv, ids, 0.1, impl=impl)
     assert torch.count_nonzero(out) == 0
+
+
+def test_sparse_mla_large_logit_range_rescale():
+    """Scores growing by far more than 2^8 across tiles exercise the lazy O rescale."""
+    torch.manual_seed(13)
+    T, K, P = 2, 512, 600
+    q = torch.randn(T, 128, 576, device=DEV).bfloat16()
+    kv = torch.randn(P, 576, device=DEV)
+    kv *= torch.linspace(0.1, 4.0, P, device=DEV)[:, None]
+    kv = kv.bfloat16()
+    ids = torch.arange(K, device=DEV, dtype=torch.int32).repeat(T, 1)
+    got = ops.sparse_mla(q, kv, ids, 0.2)
+    want = ref.sparse_mla(q.cpu(), kv.cpu(), ids.cpu(), 0.2)
+    assert rel_err(got.cpu(), want) < 2e-2
 
 
 # ---------------------------------------------------------- elementwise
@@ -221,6 +243,8 @@ def test_linear_f32_and_embed():
     got = ops.linear_f32(x, W)
     want = x.cpu().float() @ W.cpu().T
     assert rel_err(got.cpu(), want) < 1e-5
+    parts = ops.linear_split(x, ops.split_bf16(W))
+    assert rel_err((parts[:, :64] + parts[:, 64:]).cpu(), want) < 1e-5
     table = torch.randn(1000, 256, device=DEV).bfloat16()
     ids = torch.tensor([5, 0, 999, 17], device=DEV)
     assert torch.equal(ops.embed(ids, table), table[ids])
