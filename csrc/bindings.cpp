@@ -210,14 +210,18 @@ void indexer_logits(const Tensor& q, const Tensor& k, const Tensor& w, const Ten
   b200::launch_indexer_logits(a, stream());
 }
 
-void topk(const Tensor& scores, int64_t N, int64_t k, int64_t causal_start, Tensor& values, Tensor& ids) {
+void topk(const Tensor& scores, int64_t N, int64_t k, int64_t causal_start, Tensor& values, Tensor& ids,
+          int64_t algo) {
   CHECK_CUDA(scores); CHECK_DTYPE(scores, torch::kFloat32); CHECK_DTYPE(values, torch::kFloat32);
   CHECK_DTYPE(ids, torch::kInt32); CHECK_LAST_CONTIG(scores);
   TORCH_CHECK(values.is_contiguous() && ids.is_contiguous() && values.size(1) == k && ids.size(1) == k, "topk outputs");
   TORCH_CHECK(N <= scores.size(1), "topk: N exceeds scores width");
   c10::cuda::CUDAGuard g(scores.device());
+  Tensor overflow;
+  if (algo == 0) overflow = torch::zeros({scores.size(0)}, torch::dtype(torch::kInt32).device(scores.device()));
   b200::launch_topk_causal(cptr<float>(scores), scores.stride(0), scores.size(0), N, k, causal_start,
-                           ptr<float>(values), ptr<int>(ids), err_ptr(scores), stream());
+                           ptr<float>(values), ptr<int>(ids), err_ptr(scores), stream(),
+                           algo == 0 ? overflow.data_ptr<int>() : nullptr);
 }
 
 // ------------------------------------------------------------- attention

@@ -127,8 +127,10 @@ void launch_indexer_logits(const IndexerArgs& a, cudaStream_t stream);
 void launch_topk(const float* scores, int64_t ld, int R, int N, int k, float* values, int* ids,
                  int* err, cudaStream_t stream);
 // Same, with row r reading only columns [0, min(N, causal_start + r + 1)).
+// With `overflow` (R zeroed ints of caller scratch) the two-pass kernel runs
+// first and only rows it flags are redone by the multi-pass kernel.
 void launch_topk_causal(const float* scores, int64_t ld, int R, int N, int k, int causal_start,
-                        float* values, int* ids, int* err, cudaStream_t stream);
+                        float* values, int* ids, int* err, cudaStream_t stream, int* overflow = nullptr);
 
 // --------------------------------------------------------------- sparse MLA
 struct MLAArgs {

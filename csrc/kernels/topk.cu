@@ -21,6 +21,9 @@ namespace {
 
 constexpr int kThreads = 512;
 constexpr int kMaxK = 2048;
+constexpr int kThreads2 = 1024;
+constexpr int kBins = 4096;       // 12-bit first-level histogram
+constexpr int kSecCap = 6144;     // threshold-bin candidates staged in shared memory
 
 __device__ __forceinline__ uint32_t order_key(float f) {
   const uint32_t u = __float_as_uint(f);
@@ -36,7 +39,10 @@ __device__ __forceinline__ float key_value(uint32_t k) {
 __global__ void __launch_bounds__(kThreads) topk_kernel(const float* __restrict__ scores, int64_t ld,
                                                         int N, int k, int causal_start,
                                                         float* __restrict__ values,
-                                                        int* __restrict__ ids, int* err) {
+                                                        int* __restrict__ ids, int* err,
+                                                        const int* __restrict__ only_rows) {
+  // With only_rows set, rows not flagged there were finished by topk2_kernel.
+  if (only_rows && !only_rows[blockIdx.x]) return;
   __shared__ uint32_t hist[256];
   __shared__ uint64_t cand[kMaxK];
   __shared__ uint32_t s_prefix, s_krem, s_count, s_running;
@@ -174,19 +180,199 @@ __global__ void __launch_bounds__(kThreads) topk_kernel(const float* __restrict_
   }
 }
 
+
+// Two-pass variant: a 12-bit histogram pass finds the bin holding the k-th
+// key; a collect pass appends every key of a higher bin (all selected) and
+// stages the keys of the threshold bin in shared memory, where a bitonic sort
+// picks the remaining ones (larger key first, then smaller index).  Rows
+// whose threshold bin holds more than kSecCap keys set *overflow and are
+// finished by the multi-pass kernel.
+__global__ void __launch_bounds__(kThreads2) topk2_kernel(const float* __restrict__ scores, int64_t ld, int N,
+                                                          int k, int causal_start, float* __restrict__ values,
+                                                          int* __restrict__ ids, int* __restrict__ overflow,
+                                                          int* err) {
+  extern __shared__ uint8_t dyn[];
+  uint32_t* hist = reinterpret_cast<uint32_t*>(dyn);                      // kBins
+  uint64_t* cand = reinterpret_cast<uint64_t*>(dyn + kBins * 4);          // kMaxK
+  uint64_t* sec = cand + kMaxK;                                           // kSecCap (padded to pow2 in sort)
+  __shared__ uint32_t s_count, s_sec, s_bstar, s_above;
+  __shared__ uint32_t warp_sum[kThreads2 / 32];
+  const int r = blockIdx.x;
+  const float* row = scores + int64_t(r) * ld;
+  const int row_end = causal_start >= 0 ? min(N, causal_start + r + 1) : N;
+  const int take = min(k, row_end);
+  const bool vec = ((reinterpret_cast<uintptr_t>(row) & 15) == 0);
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    s_count = 0;
+    s_sec = 0;
+    s_bstar = 0;
+    s_above = 0;
+  }
+  for (int i = tid; i < kBins; i += kThreads2) hist[i] = 0;
+  __syncthreads();
+  auto for_row = [&](auto&& fn) {
+    if (vec) {
+      const int n4 = row_end / 4;
+      for (int i = tid; i < n4; i += kThreads2) {
+        const float4 v = reinterpret_cast<const float4*>(row)[i];
+        fn(4 * i, v.x);
+        fn(4 * i + 1, v.y);
+        fn(4 * i + 2, v.z);
+        fn(4 * i + 3, v.w);
+      }
+      for (int i = n4 * 4 + tid; i < row_end; i += kThreads2) fn(i, row[i]);
+    } else {
+      for (int i = tid; i < row_end; i += kThreads2) fn(i, row[i]);
+    }
+  };
+  auto composite = [](uint32_t key, int i) { return (uint64_t(key) << 32) | uint32_t(0xFFFFFFFFu - uint32_t(i)); };
+  const bool take_all = take >= row_end;
+  if (take_all) {
+    for_row([&](int i, float f) {
+      const uint32_t pos = atomicAdd(&s_count, 1u);
+      if (pos < uint32_t(kMaxK)) cand[pos] = composite(order_key(f), i);
+    });
+  } else {
+    for_row([&](int, float f) { atomicAdd(&hist[order_key(f) >> 20], 1u); });
+    __syncthreads();
+    // Suffix counts: thread t owns bins [4t, 4t+4).
+    uint32_t local[4], lsum = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      local[j] = hist[4 * tid + j];
+      lsum += local[j];
+    }
+    // inclusive scan from the top: above_incl(t) = sum over threads >= t
+    uint32_t v = lsum;
+    const int lane = tid % 32, w = tid / 32;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t n = __shfl_down_sync(0xffffffffu, v, o);
+      if (lane + o < 32) v += n;
+    }
+    if (lane == 0) warp_sum[w] = v;
+    __syncthreads();
+    uint32_t higher = 0;  // keys in warps above this one
+    for (int j = w + 1; j < kThreads2 / 32; ++j) higher += warp_sum[j];
+    uint32_t above = higher + v - lsum;  // keys in bins > 4t+3
+#pragma unroll
+    for (int j = 3; j >= 0; --j) {
+      const uint32_t b = 4 * tid + j;
+      if (above < uint32_t(take) && above + local[j] >= uint32_t(take)) {
+        s_bstar = b;
+        s_above = above;
+      }
+      above += local[j];
+    }
+    __syncthreads();
+    const uint32_t bstar = s_bstar;
+    for_row([&](int i, float f) {
+      const uint32_t key = order_key(f);
+      const uint32_t b = key >> 20;
+      if (b > bstar) {
+        const uint32_t pos = atomicAdd(&s_count, 1u);
+        if (pos < uint32_t(kMaxK)) cand[pos] = composite(key, i);
+      } else if (b == bstar) {
+        const uint32_t pos = atomicAdd(&s_sec, 1u);
+        if (pos < uint32_t(kSecCap)) sec[pos] = composite(key, i);
+      }
+    });
+    __syncthreads();
+    const uint32_t nsec = s_sec;
+    if (nsec > uint32_t(kSecCap)) {  // pathological: finished by the multi-pass kernel
+      if (tid == 0) overflow[r] = 1;
+      return;
+    }
+    // sort the threshold-bin keys, take the first (take - above)
+    int n2 = 1;
+    while (n2 < int(nsec)) n2 <<= 1;
+    for (int i = nsec + tid; i < n2; i += kThreads2) sec[i] = 0ull;
+    __syncthreads();
+    for (int size = 2; size <= n2; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int i = tid; i < n2 / 2; i += kThreads2) {
+          const int lo = 2 * stride * (i / stride) + (i % stride);
+          const int hi = lo + stride;
+          const bool desc = ((lo & size) == 0);
+          const uint64_t a = sec[lo], bb = sec[hi];
+          if ((a < bb) == desc) {
+            sec[lo] = bb;
+            sec[hi] = a;
+          }
+        }
+        __syncthreads();
+      }
+    }
+    const uint32_t base = s_count;  // == s_above
+    const uint32_t need = uint32_t(take) - s_above;
+    for (uint32_t i = tid; i < need; i += kThreads2)
+      if (base + i < uint32_t(kMaxK)) cand[base + i] = sec[i];
+    __syncthreads();
+    if (tid == 0) s_count = base + need;
+  }
+  __syncthreads();
+  const int count = min(int(s_count), kMaxK);
+  if (count != take && tid == 0) record_error(err, kErrBadIndex);
+  int n2 = 1;
+  while (n2 < count) n2 <<= 1;
+  for (int i = count + tid; i < n2; i += kThreads2) cand[i] = 0ull;
+  __syncthreads();
+  for (int size = 2; size <= n2; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = tid; i < n2 / 2; i += kThreads2) {
+        const int lo = 2 * stride * (i / stride) + (i % stride);
+        const int hi = lo + stride;
+        const bool desc = ((lo & size) == 0);
+        const uint64_t a = cand[lo], bb = cand[hi];
+        if ((a < bb) == desc) {
+          cand[lo] = bb;
+          cand[hi] = a;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  float* vout = values + int64_t(r) * k;
+  int* iout = ids + int64_t(r) * k;
+  for (int i = tid; i < k; i += kThreads2) {
+    if (i < count) {
+      const uint64_t c = cand[i];
+      const float v = key_value(uint32_t(c >> 32));
+      const int idx = int(0xFFFFFFFFu - uint32_t(c & 0xFFFFFFFFu));
+      vout[i] = v;
+      iout[i] = (__float_as_uint(v) & 0x7FFFFFFFu) >= 0x7F800000u ? -1 : idx;
+    } else {
+      vout[i] = -INFINITY;
+      iout[i] = -1;
+    }
+  }
+}
+
+
 }  // namespace
 
 void launch_topk(const float* scores, int64_t ld, int R, int N, int k, float* values, int* ids,
                  int* err, cudaStream_t stream) {
-  launch_topk_causal(scores, ld, R, N, k, -1, values, ids, err, stream);
+  launch_topk_causal(scores, ld, R, N, k, -1, values, ids, err, stream, nullptr);
 }
 
 void launch_topk_causal(const float* scores, int64_t ld, int R, int N, int k, int causal_start,
-                        float* values, int* ids, int* err, cudaStream_t stream) {
+                        float* values, int* ids, int* err, cudaStream_t stream, int* overflow) {
   if (R <= 0) return;
   if (k < 1 || k > kMaxK) throw std::invalid_argument("topk: k must be in [1, 2048]");
-  topk_kernel<<<R, kThreads, 0, stream>>>(scores, ld, N, k, causal_start, values, ids, err);
-  cuda_check(cudaGetLastError(), "topk launch");
+  if (overflow == nullptr) {
+    topk_kernel<<<R, kThreads, 0, stream>>>(scores, ld, N, k, causal_start, values, ids, err, nullptr);
+    cuda_check(cudaGetLastError(), "topk launch");
+    return;
+  }
+  const size_t smem = size_t(kBins) * 4 + size_t(kMaxK) * 8 + size_t(8192) * 8;
+  cuda_check(cudaFuncSetAttribute(topk2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+             "topk2 smem attribute");
+  topk2_kernel<<<R, kThreads2, smem, stream>>>(scores, ld, N, k, causal_start, values, ids, overflow, err);
+  cuda_check(cudaGetLastError(), "topk2 launch");
+  topk_kernel<<<R, kThreads, 0, stream>>>(scores, ld, N, k, causal_start, values, ids, err, overflow);
+  cuda_check(cudaGetLastError(), "topk fallback launch");
 }
 
 }  // namespace b200

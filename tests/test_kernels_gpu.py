@@ -121,25 +121,40 @@ def test_indexer_logits(Q, N, start):
 
 
 # ----------------------------------------------------------------- topk
-@pytest.mark.parametrize("R,N,k", [(3, 100, 64), (5, 5000, 2048), (2, 70000, 2048), (4, 1500, 2048)])
-def test_topk(R, N, k):
+@pytest.mark.parametrize("algo", [0, 1], ids=["two_pass", "multi_pass"])
+@pytest.mark.parametrize("R,N,k", [(3, 100, 64), (5, 5000, 2048), (2, 70000, 2048), (4, 1500, 2048), (300, 65536, 2048)])
+def test_topk(R, N, k, algo):
     torch.manual_seed(8)
     s = torch.randn(R, N, device=DEV)
-    v, i = ops.exact_topk(s, k)
+    v, i = ops.exact_topk(s, k, algo=algo)
     rv, ri = ref.exact_topk(s.cpu(), k)
     assert torch.equal(i.cpu(), ri)
     assert torch.equal(v.cpu(), rv)
 
 
-def test_topk_ties_and_causal():
+@pytest.mark.parametrize("algo", [0, 1])
+def test_topk_ties_and_causal(algo):
+    """Heavy ties overflow the two-pass kernel's threshold bin -> multi-pass fallback."""
     torch.manual_seed(9)
     s = torch.randint(0, 5, (6, 3000), device=DEV).float()
-    v, i = ops.exact_topk(s, 2048, causal_start=1000)
+    v, i = ops.exact_topk(s, 2048, causal_start=1000, algo=algo)
     rows = torch.arange(6)[:, None]
     cols = torch.arange(3000)[None, :]
     masked = s.cpu().masked_fill(cols > 1000 + rows, -torch.inf)
     rv, ri = ref.exact_topk(masked, 2048)
     assert torch.equal(i.cpu(), ri)
+
+
+def test_topk_moderate_ties_two_pass():
+    """Coarse values with a threshold bin that fits in shared memory."""
+    torch.manual_seed(14)
+    s = (torch.randn(8, 20000, device=DEV) * 4).round() / 4
+    v, i = ops.exact_topk(s, 2048, causal_start=15000)
+    rows = torch.arange(8)[:, None]
+    cols = torch.arange(20000)[None, :]
+    masked = s.cpu().masked_fill(cols > 15000 + rows, -torch.inf)
+    rv, ri = ref.exact_topk(masked, 2048)
+    assert torch.equal(i.cpu(), ri) and torch.equal(v.cpu(), rv)
 
 
 # ------------------------------------------------------------ sparse MLA
