@@ -60,6 +60,15 @@ void fp8_gemm(const Tensor& a_q, const Tensor& a_s_t, const Tensor& w, const Ten
   }
   a.M = M; a.N = N; a.K = K; a.lda = a_q.stride(0); a.ldb = w.stride(0);
   a.lda_s = a_s_t.stride(0); a.ldo = out.stride(0); a.err = err_ptr(a_q);
+  // Split-K scratch for GEMMs whose tile count leaves SMs idle.
+  constexpr int kMaxSplits = 8;
+  const size_t scratch = b200::fp8_gemm_scratch_bytes(M, N, K, kMaxSplits);
+  Tensor part;
+  if (scratch) {
+    part = torch::empty({int64_t(scratch / 4)}, torch::dtype(torch::kFloat32).device(a_q.device()));
+    a.partial = part.data_ptr<float>();
+    a.max_splits = kMaxSplits;
+  }
   b200::launch_fp8_gemm(a, stream());
 }
 
@@ -249,6 +258,10 @@ void sparse_mla(const Tensor& q, const Tensor& kv, const Tensor& ids, double sca
   else b200::launch_sparse_mla_split(a, int(splits), sp, stream());
 }
 
+int64_t fp8_gemm_splits(int64_t M, int64_t N, int64_t K) {
+  return b200::plan_fp8_gemm(int(M), int(N), int(K), 8).splits;
+}
+
 int64_t sparse_mla_scratch_bytes(int64_t T, int64_t H, int64_t splits) {
   return int64_t(b200::sparse_mla_scratch_bytes(T, H, splits));
 }
@@ -287,5 +300,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("topk", &topk);
   m.def("sparse_mla", &sparse_mla);
   m.def("sparse_mla_scratch_bytes", &sparse_mla_scratch_bytes);
+  m.def("fp8_gemm_splits", &fp8_gemm_splits);
   m.def("gather_rows", &gather_rows);
 }

@@ -15,11 +15,14 @@
 //              kind::f8f6f4 (M=128, N=BN, K=32) per 128-wide K block into one
 //              of two TMEM accumulators, then tcgen05.commit to release the
 //              smem stage and to signal the epilogue.
-//   warps 2-5  promotion/epilogue: each thread owns one output row; per K block
-//              it reads the fresh partial sums from TMEM (tcgen05.ld), scales
-//              them by sfa*sfb and accumulates in FP32 registers, so arbitrary
-//              (non power-of-two) weight block scales stay exact.  Two TMEM
-//              buffers let the tensor core run the next K block meanwhile.
+//   warps 2-9  promotion/epilogue: each thread owns one output row and half of
+//              the tile's columns (two warps per TMEM lane quadrant); per K
+//              block it reads the fresh partial sums from TMEM (tcgen05.ld),
+//              scales them by sfa*sfb and accumulates in FP32 registers, so
+//              arbitrary (non power-of-two) weight block scales stay exact.
+//              Two TMEM buffers let the tensor core run the next K block
+//              meanwhile.  BN = 256 for wide GEMMs (more MMA time per
+//              promotion step), BN = 128 when 256 would leave a tail wave.
 // Optional fused epilogue: residual add (out = acc + res) in FP32.
 // Every mbarrier wait is bounded (error word + orderly exit, never a hang).
 #include "../common/ptx.cuh"
@@ -30,7 +33,8 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 128;  // bytes of K per stage (= one scale block)
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each owning BN/2 columns
+constexpr int kThreads = 64 + kEpiWarps * 32;
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -50,7 +54,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tma_b, const float* __restrict__ sfa,
                     int lda_s, const float* __restrict__ sfb, __nv_bfloat16* __restrict__ out,
                     int ldo, const __nv_bfloat16* __restrict__ residual, int ldr, int M, int N,
-                    int K, int* err) {
+                    int K, int splits, float* __restrict__ partial, int* err) {
   extern __shared__ uint8_t smem_raw[];
   auto& s = *reinterpret_cast<GemmSmem<BN, STAGES>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -61,6 +65,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_tiles = num_m * num_n;
   const int num_kb = (K + BK - 1) / BK;
   const int kb_scale_stride = num_kb;  // sfb row length
+  // Work unit = (tile, K split); split-major so concurrent CTAs share a K range.
+  const int num_units = num_tiles * splits;
+  const int kps = (num_kb + splits - 1) / splits;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -69,7 +76,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.tmem_full[i], 1);
-      mbar_init(&s.tmem_empty[i], 4);
+      mbar_init(&s.tmem_empty[i], kEpiWarps);
     }
     s.abort_flag = 0;
     fence_barrier_init();
@@ -94,10 +101,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const int tile = u % num_tiles, sp = u / num_tiles;
         const int m0 = (tile % num_m) * BM;
         const int n0 = (tile / num_m) * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int kb0 = sp * kps, kb1 = min(num_kb, kb0 + kps);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1, err, kErrTimeoutSmemEmpty, abort_flag)) {
             ok = false;
             break;
@@ -124,8 +133,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       uint32_t kcount = 0;  // global K-block counter -> TMEM buffer + parity
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        for (int kb = 0; kb < num_kb; ++kb, ++kcount) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const int sp = u / num_tiles;
+        const int kb0 = sp * kps, kb1 = min(num_kb, kb0 + kps);
+        for (int kb = kb0; kb < kb1; ++kb, ++kcount) {
           const uint32_t buf = kcount & 1;
           const uint32_t bpar = (kcount >> 1) & 1;
           if (!mbar_wait(&s.tmem_empty[buf], bpar ^ 1, err, kErrTimeoutTmemEmpty, abort_flag)) {
@@ -155,26 +166,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // Epilogue warps 2..5: TMEM lane quadrant = warp % 4.
+    // Epilogue warps 2..9: TMEM lane quadrant = warp % 4; warps 2-5 own
+    // columns [0, BN/2), warps 6-9 columns [BN/2, BN).
+    constexpr int CPW = BN / 2;
     const int quad = warp & 3;
+    const int chalf = (warp - 2) / 4;
     const int row_in_tile = quad * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     uint32_t kcount = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+    for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      const int tile = u % num_tiles, sp = u / num_tiles;
+      const int kb0 = sp * kps, kb1 = min(num_kb, kb0 + kps);
       const int m0 = (tile % num_m) * BM;
-      const int n0 = (tile / num_m) * BN;
+      const int n0 = (tile / num_m) * BN + chalf * CPW;  // first column of this warp
       const int row = m0 + row_in_tile;
-      float acc[BN];
+      float acc[CPW];
 #pragma unroll
-      for (int j = 0; j < BN; ++j) acc[j] = 0.f;
-      for (int kb = 0; kb < num_kb; ++kb, ++kcount) {
+      for (int j = 0; j < CPW; ++j) acc[j] = 0.f;
+      for (int kb = kb0; kb < kb1; ++kb, ++kcount) {
         const uint32_t buf = kcount & 1;
         const uint32_t bpar = (kcount >> 1) & 1;
         const float sa = row < M ? __ldg(sfa + static_cast<size_t>(kb) * lda_s + row) : 0.f;
-        float sb[BN / 128 > 0 ? BN / 128 : 1];
+        float sb[(CPW + 127) / 128];
 #pragma unroll
-        for (int q = 0; q < (BN + 127) / 128; ++q) {
+        for (int q = 0; q < (CPW + 127) / 128; ++q) {
           const int nb = (n0 + q * 128) / 128;
           sb[q] = nb * 128 < N ? __ldg(sfb + static_cast<size_t>(nb) * kb_scale_stride + kb) : 0.f;
         }
@@ -184,28 +200,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tmem + lane_addr + buf * BN + c * 32, r);
+        for (int c = 0; c < CPW / 16; ++c) {
+          uint32_t r[16];
+          tmem_ld16(tmem + lane_addr + buf * BN + chalf * CPW + c * 16, r);
           tmem_wait_ld();
-          const float scale = sa * sb[(c * 32) / 128];
+          const float scale = sa * sb[(c * 16) / 128];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[c * 32 + j] = fmaf(__uint_as_float(r[j]), scale, acc[c * 32 + j]);
+          for (int j = 0; j < 16; ++j) acc[c * 16 + j] = fmaf(__uint_as_float(r[j]), scale, acc[c * 16 + j]);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.tmem_empty[buf]);
       }
       if (!ok) break;
-      if (row < M) {
+      if (splits > 1) {
+        // FP32 partial of this K split; the reduce kernel adds splits (+ residual).
+        if (row < M && n0 < N) {
+          float* prow = partial + (static_cast<size_t>(sp) * M + row) * N + n0;
+          const int ncols = min(CPW, N - n0);
+          if (ncols == CPW && (N % 4) == 0) {
+#pragma unroll
+            for (int j = 0; j < CPW; j += 4)
+              *reinterpret_cast<float4*>(prow + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < CPW; ++j)
+              if (j < ncols) prow[j] = acc[j];
+          }
+        }
+        continue;
+      }
+      if (row < M && n0 < N) {
         __nv_bfloat16* orow = out + static_cast<size_t>(row) * ldo + n0;
         const __nv_bfloat16* rrow = residual ? residual + static_cast<size_t>(row) * ldr + n0 : nullptr;
-        const int ncols = min(BN, N - n0);
-        const bool vec = (ncols == BN) && ((reinterpret_cast<uintptr_t>(orow) & 15) == 0) &&
+        const int ncols = min(CPW, N - n0);
+        const bool vec = (ncols == CPW) && ((reinterpret_cast<uintptr_t>(orow) & 15) == 0) &&
                          (!rrow || (reinterpret_cast<uintptr_t>(rrow) & 15) == 0);
         if (vec) {
 #pragma unroll
-          for (int j = 0; j < BN; j += 8) {
+          for (int j = 0; j < CPW; j += 8) {
             float v[8];
 #pragma unroll
             for (int t = 0; t < 8; ++t) v[t] = acc[j + t];
@@ -227,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < BN; ++j) {
+          for (int j = 0; j < CPW; ++j) {
             if (j < ncols) {
               float v = acc[j];
               if (rrow) v += __bfloat162float(rrow[j]);
@@ -247,28 +280,85 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// out[m, n] = bf16(sum_s partial[s, m, n] (+ residual[m, n])), fixed summation order.
+__global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N,
+                                     __nv_bfloat16* __restrict__ out, int ldo,
+                                     const __nv_bfloat16* __restrict__ residual, int ldr) {
+  const int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
+  if (i >= int64_t(M) * N) return;
+  const int m = int(i / N), n = int(i % N);
+  float v = 0.f;
+  for (int sp = 0; sp < splits; ++sp) v += partial[(int64_t(sp) * M + m) * N + n];
+  if (residual) v += __bfloat162float(residual[int64_t(m) * ldr + n]);
+  out[int64_t(m) * ldo + n] = __float2bfloat16_rn(v);
+}
+
 template <int BN, int STAGES>
-void launch_fp8_gemm_t(const FP8GemmArgs& a, cudaStream_t stream) {
+void launch_fp8_gemm_t(const FP8GemmArgs& a, int splits, cudaStream_t stream) {
   const CUtensorMap ta = make_tma_2d(a.A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.M, a.K, a.lda, BK, BM);
   const CUtensorMap tb = make_tma_2d(a.B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.N, a.K, a.ldb, BK, BN);
   const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
-  const int grid = std::min(tiles, sm_count());
+  const int grid = std::min(tiles * splits, sm_count());
   const size_t smem = sizeof(GemmSmem<BN, STAGES>) + 1024;
   auto kern = fp8_gemm_kernel<BN, STAGES>;
   cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
              "fp8 gemm smem attribute");
   kern<<<grid, kThreads, smem, stream>>>(ta, tb, a.sfa, a.lda_s, a.sfb, a.out, a.ldo, a.residual,
-                                         a.ldr, a.M, a.N, a.K, a.err);
+                                         a.ldr, a.M, a.N, a.K, splits, a.partial, a.err);
   cuda_check(cudaGetLastError(), "fp8 gemm launch");
+  if (splits > 1) {
+    const int64_t n = int64_t(a.M) * a.N;
+    splitk_reduce_kernel<<<int((n + 255) / 256), 256, 0, stream>>>(a.partial, splits, a.M, a.N, a.out, a.ldo,
+                                                                   a.residual, a.ldr);
+    cuda_check(cudaGetLastError(), "fp8 gemm split-k reduce launch");
+  }
 }
 
 }  // namespace
 
+FP8GemmPlan plan_fp8_gemm(int M, int N, int K, int max_splits) {
+  // BN=256 (4 stages x 48 KB) doubles the tensor-core time per promotion
+  // step; used when it still gives >= 3 full waves of tiles.  Otherwise BN=128
+  // with a K split chosen by a wave-quantisation cost model, in units of one
+  // 128x128x128 K-block step (~0.14 us):
+  //   cost(s) = ceil(tiles * s / SMs) * ceil(k_blocks / s)
+  //           + [s > 1] * (2 + s * M * N * 4 B / HBM-bandwidth / step).
+  const int sms = sm_count();
+  const int num_kb = (K + BK - 1) / BK;
+  FP8GemmPlan p{};
+  const int64_t tiles256 = int64_t((M + BM - 1) / BM) * ((N + 255) / 256);
+  if (tiles256 >= 3 * sms) {
+    p.bn = 256;
+    p.splits = 1;
+    return p;
+  }
+  p.bn = 128;
+  const int64_t tiles = int64_t((M + BM - 1) / BM) * ((N + 127) / 128);
+  int64_t best = -1;
+  for (int sp = 1; sp <= max_splits; ++sp) {
+    if (sp > 1 && num_kb / sp < 8) break;  // keep >= 8 K blocks per split
+    const int64_t waves = (tiles * sp + sms - 1) / sms;
+    const double reduce = sp > 1 ? 2.0 + double(sp) * M * N * 4.8e-6 : 0.0;
+    const int64_t cost = int64_t(double(waves * ((num_kb + sp - 1) / sp)) + reduce);
+    if (best < 0 || cost < best) {
+      best = cost;
+      p.splits = sp;
+    }
+  }
+  return p;
+}
+
+size_t fp8_gemm_scratch_bytes(int M, int N, int K, int max_splits) {
+  const FP8GemmPlan p = plan_fp8_gemm(M, N, K, max_splits);
+  return p.splits > 1 ? size_t(p.splits) * M * N * sizeof(float) : 0;
+}
+
 void launch_fp8_gemm(const FP8GemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return;
   if (a.K % 16) throw std::invalid_argument("fp8 gemm: K must be a multiple of 16");
-  // BN=128 keeps 128 FP32 accumulators per epilogue thread; 6 stages x 32 KB.
-  launch_fp8_gemm_t<128, 6>(a, stream);
+  FP8GemmPlan p = plan_fp8_gemm(a.M, a.N, a.K, a.partial ? a.max_splits : 1);
+  if (p.bn == 256) launch_fp8_gemm_t<256, 4>(a, 1, stream);
+  else launch_fp8_gemm_t<128, 6>(a, p.splits, stream);
 }
 
 }  // namespace b200

@@ -23,7 +23,15 @@ struct FP8GemmArgs {
   int64_t lda, ldb;
   int lda_s, ldo, ldr;
   int* err;
+  float* partial = nullptr;  // split-K scratch (fp8_gemm_scratch_bytes); null = no split
+  int max_splits = 1;
 };
+struct FP8GemmPlan {
+  int bn;
+  int splits;
+};
+FP8GemmPlan plan_fp8_gemm(int M, int N, int K, int max_splits);
+size_t fp8_gemm_scratch_bytes(int M, int N, int K, int max_splits);
 void launch_fp8_gemm(const FP8GemmArgs& a, cudaStream_t stream);
 
 // Batched BF16 GEMM: for g in [0, batch): out_g[m, n] = sum_k A_g[m, k] * B_g[n, k].

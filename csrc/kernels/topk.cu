@@ -31,6 +31,18 @@ __device__ __forceinline__ uint32_t order_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// Warp-aggregated append: returns this lane's slot (valid only when `take`).
+__device__ __forceinline__ uint32_t append_warp(uint32_t* counter, bool take) {
+  const uint32_t ballot = __ballot_sync(0xffffffffu, take);
+  if (!ballot) return 0;
+  const int lane = threadIdx.x % 32;
+  const int leader = __ffs(ballot) - 1;
+  uint32_t base = 0;
+  if (lane == leader) base = atomicAdd(counter, uint32_t(__popc(ballot)));
+  base = __shfl_sync(0xffffffffu, base, leader);
+  return base + __popc(ballot & ((1u << lane) - 1u));
+}
+
 __device__ __forceinline__ float key_value(uint32_t k) {
   const uint32_t u = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
   return __uint_as_float(u);
@@ -181,12 +193,13 @@ __global__ void __launch_bounds__(kThreads) topk_kernel(const float* __restrict_
 }
 
 
-// Two-pass variant: a 12-bit histogram pass finds the bin holding the k-th
-// key; a collect pass appends every key of a higher bin (all selected) and
-// stages the keys of the threshold bin in shared memory, where a bitonic sort
-// picks the remaining ones (larger key first, then smaller index).  Rows
-// whose threshold bin holds more than kSecCap keys set *overflow and are
-// finished by the multi-pass kernel.
+// Histogram-select variant: a 12-bit histogram pass finds the bin holding the
+// k-th key (refined by further 12- and 8-bit passes only while that bin holds
+// more keys than fit in shared memory); a collect pass appends every key of a
+// higher bin (all selected) and stages the threshold bin's keys in shared
+// memory, where a bitonic sort picks the remaining ones (larger key first,
+// then smaller index).  Rows whose threshold is an exact value shared by more
+// than kSecCap keys set *overflow and are finished by the multi-pass kernel.
 __global__ void __launch_bounds__(kThreads2) topk2_kernel(const float* __restrict__ scores, int64_t ld, int N,
                                                           int k, int causal_start, float* __restrict__ values,
                                                           int* __restrict__ ids, int* __restrict__ overflow,
@@ -211,72 +224,110 @@ __global__ void __launch_bounds__(kThreads2) topk2_kernel(const float* __restric
   }
   for (int i = tid; i < kBins; i += kThreads2) hist[i] = 0;
   __syncthreads();
+  // Warp-uniform row walk: every lane runs the same trip count (inactive lanes
+  // pass valid=false) so warp collectives inside fn are safe.
   auto for_row = [&](auto&& fn) {
     if (vec) {
       const int n4 = row_end / 4;
-      for (int i = tid; i < n4; i += kThreads2) {
-        const float4 v = reinterpret_cast<const float4*>(row)[i];
-        fn(4 * i, v.x);
-        fn(4 * i + 1, v.y);
-        fn(4 * i + 2, v.z);
-        fn(4 * i + 3, v.w);
+      const int trips = (n4 + kThreads2 - 1) / kThreads2;
+      for (int t = 0; t < trips; ++t) {
+        const int i = t * kThreads2 + tid;
+        const bool ok = i < n4;
+        float4 v = ok ? reinterpret_cast<const float4*>(row)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        fn(4 * i, v.x, ok);
+        fn(4 * i + 1, v.y, ok);
+        fn(4 * i + 2, v.z, ok);
+        fn(4 * i + 3, v.w, ok);
       }
-      for (int i = n4 * 4 + tid; i < row_end; i += kThreads2) fn(i, row[i]);
+      const int i = n4 * 4 + tid;  // tail (< 4 elements)
+      const bool ok = i < row_end && tid < 4;
+      fn(i, ok ? row[i] : 0.f, ok);
     } else {
-      for (int i = tid; i < row_end; i += kThreads2) fn(i, row[i]);
+      const int trips = (row_end + kThreads2 - 1) / kThreads2;
+      for (int t = 0; t < trips; ++t) {
+        const int i = t * kThreads2 + tid;
+        const bool ok = i < row_end;
+        fn(i, ok ? row[i] : 0.f, ok);
+      }
     }
   };
   auto composite = [](uint32_t key, int i) { return (uint64_t(key) << 32) | uint32_t(0xFFFFFFFFu - uint32_t(i)); };
   const bool take_all = take >= row_end;
   if (take_all) {
-    for_row([&](int i, float f) {
-      const uint32_t pos = atomicAdd(&s_count, 1u);
-      if (pos < uint32_t(kMaxK)) cand[pos] = composite(order_key(f), i);
+    for_row([&](int i, float f, bool ok) {
+      const uint32_t pos = append_warp(&s_count, ok);
+      if (ok && pos < uint32_t(kMaxK)) cand[pos] = composite(order_key(f), i);
     });
   } else {
-    for_row([&](int, float f) { atomicAdd(&hist[order_key(f) >> 20], 1u); });
-    __syncthreads();
-    // Suffix counts: thread t owns bins [4t, 4t+4).
-    uint32_t local[4], lsum = 0;
+    // Radix levels of 12, 12 and 8 bits.  After each level the bin holding
+    // the k-th key becomes the prefix; refinement stops as soon as that bin
+    // fits the shared-memory stage (clustered logits need the 2nd level).
+    uint32_t prefix = 0, above_total = 0;
+    int pbits = 0;
+    const int level_bits[3] = {12, 12, 8};
+    for (int level = 0; level < 3; ++level) {
+      const int lb = level_bits[level];
+      const int shift = 32 - pbits - lb;
+      for (int i = tid; i < kBins; i += kThreads2) hist[i] = 0;
+      __syncthreads();
+      for_row([&](int, float f, bool ok) {
+        const uint32_t key = order_key(f);
+        if (ok && (pbits == 0 || (key >> (32 - pbits)) == prefix))
+          atomicAdd(&hist[(key >> shift) & ((1u << lb) - 1u)], 1u);
+      });
+      __syncthreads();
+      // Suffix counts: thread t owns bins [4t, 4t+4).
+      uint32_t local[4], lsum = 0;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      local[j] = hist[4 * tid + j];
-      lsum += local[j];
-    }
-    // inclusive scan from the top: above_incl(t) = sum over threads >= t
-    uint32_t v = lsum;
-    const int lane = tid % 32, w = tid / 32;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t n = __shfl_down_sync(0xffffffffu, v, o);
-      if (lane + o < 32) v += n;
-    }
-    if (lane == 0) warp_sum[w] = v;
-    __syncthreads();
-    uint32_t higher = 0;  // keys in warps above this one
-    for (int j = w + 1; j < kThreads2 / 32; ++j) higher += warp_sum[j];
-    uint32_t above = higher + v - lsum;  // keys in bins > 4t+3
-#pragma unroll
-    for (int j = 3; j >= 0; --j) {
-      const uint32_t b = 4 * tid + j;
-      if (above < uint32_t(take) && above + local[j] >= uint32_t(take)) {
-        s_bstar = b;
-        s_above = above;
+      for (int j = 0; j < 4; ++j) {
+        local[j] = hist[4 * tid + j];
+        lsum += local[j];
       }
-      above += local[j];
+      uint32_t v = lsum;
+      const int lane = tid % 32, w = tid / 32;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t n = __shfl_down_sync(0xffffffffu, v, o);
+        if (lane + o < 32) v += n;
+      }
+      if (lane == 0) warp_sum[w] = v;
+      __syncthreads();
+      uint32_t higher = 0;
+      for (int j = w + 1; j < kThreads2 / 32; ++j) higher += warp_sum[j];
+      uint32_t above = above_total + higher + v - lsum;  // keys above bin 4t+3 (incl. earlier levels)
+#pragma unroll
+      for (int j = 3; j >= 0; --j) {
+        const uint32_t b = 4 * tid + j;
+        if (above < uint32_t(take) && above + local[j] >= uint32_t(take)) {
+          s_bstar = b;
+          s_above = above;
+          s_sec = local[j];  // keys in the threshold bin
+        }
+        above += local[j];
+      }
+      __syncthreads();
+      prefix = (pbits == 0 ? 0u : (prefix << lb)) | s_bstar;
+      pbits += lb;
+      above_total = s_above;
+      const uint32_t in_bin = s_sec;
+      __syncthreads();
+      if (in_bin <= uint32_t(kSecCap) || pbits == 32) break;
+    }
+    if (tid == 0) {
+      s_bstar = prefix;
+      s_sec = 0;
     }
     __syncthreads();
+    const int pshift = 32 - pbits;
     const uint32_t bstar = s_bstar;
-    for_row([&](int i, float f) {
+    for_row([&](int i, float f, bool ok) {
       const uint32_t key = order_key(f);
-      const uint32_t b = key >> 20;
-      if (b > bstar) {
-        const uint32_t pos = atomicAdd(&s_count, 1u);
-        if (pos < uint32_t(kMaxK)) cand[pos] = composite(key, i);
-      } else if (b == bstar) {
-        const uint32_t pos = atomicAdd(&s_sec, 1u);
-        if (pos < uint32_t(kSecCap)) sec[pos] = composite(key, i);
-      }
+      const uint32_t b = pshift >= 32 ? 0u : (key >> pshift);
+      const bool gt = ok && b > bstar, eq = ok && b == bstar;
+      const uint32_t pg = append_warp(&s_count, gt);
+      const uint32_t pe = append_warp(&s_sec, eq);
+      if (gt && pg < uint32_t(kMaxK)) cand[pg] = composite(key, i);
+      if (eq && pe < uint32_t(kSecCap)) sec[pe] = composite(key, i);
     });
     __syncthreads();
     const uint32_t nsec = s_sec;

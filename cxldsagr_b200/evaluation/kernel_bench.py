@@ -103,11 +103,14 @@ def bench_indexer(Q=1024, N=65536, **_):
     return {"op": "indexer_logits", "Q": Q, "N": N, "ms": ms, "tflops": flops / ms / 1e9}
 
 
-def bench_topk(R=1024, N=65536, k=2048, **_):
+def bench_topk(R=1024, N=65536, k=2048, clustered=False, **_):
     dev = "cuda"
     s = torch.randn(R, N, device=dev)
+    if clustered:  # indexer-like: most logits within a narrow band
+        s = 10.0 + 0.05 * s
     ms = time_fn(lambda: ops.exact_topk(s, k))
-    return {"op": "topk", "R": R, "N": N, "k": k, "ms": ms, "read_gbs": R * N * 4 / ms / 1e6}
+    return {"op": "topk", "R": R, "N": N, "k": k, "clustered": clustered, "ms": ms,
+            "read_gbs": R * N * 4 / ms / 1e6}
 
 
 OPS = {"sparse_mla": bench_sparse_mla, "fp8_gemm": bench_fp8_gemm, "indexer": bench_indexer, "topk": bench_topk}
@@ -122,6 +125,8 @@ def main():
     p.add_argument("--splits", type=int, default=1)
     p.add_argument("--impl", type=int, default=0)
     p.add_argument("--locality", type=float, default=0.0)
+    p.add_argument("--R", type=int, default=1024)
+    p.add_argument("--clustered", action="store_true")
     p.add_argument("--M", type=int, default=1024)
     p.add_argument("--N", type=int, default=36864)
     p.add_argument("--Kdim", type=int, default=7168)
@@ -131,6 +136,8 @@ def main():
         kw = dict(T=a.T, K=a.K, P=a.P, splits=a.splits, impl=a.impl, locality=a.locality)
         if name == "fp8_gemm":
             kw = dict(M=a.M, N=a.N, K=a.Kdim)
+        if name == "topk":
+            kw = dict(R=a.R, clustered=a.clustered)
         print(json.dumps(OPS[name](**kw)))
     torch.cuda.synchronize()
     ops.check_errors("cuda")

@@ -21,7 +21,12 @@ _MULTI_LAUNCH = {
     "sparse_mla": lambda args: 2 if len(args) > 6 and int(args[6]) > 1 else 1,  # + LSE combine
     "topk": lambda args: 3 if len(args) > 6 and int(args[6]) == 0 else 1,       # zero + 2-pass + fallback
 }
-_NO_LAUNCH = {"error_word", "sparse_mla_scratch_bytes"}
+
+
+def _fp8_gemm_launches(mod, args):
+    q, w = args[0], args[2]
+    return 2 if mod.fp8_gemm_splits(q.shape[0], w.shape[0], q.shape[1]) > 1 else 1  # + split-K reduce
+_NO_LAUNCH = {"error_word", "sparse_mla_scratch_bytes", "fp8_gemm_splits"}
 
 
 class _CountingLib:
@@ -40,6 +45,8 @@ class _CountingLib:
         if name in _NO_LAUNCH or not callable(fn):
             return fn
         multi = _MULTI_LAUNCH.get(name)
+        if name == "fp8_gemm":
+            multi = lambda args: _fp8_gemm_launches(self._mod, args)  # noqa: E731
 
         def call(*args):
             self.launches += multi(args) if multi else 1

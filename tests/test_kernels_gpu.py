@@ -74,7 +74,8 @@ def test_silu_mul_quant():
 
 
 # ------------------------------------------------------------------ gemms
-@pytest.mark.parametrize("M,N,K", [(1, 576, 7168), (128, 1536, 7168), (200, 7168, 2048), (1024, 2240, 7168), (77, 130, 256)])
+@pytest.mark.parametrize("M,N,K", [(1, 576, 7168), (128, 1536, 7168), (200, 7168, 2048), (1024, 2240, 7168), (77, 130, 256),
+                                   (128, 7168, 18432), (1024, 36864, 1024)])
 def test_fp8_gemm(M, N, K):
     torch.manual_seed(4)
     x = torch.randn(M, K, device=DEV).bfloat16()
@@ -84,11 +85,13 @@ def test_fp8_gemm(M, N, K):
     assert rel_err(got.cpu(), want) < 2e-2
 
 
-def test_fp8_gemm_residual():
+@pytest.mark.parametrize("M,N,K", [(130, 384, 1024), (128, 7168, 16384)])
+def test_fp8_gemm_residual(M, N, K):
+    """Residual fused in the epilogue (no split) and in the split-K reduce."""
     torch.manual_seed(5)
-    x = torch.randn(130, 1024, device=DEV).bfloat16()
-    res = torch.randn(130, 384, device=DEV).bfloat16()
-    w, s = quantize_weight_blocks(torch.randn(384, 1024, device=DEV) * 0.05)
+    x = torch.randn(M, K, device=DEV).bfloat16()
+    res = torch.randn(M, N, device=DEV).bfloat16()
+    w, s = quantize_weight_blocks(torch.randn(N, K, device=DEV) * 0.05)
     got = ops.fp8_linear(x, w, s, residual=res)
     want = ref.fp8_linear(x.cpu(), w.cpu(), s.cpu()).float() + res.cpu().float()
     assert rel_err(got.cpu(), want) < 2e-2
