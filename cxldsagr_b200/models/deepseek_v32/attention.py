@@ -26,31 +26,37 @@ from contextlib import nullcontext
 import torch
 
 from ... import ops
+from ...cache.indexer_cache import IndexerCache
 from ...cache.sparse_token_cache import SparseTokenCache, WorkingSetTooLarge
-from ...contracts import TokenSelection
 from .weights import AttentionWeights
 
 
+class LayerState:
+    """Per-(session, layer) state: main KV view + resident FP8 indexer keys."""
+
+    def __init__(self, kv: SparseTokenCache, index: IndexerCache):
+        self.kv = kv
+        self.index = index
+
+    @property
+    def cache(self):
+        return self.kv
+
+
 class AttentionRunner:
-    def __init__(self, cfg, weights: AttentionWeights, cache: SparseTokenCache, *, method: str = "hbm",
-                 index_capacity: int | None = None):
+    """Stateless w.r.t. requests: every call gets the session's :class:`LayerState`."""
+
+    def __init__(self, cfg, weights: AttentionWeights, *, method: str = "hbm"):
         self.cfg = cfg
         self.w = weights
-        self.cache = cache
         self.method = method
-        self.device = cache.device
-        cap = index_capacity or (cache.capacity + cache.candidate_slots)
-        self.index_keys = torch.zeros((cap, cfg.index_head_dim), dtype=torch.float8_e4m3fn, device=self.device)
-        self.index_scales = torch.zeros(cap, dtype=torch.float32, device=self.device)
-        # offset[0]: prefill mean hint, offset[1]: decode EMA of the kth score.
-        self.offset = torch.zeros(16, dtype=torch.float32, device=self.device)
         self.last_indices = None
         self.head_scale = cfg.index_n_heads ** -0.5 * cfg.index_head_dim ** -0.5
         (self.qa0, self.qa_n), (self.kv0, self.kv_n), (self.ik0, self.ik_n) = weights.spans_a
         (self.qb0, self.qb_n), (self.iq0, self.iq_n) = weights.spans_b
 
     # ------------------------------------------------------------- projection
-    def project(self, normed, quantized, pos: int, positions, freqs, scope=None):
+    def project(self, state: LayerState, normed, quantized, pos: int, positions, freqs, scope=None):
         scope = scope or (lambda _name: nullcontext())
         cfg, w = self.cfg, self.w
         T = normed.shape[0]
@@ -71,13 +77,13 @@ class AttentionRunner:
             ops.mla_q_rope(b, H, nope, rope, freqs, positions, q_proj, L)
         # KV record straight into its cache row.
         with scope("kv_record"):
-            rows = self.cache.destination_rows(T)
-            ops.kv_finish(kv, L, rope, w.kv_norm, cfg.norm_eps, freqs, positions, self.cache.records, rows)
-            self.cache.finish_append(rows)
+            rows = state.kv.destination_rows(T)
+            ops.kv_finish(kv, L, rope, w.kv_norm, cfg.norm_eps, freqs, positions, state.kv.records, rows)
+            state.kv.finish_append(rows)
         # Indexer key into the resident FP8 key cache.
         with scope("index_k"):
-            ops.index_k(ik, rope, w.index_norm_w, w.index_norm_b, cfg.norm_eps, freqs, positions,
-                        self.index_keys[pos:pos + T], self.index_scales[pos:pos + T])
+            k_rows, s_rows = state.index.rows(pos, T)
+            ops.index_k(ik, rope, w.index_norm_w, w.index_norm_b, cfg.norm_eps, freqs, positions, k_rows, s_rows)
         with scope("index_weights_f32"):
             w_raw = ops.linear_split(normed, w.index_head_split) if normed.is_cuda else ops.linear_f32(normed, w.index_head)
         iq = b[:, self.iq0:self.iq0 + self.iq_n]
@@ -87,55 +93,58 @@ class AttentionRunner:
         return q_proj, q_idx, weights
 
     # ---------------------------------------------------------------- forward
-    def forward(self, normed, quantized, pos: int, positions, freqs, *, scope=None, logits_buf=None):
+    def forward(self, state: LayerState, normed, quantized, pos: int, positions, freqs, *, scope=None,
+                logits_buf=None):
         scope = scope or (lambda _name: nullcontext())
         cfg = self.cfg
         T = normed.shape[0]
         end = pos + T
-        with self.cache.operation():
+        cache = state.kv
+        with cache.operation():
             with scope("attention_projection"):
-                q_proj, q_idx, weights = self.project(normed, quantized, pos, positions, freqs, scope)
+                q_proj, q_idx, weights = self.project(state, normed, quantized, pos, positions, freqs, scope)
+            keys, kscales = state.index.visible(end)
             with scope("indexer"):
                 if logits_buf is not None and logits_buf.shape[0] >= T and logits_buf.shape[1] >= end:
                     logits = logits_buf[:T]
                 else:
                     logits = torch.empty((T, max(4, (end + 3) // 4 * 4)), dtype=torch.float32, device=normed.device)
                 if logits.is_cuda:
-                    ops.lib().indexer_logits(q_idx, self.index_keys[:end], weights, self.index_scales[:end], logits, pos)
+                    ops.lib().indexer_logits(q_idx, keys, weights, kscales, logits, pos)
                 else:
-                    logits = ops.indexer_logits(q_idx, self.index_keys[:end], weights, self.index_scales[:end], pos)
-            if self.method == "echo" and self.cache.offload and pos > 0:
+                    logits = ops.indexer_logits(q_idx, keys, weights, kscales, pos)
+            if self.method == "echo" and cache.offload and pos > 0:
                 with scope("indexer_prefetch"):
-                    self._predictive_prefetch(logits, pos, end)
+                    self._predictive_prefetch(state, logits, pos, end)
             with scope("exact_topk"):
                 values, ids = ops.exact_topk(logits, cfg.index_topk, causal_start=pos, n=end)
-            if self.method == "echo" and self.cache.offload:
+            if self.method == "echo" and cache.offload:
                 with scope("prefetch_hint"):
-                    self._update_hints(logits, values, pos, end)
+                    self._update_hints(state, logits, values, pos, end)
             self.last_indices = ids
             with scope("sparse_mla"):
-                attn = self._consume(q_proj, ids)
+                attn = self._consume(cache, q_proj, ids)
         with scope("attention_output"):
             with scope("expand"):
                 v = ops.mla_expand(attn, self.w.wv_b)
             with scope("o_proj"):
                 return self.w.wo(v.reshape(T, -1))
 
-    def _consume(self, q, ids):
-        if not self.cache.offload:
-            return ops.sparse_mla(q, self.cache.records, ids, self.cfg.attention_scale, value_dim=self.cfg.kv_lora_rank)
+    def _consume(self, cache, q, ids):
+        if not cache.offload:
+            return ops.sparse_mla(q, cache.records, ids, self.cfg.attention_scale, value_dim=self.cfg.kv_lora_rank)
         try:
-            physical = self.cache.ensure(ids)
+            physical = cache.ensure(ids)
         except WorkingSetTooLarge:
             if len(q) == 1:
                 raise ValueError("the pool must fit one query's exact selection") from None
-            self.cache.stats.capacity_splits += 1
+            cache.stats.capacity_splits += 1
             mid = len(q) // 2
-            return torch.cat((self._consume(q[:mid], ids[:mid]), self._consume(q[mid:], ids[mid:])))
-        return ops.sparse_mla(q, self.cache.records, physical, self.cfg.attention_scale, value_dim=self.cfg.kv_lora_rank)
+            return torch.cat((self._consume(cache, q[:mid], ids[:mid]), self._consume(cache, q[mid:], ids[mid:])))
+        return ops.sparse_mla(q, cache.records, physical, self.cfg.attention_scale, value_dim=self.cfg.kv_lora_rank)
 
     # ------------------------------------------------------------ echo method
-    def _predictive_prefetch(self, logits, pos, end):
+    def _predictive_prefetch(self, state, logits, pos, end):
         """Prefetch the provable part of the coming top-k (coarse histogram threshold).
 
         For each query, bucket ``logit - offset[0]`` into 256 monotone bins; the
@@ -145,29 +154,27 @@ class AttentionRunner:
         Budget: min(8192, P - Q) records.
         """
         k = self.cfg.index_topk
-        hist_end = min(pos, self.cache.length)
+        cache = state.kv
+        hist_end = min(pos, cache.length)
         if hist_end <= k:
             return
-        rows = logits[:, :hist_end] - self.offset[0]
+        rows = logits[:, :hist_end] - state.index.offset[0]
         key = _order_bins(rows)
         counts = torch.zeros((rows.shape[0], 257), dtype=torch.int64, device=rows.device)
         counts.scatter_add_(1, key.long(), torch.ones_like(key, dtype=torch.int64))
         above = counts.flip(1).cumsum(1).flip(1)  # elements in bins >= b
         thr = (above[:, 1:] > k).sum(1)            # first bin with <= k elements above it
         pred = key > thr[:, None]
-        budget = min(8192, self.cache.slots - logits.shape[0])
+        budget = min(8192, cache.slots - logits.shape[0])
         cand = torch.nonzero(pred.any(0)).flatten()
         if budget > 0 and cand.numel():
-            self.cache.prefetch(cand, limit=budget)
+            cache.prefetch(cand, limit=budget)
 
-    def _update_hints(self, logits, values, pos, end):
-        self.offset[0] = ops.reference.prefetch_hint(logits[:, :end])
+    def _update_hints(self, state, logits, values, pos, end):
+        off = state.index.offset
+        off[0] = ops.reference.prefetch_hint(logits[:, :end])
         if logits.shape[0] == 1 and end >= 32768:
-            self.offset[1] = ops.reference.decode_hint(self.offset[1], values[0, -1])
-
-    def reset(self):
-        self.cache.reset()
-        self.offset.zero_()
+            off[1] = ops.reference.decode_hint(off[1], values[0, -1])
 
 
 def _order_bins(x: torch.Tensor) -> torch.Tensor:

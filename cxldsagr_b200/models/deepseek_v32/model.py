@@ -24,10 +24,11 @@ from dataclasses import dataclass
 import torch
 
 from ... import ops
+from ...cache.indexer_cache import IndexerCache
 from ...cache.sparse_token_cache import SparseTokenCache
 from ...cache.sparse_token_pool import SharedSparseTokenPool
 from ...config import CacheConfig, ModelConfig
-from .attention import AttentionRunner
+from .attention import AttentionRunner, LayerState
 from .weights import MLPWeights, MoEWeights, load_attention, load_mlp, load_moe
 
 
@@ -99,17 +100,79 @@ class Block:
         self.mlp = mlp
         self.post_norm = post_norm
 
-    def forward(self, hidden, residual, pos, positions, freqs, *, scope=None, logits_buf=None):
+    def forward(self, state, hidden, residual, pos, positions, freqs, *, scope=None, logits_buf=None):
         cfg = self.cfg
         scope = scope or (lambda _n: nullcontext())
         with scope("input_residual_norm"):
             normed, summed, q8, s8 = ops.norm_quant(hidden, residual, self.attention.w.input_norm, cfg.norm_eps)
-        attn = self.attention.forward(normed, (q8, s8), pos, positions, freqs, scope=scope, logits_buf=logits_buf)
+        attn = self.attention.forward(state, normed, (q8, s8), pos, positions, freqs, scope=scope,
+                                      logits_buf=logits_buf)
         with scope("post_attention_residual_norm"):
             normed2, out_res, q2, s2 = ops.norm_quant(summed, attn, self.post_norm, cfg.norm_eps)
         with scope("moe" if isinstance(self.mlp, MoE) else "dense_mlp"):
             out = self.mlp(normed2, (q2, s2), scope) if isinstance(self.mlp, DenseMLP) else self.mlp(normed2, (q2, s2))
         return out, out_res
+
+
+class ModelSession:
+    """One request history: per-layer KV views (resident or pool-backed) + indexer keys.
+
+    ``length`` is the committed history; a failed step poisons nothing but
+    the session's open step (rolled back); a session whose rollback failed is
+    marked ``failed`` and cannot execute again.
+    """
+
+    def __init__(self, model: "DeepSeekV32Model", capacity: int):
+        cc, dev, width = model.cache_cfg, model.device, model.cfg.qk_head_dim
+        self.model = model
+        self.capacity = capacity
+        self.pool_session = model.pool.allocate_session(capacity) if cc.offload else None
+        self.layers: list[LayerState] = []
+        for i in range(len(model.layer_ids)):
+            if cc.offload:
+                kv = self.pool_session.layer(i)
+            else:
+                kv = SparseTokenCache(capacity, width, device=dev, candidate_slots=cc.candidate_tokens)
+            index = IndexerCache(capacity + cc.candidate_tokens, model.cfg.index_head_dim, device=dev)
+            self.layers.append(LayerState(kv, index))
+        self.length = 0
+        self.failed = False
+        self.released = False
+
+    @property
+    def caches(self):
+        return [layer.kv for layer in self.layers]
+
+    def reset(self):
+        for layer in self.layers:
+            layer.kv.reset()
+            layer.index.offset.zero_()
+            layer.index.truncate(0)
+        self.length = 0
+        self.failed = False
+
+    def truncate(self, length: int):
+        for layer in self.layers:
+            layer.kv.truncate(length)
+            layer.index.truncate(length)
+        self.length = length
+
+    def release(self):
+        if self.released:
+            return
+        if self.pool_session is not None:
+            self.pool_session.release()
+        self.layers.clear()
+        self.released = True
+
+    def nbytes(self) -> dict:
+        """Bytes owned by this session alone (shared pool rows are not counted)."""
+        hbm = sum(layer.index.nbytes() for layer in self.layers)
+        if self.pool_session is None:
+            hbm += sum(layer.kv.records.numel() * layer.kv.records.element_size() for layer in self.layers)
+        else:
+            hbm += self.pool_session.session_bytes().get("hbm", 0)
+        return {"hbm": hbm, "dram": 0}
 
 
 @dataclass
@@ -128,7 +191,8 @@ class DeepSeekV32Model:
     """
 
     def __init__(self, cfg: ModelConfig, source, *, device="cuda", cache: CacheConfig | None = None,
-                 layers=None, pool: SharedSparseTokenPool | None = None, scope=None):
+                 layers=None, pool: SharedSparseTokenPool | None = None, scope=None,
+                 allocate_default_session: bool = True):
         self.cfg = cfg
         self.device = torch.device(device)
         self.cache_cfg = cache or CacheConfig(capacity=4096)
@@ -149,31 +213,35 @@ class DeepSeekV32Model:
             host = (host + 63) // 64 * 64
             self.pool = SharedSparseTokenPool(host, width, len(self.layer_ids), P, device=dev,
                                               candidate_slots=cc.candidate_tokens)
-        if cc.offload:
-            self.session = self.pool.allocate_session(cc.capacity)
         self.blocks: list[Block] = []
         for i, layer in enumerate(self.layer_ids):
-            if cc.offload:
-                kv_cache = self.session.layer(i)
-            else:
-                kv_cache = SparseTokenCache(cc.capacity, width, device=dev, candidate_slots=cc.candidate_tokens)
             attn_w = load_attention(source, cfg, layer, device=dev)
-            runner = AttentionRunner(cfg, attn_w, kv_cache, method=cc.method,
-                                     index_capacity=cc.capacity + cc.candidate_tokens)
+            runner = AttentionRunner(cfg, attn_w, method=cc.method)
             if cfg.is_moe_layer(layer):
                 mlp = MoE(cfg, load_moe(source, cfg, layer, device=dev))
             else:
                 mlp = DenseMLP(load_mlp(source, cfg, f"model.layers.{layer}.mlp", device=dev))
             post = source.get_tensor(f"model.layers.{layer}.post_attention_layernorm.weight").to(dev, torch.float32)
             self.blocks.append(Block(cfg, layer, runner, mlp, post.contiguous()))
-        self.length = 0
         self._logits_buf = None
         self.poisoned = False
+        self.session = self.new_session(cc.capacity) if allocate_default_session else None
+
+    # ------------------------------------------------------------- sessions
+    def new_session(self, capacity: int | None = None) -> ModelSession:
+        return ModelSession(self, capacity or self.cache_cfg.capacity)
+
+    def release_session(self, session: ModelSession):
+        session.release()
+
+    @property
+    def length(self) -> int:
+        return self.session.length
 
     # -------------------------------------------------------------- helpers
     @property
     def caches(self):
-        return [b.attention.cache for b in self.blocks]
+        return self.session.caches
 
     def _scope(self):
         return self.scope or (lambda _n: nullcontext())
@@ -190,7 +258,7 @@ class DeepSeekV32Model:
         return buf
 
     # ------------------------------------------------------------- forward
-    def _body(self, ids: torch.Tensor, start: int, chunk: int):
+    def _body(self, session: ModelSession, ids: torch.Tensor, start: int, chunk: int):
         cfg = self.cfg
         scope = self._scope()
         T = ids.numel()
@@ -203,8 +271,8 @@ class DeepSeekV32Model:
                 hidden = ops.embed(ids[c0:c1], self.embed_table)
             residual = None
             logits_buf = self._ensure_logits_buf(c1 - c0, start + c1)
-            for block in self.blocks:
-                hidden, residual = block.forward(hidden, residual, pos, positions, self.freqs,
+            for block, state in zip(self.blocks, session.layers):
+                hidden, residual = block.forward(state, hidden, residual, pos, positions, self.freqs,
                                                  scope=scope, logits_buf=logits_buf)
             out_h, out_r = hidden, residual
         with scope("final_norm_lm_head"):
@@ -218,44 +286,51 @@ class DeepSeekV32Model:
         ops.lib().bf16_gemm(last.contiguous(), 0, D, 0, self.lm_head, 0, D, 0, out, 0, V, 0, last.shape[0], V, D, 1)
         return out
 
-    def forward(self, ids, *, transient: bool = False, chunk_size: int | None = None, commit: bool = True):
-        """Run ``ids`` after the committed history; returns last-token logits.
+    def forward(self, ids, *, session: ModelSession | None = None, transient: bool = False,
+                chunk_size: int | None = None, commit: bool = True):
+        """Run ``ids`` after the session's committed history; returns last-token logits.
 
         ``transient``: candidate tokens (GR); their KV lives only in the GPU
         tail rows and is discarded (history length unchanged).
         """
         if self.poisoned:
             raise RuntimeError("model is poisoned after a failed cleanup")
+        session = session or self.session
+        if session.failed or session.released:
+            raise RuntimeError("session cannot execute after a failure or release")
         ids = ids.to(self.device).reshape(-1)
         T = ids.numel()
         if T == 0:
             raise ValueError("empty token batch")
-        start = self.length
-        for c in self.caches:
+        start = session.length
+        caches = session.caches
+        for c in caches:
             (c.begin_transient if transient else c.begin_step)(T)
         chunk = chunk_size or self.cache_cfg.chunk_size
-        if transient and any(c.offload for c in self.caches):
+        if transient and any(c.offload for c in caches):
             chunk = T  # candidate rows are one batch
         try:
-            logits = self._body(ids, start, chunk)
+            logits = self._body(session, ids, start, chunk)
         except BaseException as primary:
             errors = []
-            for c in self.caches:
+            for c in caches:
                 try:
                     c.rollback()
                 except BaseException as exc:  # noqa: BLE001 - keep every cleanup failure
                     errors.append(exc)
             if errors:
-                self.poisoned = True
+                session.failed = True
                 raise BaseExceptionGroup("forward and cache rollback failed", [primary, *errors]) from None
             raise
         if transient:
-            for c in self.caches:
+            for c in caches:
                 c.discard_transient()
         elif commit:
-            for c in self.caches:
+            for c in caches:
                 c.commit()
-            self.length = start + T
+            for layer in session.layers:
+                layer.index.commit(start + T)
+            session.length = start + T
         return ForwardResult(logits, start, T)
 
     prefill = forward
@@ -263,23 +338,19 @@ class DeepSeekV32Model:
     def extend(self, ids, **kw):
         return self.forward(ids, **kw)
 
-    def candidate(self, ids):
-        return self.forward(ids, transient=True)
+    def candidate(self, ids, *, session: ModelSession | None = None):
+        return self.forward(ids, session=session, transient=True)
 
-    def truncate(self, length: int):
-        for c in self.caches:
-            c.truncate(length)
-        self.length = length
+    def truncate(self, length: int, *, session: ModelSession | None = None):
+        (session or self.session).truncate(length)
 
-    def reset(self):
-        for b in self.blocks:
-            b.attention.reset()
-        self.length = 0
+    def reset(self, *, session: ModelSession | None = None):
+        (session or self.session).reset()
 
     # --------------------------------------------------------- CUDA graph
-    def capture_extend(self, T: int, *, warmup: int = 2) -> "ExtendGraph":
-        """Capture a T-token extend at the current history length into a CUDA graph."""
-        return ExtendGraph(self, T, warmup=warmup)
+    def capture_extend(self, T: int, *, warmup: int = 2, session: ModelSession | None = None) -> "ExtendGraph":
+        """Capture a T-token extend at the session's history length into a CUDA graph."""
+        return ExtendGraph(self, T, warmup=warmup, session=session)
 
 
 class ExtendGraph:
@@ -290,11 +361,12 @@ class ExtendGraph:
     commits with :meth:`commit` or discards with :meth:`rollback`.
     """
 
-    def __init__(self, model: DeepSeekV32Model, T: int, *, warmup: int = 2):
+    def __init__(self, model: DeepSeekV32Model, T: int, *, warmup: int = 2, session: ModelSession | None = None):
         if model.cache_cfg.offload:
             raise ValueError("graph capture covers the resident (hbm) cache method")
         self.model, self.T = model, T
-        self.start = model.length
+        self.session = session or model.session
+        self.start = self.session.length
         dev = model.device
         self.static_ids = torch.zeros(T, dtype=torch.int64, device=dev)
         model._ensure_logits_buf(T, self.start + T)
@@ -302,42 +374,43 @@ class ExtendGraph:
         stream.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(stream):
             for _ in range(warmup):
-                model.forward(self.static_ids, commit=False)
+                model.forward(self.static_ids, session=self.session, commit=False)
                 self._rewind()
         torch.cuda.current_stream(dev).wait_stream(stream)
         self.graph = torch.cuda.CUDAGraph()
-        for c in model.caches:
+        for c in self.session.caches:
             c.begin_step(T)
         from ...ops.native import launch_count
 
         n0 = launch_count()
         with torch.cuda.graph(self.graph, stream=stream):
-            self.static_logits = model._body(self.static_ids, self.start, T)
+            self.static_logits = model._body(self.session, self.static_ids, self.start, T)
         self.launches_per_replay = launch_count() - n0
         model._graph_launches = self.launches_per_replay
         self._rewind()
 
     def _rewind(self):
-        for c in self.model.caches:
+        for c in self.session.caches:
             c._step_end = None
             c.written = c.length = self.start
-        self.model.length = self.start
+        self.session.length = self.start
 
     def replay(self, ids: torch.Tensor):
-        m = self.model
-        if m.length != self.start:
+        if self.session.length != self.start:
             raise RuntimeError("extend graph was captured at another history length")
         self.static_ids.copy_(ids.reshape(-1), non_blocking=True)
-        for c in m.caches:
+        for c in self.session.caches:
             c.begin_step(self.T)
             c.written = self.start + self.T
         self.graph.replay()
         return self.static_logits
 
     def commit(self):
-        for c in self.model.caches:
+        for c in self.session.caches:
             c.commit()
-        self.model.length = self.start + self.T
+        for layer in self.session.layers:
+            layer.index.commit(self.start + self.T)
+        self.session.length = self.start + self.T
 
     def rollback(self):
         self._rewind()

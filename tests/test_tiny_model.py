@@ -33,7 +33,7 @@ def test_resident_vs_pool_offload_identical(tiny):
     r2 = ref.extend(cand).logits
     o2 = off.extend(cand).logits
     assert torch.equal(r2, o2)
-    stats = [b.attention.cache.stats for b in off.blocks]
+    stats = [c.stats for c in off.caches]
     assert sum(s.recalled_records for s in stats) > 0
     assert sum(s.evicted_records for s in stats) > 0
 
