@@ -218,6 +218,10 @@ class ResourceUsage:
     bytes: CacheFootprint = field(default_factory=CacheFootprint)
     host_pages: int = 0
     hbm_tokens: int = 0
+    owner: str = "session"
+
+    def as_mapping(self) -> dict:
+        return {"hbm": self.bytes.hbm, "dram": self.bytes.dram}
 
     @classmethod
     def coerce(cls, value) -> "ResourceUsage":

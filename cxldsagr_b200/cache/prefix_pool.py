@@ -36,7 +36,7 @@ class PrefixEntry:
 class PrefixLease:
     entry: PrefixEntry
     hit: bool
-    evicted: int
+    evicted: tuple  # user keys evicted to admit this lease
 
     @property
     def session(self):
@@ -46,6 +46,7 @@ class PrefixLease:
 class PrefixSessionPool:
     def __init__(self, budget: CacheFootprint | None, *, allocate: Callable, release: Callable,
                  measure: Callable, shared: CacheFootprint | None = None,
+                 measure_shared: Callable | None = None,
                  host_page_capacity: int = 0, hbm_token_capacity: int = 0):
         shared = shared or CacheFootprint()
         if budget is None and host_page_capacity == 0 and hbm_token_capacity == 0:
@@ -55,6 +56,7 @@ class PrefixSessionPool:
         self.budget, self.shared = budget, shared
         self.host_page_capacity, self.hbm_token_capacity = host_page_capacity, hbm_token_capacity
         self._allocate, self._release, self._measure = allocate, release, measure
+        self._measure_shared = measure_shared
         self._entries: "OrderedDict[Hashable, PrefixEntry]" = OrderedDict()
         self.evictions = 0
         self.hits = 0
@@ -119,25 +121,38 @@ class PrefixSessionPool:
         if entry is not None and entry.ready and entry.signature == signature and entry.capacity >= capacity:
             self._entries.move_to_end(key)
             self.hits += 1
-            return PrefixLease(entry, True, 0)
+            return PrefixLease(entry, True, ())
         if entry is not None:  # stale history for this user
             self.discard(key)
         self.misses += 1
-        evicted = 0
+        evicted = []
         while not self._fits(reservation, host_pages, hbm_tokens):
             victim_key = next(iter(self._entries))
             self.discard(victim_key)
-            evicted += 1
+            evicted.append(victim_key)
             self.evictions += 1
         session = self._allocate(plan if plan is not None else capacity)
         entry = PrefixEntry(key, signature, session, capacity, reservation, host_pages, hbm_tokens)
         self._entries[key] = entry
-        return PrefixLease(entry, False, evicted)
+        return PrefixLease(entry, False, tuple(evicted))
 
-    def mark_ready(self, lease: PrefixLease):
-        if self._entries.get(lease.entry.key) is not lease.entry:
-            raise RuntimeError("lease was evicted or replaced before it became ready")
-        lease.entry.ready = True
+    def mark_ready(self, lease_or_key):
+        """Publish a built prefix (by its lease or its user key)."""
+        if isinstance(lease_or_key, PrefixLease):
+            entry = lease_or_key.entry
+            if self._entries.get(entry.key) is not entry:
+                raise RuntimeError("lease was evicted or replaced before it became ready")
+        else:
+            entry = self._entries.get(lease_or_key)
+            if entry is None:
+                raise RuntimeError("no pending lease for this user")
+        entry.ready = True
+
+    def shared_bytes(self) -> CacheFootprint:
+        """Measured bytes of the shared (all-user) cache structures."""
+        if self._measure_shared is None:
+            return self.shared
+        return ResourceUsage.coerce(self._measure_shared()).bytes
 
     def audit(self) -> dict:
         """Measured per-session usage must stay within each reservation."""

@@ -279,6 +279,10 @@ class StateDictSource:
     def keys(self):
         return self.tensors.keys()
 
+    @property
+    def tensor_metadata(self) -> dict:
+        return {n: {"shape": list(t.shape), "dtype": str(t.dtype).removeprefix("torch.")} for n, t in self.tensors.items()}
+
     def get_tensor(self, name: str) -> torch.Tensor:
         try:
             return self.tensors[name]

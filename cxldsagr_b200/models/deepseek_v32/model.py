@@ -29,6 +29,7 @@ from ...cache.sparse_token_cache import SparseTokenCache
 from ...cache.sparse_token_pool import SharedSparseTokenPool
 from ...config import CacheConfig, ModelConfig
 from .attention import AttentionRunner, LayerState
+from .replay import ReplayLayout
 from .weights import MLPWeights, MoEWeights, load_attention, load_mlp, load_moe
 
 
@@ -180,6 +181,7 @@ class ForwardResult:
     logits: torch.Tensor      # fp32 [1, vocab] of the last token
     start: int
     length: int
+    hidden: torch.Tensor | None = None  # final-normed bf16 [rows of the last chunk, dim] when requested
 
 
 class DeepSeekV32Model:
@@ -192,12 +194,15 @@ class DeepSeekV32Model:
 
     def __init__(self, cfg: ModelConfig, source, *, device="cuda", cache: CacheConfig | None = None,
                  layers=None, pool: SharedSparseTokenPool | None = None, scope=None,
-                 allocate_default_session: bool = True):
+                 allocate_default_session: bool = True, replay: bool = False, allocate_pool: bool = True):
         self.cfg = cfg
         self.device = torch.device(device)
         self.cache_cfg = cache or CacheConfig(capacity=4096)
         self.layer_ids = list(range(cfg.num_hidden_layers) if layers is None else layers)
         self.scope = scope
+        # Replay: physical blocks are copies of checkpoint layers 0,1,2 repeated; blocks
+        # >= 3 take clones of their source block's inputs (see replay.ReplayLayout).
+        self.replay_layout = ReplayLayout(tuple(self.layer_ids)) if replay else None
         cc = self.cache_cfg
         dev = self.device
         self.embed_table = source.get_tensor("model.embed_tokens.weight").to(dev, torch.bfloat16).contiguous()
@@ -207,12 +212,10 @@ class DeepSeekV32Model:
         width = cfg.qk_head_dim
         self.pool = pool
         self.session = None
-        if cc.offload and pool is None:
+        if cc.offload and pool is None and allocate_pool:
             P = cc.pool_tokens or min(cc.capacity, 65536)
             host = cc.host_tokens or cc.capacity
-            host = (host + 63) // 64 * 64
-            self.pool = SharedSparseTokenPool(host, width, len(self.layer_ids), P, device=dev,
-                                              candidate_slots=cc.candidate_tokens)
+            self.attach_pool(self.make_pool(host, P))
         self.blocks: list[Block] = []
         for i, layer in enumerate(self.layer_ids):
             attn_w = load_attention(source, cfg, layer, device=dev)
@@ -224,10 +227,22 @@ class DeepSeekV32Model:
             post = source.get_tensor(f"model.layers.{layer}.post_attention_layernorm.weight").to(dev, torch.float32)
             self.blocks.append(Block(cfg, layer, runner, mlp, post.contiguous()))
         self._logits_buf = None
+        self.last_hidden = None
         self.poisoned = False
         self.session = self.new_session(cc.capacity) if allocate_default_session else None
 
     # ------------------------------------------------------------- sessions
+    def make_pool(self, host_tokens: int, pool_tokens: int) -> SharedSparseTokenPool:
+        """A shared sparse-token pool for this model's layers (host rows rounded to 64-token pages)."""
+        host = (host_tokens + 63) // 64 * 64
+        return SharedSparseTokenPool(host, self.cfg.qk_head_dim, len(self.layer_ids), pool_tokens,
+                                     device=self.device, candidate_slots=self.cache_cfg.candidate_tokens)
+
+    def attach_pool(self, pool: SharedSparseTokenPool | None):
+        if pool is not None and pool.num_layers != len(self.layer_ids):
+            raise ValueError("the pool must have one layer per model block")
+        self.pool = pool
+
     def new_session(self, capacity: int | None = None) -> ModelSession:
         return ModelSession(self, capacity or self.cache_cfg.capacity)
 
@@ -258,7 +273,7 @@ class DeepSeekV32Model:
         return buf
 
     # ------------------------------------------------------------- forward
-    def _body(self, session: ModelSession, ids: torch.Tensor, start: int, chunk: int):
+    def _body(self, session: ModelSession, ids: torch.Tensor, start: int, chunk: int, want_hidden: bool = False):
         cfg = self.cfg
         scope = self._scope()
         T = ids.numel()
@@ -271,13 +286,20 @@ class DeepSeekV32Model:
                 hidden = ops.embed(ids[c0:c1], self.embed_table)
             residual = None
             logits_buf = self._ensure_logits_buf(c1 - c0, start + c1)
-            for block, state in zip(self.blocks, session.layers):
+            replay = self.replay_layout.begin_chunk() if self.replay_layout is not None else None
+            for i, (block, state) in enumerate(zip(self.blocks, session.layers)):
+                if replay is not None:
+                    with scope("replay_input_copy"):
+                        hidden, residual = replay.for_layer(i, hidden, residual)
                 hidden, residual = block.forward(state, hidden, residual, pos, positions, self.freqs,
                                                  scope=scope, logits_buf=logits_buf)
             out_h, out_r = hidden, residual
         with scope("final_norm_lm_head"):
-            last, _ = ops.residual_rms_norm(out_h[-1:], out_r[-1:], self.final_norm, cfg.norm_eps)
+            rows = slice(None) if want_hidden else slice(-1, None)
+            normed, _ = ops.residual_rms_norm(out_h[rows], out_r[rows], self.final_norm, cfg.norm_eps)
+            last = normed[-1:]
             logits = ops.linear(last, self.lm_head).float() if not self.device.type == "cuda" else self._lm_head(last)
+        self.last_hidden = normed if want_hidden else None
         return logits
 
     def _lm_head(self, last):
@@ -287,7 +309,7 @@ class DeepSeekV32Model:
         return out
 
     def forward(self, ids, *, session: ModelSession | None = None, transient: bool = False,
-                chunk_size: int | None = None, commit: bool = True):
+                chunk_size: int | None = None, commit: bool = True, return_hidden: bool = False):
         """Run ``ids`` after the session's committed history; returns last-token logits.
 
         ``transient``: candidate tokens (GR); their KV lives only in the GPU
@@ -310,7 +332,7 @@ class DeepSeekV32Model:
         if transient and any(c.offload for c in caches):
             chunk = T  # candidate rows are one batch
         try:
-            logits = self._body(session, ids, start, chunk)
+            logits = self._body(session, ids, start, chunk, want_hidden=return_hidden)
         except BaseException as primary:
             errors = []
             for c in caches:
@@ -331,7 +353,7 @@ class DeepSeekV32Model:
             for layer in session.layers:
                 layer.index.commit(start + T)
             session.length = start + T
-        return ForwardResult(logits, start, T)
+        return ForwardResult(logits, start, T, self.last_hidden)
 
     prefill = forward
 

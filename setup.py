@@ -7,7 +7,7 @@ own arch list when an explicit -gencode flag is present).
 import glob
 import os
 
-from setuptools import setup
+from setuptools import Extension, setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -29,7 +29,14 @@ setup(
             sources=SOURCES,
             include_dirs=[os.path.join(ROOT, "csrc")],
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
-        )
+        ),
+        # Host-only CPython extension (request token validation for the serving runner).
+        Extension(
+            name="cxldsagr_b200.serving._token_validation",
+            sources=["csrc/host/token_validation.cpp"],
+            extra_compile_args=["-O3", "-std=c++17", "-Wall", "-Wextra", "-Werror"],
+            language="c++",
+        ),
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )

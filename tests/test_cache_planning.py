@@ -97,7 +97,7 @@ def test_prefix_pool_hit_miss_and_lru_eviction():
     pool.mark_ready(b)
     assert pool.acquire("a", "sig", 10, r).hit  # refreshes a
     c = pool.acquire("c", "sig", 10, r)  # evicts b (least recently used)
-    assert c.evicted == 1 and "b" not in pool and "a" in pool
+    assert c.evicted == ("b",) and "b" not in pool and "a" in pool
     assert sessions.released == [b.session]
     # Stale signature replaces the entry.
     d = pool.acquire("a", "other", 10, r)
