@@ -56,68 +56,94 @@ class AttentionRunner:
         (self.qb0, self.qb_n), (self.iq0, self.iq_n) = weights.spans_b
 
     # ------------------------------------------------------------- projection
-    def project(self, state: LayerState, normed, quantized, pos: int, positions, freqs, scope=None):
+    def project(self, state: LayerState, normed, quantized, pos: int, positions, freqs, scope=None,
+                gathered=None, rows=None):
+        """Projections of one chunk.
+
+        ``normed`` / ``quantized`` are this rank's query rows [r0, r1) of the
+        chunk (all rows when not sequence parallel).  ``gathered`` is the
+        chunk's full input (FP8 (q, scales^T) or BF16) from the all-gather;
+        the latent KV record and the indexer key are produced for every row
+        (the KV cache is replicated), the query path only for local rows.
+        """
         scope = scope or (lambda _name: nullcontext())
         cfg, w = self.cfg, self.w
-        T = normed.shape[0]
+        T_loc = normed.shape[0]
         H, nope, rope, L = cfg.n_heads, cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.kv_lora_rank
+        r0, r1 = rows if rows is not None else (0, T_loc)
         with scope("fused_a_gemm"):
-            a = w.fused_a(normed, quantized=quantized)
-        qa = a[:, self.qa0:self.qa0 + self.qa_n]
+            if gathered is None:
+                a = w.fused_a(normed, quantized=quantized)
+            elif isinstance(gathered, tuple):
+                a = w.fused_a(quantized=gathered)
+            else:
+                a = w.fused_a(gathered)
+        T = a.shape[0]
+        qa = a[r0:r1, self.qa0:self.qa0 + self.qa_n]
         kv = a[:, self.kv0:self.kv0 + self.kv_n]
         ik = a[:, self.ik0:self.ik0 + self.ik_n]
+        # KV record straight into its cache row (every row of the chunk).
+        with scope("kv_record"):
+            dst = state.kv.destination_rows(T)
+            ops.kv_finish(kv, L, rope, w.kv_norm, cfg.norm_eps, freqs, positions, state.kv.records, dst)
+            state.kv.finish_append(dst)
+        with scope("index_k"):
+            k_rows, s_rows = state.index.rows(pos, T)
+            ops.index_k(ik, rope, w.index_norm_w, w.index_norm_b, cfg.norm_eps, freqs, positions, k_rows, s_rows)
+        if T_loc == 0:
+            return None, None, None
+        q_pos = positions[r0:r1]
         with scope("q_norm"):
             qa_normed, _, qr8, qrs = ops.norm_quant(qa, None, w.q_norm, cfg.norm_eps, want_out=w.fused_b.scales is None)
         with scope("fused_b_gemm"):
             b = w.fused_b(qa_normed, quantized=(qr8, qrs))
-        q_proj = torch.empty((T, H, cfg.qk_head_dim), dtype=torch.bfloat16, device=normed.device)
+        q_proj = torch.empty((T_loc, H, cfg.qk_head_dim), dtype=torch.bfloat16, device=normed.device)
         with scope("absorb"):
             ops.mla_absorb(b, H, nope, rope, w.wk_b_t, q_proj)
         with scope("q_rope"):
-            ops.mla_q_rope(b, H, nope, rope, freqs, positions, q_proj, L)
-        # KV record straight into its cache row.
-        with scope("kv_record"):
-            rows = state.kv.destination_rows(T)
-            ops.kv_finish(kv, L, rope, w.kv_norm, cfg.norm_eps, freqs, positions, state.kv.records, rows)
-            state.kv.finish_append(rows)
-        # Indexer key into the resident FP8 key cache.
-        with scope("index_k"):
-            k_rows, s_rows = state.index.rows(pos, T)
-            ops.index_k(ik, rope, w.index_norm_w, w.index_norm_b, cfg.norm_eps, freqs, positions, k_rows, s_rows)
+            ops.mla_q_rope(b, H, nope, rope, freqs, q_pos, q_proj, L)
         with scope("index_weights_f32"):
             w_raw = ops.linear_split(normed, w.index_head_split) if normed.is_cuda else ops.linear_f32(normed, w.index_head)
         iq = b[:, self.iq0:self.iq0 + self.iq_n]
         with scope("index_q"):
-            q_idx, weights = ops.index_q(iq, cfg.index_n_heads, cfg.index_head_dim, rope, freqs, positions,
+            q_idx, weights = ops.index_q(iq, cfg.index_n_heads, cfg.index_head_dim, rope, freqs, q_pos,
                                          w_raw, self.head_scale)
         return q_proj, q_idx, weights
 
     # ---------------------------------------------------------------- forward
     def forward(self, state: LayerState, normed, quantized, pos: int, positions, freqs, *, scope=None,
-                logits_buf=None):
+                logits_buf=None, gathered=None, rows=None):
+        """One chunk of attention; returns o_proj output for this rank's query rows."""
         scope = scope or (lambda _name: nullcontext())
         cfg = self.cfg
-        T = normed.shape[0]
+        T_loc = normed.shape[0]
+        T = positions.shape[0]
+        r0, r1 = rows if rows is not None else (0, T_loc)
         end = pos + T
         cache = state.kv
         with cache.operation():
             with scope("attention_projection"):
-                q_proj, q_idx, weights = self.project(state, normed, quantized, pos, positions, freqs, scope)
+                q_proj, q_idx, weights = self.project(state, normed, quantized, pos, positions, freqs, scope,
+                                                      gathered=gathered, rows=(r0, r1))
+            if T_loc == 0:
+                return torch.empty((0, cfg.dim), dtype=torch.bfloat16, device=normed.device)
+            qpos = pos + r0
             keys, kscales = state.index.visible(end)
             with scope("indexer"):
-                if logits_buf is not None and logits_buf.shape[0] >= T and logits_buf.shape[1] >= end:
-                    logits = logits_buf[:T]
+                if logits_buf is not None and logits_buf.shape[0] >= T_loc and logits_buf.shape[1] >= end:
+                    logits = logits_buf[:T_loc]
                 else:
-                    logits = torch.empty((T, max(4, (end + 3) // 4 * 4)), dtype=torch.float32, device=normed.device)
+                    logits = torch.empty((T_loc, max(4, (end + 3) // 4 * 4)), dtype=torch.float32,
+                                         device=normed.device)
                 if logits.is_cuda:
-                    ops.lib().indexer_logits(q_idx, keys, weights, kscales, logits, pos)
+                    ops.lib().indexer_logits(q_idx, keys, weights, kscales, logits, qpos)
                 else:
-                    logits = ops.indexer_logits(q_idx, keys, weights, kscales, pos)
+                    logits = ops.indexer_logits(q_idx, keys, weights, kscales, qpos)
             if self.method == "echo" and cache.offload and pos > 0:
                 with scope("indexer_prefetch"):
                     self._predictive_prefetch(state, logits, pos, end)
             with scope("exact_topk"):
-                values, ids = ops.exact_topk(logits, cfg.index_topk, causal_start=pos, n=end)
+                values, ids = ops.exact_topk(logits, cfg.index_topk, causal_start=qpos, n=end)
             if self.method == "echo" and cache.offload:
                 with scope("prefetch_hint"):
                     self._update_hints(state, logits, values, pos, end)
@@ -128,7 +154,7 @@ class AttentionRunner:
             with scope("expand"):
                 v = ops.mla_expand(attn, self.w.wv_b)
             with scope("o_proj"):
-                return self.w.wo(v.reshape(T, -1))
+                return self.w.wo(v.reshape(T_loc, -1))
 
     def _consume(self, cache, q, ids):
         if not cache.offload:

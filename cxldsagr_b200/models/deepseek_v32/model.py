@@ -28,90 +28,148 @@ from ...cache.indexer_cache import IndexerCache
 from ...cache.sparse_token_cache import SparseTokenCache
 from ...cache.sparse_token_pool import SharedSparseTokenPool
 from ...config import CacheConfig, ModelConfig
+from ...parallel.comm import make_comm
+from ...parallel.groups import ParallelContext, shard_range, single
 from .attention import AttentionRunner, LayerState
 from .replay import ReplayLayout
 from .weights import MLPWeights, MoEWeights, load_attention, load_mlp, load_moe
 
 
 class DenseMLP:
-    def __init__(self, w: MLPWeights):
-        self.w = w
+    """SwiGLU MLP.  Under sequence parallelism the weights are column/row sharded:
+    gather the chunk (AG -> gate_up GEMM), SiLU*up, then the row-parallel down
+    GEMM whose partial sums are reduce-scattered back to the row owners."""
 
-    def __call__(self, normed, quantized, scope=None):
+    def __init__(self, w: MLPWeights, comm=None, sharded: bool = False):
+        self.w = w
+        self.comm = comm
+        self.sharded = sharded
+
+    def __call__(self, normed, quantized, scope=None, total: int | None = None):
         scope = scope or (lambda _n: nullcontext())
+        tp = self.sharded and self.comm is not None and self.comm.world > 1
         with scope("gate_up_gemm"):
-            packed = self.w.gate_up(normed, quantized=quantized)
+            if tp:
+                fp8 = self.w.gate_up.scales is not None
+                packed = self.comm.ag_linear(self.w.gate_up, normed, quantized if fp8 else None, total)
+            else:
+                packed = self.w.gate_up(normed, quantized=quantized)
         with scope("silu_mul_quant"):
             h, q, s_t = ops.silu_mul_quant(packed)
         with scope("down_gemm"):
+            if tp:
+                return self.comm.linear_rs(self.w.down, h, (q, s_t) if q is not None else None)
             return self.w.down(h, quantized=(q, s_t))
 
 
 class MoE:
     """Routed experts (sigmoid group-limited top-k) plus the shared expert.
 
-    Single-GPU path: tokens are grouped per expert and each expert runs the
-    FP8 GEMM kernels on its contiguous slice.  The expert-parallel fused
-    dispatch/combine lives in :mod:`cxldsagr_b200.parallel.ep`.
+    Token rows are routed on the rank that holds them, dispatched to the
+    expert owners (all-to-all under expert parallelism), run through the
+    owner's expert GEMMs, sent back and combined per token in a fixed
+    (token, k) slot order, so the sum is deterministic.
     """
 
-    def __init__(self, cfg: ModelConfig, w: MoEWeights):
+    def __init__(self, cfg: ModelConfig, w: MoEWeights, comm=None):
         self.cfg, self.w = cfg, w
+        self.comm = comm
         self.shared = DenseMLP(w.shared) if w.shared is not None else None
 
-    def __call__(self, normed, quantized):
+    def _experts(self, x, s_rows, experts):
+        """Run local experts over rows grouped by expert id; returns bf16 [N, D]."""
         cfg, w = self.cfg, self.w
-        ids, weights = ops.route_experts(normed, w.gate, w.bias, cfg)
-        out = torch.zeros(normed.shape, dtype=torch.float32, device=normed.device)
-        flat = ids.reshape(-1)
-        order = torch.argsort(flat, stable=True)
-        counts = torch.bincount(flat, minlength=cfg.n_routed_experts).tolist()
-        token = order // cfg.num_experts_per_tok
-        start = 0
         I = cfg.moe_intermediate_size
-        for e, n in enumerate(counts):
+        out = torch.zeros((x.shape[0], cfg.dim), dtype=torch.bfloat16, device=x.device)
+        if x.shape[0] == 0:
+            return out
+        local = experts.long() - w.experts.start
+        order = torch.argsort(local, stable=True)
+        counts = torch.bincount(local, minlength=len(w.experts)).tolist()
+        start = 0
+        for j, n in enumerate(counts):
             if n == 0:
                 continue
             sel = order[start:start + n]
             start += n
-            j = e - w.experts.start
-            if not 0 <= j < len(w.experts):
-                continue
-            rows = token[start - n:start]
-            x = normed[rows]
             if w.s_gate_up is not None:
-                packed = ops.fp8_linear(x, w.w_gate_up[j], w.s_gate_up[j])
-                h, q, s_t = ops.silu_mul_quant(packed)
-                y = ops.fp8_gemm(q, s_t, w.w_down[j], w.s_down[j])
+                q, s_t = x[sel], s_rows[sel].t().contiguous()
+                packed = ops.fp8_gemm(q, s_t, w.w_gate_up[j], w.s_gate_up[j])
+                _, hq, hs = ops.silu_mul_quant(packed)
+                y = ops.fp8_gemm(hq, hs, w.w_down[j], w.s_down[j])
             else:
-                packed = ops.linear(x, w.w_gate_up[j])
+                packed = ops.linear(x[sel], w.w_gate_up[j])
                 h = ops.silu_mul(packed[:, :I], packed[:, I:])
                 y = ops.linear(h, w.w_down[j])
-            wt = weights.reshape(-1)[sel]
-            out.index_add_(0, rows, y.float() * wt[:, None])
+            out[sel] = y.to(torch.bfloat16)
+        return out
+
+    def __call__(self, normed, quantized, scope=None):
+        cfg, w = self.cfg, self.w
+        scope = scope or (lambda _n: nullcontext())
+        T, K = normed.shape[0], cfg.num_experts_per_tok
+        with scope("moe_gate"):
+            ids, weights = ops.route_experts(normed, w.gate, w.bias, cfg)
+        fp8 = w.s_gate_up is not None
+        flat = ids.reshape(-1).long()
+        world = 1 if self.comm is None else self.comm.world
+        per = cfg.n_routed_experts // world if world > 1 else cfg.n_routed_experts
+        dest = flat // per if world > 1 else torch.zeros_like(flat)
+        order = torch.argsort(dest * cfg.n_routed_experts + flat, stable=True)   # by owner, then expert
+        token = order // K
+        if fp8:
+            q, s_t = quantized
+            rows, s_rows = q[token], s_t.t()[token].contiguous()
+        else:
+            rows, s_rows = normed[token], None
+        with scope("moe_dispatch"):
+            if world > 1:
+                rrows, rscales, rexp, sc, rc = self.comm.dispatch(rows, s_rows, dest[order], flat[order])
+            else:
+                rrows, rscales, rexp = rows, s_rows, flat[order]
+        with scope("moe_experts"):
+            y = self._experts(rrows, rscales, rexp)
+        with scope("moe_combine"):
+            back = self.comm.combine(y, sc, rc) if world > 1 else y
+            slots = torch.empty((T * K, cfg.dim), dtype=torch.bfloat16, device=normed.device)
+            slots[order] = back
+            out = (slots.view(T, K, cfg.dim).float() * weights.view(T, K, 1).float()).sum(1)
         if self.shared is not None:
-            out += self.shared(normed, quantized).float()
+            with scope("shared_expert"):
+                out += self.shared(normed, quantized).float()
         return out.bfloat16()
 
 
 class Block:
-    def __init__(self, cfg: ModelConfig, layer: int, attention: AttentionRunner, mlp, post_norm):
+    def __init__(self, cfg: ModelConfig, layer: int, attention: AttentionRunner, mlp, post_norm, comm=None):
         self.cfg, self.layer = cfg, layer
         self.attention = attention
         self.mlp = mlp
         self.post_norm = post_norm
+        self.comm = comm
 
-    def forward(self, state, hidden, residual, pos, positions, freqs, *, scope=None, logits_buf=None):
+    def forward(self, state, hidden, residual, pos, positions, freqs, *, scope=None, logits_buf=None, rows=None):
+        """``hidden``/``residual`` hold this rank's rows ``rows=(r0, r1)`` of the chunk."""
         cfg = self.cfg
         scope = scope or (lambda _n: nullcontext())
+        total = positions.shape[0]
         with scope("input_residual_norm"):
             normed, summed, q8, s8 = ops.norm_quant(hidden, residual, self.attention.w.input_norm, cfg.norm_eps)
+        gathered = None
+        if self.comm is not None and self.comm.world > 1:
+            with scope("attention_all_gather"):
+                fp8 = self.attention.w.fused_a.scales is not None
+                gathered = self.comm.gather(normed, (q8, s8) if fp8 else None, total)
         attn = self.attention.forward(state, normed, (q8, s8), pos, positions, freqs, scope=scope,
-                                      logits_buf=logits_buf)
+                                      logits_buf=logits_buf, gathered=gathered, rows=rows)
         with scope("post_attention_residual_norm"):
             normed2, out_res, q2, s2 = ops.norm_quant(summed, attn, self.post_norm, cfg.norm_eps)
-        with scope("moe" if isinstance(self.mlp, MoE) else "dense_mlp"):
-            out = self.mlp(normed2, (q2, s2), scope) if isinstance(self.mlp, DenseMLP) else self.mlp(normed2, (q2, s2))
+        if isinstance(self.mlp, MoE):
+            with scope("moe"):
+                out = self.mlp(normed2, (q2, s2), scope)
+        else:
+            with scope("dense_mlp"):
+                out = self.mlp(normed2, (q2, s2), scope, total=total)
         return out, out_res
 
 
@@ -194,12 +252,15 @@ class DeepSeekV32Model:
 
     def __init__(self, cfg: ModelConfig, source, *, device="cuda", cache: CacheConfig | None = None,
                  layers=None, pool: SharedSparseTokenPool | None = None, scope=None,
-                 allocate_default_session: bool = True, replay: bool = False, allocate_pool: bool = True):
+                 allocate_default_session: bool = True, replay: bool = False, allocate_pool: bool = True,
+                 parallel: ParallelContext | None = None):
         self.cfg = cfg
         self.device = torch.device(device)
         self.cache_cfg = cache or CacheConfig(capacity=4096)
         self.layer_ids = list(range(cfg.num_hidden_layers) if layers is None else layers)
         self.scope = scope
+        self.par = parallel or single(device)
+        self.comm = make_comm(self.par)
         # Replay: physical blocks are copies of checkpoint layers 0,1,2 repeated; blocks
         # >= 3 take clones of their source block's inputs (see replay.ReplayLayout).
         self.replay_layout = ReplayLayout(tuple(self.layer_ids)) if replay else None
@@ -217,15 +278,18 @@ class DeepSeekV32Model:
             host = cc.host_tokens or cc.capacity
             self.attach_pool(self.make_pool(host, P))
         self.blocks: list[Block] = []
+        par, comm = self.par, self.comm
         for i, layer in enumerate(self.layer_ids):
             attn_w = load_attention(source, cfg, layer, device=dev)
             runner = AttentionRunner(cfg, attn_w, method=cc.method)
             if cfg.is_moe_layer(layer):
-                mlp = MoE(cfg, load_moe(source, cfg, layer, device=dev))
+                experts = par.expert_range(cfg.n_routed_experts)
+                mlp = MoE(cfg, load_moe(source, cfg, layer, device=dev, experts=experts), comm)
             else:
-                mlp = DenseMLP(load_mlp(source, cfg, f"model.layers.{layer}.mlp", device=dev))
+                mw = load_mlp(source, cfg, f"model.layers.{layer}.mlp", device=dev, shard=(par.rank, par.world))
+                mlp = DenseMLP(mw, comm, sharded=par.world > 1)
             post = source.get_tensor(f"model.layers.{layer}.post_attention_layernorm.weight").to(dev, torch.float32)
-            self.blocks.append(Block(cfg, layer, runner, mlp, post.contiguous()))
+            self.blocks.append(Block(cfg, layer, runner, mlp, post.contiguous(), comm))
         self._logits_buf = None
         self.last_hidden = None
         self.poisoned = False
@@ -277,28 +341,43 @@ class DeepSeekV32Model:
         cfg = self.cfg
         scope = self._scope()
         T = ids.numel()
-        out_h, out_r = None, None
+        par = self.par
+        out_h, out_r, rows = None, None, (0, 0)
         for c0 in range(0, T, chunk):
             c1 = min(T, c0 + chunk)
             pos = start + c0
             positions = torch.arange(pos, start + c1, device=self.device, dtype=torch.float32)
+            rows = par.token_range(c1 - c0)
             with scope("embedding"):
-                hidden = ops.embed(ids[c0:c1], self.embed_table)
+                hidden = ops.embed(ids[c0 + rows[0]:c0 + rows[1]], self.embed_table)
             residual = None
-            logits_buf = self._ensure_logits_buf(c1 - c0, start + c1)
+            logits_buf = self._ensure_logits_buf(max(rows[1] - rows[0], 1), start + c1)
             replay = self.replay_layout.begin_chunk() if self.replay_layout is not None else None
             for i, (block, state) in enumerate(zip(self.blocks, session.layers)):
                 if replay is not None:
                     with scope("replay_input_copy"):
                         hidden, residual = replay.for_layer(i, hidden, residual)
                 hidden, residual = block.forward(state, hidden, residual, pos, positions, self.freqs,
-                                                 scope=scope, logits_buf=logits_buf)
+                                                 scope=scope, logits_buf=logits_buf, rows=rows)
             out_h, out_r = hidden, residual
         with scope("final_norm_lm_head"):
-            rows = slice(None) if want_hidden else slice(-1, None)
-            normed, _ = ops.residual_rms_norm(out_h[rows], out_r[rows], self.final_norm, cfg.norm_eps)
-            last = normed[-1:]
-            logits = ops.linear(last, self.lm_head).float() if not self.device.type == "cuda" else self._lm_head(last)
+            n_last = c1 - c0
+            owner = next(r for r in range(par.world) if par.world == 1 or
+                         shard_range(n_last, par.world, r)[0] <= n_last - 1 < shard_range(n_last, par.world, r)[1])
+            keep = slice(None) if want_hidden else slice(-1, None)
+            normed = None
+            if out_h.shape[0]:
+                normed, _ = ops.residual_rms_norm(out_h[keep], out_r[keep], self.final_norm, cfg.norm_eps)
+            logits = torch.empty((1, self.lm_head.shape[0]), dtype=torch.float32, device=self.device)
+            if par.rank == owner:
+                last = normed[-1:]
+                logits = ops.linear(last, self.lm_head).float() if self.device.type != "cuda" else self._lm_head(last)
+            if par.world > 1:
+                logits = self.comm.broadcast(logits.contiguous(), owner)
+                if want_hidden:
+                    local = normed if normed is not None else torch.empty((0, cfg.dim), dtype=torch.bfloat16,
+                                                                         device=self.device)
+                    normed = self.comm.gather_rows(local, n_last)
         self.last_hidden = normed if want_hidden else None
         return logits
 

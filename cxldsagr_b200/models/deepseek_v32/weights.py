@@ -161,11 +161,36 @@ def load_attention(source, cfg: ModelConfig, layer: int, *, device) -> Attention
     )
 
 
-def load_mlp(source, cfg: ModelConfig, stem: str, *, device) -> MLPWeights:
+def _slice_rows(lin: Linear, r0: int, r1: int) -> Linear:
+    if lin.scales is None:
+        return Linear(lin.weight[r0:r1].contiguous())
+    if r0 % 128 or r1 % 128:
+        raise ValueError("FP8 row shards must align to the 128-row scale blocks")
+    return Linear(lin.weight[r0:r1].contiguous(), lin.scales[r0 // 128:r1 // 128].contiguous())
+
+
+def _slice_cols(lin: Linear, c0: int, c1: int) -> Linear:
+    if lin.scales is None:
+        return Linear(lin.weight[:, c0:c1].contiguous())
+    if c0 % 128 or c1 % 128:
+        raise ValueError("FP8 column shards must align to the 128-column scale blocks")
+    return Linear(lin.weight[:, c0:c1].contiguous(), lin.scales[:, c0 // 128:c1 // 128].contiguous())
+
+
+def load_mlp(source, cfg: ModelConfig, stem: str, *, device, shard: tuple[int, int] = (0, 1)) -> MLPWeights:
+    """Dense SwiGLU MLP; ``shard=(rank, world)`` keeps a column slice of gate/up and
+    the matching row slice (input columns) of down (tensor parallel)."""
     dt = cfg.weight_dtype
     gate = load_linear(source, stem + ".gate_proj", device=device, dtype=dt)
     up = load_linear(source, stem + ".up_proj", device=device, dtype=dt)
     down = load_linear(source, stem + ".down_proj", device=device, dtype=dt)
+    rank, world = shard
+    if world > 1:
+        inter = gate.out_features
+        if inter % world:
+            raise ValueError("intermediate size must divide across ranks")
+        c0, c1 = rank * inter // world, (rank + 1) * inter // world
+        gate, up, down = _slice_rows(gate, c0, c1), _slice_rows(up, c0, c1), _slice_cols(down, c0, c1)
     gate_up, _ = pack_linears([gate, up])
     return MLPWeights(gate_up, down, gate.out_features)
 

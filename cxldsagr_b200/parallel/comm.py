@@ -1,0 +1,96 @@
+"""Communication-fused linear ops used by the sequence/expert-parallel model.
+
+Each op is named for the compute it wraps, so a backend can fuse the
+collective into the kernel:
+
+* :meth:`Comm.ag_linear`  — all-gather of the row-sharded input, then a linear
+  over all rows (AG -> GEMM);
+* :meth:`Comm.linear_rs`  — a row-parallel linear whose partial sums are
+  reduce-scattered by rows (GEMM -> RS);
+* :meth:`Comm.dispatch` / :meth:`Comm.combine` — expert-parallel all-to-all of
+  token rows to the expert owners and of expert outputs back.
+
+:class:`Comm` is the baseline over ``torch.distributed`` (NCCL on GPUs, gloo on
+CPU): a library collective followed by this package's GEMM.  The fused
+peer-memory backend (:mod:`.p2p`) implements the same methods with one kernel
+per op.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import ops
+from . import collectives as C
+from .groups import ParallelContext
+
+
+class Comm:
+    def __init__(self, ctx: ParallelContext):
+        self.ctx = ctx
+
+    @property
+    def world(self) -> int:
+        return self.ctx.world
+
+    # ------------------------------------------------------------------ AG
+    def gather(self, normed, quantized, total: int):
+        """Full-chunk input of a column-parallel/replicated linear: FP8 (q, s^T) or BF16 rows."""
+        if self.world == 1:
+            return quantized if quantized is not None and quantized[0] is not None else normed
+        if quantized is not None and quantized[0] is not None:
+            q, s_t = quantized
+            return C.all_gather_rows(self.ctx, q, total, 0), C.all_gather_rows(self.ctx, s_t, total, 1)
+        return C.all_gather_rows(self.ctx, normed, total, 0)
+
+    def ag_linear(self, lin, normed, quantized, total: int) -> torch.Tensor:
+        g = self.gather(normed, quantized, total)
+        return lin(quantized=g) if isinstance(g, tuple) else lin(g)
+
+    # ------------------------------------------------------------------ RS
+    def linear_rs(self, lin, h, quantized) -> torch.Tensor:
+        """Row-parallel linear over all rows, reduced and scattered to the row owners."""
+        partial = lin(h, quantized=quantized)
+        if self.world == 1:
+            return partial
+        return C.reduce_scatter_rows(self.ctx, partial, out_dtype=torch.bfloat16)
+
+    # -------------------------------------------------------------- EP a2a
+    def dispatch(self, rows: torch.Tensor, scales_rows, dest: torch.Tensor, experts: torch.Tensor):
+        """Send token rows to expert owners.
+
+        ``rows`` [N, D] are already ordered by destination rank (``dest``
+        non-decreasing); ``scales_rows`` [N, D/128] (FP8 rows) or None;
+        ``experts`` [N] global expert id per row.  Returns the received rows,
+        scales, expert ids and the per-source counts.
+        """
+        counts = torch.bincount(dest, minlength=self.world).tolist()
+        recv, rc = C.all_to_all_rows(self.ctx, rows, counts)
+        rs = C.all_to_all_back(self.ctx, scales_rows, counts, rc) if scales_rows is not None else None
+        re = C.all_to_all_back(self.ctx, experts.to(torch.int32), counts, rc)
+        return recv, rs, re, counts, rc
+
+    def combine(self, out_rows: torch.Tensor, send_counts, recv_counts) -> torch.Tensor:
+        """Return expert outputs to the rows' source ranks (inverse of :meth:`dispatch`)."""
+        return C.all_to_all_back(self.ctx, out_rows, recv_counts, send_counts)
+
+    # ---------------------------------------------------------------- misc
+    def gather_rows(self, x, total: int):
+        return x if self.world == 1 else C.all_gather_rows(self.ctx, x, total, 0)
+
+    def broadcast(self, x, src: int):
+        return C.broadcast(self.ctx, x, src)
+
+
+def make_comm(ctx: ParallelContext) -> Comm:
+    if ctx.backend == "p2p" and ctx.world > 1:
+        from .p2p import P2PComm
+
+        return P2PComm(ctx)
+    return Comm(ctx)
+
+
+def quantize_rows(x: torch.Tensor):
+    """FP8 rows + per-row scales [N, D/128] (row-major, for row-wise transport)."""
+    q, s_t = ops.quantize_act(x)
+    return q, s_t.t().contiguous()
