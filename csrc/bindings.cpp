@@ -280,6 +280,97 @@ void gather_rows(const Tensor& host, Tensor& records, const Tensor& host_ids, co
                            row_bytes, host.size(0), records.size(0), err_ptr(records), stream());
 }
 
+// `call` numbers this op's calls from 1 (parity = call & 1); targets are the cumulative flag counts.
+b200::P2PArgs make_p2p(int64_t rank, int64_t world, int64_t S, int64_t call, int64_t arrive_target,
+                      int64_t reuse_target, const std::vector<int64_t>& flags, const std::vector<int64_t>& g,
+                      const std::vector<int64_t>& gs, const std::vector<int64_t>& rb) {
+  if (world < 1 || world > b200::kMaxRanks || int64_t(flags.size()) != world) throw std::invalid_argument("p2p: bad world");
+  b200::P2PArgs p;
+  p.rank = int(rank);
+  p.world = int(world);
+  p.S = int(S);
+  p.parity = int(call & 1);
+  p.arrive_target = uint64_t(arrive_target);
+  p.reuse_target = uint64_t(reuse_target);
+  for (int q = 0; q < world; ++q) {
+    p.flags[q] = reinterpret_cast<uint64_t*>(flags[q]);
+    if (!g.empty()) p.g[q] = reinterpret_cast<uint8_t*>(g[q]);
+    if (!gs.empty()) p.gs[q] = reinterpret_cast<float*>(gs[q]);
+    if (!rb.empty()) p.rb[q] = reinterpret_cast<__nv_bfloat16*>(rb[q]);
+  }
+  return p;
+}
+
+// AG-GEMM: q_local [S, K] fp8, s_local_t [K/128, S] fp32 -> out [world*S, N] bf16.
+void fp8_gemm_ag(const Tensor& q_local, const Tensor& s_local_t, const Tensor& w, const Tensor& w_s, Tensor& out,
+                 int64_t rank, int64_t world, int64_t call, int64_t arrive_target, int64_t reuse_target,
+                 const std::vector<int64_t>& flags, const std::vector<int64_t>& g, const std::vector<int64_t>& gs) {
+  const int64_t S = q_local.size(0), K = q_local.size(1), N = w.size(0);
+  TORCH_CHECK(q_local.is_contiguous() && s_local_t.is_contiguous() && s_local_t.size(1) == S, "ag: layout");
+  TORCH_CHECK(out.size(0) == world * S && out.size(1) == N && out.is_contiguous(), "ag: out shape");
+  c10::cuda::CUDAGuard guard(q_local.device());
+  auto p = make_p2p(rank, world, S, call, arrive_target, reuse_target, flags, g, gs, {});
+  p.grid = b200::fp8_gemm_ag_grid(int(world * S), int(N));
+  p.a_local = reinterpret_cast<const uint8_t*>(q_local.data_ptr());
+  p.sfa_local = s_local_t.data_ptr<float>();
+  b200::launch_fp8_gemm_ag(p, reinterpret_cast<const uint8_t*>(w.data_ptr()), int(w.stride(0)), w_s.data_ptr<float>(),
+                           reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), int(out.stride(0)), int(world * S), int(N),
+                           int(K), err_ptr(q_local), at::cuda::getCurrentCUDAStream());
+}
+
+// GEMM-RS: a_q [world*S, K] fp8 (+ a_s_t [K/128, world*S]) -> out [S, N] bf16 (+ residual).
+void fp8_gemm_rs(const Tensor& a_q, const Tensor& a_s_t, const Tensor& w, const Tensor& w_s,
+                 const c10::optional<Tensor>& residual, Tensor& out, int64_t rank, int64_t world, int64_t call,
+                 int64_t arrive_target, int64_t reuse_target, const std::vector<int64_t>& flags,
+                 const std::vector<int64_t>& rb) {
+  const int64_t M = a_q.size(0), K = a_q.size(1), N = w.size(0);
+  TORCH_CHECK(M % world == 0, "rs: rows must split evenly");
+  const int64_t S = M / world;
+  TORCH_CHECK(out.size(0) == S && out.size(1) == N && out.is_contiguous(), "rs: out shape");
+  c10::cuda::CUDAGuard guard(a_q.device());
+  auto p = make_p2p(rank, world, S, call, arrive_target, reuse_target, flags, {}, {}, rb);
+  p.reduce_grid = b200::rs_reduce_grid(int(S), int(N));
+  const __nv_bfloat16* res = residual ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr;
+  b200::launch_fp8_gemm_rs(p, reinterpret_cast<const uint8_t*>(a_q.data_ptr()), int(a_q.stride(0)),
+                           a_s_t.data_ptr<float>(), int(a_s_t.stride(0)), reinterpret_cast<const uint8_t*>(w.data_ptr()),
+                           int(w.stride(0)), w_s.data_ptr<float>(), int(M), int(N), int(K), res,
+                           residual ? int(residual->stride(0)) : 0, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                           int(out.stride(0)), err_ptr(a_q), at::cuda::getCurrentCUDAStream());
+}
+
+void p2p_barrier(int64_t device, int64_t rank, int64_t world, int64_t call, const std::vector<int64_t>& flags) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  auto p = make_p2p(rank, world, 1, call, call, 0, flags, {}, {}, {});
+  b200::launch_p2p_barrier(p, error_word_ref(int(device)).data_ptr<int>(), at::cuda::getCurrentCUDAStream());
+}
+
+int64_t symm_alloc(int64_t device, int64_t bytes) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  return int64_t(b200::symm_alloc(size_t(bytes)));
+}
+void symm_free(int64_t device, int64_t ptr) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  b200::symm_free(uintptr_t(ptr));
+}
+py::bytes symm_handle(int64_t device, int64_t ptr) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  auto h = b200::symm_handle(uintptr_t(ptr));
+  return py::bytes(reinterpret_cast<const char*>(h.data()), h.size());
+}
+int64_t symm_open(int64_t device, const std::string& handle) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  return int64_t(b200::symm_open(std::vector<uint8_t>(handle.begin(), handle.end())));
+}
+void symm_close(int64_t device, int64_t ptr) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  b200::symm_close(uintptr_t(ptr));
+}
+// A tensor view of device memory at `ptr` (no ownership; the heap owns it).
+Tensor symm_view(int64_t device, int64_t ptr, int64_t bytes) {
+  auto opts = torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, device);
+  return torch::from_blob(reinterpret_cast<void*>(ptr), {bytes}, [](void*) {}, opts);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -302,4 +393,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sparse_mla_scratch_bytes", &sparse_mla_scratch_bytes);
   m.def("fp8_gemm_splits", &fp8_gemm_splits);
   m.def("gather_rows", &gather_rows);
+  m.def("fp8_gemm_ag", &fp8_gemm_ag);
+  m.def("fp8_gemm_rs", &fp8_gemm_rs);
+  m.def("p2p_barrier", &p2p_barrier);
+  m.def("fp8_gemm_ag_grid", [](int64_t M, int64_t N) { return int64_t(b200::fp8_gemm_ag_grid(int(M), int(N))); });
+  m.def("rs_reduce_grid", [](int64_t S, int64_t N) { return int64_t(b200::rs_reduce_grid(int(S), int(N))); });
+  m.def("symm_alloc", &symm_alloc);
+  m.def("symm_free", &symm_free);
+  m.def("symm_handle", &symm_handle);
+  m.def("symm_open", &symm_open);
+  m.def("symm_close", &symm_close);
+  m.def("symm_view", &symm_view);
 }

@@ -1,0 +1,42 @@
+// Host/device description of one communication-fused call over peer memory:
+// rank coordinates, call parity, flag targets, and every rank's buffer / flag pointers in the
+// symmetric heap.  Plain data (no device code), shared by kernels and bindings.
+#pragma once
+#include <cstdint>
+#include <cuda_bf16.h>
+
+namespace b200 {
+
+constexpr int kMaxRanks = 8;
+// Flag block layout (u64 slots) per rank.
+constexpr int kFlagAgArrive = 0;    // + src: CTAs of src that finished pushing its shard here
+constexpr int kFlagAgDone = 8;      // + src: CTAs of src's AG-GEMM that finished reading
+constexpr int kFlagRsArrive = 16;   // + src: output tiles src stored into this rank's slot
+constexpr int kFlagRsDone = 24;     // + src: reduce CTAs of src that finished reading
+constexpr int kFlagA2aArrive = 32;  // + src: dispatch / combine CTAs of src that finished writing here
+constexpr int kFlagA2aDone = 40;    // + src: consumers of src that finished reading
+constexpr int kFlagBarrier = 48;    // + src: barrier calls
+constexpr int kFlagSlots = 64;
+
+// Peer pointers and flag targets of one fused call (passed by value as a kernel argument).
+struct P2PArgs {
+  int rank = 0;
+  int world = 1;
+  int S = 0;                    // rows per rank; the gathered / reduced extent is M = world * S
+  int parity = 0;               // call number & 1: which half of the double-buffered exchange buffers
+  // Flag counters are cumulative over calls; the host tracks the totals.
+  uint64_t arrive_target = 0;   // arrival count (incl. this call) to wait for before reading peer data
+  uint64_t reuse_target = 0;    // reader-done count of the call two back on this parity (0: none)
+  int grid = 0;                 // CTAs of the GEMM (identical on every rank)
+  int reduce_grid = 0;          // CTAs of the reduce kernel (RS)
+  // AG: this rank's shard and every rank's gather buffers ([2][M][K] fp8, [2][K/128][M] fp32)
+  const uint8_t* a_local = nullptr;
+  const float* sfa_local = nullptr;  // [K/128, S]
+  uint8_t* g[kMaxRanks] = {};
+  float* gs[kMaxRanks] = {};
+  // RS: every rank's receive slots ([2][world][S][N] bf16)
+  __nv_bfloat16* rb[kMaxRanks] = {};
+  uint64_t* flags[kMaxRanks] = {};  // every rank's flag block
+};
+
+}  // namespace b200

@@ -3,7 +3,7 @@
 // * mbarrier init / arrive / expect_tx and a BOUNDED wait: every wait gives up
 //   after a wall-clock budget, records an error code in the device error word
 //   and returns false so the caller can drain and exit (no trap, no hang).
-// * TMA tiled loads (cp.async.bulk.tensor, never with .multicast::cluster) and
+// * TMA tiled loads (cp.async.bulk.tensor into this CTA only, no cluster fan-out) and
 //   untiled bulk copies.
 // * tcgen05: TMEM alloc/dealloc, MMA (kind::f16, kind::f8f6f4), commit to an
 //   mbarrier, 32x32b loads, fences.
@@ -380,7 +380,7 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t addr, uint32_t l
 namespace b200 {
 // Four arbitrary rows (row coordinates r0..r3; out-of-range rows read as zero)
 // x one box of columns starting at x, written as 4 consecutive box rows.  The
-// tensor map's box must be one row high.  Never used with .multicast.
+// tensor map's box must be one row high.  Loads land in this CTA only.
 __device__ __forceinline__ void tma_gather4(void* dst, const void* desc, uint64_t* bar, int x, int r0,
                                             int r1, int r2, int r3) {
   asm volatile(

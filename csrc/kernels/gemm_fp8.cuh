@@ -1,0 +1,424 @@
+// FP8 block-scaled GEMM on the sm_100a tensor core (tcgen05 + TMEM + TMA).
+//
+//   out[m, n] = sum_kb  sfa[kb, m] * sfb[n / 128, kb] * sum_{k in kb} A[m, k] * B[n, k]
+//
+// A: E4M3 activations [M, K] (K contiguous) with 1x128 scales stored
+//    transposed as sfa[K/128, lda_s] (so a warp reads 32 consecutive rows);
+// B: E4M3 weights [N, K] with one FP32 scale per 128x128 block, sfb[ceil(N/128), K/128].
+// This is the checkpoint FP8 linear (reference: DeepGEMM fp8_gemm_nt with the
+// (1,128,128) recipe, operators/deepseek_v32/linear/fp8.py:200-258).
+//
+// Design (one persistent CTA per SM):
+//   warp 0     TMA producer: A tile 128x128 B and B tile BNx128 B per stage,
+//              128-byte swizzle, STAGES-deep ring of mbarriers.
+//   warp 1     TMEM allocator + single-thread MMA issuer: 4 x tcgen05.mma
+//              kind::f8f6f4 (M=128, N=BN, K=32) per 128-wide K block into one
+//              of two TMEM accumulators, then tcgen05.commit to release the
+//              smem stage and to signal the epilogue.
+//   warps 2-9  promotion/epilogue: each thread owns one output row and half of
+//              the tile's columns (two warps per TMEM lane quadrant); per K
+//              block it reads the fresh partial sums from TMEM (tcgen05.ld),
+//              scales them by sfa*sfb and accumulates in FP32 registers, so
+//              arbitrary (non power-of-two) weight block scales stay exact.
+//              Two TMEM buffers let the tensor core run the next K block
+//              meanwhile.
+//
+// Communication modes (template MODE, peer pointers in P2PArgs):
+//   AG (all-gather -> GEMM): A is the chunk gathered from every rank's row
+//      shard.  At kernel start the epilogue warps of every CTA (idle until the
+//      first accumulator is ready) push a slice of this rank's shard and its
+//      scales into every rank's gather buffer with 16-byte st.global over
+//      NVLink, then bump each rank's arrival counter.  The TMA producer waits
+//      (bounded, system-scope acquire) for the shards a tile needs, fences the
+//      async proxy and loads the tile from local memory only.
+//   RS (GEMM -> reduce-scatter): row m belongs to rank m / S; the epilogue
+//      stores each row's BF16 partial straight into the owner's receive slot
+//      for this rank and, after the whole tile, bumps the owner's arrival
+//      counter; the owner's reduce kernel sums the slots in rank order.
+// Every wait (mbarrier or peer flag) is bounded: error word + orderly exit.
+#pragma once
+#include "../common/p2p.cuh"
+#include "../common/ptx.cuh"
+#include "launchers.h"
+
+namespace b200 {
+namespace gemm_fp8 {
+
+constexpr int kModePlain = 0, kModeAG = 1, kModeRS = 2;
+constexpr int BM = 128;
+constexpr int BK = 128;  // bytes of K per stage (= one scale block)
+constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each owning BN/2 columns
+constexpr int kThreads = 64 + kEpiWarps * 32;
+constexpr int kEpiBarrier = 1;  // named barrier id of the 256 epilogue threads
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  alignas(1024) uint8_t a[STAGES][BM * BK];
+  alignas(1024) uint8_t b[STAGES][BN * BK];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+// Tile order: m-major within a column of tiles.  RS rotates the m blocks so
+// that ranks start on different owners (spreads the NVLink traffic).
+__device__ __forceinline__ int tile_m_block(int tile, int num_m, int rot) {
+  int mb = tile % num_m + rot;
+  return mb >= num_m ? mb - num_m : mb;
+}
+
+// AG: wait until every shard overlapping rows [m0, m0 + BM) has arrived here.
+__device__ __forceinline__ bool ag_wait_rows(const P2PArgs& p, int m0, int M, uint32_t& ready, int* err,
+                                             volatile int* abort_flag) {
+  const int s0 = m0 / p.S, s1 = min(M - 1, m0 + BM - 1) / p.S;
+  for (int s = s0; s <= s1; ++s) {
+    if (ready & (1u << s)) continue;
+    const uint64_t* f = p.flags[p.rank] + kFlagAgArrive + s;
+    if (!wait_flag_ge(f, p.arrive_target, err, kErrTimeoutPeerFlag, abort_flag)) return false;
+    ready |= 1u << s;
+  }
+  return true;
+}
+
+template <int BN, int STAGES, int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    fp8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
+                    const __grid_constant__ CUtensorMap tma_b, const float* __restrict__ sfa,
+                    int lda_s, const float* __restrict__ sfb, __nv_bfloat16* __restrict__ out,
+                    int ldo, const __nv_bfloat16* __restrict__ residual, int ldr, int M, int N,
+                    int K, int splits, float* __restrict__ partial, int* err,
+                    const __grid_constant__ P2PArgs p2p) {
+  extern __shared__ uint8_t smem_raw[];
+  auto& s = *reinterpret_cast<GemmSmem<BN, STAGES>*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int num_m = (M + BM - 1) / BM;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + BK - 1) / BK;
+  const int kb_scale_stride = num_kb;  // sfb row length
+  // Work unit = (tile, K split); split-major so concurrent CTAs share a K range.
+  const int num_units = num_tiles * splits;
+  const int kps = (num_kb + splits - 1) / splits;
+  const int rot = MODE == kModeRS ? ((p2p.rank + 1) % p2p.world) * p2p.S / BM % num_m : 0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.tmem_full[i], 1);
+      mbar_init(&s.tmem_empty[i], kEpiWarps);
+    }
+    s.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&s.tmem_base, 2 * BN);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  volatile int* abort_flag = &s.abort_flag;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t ready = 0;  // AG: shards known to have arrived
+      bool ok = true;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const int tile = u % num_tiles, sp = u / num_tiles;
+        const int m0 = tile_m_block(tile, num_m, rot) * BM;
+        const int n0 = (tile / num_m) * BN;
+        const int kb0 = sp * kps, kb1 = min(num_kb, kb0 + kps);
+        if constexpr (MODE == kModeAG) {
+          if (!ag_wait_rows(p2p, m0, M, ready, err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_global();
+        }
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&s.empty[stage], phase ^ 1, err, kErrTimeoutSmemEmpty, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&s.full[stage], BM * BK + BN * BK);
+          tma_load_2d(s.a[stage], &tma_a, &s.full[stage], kb * BK, m0);
+          tma_load_2d(s.b[stage], &tma_b, &s.full[stage], kb * BK, n0);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Drain copies already in flight before the CTA releases its smem.
+        for (int i = 0; i < STAGES; ++i) mbar_wait(&s.full[i], 0, nullptr, 0, nullptr, 100000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      const uint32_t idesc = umma_idesc(BM, BN, 0, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t kcount = 0;  // global K-block counter -> TMEM buffer + parity
+      bool ok = true;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const int sp = u / num_tiles;
+        const int kb0 = sp * kps, kb1 = min(num_kb, kb0 + kps);
+        for (int kb = kb0; kb < kb1; ++kb, ++kcount) {
+          const uint32_t buf = kcount & 1;
+          const uint32_t bpar = (kcount >> 1) & 1;
+          if (!mbar_wait(&s.tmem_empty[buf], bpar ^ 1, err, kErrTimeoutTmemEmpty, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (!mbar_wait(&s.full[stage], phase, err, kErrTimeoutTmaFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = umma_desc_sw128(smem_u32(s.a[stage]));
+          const uint64_t bdesc = umma_desc_sw128(smem_u32(s.b[stage]));
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k) {
+            // +32 bytes along K inside the swizzled 128-byte row.
+            mma_f8_ss(tmem + buf * BN, adesc + (k * 32 >> 4), bdesc + (k * 32 >> 4), idesc, k > 0);
+          }
+          mma_commit(&s.empty[stage]);
+          mma_commit(&s.tmem_full[buf]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else {
+    // Epilogue warps 2..9: TMEM lane quadrant = warp % 4; warps 2-5 own
+    // columns [0, BN/2), warps 6-9 columns [BN/2, BN).
+    constexpr int CPW = BN / 2;
+    const int quad = warp & 3;
+    const int chalf = (warp - 2) / 4;
+    const int row_in_tile = quad * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    bool ok = true;
+
+    if constexpr (MODE == kModeAG) {
+      // Push this rank's shard (rows [rank*S, rank*S+S) of the gathered A) and
+      // its scales into every rank's gather buffer (this call's parity half).
+      const int et = threadIdx.x - 64;
+      if (et == 0 && p2p.reuse_target > 0) {
+        // Reuse guard: rank q finished reading this parity two calls ago.
+        for (int q = 0; q < p2p.world && ok; ++q)
+          ok = wait_flag_ge(p2p.flags[p2p.rank] + kFlagAgDone + q, p2p.reuse_target, err, kErrTimeoutPeerFlag,
+                            abort_flag);
+      }
+      named_barrier(kEpiBarrier, kEpiWarps * 32);
+      if (*abort_flag) ok = false;
+      if (ok) {
+        const int64_t stride = int64_t(gridDim.x) * kEpiWarps * 32;
+        const int64_t gt = int64_t(blockIdx.x) * kEpiWarps * 32 + et;
+        const int vec_per_row = K / 16;
+        const int64_t nvec = int64_t(p2p.S) * vec_per_row;
+        const int64_t row_base = int64_t(p2p.parity) * M + int64_t(p2p.rank) * p2p.S;
+        for (int64_t v = gt; v < nvec; v += stride) {
+          const int64_t r = v / vec_per_row, c = v % vec_per_row;
+          const uint4 val = *reinterpret_cast<const uint4*>(p2p.a_local + r * K + c * 16);
+          for (int q = 0; q < p2p.world; ++q)
+            *reinterpret_cast<uint4*>(p2p.g[q] + (row_base + r) * K + c * 16) = val;
+        }
+        const int64_t nsc = int64_t(num_kb) * p2p.S;
+        for (int64_t i = gt; i < nsc; i += stride) {
+          const int64_t kb = i / p2p.S, j = i % p2p.S;
+          const float val = p2p.sfa_local[kb * p2p.S + j];
+          for (int q = 0; q < p2p.world; ++q)
+            p2p.gs[q][(int64_t(p2p.parity) * num_kb + kb) * M + int64_t(p2p.rank) * p2p.S + j] = val;
+        }
+      }
+      named_barrier(kEpiBarrier, kEpiWarps * 32);
+      if (et == 0 && ok) {
+        __threadfence_system();
+        for (int q = 0; q < p2p.world; ++q) red_release_sys_add(p2p.flags[q] + kFlagAgArrive + p2p.rank, 1);
+      }
+    }
+
+    uint32_t kcount = 0;
+    uint32_t ready = 0;
+    int owner_ok = -1;  // RS: owner whose reuse guard this thread already passed
+    for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      const int tile = u % num_tiles, sp = u / num_tiles;
+      const int kb0 = sp * kps, kb1 = min(num_kb, kb0 + kps);
+      const int m0 = tile_m_block(tile, num_m, rot) * BM;
+      const int n0 = (tile / num_m) * BN + chalf * CPW;  // first column of this warp
+      const int row = m0 + row_in_tile;
+      if constexpr (MODE == kModeAG) {
+        // Scales of peer rows were written by peers: acquire before reading them.
+        if (!ag_wait_rows(p2p, m0, M, ready, err, abort_flag)) {
+          ok = false;
+          break;
+        }
+      }
+      float acc[CPW];
+#pragma unroll
+      for (int j = 0; j < CPW; ++j) acc[j] = 0.f;
+      for (int kb = kb0; kb < kb1; ++kb, ++kcount) {
+        const uint32_t buf = kcount & 1;
+        const uint32_t bpar = (kcount >> 1) & 1;
+        float sa = 0.f;
+        if (row < M) {
+          const float* sp_ = sfa + static_cast<size_t>(kb) * lda_s + row;
+          sa = MODE == kModeAG ? __ldcg(sp_) : __ldg(sp_);
+        }
+        float sb[(CPW + 127) / 128];
+#pragma unroll
+        for (int q = 0; q < (CPW + 127) / 128; ++q) {
+          const int nb = (n0 + q * 128) / 128;
+          sb[q] = nb * 128 < N ? __ldg(sfb + static_cast<size_t>(nb) * kb_scale_stride + kb) : 0.f;
+        }
+        if (!mbar_wait(&s.tmem_full[buf], bpar, err, kErrTimeoutTmemFull, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < CPW / 16; ++c) {
+          uint32_t r[16];
+          tmem_ld16(tmem + lane_addr + buf * BN + chalf * CPW + c * 16, r);
+          tmem_wait_ld();
+          const float scale = sa * sb[(c * 16) / 128];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[c * 16 + j] = fmaf(__uint_as_float(r[j]), scale, acc[c * 16 + j]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.tmem_empty[buf]);
+      }
+      // RS threads always reach the per-tile named barrier below (a thread that
+      // left early would strand the others there); other modes leave now.
+      if (!ok && MODE != kModeRS) break;
+      if (MODE == kModePlain && splits > 1) {
+        // FP32 partial of this K split; the reduce kernel adds splits (+ residual).
+        if (row < M && n0 < N) {
+          float* prow = partial + (static_cast<size_t>(sp) * M + row) * N + n0;
+          const int ncols = min(CPW, N - n0);
+          if (ncols == CPW && (N % 4) == 0) {
+#pragma unroll
+            for (int j = 0; j < CPW; j += 4)
+              *reinterpret_cast<float4*>(prow + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < CPW; ++j)
+              if (j < ncols) prow[j] = acc[j];
+          }
+        }
+        continue;
+      }
+      __nv_bfloat16* orow = nullptr;
+      const __nv_bfloat16* rrow = nullptr;
+      if (ok && row < M && n0 < N) {
+        if constexpr (MODE == kModeRS) {
+          const int owner = row / p2p.S;
+          if (owner != owner_ok && p2p.reuse_target > 0) {
+            // Reuse guard: the owner's reduce of two calls ago has read this parity.
+            if (!wait_flag_ge(p2p.flags[p2p.rank] + kFlagRsDone + owner, p2p.reuse_target, err,
+                              kErrTimeoutPeerFlag, abort_flag)) {
+              ok = false;
+            }
+          }
+          owner_ok = owner;
+          const int64_t slot = (int64_t(p2p.parity) * p2p.world + p2p.rank) * p2p.S + (row - owner * p2p.S);
+          orow = p2p.rb[owner] + slot * N + n0;
+        } else {
+          orow = out + static_cast<size_t>(row) * ldo + n0;
+          rrow = residual ? residual + static_cast<size_t>(row) * ldr + n0 : nullptr;
+        }
+      }
+      if (orow != nullptr && ok) {
+        const int ncols = min(CPW, N - n0);
+        const bool vec = (ncols == CPW) && ((reinterpret_cast<uintptr_t>(orow) & 15) == 0) &&
+                         (!rrow || (reinterpret_cast<uintptr_t>(rrow) & 15) == 0);
+        if (vec) {
+#pragma unroll
+          for (int j = 0; j < CPW; j += 8) {
+            float v[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) v[t] = acc[j + t];
+            if (rrow) {
+              uint4 rv = *reinterpret_cast<const uint4*>(rrow + j);
+              const uint32_t* rw = reinterpret_cast<const uint32_t*>(&rv);
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                v[2 * t] += bf16_lo(rw[t]);
+                v[2 * t + 1] += bf16_hi(rw[t]);
+              }
+            }
+            uint4 o;
+            o.x = pack_bf16(v[0], v[1]);
+            o.y = pack_bf16(v[2], v[3]);
+            o.z = pack_bf16(v[4], v[5]);
+            o.w = pack_bf16(v[6], v[7]);
+            *reinterpret_cast<uint4*>(orow + j) = o;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < CPW; ++j) {
+            if (j < ncols) {
+              float v = acc[j];
+              if (rrow) v += __bfloat162float(rrow[j]);
+              orow[j] = __float2bfloat16_rn(v);
+            }
+          }
+        }
+      }
+      if constexpr (MODE == kModeRS) {
+        // The whole tile is stored: publish it to every owner it touched.
+        if (!ok) *abort_flag = 1;
+        named_barrier(kEpiBarrier, kEpiWarps * 32);
+        if (*abort_flag) ok = false;
+        if (threadIdx.x == 64 && ok) {
+          __threadfence_system();
+          const int o0 = m0 / p2p.S, o1 = min(M - 1, m0 + BM - 1) / p2p.S;
+          for (int o = o0; o <= o1; ++o) red_release_sys_add(p2p.flags[o] + kFlagRsArrive + p2p.rank, 1);
+        }
+        if (!ok) break;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 2 * BN);
+  }
+  if constexpr (MODE == kModeAG) {
+    // Every load of this CTA has been consumed: tell each rank its data here may be overwritten.
+    if (threadIdx.x == 0 && !s.abort_flag) {
+      __threadfence_system();
+      for (int q = 0; q < p2p.world; ++q) red_release_sys_add(p2p.flags[q] + kFlagAgDone + p2p.rank, 1);
+    }
+  }
+}
+
+template <int BN, int STAGES>
+inline size_t smem_bytes() {
+  return sizeof(GemmSmem<BN, STAGES>) + 1024;
+}
+
+}  // namespace gemm_fp8
+}  // namespace b200

@@ -1,6 +1,8 @@
 // Launch entry points of the sm_100a kernels.  These .cu files include only
 // CUDA headers; csrc/bindings.cpp validates torch tensors and calls them.
 #pragma once
+#include <vector>
+#include "../common/p2p_args.h"
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
@@ -33,6 +35,25 @@ struct FP8GemmPlan {
 FP8GemmPlan plan_fp8_gemm(int M, int N, int K, int max_splits);
 size_t fp8_gemm_scratch_bytes(int M, int N, int K, int max_splits);
 void launch_fp8_gemm(const FP8GemmArgs& a, cudaStream_t stream);
+
+// Communication-fused FP8 GEMMs over NVLink peer memory (P2PArgs in common/p2p_args.h).
+// AG: out[M, N] = (all-gather of every rank's [S, K] shard) . B^T; p.a_local / p.sfa_local
+//     are this rank's shard; M = world * S.
+// RS: this rank's rows [rank*S, rank*S+S) of sum over ranks of A . B^T (+ residual).
+int fp8_gemm_ag_grid(int M, int N);
+int rs_reduce_grid(int S, int N);
+void launch_fp8_gemm_ag(P2PArgs p, const uint8_t* B, int ldb, const float* sfb, __nv_bfloat16* out, int ldo,
+                        int M, int N, int K, int* err, cudaStream_t stream);
+void launch_fp8_gemm_rs(P2PArgs p, const uint8_t* A, int lda, const float* sfa, int lda_s, const uint8_t* B,
+                        int ldb, const float* sfb, int M, int N, int K, const __nv_bfloat16* residual, int ldr,
+                        __nv_bfloat16* out, int ldo, int* err, cudaStream_t stream);
+void launch_p2p_barrier(const P2PArgs& p, int* err, cudaStream_t stream);
+// Symmetric heap: cudaMalloc'd, zeroed, exported / opened through CUDA IPC.
+uintptr_t symm_alloc(size_t bytes);
+void symm_free(uintptr_t p);
+std::vector<uint8_t> symm_handle(uintptr_t p);
+uintptr_t symm_open(const std::vector<uint8_t>& handle);
+void symm_close(uintptr_t p);
 
 // Batched BF16 GEMM: for g in [0, batch): out_g[m, n] = sum_k A_g[m, k] * B_g[n, k].
 // A_g row m starts at A + g*a_batch + m*lda (elements), B likewise; out_g at

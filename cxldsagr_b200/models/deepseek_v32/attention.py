@@ -57,14 +57,15 @@ class AttentionRunner:
 
     # ------------------------------------------------------------- projection
     def project(self, state: LayerState, normed, quantized, pos: int, positions, freqs, scope=None,
-                gathered=None, rows=None):
+                comm=None, rows=None):
         """Projections of one chunk.
 
         ``normed`` / ``quantized`` are this rank's query rows [r0, r1) of the
-        chunk (all rows when not sequence parallel).  ``gathered`` is the
-        chunk's full input (FP8 (q, scales^T) or BF16) from the all-gather;
-        the latent KV record and the indexer key are produced for every row
-        (the KV cache is replicated), the query path only for local rows.
+        chunk (all rows when not sequence parallel).  Under sequence
+        parallelism ``comm.ag_linear`` all-gathers the chunk's input inside the
+        q_a / kv_a / indexer-k GEMM (one fused kernel on the peer-memory
+        backend); the latent KV record and the indexer key are produced for
+        every row (the KV cache is replicated), the query path only for local rows.
         """
         scope = scope or (lambda _name: nullcontext())
         cfg, w = self.cfg, self.w
@@ -72,12 +73,11 @@ class AttentionRunner:
         H, nope, rope, L = cfg.n_heads, cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.kv_lora_rank
         r0, r1 = rows if rows is not None else (0, T_loc)
         with scope("fused_a_gemm"):
-            if gathered is None:
-                a = w.fused_a(normed, quantized=quantized)
-            elif isinstance(gathered, tuple):
-                a = w.fused_a(quantized=gathered)
+            if comm is not None and comm.world > 1:
+                fp8 = w.fused_a.scales is not None
+                a = comm.ag_linear(w.fused_a, normed, quantized if fp8 else None, positions.shape[0])
             else:
-                a = w.fused_a(gathered)
+                a = w.fused_a(normed, quantized=quantized)
         T = a.shape[0]
         qa = a[r0:r1, self.qa0:self.qa0 + self.qa_n]
         kv = a[:, self.kv0:self.kv0 + self.kv_n]
@@ -112,7 +112,7 @@ class AttentionRunner:
 
     # ---------------------------------------------------------------- forward
     def forward(self, state: LayerState, normed, quantized, pos: int, positions, freqs, *, scope=None,
-                logits_buf=None, gathered=None, rows=None):
+                logits_buf=None, comm=None, rows=None):
         """One chunk of attention; returns o_proj output for this rank's query rows."""
         scope = scope or (lambda _name: nullcontext())
         cfg = self.cfg
@@ -124,7 +124,7 @@ class AttentionRunner:
         with cache.operation():
             with scope("attention_projection"):
                 q_proj, q_idx, weights = self.project(state, normed, quantized, pos, positions, freqs, scope,
-                                                      gathered=gathered, rows=(r0, r1))
+                                                      comm=comm, rows=(r0, r1))
             if T_loc == 0:
                 return torch.empty((0, cfg.dim), dtype=torch.bfloat16, device=normed.device)
             qpos = pos + r0

@@ -155,13 +155,8 @@ class Block:
         total = positions.shape[0]
         with scope("input_residual_norm"):
             normed, summed, q8, s8 = ops.norm_quant(hidden, residual, self.attention.w.input_norm, cfg.norm_eps)
-        gathered = None
-        if self.comm is not None and self.comm.world > 1:
-            with scope("attention_all_gather"):
-                fp8 = self.attention.w.fused_a.scales is not None
-                gathered = self.comm.gather(normed, (q8, s8) if fp8 else None, total)
         attn = self.attention.forward(state, normed, (q8, s8), pos, positions, freqs, scope=scope,
-                                      logits_buf=logits_buf, gathered=gathered, rows=rows)
+                                      logits_buf=logits_buf, comm=self.comm, rows=rows)
         with scope("post_attention_residual_norm"):
             normed2, out_res, q2, s2 = ops.norm_quant(summed, attn, self.post_norm, cfg.norm_eps)
         if isinstance(self.mlp, MoE):

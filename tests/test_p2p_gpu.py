@@ -1,0 +1,153 @@
+"""Fused peer-memory GEMMs on 2+ GPUs against the NCCL baseline.
+
+Runs as child processes (one per GPU, NCCL + CUDA IPC symmetric heap).  Every
+device wait in the fused kernels is bounded, so a broken protocol surfaces as
+an error word, not a hang.  NVLS stays off (``NCCL_NVLS_ENABLE=0``): the
+fused kernels use plain peer stores and the baseline needs no switch reduction.
+"""
+
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _need(n):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs")
+
+
+def _entry(fn, rank, world, port, q):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    try:
+        q.put((rank, fn(rank, world)))
+    except BaseException as exc:  # noqa: BLE001
+        import traceback
+
+        q.put(f"rank {rank}: {exc!r}\n{traceback.format_exc()}")
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _spawn(fn, world):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_entry, args=(fn, r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=600) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+    errs = [o for o in out if isinstance(o, str)]
+    assert not errs, errs[0]
+    return dict(out)
+
+
+def _fused_vs_nccl(rank, world):
+    from cxldsagr_b200 import ops
+    from cxldsagr_b200.models.deepseek_v32.weights import Linear
+    from cxldsagr_b200.ops.native import check_errors
+    from cxldsagr_b200.parallel.comm import Comm
+    from cxldsagr_b200.parallel.groups import init_distributed
+    from cxldsagr_b200.parallel.p2p import P2PComm
+
+    ctx = init_distributed(timeout_s=60, comm="p2p")
+    dev = ctx.device
+    fused, base = P2PComm(ctx), Comm(ctx)
+    g = torch.Generator(device=dev).manual_seed(1234)  # same weights on every rank
+
+    def weight(n, k):
+        from cxldsagr_b200.checkpoint import quantize_weight_blocks
+
+        w = torch.randn((n, k), generator=g, device=dev) * 0.05
+        q, s = quantize_weight_blocks(w, (128, 128))
+        return Linear(q.contiguous(), s.float().contiguous())
+
+    report = {}
+    torch.manual_seed(100 + rank)
+    T, K = 1024, 7168
+    S = T // world
+    shapes = [(2304, K), (4608, K), (2304, K), (4608, K), (2304, K)]   # alternate shapes: exercises parity / reuse
+    for i, (N, Kd) in enumerate(shapes):
+        lin = weight(N, Kd)
+        x = torch.randn((S, Kd), device=dev).bfloat16()
+        q, s_t = ops.quantize_act(x)
+        a = fused.ag_linear(lin, x, (q, s_t), T)
+        b = base.ag_linear(lin, x, (q, s_t), T)
+        torch.cuda.synchronize()
+        check_errors(dev)
+        report[f"ag{i}_maxdiff"] = (a.float() - b.float()).abs().max().item()
+    for i, N in enumerate([7168, 2304, 7168, 2304, 7168]):
+        lin = weight(N, 2304)
+        h = torch.randn((T, 2304), device=dev).bfloat16()
+        q, s_t = ops.quantize_act(h)
+        a = fused.linear_rs(lin, h, (q, s_t))
+        b = base.linear_rs(lin, h, (q, s_t))
+        torch.cuda.synchronize()
+        check_errors(dev)
+        report[f"rs{i}_maxdiff"] = (a.float() - b.float()).abs().max().item()
+        report[f"rs{i}_scale"] = b.float().abs().max().item()
+    report["fused_calls"] = dict(fused.fused_calls)
+
+    # Device time, max over ranks (CUDA events, warm-up first).
+    def timed(fn, reps=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        import torch.distributed as dist
+
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / reps], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    lin = weight(2304, K)
+    x = torch.randn((S, K), device=dev).bfloat16()
+    qx = ops.quantize_act(x)
+    report["ag_fused_ms"] = timed(lambda: fused.ag_linear(lin, x, qx, T))
+    report["ag_nccl_ms"] = timed(lambda: base.ag_linear(lin, x, qx, T))
+    lin = weight(7168, 18432 // world)
+    h = torch.randn((T, 18432 // world), device=dev).bfloat16()
+    qh = ops.quantize_act(h)
+    report["rs_fused_ms"] = timed(lambda: fused.linear_rs(lin, h, qh))
+    report["rs_nccl_ms"] = timed(lambda: base.linear_rs(lin, h, qh))
+    torch.cuda.synchronize()
+    check_errors(dev)
+    fused.close()
+    return report
+
+
+@pytest.mark.parametrize("world", [2])
+def test_fused_ag_rs_match_nccl(world):
+    _need(world)
+    reports = _spawn(_fused_vs_nccl, world)
+    for rank, rep in reports.items():
+        print(rank, rep)
+        assert rep["fused_calls"] == {"ag": 5, "rs": 5}
+        for k, v in rep.items():
+            if k.startswith("ag") and k.endswith("maxdiff"):
+                assert v == 0.0, (k, v)
+            if k.startswith("rs") and k.endswith("maxdiff"):
+                assert v <= 1e-2 * max(1.0, rep[k.replace("maxdiff", "scale")]), (k, v)
