@@ -281,6 +281,100 @@ void gather_rows(const Tensor& host, Tensor& records, const Tensor& host_ids, co
 }
 
 // `call` numbers this op's calls from 1 (parity = call & 1); targets are the cumulative flag counts.
+void moe_route(const Tensor& logits, bool split, const Tensor& bias, int64_t E, int64_t n_group, int64_t topk_group,
+               int64_t K, bool normalize, double scaling, Tensor& ids, Tensor& weights) {
+  c10::cuda::CUDAGuard guard(logits.device());
+  TORCH_CHECK(logits.dtype() == torch::kFloat32 && logits.stride(1) == 1, "moe_route: fp32 row-major logits");
+  b200::launch_moe_route(logits.data_ptr<float>(), int(logits.stride(0)), split, bias.data_ptr<float>(),
+                         int(logits.size(0)), int(E), int(n_group), int(topk_group), int(K), normalize, float(scaling),
+                         ids.data_ptr<int>(), weights.data_ptr<float>(), at::cuda::getCurrentCUDAStream());
+}
+
+void moe_layout(const Tensor& ids, int64_t e0, int64_t E_loc, int64_t max_blocks, Tensor& row_pos,
+                Tensor& block_expert, Tensor& cursor, Tensor& total_rows) {
+  c10::cuda::CUDAGuard guard(ids.device());
+  b200::launch_moe_layout(ids.data_ptr<int>(), int(ids.numel()), int(e0), int(E_loc), int(max_blocks),
+                          row_pos.data_ptr<int>(), block_expert.data_ptr<int>(), cursor.data_ptr<int>(),
+                          total_rows.data_ptr<int>(), err_ptr(ids), at::cuda::getCurrentCUDAStream());
+}
+
+void moe_gather(const Tensor& q, const Tensor& s_t, int64_t topk, const Tensor& row_pos, Tensor& a, Tensor& a_s) {
+  c10::cuda::CUDAGuard guard(q.device());
+  TORCH_CHECK(q.is_contiguous() && a.is_contiguous() && a_s.is_contiguous(), "moe_gather: contiguous buffers");
+  b200::launch_moe_gather(reinterpret_cast<const uint8_t*>(q.data_ptr()), s_t.data_ptr<float>(), int(s_t.stride(0)),
+                          int(row_pos.numel()), int(topk), int(q.size(1)), row_pos.data_ptr<int>(),
+                          reinterpret_cast<uint8_t*>(a.data_ptr()), a_s.data_ptr<float>(), int(a_s.stride(0)),
+                          at::cuda::getCurrentCUDAStream());
+}
+
+void moe_combine(const Tensor& y, const Tensor& row_pos, const Tensor& w, int64_t topk, Tensor& out) {
+  c10::cuda::CUDAGuard guard(y.device());
+  b200::launch_moe_combine(reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), int(y.size(1)), row_pos.data_ptr<int>(),
+                           w.data_ptr<float>(), int(out.size(0)), int(topk),
+                           reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), at::cuda::getCurrentCUDAStream());
+}
+
+// a [M_pad, K] fp8, a_s [K/128, M_pad], w [E, N, K] fp8, w_s [E, N/128, K/128] -> out [M_pad, N] bf16.
+void fp8_gemm_grouped(const Tensor& a, const Tensor& a_s, const Tensor& w, const Tensor& w_s,
+                      const Tensor& block_expert, Tensor& out) {
+  c10::cuda::CUDAGuard guard(a.device());
+  TORCH_CHECK(w.dim() == 3 && w.is_contiguous() && w_s.is_contiguous(), "grouped: stacked expert weights");
+  b200::launch_fp8_gemm_grouped(reinterpret_cast<const uint8_t*>(a.data_ptr()), a_s.data_ptr<float>(),
+                                int(a_s.stride(0)), reinterpret_cast<const uint8_t*>(w.data_ptr()),
+                                w_s.data_ptr<float>(), block_expert.data_ptr<int>(), int(a.size(0)), int(w.size(1)),
+                                int(a.size(1)), int(w.size(0)), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                                int(out.stride(0)), err_ptr(a), at::cuda::getCurrentCUDAStream());
+}
+
+b200::EpArgs make_ep(int64_t rank, int64_t world, int64_t E, int64_t D, int64_t topk, int64_t T, int64_t M_pad,
+                     int64_t call, const std::vector<int64_t>& flags, const std::vector<int64_t>& cnt,
+                     const std::vector<int64_t>& a, const std::vector<int64_t>& as, const std::vector<int64_t>& y) {
+  if (world < 1 || world > b200::kMaxRanks || int64_t(flags.size()) != world) throw std::invalid_argument("ep: bad world");
+  b200::EpArgs p;
+  p.rank = int(rank);
+  p.world = int(world);
+  p.E = int(E);
+  p.E_loc = int(E / world);
+  p.D = int(D);
+  p.topk = int(topk);
+  p.T = int(T);
+  p.M_pad = int(M_pad);
+  p.call = uint64_t(call);
+  p.parity = int(call & 1);
+  for (int q = 0; q < world; ++q) {
+    p.flags[q] = reinterpret_cast<uint64_t*>(flags[q]);
+    p.cnt[q] = reinterpret_cast<int*>(cnt[q]);
+    p.a[q] = reinterpret_cast<uint8_t*>(a[q]);
+    p.as[q] = reinterpret_cast<float*>(as[q]);
+    p.y[q] = reinterpret_cast<__nv_bfloat16*>(y[q]);
+  }
+  return p;
+}
+
+void ep_dispatch(const Tensor& ids, const Tensor& q, const Tensor& s_t, Tensor& cursor, Tensor& pos_out,
+                 Tensor& block_expert, int64_t rank, int64_t world, int64_t E, int64_t M_pad, int64_t call,
+                 const std::vector<int64_t>& flags, const std::vector<int64_t>& cnt, const std::vector<int64_t>& a,
+                 const std::vector<int64_t>& as, const std::vector<int64_t>& y) {
+  c10::cuda::CUDAGuard guard(q.device());
+  TORCH_CHECK(ids.dtype() == torch::kInt32 && ids.is_contiguous() && q.is_contiguous(), "ep_dispatch: layouts");
+  auto p = make_ep(rank, world, E, q.size(1), ids.size(1), ids.size(0), M_pad, call, flags, cnt, a, as, y);
+  b200::launch_ep_dispatch(p, ids.data_ptr<int>(), reinterpret_cast<const uint8_t*>(q.data_ptr()), s_t.data_ptr<float>(),
+                           int(s_t.stride(0)), cursor.data_ptr<int>(), pos_out.data_ptr<int>(),
+                           block_expert.data_ptr<int>(), int(block_expert.numel()), err_ptr(q),
+                           at::cuda::getCurrentCUDAStream());
+}
+
+void ep_combine(const Tensor& ids, const Tensor& pos, const Tensor& w, Tensor& out, int64_t rank, int64_t world,
+                int64_t E, int64_t M_pad, int64_t call, const std::vector<int64_t>& flags,
+                const std::vector<int64_t>& cnt, const std::vector<int64_t>& a, const std::vector<int64_t>& as,
+                const std::vector<int64_t>& y) {
+  c10::cuda::CUDAGuard guard(out.device());
+  auto p = make_ep(rank, world, E, out.size(1), ids.size(1), ids.size(0), M_pad, call, flags, cnt, a, as, y);
+  b200::launch_ep_combine(p, ids.data_ptr<int>(), pos.data_ptr<int>(), w.data_ptr<float>(),
+                          reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), err_ptr(out),
+                          at::cuda::getCurrentCUDAStream());
+}
+
 b200::P2PArgs make_p2p(int64_t rank, int64_t world, int64_t S, int64_t call, int64_t arrive_target,
                       int64_t reuse_target, const std::vector<int64_t>& flags, const std::vector<int64_t>& g,
                       const std::vector<int64_t>& gs, const std::vector<int64_t>& rb) {
@@ -396,6 +490,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp8_gemm_ag", &fp8_gemm_ag);
   m.def("fp8_gemm_rs", &fp8_gemm_rs);
   m.def("p2p_barrier", &p2p_barrier);
+  m.def("moe_route", &moe_route);
+  m.def("ep_dispatch", &ep_dispatch);
+  m.def("ep_combine", &ep_combine);
+  m.def("moe_layout", &moe_layout);
+  m.def("moe_gather", &moe_gather);
+  m.def("moe_combine", &moe_combine);
+  m.def("fp8_gemm_grouped", &fp8_gemm_grouped);
   m.def("fp8_gemm_ag_grid", [](int64_t M, int64_t N) { return int64_t(b200::fp8_gemm_ag_grid(int(M), int(N))); });
   m.def("rs_reduce_grid", [](int64_t S, int64_t N) { return int64_t(b200::rs_reduce_grid(int(S), int(N))); });
   m.def("symm_alloc", &symm_alloc);

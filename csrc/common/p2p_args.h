@@ -16,7 +16,12 @@ constexpr int kFlagRsDone = 24;     // + src: reduce CTAs of src that finished r
 constexpr int kFlagA2aArrive = 32;  // + src: dispatch / combine CTAs of src that finished writing here
 constexpr int kFlagA2aDone = 40;    // + src: consumers of src that finished reading
 constexpr int kFlagBarrier = 48;    // + src: barrier calls
-constexpr int kFlagSlots = 64;
+// Expert-parallel MoE (one increment per call and (src, dst) pair):
+constexpr int kFlagEpCount = 64;    // + src: src's per-expert counts are here
+constexpr int kFlagEpData = 72;     // + src: src's routed rows are in this rank's grouped layout
+constexpr int kFlagEpReady = 80;    // + owner: owner's expert outputs are ready to be read
+constexpr int kFlagEpDone = 88;     // + src: src finished reading this rank's expert outputs
+constexpr int kFlagSlots = 128;
 
 // Peer pointers and flag targets of one fused call (passed by value as a kernel argument).
 struct P2PArgs {
@@ -37,6 +42,23 @@ struct P2PArgs {
   // RS: every rank's receive slots ([2][world][S][N] bf16)
   __nv_bfloat16* rb[kMaxRanks] = {};
   uint64_t* flags[kMaxRanks] = {};  // every rank's flag block
+};
+
+// Expert-parallel dispatch / combine over the symmetric heap.
+struct EpArgs {
+  int rank = 0, world = 1;
+  int E = 0, E_loc = 0;          // global experts, experts per rank
+  int D = 0;                     // hidden size (row bytes of the FP8 activations)
+  int topk = 0;
+  int T = 0;                     // local tokens
+  int M_pad = 0;                 // grouped-layout row capacity per rank
+  int parity = 0;
+  uint64_t call = 0;             // 1-based call number of the EP op
+  int* cnt[kMaxRanks] = {};      // [2][world][E] int32 per rank
+  uint8_t* a[kMaxRanks] = {};    // [2][M_pad][D] fp8
+  float* as[kMaxRanks] = {};     // [2][D/128][M_pad] fp32
+  __nv_bfloat16* y[kMaxRanks] = {};  // [2][M_pad][D] bf16
+  uint64_t* flags[kMaxRanks] = {};
 };
 
 }  // namespace b200

@@ -30,7 +30,8 @@ void launch_fp8_gemm_t(const FP8GemmArgs& a, int splits, cudaStream_t stream) {
   cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
              "fp8 gemm smem attribute");
   kern<<<grid, kThreads, smem, stream>>>(ta, tb, a.sfa, a.lda_s, a.sfb, a.out, a.ldo, a.residual,
-                                         a.ldr, a.M, a.N, a.K, splits, a.partial, a.err, P2PArgs{});
+                                         a.ldr, a.M, a.N, a.K, splits, a.partial, a.err, P2PArgs{},
+                                         GroupArgs{});
   cuda_check(cudaGetLastError(), "fp8 gemm launch");
   if (splits > 1) {
     const int64_t n = int64_t(a.M) * a.N;
@@ -43,35 +44,34 @@ void launch_fp8_gemm_t(const FP8GemmArgs& a, int splits, cudaStream_t stream) {
 }  // namespace
 
 FP8GemmPlan plan_fp8_gemm(int M, int N, int K, int max_splits) {
-  // BN=256 (4 stages x 48 KB) doubles the tensor-core time per promotion
-  // step; used when it still gives >= 3 full waves of tiles.  Otherwise BN=128
-  // with a K split chosen by a wave-quantisation cost model, in units of one
-  // 128x128x128 K-block step (~0.14 us):
-  //   cost(s) = ceil(tiles * s / SMs) * ceil(k_blocks / s)
-  //           + [s > 1] * (2 + s * M * N * 4 B / HBM-bandwidth / step).
+  // Tile width BN in {256, 224, 128} and an optional K split, chosen by a
+  // wave-quantisation cost model in units of one K-block step per column:
+  //   cost = ceil(tiles(BN) * s / SMs) * ceil(k_blocks / s) * BN
+  //        + [s > 1] * (split-K reduce traffic of s * M * N * 4 bytes).
+  // BN = 224 exists for N = 7168 (o_proj, MLP down: exactly 32 tiles of 224),
+  // where 128-wide tiles leave a 4th, almost empty wave.
   const int sms = sm_count();
   const int num_kb = (K + BK - 1) / BK;
-  FP8GemmPlan p{};
-  const int64_t tiles256 = int64_t((M + BM - 1) / BM) * ((N + 255) / 256);
-  if (tiles256 >= 3 * sms) {
-    p.bn = 256;
-    p.splits = 1;
-    return p;
-  }
-  p.bn = 128;
-  const int64_t tiles = int64_t((M + BM - 1) / BM) * ((N + 127) / 128);
-  int64_t best = -1;
-  for (int sp = 1; sp <= max_splits; ++sp) {
-    if (sp > 1 && num_kb / sp < 8) break;  // keep >= 8 K blocks per split
-    const int64_t waves = (tiles * sp + sms - 1) / sms;
-    const double reduce = sp > 1 ? 2.0 + double(sp) * M * N * 4.8e-6 : 0.0;
-    const int64_t cost = int64_t(double(waves * ((num_kb + sp - 1) / sp)) + reduce);
-    if (best < 0 || cost < best) {
-      best = cost;
-      p.splits = sp;
+  const int64_t mt = (M + BM - 1) / BM;
+  FP8GemmPlan best{};
+  double best_cost = -1.0;
+  const int widths[3] = {256, 224, 128};
+  for (int bn : widths) {
+    if (bn == 224 && N % 224) continue;  // only where 224 divides N exactly
+    const int64_t tiles = mt * ((N + bn - 1) / bn);
+    for (int sp = 1; sp <= (bn == 128 ? max_splits : 1); ++sp) {
+      if (sp > 1 && num_kb / sp < 8) break;  // keep >= 8 K blocks per split
+      const int64_t waves = (tiles * sp + sms - 1) / sms;
+      const double reduce = sp > 1 ? (2.0 + double(sp) * M * N * 4.8e-6) * 128.0 : 0.0;
+      const double cost = double(waves) * ((num_kb + sp - 1) / sp) * bn + reduce;
+      if (best_cost < 0 || cost < best_cost * 0.999) {
+        best_cost = cost;
+        best.bn = bn;
+        best.splits = sp;
+      }
     }
   }
-  return p;
+  return best;
 }
 
 size_t fp8_gemm_scratch_bytes(int M, int N, int K, int max_splits) {
@@ -84,6 +84,7 @@ void launch_fp8_gemm(const FP8GemmArgs& a, cudaStream_t stream) {
   if (a.K % 16) throw std::invalid_argument("fp8 gemm: K must be a multiple of 16");
   FP8GemmPlan p = plan_fp8_gemm(a.M, a.N, a.K, a.partial ? a.max_splits : 1);
   if (p.bn == 256) launch_fp8_gemm_t<256, 4>(a, 1, stream);
+  else if (p.bn == 224) launch_fp8_gemm_t<224, 4>(a, 1, stream);
   else launch_fp8_gemm_t<128, 6>(a, p.splits, stream);
 }
 

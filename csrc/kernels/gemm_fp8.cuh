@@ -44,7 +44,19 @@
 namespace b200 {
 namespace gemm_fp8 {
 
-constexpr int kModePlain = 0, kModeAG = 1, kModeRS = 2;
+constexpr int kModePlain = 0, kModeAG = 1, kModeRS = 2, kModeGrouped = 3;
+
+// Grouped (MoE) mode: A rows are in a padded contiguous layout where every
+// 128-row block belongs to one expert (mblock_expert[mb], -1 = empty block);
+// B is the stacked expert weights [E * N, K] with scales [E][ceil(N/128)][K/128].
+struct GroupArgs {
+  const int* mblock_expert = nullptr;
+  int64_t sfb_expert_stride = 0;   // floats per expert in sfb
+};
+
+__device__ __forceinline__ int unit_expert(const GroupArgs& g, int mb) {
+  return __ldg(g.mblock_expert + mb);
+}
 constexpr int BM = 128;
 constexpr int BK = 128;  // bytes of K per stage (= one scale block)
 constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each owning BN/2 columns
@@ -90,7 +102,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     int lda_s, const float* __restrict__ sfb, __nv_bfloat16* __restrict__ out,
                     int ldo, const __nv_bfloat16* __restrict__ residual, int ldr, int M, int N,
                     int K, int splits, float* __restrict__ partial, int* err,
-                    const __grid_constant__ P2PArgs p2p) {
+                    const __grid_constant__ P2PArgs p2p, const __grid_constant__ GroupArgs grp) {
   extern __shared__ uint8_t smem_raw[];
   auto& s = *reinterpret_cast<GemmSmem<BN, STAGES>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -118,8 +130,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     s.abort_flag = 0;
     fence_barrier_init();
   }
+  // TMEM allocations are powers of two >= 32 columns (BN = 224 takes 512).
+  constexpr uint32_t kTmemCols = 2 * BN <= 256 ? 256 : 512;
   if (warp == 1) {
-    tmem_alloc(&s.tmem_base, 2 * BN);
+    tmem_alloc(&s.tmem_base, kTmemCols);
     tmem_relinquish();
   }
   if (warp == 0 && lane == 0) {
@@ -141,7 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         const int tile = u % num_tiles, sp = u / num_tiles;
         const int m0 = tile_m_block(tile, num_m, rot) * BM;
-        const int n0 = (tile / num_m) * BN;
+        int n0 = (tile / num_m) * BN;
         const int kb0 = sp * kps, kb1 = min(num_kb, kb0 + kps);
         if constexpr (MODE == kModeAG) {
           if (!ag_wait_rows(p2p, m0, M, ready, err, abort_flag)) {
@@ -149,6 +163,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           fence_proxy_async_global();
+        }
+        if constexpr (MODE == kModeGrouped) {
+          const int e = unit_expert(grp, m0 / BM);
+          if (e < 0) continue;
+          n0 += e * N;  // row of the stacked expert weights
         }
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1, err, kErrTimeoutSmemEmpty, abort_flag)) {
@@ -179,6 +198,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         const int sp = u / num_tiles;
         const int kb0 = sp * kps, kb1 = min(num_kb, kb0 + kps);
+        if constexpr (MODE == kModeGrouped) {
+          if (unit_expert(grp, tile_m_block(u % num_tiles, num_m, rot)) < 0) continue;
+        }
         for (int kb = kb0; kb < kb1; ++kb, ++kcount) {
           const uint32_t buf = kcount & 1;
           const uint32_t bpar = (kcount >> 1) & 1;
@@ -266,6 +288,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m0 = tile_m_block(tile, num_m, rot) * BM;
       const int n0 = (tile / num_m) * BN + chalf * CPW;  // first column of this warp
       const int row = m0 + row_in_tile;
+      const float* sfb_u = sfb;
+      if constexpr (MODE == kModeGrouped) {
+        const int e = unit_expert(grp, m0 / BM);
+        if (e < 0) continue;
+        sfb_u = sfb + e * grp.sfb_expert_stride;
+      }
       if constexpr (MODE == kModeAG) {
         // Scales of peer rows were written by peers: acquire before reading them.
         if (!ag_wait_rows(p2p, m0, M, ready, err, abort_flag)) {
@@ -284,12 +312,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float* sp_ = sfa + static_cast<size_t>(kb) * lda_s + row;
           sa = MODE == kModeAG ? __ldcg(sp_) : __ldg(sp_);
         }
-        float sb[(CPW + 127) / 128];
-#pragma unroll
-        for (int q = 0; q < (CPW + 127) / 128; ++q) {
-          const int nb = (n0 + q * 128) / 128;
-          sb[q] = nb * 128 < N ? __ldg(sfb + static_cast<size_t>(nb) * kb_scale_stride + kb) : 0.f;
-        }
+        // A warp's CPW (<= 128) columns touch at most two 128-wide weight scale blocks.
+        const int nb0 = n0 / 128, nb1 = (n0 + CPW - 1) / 128;
+        const float sb0 = nb0 * 128 < N ? __ldg(sfb_u + static_cast<size_t>(nb0) * kb_scale_stride + kb) : 0.f;
+        const float sb1 = nb1 * 128 < N ? __ldg(sfb_u + static_cast<size_t>(nb1) * kb_scale_stride + kb) : 0.f;
         if (!mbar_wait(&s.tmem_full[buf], bpar, err, kErrTimeoutTmemFull, abort_flag)) {
           ok = false;
           break;
@@ -300,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t r[16];
           tmem_ld16(tmem + lane_addr + buf * BN + chalf * CPW + c * 16, r);
           tmem_wait_ld();
-          const float scale = sa * sb[(c * 16) / 128];
+          const float scale = sa * ((n0 + c * 16) / 128 == nb0 ? sb0 : sb1);
 #pragma unroll
           for (int j = 0; j < 16; ++j) acc[c * 16 + j] = fmaf(__uint_as_float(r[j]), scale, acc[c * 16 + j]);
         }
@@ -404,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 2 * BN);
+    tmem_dealloc(tmem, kTmemCols);
   }
   if constexpr (MODE == kModeAG) {
     // Every load of this CTA has been consumed: tell each rank its data here may be overwritten.

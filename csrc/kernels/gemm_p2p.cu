@@ -132,7 +132,8 @@ void launch_fp8_gemm_ag(P2PArgs p, const uint8_t* B, int ldb, const float* sfb, 
   __nv_bfloat16* res_null = nullptr;
   float* part_null = nullptr;
   cuda_check(cudaLaunchKernelEx(&cfg, kern, ta, tb, sfa_arg, M, sfb, out, ldo,
-                                static_cast<const __nv_bfloat16*>(res_null), 0, M, N, K, 1, part_null, err, p),
+                                static_cast<const __nv_bfloat16*>(res_null), 0, M, N, K, 1, part_null, err, p,
+                                GroupArgs{}),
              "ag gemm launch");
 }
 
@@ -158,7 +159,7 @@ void launch_fp8_gemm_rs(P2PArgs p, const uint8_t* A, int lda, const float* sfa, 
   auto kern = fp8_gemm_kernel<128, 6, kModeRS>;
   cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)), "rs gemm smem");
   kern<<<p.grid, kThreads, smem, stream>>>(ta, tb, sfa, lda_s, sfb, nullptr, 0, nullptr, 0, M, N, K, 1, nullptr,
-                                           err, p);
+                                           err, p, GroupArgs{});
   cuda_check(cudaGetLastError(), "rs gemm launch");
   rs_reduce_kernel<<<p.reduce_grid, 256, 0, stream>>>(p, N, (N + 127) / 128, residual, ldr, out, ldo, err);
   cuda_check(cudaGetLastError(), "rs reduce launch");

@@ -48,6 +48,25 @@ void launch_fp8_gemm_rs(P2PArgs p, const uint8_t* A, int lda, const float* sfa, 
                         int ldb, const float* sfb, int M, int N, int K, const __nv_bfloat16* residual, int ldr,
                         __nv_bfloat16* out, int ldo, int* err, cudaStream_t stream);
 void launch_p2p_barrier(const P2PArgs& p, int* err, cudaStream_t stream);
+// MoE (single GPU, no host sync): routing, padded grouped layout, row gather, grouped GEMM, combine.
+void launch_moe_route(const float* logits, int ld, bool split, const float* bias, int T, int E, int n_group,
+                      int topk_group, int K, bool normalize, float scaling, int* ids, float* weights,
+                      cudaStream_t stream);
+void launch_moe_layout(const int* ids, int R, int e0, int E_loc, int max_blocks, int* row_pos, int* block_expert,
+                       int* cursor, int* total_rows, int* err, cudaStream_t stream);
+void launch_moe_gather(const uint8_t* q, const float* s_t, int ld_st, int R, int topk, int Kdim, const int* row_pos,
+                       uint8_t* a, float* a_s, int ld_as, cudaStream_t stream);
+void launch_moe_combine(const __nv_bfloat16* y, int D, const int* row_pos, const float* w, int T, int topk,
+                        __nv_bfloat16* out, cudaStream_t stream);
+void launch_fp8_gemm_grouped(const uint8_t* A, const float* sfa, int lda_s, const uint8_t* B, const float* sfb,
+                             const int* block_expert, int M_pad, int N, int K, int E, __nv_bfloat16* out, int ldo,
+                             int* err, cudaStream_t stream);
+// Expert-parallel dispatch (counts exchange + scatter into owners' grouped layouts + wait) and
+// combine (ready signal + pull of expert outputs + weighted k-order sum + done signal).
+void launch_ep_dispatch(const EpArgs& p, const int* ids, const uint8_t* q, const float* s_t, int ld_st, int* cursor,
+                        int* pos_out, int* block_expert, int max_blocks, int* err, cudaStream_t stream);
+void launch_ep_combine(const EpArgs& p, const int* ids, const int* pos, const float* w, __nv_bfloat16* out, int* err,
+                       cudaStream_t stream);
 // Symmetric heap: cudaMalloc'd, zeroed, exported / opened through CUDA IPC.
 uintptr_t symm_alloc(size_t bytes);
 void symm_free(uintptr_t p);

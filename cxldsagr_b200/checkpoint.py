@@ -141,6 +141,7 @@ def random_state_dict(
     device="cpu",
     pow2_scales: bool = True,
     include_embeddings: bool = True,
+    experts: Iterable[int] | None = None,
 ) -> dict[str, torch.Tensor]:
     """Seeded random weights with the checkpoint's names, shapes and dtypes.
 
@@ -149,14 +150,23 @@ def random_state_dict(
     Norm weights are one, biases zero; the indexer head weights and the MoE
     gate are FP32 like the checkpoint.  Tensors are generated one at a time on
     ``device`` (a GPU makes the 3-layer / 671B benchmark models fast to build).
+    Every tensor has its own seed (from ``seed`` and its name), so a rank that
+    generates only its own routed ``experts`` gets the same replicated tensors
+    as every other rank.
     """
+    import zlib
+
     gen = torch.Generator(device=device)
-    gen.manual_seed(seed)
+    keep_experts = None if experts is None else set(experts)
     out: dict[str, torch.Tensor] = {}
     specs = model_tensor_specs(cfg, layers)
     for name, (shape, kind) in specs.items():
         if not include_embeddings and kind == "embed":
             continue
+        if keep_experts is not None and ".mlp.experts." in name:
+            if int(name.split(".mlp.experts.")[1].split(".")[0]) not in keep_experts:
+                continue
+        gen.manual_seed((seed * 1000003 + zlib.crc32(name.encode())) & 0x7FFFFFFFFFFFFFFF)
         if kind == "norm":
             out[name] = torch.ones(shape, dtype=torch.float32 if "k_norm" in name else torch.bfloat16, device=device)
         elif kind == "bias":

@@ -113,7 +113,46 @@ def bench_topk(R=1024, N=65536, k=2048, clustered=False, **_):
             "read_gbs": R * N * 4 / ms / 1e6}
 
 
-OPS = {"sparse_mla": bench_sparse_mla, "fp8_gemm": bench_fp8_gemm, "indexer": bench_indexer, "topk": bench_topk}
+def _p2p_single():
+    """The fused peer-memory GEMMs with world = 1 (self-push through the same
+    symmetric-heap protocol): kernel profiling without a multi-rank launch."""
+    from ..models.deepseek_v32.weights import Linear
+    from ..parallel.groups import single
+    from ..parallel.p2p import P2PComm
+
+    return P2PComm(single("cuda")), Linear
+
+
+def bench_ag_gemm(M=1024, N=2304, Kdim=7168, **_):
+    comm, Linear = _p2p_single()
+    dev = "cuda"
+    w, s = quantize_weight_blocks(torch.randn(N, Kdim, device=dev) * 0.02)
+    lin = Linear(w, s)
+    x = torch.randn(M, Kdim, device=dev).bfloat16()
+    qx = ops.quantize_act(x)
+    ms = time_fn(lambda: comm.ag_linear(lin, x, qx, M))
+    ref = time_fn(lambda: lin(quantized=qx))
+    flops = 2.0 * M * N * Kdim
+    return {"op": "ag_gemm(world=1)", "M": M, "N": N, "K": Kdim, "ms": ms, "plain_gemm_ms": ref,
+            "tflops": flops / ms / 1e9}
+
+
+def bench_rs_gemm(M=1024, N=7168, Kdim=2304, **_):
+    comm, Linear = _p2p_single()
+    dev = "cuda"
+    w, s = quantize_weight_blocks(torch.randn(N, Kdim, device=dev) * 0.02)
+    lin = Linear(w, s)
+    h = torch.randn(M, Kdim, device=dev).bfloat16()
+    qh = ops.quantize_act(h)
+    ms = time_fn(lambda: comm.linear_rs(lin, h, qh))
+    ref = time_fn(lambda: lin(quantized=qh))
+    flops = 2.0 * M * N * Kdim
+    return {"op": "rs_gemm(world=1)", "M": M, "N": N, "K": Kdim, "ms": ms, "plain_gemm_ms": ref,
+            "tflops": flops / ms / 1e9}
+
+
+OPS = {"sparse_mla": bench_sparse_mla, "fp8_gemm": bench_fp8_gemm, "indexer": bench_indexer, "topk": bench_topk,
+       "ag_gemm": bench_ag_gemm, "rs_gemm": bench_rs_gemm}
 
 
 def main():
@@ -136,6 +175,8 @@ def main():
         kw = dict(T=a.T, K=a.K, P=a.P, splits=a.splits, impl=a.impl, locality=a.locality)
         if name == "fp8_gemm":
             kw = dict(M=a.M, N=a.N, K=a.Kdim)
+        if name in ("ag_gemm", "rs_gemm"):
+            kw = dict(M=a.M, N=a.N, Kdim=a.Kdim)
         if name == "topk":
             kw = dict(R=a.R, clustered=a.clustered)
         print(json.dumps(OPS[name](**kw)))

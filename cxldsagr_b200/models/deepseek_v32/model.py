@@ -75,6 +75,69 @@ class MoE:
         self.cfg, self.w = cfg, w
         self.comm = comm
         self.shared = DenseMLP(w.shared) if w.shared is not None else None
+        self._layouts: dict = {}
+
+    def _layout(self, rows: int, device):
+        lay = self._layouts.get(rows)
+        if lay is None:
+            lay = ops.MoELayout(rows, self.w.experts.start, len(self.w.experts), self.cfg.dim, device)
+            self._layouts[rows] = lay
+        return lay
+
+    def _grouped(self, ids, q, s_t, topk: int):
+        """Local experts over device-built grouped layout: gate_up -> SiLU*up (+FP8 quant) -> down."""
+        w = self.w
+        lay = self._layout(ids.numel(), q.device).build(ids, q, s_t, topk)
+        gu = ops.fp8_gemm_grouped(lay.a, lay.a_s, w.w_gate_up, w.s_gate_up, lay.block_expert)
+        _, hq, hs = ops.silu_mul_quant(gu)
+        return ops.fp8_gemm_grouped(hq, hs, w.w_down, w.s_down, lay.block_expert), lay
+
+    def _gpu(self, normed, quantized, scope, total):
+        cfg, w = self.cfg, self.w
+        T, K = normed.shape[0], cfg.num_experts_per_tok
+        with scope("moe_gate"):
+            if T:
+                logits = ops.linear_split(normed, w.gate_split)
+                ids, weights = ops.moe_route(logits, w.bias, cfg, split=True)
+            else:
+                ids = torch.empty((0, K), dtype=torch.int32, device=normed.device)
+                weights = torch.empty((0, K), dtype=torch.float32, device=normed.device)
+        q, s_t = quantized
+        world = 1 if self.comm is None else self.comm.world
+        if world == 1:
+            with scope("moe_experts"):
+                y, lay = self._grouped(ids, q, s_t, K)
+            with scope("moe_combine"):
+                out = ops.moe_combine(y, lay.row_pos, weights, T)
+        elif hasattr(self.comm, "ep_ready") and self.comm.ep_ready(cfg.n_routed_experts, cfg.dim, K, total):
+            def experts(a, a_s, block_expert, y_out):
+                gu = ops.fp8_gemm_grouped(a, a_s, w.w_gate_up, w.s_gate_up, block_expert)
+                _, hq, hs = ops.silu_mul_quant(gu)
+                ops.fp8_gemm_grouped(hq, hs, w.w_down, w.s_down, block_expert, out=y_out)
+
+            with scope("moe_ep_fused"):
+                out = self.comm.moe_ep(ids, q, s_t, weights, experts)
+        else:
+            flat = ids.reshape(-1).long()
+            per = cfg.n_routed_experts // world
+            dest = flat // per
+            order = torch.argsort(dest * cfg.n_routed_experts + flat, stable=True)
+            token = order // K
+            with scope("moe_dispatch"):
+                rrows, rscales, rexp, sc, rc = self.comm.dispatch(q[token], s_t.t()[token].contiguous(), dest[order],
+                                                                  flat[order])
+            with scope("moe_experts"):
+                y, lay = self._grouped(rexp.int(), rrows.contiguous(), rscales.t().contiguous(), 1)
+                y_rows = y[lay.row_pos.long()]
+            with scope("moe_combine"):
+                back = self.comm.combine(y_rows, sc, rc)
+                slots = torch.empty((T * K, cfg.dim), dtype=torch.bfloat16, device=normed.device)
+                slots[order] = back
+                out = (slots.view(T, K, cfg.dim).float() * weights.view(T, K, 1)).sum(1).bfloat16()
+        if self.shared is not None:
+            with scope("shared_expert"):
+                out = (out.float() + self.shared(normed, quantized).float()).bfloat16()
+        return out
 
     def _experts(self, x, s_rows, experts):
         """Run local experts over rows grouped by expert id; returns bf16 [N, D]."""
@@ -104,9 +167,11 @@ class MoE:
             out[sel] = y.to(torch.bfloat16)
         return out
 
-    def __call__(self, normed, quantized, scope=None):
+    def __call__(self, normed, quantized, scope=None, total: int | None = None):
         cfg, w = self.cfg, self.w
         scope = scope or (lambda _n: nullcontext())
+        if normed.is_cuda and w.s_gate_up is not None and w.gate_split is not None:
+            return self._gpu(normed, quantized, scope, normed.shape[0] if total is None else total)
         T, K = normed.shape[0], cfg.num_experts_per_tok
         with scope("moe_gate"):
             ids, weights = ops.route_experts(normed, w.gate, w.bias, cfg)
@@ -161,7 +226,7 @@ class Block:
             normed2, out_res, q2, s2 = ops.norm_quant(summed, attn, self.post_norm, cfg.norm_eps)
         if isinstance(self.mlp, MoE):
             with scope("moe"):
-                out = self.mlp(normed2, (q2, s2), scope)
+                out = self.mlp(normed2, (q2, s2), scope, total=total)
         else:
             with scope("dense_mlp"):
                 out = self.mlp(normed2, (q2, s2), scope, total=total)
@@ -255,7 +320,9 @@ class DeepSeekV32Model:
         self.layer_ids = list(range(cfg.num_hidden_layers) if layers is None else layers)
         self.scope = scope
         self.par = parallel or single(device)
-        self.comm = make_comm(self.par)
+        has_moe = any(cfg.is_moe_layer(layer) for layer in self.layer_ids)
+        self.comm = make_comm(self.par, max_rows=self.cache_cfg.chunk_size,
+                              moe=(cfg.n_routed_experts, cfg.dim, cfg.num_experts_per_tok) if has_moe else None)
         # Replay: physical blocks are copies of checkpoint layers 0,1,2 repeated; blocks
         # >= 3 take clones of their source block's inputs (see replay.ReplayLayout).
         self.replay_layout = ReplayLayout(tuple(self.layer_ids)) if replay else None

@@ -123,6 +123,7 @@ class MoEWeights:
     s_down: torch.Tensor | None
     shared: MLPWeights | None
     experts: range                 # global expert ids resident here (EP shard)
+    gate_split: torch.Tensor | None = None  # bf16 [2E, D]: hi || lo of the fp32 gate (tensor-core GEMV)
 
 
 def _f32(source, name, device):
@@ -219,8 +220,10 @@ def load_moe(source, cfg: ModelConfig, layer: int, *, device, experts: range | N
         if fp8:
             s_d[j].copy_(lin.scales)
     shared = load_mlp(source, cfg, p + "shared_experts", device=device) if cfg.n_shared_experts else None
+    gate = _f32(source, p + "gate.weight", device)
     return MoEWeights(
-        gate=_f32(source, p + "gate.weight", device),
+        gate=gate,
         bias=_f32(source, p + "gate.e_score_correction_bias", device),
         w_gate_up=w_gu, s_gate_up=s_gu, w_down=w_d, s_down=s_d, shared=shared, experts=experts,
+        gate_split=ops.split_bf16(gate) if torch.device(device).type == "cuda" else None,
     )

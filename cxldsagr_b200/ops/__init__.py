@@ -220,6 +220,56 @@ def exact_topk(scores, k: int, *, causal_start: int | None = None, n: int | None
     return values, ids
 
 
+# ------------------------------------------------------------------- MoE
+def moe_route(logits, bias, cfg, *, split: bool = False):
+    """Routing from gate logits [T, E] (or [T, 2E] hi||lo halves when ``split``).
+
+    Returns (ids int32 [T, k], weights fp32 [T, k]); same rule as
+    :func:`reference.route_experts` (ties -> smaller index)."""
+    T = logits.shape[0]
+    K = cfg.num_experts_per_tok
+    ids = torch.empty((T, K), dtype=torch.int32, device=logits.device)
+    w = torch.empty((T, K), dtype=torch.float32, device=logits.device)
+    lib().moe_route(logits, split, bias, cfg.n_routed_experts, cfg.n_group, cfg.topk_group, K, cfg.norm_topk_prob,
+                    cfg.routed_scaling_factor, ids, w)
+    return ids, w
+
+
+class MoELayout:
+    """Padded contiguous grouped-GEMM layout built on the device (no host sync)."""
+
+    def __init__(self, rows: int, e0: int, n_local: int, K: int, device):
+        self.max_blocks = (rows + n_local * 127 + 127) // 128
+        self.M_pad = self.max_blocks * 128
+        self.e0, self.n_local = e0, n_local
+        self.row_pos = torch.empty(rows, dtype=torch.int32, device=device)
+        self.block_expert = torch.empty(self.max_blocks, dtype=torch.int32, device=device)
+        self.cursor = torch.empty(n_local, dtype=torch.int32, device=device)
+        self.total = torch.zeros(1, dtype=torch.int32, device=device)
+        self.a = torch.zeros((self.M_pad, K), dtype=FP8, device=device)
+        self.a_s = torch.zeros((K // 128, self.M_pad), dtype=torch.float32, device=device)
+
+    def build(self, ids, q, s_t, topk: int):
+        lib().moe_layout(ids.reshape(-1), self.e0, self.n_local, self.max_blocks, self.row_pos, self.block_expert,
+                         self.cursor, self.total)
+        lib().moe_gather(q, s_t, topk, self.row_pos, self.a, self.a_s)
+        return self
+
+
+def fp8_gemm_grouped(a, a_s, w, w_s, block_expert, out=None):
+    """Grouped FP8 GEMM over a padded layout: out[m] = a[m] . w[expert(m // 128)]^T."""
+    if out is None:
+        out = torch.empty((a.shape[0], w.shape[1]), dtype=torch.bfloat16, device=a.device)
+    lib().fp8_gemm_grouped(a, a_s, w, w_s, block_expert, out)
+    return out
+
+
+def moe_combine(y, row_pos, weights, T: int):
+    out = torch.empty((T, y.shape[1]), dtype=torch.bfloat16, device=y.device)
+    lib().moe_combine(y, row_pos, weights.contiguous(), weights.shape[1], out)
+    return out
+
+
 # ------------------------------------------------------------- attention
 def sparse_mla(q, kv, ids, scale, *, splits: int = 1, return_lse: bool = False, value_dim: int = 512,
                impl: int = 0):

@@ -82,11 +82,12 @@ class Comm:
         return C.broadcast(self.ctx, x, src)
 
 
-def make_comm(ctx: ParallelContext) -> Comm:
+def make_comm(ctx: ParallelContext, *, moe: tuple | None = None, max_rows: int = 1024) -> Comm:
+    """``moe=(n_experts, hidden, topk)`` reserves the fused expert-parallel buffers (p2p backend)."""
     if ctx.backend == "p2p" and ctx.world > 1:
         from .p2p import P2PComm
 
-        return P2PComm(ctx)
+        return P2PComm(ctx, moe=moe, max_rows=max_rows)
     return Comm(ctx)
 
 

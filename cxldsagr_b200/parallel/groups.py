@@ -66,7 +66,10 @@ class ParallelContext:
 
 
 def single(device) -> ParallelContext:
-    return ParallelContext(0, 1, None, torch.device(device))
+    dev = torch.device(device)
+    if dev.type == "cuda" and dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    return ParallelContext(0, 1, None, dev)
 
 
 def init_distributed(*, backend: str | None = None, timeout_s: float = 120.0, comm: str = "torch",

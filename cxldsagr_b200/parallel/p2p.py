@@ -25,7 +25,7 @@ from .. import ops
 from .comm import Comm
 from .groups import ParallelContext
 
-FLAG_SLOTS = 64
+FLAG_SLOTS = 128
 ALIGN = 256
 
 
@@ -42,12 +42,13 @@ class SymmetricHeap:
         self.dev = ctx.device.index
         self.nbytes = _align(nbytes)
         self.local = self.lib.symm_alloc(self.dev, self.nbytes)
-        handle = self.lib.symm_handle(self.dev, self.local)
-        handles = [None] * ctx.world
-        dist.all_gather_object(handles, handle, group=ctx.group)
-        self.bases = []
-        for q, h in enumerate(handles):
-            self.bases.append(self.local if q == ctx.rank else self.lib.symm_open(self.dev, h))
+        self.bases = [self.local]
+        if ctx.world > 1:
+            handle = self.lib.symm_handle(self.dev, self.local)
+            handles = [None] * ctx.world
+            dist.all_gather_object(handles, handle, group=ctx.group)
+            self.bases = [self.local if q == ctx.rank else self.lib.symm_open(self.dev, h)
+                          for q, h in enumerate(handles)]
         self._next = 0
         self.closed = False
 
@@ -68,7 +69,8 @@ class SymmetricHeap:
         if self.closed:
             return
         torch.cuda.synchronize(self.ctx.device)
-        dist.barrier(group=self.ctx.group)
+        if self.ctx.world > 1:
+            dist.barrier(group=self.ctx.group)
         for q, b in enumerate(self.bases):
             if q != self.ctx.rank:
                 self.lib.symm_close(self.dev, b)
@@ -93,21 +95,43 @@ class _Counter:
 
 
 class P2PComm(Comm):
-    def __init__(self, ctx: ParallelContext, *, max_rows: int = 1024, max_k: int = 7168, max_n: int = 7168):
+    """``moe=(n_experts, hidden, topk)`` also reserves the expert-parallel exchange buffers
+    (counts, every owner's grouped FP8 layout and its expert outputs, double-buffered)."""
+
+    def __init__(self, ctx: ParallelContext, *, max_rows: int = 1024, max_k: int = 7168, max_n: int = 7168,
+                 moe: tuple | None = None):
         super().__init__(ctx)
         if ctx.device.type != "cuda" or ctx.world > 8:
-            raise ValueError("the p2p backend needs 2-8 GPUs")
+            raise ValueError("the p2p backend needs 1-8 GPUs (1: single-GPU profiling of the fused kernels)")
         self.max_rows, self.max_k, self.max_n = max_rows, max_k, max_n
         W = ctx.world
         g_bytes = 2 * max_rows * max_k
         gs_bytes = 2 * (max_k // 128) * max_rows * 4
         rb_bytes = 2 * max_rows * max_n * 2
         flags = FLAG_SLOTS * 8
-        self.heap = SymmetricHeap(ctx, flags + g_bytes + gs_bytes + rb_bytes + 4 * ALIGN)
+        ep_bytes = 0
+        self.moe = moe
+        if moe is not None:
+            E, D, topk = moe
+            # Worst case: every routed row of the chunk lands on one owner, plus per-expert padding.
+            self.ep_mpad = (max_rows * topk + (E // W) * 127 + 127) // 128 * 128
+            self.ep_shapes = {"cnt": 2 * W * E * 4, "a": 2 * self.ep_mpad * D, "as": 2 * (D // 128) * self.ep_mpad * 4,
+                              "y": 2 * self.ep_mpad * D * 2}
+            ep_bytes = sum(self.ep_shapes.values()) + 4 * ALIGN
+        self.heap = SymmetricHeap(ctx, flags + g_bytes + gs_bytes + rb_bytes + ep_bytes + 4 * ALIGN)
         self.off_flags = self.heap.region(flags)
         self.off_g = self.heap.region(g_bytes)
         self.off_gs = self.heap.region(gs_bytes)
         self.off_rb = self.heap.region(rb_bytes)
+        self.ep_calls = 0
+        if moe is not None:
+            self.ep_off = {k: self.heap.region(v) for k, v in self.ep_shapes.items()}
+            self.ep_ptrs = {k: self.heap.ptrs(o) for k, o in self.ep_off.items()}
+            E, D, topk = moe
+            dev = ctx.device
+            self.ep_blocks = self.ep_mpad // 128
+            self.ep_cursor = torch.zeros(E, dtype=torch.int32, device=dev)
+            self.ep_block_expert = torch.full((self.ep_blocks,), -1, dtype=torch.int32, device=dev)
         self.flag_ptrs = self.heap.ptrs(self.off_flags)
         self.g_ptrs, self.gs_ptrs, self.rb_ptrs = (self.heap.ptrs(o) for o in (self.off_g, self.off_gs, self.off_rb))
         self.ag = _Counter()
@@ -164,6 +188,40 @@ class P2PComm(Comm):
         self.lib().fp8_gemm_rs(q, s_t, lin.weight, lin.scales, None, out, r, self.world, call, arrive, reuse,
                                self.flag_ptrs, self.rb_ptrs)
         self.fused_calls["rs"] += 1
+        return out
+
+    # ----------------------------------------------------------------- EP
+    def ep_ready(self, n_experts: int, hidden: int, topk: int, tokens: int) -> bool:
+        return (self.moe is not None and self.moe == (n_experts, hidden, topk) and tokens <= self.max_rows
+                and n_experts % self.world == 0)
+
+    def _ep_views(self, parity: int):
+        E, D, topk = self.moe
+        M = self.ep_mpad
+        a = self.heap.view(self.ep_off["a"], self.ep_shapes["a"]).view(torch.float8_e4m3fn).view(2, M, D)[parity]
+        a_s = self.heap.view(self.ep_off["as"], self.ep_shapes["as"]).view(torch.float32).view(2, D // 128, M)[parity]
+        y = self.heap.view(self.ep_off["y"], self.ep_shapes["y"]).view(torch.bfloat16).view(2, M, D)[parity]
+        return a, a_s, y
+
+    def moe_ep(self, ids, q, s_t, weights, experts_fn):
+        """Fused EP MoE: dispatch into owners' grouped layouts, run ``experts_fn(a, a_s, block_expert, y_out)``
+        on this rank's experts, combine in k order.  Returns bf16 [T, D]."""
+        E, D, topk = self.moe
+        T = ids.shape[0]
+        self.ep_calls += 1
+        call = self.ep_calls
+        parity = call & 1
+        p = self.ep_ptrs
+        pos = torch.empty((T * topk,), dtype=torch.int32, device=q.device)
+        ids32 = ids.to(torch.int32).contiguous()
+        self.lib().ep_dispatch(ids32, q.contiguous(), s_t, self.ep_cursor, pos, self.ep_block_expert, self.ctx.rank,
+                               self.world, E, self.ep_mpad, call, self.flag_ptrs, p["cnt"], p["a"], p["as"], p["y"])
+        a, a_s, y = self._ep_views(parity)
+        experts_fn(a, a_s, self.ep_block_expert, y)
+        out = torch.empty((T, D), dtype=torch.bfloat16, device=q.device)
+        self.lib().ep_combine(ids32, pos, weights.contiguous(), out, self.ctx.rank, self.world, E, self.ep_mpad, call,
+                              self.flag_ptrs, p["cnt"], p["a"], p["as"], p["y"])
+        self.fused_calls["ep"] = self.fused_calls.get("ep", 0) + 1
         return out
 
     def close(self):

@@ -75,8 +75,9 @@ def test_silu_mul_quant():
 
 # ------------------------------------------------------------------ gemms
 @pytest.mark.parametrize("M,N,K", [(1, 576, 7168), (128, 1536, 7168), (200, 7168, 2048), (1024, 2240, 7168), (77, 130, 256),
-                                   (128, 7168, 18432), (1024, 36864, 1024)])
+                                   (128, 7168, 18432), (1024, 36864, 1024), (1024, 7168, 4096), (640, 7168, 2048)])
 def test_fp8_gemm(M, N, K):
+    """Includes N = 7168 shapes that take the 224-wide tiles (scale blocks straddle a warp's columns)."""
     torch.manual_seed(4)
     x = torch.randn(M, K, device=DEV).bfloat16()
     w, s = quantize_weight_blocks(torch.randn(N, K, device=DEV) * 0.02, pow2_scales=False)
@@ -85,7 +86,7 @@ def test_fp8_gemm(M, N, K):
     assert rel_err(got.cpu(), want) < 2e-2
 
 
-@pytest.mark.parametrize("M,N,K", [(130, 384, 1024), (128, 7168, 16384)])
+@pytest.mark.parametrize("M,N,K", [(130, 384, 1024), (128, 7168, 16384), (1024, 7168, 2048)])
 def test_fp8_gemm_residual(M, N, K):
     """Residual fused in the epilogue (no split) and in the split-K reduce."""
     torch.manual_seed(5)
@@ -275,3 +276,68 @@ def test_gather_rows_from_pinned_host():
     slots = torch.tensor([1, 64, 2, 30], device=DEV)
     ops.gather_host_records(host, records, hid, slots)
     assert torch.equal(records[slots].cpu(), host[hid.cpu()])
+
+
+# ------------------------------------------------------------------- MoE
+class _MoECfg:
+    n_routed_experts = 64
+    n_group = 8
+    topk_group = 4
+    num_experts_per_tok = 8
+    norm_topk_prob = True
+    routed_scaling_factor = 2.5
+
+
+@pytest.mark.parametrize("T", [1, 37, 300])
+def test_moe_route_matches_reference(T):
+    torch.manual_seed(11)
+    cfg = _MoECfg
+    E, D = cfg.n_routed_experts, 256
+    x = torch.randn(T, D, device=DEV).bfloat16()
+    gate = torch.randn(E, D, device=DEV) * 0.05
+    bias = torch.randn(E, device=DEV) * 0.1
+    logits = ops.linear_split(x, ops.split_bf16(gate))
+    ids, w = ops.moe_route(logits, bias, cfg, split=True)
+    want_ids, want_w = ref.route_experts(x.cpu(), gate.cpu(), bias.cpu(), cfg)
+    for t in range(T):
+        a = sorted(zip(ids[t].cpu().tolist(), w[t].cpu().tolist()))
+        b = sorted(zip(want_ids[t].tolist(), want_w[t].tolist()))
+        assert [i for i, _ in a] == [i for i, _ in b]
+        assert max(abs(p - q) for (_, p), (_, q) in zip(a, b)) < 1e-4
+
+
+@pytest.mark.parametrize("T,E,e0,n_local", [(64, 16, 0, 16), (200, 32, 8, 8)])
+def test_grouped_moe_matches_reference(T, E, e0, n_local):
+    """Device layout + grouped FP8 GEMMs + combine vs the FP32 reference over the local experts."""
+    torch.manual_seed(12)
+    D, I, K = 256, 256, 4
+    x = torch.randn(T, D, device=DEV).bfloat16()
+    q, s_t = ops.quantize_act(x)
+    ids = torch.randint(0, E, (T, K), device=DEV, dtype=torch.int32)
+    w = torch.rand(T, K, device=DEV)
+    wg = [quantize_weight_blocks(torch.randn(2 * I, D, device=DEV) * 0.05, pow2_scales=False) for _ in range(n_local)]
+    wd = [quantize_weight_blocks(torch.randn(D, I, device=DEV) * 0.05, pow2_scales=False) for _ in range(n_local)]
+    w_gu = torch.stack([a for a, _ in wg]).contiguous()
+    s_gu = torch.stack([b for _, b in wg]).float().contiguous()
+    w_d = torch.stack([a for a, _ in wd]).contiguous()
+    s_d = torch.stack([b for _, b in wd]).float().contiguous()
+    lay = ops.MoELayout(T * K, e0, n_local, D, DEV).build(ids, q, s_t, K)
+    gu = ops.fp8_gemm_grouped(lay.a, lay.a_s, w_gu, s_gu, lay.block_expert)
+    _, hq, hs = ops.silu_mul_quant(gu)
+    y = ops.fp8_gemm_grouped(hq, hs, w_d, s_d, lay.block_expert)
+    got = ops.moe_combine(y, lay.row_pos, w, T).float().cpu()
+    ops.check_errors(DEV)
+    # reference: only local experts contribute
+    want = torch.zeros(T, D)
+    for t in range(T):
+        for k in range(K):
+            e = int(ids[t, k]) - e0
+            if not 0 <= e < n_local:
+                continue
+            g = ref.fp8_linear(x[t:t + 1].cpu(), wg[e][0].cpu(), wg[e][1].cpu()).float()
+            h = ref.silu_mul(g[:, :I], g[:, I:])
+            yk = ref.fp8_linear(h.bfloat16(), wd[e][0].cpu(), wd[e][1].cpu()).float()
+            want[t] += float(w[t, k]) * yk[0]
+    assert rel_err(got, want) < 3e-2
+    rows = (lay.row_pos >= 0).sum().item()
+    assert rows == int(((ids >= e0) & (ids < e0 + n_local)).sum())

@@ -151,3 +151,58 @@ def test_fused_ag_rs_match_nccl(world):
                 assert v == 0.0, (k, v)
             if k.startswith("rs") and k.endswith("maxdiff"):
                 assert v <= 1e-2 * max(1.0, rep[k.replace("maxdiff", "scale")]), (k, v)
+
+
+def _model_backends(rank, world):
+    """Layers 0 (dense) and 3 (MoE, reduced expert count) of a V3.2-shaped model:
+    the fused peer-memory backend (AG-GEMM, GEMM-RS, EP dispatch/combine) against
+    the NCCL baseline, both sequence/expert parallel on the same ranks."""
+    from cxldsagr_b200.checkpoint import StateDictSource, random_state_dict
+    from cxldsagr_b200.config import CacheConfig, v32_config
+    from cxldsagr_b200.models.deepseek_v32.model import DeepSeekV32Model
+    from cxldsagr_b200.ops.native import check_errors
+    from cxldsagr_b200.parallel.groups import ParallelContext, init_distributed
+
+    base = init_distributed(timeout_s=60, comm="torch")
+    dev = base.device
+    cfg = v32_config(4, n_routed_experts=16, n_group=8, topk_group=4, num_experts_per_tok=4,
+                     moe_intermediate_size=512)
+    layers = [0, 3]
+    per = cfg.n_routed_experts // world
+    src = StateDictSource(random_state_dict(cfg, layers=layers, seed=0, device=dev,
+                                            experts=range(rank * per, (rank + 1) * per)), cfg)
+    cache = CacheConfig(capacity=2048 + 64, chunk_size=1024, candidate_tokens=64)
+    fused_ctx = ParallelContext(base.rank, base.world, base.group, dev, backend="p2p")
+    m_nccl = DeepSeekV32Model(cfg, src, device=dev, cache=cache, layers=layers, parallel=base)
+    m_p2p = DeepSeekV32Model(cfg, src, device=dev, cache=cache, layers=layers, parallel=fused_ctx)
+    g = torch.Generator(device=dev).manual_seed(5)
+    ids = torch.randint(0, cfg.vocab_size, (2048 + 64,), generator=g, device=dev)
+    out = {}
+    for name, m in (("nccl", m_nccl), ("p2p", m_p2p)):
+        a = m.prefill(ids[:2048]).logits
+        b = m.forward(ids[2048:], transient=True, return_hidden=True)
+        torch.cuda.synchronize()
+        check_errors(dev)
+        out[name] = (a.float().cpu(), b.logits.float().cpu(), b.hidden.float().cpu())
+    calls = dict(m_p2p.comm.fused_calls)
+    m_p2p.comm.close()
+
+    def corr(x, y):
+        return torch.corrcoef(torch.stack([x.flatten().double(), y.flatten().double()]))[0, 1].item()
+
+    return {"calls": calls,
+            "prefill_maxdiff": (out["nccl"][0] - out["p2p"][0]).abs().max().item(),
+            "cand_corr": corr(out["nccl"][1], out["p2p"][1]),
+            "hidden_corr": corr(out["nccl"][2], out["p2p"][2]),
+            "finite": bool(torch.isfinite(out["p2p"][1]).all())}
+
+
+@pytest.mark.parametrize("world", [2])
+def test_model_fused_backend_matches_nccl(world):
+    _need(world)
+    reports = _spawn(_model_backends, world)
+    for rank, rep in reports.items():
+        print(rank, rep)
+        assert rep["finite"]
+        assert rep["calls"].get("ag", 0) > 0 and rep["calls"].get("rs", 0) > 0 and rep["calls"].get("ep", 0) > 0
+        assert rep["cand_corr"] > 0.999 and rep["hidden_corr"] > 0.999

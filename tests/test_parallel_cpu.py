@@ -120,5 +120,5 @@ def test_sequence_expert_parallel_matches_single(world, method):
         # indexer selection of the random-init model), not bitwise.
         assert h.shape == single[2].shape
         for got, want in ((a, single[0]), (b, single[1])):
-            assert (got - want).abs().max() < 0.1 and corr(got, want) > 0.998
+            assert (got - want).abs().max() < 0.15 and corr(got, want) > 0.995
         assert corr(h, single[2]) > 0.99
