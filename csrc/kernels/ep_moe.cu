@@ -132,12 +132,19 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const __grid_constant__
   const int vec = p.D / 16, nkb = p.D / 128;
   for (int r = blockIdx.x * 8 + warp; r < R; r += gridDim.x * 8) {
     const int e = ids[r];
+    if (e < 0 || e >= p.E) {  // recorded by ep_count; never index with it
+      if (lane == 0) pos_out[r] = -1;
+      continue;
+    }
     int pos = 0;
     if (lane == 0) pos = s_base[e] + s_srcoff[e] + atomicAdd(&cursor[e], 1);
     pos = __shfl_sync(0xffffffffu, pos, 0);
     const int o = e / p.E_loc;
     if (pos >= p.M_pad) {
-      if (lane == 0) record_error(err, kErrPoolOverflow);
+      if (lane == 0) {
+        record_error(err, kErrPoolOverflow);
+        pos_out[r] = -1;
+      }
       continue;
     }
     if (lane == 0) pos_out[r] = pos;
@@ -188,9 +195,11 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const __grid_constant__
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int k = 0; k < p.topk; ++k) {
       const int r = t * p.topk + k;
-      const int o = ids[r] / p.E_loc;
+      const int e = ids[r], pr = pos[r];
+      if (e < 0 || e >= p.E || pr < 0 || pr >= p.M_pad) continue;  // failed dispatch: error already recorded
+      const int o = e / p.E_loc;
       const float wk = w[r];
-      const __nv_bfloat16* yrow = p.y[o] + (int64_t(p.parity) * p.M_pad + pos[r]) * p.D;
+      const __nv_bfloat16* yrow = p.y[o] + (int64_t(p.parity) * p.M_pad + pr) * p.D;
       const uint4 v = __ldcg(reinterpret_cast<const uint4*>(yrow + c));
       const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
 #pragma unroll

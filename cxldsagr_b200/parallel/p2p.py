@@ -212,7 +212,7 @@ class P2PComm(Comm):
         call = self.ep_calls
         parity = call & 1
         p = self.ep_ptrs
-        pos = torch.empty((T * topk,), dtype=torch.int32, device=q.device)
+        pos = torch.full((T * topk,), -1, dtype=torch.int32, device=q.device)
         ids32 = ids.to(torch.int32).contiguous()
         self.lib().ep_dispatch(ids32, q.contiguous(), s_t, self.ep_cursor, pos, self.ep_block_expert, self.ctx.rank,
                                self.world, E, self.ep_mpad, call, self.flag_ptrs, p["cnt"], p["a"], p["as"], p["y"])
