@@ -45,6 +45,12 @@ def parse():
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--e2e-steps", type=int, default=2)
     p.add_argument("--profile", action="store_true", help="print a per-scope device-time breakdown to stderr")
+    p.add_argument("--parallel", default="dp", choices=["dp", "sp"],
+                   help="dp: every rank serves its own request (weak scaling); sp: one request across all ranks "
+                        "(sequence-parallel attention, column/row-parallel dense MLP, expert-parallel MoE)")
+    p.add_argument("--comm", default="p2p", choices=["p2p", "torch"],
+                   help="sp collectives: fused peer-memory kernels (p2p) or the NCCL baseline (torch)")
+    p.add_argument("--full", action="store_true", help="the full 61-layer model (3 dense + 58 MoE layers)")
     return p.parse_args()
 
 
@@ -65,7 +71,7 @@ def main():
     import torch.distributed as dist
 
     from cxldsagr_b200 import ops
-    from cxldsagr_b200.checkpoint import StateDictSource, random_state_dict
+    from cxldsagr_b200.checkpoint import RandomSource
     from cxldsagr_b200.config import CacheConfig, v32_config
     from cxldsagr_b200.models.deepseek_v32.model import DeepSeekV32Model
     from cxldsagr_b200.ops.native import launch_count
@@ -82,16 +88,24 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
     H, A = args.history, args.extend
-    cfg = v32_config(layers=args.layers)
-    src = StateDictSource(random_state_dict(cfg, layers=range(args.layers), seed=0, device=dev))
+    sp = args.parallel == "sp" and world > 1
+    n_layers = 61 if args.full else args.layers
+    cfg = v32_config(layers=n_layers)
+    src = RandomSource(cfg, layers=range(n_layers), seed=0, device=dev)
     offload = args.method != "hbm"
     cache = CacheConfig(method=args.method, capacity=H + A, chunk_size=args.chunk,
-                        pool_tokens=(H + A) // 2 if offload else None, host_tokens=H + A)
-    model = DeepSeekV32Model(cfg, src, device=dev, cache=cache)
+                        pool_tokens=(H + A) // 2 if offload else None, host_tokens=H + A, candidate_tokens=A)
+    par = None
+    if sp:
+        from cxldsagr_b200.parallel.groups import ParallelContext
+
+        par = ParallelContext(rank, world, dist.group.WORLD, dev, backend=args.comm)
+    model = DeepSeekV32Model(cfg, src, device=dev, cache=cache, parallel=par)
     del src
     torch.cuda.empty_cache()
 
-    g = torch.Generator().manual_seed(1234 + rank)
+    # sp: every rank holds the same request (its rows of each chunk); dp: one request per rank.
+    g = torch.Generator().manual_seed(1234 + (0 if sp else rank))
     hist_host = torch.randint(0, cfg.vocab_size, (H,), generator=g).pin_memory()
     ext_host = torch.randint(0, cfg.vocab_size, (A,), generator=g).pin_memory()
     hist = hist_host.to(dev)
@@ -108,7 +122,7 @@ def main():
         model.prefill(hist)
         if events:
             events[1].record(stream)
-        if not args.no_graph and not offload:
+        if not args.no_graph and not offload and not sp:
             if graph is None:
                 graph = model.capture_extend(A)
             graph.replay(ext)
@@ -186,40 +200,48 @@ def main():
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
     prefill_ms, extend_ms, total_ms, e2e_s = stats.tolist()
-    prefill_tok_s = world * H / (prefill_ms / 1e3)
+    requests = 1 if sp else world
+    prefill_tok_s = requests * H / (prefill_ms / 1e3)
+    model_name = ("DeepSeek-V3.2 (61 layers: 3 dense + 58 MoE, 256 routed experts top-8)" if args.full else
+                  "DeepSeek-V3.2 layers 0-2 + embedding + final norm + last-token LM head")
+    if sp:
+        parallelism = f"sp{world}+ep{world} ({'fused peer-memory kernels' if args.comm == 'p2p' else 'NCCL baseline'})"
+    else:
+        parallelism = f"dp{world}" if world > 1 else "single"
     if rank == 0:
         out = {
             "metric": METRIC,
             "value": round(prefill_tok_s, 1),
-            "unit": "prefill tokens/s per box (64K history, layers 0-2)",
+            "unit": ("prefill tokens/s per box (one 64K request across the box)" if sp else
+                     "prefill tokens/s per box (64K history per request, one request per GPU)"),
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": round(total_ms / args.steps, 3),
             "higher_is_better": True,
-            "scaling": "weak",
-            "vs_baseline": round(prefill_tok_s / (world * BASELINE_PREFILL_TOK_S), 4),
+            "scaling": "strong" if sp else "weak",
+            "vs_baseline": round(prefill_tok_s / (requests * BASELINE_PREFILL_TOK_S), 4),
             "dtype": "bf16",
-            "data": "synthetic (uniform random token ids; random-init weights of the DeepSeek-V3.2 layer 0-2 "
+            "data": "synthetic (uniform random token ids; random-init weights of the DeepSeek-V3.2 "
                     "architecture, FP8 128x128 block-scaled linears)",
             "config": {
-                "model": "DeepSeek-V3.2 layers 0-2 + embedding + final norm + last-token LM head",
-                "global_batch": world,
+                "model": model_name,
+                "global_batch": requests,
                 "seq_len": H + A,
                 "history": H,
                 "extend": A,
                 "chunk": args.chunk,
                 "cache_method": args.method,
-                "parallelism": f"dp{world}" if world > 1 else "single",
+                "parallelism": parallelism,
                 "l2": "no flush: per-step weight stream (3.7 GB) exceeds L2",
-                "extend_graph": not args.no_graph and not offload,
+                "extend_graph": not args.no_graph and not offload and not sp,
             },
             "prefill_ms": round(prefill_ms, 3),
             "extend_ms": round(extend_ms, 4),
             "extend_vs_baseline": round(BASELINE_EXTEND_MS / extend_ms, 4),
             "clocks": clocks,
             "e2e": {
-                "value": round(world * H / e2e_s, 1),
+                "value": round(requests * H / e2e_s, 1),
                 "unit": "prefill tokens/s per box, end to end (public API, pinned ids in, logits out, "
                         "prefill + extend wall clock)",
                 "request_ms": round(e2e_s * 1e3, 3),
@@ -231,6 +253,8 @@ def main():
         print(json.dumps(out))
     if graph is not None:
         del graph
+    if hasattr(model.comm, "close"):
+        model.comm.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -239,6 +239,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row_in_tile = quad * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     bool ok = true;
+    // RS staging tile [BM][BN + 8] bf16 after the pipeline buffers (dynamic smem).
+    __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(&s) + sizeof(GemmSmem<BN, STAGES>));
 
     if constexpr (MODE == kModeAG) {
       // Push this rank's shard (rows [rank*S, rank*S+S) of the gathered A) and
@@ -354,59 +356,81 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         continue;
       }
-      __nv_bfloat16* orow = nullptr;
-      const __nv_bfloat16* rrow = nullptr;
-      if (ok && row < M && n0 < N) {
-        if constexpr (MODE == kModeRS) {
-          const int owner = row / p2p.S;
+      if constexpr (MODE == kModeRS) {
+        // Stage the BF16 tile in smem, then write each owner row as contiguous
+        // 16-byte chunks by consecutive threads (coalesced NVLink writes).
+        __nv_bfloat16* st = stage + row_in_tile * (BN + 8) + chalf * CPW;
+#pragma unroll
+        for (int j = 0; j < CPW; j += 8) {
+          uint4 o;
+          o.x = pack_bf16(acc[j], acc[j + 1]);
+          o.y = pack_bf16(acc[j + 2], acc[j + 3]);
+          o.z = pack_bf16(acc[j + 4], acc[j + 5]);
+          o.w = pack_bf16(acc[j + 6], acc[j + 7]);
+          *reinterpret_cast<uint4*>(st + j) = o;
+        }
+        named_barrier(kEpiBarrier, kEpiWarps * 32);
+        const int tn0 = (tile / num_m) * BN;
+        constexpr int kChunks = BN / 8;
+        for (int i = threadIdx.x - 64; i < BM * kChunks && ok; i += kEpiWarps * 32) {
+          const int r = i / kChunks, c = (i % kChunks) * 8;
+          const int grow = m0 + r;
+          if (grow >= M || tn0 + c >= N) continue;
+          const int owner = grow / p2p.S;
           if (owner != owner_ok && p2p.reuse_target > 0) {
             // Reuse guard: the owner's reduce of two calls ago has read this parity.
             if (!wait_flag_ge(p2p.flags[p2p.rank] + kFlagRsDone + owner, p2p.reuse_target, err,
                               kErrTimeoutPeerFlag, abort_flag)) {
               ok = false;
+              break;
             }
           }
           owner_ok = owner;
-          const int64_t slot = (int64_t(p2p.parity) * p2p.world + p2p.rank) * p2p.S + (row - owner * p2p.S);
-          orow = p2p.rb[owner] + slot * N + n0;
-        } else {
+          const int64_t slot = (int64_t(p2p.parity) * p2p.world + p2p.rank) * p2p.S + (grow - owner * p2p.S);
+          *reinterpret_cast<uint4*>(p2p.rb[owner] + slot * N + tn0 + c) =
+              *reinterpret_cast<const uint4*>(stage + r * (BN + 8) + c);
+        }
+      } else {
+        __nv_bfloat16* orow = nullptr;
+        const __nv_bfloat16* rrow = nullptr;
+        if (ok && row < M && n0 < N) {
           orow = out + static_cast<size_t>(row) * ldo + n0;
           rrow = residual ? residual + static_cast<size_t>(row) * ldr + n0 : nullptr;
         }
-      }
-      if (orow != nullptr && ok) {
-        const int ncols = min(CPW, N - n0);
-        const bool vec = (ncols == CPW) && ((reinterpret_cast<uintptr_t>(orow) & 15) == 0) &&
-                         (!rrow || (reinterpret_cast<uintptr_t>(rrow) & 15) == 0);
-        if (vec) {
+        if (orow != nullptr) {
+          const int ncols = min(CPW, N - n0);
+          const bool vec = (ncols == CPW) && ((reinterpret_cast<uintptr_t>(orow) & 15) == 0) &&
+                           (!rrow || (reinterpret_cast<uintptr_t>(rrow) & 15) == 0);
+          if (vec) {
 #pragma unroll
-          for (int j = 0; j < CPW; j += 8) {
-            float v[8];
+            for (int j = 0; j < CPW; j += 8) {
+              float v[8];
 #pragma unroll
-            for (int t = 0; t < 8; ++t) v[t] = acc[j + t];
-            if (rrow) {
-              uint4 rv = *reinterpret_cast<const uint4*>(rrow + j);
-              const uint32_t* rw = reinterpret_cast<const uint32_t*>(&rv);
+              for (int t = 0; t < 8; ++t) v[t] = acc[j + t];
+              if (rrow) {
+                uint4 rv = *reinterpret_cast<const uint4*>(rrow + j);
+                const uint32_t* rw = reinterpret_cast<const uint32_t*>(&rv);
 #pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                v[2 * t] += bf16_lo(rw[t]);
-                v[2 * t + 1] += bf16_hi(rw[t]);
+                for (int t = 0; t < 4; ++t) {
+                  v[2 * t] += bf16_lo(rw[t]);
+                  v[2 * t + 1] += bf16_hi(rw[t]);
+                }
               }
+              uint4 o;
+              o.x = pack_bf16(v[0], v[1]);
+              o.y = pack_bf16(v[2], v[3]);
+              o.z = pack_bf16(v[4], v[5]);
+              o.w = pack_bf16(v[6], v[7]);
+              *reinterpret_cast<uint4*>(orow + j) = o;
             }
-            uint4 o;
-            o.x = pack_bf16(v[0], v[1]);
-            o.y = pack_bf16(v[2], v[3]);
-            o.z = pack_bf16(v[4], v[5]);
-            o.w = pack_bf16(v[6], v[7]);
-            *reinterpret_cast<uint4*>(orow + j) = o;
-          }
-        } else {
+          } else {
 #pragma unroll
-          for (int j = 0; j < CPW; ++j) {
-            if (j < ncols) {
-              float v = acc[j];
-              if (rrow) v += __bfloat162float(rrow[j]);
-              orow[j] = __float2bfloat16_rn(v);
+            for (int j = 0; j < CPW; ++j) {
+              if (j < ncols) {
+                float v = acc[j];
+                if (rrow) v += __bfloat162float(rrow[j]);
+                orow[j] = __float2bfloat16_rn(v);
+              }
             }
           }
         }
@@ -441,9 +465,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int MODE = kModePlain>
 inline size_t smem_bytes() {
-  return sizeof(GemmSmem<BN, STAGES>) + 1024;
+  return sizeof(GemmSmem<BN, STAGES>) + 1024 + (MODE == kModeRS ? size_t(BM) * (BN + 8) * 2 : 0);
 }
 
 }  // namespace gemm_fp8

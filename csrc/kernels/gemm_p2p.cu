@@ -155,8 +155,8 @@ void launch_fp8_gemm_rs(P2PArgs p, const uint8_t* A, int lda, const float* sfa, 
   const int tiles = ((M + BM - 1) / BM) * ((N + 127) / 128);
   p.grid = std::min(tiles, sm_count());
   if (p.reduce_grid != rs_reduce_grid(p.S, N)) throw std::invalid_argument("rs gemm: reduce grid differs from plan");
-  const size_t smem = smem_bytes<128, 6>();
-  auto kern = fp8_gemm_kernel<128, 6, kModeRS>;
+  const size_t smem = smem_bytes<128, 5, kModeRS>();
+  auto kern = fp8_gemm_kernel<128, 5, kModeRS>;
   cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)), "rs gemm smem");
   kern<<<p.grid, kThreads, smem, stream>>>(ta, tb, sfa, lda_s, sfb, nullptr, 0, nullptr, 0, M, N, K, 1, nullptr,
                                            err, p, GroupArgs{});

@@ -132,6 +132,33 @@ def dequantize_weight_blocks(w: torch.Tensor, scales: torch.Tensor, block=(128, 
 
 
 # ------------------------------------------------------------- random init
+def _random_tensors(name: str, shape, kind: str, cfg: ModelConfig, gen, *, seed: int, std: float, device,
+                    pow2_scales: bool) -> dict[str, torch.Tensor]:
+    """The tensor(s) named ``name`` (an FP8 linear also yields its ``weight_scale_inv``)."""
+    import zlib
+
+    gen.manual_seed((seed * 1000003 + zlib.crc32(name.encode())) & 0x7FFFFFFFFFFFFFFF)
+    if kind == "norm":
+        return {name: torch.ones(shape, dtype=torch.float32 if "k_norm" in name else torch.bfloat16, device=device)}
+    if kind == "bias":
+        return {name: torch.zeros(shape, dtype=torch.float32, device=device)}
+    if kind == "fp32":
+        return {name: torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std}
+    if kind == "embed":
+        return {name: (torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std).bfloat16()}
+    w = torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std
+    if cfg.weight_dtype == "fp8":
+        q, sc = quantize_weight_blocks(w, cfg.weight_block_size, pow2_scales)
+        return {name: q, name[: -len(".weight")] + ".weight_scale_inv": sc}
+    return {name: w.bfloat16()}
+
+
+def _expert_of(name: str):
+    if ".mlp.experts." not in name:
+        return None
+    return int(name.split(".mlp.experts.")[1].split(".")[0])
+
+
 def random_state_dict(
     cfg: ModelConfig,
     layers: Iterable[int] | None = None,
@@ -154,37 +181,67 @@ def random_state_dict(
     generates only its own routed ``experts`` gets the same replicated tensors
     as every other rank.
     """
-    import zlib
-
     gen = torch.Generator(device=device)
-    keep_experts = None if experts is None else set(experts)
+    keep = None if experts is None else set(experts)
     out: dict[str, torch.Tensor] = {}
-    specs = model_tensor_specs(cfg, layers)
-    for name, (shape, kind) in specs.items():
+    for name, (shape, kind) in model_tensor_specs(cfg, layers).items():
         if not include_embeddings and kind == "embed":
             continue
-        if keep_experts is not None and ".mlp.experts." in name:
-            if int(name.split(".mlp.experts.")[1].split(".")[0]) not in keep_experts:
-                continue
-        gen.manual_seed((seed * 1000003 + zlib.crc32(name.encode())) & 0x7FFFFFFFFFFFFFFF)
-        if kind == "norm":
-            out[name] = torch.ones(shape, dtype=torch.float32 if "k_norm" in name else torch.bfloat16, device=device)
-        elif kind == "bias":
-            out[name] = torch.zeros(shape, dtype=torch.float32, device=device)
-        elif kind == "fp32":
-            out[name] = torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std
-        elif kind == "embed":
-            out[name] = (torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std).bfloat16()
-        else:
-            w = torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std
-            if cfg.weight_dtype == "fp8":
-                q, s = quantize_weight_blocks(w, cfg.weight_block_size, pow2_scales)
-                out[name] = q
-                out[name[: -len(".weight")] + ".weight_scale_inv"] = s
-            else:
-                out[name] = w.bfloat16()
-            del w
+        e = _expert_of(name)
+        if keep is not None and e is not None and e not in keep:
+            continue
+        out.update(_random_tensors(name, shape, kind, cfg, gen, seed=seed, std=std, device=device,
+                                   pow2_scales=pow2_scales))
     return out
+
+
+class RandomSource:
+    """Lazily generated random weights (same values as :func:`random_state_dict`).
+
+    Each tensor is created when the model loader asks for it, so a 61-layer
+    671B model can be built rank by rank without ever holding a full state
+    dict next to the loaded weights.
+    """
+
+    def __init__(self, cfg: ModelConfig, layers: Iterable[int] | None = None, *, seed: int = 0, std: float = 0.02,
+                 device="cpu", pow2_scales: bool = True):
+        self.cfg = cfg
+        self.config = cfg
+        self.device = device
+        self.seed, self.std, self.pow2 = seed, std, pow2_scales
+        self.specs = model_tensor_specs(cfg, layers)
+        self._scale_of = {n[: -len(".weight")] + ".weight_scale_inv": n for n, (_, k) in self.specs.items()
+                          if k not in ("norm", "bias", "fp32", "embed") and cfg.weight_dtype == "fp8"}
+        self._gen = torch.Generator(device=device)
+        self._cache: dict[str, torch.Tensor] = {}
+
+    def __contains__(self, name):
+        return name in self.specs or name in self._scale_of
+
+    def keys(self):
+        return list(self.specs) + list(self._scale_of)
+
+    @property
+    def tensor_metadata(self) -> dict:
+        meta = {n: {"shape": list(shape)} for n, (shape, _) in self.specs.items()}
+        for sname, wname in self._scale_of.items():
+            n, k = self.specs[wname][0]
+            bn, bk = self.cfg.weight_block_size
+            meta[sname] = {"shape": [_cdiv(n, bn), _cdiv(k, bk)]}
+        return meta
+
+    def get_tensor(self, name: str) -> torch.Tensor:
+        if name in self._cache:
+            return self._cache.pop(name)
+        base = self._scale_of.get(name, name)
+        if base not in self.specs:
+            raise KeyError(f"required tensor {name!r} is absent")
+        shape, kind = self.specs[base]
+        made = _random_tensors(base, shape, kind, self.cfg, self._gen, seed=self.seed, std=self.std,
+                               device=self.device, pow2_scales=self.pow2)
+        out = made.pop(name)
+        self._cache.update(made)  # the partner (weight or its scales), asked for next by the loader
+        return out
 
 
 # --------------------------------------------------------------- writer
