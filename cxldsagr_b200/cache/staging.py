@@ -43,6 +43,32 @@ class StagingLease:
             self.event.record(st.stream)
         return self
 
+    def prefetch_runs(self, host: torch.Tensor, runs, rows: int, *, before=None):
+        """Copy host rows into this buffer: ``runs`` yields (buffer row, count, host row).
+
+        ``before`` runs on the staging stream first (e.g. waits for pending
+        host writes).  One cudaMemcpyAsync per contiguous run.
+        """
+        st = self.staging
+        if rows > st.buffers[self.index].shape[0]:
+            raise ValueError("history exceeds the staging buffer")
+        self.rows = rows
+        buf = st.buffers[self.index]
+        if st.stream is None:
+            for lo, n, h in runs:
+                buf[lo:lo + n].copy_(host[h:h + n])
+            return self
+        if st.consumed[self.index] is not None:
+            st.stream.wait_event(st.consumed[self.index])
+        with torch.cuda.stream(st.stream):
+            if before is not None:
+                before()
+            for lo, n, h in runs:
+                buf[lo:lo + n].copy_(host[h:h + n], non_blocking=True)
+            self.event = torch.cuda.Event()
+            self.event.record(st.stream)
+        return self
+
     def wait_ready(self) -> torch.Tensor:
         if self.event is not None:
             torch.cuda.current_stream(self.staging.device).wait_event(self.event)

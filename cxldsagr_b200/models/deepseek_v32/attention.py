@@ -37,6 +37,8 @@ class LayerState:
     def __init__(self, kv: SparseTokenCache, index: IndexerCache):
         self.kv = kv
         self.index = index
+        self.dense = None       # dense_prefetch: staged [rows, 576] history of this layer for the current chunk
+        self.last_rows = None   # physical rows of the chunk's new records
 
     @property
     def cache(self):
@@ -87,6 +89,10 @@ class AttentionRunner:
             dst = state.kv.destination_rows(T)
             ops.kv_finish(kv, L, rope, w.kv_norm, cfg.norm_eps, freqs, positions, state.kv.records, dst)
             state.kv.finish_append(dst)
+            state.last_rows = dst
+            if state.dense is not None:
+                # The staged history plus this chunk's records (logical row = staged row).
+                state.dense[pos:pos + T] = state.kv.records[dst]
         with scope("index_k"):
             k_rows, s_rows = state.index.rows(pos, T)
             ops.index_k(ik, rope, w.index_norm_w, w.index_norm_b, cfg.norm_eps, freqs, positions, k_rows, s_rows)
@@ -149,7 +155,10 @@ class AttentionRunner:
                     self._update_hints(state, logits, values, pos, end)
             self.last_indices = ids
             with scope("sparse_mla"):
-                attn = self._consume(cache, q_proj, ids)
+                if state.dense is not None:
+                    attn = ops.sparse_mla(q_proj, state.dense, ids, cfg.attention_scale, value_dim=cfg.kv_lora_rank)
+                else:
+                    attn = self._consume(cache, q_proj, ids)
         with scope("attention_output"):
             with scope("expand"):
                 v = ops.mla_expand(attn, self.w.wv_b)

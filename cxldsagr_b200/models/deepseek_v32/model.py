@@ -352,6 +352,11 @@ class DeepSeekV32Model:
                 mlp = DenseMLP(mw, comm, sharded=par.world > 1)
             post = source.get_tensor(f"model.layers.{layer}.post_attention_layernorm.weight").to(dev, torch.float32)
             self.blocks.append(Block(cfg, layer, runner, mlp, post.contiguous(), comm))
+        self.dense_staging = None
+        if cc.method == "dense_prefetch":
+            from ...cache.staging import DoubleBufferStaging
+
+            self.dense_staging = DoubleBufferStaging(cc.capacity + cc.candidate_tokens, cfg.qk_head_dim, device=dev)
         self._logits_buf = None
         self.last_hidden = None
         self.poisoned = False
@@ -415,12 +420,27 @@ class DeepSeekV32Model:
             residual = None
             logits_buf = self._ensure_logits_buf(max(rows[1] - rows[0], 1), start + c1)
             replay = self.replay_layout.begin_chunk() if self.replay_layout is not None else None
+            dense = self.dense_staging is not None and session.pool_session is not None
+            nxt = self._stage_history(session, 0, pos) if dense else None
             for i, (block, state) in enumerate(zip(self.blocks, session.layers)):
                 if replay is not None:
                     with scope("replay_input_copy"):
                         hidden, residual = replay.for_layer(i, hidden, residual)
-                hidden, residual = block.forward(state, hidden, residual, pos, positions, self.freqs,
-                                                 scope=scope, logits_buf=logits_buf, rows=rows)
+                cur = None
+                if dense:
+                    cur = nxt
+                    with scope("dense_history_wait"):
+                        cur.wait_ready()
+                    state.dense = self.dense_staging.buffers[cur.index]
+                    if i + 1 < len(self.blocks):  # next layer's history streams in meanwhile
+                        nxt = self._stage_history(session, i + 1, pos)
+                try:
+                    hidden, residual = block.forward(state, hidden, residual, pos, positions, self.freqs,
+                                                     scope=scope, logits_buf=logits_buf, rows=rows)
+                finally:
+                    if cur is not None:
+                        state.dense = None
+                        cur.release()
             out_h, out_r = hidden, residual
         with scope("final_norm_lm_head"):
             n_last = c1 - c0
@@ -442,6 +462,15 @@ class DeepSeekV32Model:
                     normed = self.comm.gather_rows(local, n_last)
         self.last_hidden = normed if want_hidden else None
         return logits
+
+    def _stage_history(self, session, layer: int, rows: int):
+        """Copy-engine DMA of layer ``layer``'s committed history [0, rows) from pinned host pages."""
+        lease = self.dense_staging.lease()
+        ps = session.pool_session
+        host = self.pool.layers[layer].host
+        runs = list(ps.host_runs(0, rows)) if rows else []
+        return lease.prefetch_runs(host, runs, rows,
+                                   before=lambda: self.pool.wait_host(ps, layer))
 
     def _lm_head(self, last):
         out = torch.empty((last.shape[0], self.lm_head.shape[0]), dtype=torch.float32, device=self.device)

@@ -66,3 +66,18 @@ def test_checkpoint_roundtrip(tmp_path, tiny):
     m2 = DeepSeekV32Model(cfg, src, device="cpu", cache=CacheConfig(capacity=128))
     ids = torch.arange(40) % cfg.vocab_size
     assert torch.equal(m1.prefill(ids).logits, m2.prefill(ids).logits)
+
+
+@pytest.mark.parametrize("method", ["dense_prefetch", "echo"])
+def test_offload_methods_match_resident(tiny, method):
+    """Whole-history staging (dense_prefetch) and predicted prefetch + exact recall (echo)
+    give the resident results bitwise: prefill, a transient candidate batch, a committed extend."""
+    cfg, src = tiny
+    g = torch.Generator().manual_seed(3)
+    hist = torch.randint(0, cfg.vocab_size, (1024,), generator=g)
+    cand = torch.randint(0, cfg.vocab_size, (16,), generator=g)
+    ref = _model(cfg, src, "hbm")
+    off = _model(cfg, src, method, pool_tokens=512 if method == "dense_prefetch" else 256, host_tokens=1024 + 64)
+    assert torch.equal(ref.prefill(hist).logits, off.prefill(hist).logits)
+    assert torch.equal(ref.candidate(cand).logits, off.candidate(cand).logits)
+    assert torch.equal(ref.extend(cand).logits, off.extend(cand).logits)
