@@ -52,13 +52,13 @@ constexpr float kRescaleThreshold = 8.f;  // log2 units
 struct Smem {
   alignas(1024) uint8_t q[kMaxChunks][kQChunkBytes];
   alignas(1024) uint8_t kv[KV_STAGES][kMaxChunks][kKVChunkBytes];
-  alignas(1024) uint8_t p[H * 128];      // P rows padded to 128 B (keys 0-31 used)
+  alignas(1024) uint8_t p[H * 128];      // P rows of 128 B: tile parity 0 in bytes 0-63, parity 1 in 64-127
   alignas(16) float xchg[2][H * kXStride];
   alignas(16) int ids[KV_STAGES][BKV];
   uint64_t q_full;
   uint64_t kv_full[KV_STAGES], kv_empty[KV_STAGES];
   uint64_t s_full[S_BUFS], s_empty[S_BUFS];
-  uint64_t p_full, p_empty, o_full;
+  uint64_t p_full[2], p_empty[2], o_full;
   uint64_t xchg_full[2], xchg_empty[2];
   uint32_t tmem_base;
   int abort_flag;
@@ -106,8 +106,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.xchg_full[i], 1);   // local expect_tx + the peer's st.async bytes
       mbar_init(&s.xchg_empty[i], 4);  // remote arrive per peer softmax warp
     }
-    mbar_init(&s.p_full, 4);
-    mbar_init(&s.p_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.p_full[i], 4);
+      mbar_init(&s.p_empty[i], 1);
+    }
     mbar_init(&s.o_full, 1);
     // Arm the first two exchange phases before the cluster barrier: the peer's
     // st.async bytes may only land on a phase whose expect_tx is posted.
@@ -191,11 +193,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = i % KV_STAGES;
         tc_fence_after();
         const uint64_t vdesc = umma_desc_sw128_mn(smem_u32(s.kv[st]), kKVChunkBytes);
+        const uint64_t pbuf = pdesc + uint64_t((i & 1) * 64 >> 4);  // P parity half of the 128-byte rows
 #pragma unroll
         for (int k = 0; k < ((dbg & 8) ? 1 : BKV / 16); ++k)
-          mma_f16_ss(tmem_o, pdesc + ((k * 32) >> 4), vdesc + ((k * 16 * 128) >> 4), idesc_pv,
+          mma_f16_ss(tmem_o, pbuf + ((k * 32) >> 4), vdesc + ((k * 16 * 128) >> 4), idesc_pv,
                      (i > 0 || k > 0) ? 1u : 0u);
-        mma_commit(&s.p_empty);
+        mma_commit(&s.p_empty[i & 1]);
         mma_commit(&s.kv_empty[st]);
       };
       int nq = 0, np = 0;
@@ -208,7 +211,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           issue_qk(nq++);
           progressed = true;
         }
-        if (np < nq && mbar_test(&s.p_full, np & 1)) {
+        if (np < nq && mbar_test(&s.p_full[np & 1], (np >> 1) & 1)) {
           issue_pv(np++);
           progressed = true;
         }
@@ -329,13 +332,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         pk[j] = pack_bf16(a, c);
       }
       l += psum;
-      if (i > 0) {
-        if (!mbar_wait(&s.p_empty, (i - 1) & 1, err, kErrTimeoutTmemEmpty, abort_flag)) {
+      // P is double-buffered (tile parity), so P(i) only waits for P.V(i-2);
+      // a rescale of O also waits for P.V(i-1) (the last MMA adding into O).
+      if (i >= 2) {
+        if (!mbar_wait(&s.p_empty[i & 1], ((i - 2) >> 1) & 1, err, kErrTimeoutTmemEmpty, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
+      }
+      if (i >= 1) {
         if (__any_sync(0xffffffffu, rescale)) {
+          if (!mbar_wait(&s.p_empty[(i - 1) & 1], ((i - 1) >> 1) & 1, err, kErrTimeoutTmemEmpty, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll 1
           for (int c = 0; c < 8; ++c) {
             uint32_t r[32];
@@ -350,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
-        const uint32_t addr = p_row + ((g ^ (h & 7)) << 4);
+        const uint32_t addr = p_row + (((g + 4 * (i & 1)) ^ (h & 7)) << 4);
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * g]), "r"(pk[4 * g + 1]),
                      "r"(pk[4 * g + 2]), "r"(pk[4 * g + 3])
                      : "memory");
@@ -358,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s.p_full);
+      if (lane == 0) mbar_arrive(&s.p_full[i & 1]);
 #pragma unroll
       for (int j = 0; j < BKV; ++j) cur[j] = nxt[j];
     }

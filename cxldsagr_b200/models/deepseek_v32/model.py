@@ -71,17 +71,21 @@ class MoE:
     (token, k) slot order, so the sum is deterministic.
     """
 
-    def __init__(self, cfg: ModelConfig, w: MoEWeights, comm=None):
+    def __init__(self, cfg: ModelConfig, w: MoEWeights, comm=None, workspace: dict | None = None):
         self.cfg, self.w = cfg, w
         self.comm = comm
         self.shared = DenseMLP(w.shared) if w.shared is not None else None
-        self._layouts: dict = {}
+        # Grouped-layout workspaces, shared by every MoE layer of the model (layers run one
+        # after another) and bucketed by row count (powers of two) so memory stays bounded.
+        self._layouts = workspace if workspace is not None else {}
 
     def _layout(self, rows: int, device):
-        lay = self._layouts.get(rows)
+        bucket = max(128, 1 << max(0, rows - 1).bit_length())
+        key = (bucket, self.w.experts.start, len(self.w.experts))
+        lay = self._layouts.get(key)
         if lay is None:
-            lay = ops.MoELayout(rows, self.w.experts.start, len(self.w.experts), self.cfg.dim, device)
-            self._layouts[rows] = lay
+            lay = ops.MoELayout(bucket, self.w.experts.start, len(self.w.experts), self.cfg.dim, device)
+            self._layouts[key] = lay
         return lay
 
     def _grouped(self, ids, q, s_t, topk: int):
@@ -108,7 +112,7 @@ class MoE:
             with scope("moe_experts"):
                 y, lay = self._grouped(ids, q, s_t, K)
             with scope("moe_combine"):
-                out = ops.moe_combine(y, lay.row_pos, weights, T)
+                out = ops.moe_combine(y, lay.positions, weights, T)
         elif hasattr(self.comm, "ep_ready") and self.comm.ep_ready(cfg.n_routed_experts, cfg.dim, K, total):
             def experts(a, a_s, block_expert, y_out):
                 gu = ops.fp8_gemm_grouped(a, a_s, w.w_gate_up, w.s_gate_up, block_expert)
@@ -128,7 +132,7 @@ class MoE:
                                                                   flat[order])
             with scope("moe_experts"):
                 y, lay = self._grouped(rexp.int(), rrows.contiguous(), rscales.t().contiguous(), 1)
-                y_rows = y[lay.row_pos.long()]
+                y_rows = y[lay.positions.long()]
             with scope("moe_combine"):
                 back = self.comm.combine(y_rows, sc, rc)
                 slots = torch.empty((T * K, cfg.dim), dtype=torch.bfloat16, device=normed.device)
@@ -341,12 +345,13 @@ class DeepSeekV32Model:
             self.attach_pool(self.make_pool(host, P))
         self.blocks: list[Block] = []
         par, comm = self.par, self.comm
+        self._moe_workspace: dict = {}
         for i, layer in enumerate(self.layer_ids):
             attn_w = load_attention(source, cfg, layer, device=dev)
             runner = AttentionRunner(cfg, attn_w, method=cc.method)
             if cfg.is_moe_layer(layer):
                 experts = par.expert_range(cfg.n_routed_experts)
-                mlp = MoE(cfg, load_moe(source, cfg, layer, device=dev, experts=experts), comm)
+                mlp = MoE(cfg, load_moe(source, cfg, layer, device=dev, experts=experts), comm, self._moe_workspace)
             else:
                 mw = load_mlp(source, cfg, f"model.layers.{layer}.mlp", device=dev, shard=(par.rank, par.world))
                 mlp = DenseMLP(mw, comm, sharded=par.world > 1)

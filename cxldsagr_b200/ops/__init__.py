@@ -250,10 +250,19 @@ class MoELayout:
         self.a_s = torch.zeros((K // 128, self.M_pad), dtype=torch.float32, device=device)
 
     def build(self, ids, q, s_t, topk: int):
-        lib().moe_layout(ids.reshape(-1), self.e0, self.n_local, self.max_blocks, self.row_pos, self.block_expert,
+        """Lay out ``ids`` (<= the workspace's row capacity) for the grouped GEMM; ``row_pos`` covers them."""
+        n = ids.numel()
+        if n > self.row_pos.numel():
+            raise ValueError("more routed rows than the layout workspace holds")
+        self.rows = n
+        lib().moe_layout(ids.reshape(-1), self.e0, self.n_local, self.max_blocks, self.row_pos[:n], self.block_expert,
                          self.cursor, self.total)
-        lib().moe_gather(q, s_t, topk, self.row_pos, self.a, self.a_s)
+        lib().moe_gather(q, s_t, topk, self.row_pos[:n], self.a, self.a_s)
         return self
+
+    @property
+    def positions(self):
+        return self.row_pos[: self.rows]
 
 
 def fp8_gemm_grouped(a, a_s, w, w_s, block_expert, out=None):

@@ -1,0 +1,76 @@
+"""CPU tests: provenance, receipts, cache memory audit, serving comparison."""
+
+import json
+
+import pytest
+import torch
+
+from cxldsagr_b200.cache.capacity import CacheFootprint
+from cxldsagr_b200.evaluation import cache_memory_audit as audit
+from cxldsagr_b200.evaluation import provenance, serving_comparison, validation
+
+
+def test_source_snapshot_and_verify():
+    snap = provenance.source_snapshot()
+    assert "bench.py" in snap["files"] and any(p.endswith("gemm_fp8.cuh") for p in snap["files"])
+    assert provenance.verify_source_snapshot(snap) == []
+    fake = {"files": dict(snap["files"])}
+    fake["files"]["bench.py"] = "0" * 64
+    assert "bench.py" in provenance.verify_source_snapshot(fake)
+
+
+def test_numerical_comparison_and_evidence(tmp_path):
+    a = torch.arange(6.0).view(2, 3)
+    r = provenance.numerical_comparison(a + 1e-6, a, atol=1e-5, rtol=0)
+    assert r["ok"] and not r["bitwise"]
+    assert not provenance.numerical_comparison(a, a.t(), atol=1, rtol=1)["ok"]
+    rec = provenance.save_numerical_evidence(tmp_path, name="x", tensors={"logits": a})
+    assert rec["logits"]["shape"] == [2, 3] and (tmp_path / "x.logits.pt").exists()
+
+
+def test_receipts_bind_identity(tmp_path):
+    cfg = {"model": "tiny", "steps": 3}
+    validation.write_receipt(tmp_path / "check.json", "check", cfg)
+    assert validation.require_receipt(tmp_path / "check.json", "check", cfg)["kind"] == "check"
+    with pytest.raises(ValueError):
+        validation.require_receipt(tmp_path / "check.json", "check", {"model": "other"})
+    with pytest.raises(FileExistsError):
+        validation.write_receipt(tmp_path / "check.json", "check", cfg)
+    with pytest.raises(FileNotFoundError):
+        validation.require_receipt(tmp_path / "bench.json", "bench", cfg)
+    assert validation.without_performance({"latency_ms": 1, "hits": 2}) == {"hits": 2}
+
+
+def test_storage_inventory_counts_storages_once():
+    base = torch.zeros(100, dtype=torch.uint8)
+    inv = audit.storage_inventory({"shared_pool.a": base, "shared_pool.alias": base[10:], "session.x": torch.zeros(8)})
+    assert inv["shared_pool"]["dram"] == 100 and inv["session"]["dram"] == 32
+    rep = audit.CacheMemoryAudit({"session": CacheFootprint(0, 16)}).check(inv)
+    assert not rep["ok"] and rep["violations"][0]["category"] == "session"
+
+
+def test_model_cache_inventory_and_audit_cli(tmp_path):
+    from cxldsagr_b200.checkpoint import StateDictSource, random_state_dict
+    from cxldsagr_b200.config import CacheConfig, tiny_config
+    from cxldsagr_b200.models.deepseek_v32.model import DeepSeekV32Model
+
+    cfg = tiny_config()
+    m = DeepSeekV32Model(cfg, StateDictSource(random_state_dict(cfg)), device="cpu",
+                         cache=CacheConfig(method="serial_sparse", capacity=256, pool_tokens=128, host_tokens=256))
+    inv = audit.storage_inventory(audit.model_cache_tensors(m, [m.session]))
+    assert inv["shared_pool"]["dram"] > 0 and inv["session"]["dram"] > 0
+    log = tmp_path / "run.jsonl"
+    rows = [{"status": "started", "scheme": "hbm", "workload_sha256": "w"},
+            {"status": "completed", "metrics": {"request_cache_hbm_bytes": 10, "request_cache_dram_bytes": 5,
+                                                "hbm_budget_bytes": 100, "dram_budget_bytes": 100,
+                                                "latency_ms": 3.0, "is_revisit": False, "prefix_cache_hit": False,
+                                                "evicted_users": []}},
+            {"status": "completed", "metrics": {"request_cache_hbm_bytes": 10, "request_cache_dram_bytes": 5,
+                                                "hbm_budget_bytes": 100, "dram_budget_bytes": 100,
+                                                "latency_ms": 1.0, "is_revisit": True, "prefix_cache_hit": True,
+                                                "evicted_users": [3]}}]
+    log.write_text("\n".join(json.dumps(r) for r in rows))
+    assert audit.main([str(log)]) == 0
+    res = serving_comparison.compare([serving_comparison.collect_run(str(log))] * 2)
+    assert res["same_workload"] and res["runs"][0]["revisit_ms"]["mean"] == 1.0
+    assert "| hbm |" in serving_comparison.markdown(res)

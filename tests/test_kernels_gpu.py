@@ -325,7 +325,7 @@ def test_grouped_moe_matches_reference(T, E, e0, n_local):
     gu = ops.fp8_gemm_grouped(lay.a, lay.a_s, w_gu, s_gu, lay.block_expert)
     _, hq, hs = ops.silu_mul_quant(gu)
     y = ops.fp8_gemm_grouped(hq, hs, w_d, s_d, lay.block_expert)
-    got = ops.moe_combine(y, lay.row_pos, w, T).float().cpu()
+    got = ops.moe_combine(y, lay.positions, w, T).float().cpu()
     ops.check_errors(DEV)
     # reference: only local experts contribute
     want = torch.zeros(T, D)
@@ -339,5 +339,5 @@ def test_grouped_moe_matches_reference(T, E, e0, n_local):
             yk = ref.fp8_linear(h.bfloat16(), wd[e][0].cpu(), wd[e][1].cpu()).float()
             want[t] += float(w[t, k]) * yk[0]
     assert rel_err(got, want) < 3e-2
-    rows = (lay.row_pos >= 0).sum().item()
+    rows = (lay.positions >= 0).sum().item()
     assert rows == int(((ids >= e0) & (ids < e0 + n_local)).sum())
