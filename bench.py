@@ -93,8 +93,10 @@ def main():
     cfg = v32_config(layers=n_layers)
     src = RandomSource(cfg, layers=range(n_layers), seed=0, device=dev)
     offload = args.method != "hbm"
+    # Offload methods: P = NH = H + A and a cold extend (HBM residency of the main KV
+    # dropped after prefill; DRAM copy and resident indexer kept), the reference's setting.
     cache = CacheConfig(method=args.method, capacity=H + A, chunk_size=args.chunk,
-                        pool_tokens=(H + A) // 2 if offload else None, host_tokens=H + A, candidate_tokens=A)
+                        pool_tokens=(H + A) if offload else None, host_tokens=H + A, candidate_tokens=A)
     par = None
     if sp:
         from cxldsagr_b200.parallel.groups import ParallelContext
@@ -120,9 +122,11 @@ def main():
         if events:
             events[0].record(stream)
         model.prefill(hist)
+        if offload:
+            model.clear_residency()
         if events:
             events[1].record(stream)
-        if not args.no_graph and not offload and not sp:
+        if not args.no_graph and args.method != "dense_prefetch" and not sp:
             if graph is None:
                 graph = model.capture_extend(A)
             graph.replay(ext)
@@ -232,9 +236,11 @@ def main():
                 "extend": A,
                 "chunk": args.chunk,
                 "cache_method": args.method,
+                "pool_tokens": (H + A) if offload else None,
+                "extend_residency": "cold (HBM copies of the history dropped before the extend)" if offload else "resident",
                 "parallelism": parallelism,
                 "l2": "no flush: per-step weight stream (3.7 GB) exceeds L2",
-                "extend_graph": not args.no_graph and not offload and not sp,
+                "extend_graph": not args.no_graph and args.method != "dense_prefetch" and not sp,
             },
             "prefill_ms": round(prefill_ms, 3),
             "extend_ms": round(extend_ms, 4),

@@ -280,6 +280,99 @@ void gather_rows(const Tensor& host, Tensor& records, const Tensor& host_ids, co
                            row_bytes, host.size(0), records.size(0), err_ptr(records), stream());
 }
 
+b200::PoolRecallArgs pool_args(const c10::optional<Tensor>& ids, int64_t hist_end, const c10::optional<Tensor>& page_table,
+                               Tensor& h2d, Tensor& d2h, Tensor& priority, Tensor& meta, Tensor& mark,
+                               Tensor& miss_list, Tensor& victims, Tensor& stats) {
+  CHECK_DTYPE(h2d, torch::kInt32); CHECK_DTYPE(d2h, torch::kInt64); CHECK_DTYPE(priority, torch::kInt64);
+  CHECK_DTYPE(meta, torch::kInt64); CHECK_DTYPE(mark, torch::kInt32); CHECK_DTYPE(miss_list, torch::kInt64);
+  CHECK_DTYPE(victims, torch::kInt64); CHECK_DTYPE(stats, torch::kInt64);
+  TORCH_CHECK(d2h.numel() == priority.numel() && miss_list.numel() >= d2h.numel() && victims.numel() >= d2h.numel() &&
+              mark.numel() == h2d.numel() && meta.numel() >= 4 && stats.numel() >= 5, "pool metadata shapes");
+  b200::PoolRecallArgs a;
+  if (ids && ids->defined()) {
+    CHECK_DTYPE((*ids), torch::kInt32);
+    TORCH_CHECK(ids->is_contiguous(), "pool: contiguous ids");
+    a.ids = ids->data_ptr<int>();
+    a.n = int(ids->numel());
+  }
+  if (page_table && page_table->defined()) {
+    CHECK_DTYPE((*page_table), torch::kInt32);
+    a.page_table = page_table->data_ptr<int>();
+    a.npages = int(page_table->numel());
+  }
+  a.hist_end = int(hist_end);
+  a.h2d = h2d.data_ptr<int>();
+  a.d2h = d2h.data_ptr<int64_t>();
+  a.priority = priority.data_ptr<int64_t>();
+  a.P = int(d2h.numel() - 1);
+  a.meta = meta.data_ptr<int64_t>();
+  a.mark = mark.data_ptr<int>();
+  a.host_rows = h2d.numel();
+  a.miss_list = miss_list.data_ptr<int64_t>();
+  a.victims = victims.data_ptr<int64_t>();
+  a.max_miss = int(d2h.numel());
+  a.stats = stats.data_ptr<int64_t>();
+  a.err = err_ptr(h2d);
+  return a;
+}
+
+// begin + classify: dedupe the selection, stamp resident rows, collect misses (all on the device).
+void pool_recall(const Tensor& ids, int64_t hist_end, const Tensor& page_table, Tensor& h2d, Tensor& d2h,
+                 Tensor& priority, Tensor& meta, Tensor& mark, Tensor& miss_list, Tensor& victims, Tensor& stats) {
+  c10::cuda::CUDAGuard g(h2d.device());
+  auto a = pool_args(ids, hist_end, page_table, h2d, d2h, priority, meta, mark, miss_list, victims, stats);
+  b200::launch_pool_recall(a, stream());
+}
+
+// Choose k slots (k_host >= 0, else the device miss count; k_limit caps it), map new_rows (or the misses).
+void pool_select(Tensor& h2d, Tensor& d2h, Tensor& priority, Tensor& meta, Tensor& mark, Tensor& miss_list,
+                 Tensor& victims, Tensor& stats, int64_t k_host, int64_t k_limit, const c10::optional<Tensor>& new_rows,
+                 int64_t count_slot) {
+  c10::cuda::CUDAGuard g(h2d.device());
+  auto a = pool_args(c10::nullopt, 0, c10::nullopt, h2d, d2h, priority, meta, mark, miss_list, victims, stats);
+  const int64_t* rows = nullptr;
+  if (new_rows && new_rows->defined()) {
+    CHECK_DTYPE((*new_rows), torch::kInt64);
+    TORCH_CHECK(new_rows->numel() >= k_host, "pool_select: new_rows shorter than k");
+    rows = new_rows->data_ptr<int64_t>();
+  }
+  TORCH_CHECK(k_host <= a.P, "pool_select: more rows than slots");
+  b200::launch_pool_begin(a.meta, stream());  // a select without classify is its own event
+  b200::launch_pool_select(a, int(k_host), int(k_limit), rows, int(count_slot), stream());
+}
+
+// Continue a pool_recall event: select victims for the device-side misses (no begin).
+void pool_recall_select(Tensor& h2d, Tensor& d2h, Tensor& priority, Tensor& meta, Tensor& mark, Tensor& miss_list,
+                        Tensor& victims, Tensor& stats, int64_t k_limit, int64_t count_slot) {
+  c10::cuda::CUDAGuard g(h2d.device());
+  auto a = pool_args(c10::nullopt, 0, c10::nullopt, h2d, d2h, priority, meta, mark, miss_list, victims, stats);
+  b200::launch_pool_select(a, -1, int(k_limit), nullptr, int(count_slot), stream());
+}
+
+// pred_ids[c] = c for history rows certainly in some row's top-k (caller pre-fills -1).
+void echo_predict(const Tensor& logits, int64_t rows, int64_t hist_end, const Tensor& offset, int64_t k, Tensor& pred_ids) {
+  c10::cuda::CUDAGuard g(logits.device());
+  CHECK_DTYPE(logits, torch::kFloat32); CHECK_DTYPE(offset, torch::kFloat32); CHECK_DTYPE(pred_ids, torch::kInt32);
+  TORCH_CHECK(logits.stride(1) == 1 && pred_ids.numel() >= hist_end && logits.size(1) >= hist_end, "echo_predict shapes");
+  b200::launch_echo_predict(logits.data_ptr<float>(), logits.stride(0), int(rows), int(hist_end), offset.data_ptr<float>(),
+                            int(k), pred_ids.data_ptr<int>(), stream());
+}
+
+void pool_map(const Tensor& ids, int64_t hist_end, int64_t tail, int64_t committed_end, const Tensor& page_table,
+              const Tensor& h2d, Tensor& out) {
+  c10::cuda::CUDAGuard g(h2d.device());
+  CHECK_DTYPE(ids, torch::kInt32); CHECK_DTYPE(out, torch::kInt32); CHECK_DTYPE(page_table, torch::kInt32);
+  CHECK_DTYPE(h2d, torch::kInt32);
+  b200::PoolRecallArgs a;
+  a.ids = ids.data_ptr<int>();
+  a.n = int(ids.numel());
+  a.hist_end = int(hist_end);
+  a.page_table = page_table.data_ptr<int>();
+  a.npages = int(page_table.numel());
+  a.h2d = const_cast<int*>(h2d.data_ptr<int>());
+  b200::launch_pool_map(a, int(tail), int(committed_end), out.data_ptr<int>(), stream());
+}
+
 // `call` numbers this op's calls from 1 (parity = call & 1); targets are the cumulative flag counts.
 void moe_route(const Tensor& logits, bool split, const Tensor& bias, int64_t E, int64_t n_group, int64_t topk_group,
                int64_t K, bool normalize, double scaling, Tensor& ids, Tensor& weights) {
@@ -487,6 +580,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sparse_mla_scratch_bytes", &sparse_mla_scratch_bytes);
   m.def("fp8_gemm_splits", &fp8_gemm_splits);
   m.def("gather_rows", &gather_rows);
+  m.def("pool_recall", &pool_recall);
+  m.def("pool_select", &pool_select);
+  m.def("pool_recall_select", &pool_recall_select);
+  m.def("pool_map", &pool_map);
+  m.def("echo_predict", &echo_predict);
   m.def("fp8_gemm_ag", &fp8_gemm_ag);
   m.def("fp8_gemm_rs", &fp8_gemm_rs);
   m.def("p2p_barrier", &p2p_barrier);

@@ -67,6 +67,33 @@ void launch_ep_dispatch(const EpArgs& p, const int* ids, const uint8_t* q, const
                         int* pos_out, int* block_expert, int max_blocks, int* err, cudaStream_t stream);
 void launch_ep_combine(const EpArgs& p, const int* ids, const int* pos, const float* w, __nv_bfloat16* out, int* err,
                        cudaStream_t stream);
+// Shared sparse-token pool metadata on the device (csrc/kernels/pool_meta.cu).
+struct PoolRecallArgs {
+  const int* ids = nullptr;      // selected logical rows (-1 = padding)
+  int n = 0;
+  int hist_end = 0;              // logical rows below this are history (pool slots); above: transient tail
+  const int* page_table = nullptr;
+  int npages = 0;
+  int* h2d = nullptr;            // [host_rows] int32
+  int64_t* d2h = nullptr;        // [P+1]
+  int64_t* priority = nullptr;   // [P+1]
+  int P = 0;                     // slots (excluding the sentinel)
+  int64_t* meta = nullptr;       // [8]: clock, epoch, miss count, overflow
+  int* mark = nullptr;           // [host_rows] epoch marks
+  int64_t host_rows = 0;
+  int64_t* miss_list = nullptr;  // [P+1]
+  int64_t* victims = nullptr;    // [P+1]
+  int max_miss = 0;
+  int64_t* stats = nullptr;      // per-cache device counters
+  int* err = nullptr;
+};
+void launch_pool_begin(int64_t* meta, cudaStream_t stream);
+void launch_echo_predict(const float* logits, int64_t ld, int rows, int hist_end, const float* offset, int k,
+                         int* pred_ids, cudaStream_t stream);
+void launch_pool_recall(const PoolRecallArgs& a, cudaStream_t stream);
+void launch_pool_select(const PoolRecallArgs& a, int k_host, int k_limit, const int64_t* new_rows, int count_slot,
+                        cudaStream_t stream);
+void launch_pool_map(const PoolRecallArgs& a, int tail, int committed_end, int* out, cudaStream_t stream);
 // Symmetric heap: cudaMalloc'd, zeroed, exported / opened through CUDA IPC.
 uintptr_t symm_alloc(size_t bytes);
 void symm_free(uintptr_t p);

@@ -31,6 +31,14 @@ class IndexerCache:
             raise ValueError("indexer rows exceed the session capacity")
         return self.keys[start:start + count], self.scales[start:start + count]
 
+    def pred_ids(self, end: int) -> torch.Tensor:
+        """Scratch list [end] of predicted history rows, reset to -1 (no host sync)."""
+        if getattr(self, "_pred", None) is None or self._pred.numel() < end:
+            self._pred = torch.empty(self.capacity, dtype=torch.int32, device=self.keys.device)
+        view = self._pred[:end]
+        view.fill_(-1)
+        return view
+
     def visible(self, end: int):
         return self.keys[:end], self.scales[:end]
 

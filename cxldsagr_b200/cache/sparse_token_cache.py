@@ -43,13 +43,17 @@ class CacheStats:
     device_to_host_bytes: int = 0
 
 
+# Device counters of a cache (accumulated by the pool kernels / tensor ops, no host sync):
+_SELECTED, _RESIDENT, _EVICTED, _RECALLED, _PREFETCHED = 0, 1, 2, 3, 5
+
+
 class SparseTokenCache:
     def __init__(self, capacity: int, width: int, *, device="cuda", dtype=torch.bfloat16,
                  slots: int | None = None, candidate_slots: int = 0):
         """Standalone cache: resident (``slots`` None) or a private pool of ``slots`` rows."""
         if capacity < 1 or width < 1:
             raise ValueError("capacity and width must be positive")
-        self.stats = CacheStats()
+        self._init_stats(device)
         if slots is not None:
             host = ((capacity + PAGE_SIZE - 1) // PAGE_SIZE) * PAGE_SIZE
             pool = SharedSparseTokenPool(host, width, 1, slots, device=device, dtype=dtype,
@@ -74,9 +78,29 @@ class SparseTokenCache:
     @classmethod
     def shared(cls, session: SparseTokenSession, layer: int) -> "SparseTokenCache":
         self = object.__new__(cls)
-        self.stats = CacheStats()
+        self._init_stats(session.pool.device)
         self._bind(session, layer)
         return self
+
+    def _init_stats(self, device):
+        self._stats = CacheStats()
+        self._dev = torch.zeros(8, dtype=torch.int64, device=_device(device))
+        self._scratch = torch.zeros(8, dtype=torch.int64, device=_device(device))
+
+    @property
+    def stats(self) -> CacheStats:
+        """Counters (device-counted fields are read back here, which synchronises)."""
+        d = self._dev.tolist()
+        st = self._stats
+        st.selection_records, st.resident_selection_records = d[_SELECTED], d[_RESIDENT]
+        st.evicted_records, st.recalled_records, st.prefetched_records = d[_EVICTED], d[_RECALLED], d[_PREFETCHED]
+        st.host_to_device_bytes = (d[_RECALLED] + d[_PREFETCHED]) * self.record_bytes
+        return st
+
+    @property
+    def native(self) -> bool:
+        """Pool metadata handled by the device kernels (CUDA pools)."""
+        return self._pool is not None and self.device.type == "cuda"
 
     def _bind(self, session, layer):
         pool = session.pool
@@ -187,7 +211,8 @@ class SparseTokenCache:
         if self._step_end is not None:
             self.rollback()
         self.truncate(0)
-        self.stats = CacheStats()
+        self._stats = CacheStats()
+        self._dev.zero_()
 
     # ----------------------------------------------------------------- append
     def destination_rows(self, count: int) -> torch.Tensor:
@@ -209,9 +234,15 @@ class SparseTokenCache:
             raise WorkingSetTooLarge("new KV batch exceeds the shared pool")
         with self.operation():
             glob = self.logical_to_global(torch.arange(start, start + count, device=self.device))
-            chosen = self._pool.available_slots(self.layer_id, glob, count)
-            self.stats.evicted_records += self._pool.evict(self.layer_id, chosen)
             pool = self._pool.layers[self.layer_id]
+            if self.native:
+                from .. import ops
+
+                ops.lib().pool_select(pool.h2d, pool.d2h, pool.priority, pool.meta, pool.mark, pool.miss_list,
+                                      pool.victims, self._dev, count, -1, glob, -1)
+                return pool.victims[:count].clone()
+            chosen = self._pool.available_slots(self.layer_id, glob, count)
+            self._dev[_EVICTED] += self._pool.evict(self.layer_id, chosen)
             pool.h2d[glob] = chosen.int()
             pool.d2h[chosen] = glob
             self._pool.stamp(self.layer_id, chosen)
@@ -222,11 +253,11 @@ class SparseTokenCache:
         start, count = self.written, rows.numel()
         if self._pool is not None and self.transient_start is None:
             self._pool.write_host(self.session, self.layer_id, start, self.records[rows])
-            self.stats.device_to_host_bytes += count * self.record_bytes
+            self._stats.device_to_host_bytes += count * self.record_bytes
         if self.transient_start is not None:
-            self.stats.transient_written_records += count
+            self._stats.transient_written_records += count
         self.written = start + count
-        self.stats.written_records += count
+        self._stats.written_records += count
         return start
 
     def append(self, records: torch.Tensor) -> int:
@@ -247,6 +278,8 @@ class SparseTokenCache:
         self._check()
         if self._pool is None:
             return torch.where((indices >= 0) & (indices < self.written), indices, -1).int()
+        if self.native:
+            return self._ensure_native(indices)
         flat = indices.reshape(-1).long()
         uniq = torch.unique(flat[flat >= 0])
         if uniq.numel() and int(uniq[-1]) >= self.written:
@@ -254,25 +287,24 @@ class SparseTokenCache:
         history = uniq if self.transient_start is None else uniq[uniq < self.transient_start]
         if history.numel() > self.slots:
             raise WorkingSetTooLarge(f"{history.numel()} selected records exceed {self.slots} slots")
-        self.stats.max_working_set = max(self.stats.max_working_set, int(uniq.numel()))
+        self._stats.max_working_set = max(self._stats.max_working_set, int(uniq.numel()))
         pool = self._pool.layers[self.layer_id]
         with self.operation():
             glob = self.logical_to_global(history)
             mapped = pool.h2d[glob]
             missing = glob[mapped == MISSING]
-            self.stats.selection_records += int(uniq.numel())
-            self.stats.resident_selection_records += int(uniq.numel() - missing.numel())
+            self._dev[_SELECTED] += int(uniq.numel())
+            self._dev[_RESIDENT] += int(uniq.numel() - missing.numel())
             if missing.numel():
                 self._pool.wait_host(self.session, self.layer_id)
                 chosen = self._pool.available_slots(self.layer_id, glob, missing.numel())
-                self.stats.evicted_records += self._pool.evict(self.layer_id, chosen)
+                self._dev[_EVICTED] += self._pool.evict(self.layer_id, chosen)
                 from .. import ops
 
                 ops.gather_host_records(pool.host, pool.records, missing, chosen)
                 pool.h2d[missing] = chosen.int()
                 pool.d2h[chosen] = missing
-                self.stats.recalled_records += int(missing.numel())
-                self.stats.host_to_device_bytes += int(missing.numel()) * self.record_bytes
+                self._dev[_RECALLED] += int(missing.numel())
             # One protection event for the whole selection (hits and recalls).
             self._pool.stamp(self.layer_id, pool.h2d[glob].long())
             if self.transient_start is None:
@@ -292,6 +324,8 @@ class SparseTokenCache:
         """
         if self._pool is None or not logical.numel():
             return 0
+        if self.native:
+            return self._prefetch_native(logical, limit)
         logical = torch.unique(logical.long())
         logical = logical[(logical >= 0) & (logical < self.length)]
         if limit is not None:
@@ -306,7 +340,7 @@ class SparseTokenCache:
                 missing = missing[: self.slots]
             self._pool.wait_host(self.session, self.layer_id)
             chosen = self._pool.available_slots(self.layer_id, glob, missing.numel())
-            self.stats.evicted_records += self._pool.evict(self.layer_id, chosen)
+            self._dev[_EVICTED] += self._pool.evict(self.layer_id, chosen)
             from .. import ops
 
             ops.gather_host_records(pool.host, pool.records, missing, chosen)
@@ -314,9 +348,48 @@ class SparseTokenCache:
             pool.d2h[chosen] = missing
             self._pool.stamp(self.layer_id, chosen)
             n = int(missing.numel())
-            self.stats.prefetched_records += n
-            self.stats.host_to_device_bytes += n * self.record_bytes
+            self._dev[_PREFETCHED] += n
             return n
+
+    # ---------------------------------------------------------- native paths
+    def _recall_native(self, ids32: torch.Tensor, hist_end: int, *, k_limit: int, count_slot: int, stats):
+        """One device-side event: classify ``ids32`` (stamp hits, list misses), choose
+        slots for the misses, copy their host rows in.  No host synchronisation."""
+        from .. import ops
+
+        pool = self._pool.layers[self.layer_id]
+        lib = ops.lib()
+        lib.pool_recall(ids32, hist_end, self.session.page_table, pool.h2d, pool.d2h, pool.priority, pool.meta,
+                        pool.mark, pool.miss_list, pool.victims, stats)
+        self._pool.wait_host(self.session, self.layer_id)   # host rows written by earlier appends are complete
+        lib.pool_recall_select(pool.h2d, pool.d2h, pool.priority, pool.meta, pool.mark, pool.miss_list,
+                               pool.victims, self._dev if stats is self._scratch else stats, k_limit, count_slot)
+        # meta[2] now holds the rows placed; its low 32 bits are the gather's device-side count.
+        count = pool.meta.view(torch.int32)[4:5]
+        ops.gather_host_records(pool.host, pool.records, pool.miss_list, pool.victims, device_count=count)
+        return pool
+
+    def _ensure_native(self, indices: torch.Tensor) -> torch.Tensor:
+        from .. import ops
+
+        ids = indices.reshape(-1)
+        ids32 = ids if ids.dtype == torch.int32 and ids.is_contiguous() else ids.to(torch.int32).contiguous()
+        hist_end = self.transient_start if self.transient_start is not None else self.written
+        with self.operation():
+            pool = self._recall_native(ids32, hist_end, k_limit=-1, count_slot=_RECALLED, stats=self._dev)
+            out = torch.empty_like(ids32)
+            ops.lib().pool_map(ids32, hist_end, self.slots + 1, self.written, self.session.page_table, pool.h2d, out)
+            # The union can only exceed the pool when the selection is larger than it.
+            if min(ids32.numel(), hist_end) > self.slots and int(pool.meta[3]):
+                raise WorkingSetTooLarge("selected records exceed the device working set")
+        return out.view(indices.shape)
+
+    def _prefetch_native(self, logical: torch.Tensor, limit: int | None) -> int:
+        ids32 = logical.to(torch.int32).contiguous()
+        with self.operation():
+            self._recall_native(ids32, self.length, k_limit=-1 if limit is None else int(limit),
+                                count_slot=_PREFETCHED, stats=self._scratch)
+        return -1   # placed on the device; the count is in the prefetched counter
 
     # ---------------------------------------------------------- diagnostics
     def metrics(self) -> dict:

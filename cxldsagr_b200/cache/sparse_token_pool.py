@@ -48,8 +48,19 @@ class LayerPool:
     h2d: torch.Tensor
     d2h: torch.Tensor
     priority: torch.Tensor
-    clock: int = 0
+    # Device-resident metadata of the native (no host sync) path:
+    # meta = [clock, epoch, miss count, overflow, ...]; mark [NH] epoch marks;
+    # miss_list / victims [P+1] scratch of one event.
+    meta: torch.Tensor = None
+    mark: torch.Tensor = None
+    miss_list: torch.Tensor = None
+    victims: torch.Tensor = None
     lease_owner: int | None = None
+
+    @property
+    def clock(self):
+        """The clock as a 0-d tensor (device-resident; reading it as an int synchronises)."""
+        return self.meta[0]
 
 
 @dataclass
@@ -93,7 +104,7 @@ class SharedSparseTokenPool:
         host = host_capacity * width * size
         if torch.device(device).type == "cuda":
             host = pinned_allocation_bytes(host)
-        per_layer = (slots + 1 + candidate_slots) * width * size + host_capacity * 4 + (slots + 1) * 16
+        per_layer = ((slots + 1 + candidate_slots) * width * size + host_capacity * 8 + (slots + 1) * 32 + 64)
         hbm = layers * per_layer
         if torch.device(device).type == "cpu":
             return {"hbm": 0, "dram": hbm + layers * host}
@@ -118,6 +129,10 @@ class SharedSparseTokenPool:
                 h2d=torch.full((host_capacity,), MISSING, dtype=torch.int32, device=self.device),
                 d2h=torch.full((slots + 1,), MISSING, dtype=torch.int64, device=self.device),
                 priority=priority,
+                meta=torch.zeros(8, dtype=torch.int64, device=self.device),
+                mark=torch.zeros(host_capacity, dtype=torch.int32, device=self.device),
+                miss_list=torch.zeros(slots + 1, dtype=torch.int64, device=self.device),
+                victims=torch.zeros(slots + 1, dtype=torch.int64, device=self.device),
             ))
         self._free_pages = list(range(host_capacity // PAGE_SIZE - 1, -1, -1))
         self._sessions: dict[int, SparseTokenSession] = {}
@@ -126,6 +141,7 @@ class SharedSparseTokenPool:
         self._active: tuple[int, int] | None = None
         self._transient_owner: dict[int, int] = {}
         self._writes: deque[_HostWrite] = deque()
+        self._captured: list[_HostWrite] = []
         self._copy_stream = torch.cuda.Stream(device=self.device) if pin else None
         self._last_stream = None
         self.closed = False
@@ -139,7 +155,8 @@ class SharedSparseTokenPool:
     def shared_bytes(self) -> dict:
         ts = []
         for layer in self.layers:
-            ts += [layer.host, layer.records, layer.h2d, layer.d2h, layer.priority]
+            ts += [layer.host, layer.records, layer.h2d, layer.d2h, layer.priority, layer.meta, layer.mark,
+                   layer.miss_list, layer.victims]
         return tensor_bytes(ts)
 
     def _check(self):
@@ -231,7 +248,9 @@ class SharedSparseTokenPool:
             for lo, n, hstart in session.host_runs(start, len(source)):
                 host[hstart:hstart + n].copy_(source[lo:lo + n])
             return
-        self._reap(make_room=True)
+        capturing = torch.cuda.is_current_stream_capturing()
+        if not capturing:
+            self._reap(make_room=True)
         stream = torch.cuda.current_stream(self.device)
         self._copy_stream.wait_stream(stream)
         with torch.cuda.stream(self._copy_stream):
@@ -239,17 +258,37 @@ class SharedSparseTokenPool:
                 host[hstart:hstart + n].copy_(source[lo:lo + n], non_blocking=True)
             event = torch.cuda.Event()
             event.record(self._copy_stream)
+        if capturing:
+            # Inside a CUDA graph the copy is a graph node; the graph joins it back
+            # (join_writes) and the source lives in the graph's private pool.
+            self._captured.append(_HostWrite(session.owner, layer, event, source))
+            return
         source.record_stream(self._copy_stream)
         self._writes.append(_HostWrite(session.owner, layer, event, source))
 
+    def join_writes(self):
+        """Make the current stream wait for every host write issued so far (no host sync)."""
+        if self.device.type == "cuda":
+            torch.cuda.current_stream(self.device).wait_stream(self._copy_stream)
+
+    def end_capture(self):
+        """Forget the host-write tickets recorded inside a graph capture."""
+        self._captured.clear()
+
     def wait_host(self, session, layer: int):
         """Make the current stream wait for this (session, layer)'s pending host writes."""
-        self._reap()
-        if self.device.type == "cuda":
-            stream = torch.cuda.current_stream(self.device)
-            for t in self._writes:
+        if self.device.type != "cuda":
+            return
+        stream = torch.cuda.current_stream(self.device)
+        if torch.cuda.is_current_stream_capturing():
+            for t in self._captured:
                 if t.owner == session.owner and t.layer == layer:
                     stream.wait_event(t.event)
+            return
+        self._reap()
+        for t in self._writes:
+            if t.owner == session.owner and t.layer == layer:
+                stream.wait_event(t.event)
 
     def drain(self):
         try:
@@ -269,8 +308,8 @@ class SharedSparseTokenPool:
         """One FIFO event: stamp ``physical`` slots with the current clock value."""
         pool = self.layers[layer]
         if physical.numel():
-            pool.priority[physical.long()] = pool.clock
-        pool.clock += 1
+            pool.priority[physical.long()] = pool.meta[0]
+        pool.meta[0] += 1
         pool.priority[0] = MISSING
 
     def release_ids(self, layer: int, global_ids: torch.Tensor):
@@ -320,7 +359,7 @@ class SharedSparseTokenPool:
         self.drain()
         layers = [
             {"records": l.records.clone(), "h2d": l.h2d.clone(), "d2h": l.d2h.clone(),
-             "priority": l.priority.clone(), "clock": l.clock}
+             "priority": l.priority.clone(), "meta": l.meta.clone()}
             for l in self.layers
         ]
         sessions = {o: [s.layer(i)._state() for i in range(self.num_layers)] for o, s in self._sessions.items()}
@@ -334,9 +373,8 @@ class SharedSparseTokenPool:
             raise ValueError(snap.reason)
         self.drain()
         for layer, state in zip(self.layers, snap.layers):
-            for name in ("records", "h2d", "d2h", "priority"):
+            for name in ("records", "h2d", "d2h", "priority", "meta"):
                 getattr(layer, name).copy_(state[name])
-            layer.clock = state["clock"]
         for owner, states in snap.sessions.items():
             for i, st in enumerate(states):
                 self._sessions[owner].layer(i)._restore(st)

@@ -193,6 +193,15 @@ class AttentionRunner:
         hist_end = min(pos, cache.length)
         if hist_end <= k:
             return
+        budget = min(8192, cache.slots - logits.shape[0])
+        if budget <= 0:
+            return
+        if logits.is_cuda and getattr(cache, "native", False):
+            # Device predictor + device recall: no host synchronisation.
+            pred = state.index.pred_ids(hist_end)
+            ops.lib().echo_predict(logits, logits.shape[0], hist_end, state.index.offset, k, pred)
+            cache.prefetch(pred, limit=budget)
+            return
         rows = logits[:, :hist_end] - state.index.offset[0]
         key = _order_bins(rows)
         counts = torch.zeros((rows.shape[0], 257), dtype=torch.int64, device=rows.device)
@@ -200,9 +209,8 @@ class AttentionRunner:
         above = counts.flip(1).cumsum(1).flip(1)  # elements in bins >= b
         thr = (above[:, 1:] > k).sum(1)            # first bin with <= k elements above it
         pred = key > thr[:, None]
-        budget = min(8192, cache.slots - logits.shape[0])
         cand = torch.nonzero(pred.any(0)).flatten()
-        if budget > 0 and cand.numel():
+        if cand.numel():
             cache.prefetch(cand, limit=budget)
 
     def _update_hints(self, state, logits, values, pos, end):

@@ -541,6 +541,17 @@ class DeepSeekV32Model:
     def truncate(self, length: int, *, session: ModelSession | None = None):
         (session or self.session).truncate(length)
 
+    def clear_residency(self, *, session: ModelSession | None = None):
+        """Drop the HBM copies of a session's offloaded history (host copies and indexer keys stay):
+        the next steps recall every selected row from DRAM."""
+        session = session or self.session
+        if session.pool_session is None or self.pool is None:
+            return
+        self.pool.drain()
+        ids = session.pool_session.global_ids()
+        for i in range(len(self.layer_ids)):
+            self.pool.release_ids(i, ids)
+
     def reset(self, *, session: ModelSession | None = None):
         (session or self.session).reset()
 
@@ -551,16 +562,21 @@ class DeepSeekV32Model:
 
 
 class ExtendGraph:
-    """One CUDA graph for a whole T-token extend step of the resident (hbm) method.
+    """One CUDA graph for a whole T-token extend step.
 
     Each replay re-opens the cache step on the host (cheap bookkeeping), copies
     the token ids into the static input and launches the graph; the caller
-    commits with :meth:`commit` or discards with :meth:`rollback`.
+    commits with :meth:`commit` or discards with :meth:`rollback`.  Offload
+    methods (serial_sparse, echo) are captured too: their pool metadata,
+    predictor, recall and host write-back run on the device with no host
+    decision inside the step, so every replay acts on the pool state of its
+    own time.  (dense_prefetch stages through a second stream with host-side
+    lease state and is not captured.)
     """
 
     def __init__(self, model: DeepSeekV32Model, T: int, *, warmup: int = 2, session: ModelSession | None = None):
-        if model.cache_cfg.offload:
-            raise ValueError("graph capture covers the resident (hbm) cache method")
+        if model.cache_cfg.method == "dense_prefetch":
+            raise ValueError("the dense_prefetch method runs its extend eagerly")
         self.model, self.T = model, T
         self.session = session or model.session
         self.start = self.session.length
@@ -574,6 +590,9 @@ class ExtendGraph:
                 model.forward(self.static_ids, session=self.session, commit=False)
                 self._rewind()
         torch.cuda.current_stream(dev).wait_stream(stream)
+        pool = model.pool if self.session.pool_session is not None else None
+        if pool is not None:
+            pool.drain()   # no host-write ticket from before the capture is waited on inside it
         self.graph = torch.cuda.CUDAGraph()
         for c in self.session.caches:
             c.begin_step(T)
@@ -582,6 +601,10 @@ class ExtendGraph:
         n0 = launch_count()
         with torch.cuda.graph(self.graph, stream=stream):
             self.static_logits = model._body(self.session, self.static_ids, self.start, T)
+            if pool is not None:
+                pool.join_writes()
+        if pool is not None:
+            pool.end_capture()
         self.launches_per_replay = launch_count() - n0
         model._graph_launches = self.launches_per_replay
         self._rewind()
@@ -589,6 +612,11 @@ class ExtendGraph:
     def _rewind(self):
         for c in self.session.caches:
             c._step_end = None
+            if c.offload and max(c.written, c.length) > self.start:
+                # Unmap the step's rows from the pool (their slots become free).
+                top = max(c.written, c.length)
+                ids = c.logical_to_global(torch.arange(self.start, top, device=c.device))
+                c._pool.release_ids(c.layer_id, ids)
             c.written = c.length = self.start
         self.session.length = self.start
 

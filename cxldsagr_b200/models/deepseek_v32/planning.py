@@ -82,7 +82,7 @@ def shared_pool_bytes(config: ServingResourceConfig, host_tokens: int, candidate
     """Bytes of the per-layer shared pool (exactly the tensors SharedSparseTokenPool allocates)."""
     L, P, w = config.num_layers, config.slots, config.width
     rows = (P + 1 + candidate) * w * 2
-    maps = host_tokens * 4 + (P + 1) * 8 * 2
+    maps = host_tokens * 8 + (P + 1) * 8 * 4 + 64   # h2d + marks, d2h + priority + miss list + victims, meta
     host = pinned_allocation_bytes(host_tokens * w * 2) if config.on_gpu else host_tokens * w * 2
     if config.on_gpu:
         return CacheFootprint(L * (rows + maps), L * host)

@@ -341,3 +341,68 @@ def test_grouped_moe_matches_reference(T, E, e0, n_local):
     assert rel_err(got, want) < 3e-2
     rows = (lay.positions >= 0).sum().item()
     assert rows == int(((ids >= e0) & (ids < e0 + n_local)).sum())
+
+
+# ------------------------------------------------------- pool metadata (native)
+@pytest.mark.parametrize("slots", [96, 256])
+def test_native_pool_recall_matches_resident(slots):
+    """Appends, exact recall and transient tails through the device-side pool
+    metadata give the resident rows bit for bit, including under eviction."""
+    from cxldsagr_b200.cache.sparse_token_cache import SparseTokenCache
+
+    torch.manual_seed(21)
+    width, cap, cand = 576, 640, 32
+    res = SparseTokenCache(cap + cand, width, device=DEV, candidate_slots=cand)
+    off = SparseTokenCache(cap + cand, width, device=DEV, slots=slots, candidate_slots=cand)
+    assert off.native
+    for step in range(10):
+        n = 64
+        recs = torch.randn(n, width, device=DEV).bfloat16()
+        for c in (res, off):
+            c.begin_step(n)
+            c.append(recs)
+            c.commit()
+        hist = res.length
+        q = 8 if slots >= 96 else 1
+        ids = torch.randint(-1, hist, (q, 12), device=DEV, dtype=torch.int32)
+        phys_r = res.ensure(ids)
+        phys_o = off.ensure(ids)
+        valid = ids >= 0
+        assert torch.equal(res.records[phys_r[valid].long()], off.records[phys_o[valid].long()])
+        assert bool((phys_o[~valid] == -1).all())
+    # transient candidate tail
+    crec = torch.randn(cand, width, device=DEV).bfloat16()
+    for c in (res, off):
+        c.begin_transient(cand)
+        c.append(crec)
+    ids = torch.cat([torch.randint(0, res.length, (4, 8), device=DEV),
+                     res.length + torch.randint(0, cand, (4, 4), device=DEV)], 1).int()
+    a, b = res.ensure(ids), off.ensure(ids)
+    assert torch.equal(res.records[a.long()], off.records[b.long()])
+    for c in (res, off):
+        c.discard_transient()
+    ops.check_errors(DEV)
+    st = off.stats
+    assert st.recalled_records > 0 and st.evicted_records > 0 and st.selection_records > 0
+
+
+@pytest.mark.parametrize("rows,hist,k", [(1, 5000, 2048), (16, 3000, 64), (4, 70000, 2048)])
+def test_echo_predictor_matches_reference(rows, hist, k):
+    """Device ECHO predictor = the histogram-threshold rule of the Python predictor."""
+    from cxldsagr_b200.models.deepseek_v32.attention import _order_bins
+
+    torch.manual_seed(23)
+    logits = torch.randn(rows, hist + 7, device=DEV) * 3
+    logits[:, 5] = -torch.inf
+    offset = torch.tensor([0.25] + [0.0] * 15, device=DEV)
+    pred = torch.full((hist,), -1, dtype=torch.int32, device=DEV)
+    ops.lib().echo_predict(logits, rows, hist, offset, k, pred)
+    key = _order_bins(logits[:, :hist] - offset[0])
+    counts = torch.zeros((rows, 257), dtype=torch.int64, device=DEV)
+    counts.scatter_add_(1, key.long(), torch.ones_like(key, dtype=torch.int64))
+    above = counts.flip(1).cumsum(1).flip(1)
+    thr = (above[:, 1:] > k).sum(1)
+    want = torch.nonzero((key > thr[:, None]).any(0)).flatten()
+    got = torch.nonzero(pred >= 0).flatten()
+    assert torch.equal(got, want)
+    assert bool((pred[got] == got.int()).all())
