@@ -91,6 +91,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ntiles = k_end > k_begin ? (k_end - k_begin + BKV - 1) / BKV : 0;
   const int* row_ids = ids + int64_t(t) * K;
   const bool exchange = !(dbg & 2);
+  // P (softmax probabilities, bf16) goes to TMEM columns 384.. (double-buffered by
+  // tile parity) and feeds P.V as the TMEM A operand; dbg bit 32 selects the
+  // shared-memory P path instead.
+  const bool p_tmem = !(dbg & 32);
 
   if (threadIdx.x == 0) {
     mbar_init(&s.q_full, 1);
@@ -130,6 +134,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
   const uint32_t tmem_o = tmem + 128;  // S buffers at columns 0, 32, 64
+  const uint32_t tmem_p = tmem + 384;  // P: two 16-column (32 keys of bf16 pairs) buffers
   volatile int* abort_flag = &s.abort_flag;
 
   if (warp == 4) {
@@ -194,10 +199,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint64_t vdesc = umma_desc_sw128_mn(smem_u32(s.kv[st]), kKVChunkBytes);
         const uint64_t pbuf = pdesc + uint64_t((i & 1) * 64 >> 4);  // P parity half of the 128-byte rows
+        const uint32_t ptm = tmem_p + uint32_t((i & 1) * (BKV / 2));
 #pragma unroll
-        for (int k = 0; k < ((dbg & 8) ? 1 : BKV / 16); ++k)
-          mma_f16_ss(tmem_o, pbuf + ((k * 32) >> 4), vdesc + ((k * 16 * 128) >> 4), idesc_pv,
-                     (i > 0 || k > 0) ? 1u : 0u);
+        for (int k = 0; k < ((dbg & 8) ? 1 : BKV / 16); ++k) {
+          if (p_tmem)
+            mma_f16_ts(tmem_o, ptm + k * 8, vdesc + ((k * 16 * 128) >> 4), idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
+          else
+            mma_f16_ss(tmem_o, pbuf + ((k * 32) >> 4), vdesc + ((k * 16 * 128) >> 4), idesc_pv,
+                       (i > 0 || k > 0) ? 1u : 0u);
+        }
         mma_commit(&s.p_empty[i & 1]);
         mma_commit(&s.kv_empty[st]);
       };
@@ -360,14 +370,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_st();
         }
       }
+      if (p_tmem) {
+        tmem_st16(tmem_p + lane_addr + uint32_t((i & 1) * (BKV / 2)), pk);
+        tmem_wait_st();
+      } else {
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const uint32_t addr = p_row + (((g + 4 * (i & 1)) ^ (h & 7)) << 4);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * g]), "r"(pk[4 * g + 1]),
-                     "r"(pk[4 * g + 2]), "r"(pk[4 * g + 3])
-                     : "memory");
+        for (int g = 0; g < 4; ++g) {
+          const uint32_t addr = p_row + (((g + 4 * (i & 1)) ^ (h & 7)) << 4);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * g]), "r"(pk[4 * g + 1]),
+                       "r"(pk[4 * g + 2]), "r"(pk[4 * g + 3])
+                       : "memory");
+        }
+        fence_proxy_async();
       }
-      fence_proxy_async();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.p_full[i & 1]);
