@@ -258,6 +258,12 @@ void sparse_mla(const Tensor& q, const Tensor& kv, const Tensor& ids, double sca
   else b200::launch_sparse_mla_split(a, int(splits), sp, stream());
 }
 
+Tensor sparse_mla_trace() {
+  Tensor t = torch::empty({4, 65, 16}, torch::kInt64);
+  b200::copy_sparse_mla_trace(reinterpret_cast<unsigned long long*>(t.data_ptr<int64_t>()));
+  return t;
+}
+
 int64_t fp8_gemm_splits(int64_t M, int64_t N, int64_t K) {
   return b200::plan_fp8_gemm(int(M), int(N), int(K), 8).splits;
 }
@@ -578,6 +584,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("topk", &topk);
   m.def("sparse_mla", &sparse_mla);
   m.def("sparse_mla_scratch_bytes", &sparse_mla_scratch_bytes);
+  m.def("sparse_mla_trace", &sparse_mla_trace);
   m.def("fp8_gemm_splits", &fp8_gemm_splits);
   m.def("gather_rows", &gather_rows);
   m.def("pool_recall", &pool_recall);

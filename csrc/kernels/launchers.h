@@ -225,6 +225,8 @@ size_t sparse_mla_scratch_bytes(int T, int H, int splits);
 void launch_sparse_mla_split(const MLAArgs& a, int splits, float* scratch, cudaStream_t stream);
 // tcgen05 version (2-CTA clusters exchanging partial S through DSMEM).
 void launch_sparse_mla_tc(const MLAArgs& a, int splits, float* scratch, cudaStream_t stream, int dbg = 0);
+// Per-tile event clocks of the last launch with dbg bit 64 ([4][65][16] u64).
+void copy_sparse_mla_trace(unsigned long long* host);
 // out[t,h,:] = sum_s exp(lse_s - lse) * part_o[s,t,h,:]; lse = logsumexp_s lse_s.
 void launch_mla_combine(const float* part_o, const float* part_lse, int splits, int T, int H,
                         __nv_bfloat16* out, float* lse, cudaStream_t stream);

@@ -16,21 +16,28 @@
 // (a + b == b + a), so both run an identical online softmax and each needs
 // only its half of every gathered KV record.
 //
-// Per CTA: warps 0-3 softmax/epilogue (thread = head = TMEM lane), warp 4
-// gathers the selected rows' dim slice with TMA gather4 (4 rows per
-// instruction, hardware 128-byte swizzle, out-of-range padding rows read as
-// zero) and loads Q by 2-D TMA, warp 5 allocates TMEM and
-// issues tcgen05.mma: QK (M=128 heads, N=64 keys, K=16 per instruction, both
-// operands K-major) into one of two S buffers, then P.V (M=128, N=256, K=16;
-// P K-major from shared memory, V MN-major straight from the gathered tile)
-// into O.  Latency hiding: 32-key tiles in a 4-deep KV ring (the gather runs
-// up to three tiles ahead), QK of tile i+1 is issued as soon as its rows land
-// (ahead of P.V of tile i), and the partial-S exchange is double buffered
-// with the sender one tile ahead of the reducer.  The running max is rescaled
-// lazily (only when it grows by more than 2^8), so O is rarely touched by the
+// Per CTA: warps 0-3 softmax/epilogue (thread = head = TMEM lane); warps 4-7
+// read the CTA's partial S from TMEM and send it to the peer (so the send of
+// tile i+1 overlaps the softmax of tile i); warps 8-11 gather 8 selected rows
+// each with cp.async (16 bytes per lane, written in the 128-byte swizzled
+// layout the tensor core reads; padding rows are zero-filled), warp 8 also
+// loads Q by 2-D TMA; warp 12 allocates TMEM and issues tcgen05.mma: QK
+// (M=128 heads, N=32 keys, K=16 per instruction, both operands K-major) into
+// one of three S buffers, then P.V (M=128, N=256, K=16; P from TMEM, V
+// MN-major straight from the gathered tile) into O.
+// Gathering from four warps matters: on B200 a single warp issuing either TMA
+// gather4 or cp.async for 128-byte row pieces sustains ~1.9 TB/s over the GPU,
+// four cp.async warps ~4.1 TB/s (random 640-byte slices of a 75 MB table).
+// Latency hiding: 32-key tiles in a 5-deep KV ring (the gather runs up to four
+// tiles ahead), QK of tile i+1 is issued as soon as its rows land (ahead of
+// P.V of tile i), and the partial-S exchange is double buffered with the
+// sender one tile ahead of the reducer.  The running max is rescaled lazily
+// (only when it grows by more than 2^8), so O is rarely touched by the
 // softmax warps.  All waits are bounded (error word + exit).
 #include "../common/ptx.cuh"
 #include "launchers.h"
+
+#include <type_traits>
 
 namespace b200 {
 namespace {
@@ -39,21 +46,25 @@ constexpr int D = 576;
 constexpr int DV = 512;
 constexpr int H = 128;
 constexpr int BKV = 32;                   // keys per tile
-constexpr int KV_STAGES = 4;
-constexpr int S_BUFS = 3;                 // TMEM partial-S buffers (QK runs up to 3 tiles ahead)
+constexpr int KV_STAGES = 8;
+constexpr int S_BUFS = 2;                 // TMEM partial-S buffers (QK runs up to 2 tiles ahead)
 constexpr int kMaxChunks = 5;             // 64-dim (128-byte) chunks per CTA
-constexpr int kQChunkBytes = H * 128;     // 16 KB
 constexpr int kKVChunkBytes = BKV * 128;  // 4 KB
-constexpr int kXStride = BKV + 4;         // floats per exchange row (144 B)
-constexpr int kXBytes = H * BKV * 4;      // payload of one exchange (16 KB)
-constexpr int kThreads = 192;             // warps 0-3 softmax, 4 producer, 5 MMA
+constexpr int kXStride = BKV / 2 + 4;     // 32-bit words per exchange row: 32 FP16 logits + pad (80 B)
+constexpr int kXBytes = H * BKV * 2;      // payload of one exchange (8 KB)
+// TMEM columns: O [0, 256), S buffers [256, 320), P [320, 352), Q [352, 512).
+constexpr uint32_t kTmemS = 256, kTmemP = 320, kTmemQ = 352;
+constexpr int kSenderWarp0 = 4;           // warps 0-3 softmax, 4-7 send S, 8-11 gather, 12 MMA
+constexpr int kProducerWarp0 = 8;
+constexpr int kProducers = 4;
+constexpr int kMmaWarp = kProducerWarp0 + kProducers;
+constexpr int kThreads = 32 * (kMmaWarp + 1);
+constexpr int kRowsPerProducer = BKV / kProducers;
 constexpr float kRescaleThreshold = 8.f;  // log2 units
 
 struct Smem {
-  alignas(1024) uint8_t q[kMaxChunks][kQChunkBytes];
   alignas(1024) uint8_t kv[KV_STAGES][kMaxChunks][kKVChunkBytes];
-  alignas(1024) uint8_t p[H * 128];      // P rows of 128 B: tile parity 0 in bytes 0-63, parity 1 in 64-127
-  alignas(16) float xchg[2][H * kXStride];
+  alignas(16) uint32_t xchg[2][H * kXStride];
   alignas(16) int ids[KV_STAGES][BKV];
   uint64_t q_full;
   uint64_t kv_full[KV_STAGES], kv_empty[KV_STAGES];
@@ -64,13 +75,25 @@ struct Smem {
   int abort_flag;
 };
 
+// Debug timeline (dbg bit 64): clock64 stamps of per-tile events for two
+// clusters (the first and the 371st), read back by copy_sparse_mla_trace.
+// Events per tile: 0 gather started, 1 QK issued, 2 P.V issued, 3 S read from
+// TMEM, 4 partial S sent, 5 peer partial S received, 6 KV tile seen by the
+// softmax, 7 P written, 8 gather issued, 9 rows seen by the MMA thread, 10 QK
+// issue start, 11 P.V issue start, 12 exchange added, 13 exchange released,
+// 14 P computed, 15 P buffer free.
+// Row 64: 0 start, 1 Q landed, 2 O done, 3 end.
+constexpr int kTraceTiles = 64;
+constexpr int kTraceMidCluster = 370;
+__device__ unsigned long long g_mla_trace[4][kTraceTiles + 1][16];
+
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    sparse_mla_tc_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constant__ CUtensorMap tma_kv,
-                         const int* __restrict__ ids, int T, int K, int P, float scale_log2, int splits,
+    sparse_mla_tc_kernel(const __nv_bfloat16* __restrict__ q, const uint8_t* __restrict__ kv_rows, const int* __restrict__ ids, int T, int K, int P,
+                         float scale_log2, int splits,
                          __nv_bfloat16* __restrict__ out, float* __restrict__ part_o,
                          float* __restrict__ part_lse, float* __restrict__ lse_out, int* err,
                          int dbg) {
@@ -91,20 +114,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ntiles = k_end > k_begin ? (k_end - k_begin + BKV - 1) / BKV : 0;
   const int* row_ids = ids + int64_t(t) * K;
   const bool exchange = !(dbg & 2);
-  // P (softmax probabilities, bf16) goes to TMEM columns 384.. (double-buffered by
-  // tile parity) and feeds P.V as the TMEM A operand; dbg bit 32 selects the
-  // shared-memory P path instead.
-  const bool p_tmem = !(dbg & 32);
+  int trace_slot = -1;
+  if (dbg & 64) {
+    if (blockIdx.x < 2) trace_slot = int(blockIdx.x);
+    else if ((blockIdx.x >> 1) == kTraceMidCluster) trace_slot = 2 + int(blockIdx.x & 1);
+  }
+  auto trace = [&](int tile, int ev) {
+    if (trace_slot >= 0 && tile <= kTraceTiles) g_mla_trace[trace_slot][tile][ev] = clock64();
+  };
+  if (threadIdx.x == 0) trace(kTraceTiles, 0);
 
   if (threadIdx.x == 0) {
-    mbar_init(&s.q_full, 1);
+    mbar_init(&s.q_full, 4);  // one arrive per softmax warp once its heads' Q rows are in TMEM
     for (int i = 0; i < KV_STAGES; ++i) {
-      mbar_init(&s.kv_full[i], 1);
+      mbar_init(&s.kv_full[i], kProducers);  // plus one pending count per lane until its cp.async rows land
       mbar_init(&s.kv_empty[i], 1);
     }
     for (int i = 0; i < S_BUFS; ++i) {
       mbar_init(&s.s_full[i], 1);
-      mbar_init(&s.s_empty[i], 4);     // one arrive per softmax warp
+      mbar_init(&s.s_empty[i], 8);     // one arrive per softmax and per sender warp
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.xchg_full[i], 1);   // local expect_tx + the peer's st.async bytes
@@ -124,7 +152,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     s.abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc(&s.tmem_base, 512);
     tmem_relinquish();
   }
@@ -133,88 +161,101 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync_all();  // peer barriers initialised before any remote operation
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
-  const uint32_t tmem_o = tmem + 128;  // S buffers at columns 0, 32, 64
-  const uint32_t tmem_p = tmem + 384;  // P: two 16-column (32 keys of bf16 pairs) buffers
+  const uint32_t tmem_o = tmem;
+  const uint32_t tmem_s = tmem + kTmemS;  // S(i) at column tmem_s + (i % S_BUFS) * BKV
+  const uint32_t tmem_p = tmem + kTmemP;  // P: two 16-column (32 keys of bf16 pairs) buffers
+  const uint32_t tmem_q = tmem + kTmemQ;  // Q: this CTA's dim slice as bf16 pairs (QK's A operand)
   volatile int* abort_flag = &s.abort_flag;
 
-  if (warp == 4) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      tma_prefetch_desc(&tma_q);
-      tma_prefetch_desc(&tma_kv);
-      mbar_arrive_expect_tx(&s.q_full, nch * kQChunkBytes);
-      for (int j = 0; j < nch; ++j) tma_load_2d(s.q[j], &tma_q, &s.q_full, dim0 + 64 * j, t * H);
-    }
+  if (warp >= kProducerWarp0 && warp < kMmaWarp) {
+    // ----------------------------------------------------------- producers
+    // Producer warp pw gathers rows [8 pw, 8 pw + 8) of every tile: 16-byte
+    // unit g of its share is row 8 pw + g / units, unit u = g % units of the
+    // row's slice, stored in chunk u / 8 at swizzled unit (u % 8) ^ (row % 8).
+    // The ids of tile i+1 are loaded while tile i is issued.
+    const int pw = warp - kProducerWarp0;
+    auto load_id = [&](int i) {
+      const int jj = k_begin + i * BKV + kRowsPerProducer * pw + lane;
+      int id = -1;
+      if (lane < kRowsPerProducer && i < ntiles && jj < k_end) id = __ldg(row_ids + jj);
+      return (id >= 0 && id < P) ? id : -1;
+    };
+    int next_id = load_id(0);
+    const uint8_t* base = kv_rows + dim0 * 2;
     for (int i = 0; i < ntiles; ++i) {
       const int st = i % KV_STAGES;
+      const int my_id = next_id;
+      next_id = load_id(i + 1);
       if (!mbar_wait(&s.kv_empty[st], ((i / KV_STAGES) & 1) ^ 1, err, kErrTimeoutSmemEmpty, abort_flag)) break;
-      const int key0 = k_begin + i * BKV;
-      int r[4] = {-1, -1, -1, -1};
-      if (lane < BKV / 4) {
+      if (pw == 0 && lane == 0) trace(i, 0);
+      if (lane < kRowsPerProducer) s.ids[st][kRowsPerProducer * pw + lane] = my_id;
+      if (!(dbg & 1)) {
+        auto gather = [&](auto units_c) {
+          constexpr int units = decltype(units_c)::value;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int jj = key0 + 4 * lane + e;
-          const int id = jj < k_end ? __ldg(row_ids + jj) : -1;
-          r[e] = (id >= 0 && id < P) ? id : -1;
-          s.ids[st][4 * lane + e] = r[e];
-        }
+          for (int k = 0; k < units * kRowsPerProducer / 32; ++k) {
+            const int g = k * 32 + lane;
+            const int rl = g / units, u = g % units;
+            const int row = kRowsPerProducer * pw + rl;
+            const int id = __shfl_sync(0xffffffffu, my_id, rl);
+            const uint32_t dst = smem_u32(s.kv[st][u >> 3]) + row * 128 + (((u & 7) ^ (row & 7)) << 4);
+            cp_async16_zfill(dst, id >= 0 ? base + int64_t(id) * (D * 2) + u * 16 : kv_rows, id >= 0);
+          }
+        };
+        if (nch == 4) gather(std::integral_constant<int, 32>{});
+        else gather(std::integral_constant<int, 40>{});
+        cp_async_mbar_arrive(&s.kv_full[st]);
       }
       __syncwarp();
-      if (lane == 0) {
-        if (dbg & 1) mbar_arrive(&s.kv_full[st]);
-        else mbar_arrive_expect_tx(&s.kv_full[st], BKV * 128 * nch);
-      }
-      __syncwarp();
-      if (lane < BKV / 4 && !(dbg & 1)) {
-        for (int j = 0; j < nch; ++j)
-          tma_gather4(s.kv[st][j] + lane * 4 * 128, &tma_kv, &s.kv_full[st], dim0 + 64 * j, r[0], r[1], r[2], r[3]);
-      }
+      if (lane == 0) mbar_arrive(&s.kv_full[st]);
+      if (pw == 0 && lane == 0) trace(i, 8);
     }
-  } else if (warp == 5) {
+    cp_async_wait_all();  // no copy may land after an aborted CTA has exited
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
       const uint32_t idesc_qk = umma_idesc(128, BKV, 1, 1);
       const uint32_t idesc_pv = umma_idesc(128, 256, 1, 1) | (1u << 16);  // B (V) MN-major
-      const uint64_t pdesc = umma_desc_sw128(smem_u32(s.p));
       bool ok = mbar_wait(&s.q_full, 0, err, kErrTimeoutTmaFull, abort_flag);
+      trace(kTraceTiles, 1);
       tc_fence_after();
       // Non-blocking issue: QK(j) as soon as tile j's rows and an S buffer
       // are ready (at most S_BUFS tiles ahead of P.V), P.V(i) as soon as P(i)
       // is written.  A slow gather never holds back a ready P.V and vice versa.
       auto issue_qk = [&](int i) {
         const int st = i % KV_STAGES, b = i % S_BUFS;
+        trace(i, 10);
+        fence_proxy_async();  // cp.async (generic proxy) writes before the tensor core reads them
         tc_fence_after();
         for (int j = 0; j < ((dbg & 4) ? 1 : nch); ++j) {
-          const uint64_t adesc = umma_desc_sw128(smem_u32(s.q[j]));
           const uint64_t bdesc = umma_desc_sw128(smem_u32(s.kv[st][j]));
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            mma_f16_ss(tmem + b * BKV, adesc + ((k * 32) >> 4), bdesc + ((k * 32) >> 4), idesc_qk,
+            mma_f16_ts(tmem_s + b * BKV, tmem_q + j * 32 + k * 8, bdesc + ((k * 32) >> 4), idesc_qk,
                        (j > 0 || k > 0) ? 1u : 0u);
         }
         mma_commit(&s.s_full[b]);
+        trace(i, 1);
       };
       auto issue_pv = [&](int i) {
         const int st = i % KV_STAGES;
+        trace(i, 11);
         tc_fence_after();
         const uint64_t vdesc = umma_desc_sw128_mn(smem_u32(s.kv[st]), kKVChunkBytes);
-        const uint64_t pbuf = pdesc + uint64_t((i & 1) * 64 >> 4);  // P parity half of the 128-byte rows
         const uint32_t ptm = tmem_p + uint32_t((i & 1) * (BKV / 2));
 #pragma unroll
-        for (int k = 0; k < ((dbg & 8) ? 1 : BKV / 16); ++k) {
-          if (p_tmem)
-            mma_f16_ts(tmem_o, ptm + k * 8, vdesc + ((k * 16 * 128) >> 4), idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
-          else
-            mma_f16_ss(tmem_o, pbuf + ((k * 32) >> 4), vdesc + ((k * 16 * 128) >> 4), idesc_pv,
-                       (i > 0 || k > 0) ? 1u : 0u);
-        }
+        for (int k = 0; k < ((dbg & 8) ? 1 : BKV / 16); ++k)
+          mma_f16_ts(tmem_o, ptm + k * 8, vdesc + ((k * 16 * 128) >> 4), idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
         mma_commit(&s.p_empty[i & 1]);
         mma_commit(&s.kv_empty[st]);
+        trace(i, 2);
       };
-      int nq = 0, np = 0;
+      int nq = 0, np = 0, nseen = 0;
       uint64_t idle_since = 0;
       while (ok && np < ntiles) {
         bool progressed = false;
+        if (trace_slot >= 0 && nseen < ntiles && mbar_test(&s.kv_full[nseen % KV_STAGES], (nseen / KV_STAGES) & 1))
+          trace(nseen++, 9);
         if (nq < ntiles && nq < np + S_BUFS &&
             mbar_test(&s.kv_full[nq % KV_STAGES], (nq / KV_STAGES) & 1) &&
             mbar_test(&s.s_empty[nq % S_BUFS], ((nq / S_BUFS) & 1) ^ 1)) {
@@ -237,78 +278,152 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (ok && ntiles > 0) mma_commit(&s.o_full);
     }
-  } else {
-    // ------------------------------------------------------------ softmax
-    const int h = threadIdx.x;  // head == TMEM lane
-    const uint32_t lane_addr = uint32_t(warp * 32) << 16;
+  } else if (warp >= kSenderWarp0) {
+    // ------------------------------------------------------------- senders
+    // Read this CTA's partial S of every tile from TMEM and store it, scaled
+    // and as FP16 pairs, into the peer's exchange buffer, running ahead of
+    // the softmax warps (which read the same TMEM columns) by up to one
+    // exchange buffer.
+    const int h = threadIdx.x - 32 * kSenderWarp0;  // head == TMEM lane
+    const uint32_t lane_addr = uint32_t((warp - kSenderWarp0) * 32) << 16;
     const uint32_t x_remote[2] = {mapa_shared(smem_u32(s.xchg[0]) + h * kXStride * 4, peer),
                                   mapa_shared(smem_u32(s.xchg[1]) + h * kXStride * 4, peer)};
     const uint32_t xfull_remote[2] = {mapa_shared(smem_u32(&s.xchg_full[0]), peer),
                                       mapa_shared(smem_u32(&s.xchg_full[1]), peer)};
-    const uint32_t xempty_remote[2] = {mapa_shared(smem_u32(&s.xchg_empty[0]), peer),
-                                       mapa_shared(smem_u32(&s.xchg_empty[1]), peer)};
-    const uint32_t p_row = smem_u32(s.p) + h * 128;
-    float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    float cur[BKV], nxt[BKV];
-    // Read this CTA's partial S of tile i from TMEM and send it to the peer.
-    auto take_and_send = [&](int i, float (&dst)[BKV]) -> bool {
+    for (int i = 0; i < ntiles && ok; ++i) {
       const int sb = i % S_BUFS;
       const int b = i & 1;  // exchange buffer
-      if (!mbar_wait(&s.s_full[sb], (i / S_BUFS) & 1, err, kErrTimeoutTmemFull, abort_flag)) return false;
+      if (!mbar_wait(&s.s_full[sb], (i / S_BUFS) & 1, err, kErrTimeoutTmemFull, abort_flag)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       uint32_t r[32];
-      tmem_ld32(tmem + lane_addr + sb * BKV, r);
-      tmem_wait_ld();
-#pragma unroll
-      for (int j = 0; j < BKV; ++j) dst[j] = __uint_as_float(r[j]);
+      if (exchange) {
+        tmem_ld32(tmem_s + lane_addr + sb * BKV, r);
+        tmem_wait_ld();
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.s_empty[sb]);
       if (exchange) {
         // The peer's buffer b is free once it released tile i-2.
-        if (i >= 2 && !mbar_wait_cluster(&s.xchg_empty[b], ((i >> 1) - 1) & 1, err, kErrTimeoutPeerFlag, abort_flag))
-          return false;
+        if (i >= 2 && !mbar_wait_cluster(&s.xchg_empty[b], ((i >> 1) - 1) & 1, err, kErrTimeoutPeerFlag, abort_flag)) {
+          ok = false;
+          break;
+        }
+        uint32_t hw[BKV / 2];
 #pragma unroll
-        for (int j = 0; j < BKV; j += 4)
-          st_async_v4(x_remote[b] + j * 4, dst[j], dst[j + 1], dst[j + 2], dst[j + 3], xfull_remote[b]);
+        for (int j = 0; j < BKV / 2; ++j)
+          hw[j] = pack_half2(__uint_as_float(r[2 * j]) * scale_log2, __uint_as_float(r[2 * j + 1]) * scale_log2);
+#pragma unroll
+        for (int j = 0; j < BKV / 2; j += 4)
+          st_async_v4(x_remote[b] + j * 4, __uint_as_float(hw[j]), __uint_as_float(hw[j + 1]),
+                      __uint_as_float(hw[j + 2]), __uint_as_float(hw[j + 3]), xfull_remote[b]);
+        if (h == 0) trace(i, 4);
       }
-      return true;
-    };
-    if (ntiles > 0) ok = take_and_send(0, cur);
+    }
+    // The peer's last remote accesses to this CTA are its releases of the
+    // final two exchange tiles; wait for them before shared memory goes away.
+    if (ok && exchange) {
+      for (int j = max(0, ntiles - 2); j < ntiles; ++j)
+        mbar_wait_cluster(&s.xchg_empty[j & 1], (j >> 1) & 1, err, kErrTimeoutPeerFlag, abort_flag);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int h = threadIdx.x;  // head == TMEM lane
+    const uint32_t lane_addr = uint32_t(warp * 32) << 16;
+    const uint32_t xempty_remote[2] = {mapa_shared(smem_u32(&s.xchg_empty[0]), peer),
+                                       mapa_shared(smem_u32(&s.xchg_empty[1]), peer)};
+    // Q rows of this thread's head into TMEM (QK's A operand): 32-bit column
+    // c holds dims (2c, 2c+1) of the CTA's slice, exactly the bf16 pair order
+    // of the row in memory.
+    {
+      const uint4* qrow = reinterpret_cast<const uint4*>(q + (int64_t(t) * H + h) * D + dim0);
+      auto put = [&](int c0, int n) {
+        uint32_t w[2][32];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          if (c < n) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              const uint4 x = __ldg(qrow + (c0 + c) * 8 + v);
+              w[c][4 * v] = x.x;
+              w[c][4 * v + 1] = x.y;
+              w[c][4 * v + 2] = x.z;
+              w[c][4 * v + 3] = x.w;
+            }
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+          if (c < n) tmem_st32(tmem_q + lane_addr + (c0 + c) * 32, w[c]);
+      };
+      put(0, 2);
+      put(2, 2);
+      put(4, nch - 4);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.q_full);
+    }
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    float cur[BKV];
     for (int i = 0; i < ntiles && ok; ++i) {
       const int b = i & 1;
-      if (i + 1 < ntiles && !take_and_send(i + 1, nxt)) {
+      const int sb = i % S_BUFS;
+      if (!mbar_wait(&s.s_full[sb], (i / S_BUFS) & 1, err, kErrTimeoutTmemFull, abort_flag)) {
         ok = false;
         break;
       }
+      tc_fence_after();
+      {
+        uint32_t r[32];
+        tmem_ld32(tmem_s + lane_addr + sb * BKV, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < BKV; ++j) cur[j] = __uint_as_float(r[j]) * scale_log2;
+      }
+      if (threadIdx.x == 0) trace(i, 3);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.s_empty[sb]);
       if (exchange) {
         if (!mbar_wait_cluster(&s.xchg_full[b], (i >> 1) & 1, err, kErrTimeoutPeerFlag, abort_flag)) {
           ok = false;
           break;
         }
-        const float4* xr = reinterpret_cast<const float4*>(s.xchg[b] + h * kXStride);
+        if (threadIdx.x == 0) trace(i, 5);
+        const uint4* xr = reinterpret_cast<const uint4*>(s.xchg[b] + h * kXStride);
 #pragma unroll
-        for (int j = 0; j < BKV / 4; ++j) {
-          const float4 v = xr[j];
-          cur[4 * j] += v.x;
-          cur[4 * j + 1] += v.y;
-          cur[4 * j + 2] += v.z;
-          cur[4 * j + 3] += v.w;
+        for (int j = 0; j < BKV / 8; ++j) {
+          const uint4 v = xr[j];
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = unpack_half2(w[e]);
+            cur[8 * j + 2 * e] += f.x;
+            cur[8 * j + 2 * e + 1] += f.y;
+          }
         }
+        if (threadIdx.x == 0) trace(i, 12);
         __syncwarp();
         if (lane == 0) {
           // Arm tile i+2's phase on this buffer before letting the peer reuse it.
           if (h == 0 && i + 2 < ntiles) mbar_arrive_expect_tx(&s.xchg_full[b], kXBytes);
           mbar_arrive_remote(xempty_remote[b]);
         }
+        if (threadIdx.x == 0) trace(i, 13);
       }
-      // ---- mask padding, scale, online softmax with lazy rescale
+      // ---- mask padding, online softmax with lazy rescale
       const int st = i % KV_STAGES;
       if (!mbar_wait(&s.kv_full[st], (i / KV_STAGES) & 1, err, kErrTimeoutTmaFull, abort_flag)) {
         ok = false;
         break;
       }
+      if (threadIdx.x == 0) trace(i, 6);
       float mt = -INFINITY;
       const int4* idp = reinterpret_cast<const int4*>(s.ids[st]);
 #pragma unroll
@@ -317,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int iv[4] = {idv.x, idv.y, idv.z, idv.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float x = iv[e] >= 0 ? cur[j + e] * scale_log2 : -INFINITY;
+          const float x = iv[e] >= 0 ? cur[j + e] : -INFINITY;
           cur[j + e] = x;
           mt = fmaxf(mt, x);
         }
@@ -342,6 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         pk[j] = pack_bf16(a, c);
       }
       l += psum;
+      if (threadIdx.x == 0) trace(i, 14);
       // P is double-buffered (tile parity), so P(i) only waits for P.V(i-2);
       // a rescale of O also waits for P.V(i-1) (the last MMA adding into O).
       if (i >= 2) {
@@ -370,30 +486,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_st();
         }
       }
-      if (p_tmem) {
-        tmem_st16(tmem_p + lane_addr + uint32_t((i & 1) * (BKV / 2)), pk);
-        tmem_wait_st();
-      } else {
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const uint32_t addr = p_row + (((g + 4 * (i & 1)) ^ (h & 7)) << 4);
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * g]), "r"(pk[4 * g + 1]),
-                       "r"(pk[4 * g + 2]), "r"(pk[4 * g + 3])
-                       : "memory");
-        }
-        fence_proxy_async();
-      }
+      if (threadIdx.x == 0) trace(i, 15);
+      tmem_st16(tmem_p + lane_addr + uint32_t((i & 1) * (BKV / 2)), pk);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.p_full[i & 1]);
-#pragma unroll
-      for (int j = 0; j < BKV; ++j) cur[j] = nxt[j];
+      if (threadIdx.x == 0) trace(i, 7);
     }
     // ---- epilogue: O / l
     const float inv = l > 0.f ? 1.f / l : 0.f;
     const float lse = l > 0.f ? (m_used + log2f(l)) * 0.69314718055994531f : -INFINITY;
     const bool have_o = ok && ntiles > 0 && mbar_wait(&s.o_full, 0, err, kErrTimeoutTmemFull, abort_flag);
     if (have_o) tc_fence_after();
+    if (threadIdx.x == 0) trace(kTraceTiles, 2);
     const int vd0 = int(crank) * 256;
 #pragma unroll 1
     for (int c = 0; c < 8; ++c) {
@@ -432,23 +538,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         part_lse[(int64_t(split) * T + t) * H + h] = lse;
       }
     }
-    // The peer's last remote accesses to this CTA are its releases of the
-    // final two exchange tiles; wait for them before shared memory goes away.
-    if (ok && exchange) {
-      for (int j = max(0, ntiles - 2); j < ntiles; ++j)
-        mbar_wait_cluster(&s.xchg_empty[j & 1], (j >> 1) & 1, err, kErrTimeoutPeerFlag, abort_flag);
-    }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (threadIdx.x == 0) trace(kTraceTiles, 3);
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
 }
 
 }  // namespace
+
+void copy_sparse_mla_trace(unsigned long long* host) {
+  cuda_check(cudaMemcpyFromSymbol(host, g_mla_trace, sizeof(g_mla_trace)), "sparse_mla trace copy");
+}
 
 void launch_sparse_mla_tc(const MLAArgs& a, int splits, float* scratch, cudaStream_t stream, int dbg) {
   if (a.T <= 0) return;
@@ -470,13 +575,10 @@ void launch_sparse_mla_tc(const MLAArgs& a, int splits, float* scratch, cudaStre
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const float scale_log2 = a.scale * 1.4426950408889634f;
-  // Q as [T*128 rows, 576] with 64-column boxes of all 128 heads; KV as
-  // [P rows, 576] with one-row boxes for gather4.
-  const CUtensorMap tq = make_tma_2d(a.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, int64_t(a.T) * H, D, D * 2, 64, H);
-  const CUtensorMap tkv = make_tma_2d(a.kv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.P, D, D * 2, 64, 1);
   float* part_o = splits > 1 ? scratch : nullptr;
   float* part_lse = splits > 1 ? scratch + size_t(splits) * a.T * a.H * DV : nullptr;
-  cuda_check(cudaLaunchKernelEx(&cfg, sparse_mla_tc_kernel, tq, tkv, a.ids, a.T, a.K, a.P, scale_log2, splits,
+  cuda_check(cudaLaunchKernelEx(&cfg, sparse_mla_tc_kernel, a.q, reinterpret_cast<const uint8_t*>(a.kv), a.ids,
+                                a.T, a.K, a.P, scale_log2, splits,
                                 a.out, part_o, part_lse, a.lse, a.err, dbg),
              "sparse_mla_tc launch");
   if (splits > 1) launch_mla_combine(part_o, part_lse, splits, a.T, a.H, a.out, a.lse, stream);

@@ -162,7 +162,7 @@ def test_topk_moderate_ties_two_pass():
 
 
 # ------------------------------------------------------------ sparse MLA
-@pytest.mark.parametrize("impl", [0, 1, 48], ids=["tcgen05", "mma_sync", "tcgen05_smem_p"])
+@pytest.mark.parametrize("impl", [0, 1], ids=["tcgen05", "mma_sync"])
 @pytest.mark.parametrize("T,K,P,splits", [(2, 2048, 5000, 1), (3, 256, 300, 1), (1, 2048, 9000, 16), (5, 100, 64, 4),
                                           (300, 2048, 70000, 1)])
 def test_sparse_mla(T, K, P, splits, impl):
@@ -185,7 +185,7 @@ def test_sparse_mla(T, K, P, splits, impl):
     assert torch.allclose(lse.cpu(), wlse, atol=2e-2, rtol=1e-3)
 
 
-@pytest.mark.parametrize("impl", [0, 1, 48])
+@pytest.mark.parametrize("impl", [0, 1])
 def test_sparse_mla_all_padding_is_zero(impl):
     q = torch.randn(2, 128, 576, device=DEV).bfloat16()
     kv = torch.randn(10, 576, device=DEV).bfloat16()
