@@ -11,28 +11,34 @@
 // exactly all 512 TMEM columns of an SM, leaving no room for S.  So CTA c of
 // the pair owns V dims [256c, 256c+256) (256 TMEM columns) and computes the
 // partial S = Q K^T over its own share of the 576 QK dims (CTA0: dims 0-255,
-// CTA1: dims 256-575).  Each tile the two CTAs swap their 128x64 FP32 partial
-// S through distributed shared memory and both add them in the same order
-// (a + b == b + a), so both run an identical online softmax and each needs
-// only its half of every gathered KV record.
+// CTA1: dims 256-575).  Each tile the two CTAs swap their 128x32 partial S
+// (scaled, FP16) through distributed shared memory; each adds the peer's half
+// to its own FP32 half, so each needs only its half of every gathered KV
+// record.  The two CTAs' logits differ only by the FP16 rounding of one half
+// (~2^-11 relative), and each CTA's softmax is self-consistent (its own P and
+// l normalise its own V dims).
 //
 // Per CTA: warps 0-3 softmax/epilogue (thread = head = TMEM lane); warps 4-7
-// read the CTA's partial S from TMEM and send it to the peer (so the send of
-// tile i+1 overlaps the softmax of tile i); warps 8-11 gather 8 selected rows
-// each with cp.async (16 bytes per lane, written in the 128-byte swizzled
-// layout the tensor core reads; padding rows are zero-filled), warp 8 also
-// loads Q by 2-D TMA; warp 12 allocates TMEM and issues tcgen05.mma: QK
-// (M=128 heads, N=32 keys, K=16 per instruction, both operands K-major) into
-// one of three S buffers, then P.V (M=128, N=256, K=16; P from TMEM, V
-// MN-major straight from the gathered tile) into O.
-// Gathering from four warps matters: on B200 a single warp issuing either TMA
-// gather4 or cp.async for 128-byte row pieces sustains ~1.9 TB/s over the GPU,
-// four cp.async warps ~4.1 TB/s (random 640-byte slices of a 75 MB table).
-// Latency hiding: 32-key tiles in a 5-deep KV ring (the gather runs up to four
-// tiles ahead), QK of tile i+1 is issued as soon as its rows land (ahead of
-// P.V of tile i), and the partial-S exchange is double buffered with the
-// sender one tile ahead of the reducer.  The running max is rescaled lazily
-// (only when it grows by more than 2^8), so O is rarely touched by the
+// read the CTA's partial S from TMEM and send it, scaled and as FP16 pairs
+// (8 KB per tile), into the peer's exchange buffer; warps 8-11 gather 8
+// selected rows each with cp.async (16 bytes per lane, written in the 128-byte
+// swizzled layout the tensor core reads; padding rows are zero-filled); warp
+// 12 allocates TMEM and issues tcgen05.mma: QK (M=128 heads, N=32 keys, K=16
+// per instruction; A = Q resident in TMEM, B = the gathered K rows) into one
+// of two S buffers, then P.V (M=128, N=256, K=16; P from TMEM, V MN-major
+// straight from the gathered tile) into O.
+//
+// Measured on B200 (per-tile event clocks, dbg bit 64), which set this shape:
+// a single warp issuing TMA gather4 or cp.async for 128-byte row pieces
+// sustains only ~1.9 TB/s over the GPU, four cp.async warps ~4.1 TB/s; a
+// cluster-scope release on the remote arrive costs ~1 us; DSMEM moves ~7-8
+// bytes/clock/SM, so partial S crosses as FP16; Q re-read from shared memory
+// by every QK cost 80 KB of shared-memory bandwidth per tile, so it lives in
+// TMEM.  Latency hiding: 32-key tiles in an 8-deep KV ring (the gather runs up
+// to seven tiles ahead), QK of tile j is issued as soon as its rows land and
+// the S buffer of tile j-2 has been read (so the sender runs ahead of the
+// softmax), the exchange is double buffered, and the running max is rescaled
+// lazily (only when it grows by more than 2^8), so O is rarely touched by the
 // softmax warps.  All waits are bounded (error word + exit).
 #include "../common/ptx.cuh"
 #include "launchers.h"
@@ -220,8 +226,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       trace(kTraceTiles, 1);
       tc_fence_after();
       // Non-blocking issue: QK(j) as soon as tile j's rows and an S buffer
-      // are ready (at most S_BUFS tiles ahead of P.V), P.V(i) as soon as P(i)
-      // is written.  A slow gather never holds back a ready P.V and vice versa.
+      // are ready (the buffer of S(j-2) is free once the softmax and sender
+      // warps have read it, which lets the sender run a tile further ahead),
+      // P.V(i) as soon as P(i) is written.  A slow gather never holds back a
+      // ready P.V and vice versa.
       auto issue_qk = [&](int i) {
         const int st = i % KV_STAGES, b = i % S_BUFS;
         trace(i, 10);
@@ -256,8 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool progressed = false;
         if (trace_slot >= 0 && nseen < ntiles && mbar_test(&s.kv_full[nseen % KV_STAGES], (nseen / KV_STAGES) & 1))
           trace(nseen++, 9);
-        if (nq < ntiles && nq < np + S_BUFS &&
-            mbar_test(&s.kv_full[nq % KV_STAGES], (nq / KV_STAGES) & 1) &&
+        if (nq < ntiles && mbar_test(&s.kv_full[nq % KV_STAGES], (nq / KV_STAGES) & 1) &&
             mbar_test(&s.s_empty[nq % S_BUFS], ((nq / S_BUFS) & 1) ^ 1)) {
           issue_qk(nq++);
           progressed = true;
@@ -390,6 +397,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.s_empty[sb]);
+      const int st = i % KV_STAGES;
+      if (!mbar_wait(&s.kv_full[st], (i / KV_STAGES) & 1, err, kErrTimeoutTmaFull, abort_flag)) {
+        ok = false;
+        break;
+      }
       if (exchange) {
         if (!mbar_wait_cluster(&s.xchg_full[b], (i >> 1) & 1, err, kErrTimeoutPeerFlag, abort_flag)) {
           ok = false;
@@ -409,34 +421,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (threadIdx.x == 0) trace(i, 12);
-        __syncwarp();
-        if (lane == 0) {
-          // Arm tile i+2's phase on this buffer before letting the peer reuse it.
-          if (h == 0 && i + 2 < ntiles) mbar_arrive_expect_tx(&s.xchg_full[b], kXBytes);
-          mbar_arrive_remote(xempty_remote[b]);
-        }
-        if (threadIdx.x == 0) trace(i, 13);
       }
       // ---- mask padding, online softmax with lazy rescale
-      const int st = i % KV_STAGES;
-      if (!mbar_wait(&s.kv_full[st], (i / KV_STAGES) & 1, err, kErrTimeoutTmaFull, abort_flag)) {
-        ok = false;
-        break;
-      }
       if (threadIdx.x == 0) trace(i, 6);
-      float mt = -INFINITY;
       const int4* idp = reinterpret_cast<const int4*>(s.ids[st]);
 #pragma unroll
-      for (int j = 0; j < BKV; j += 4) {
-        const int4 idv = idp[j / 4];
+      for (int j = 0; j < BKV / 4; ++j) {
+        const int4 idv = idp[j];
         const int iv[4] = {idv.x, idv.y, idv.z, idv.w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float x = iv[e] >= 0 ? cur[j + e] : -INFINITY;
-          cur[j + e] = x;
-          mt = fmaxf(mt, x);
-        }
+        for (int e = 0; e < 4; ++e)
+          if (iv[e] < 0) cur[4 * j + e] = -INFINITY;
       }
+      float mx[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx[j] = fmaxf(fmaxf(cur[j], cur[j + 8]), fmaxf(cur[j + 16], cur[j + 24]));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) mx[j] = fmaxf(mx[j], mx[j + 4]);
+      const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
       bool rescale = false;
       float alpha = 1.f;
       if (m_used == -INFINITY) {
@@ -449,14 +451,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float base = m_used == -INFINITY ? 0.f : m_used;
       uint32_t pk[BKV / 2];
-      float psum = 0.f;
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int j = 0; j < BKV / 2; ++j) {
-        const float a = exp2f(cur[2 * j] - base), c = exp2f(cur[2 * j + 1] - base);
-        psum += a + c;
+        const float a = ex2_approx(cur[2 * j] - base), c = ex2_approx(cur[2 * j + 1] - base);
+        ps[j & 3] += a + c;
         pk[j] = pack_bf16(a, c);
       }
-      l += psum;
+      l += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+      if (threadIdx.x == 0) trace(i, 14);
       if (threadIdx.x == 0) trace(i, 14);
       // P is double-buffered (tile parity), so P(i) only waits for P.V(i-2);
       // a rescale of O also waits for P.V(i-1) (the last MMA adding into O).
@@ -487,11 +490,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (threadIdx.x == 0) trace(i, 15);
+      if (threadIdx.x == 0) trace(i, 15);
       tmem_st16(tmem_p + lane_addr + uint32_t((i & 1) * (BKV / 2)), pk);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s.p_full[i & 1]);
+      if (lane == 0) {
+        mbar_arrive(&s.p_full[i & 1]);
+        if (exchange) {
+          // Release exchange buffer b to the peer (off the P.V critical path);
+          // arm tile i+2's phase on it first.
+          if (h == 0 && i + 2 < ntiles) mbar_arrive_expect_tx(&s.xchg_full[b], kXBytes);
+          mbar_arrive_remote(xempty_remote[b]);
+        }
+      }
       if (threadIdx.x == 0) trace(i, 7);
     }
     // ---- epilogue: O / l
