@@ -37,7 +37,7 @@ const T* cptr(const Tensor& t) { return reinterpret_cast<const T*>(t.data_ptr())
 
 // ------------------------------------------------------------------ GEMMs
 void fp8_gemm(const Tensor& a_q, const Tensor& a_s_t, const Tensor& w, const Tensor& w_s, Tensor& out,
-              const c10::optional<Tensor>& residual) {
+              const c10::optional<Tensor>& residual, bool ue8m0) {
   CHECK_CUDA(a_q); CHECK_CUDA(w); CHECK_CUDA(out);
   CHECK_DTYPE(a_q, torch::kFloat8_e4m3fn); CHECK_DTYPE(w, torch::kFloat8_e4m3fn);
   CHECK_DTYPE(a_s_t, torch::kFloat32); CHECK_DTYPE(w_s, torch::kFloat32); CHECK_DTYPE(out, torch::kBFloat16);
@@ -60,6 +60,7 @@ void fp8_gemm(const Tensor& a_q, const Tensor& a_s_t, const Tensor& w, const Ten
   }
   a.M = M; a.N = N; a.K = K; a.lda = a_q.stride(0); a.ldb = w.stride(0);
   a.lda_s = a_s_t.stride(0); a.ldo = out.stride(0); a.err = err_ptr(a_q);
+  a.ue8m0 = ue8m0;
   // Split-K scratch for GEMMs whose tile count leaves SMs idle.
   constexpr int kMaxSplits = 8;
   const size_t scratch = b200::fp8_gemm_scratch_bytes(M, N, K, kMaxSplits);

@@ -271,6 +271,46 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t addr) {
   return d;
 }
 
+// Block-scaled FP8 MMA (kind::mxf8f6f4.block_scale, one UE8M0 scale per 32 K
+// elements): D (+)= (A * 2^sfa) (B * 2^sfb), the scales read from TMEM at
+// sfa_tmem / sfb_tmem.  The byte of the 32-bit scale column used by this MMA
+// (its 32-element K sub-block) is the sf id in the instruction descriptor.
+__device__ __forceinline__ void mma_f8_bs(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// Instruction descriptor of mma_f8_bs: E4M3 x E4M3, both K-major, UE8M0 scales,
+// FP32 accumulate; sf_a / sf_b select the scale byte (K sub-block 0-3).
+__host__ __device__ constexpr uint32_t umma_idesc_bs(uint32_t m, uint32_t n, uint32_t sf_a, uint32_t sf_b) {
+  return (sf_b << 4)              // scale factor B id
+         | ((n >> 3) << 17)       // N >> 3
+         | (1u << 23)             // scale format UE8M0
+         | ((m >> 4) << 24)       // M >> 4
+         | (sf_a << 29);          // scale factor A id
+}
+
+// Shared-memory descriptor of an unswizzled K-major block of 16-byte rows
+// (8-row core matrices sbo_bytes apart), the source format of tcgen05.cp.
+__device__ __forceinline__ uint64_t umma_desc_noswz(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;  // version (sm100); layout type 0 = no swizzle
+  return d;
+}
+
+// Copy 32 rows x 16 bytes from shared memory into TMEM lanes 0-31 of all four
+// lane quarters (4 columns), as the scale-factor operand of mma_f8_bs reads it.
+__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
 // Instruction descriptor: fp32 accumulate, both operands K-major.
 // a_fmt/b_fmt: kind::f16 -> 0 F16, 1 BF16; kind::f8f6f4 -> 0 E4M3, 1 E5M2.
 __host__ __device__ constexpr uint32_t umma_idesc(uint32_t m, uint32_t n, uint32_t a_fmt,

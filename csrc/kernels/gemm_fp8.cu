@@ -19,14 +19,14 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int spli
   out[int64_t(m) * ldo + n] = __float2bfloat16_rn(v);
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool BS>
 void launch_fp8_gemm_t(const FP8GemmArgs& a, int splits, cudaStream_t stream) {
   const CUtensorMap ta = make_tma_2d(a.A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.M, a.K, a.lda, BK, BM);
   const CUtensorMap tb = make_tma_2d(a.B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.N, a.K, a.ldb, BK, BN);
   const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
   const int grid = std::min(tiles * splits, sm_count());
-  const size_t smem = smem_bytes<BN, STAGES>();
-  auto kern = fp8_gemm_kernel<BN, STAGES, kModePlain>;
+  const size_t smem = smem_bytes<BN, STAGES, kModePlain, BS>();
+  auto kern = fp8_gemm_kernel<BN, STAGES, kModePlain, BS>;
   cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
              "fp8 gemm smem attribute");
   kern<<<grid, kThreads, smem, stream>>>(ta, tb, a.sfa, a.lda_s, a.sfb, a.out, a.ldo, a.residual,
@@ -83,9 +83,15 @@ void launch_fp8_gemm(const FP8GemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return;
   if (a.K % 16) throw std::invalid_argument("fp8 gemm: K must be a multiple of 16");
   FP8GemmPlan p = plan_fp8_gemm(a.M, a.N, a.K, a.partial ? a.max_splits : 1);
-  if (p.bn == 256) launch_fp8_gemm_t<256, 4>(a, 1, stream);
-  else if (p.bn == 224) launch_fp8_gemm_t<224, 4>(a, 1, stream);
-  else launch_fp8_gemm_t<128, 6>(a, p.splits, stream);
+  if (a.ue8m0) {
+    if (p.bn == 256) launch_fp8_gemm_t<256, 4, true>(a, 1, stream);
+    else if (p.bn == 224) launch_fp8_gemm_t<224, 4, true>(a, 1, stream);
+    else launch_fp8_gemm_t<128, 6, true>(a, p.splits, stream);
+  } else {
+    if (p.bn == 256) launch_fp8_gemm_t<256, 4, false>(a, 1, stream);
+    else if (p.bn == 224) launch_fp8_gemm_t<224, 4, false>(a, 1, stream);
+    else launch_fp8_gemm_t<128, 6, false>(a, p.splits, stream);
+  }
 }
 
 }  // namespace b200

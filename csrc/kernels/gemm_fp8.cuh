@@ -63,10 +63,33 @@ constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each owning BN/2 co
 constexpr int kThreads = 64 + kEpiWarps * 32;
 constexpr int kEpiBarrier = 1;  // named barrier id of the 256 epilogue threads
 
-template <int BN, int STAGES>
+// Block-scaled mode (BS): the tensor core applies the UE8M0 scales itself
+// (tcgen05.mma kind::mxf8f6f4.block_scale), so the accumulator of a tile is
+// read once instead of promoted per K block.  The producer writes scale
+// chunks in the layout tcgen05.cp.32x128b.warpx4 copies into TMEM: a chunk
+// covers 128 rows, row r0 + 32 r1 at byte 16 r0 + 4 r1 + j; TMEM then holds,
+// in lane r0 of every lane quarter, column r1 = row group, and the MMA picks
+// byte j with its sf id.  The hardware meant byte j for the j-th 32-element
+// K sub-block; since these scales are constant over a 128-wide K block, byte j
+// here carries K block 4g + j instead and every MMA of that block uses sf id
+// j.  One chunk copy then serves a group of four K blocks (4x fewer
+// tcgen05.cp in the in-order tensor pipe).  The producer loads a group's FP32
+// scales a whole group ahead and packs them only when the group is written:
+// under the kernel's own TMA traffic an L2 round trip outlasts several
+// stages.  Measured on B200 (M = 1024): at parity with the promotion path for
+// BN = 224 (two accumulators), slower for BN = 256 with short K (one
+// accumulator, the epilogue serialises with the next tile); both paths are
+// limited by the operand feed of 128 x BN tiles, not by the promotion.
+constexpr int kSfChunk = 512;       // bytes of one 128-row scale chunk
+constexpr int kSfSlotCols = 12;     // TMEM columns per scale slot: SFA 4 + SFB 2 x 4
+constexpr int kSfSlots = 4;
+constexpr uint32_t kSfCol0 = 512 - kSfSlots * kSfSlotCols;
+
+template <int BN, int STAGES, bool BS = false>
 struct GemmSmem {
   alignas(1024) uint8_t a[STAGES][BM * BK];
   alignas(1024) uint8_t b[STAGES][BN * BK];
+  alignas(128) uint8_t sf[BS ? STAGES : 1][BS ? 3 * kSfChunk : 16];  // SFA, SFB rows 0-127, SFB rows 128-255
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
   uint64_t tmem_full[2];
@@ -95,7 +118,10 @@ __device__ __forceinline__ bool ag_wait_rows(const P2PArgs& p, int m0, int M, ui
   return true;
 }
 
-template <int BN, int STAGES, int MODE>
+// UE8M0 code of a power-of-two FP32 scale: its biased exponent.
+__device__ __forceinline__ uint32_t ue8m0_byte(float v) { return (__float_as_uint(v) >> 23) & 0xFFu; }
+
+template <int BN, int STAGES, int MODE, bool BS = false>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                     const __grid_constant__ CUtensorMap tma_b, const float* __restrict__ sfa,
@@ -104,7 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     int K, int splits, float* __restrict__ partial, int* err,
                     const __grid_constant__ P2PArgs p2p, const __grid_constant__ GroupArgs grp) {
   extern __shared__ uint8_t smem_raw[];
-  auto& s = *reinterpret_cast<GemmSmem<BN, STAGES>*>(
+  auto& s = *reinterpret_cast<GemmSmem<BN, STAGES, BS>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -131,7 +157,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
   }
   // TMEM allocations are powers of two >= 32 columns (BN = 224 takes 512).
-  constexpr uint32_t kTmemCols = 2 * BN <= 256 ? 256 : 512;
+  // BS: the scale slots take the top 48 columns; BN = 256 then keeps one
+  // accumulator (the epilogue of a tile and the next tile's MMAs serialise).
+  constexpr uint32_t kTmemCols = BS ? 512 : (2 * BN <= 256 ? 256 : 512);
+  constexpr int kAccBufs = (!BS || 2 * BN <= int(kSfCol0)) ? 2 : 1;
   if (warp == 1) {
     tmem_alloc(&s.tmem_base, kTmemCols);
     tmem_relinquish();
@@ -146,7 +175,136 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = s.tmem_base;
   volatile int* abort_flag = &s.abort_flag;
 
-  if (warp == 0) {
+  if (warp == 0 && BS) {
+    // Whole warp: lane 0 issues the TMA loads, every lane writes 16 bytes of
+    // each scale chunk (rows lane + 32 r, r = 0..3).  The stage loads of this
+    // CTA are walked as one flat sequence so that the scales of the next stage
+    // are loaded while the current one is issued (their global-load latency
+    // would otherwise exceed a stage's MMA time).
+    struct Cursor {
+      int u = 0, kb = 0, kbs = 0, kb1 = 0, m0 = 0, nc0 = 0, n0 = 0;
+      const float* sfb_u = nullptr;
+      __device__ bool group_lead() const { return ((kb - kbs) & 3) == 0; }
+    };
+    // Moves c to its unit's next K block, else to the next unit with work;
+    // false past the end.
+    auto enter_unit = [&](Cursor& c) -> bool {
+      for (; c.u < num_units; c.u += gridDim.x) {
+        const int tile = c.u % num_tiles, sp = c.u / num_tiles;
+        c.m0 = tile_m_block(tile, num_m, rot) * BM;
+        c.nc0 = (tile / num_m) * BN;
+        c.n0 = c.nc0;
+        c.sfb_u = sfb;
+        c.kb = c.kbs = sp * kps;
+        c.kb1 = min(num_kb, c.kb + kps);
+        if constexpr (MODE == kModeGrouped) {
+          const int e = unit_expert(grp, c.m0 / BM);
+          if (e < 0) continue;
+          c.n0 += e * N;
+          c.sfb_u = sfb + e * grp.sfb_expert_stride;
+        }
+        if (c.kb < c.kb1) return true;
+      }
+      return false;
+    };
+    // Raw scales of the group of (up to) four K blocks starting at c.kb (rows
+    // lane + 32 r of the SFA chunk and of the two SFB chunks), loaded a group
+    // ahead and only packed into UE8M0 words (byte g = K block c.kb + g) when
+    // the group is written, so the loads' latency is not waited for early.
+    struct RawScales {
+      float a[4][4];     // [g][r]
+      float b[2][4][4];  // [chunk][g][r]
+    };
+    auto load_raw = [&](const Cursor& c, RawScales& raw) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const int kb = c.kb + g;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int row = c.m0 + lane + 32 * r;
+          raw.a[g][r] = kb < c.kb1 && row < M ? __ldg(sfa + static_cast<size_t>(kb) * lda_s + row) : 0.f;
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int n = c.nc0 + 128 * j + lane + 32 * r;
+            raw.b[j][g][r] =
+                kb < c.kb1 && n < N ? __ldg(c.sfb_u + static_cast<size_t>(n / 128) * kb_scale_stride + kb) : 0.f;
+          }
+        }
+      }
+    };
+    auto pack = [&](const RawScales& raw, uint32_t (&wa)[4], uint32_t (&wb)[2][4]) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        wa[r] = 0u;
+        wb[0][r] = 0u;
+        wb[1][r] = 0u;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          wa[r] |= ue8m0_byte(raw.a[g][r]) << (8 * g);
+          wb[0][r] |= ue8m0_byte(raw.b[0][g][r]) << (8 * g);
+          wb[1][r] |= ue8m0_byte(raw.b[1][g][r]) << (8 * g);
+        }
+      }
+    };
+    // Steps c to the next stage load; false past the end.
+    auto advance = [&](Cursor& c) -> bool {
+      if (++c.kb < c.kb1) return true;
+      c.u += gridDim.x;
+      return enter_unit(c);
+    };
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    Cursor cur;
+    cur.u = blockIdx.x;
+    bool have = enter_unit(cur);
+    // Scales of the current group (raw, packed at its lead stage) and of the
+    // next one (ahead): a group's loads are issued at the lead stage of the
+    // group before it, a whole group (up to four stage loads) ahead of use,
+    // because under the kernel's own TMA traffic an L2 round trip outlasts a
+    // stage's MMAs.
+    RawScales raw, ahead;
+    uint32_t wa[4], wb[2][4];
+    if (have) load_raw(cur, raw);
+    while (have) {
+      if (cur.group_lead()) {
+        pack(raw, wa, wb);
+        Cursor nl = cur;  // lead stage of the next group
+        bool more = advance(nl);
+        while (more && !nl.group_lead()) more = advance(nl);
+        if (more) load_raw(nl, ahead);
+      }
+      const bool got = lane == 0 && mbar_wait(&s.empty[stage], phase ^ 1, err, kErrTimeoutSmemEmpty, abort_flag);
+      if (!__shfl_sync(0xffffffffu, got, 0)) {
+        ok = false;
+        break;
+      }
+      if (cur.group_lead()) {
+        *reinterpret_cast<uint4*>(s.sf[stage] + 16 * lane) = make_uint4(wa[0], wa[1], wa[2], wa[3]);
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+          *reinterpret_cast<uint4*>(s.sf[stage] + kSfChunk * (1 + j) + 16 * lane) =
+              make_uint4(wb[j][0], wb[j][1], wb[j][2], wb[j][3]);
+        fence_proxy_async();  // generic writes before tcgen05.cp reads them
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&s.full[stage], BM * BK + BN * BK);
+        tma_load_2d(s.a[stage], &tma_a, &s.full[stage], cur.kb * BK, cur.m0);
+        tma_load_2d(s.b[stage], &tma_b, &s.full[stage], cur.kb * BK, cur.n0);
+      }
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1;
+      }
+      have = advance(cur);
+      if (have && cur.group_lead()) raw = ahead;
+    }
+    if (!ok && lane == 0) {
+      // Drain copies already in flight before the CTA releases its smem.
+      for (int i = 0; i < STAGES; ++i) mbar_wait(&s.full[i], 0, nullptr, 0, nullptr, 100000000ull);
+    }
+  } else if (warp == 0) {
     if (elect_one()) {
       int stage = 0;
       uint32_t phase = 0;
@@ -186,6 +344,59 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) {
         // Drain copies already in flight before the CTA releases its smem.
         for (int i = 0; i < STAGES; ++i) mbar_wait(&s.full[i], 0, nullptr, 0, nullptr, 100000000ull);
+      }
+    }
+  } else if (warp == 1 && BS) {
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t gcount = 0, tcount = 0;  // scale groups copied, tiles finished
+      bool ok = true;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const int sp = u / num_tiles;
+        const int kb0 = sp * kps, kb1 = min(num_kb, kb0 + kps);
+        if constexpr (MODE == kModeGrouped) {
+          if (unit_expert(grp, tile_m_block(u % num_tiles, num_m, rot)) < 0) continue;
+        }
+        const uint32_t buf = kAccBufs == 2 ? (tcount & 1) : 0;
+        const uint32_t bpar = kAccBufs == 2 ? ((tcount >> 1) & 1) : (tcount & 1);
+        if (!mbar_wait(&s.tmem_empty[buf], bpar ^ 1, err, kErrTimeoutTmemEmpty, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t sfa_t = 0, sfb_t = 0;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&s.full[stage], phase, err, kErrTimeoutTmaFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t g = uint32_t(kb - kb0) & 3;  // this block's byte in the group's scale words
+          if (g == 0) {
+            sfa_t = tmem + kSfCol0 + (gcount++ % kSfSlots) * kSfSlotCols;
+            sfb_t = sfa_t + 4;
+            const uint32_t sf_base = smem_u32(s.sf[stage]);
+            tmem_cp_32x128b_x4(sfa_t, umma_desc_noswz(sf_base, kSfChunk, 128));
+            tmem_cp_32x128b_x4(sfb_t, umma_desc_noswz(sf_base + kSfChunk, kSfChunk, 128));
+            if (BN > 128) tmem_cp_32x128b_x4(sfb_t + 4, umma_desc_noswz(sf_base + 2 * kSfChunk, kSfChunk, 128));
+          }
+          const uint64_t adesc = umma_desc_sw128(smem_u32(s.a[stage]));
+          const uint64_t bdesc = umma_desc_sw128(smem_u32(s.b[stage]));
+          const uint32_t idesc = umma_idesc_bs(BM, BN, g, g);
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k)
+            mma_f8_bs(tmem + buf * BN, adesc + (k * 32 >> 4), bdesc + (k * 32 >> 4), idesc, sfa_t, sfb_t,
+                      (kb > kb0 || k > 0) ? 1u : 0u);
+          mma_commit(&s.empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&s.tmem_full[buf]);
+        ++tcount;
       }
     }
   } else if (warp == 1) {
@@ -240,7 +451,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     bool ok = true;
     // RS staging tile [BM][BN + 8] bf16 after the pipeline buffers (dynamic smem).
-    __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(&s) + sizeof(GemmSmem<BN, STAGES>));
+    __nv_bfloat16* stage =
+        reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(&s) + sizeof(GemmSmem<BN, STAGES, BS>));
 
     if constexpr (MODE == kModeAG) {
       // Push this rank's shard (rows [rank*S, rank*S+S) of the gathered A) and
@@ -282,6 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     uint32_t kcount = 0;
+    uint32_t tcount = 0;  // BS: tiles finished (accumulator buffer + parity)
     uint32_t ready = 0;
     int owner_ok = -1;  // RS: owner whose reuse guard this thread already passed
     for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
@@ -306,35 +519,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       float acc[CPW];
 #pragma unroll
       for (int j = 0; j < CPW; ++j) acc[j] = 0.f;
-      for (int kb = kb0; kb < kb1; ++kb, ++kcount) {
-        const uint32_t buf = kcount & 1;
-        const uint32_t bpar = (kcount >> 1) & 1;
-        float sa = 0.f;
-        if (row < M) {
-          const float* sp_ = sfa + static_cast<size_t>(kb) * lda_s + row;
-          sa = MODE == kModeAG ? __ldcg(sp_) : __ldg(sp_);
-        }
-        // A warp's CPW (<= 128) columns touch at most two 128-wide weight scale blocks.
-        const int nb0 = n0 / 128, nb1 = (n0 + CPW - 1) / 128;
-        const float sb0 = nb0 * 128 < N ? __ldg(sfb_u + static_cast<size_t>(nb0) * kb_scale_stride + kb) : 0.f;
-        const float sb1 = nb1 * 128 < N ? __ldg(sfb_u + static_cast<size_t>(nb1) * kb_scale_stride + kb) : 0.f;
+      if constexpr (BS) {
+        // The tile's finished accumulator, read once.
+        const uint32_t buf = kAccBufs == 2 ? (tcount & 1) : 0;
+        const uint32_t bpar = kAccBufs == 2 ? ((tcount >> 1) & 1) : (tcount & 1);
+        ++tcount;
         if (!mbar_wait(&s.tmem_full[buf], bpar, err, kErrTimeoutTmemFull, abort_flag)) {
           ok = false;
-          break;
-        }
-        tc_fence_after();
+        } else {
+          tc_fence_after();
+          if (kb0 < kb1) {
 #pragma unroll
-        for (int c = 0; c < CPW / 16; ++c) {
-          uint32_t r[16];
-          tmem_ld16(tmem + lane_addr + buf * BN + chalf * CPW + c * 16, r);
-          tmem_wait_ld();
-          const float scale = sa * ((n0 + c * 16) / 128 == nb0 ? sb0 : sb1);
+            for (int c = 0; c < CPW / 16; ++c) {
+              uint32_t r[16];
+              tmem_ld16(tmem + lane_addr + buf * BN + chalf * CPW + c * 16, r);
+              tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) acc[c * 16 + j] = fmaf(__uint_as_float(r[j]), scale, acc[c * 16 + j]);
+              for (int j = 0; j < 16; ++j) acc[c * 16 + j] = __uint_as_float(r[j]);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.tmem_empty[buf]);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s.tmem_empty[buf]);
+      } else {
+        for (int kb = kb0; kb < kb1; ++kb, ++kcount) {
+          const uint32_t buf = kcount & 1;
+          const uint32_t bpar = (kcount >> 1) & 1;
+          float sa = 0.f;
+          if (row < M) {
+            const float* sp_ = sfa + static_cast<size_t>(kb) * lda_s + row;
+            sa = MODE == kModeAG ? __ldcg(sp_) : __ldg(sp_);
+          }
+          // A warp's CPW (<= 128) columns touch at most two 128-wide weight scale blocks.
+          const int nb0 = n0 / 128, nb1 = (n0 + CPW - 1) / 128;
+          const float sb0 = nb0 * 128 < N ? __ldg(sfb_u + static_cast<size_t>(nb0) * kb_scale_stride + kb) : 0.f;
+          const float sb1 = nb1 * 128 < N ? __ldg(sfb_u + static_cast<size_t>(nb1) * kb_scale_stride + kb) : 0.f;
+          if (!mbar_wait(&s.tmem_full[buf], bpar, err, kErrTimeoutTmemFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < CPW / 16; ++c) {
+            uint32_t r[16];
+            tmem_ld16(tmem + lane_addr + buf * BN + chalf * CPW + c * 16, r);
+            tmem_wait_ld();
+            const float scale = sa * ((n0 + c * 16) / 128 == nb0 ? sb0 : sb1);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[c * 16 + j] = fmaf(__uint_as_float(r[j]), scale, acc[c * 16 + j]);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.tmem_empty[buf]);
+        }
       }
       // RS threads always reach the per-tile named barrier below (a thread that
       // left early would strand the others there); other modes leave now.
@@ -465,9 +703,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int BN, int STAGES, int MODE = kModePlain>
+template <int BN, int STAGES, int MODE = kModePlain, bool BS = false>
 inline size_t smem_bytes() {
-  return sizeof(GemmSmem<BN, STAGES>) + 1024 + (MODE == kModeRS ? size_t(BM) * (BN + 8) * 2 : 0);
+  return sizeof(GemmSmem<BN, STAGES, BS>) + 1024 + (MODE == kModeRS ? size_t(BM) * (BN + 8) * 2 : 0);
 }
 
 }  // namespace gemm_fp8

@@ -27,6 +27,7 @@ struct FP8GemmArgs {
   int* err;
   float* partial = nullptr;  // split-K scratch (fp8_gemm_scratch_bytes); null = no split
   int max_splits = 1;
+  bool ue8m0 = false;        // every scale is a power of two: block-scaled tensor-core MMA
 };
 struct FP8GemmPlan {
   int bn;

@@ -77,15 +77,17 @@ def bench_sparse_mla(T=256, K=2048, P=65664, splits=1, impl=0, locality=0.0, **_
             "gather_gbs": gather / ms / 1e6, "peaks": pk["source"]}
 
 
-def bench_fp8_gemm(M=1024, N=36864, K=7168, **_):
+def bench_fp8_gemm(M=1024, N=36864, K=7168, ue8m0=False, **_):
+    """Power-of-two block scales (the checkpoint convention); ``ue8m0`` picks the
+    block-scaled tensor-core path, otherwise the per-K-block FP32 promotion."""
     dev = "cuda"
     x = torch.randn(M, K, device=dev).bfloat16()
     w, s = quantize_weight_blocks(torch.randn(N, K, device=dev) * 0.02)
     q, s_t = ops.quantize_act(x)
     out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
-    ms = time_fn(lambda: ops.fp8_gemm(q, s_t, w, s, out=out))
+    ms = time_fn(lambda: ops.fp8_gemm(q, s_t, w, s, out=out, ue8m0=ue8m0))
     flops = 2.0 * M * N * K
-    return {"op": "fp8_gemm", "M": M, "N": N, "K": K, "ms": ms, "tflops": flops / ms / 1e9,
+    return {"op": "fp8_gemm", "M": M, "N": N, "K": K, "ue8m0": ue8m0, "ms": ms, "tflops": flops / ms / 1e9,
             "bytes_gbs": (N * K + M * K + M * N * 2) / ms / 1e6}
 
 
@@ -169,12 +171,13 @@ def main():
     p.add_argument("--M", type=int, default=1024)
     p.add_argument("--N", type=int, default=36864)
     p.add_argument("--Kdim", type=int, default=7168)
+    p.add_argument("--block-scaled", action="store_true", help="fp8_gemm: block-scaled (UE8M0) tensor-core path")
     a = p.parse_args()
     names = list(OPS) if a.op == "all" else a.op.split(",")
     for name in names:
         kw = dict(T=a.T, K=a.K, P=a.P, splits=a.splits, impl=a.impl, locality=a.locality)
         if name == "fp8_gemm":
-            kw = dict(M=a.M, N=a.N, K=a.Kdim)
+            kw = dict(M=a.M, N=a.N, K=a.Kdim, ue8m0=a.block_scaled)
         if name in ("ag_gemm", "rs_gemm"):
             kw = dict(M=a.M, N=a.N, Kdim=a.Kdim)
         if name == "topk":

@@ -33,6 +33,11 @@ class Linear:
 
     weight: torch.Tensor
     scales: torch.Tensor | None = None
+    # Power-of-two block scales may take the block-scaled tensor-core MMA
+    # (ops.fp8_gemm ue8m0=True).  Off by default: on B200 it measured at parity
+    # with the FP32-promotion kernel for 128 x 224 tiles and slower for 128 x 256
+    # tiles with short K (one TMEM accumulator), both being operand-feed bound.
+    ue8m0: bool = False
 
     @property
     def out_features(self) -> int:
@@ -46,8 +51,8 @@ class Linear:
             return y if residual is None else (y.float() + residual.float()).bfloat16()
         if quantized is not None:
             q, s_t = quantized
-            return ops.fp8_gemm(q, s_t, self.weight, self.scales, out=out, residual=residual)
-        return ops.fp8_linear(x, self.weight, self.scales, out=out, residual=residual)
+            return ops.fp8_gemm(q, s_t, self.weight, self.scales, out=out, residual=residual, ue8m0=self.ue8m0)
+        return ops.fp8_linear(x, self.weight, self.scales, out=out, residual=residual, ue8m0=self.ue8m0)
 
 
 def load_linear(source, stem: str, *, device, dtype: str) -> Linear:

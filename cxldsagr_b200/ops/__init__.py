@@ -78,8 +78,20 @@ def quantize_index(x, scale_fmt="ue8m0"):
 
 
 # ----------------------------------------------------------------- gemms
-def fp8_gemm(q, s_t, weight, w_scales, *, out=None, residual=None):
-    """BF16 [M,N] = dequant(q, s_t) @ dequant(weight, w_scales)^T (+ residual)."""
+def is_ue8m0(scales) -> bool:
+    """True when every scale is a positive power of two (UE8M0-representable)."""
+    s = scales.float()
+    return bool(torch.all(s > 0) and torch.equal(s, torch.exp2(torch.round(torch.log2(s)))))
+
+
+def fp8_gemm(q, s_t, weight, w_scales, *, out=None, residual=None, ue8m0: bool = False):
+    """BF16 [M,N] = dequant(q, s_t) @ dequant(weight, w_scales)^T (+ residual).
+
+    ``ue8m0``: the weight scales are powers of two (``is_ue8m0``); the
+    activation scales always are (``quantize_act``).  The tensor core then
+    applies both scales itself (block-scaled MMA) instead of the kernel
+    promoting every 128-wide K block in FP32.
+    """
     if not _cuda(q):
         a = reference.dequantize_act(q, s_t.t())
         res = a @ reference.dequantize_weight(weight, w_scales).T
@@ -88,11 +100,11 @@ def fp8_gemm(q, s_t, weight, w_scales, *, out=None, residual=None):
         return res.to(torch.bfloat16)
     M, N = q.shape[0], weight.shape[0]
     out = torch.empty((M, N), dtype=torch.bfloat16, device=q.device) if out is None else out
-    lib().fp8_gemm(q, s_t, weight, w_scales, out, residual)
+    lib().fp8_gemm(q, s_t, weight, w_scales, out, residual, bool(ue8m0))
     return out
 
 
-def fp8_linear(x, weight, w_scales, *, out=None, residual=None):
+def fp8_linear(x, weight, w_scales, *, out=None, residual=None, ue8m0: bool = False):
     """Checkpoint FP8 linear: quantise x 1x128 (UE8M0), block-scaled GEMM -> BF16."""
     x2 = x.reshape(-1, x.shape[-1])
     if not _cuda(x):
@@ -101,7 +113,8 @@ def fp8_linear(x, weight, w_scales, *, out=None, residual=None):
             res = (res.float() + residual.float()).bfloat16()
         return res.reshape(*x.shape[:-1], weight.shape[0])
     q, s_t = quantize_act(x2.contiguous())
-    return fp8_gemm(q, s_t, weight, w_scales, out=out, residual=residual).reshape(*x.shape[:-1], weight.shape[0])
+    return fp8_gemm(q, s_t, weight, w_scales, out=out, residual=residual,
+                    ue8m0=ue8m0).reshape(*x.shape[:-1], weight.shape[0])
 
 
 def linear(x, weight, scales=None):

@@ -86,6 +86,24 @@ def test_fp8_gemm(M, N, K):
     assert rel_err(got.cpu(), want) < 2e-2
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 576, 7168), (128, 1536, 7168), (200, 7168, 2048), (1024, 2240, 7168),
+                                   (77, 130, 256), (128, 7168, 18432), (1024, 36864, 1024), (1024, 7168, 4096),
+                                   (640, 7168, 2048), (1024, 18432, 7168)])
+def test_fp8_gemm_block_scaled(M, N, K):
+    """Power-of-two scales through the block-scaled MMA (tcgen05 kind::mxf8f6f4.block_scale):
+    every tile width (256 with one accumulator, 224 and 128 with two) and split-K."""
+    torch.manual_seed(6)
+    x = torch.randn(M, K, device=DEV).bfloat16()
+    w, s = quantize_weight_blocks(torch.randn(N, K, device=DEV) * 0.02)
+    assert ops.is_ue8m0(s)
+    res = torch.randn(M, N, device=DEV).bfloat16()
+    got = ops.fp8_linear(x, w, s, residual=res, ue8m0=True)
+    want = ref.fp8_linear(x.cpu(), w.cpu(), s.cpu()).float() + res.cpu().float()
+    assert rel_err(got.cpu(), want) < 2e-2
+    promoted = ops.fp8_linear(x, w, s, residual=res)
+    assert rel_err(got.cpu(), promoted.cpu().float()) < 5e-3
+
+
 @pytest.mark.parametrize("M,N,K", [(130, 384, 1024), (128, 7168, 16384), (1024, 7168, 2048)])
 def test_fp8_gemm_residual(M, N, K):
     """Residual fused in the epilogue (no split) and in the split-K reduce."""
