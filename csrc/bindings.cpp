@@ -313,6 +313,7 @@ b200::PoolRecallArgs pool_args(const c10::optional<Tensor>& ids, int64_t hist_en
   a.priority = priority.data_ptr<int64_t>();
   a.P = int(d2h.numel() - 1);
   a.meta = meta.data_ptr<int64_t>();
+  a.meta_words = int(meta.numel());
   a.mark = mark.data_ptr<int>();
   a.host_rows = h2d.numel();
   a.miss_list = miss_list.data_ptr<int64_t>();

@@ -79,7 +79,8 @@ struct PoolRecallArgs {
   int64_t* d2h = nullptr;        // [P+1]
   int64_t* priority = nullptr;   // [P+1]
   int P = 0;                     // slots (excluding the sentinel)
-  int64_t* meta = nullptr;       // [8]: clock, epoch, miss count, overflow
+  int64_t* meta = nullptr;       // [meta_words]: clock, epoch, miss count, overflow, ..., selection scratch
+  int meta_words = 0;
   int* mark = nullptr;           // [host_rows] epoch marks
   int64_t host_rows = 0;
   int64_t* miss_list = nullptr;  // [P+1]

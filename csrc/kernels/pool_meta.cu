@@ -113,55 +113,140 @@ __device__ __forceinline__ int block_scan(int v, int* s_warp, int& total) {
   return before;
 }
 
-// One CTA.  k = k_host (>= 0) or min(meta[2], max_miss); new_rows = globals (append) or miss_list (recall).
+// Victim selection.  k = k_host (>= 0) or min(meta[2], max_miss) rows,
+// new_rows = globals (append) or miss_list (recall).  Victims are taken in
+// slot order: free slots first; when fewer than k are free, every eligible
+// slot (not stamped in this event) ordered by (stamp, slot).  Two launches:
+// pool_count_kernel counts free / eligible slots per block of slots (and
+// snapshots the event clock and k); pool_select_kernel then places the
+// free-first case from every block in parallel (each block knows how many
+// free slots precede it) and leaves the eviction case to block 0, which runs
+// a radix select of the k-th smallest key over all slots.
 // stats: [2] evicted; the k placed rows are also added to stats[count_slot] when count_slot >= 0.
-__global__ void __launch_bounds__(kSelThreads) pool_select_kernel(
-    int64_t* __restrict__ priority, int64_t* __restrict__ d2h, int* __restrict__ h2d, int P, int64_t* __restrict__ meta,
-    int k_host, int k_limit, const int64_t* __restrict__ new_rows, int64_t* __restrict__ victims, int max_victims,
-    int64_t* __restrict__ stats, int count_slot, int* err) {
-  __shared__ int s_hist[256];
-  __shared__ int s_warp[kSelThreads / 32];
-  __shared__ unsigned long long s_prefix;
-  __shared__ int s_remaining, s_free, s_eligible, s_k;
+constexpr int kSelBlocks = 64;
+constexpr int kMetaSnap = 8;     // meta[8] = clock of the event, meta[9] = k
+constexpr int kMetaCounts = 16;  // meta[16 + 2b] free, meta[17 + 2b] eligible slots of block b
+
+__host__ __device__ inline int sel_blocks(int P) { return P < 1 ? 1 : (P + 1023) / 1024 < kSelBlocks ? (P + 1023) / 1024 : kSelBlocks; }
+
+__global__ void __launch_bounds__(kSelThreads) pool_count_kernel(const int64_t* __restrict__ priority,
+                                                                  const int64_t* __restrict__ d2h, int P,
+                                                                  int64_t* __restrict__ meta, int k_host, int k_limit,
+                                                                  int max_victims) {
+  __shared__ int s_free, s_elig;
+  const int nb = gridDim.x, per = (P + nb - 1) / nb;
+  const int lo = 1 + blockIdx.x * per, hi = min(P + 1, lo + per);
   const int64_t clock = meta[0];
   if (threadIdx.x == 0) {
-    long long k = k_host >= 0 ? k_host : meta[2];
-    if (k > max_victims) {
-      k = max_victims;
-      meta[3] = 1;
-    }
-    if (k_limit >= 0 && k > k_limit) k = k_limit;
-    s_k = int(k);
     s_free = 0;
-    s_eligible = 0;
+    s_elig = 0;
   }
   __syncthreads();
-  // Free / eligible counts (slot 0 is the sentinel).
   int nfree = 0, nelig = 0;
-  for (int s = 1 + threadIdx.x; s <= P; s += blockDim.x) {
+  for (int s = lo + threadIdx.x; s < hi; s += blockDim.x) {
     const uint64_t key = slot_key(priority, d2h, s, clock);
     nfree += key == 0ull;
     nelig += key != ~0ull;
   }
-  atomicAdd(&s_free, nfree);
-  atomicAdd(&s_eligible, nelig);
+  nfree = __reduce_add_sync(0xffffffffu, nfree);
+  nelig = __reduce_add_sync(0xffffffffu, nelig);
+  if ((threadIdx.x & 31) == 0) {
+    atomicAdd(&s_free, nfree);
+    atomicAdd(&s_elig, nelig);
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
-    if (s_eligible < s_k) {
-      meta[3] = 1;
-      record_error(err, kErrPoolOverflow);
-      s_k = s_eligible;
+    meta[kMetaCounts + 2 * blockIdx.x] = s_free;
+    meta[kMetaCounts + 2 * blockIdx.x + 1] = s_elig;
+    if (blockIdx.x == 0) {
+      long long k = k_host >= 0 ? k_host : meta[2];
+      if (k > max_victims) {
+        k = max_victims;
+        meta[3] = 1;
+      }
+      if (k_limit >= 0 && k > k_limit) k = k_limit;
+      meta[kMetaSnap] = clock;
+      meta[kMetaSnap + 1] = k;
     }
-    s_prefix = 0ull;
-    s_remaining = s_k;
+  }
+}
+
+// Evict the old owner of slot s (if any) and map global row g there.
+__device__ __forceinline__ void place(int s, int64_t g, int64_t clock, int* h2d, int64_t* d2h, int64_t* priority,
+                                      int64_t* stats) {
+  const int64_t old = d2h[s];
+  if (old != kMissing) {
+    h2d[old] = kMissing;
+    atomicAdd(u64(&stats[2]), 1ull);
+  }
+  d2h[s] = g;
+  h2d[g] = s;
+  priority[s] = clock;
+}
+
+__global__ void __launch_bounds__(kSelThreads) pool_select_kernel(
+    int64_t* __restrict__ priority, int64_t* __restrict__ d2h, int* __restrict__ h2d, int P, int64_t* __restrict__ meta,
+    const int64_t* __restrict__ new_rows, int64_t* __restrict__ victims, int64_t* __restrict__ stats, int count_slot,
+    int* err) {
+  __shared__ int s_hist[256];
+  __shared__ int s_warp[kSelThreads / 32];
+  __shared__ unsigned long long s_prefix;
+  __shared__ int s_remaining, s_k, s_before, s_free_total;
+  const int nb = gridDim.x, per = (P + nb - 1) / nb;
+  const int64_t clock = meta[kMetaSnap];
+  if (threadIdx.x < 32) {
+    // Totals over all blocks and the free slots of the blocks before this one.
+    int f = 0, e = 0, before = 0;
+    for (int b = threadIdx.x; b < nb; b += 32) {
+      const int fb = int(meta[kMetaCounts + 2 * b]);
+      f += fb;
+      e += int(meta[kMetaCounts + 2 * b + 1]);
+      if (b < int(blockIdx.x)) before += fb;
+    }
+    f = __reduce_add_sync(0xffffffffu, f);
+    e = __reduce_add_sync(0xffffffffu, e);
+    before = __reduce_add_sync(0xffffffffu, before);
+    if (threadIdx.x == 0) {
+      int k = int(meta[kMetaSnap + 1]);
+      if (e < k) {
+        if (blockIdx.x == 0) {
+          meta[3] = 1;
+          record_error(err, kErrPoolOverflow);
+        }
+        k = e;
+      }
+      s_k = k;
+      s_before = before;
+      s_free_total = f;
+    }
   }
   __syncthreads();
   const int k = s_k;
-  uint64_t thr = 0ull;
-  if (k > 0 && s_free < k) {
-    // Radix select of the k-th smallest key (8 passes of 8 bits, most significant first).
+  if (s_free_total >= k) {
+    // Free-first: this block's free slots take ranks before + 0, 1, ... < k.
+    int base = s_before;
+    const int lo = 1 + blockIdx.x * per, hi = min(P + 1, lo + per);
+    for (int s0 = lo; s0 < hi && base < k; s0 += blockDim.x) {
+      const int s = s0 + threadIdx.x;
+      const int is_free = (s < hi && slot_key(priority, d2h, s, clock) == 0ull) ? 1 : 0;
+      int tot;
+      const int p = block_scan(is_free, s_warp, tot);
+      if (is_free && base + p < k) {
+        victims[base + p] = s;
+        place(s, new_rows[base + p], clock, h2d, d2h, priority, stats);
+      }
+      base += tot;
+    }
+  } else if (blockIdx.x == 0) {
+    // Eviction: radix select of the k-th smallest key (8 passes of 8 bits, most
+    // significant first), then every key below it and the first keys equal to it.
+    if (threadIdx.x == 0) {
+      s_prefix = 0ull;
+      s_remaining = k;
+    }
+    __syncthreads();
     uint64_t mask = 0ull;
-    for (int shift = 56; shift >= 0; shift -= 8) {
+    for (int shift = 56; shift >= 0 && k > 0; shift -= 8) {
       for (int b = threadIdx.x; b < 256; b += blockDim.x) s_hist[b] = 0;
       __syncthreads();
       const uint64_t prefix = s_prefix;
@@ -179,43 +264,32 @@ __global__ void __launch_bounds__(kSelThreads) pool_select_kernel(
       mask |= 255ull << shift;
       __syncthreads();
     }
-    thr = s_prefix;
-  }
-  // Victims in slot order: every key < thr, then keys == thr until k.
-  const int need_eq = (k > 0 && s_free < k) ? s_remaining : k;   // free-first case: thr = 0, take k zeros
-  const int n_less = k - need_eq;
-  int base_less = 0, base_eq = 0;
-  for (int s0 = 1; s0 <= P; s0 += blockDim.x) {
-    const int s = s0 + threadIdx.x;
-    uint64_t key = ~0ull;
-    if (s <= P) key = slot_key(priority, d2h, s, clock);
-    const int is_less = (key != ~0ull && key < thr) ? 1 : 0;
-    const int is_eq = (key != ~0ull && key == thr) ? 1 : 0;
-    int tot_less, tot_eq;
-    const int p_less = block_scan(is_less, s_warp, tot_less);
-    const int p_eq = block_scan(is_eq, s_warp, tot_eq);
-    if (is_less && base_less + p_less < n_less) victims[base_less + p_less] = s;
-    if (is_eq && base_eq + p_eq < need_eq) victims[n_less + base_eq + p_eq] = s;
-    base_less += tot_less;
-    base_eq += tot_eq;
-    if (base_less >= n_less && base_eq >= need_eq) break;
-  }
-  __syncthreads();
-  // Evict, map, stamp.
-  for (int j = threadIdx.x; j < k; j += blockDim.x) {
-    const int s = int(victims[j]);
-    const int64_t old = d2h[s];
-    if (old != kMissing) {
-      h2d[old] = kMissing;
-      atomicAdd(u64(&stats[2]), 1ull);
+    const uint64_t thr = s_prefix;
+    const int need_eq = k > 0 ? s_remaining : 0;
+    const int n_less = k - need_eq;
+    int base_less = 0, base_eq = 0;
+    for (int s0 = 1; s0 <= P && k > 0; s0 += blockDim.x) {
+      const int s = s0 + threadIdx.x;
+      uint64_t key = ~0ull;
+      if (s <= P) key = slot_key(priority, d2h, s, clock);
+      const int is_less = (key != ~0ull && key < thr) ? 1 : 0;
+      const int is_eq = (key != ~0ull && key == thr) ? 1 : 0;
+      int tot_less, tot_eq;
+      const int p_less = block_scan(is_less, s_warp, tot_less);
+      const int p_eq = block_scan(is_eq, s_warp, tot_eq);
+      if (is_less && base_less + p_less < n_less) victims[base_less + p_less] = s;
+      if (is_eq && base_eq + p_eq < need_eq) victims[n_less + base_eq + p_eq] = s;
+      base_less += tot_less;
+      base_eq += tot_eq;
+      if (base_less >= n_less && base_eq >= need_eq) break;
     }
-    const int64_t g = new_rows[j];
-    d2h[s] = g;
-    h2d[g] = s;
-    priority[s] = clock;
+    __syncthreads();
+    for (int j = threadIdx.x; j < k; j += blockDim.x)
+      place(int(victims[j]), new_rows[j], clock, h2d, d2h, priority, stats);
   }
-  __syncthreads();
-  if (threadIdx.x == 0) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    // Only block 0 writes meta[0] and meta[2]; every block read the event's
+    // clock and k from the snapshot words.
     meta[0] = clock + 1;
     meta[2] = k;  // the rows actually placed (the gather copies this many)
     priority[0] = kMissing;
@@ -310,9 +384,13 @@ void launch_pool_recall(const PoolRecallArgs& a, cudaStream_t stream) {
 void launch_pool_select(const PoolRecallArgs& a, int k_host, int k_limit, const int64_t* new_rows, int count_slot,
                         cudaStream_t stream) {
   if (count_slot > 7) throw std::invalid_argument("pool select: counter slot out of range");
-  pool_select_kernel<<<1, kSelThreads, 0, stream>>>(a.priority, a.d2h, a.h2d, a.P, a.meta, k_host, k_limit,
-                                                    new_rows ? new_rows : a.miss_list, a.victims, a.max_miss,
-                                                    a.stats, count_slot, a.err);
+  if (a.meta_words < kMetaCounts + 2 * kSelBlocks)
+    throw std::invalid_argument("pool select: meta needs the selection scratch words");
+  const int nb = sel_blocks(a.P);
+  pool_count_kernel<<<nb, kSelThreads, 0, stream>>>(a.priority, a.d2h, a.P, a.meta, k_host, k_limit, a.max_miss);
+  pool_select_kernel<<<nb, kSelThreads, 0, stream>>>(a.priority, a.d2h, a.h2d, a.P, a.meta,
+                                                     new_rows ? new_rows : a.miss_list, a.victims, a.stats,
+                                                     count_slot, a.err);
   cuda_check(cudaGetLastError(), "pool select launch");
 }
 

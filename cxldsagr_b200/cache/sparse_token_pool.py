@@ -41,6 +41,11 @@ def _device(device) -> torch.device:
     return d
 
 
+# int64 words of a layer's device metadata: 8 state words + the victim
+# selection's scratch (2 snapshot words, 6 spare, 2 x 64 per-block counts).
+POOL_META_WORDS = 8 + 8 + 2 * 64
+
+
 @dataclass
 class LayerPool:
     host: torch.Tensor
@@ -49,7 +54,8 @@ class LayerPool:
     d2h: torch.Tensor
     priority: torch.Tensor
     # Device-resident metadata of the native (no host sync) path:
-    # meta = [clock, epoch, miss count, overflow, ...]; mark [NH] epoch marks;
+    # meta = [clock, epoch, miss count, overflow, ...; words 8+ are the victim
+    # selection's scratch (event snapshot and per-block slot counts)]; mark [NH] epoch marks;
     # miss_list / victims [P+1] scratch of one event.
     meta: torch.Tensor = None
     mark: torch.Tensor = None
@@ -129,7 +135,7 @@ class SharedSparseTokenPool:
                 h2d=torch.full((host_capacity,), MISSING, dtype=torch.int32, device=self.device),
                 d2h=torch.full((slots + 1,), MISSING, dtype=torch.int64, device=self.device),
                 priority=priority,
-                meta=torch.zeros(8, dtype=torch.int64, device=self.device),
+                meta=torch.zeros(POOL_META_WORDS, dtype=torch.int64, device=self.device),
                 mark=torch.zeros(host_capacity, dtype=torch.int32, device=self.device),
                 miss_list=torch.zeros(slots + 1, dtype=torch.int64, device=self.device),
                 victims=torch.zeros(slots + 1, dtype=torch.int64, device=self.device),

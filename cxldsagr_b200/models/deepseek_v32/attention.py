@@ -86,9 +86,12 @@ class AttentionRunner:
         ik = a[:, self.ik0:self.ik0 + self.ik_n]
         # KV record straight into its cache row (every row of the chunk).
         with scope("kv_record"):
-            dst = state.kv.destination_rows(T)
-            ops.kv_finish(kv, L, rope, w.kv_norm, cfg.norm_eps, freqs, positions, state.kv.records, dst)
-            state.kv.finish_append(dst)
+            with scope("slots"):
+                dst = state.kv.destination_rows(T)
+            with scope("finish"):
+                ops.kv_finish(kv, L, rope, w.kv_norm, cfg.norm_eps, freqs, positions, state.kv.records, dst)
+            with scope("host_write"):
+                state.kv.finish_append(dst)
             state.last_rows = dst
             if state.dense is not None:
                 # The staged history plus this chunk's records (logical row = staged row).
