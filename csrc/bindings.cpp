@@ -357,6 +357,17 @@ void pool_recall_select(Tensor& h2d, Tensor& d2h, Tensor& priority, Tensor& meta
   b200::launch_pool_select(a, -1, int(k_limit), nullptr, int(count_slot), stream());
 }
 
+// offset[0] = mean of the finite logits of the last min(4, rows) rows over columns [0, cols).
+void echo_hint(const Tensor& logits, int64_t rows, int64_t cols, Tensor& offset) {
+  c10::cuda::CUDAGuard g(logits.device());
+  CHECK_DTYPE(logits, torch::kFloat32); CHECK_DTYPE(offset, torch::kFloat32);
+  TORCH_CHECK(logits.stride(1) == 1 && rows <= logits.size(0) && cols <= logits.size(1), "echo_hint shapes");
+  const int64_t tail = rows < 4 ? rows : 4;
+  if (tail <= 0) return;
+  b200::launch_echo_hint(logits.data_ptr<float>(), logits.stride(0), int(rows - tail), int(tail), int(cols),
+                         offset.data_ptr<float>(), stream());
+}
+
 // pred_ids[c] = c for history rows certainly in some row's top-k (caller pre-fills -1).
 void echo_predict(const Tensor& logits, int64_t rows, int64_t hist_end, const Tensor& offset, int64_t k, Tensor& pred_ids) {
   c10::cuda::CUDAGuard g(logits.device());
@@ -594,6 +605,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("pool_recall_select", &pool_recall_select);
   m.def("pool_map", &pool_map);
   m.def("echo_predict", &echo_predict);
+  m.def("echo_hint", &echo_hint);
   m.def("fp8_gemm_ag", &fp8_gemm_ag);
   m.def("fp8_gemm_rs", &fp8_gemm_rs);
   m.def("p2p_barrier", &p2p_barrier);

@@ -92,6 +92,8 @@ struct PoolRecallArgs {
 void launch_pool_begin(int64_t* meta, cudaStream_t stream);
 void launch_echo_predict(const float* logits, int64_t ld, int rows, int hist_end, const float* offset, int k,
                          int* pred_ids, cudaStream_t stream);
+// out[0] = mean of the finite values of logits rows [row0, row0 + rows), columns [0, cols).
+void launch_echo_hint(const float* logits, int64_t ld, int row0, int rows, int cols, float* out, cudaStream_t stream);
 void launch_pool_recall(const PoolRecallArgs& a, cudaStream_t stream);
 void launch_pool_select(const PoolRecallArgs& a, int k_host, int k_limit, const int64_t* new_rows, int count_slot,
                         cudaStream_t stream);

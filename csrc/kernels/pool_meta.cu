@@ -362,6 +362,51 @@ __global__ void __launch_bounds__(512) echo_predict_kernel(const float* __restri
 
 }  // namespace
 
+// ECHO offset[0] hint: mean of the finite logits in rows [row0, row0 + rows),
+// columns [0, cols) (the reference's prefetch hint over the last four query
+// rows).  One CTA, fixed reduction order, so the hint is deterministic.
+__global__ void __launch_bounds__(1024) echo_hint_kernel(const float* __restrict__ logits, int64_t ld, int row0,
+                                                         int rows, int cols, float* __restrict__ out) {
+  __shared__ float s_sum[32];
+  __shared__ int s_cnt[32];
+  float sum = 0.f;
+  int cnt = 0;
+  for (int r = 0; r < rows; ++r) {
+    const float* row = logits + int64_t(row0 + r) * ld;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+      const float v = row[c];
+      if (isfinite(v)) {
+        sum += v;
+        ++cnt;
+      }
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    s_sum[threadIdx.x >> 5] = sum;
+    s_cnt[threadIdx.x >> 5] = cnt;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int nw = blockDim.x >> 5;
+    sum = threadIdx.x < nw ? s_sum[threadIdx.x] : 0.f;
+    cnt = threadIdx.x < nw ? s_cnt[threadIdx.x] : 0;
+    for (int o = 16; o > 0; o >>= 1) {
+      sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+    }
+    if (threadIdx.x == 0) out[0] = sum / float(cnt > 1 ? cnt : 1);
+  }
+}
+
+void launch_echo_hint(const float* logits, int64_t ld, int row0, int rows, int cols, float* out, cudaStream_t stream) {
+  echo_hint_kernel<<<1, 1024, 0, stream>>>(logits, ld, row0, rows, cols, out);
+  cuda_check(cudaGetLastError(), "echo hint launch");
+}
+
 void launch_echo_predict(const float* logits, int64_t ld, int rows, int hist_end, const float* offset, int k,
                          int* pred_ids, cudaStream_t stream) {
   if (rows <= 0 || hist_end <= 0) return;

@@ -218,7 +218,10 @@ class AttentionRunner:
 
     def _update_hints(self, state, logits, values, pos, end):
         off = state.index.offset
-        off[0] = ops.reference.prefetch_hint(logits[:, :end])
+        if logits.is_cuda:
+            ops.lib().echo_hint(logits, logits.shape[0], end, off)  # one kernel, no host sync
+        else:
+            off[0] = ops.reference.prefetch_hint(logits[:, :end])
         if logits.shape[0] == 1 and end >= 32768:
             off[1] = ops.reference.decode_hint(off[1], values[0, -1])
 

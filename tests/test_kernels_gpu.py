@@ -424,3 +424,16 @@ def test_echo_predictor_matches_reference(rows, hist, k):
     got = torch.nonzero(pred >= 0).flatten()
     assert torch.equal(got, want)
     assert bool((pred[got] == got.int()).all())
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 700), (3, 5000), (16, 70000)])
+def test_echo_hint_matches_reference(rows, cols):
+    """Device ECHO offset[0] hint = mean of the finite logits of the last min(4, Q) rows."""
+    torch.manual_seed(24)
+    logits = torch.randn(rows, cols + 9, device=DEV) * 2 + 1
+    logits[:, 3] = -torch.inf
+    logits[-1, 7] = torch.nan
+    offset = torch.zeros(16, device=DEV)
+    ops.lib().echo_hint(logits, rows, cols, offset)
+    want = ref.prefetch_hint(logits[:, :cols].cpu())
+    assert abs(float(offset[0]) - float(want)) < 1e-4 * max(1.0, abs(float(want)))
