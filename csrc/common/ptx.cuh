@@ -344,6 +344,16 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// (a0, a1) += (x0, x1) * (w0, w1) with one packed FP32x2 FMA (sm_100); each
+// lane is an ordinary round-to-nearest fmaf.
+__device__ __forceinline__ void fma_f32x2(float& a0, float& a1, float x0, float x1, float w0, float w1) {
+  asm("{\n\t.reg .b64 x, w, a;\n\t"
+      "mov.b64 x, {%2, %3};\n\tmov.b64 w, {%4, %5};\n\tmov.b64 a, {%0, %1};\n\t"
+      "fma.rn.f32x2 a, x, w, a;\n\tmov.b64 {%0, %1}, a;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(x0), "f"(x1), "f"(w0), "f"(w1));
+}
+
 // 2^x by the MUFU ex2 instruction (approximate, denormal results flushed to
 // zero); -inf gives 0.
 __device__ __forceinline__ float ex2_approx(float x) {

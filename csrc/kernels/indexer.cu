@@ -197,7 +197,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         float out[2];
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-          float acc = 0.f;
+          // Two packed FP32x2 accumulators (even / odd heads of each quad);
+          // the ReLU stays scalar (there is no packed max).
+          float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
           const float4* wv = reinterpret_cast<const float4*>(s.w[ew][j]);
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
@@ -207,13 +209,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int h4 = 0; h4 < 8; ++h4) {
               const float4 ww = wv[c * 8 + h4];
-              acc = fmaf(fmaxf(__uint_as_float(r[4 * h4 + 0]), 0.f), ww.x, acc);
-              acc = fmaf(fmaxf(__uint_as_float(r[4 * h4 + 1]), 0.f), ww.y, acc);
-              acc = fmaf(fmaxf(__uint_as_float(r[4 * h4 + 2]), 0.f), ww.z, acc);
-              acc = fmaf(fmaxf(__uint_as_float(r[4 * h4 + 3]), 0.f), ww.w, acc);
+              fma_f32x2(a0, a1, fmaxf(__uint_as_float(r[4 * h4 + 0]), 0.f), fmaxf(__uint_as_float(r[4 * h4 + 1]), 0.f),
+                        ww.x, ww.y);
+              fma_f32x2(b0, b1, fmaxf(__uint_as_float(r[4 * h4 + 2]), 0.f), fmaxf(__uint_as_float(r[4 * h4 + 3]), 0.f),
+                        ww.z, ww.w);
             }
           }
-          out[j] = acc * ks;
+          out[j] = ((a0 + a1) + (b0 + b1)) * ks;
         }
         tc_fence_before();
         __syncwarp();

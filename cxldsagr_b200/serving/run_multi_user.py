@@ -39,6 +39,8 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--num-users", type=int, default=8)
     p.add_argument("--count", type=int, default=16)
     p.add_argument("--max-revisits", type=int)
+    p.add_argument("--sampling", choices=("weighted", "sequential"), default="weighted",
+                   help="user order: heat-weighted draws, or every user in turn (rounds)")
     p.add_argument("--seed", type=int, default=42)
     p.add_argument("--history-tokens", type=int, default=16384, help="complete fixed prefix incl. instruction")
     p.add_argument("--candidate-tokens", type=int, default=1024, help="complete changing candidate suffix")
@@ -64,6 +66,8 @@ def validate_args(args, parser) -> None:
         parser.error("--seed must be nonnegative")
     if args.max_revisits is not None and args.max_revisits < 0:
         parser.error("--max-revisits must be nonnegative")
+    if args.sampling == "sequential" and args.max_revisits is not None:
+        parser.error("--sampling sequential does not take --max-revisits")
     if (args.model_path is None) == (not args.random_init):
         parser.error("give exactly one of --model-path or --random-init")
     if args.resource_mode == "fixed-pools":
@@ -100,7 +104,8 @@ def build_requests(args):
     wl = build_workload(WorkloadConfig(
         "deepseek_v32", args.num_users, args.count, history_tokens=args.history_tokens,
         candidate_tokens=args.candidate_tokens, seed=args.seed, max_revisits=args.max_revisits,
-        context_limit=args.context_limit, heat_path=str(args.heat_curves) if args.heat_curves else None),
+        context_limit=args.context_limit, heat_path=str(args.heat_curves) if args.heat_curves else None,
+        sampling=args.sampling),
         tokenizer=args.tokenizer)
     return wl
 
