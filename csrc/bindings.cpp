@@ -259,6 +259,13 @@ void sparse_mla(const Tensor& q, const Tensor& kv, const Tensor& ids, double sca
   else b200::launch_sparse_mla_split(a, int(splits), sp, stream());
 }
 
+Tensor topk_trace(int64_t row) {
+  Tensor t = torch::empty({16}, torch::kInt64);
+  if (row >= -1) b200::set_topk_trace_row(int(row));
+  b200::copy_topk_trace(reinterpret_cast<unsigned long long*>(t.data_ptr<int64_t>()));
+  return t;
+}
+
 Tensor sparse_mla_trace() {
   Tensor t = torch::empty({4, 65, 16}, torch::kInt64);
   b200::copy_sparse_mla_trace(reinterpret_cast<unsigned long long*>(t.data_ptr<int64_t>()));
@@ -598,6 +605,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sparse_mla", &sparse_mla);
   m.def("sparse_mla_scratch_bytes", &sparse_mla_scratch_bytes);
   m.def("sparse_mla_trace", &sparse_mla_trace);
+  m.def("topk_trace", &topk_trace);
   m.def("fp8_gemm_splits", &fp8_gemm_splits);
   m.def("gather_rows", &gather_rows);
   m.def("pool_recall", &pool_recall);

@@ -56,11 +56,12 @@ void launch_gather_rows(const uint8_t* host, uint8_t* records, const int64_t* ho
                         int64_t host_rows, int64_t pool_rows, int* err, cudaStream_t stream) {
   if (n <= 0) return;
   if (row_bytes % 16) throw std::invalid_argument("gather_rows: row bytes must be a multiple of 16");
-  // The gather sits on the critical path of a recall (attention waits for it):
-  // up to 2 CTAs per SM of 256 threads, each with kUnroll loads in flight.
+  // At most 64 CTAs of 256 threads, each thread with kUnroll 16-byte loads in
+  // flight: on B200 that already saturates PCIe (49 GB/s of a 55 GB/s pinned
+  // copy for 39K scattered rows, as with 2 CTAs per SM) and leaves the other
+  // SMs free, so a fetch on a side stream overlaps another layer's attention.
   const int64_t chunks = int64_t(n) * (row_bytes / 16);
-  const int blocks = int(std::max<int64_t>(1, std::min<int64_t>((chunks + 256 * kUnroll - 1) / (256 * kUnroll),
-                                                              2 * sm_count())));
+  const int blocks = int(std::max<int64_t>(1, std::min<int64_t>((chunks + 256 * kUnroll - 1) / (256 * kUnroll), 64)));
   gather_rows_kernel<<<blocks, 256, 0, stream>>>(host, records, host_ids, slots, n, device_count,
                                                  row_bytes, host_rows, pool_rows, err);
   cuda_check(cudaGetLastError(), "gather_rows launch");

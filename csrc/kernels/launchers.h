@@ -229,6 +229,9 @@ size_t sparse_mla_scratch_bytes(int T, int H, int splits);
 void launch_sparse_mla_split(const MLAArgs& a, int splits, float* scratch, cudaStream_t stream);
 // tcgen05 version (2-CTA clusters exchanging partial S through DSMEM).
 void launch_sparse_mla_tc(const MLAArgs& a, int splits, float* scratch, cudaStream_t stream, int dbg = 0);
+// Top-k debug timeline: clock64 at the phase boundaries of one row (-1 = off).
+void set_topk_trace_row(int row);
+void copy_topk_trace(unsigned long long* host);
 // Per-tile event clocks of the last launch with dbg bit 64 ([4][65][16] u64).
 void copy_sparse_mla_trace(unsigned long long* host);
 // out[t,h,:] = sum_s exp(lse_s - lse) * part_o[s,t,h,:]; lse = logsumexp_s lse_s.

@@ -24,23 +24,16 @@ constexpr int kMaxK = 2048;
 constexpr int kThreads2 = 1024;
 constexpr int kBins = 4096;       // 12-bit first-level histogram
 constexpr int kSecCap = 6144;     // threshold-bin candidates staged in shared memory
+// Debug: clock64 at the phase boundaries of row g_topk_trace_row (-1 = off),
+// read back by copy_topk_trace: start, level passes (up to 3), collect,
+// staged levels, select, sort, end.
+__device__ int g_topk_trace_row = -1;
+__device__ unsigned long long g_topk_trace[16];
 
 __device__ __forceinline__ uint32_t order_key(float f) {
   const uint32_t u = __float_as_uint(f);
   if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0u;  // NaN sorts below everything
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
-// Warp-aggregated append: returns this lane's slot (valid only when `take`).
-__device__ __forceinline__ uint32_t append_warp(uint32_t* counter, bool take) {
-  const uint32_t ballot = __ballot_sync(0xffffffffu, take);
-  if (!ballot) return 0;
-  const int lane = threadIdx.x % 32;
-  const int leader = __ffs(ballot) - 1;
-  uint32_t base = 0;
-  if (lane == leader) base = atomicAdd(counter, uint32_t(__popc(ballot)));
-  base = __shfl_sync(0xffffffffu, base, leader);
-  return base + __popc(ballot & ((1u << lane) - 1u));
 }
 
 __device__ __forceinline__ float key_value(uint32_t k) {
@@ -164,7 +157,7 @@ __global__ void __launch_bounds__(kThreads) topk_kernel(const float* __restrict_
   for (int size = 2; size <= n2; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
       for (int i = threadIdx.x; i < n2 / 2; i += kThreads) {
-        const int lo = 2 * stride * (i / stride) + (i % stride);
+        const int lo = 2 * i - (i & (stride - 1));  // 2 stride (i / stride) + i % stride, stride = 2^m
         const int hi = lo + stride;
         const bool desc = ((lo & size) == 0);
         const uint64_t a = cand[lo], b = cand[hi];
@@ -193,13 +186,23 @@ __global__ void __launch_bounds__(kThreads) topk_kernel(const float* __restrict_
 }
 
 
-// Histogram-select variant: a 12-bit histogram pass finds the bin holding the
-// k-th key (refined by further 12- and 8-bit passes only while that bin holds
-// more keys than fit in shared memory); a collect pass appends every key of a
-// higher bin (all selected) and stages the threshold bin's keys in shared
-// memory, where a bitonic sort picks the remaining ones (larger key first,
-// then smaller index).  Rows whose threshold is an exact value shared by more
-// than kSecCap keys set *overflow and are finished by the multi-pass kernel.
+// Histogram-select variant (one CTA of 1024 threads per row):
+//  1. radix levels of 12, 12 and 8 bits over the row's order keys find the
+//     bin holding the take-th largest key, stopping as soon as that bin fits
+//     the shared-memory stage (kSecCap keys);
+//  2. one collect pass appends every key of a higher bin to the result (all
+//     selected) and stages the threshold bin's (key, ~index) composites;
+//  3. radix levels over the staged composites (the key bits below the prefix,
+//     then the index bits) find the exact last composite taken; composites
+//     are distinct, so ties are settled by the smaller index with no special
+//     case, and the stage is never sorted;
+//  4. a bitonic sort of the take (<= 2048) results orders them (larger key,
+//     then smaller index).
+// Row passes read 4 floats per lane per step with two steps in flight, and
+// collect with one warp scan per step instead of a warp vote per element.
+// Rows whose threshold bin still exceeds kSecCap after 32 key bits (one
+// value shared by > kSecCap keys) set *overflow and are finished by the
+// multi-pass kernel.
 __global__ void __launch_bounds__(kThreads2) topk2_kernel(const float* __restrict__ scores, int64_t ld, int N,
                                                           int k, int causal_start, float* __restrict__ values,
                                                           int* __restrict__ ids, int* __restrict__ overflow,
@@ -207,62 +210,148 @@ __global__ void __launch_bounds__(kThreads2) topk2_kernel(const float* __restric
   extern __shared__ uint8_t dyn[];
   uint32_t* hist = reinterpret_cast<uint32_t*>(dyn);                      // kBins
   uint64_t* cand = reinterpret_cast<uint64_t*>(dyn + kBins * 4);          // kMaxK
-  uint64_t* sec = cand + kMaxK;                                           // kSecCap (padded to pow2 in sort)
-  __shared__ uint32_t s_count, s_sec, s_bstar, s_above;
+  uint64_t* sec = cand + kMaxK;                                           // kSecCap
+  __shared__ unsigned long long s_pack;  // collect counters: results (low 32), staged (high 32)
+  __shared__ uint32_t s_bstar, s_above, s_in;
   __shared__ uint32_t warp_sum[kThreads2 / 32];
   const int r = blockIdx.x;
   const float* row = scores + int64_t(r) * ld;
   const int row_end = causal_start >= 0 ? min(N, causal_start + r + 1) : N;
   const int take = min(k, row_end);
   const bool vec = ((reinterpret_cast<uintptr_t>(row) & 15) == 0);
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid % 32, wid = tid / 32;
+  const bool tracing = r == g_topk_trace_row;
+  int tp = 0;
+  auto mark = [&]() {
+    if (tracing && tid == 0 && tp < 16) g_topk_trace[tp] = clock64();
+    ++tp;
+  };
+  mark();
   if (tid == 0) {
-    s_count = 0;
-    s_sec = 0;
+    s_pack = 0ull;
     s_bstar = 0;
     s_above = 0;
+    s_in = 0;
   }
-  for (int i = tid; i < kBins; i += kThreads2) hist[i] = 0;
   __syncthreads();
-  // Warp-uniform row walk: every lane runs the same trip count (inactive lanes
-  // pass valid=false) so warp collectives inside fn are safe.
-  auto for_row = [&](auto&& fn) {
-    if (vec) {
-      const int n4 = row_end / 4;
-      const int trips = (n4 + kThreads2 - 1) / kThreads2;
-      for (int t = 0; t < trips; ++t) {
-        const int i = t * kThreads2 + tid;
-        const bool ok = i < n4;
-        float4 v = ok ? reinterpret_cast<const float4*>(row)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-        fn(4 * i, v.x, ok);
-        fn(4 * i + 1, v.y, ok);
-        fn(4 * i + 2, v.z, ok);
-        fn(4 * i + 3, v.w, ok);
+
+  // Row walk in steps of 4 consecutive floats per lane (element 4i+j of the
+  // row), kInflight steps' loads in flight (a single row pass is otherwise
+  // bound by the load latency).  Every lane runs the same trip count
+  // (invalid elements have ok = false) so warp collectives in fn are safe.
+  constexpr int kInflight = 4;
+  auto for_row4 = [&](auto&& fn) {
+    const int n4 = vec ? row_end / 4 : 0;
+    const int steps = (n4 + kThreads2 - 1) / kThreads2;
+    for (int t = 0; t < steps; t += kInflight) {
+      float4 v[kInflight];
+#pragma unroll
+      for (int u = 0; u < kInflight; ++u) {
+        const int i = (t + u) * kThreads2 + tid;
+        v[u] = (t + u < steps && i < n4) ? __ldg(reinterpret_cast<const float4*>(row) + i)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      const int i = n4 * 4 + tid;  // tail (< 4 elements)
-      const bool ok = i < row_end && tid < 4;
-      fn(i, ok ? row[i] : 0.f, ok);
-    } else {
-      const int trips = (row_end + kThreads2 - 1) / kThreads2;
-      for (int t = 0; t < trips; ++t) {
-        const int i = t * kThreads2 + tid;
-        const bool ok = i < row_end;
-        fn(i, ok ? row[i] : 0.f, ok);
+#pragma unroll
+      for (int u = 0; u < kInflight; ++u) {
+        if (t + u >= steps) break;  // uniform
+        const int i = (t + u) * kThreads2 + tid;
+        const float f[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+        fn(4 * i, f, i < n4);
       }
+    }
+    // Tail (and unaligned rows): scalar elements, 4 per lane per step.
+    const int t0 = n4 * 4;
+    const int rest = row_end - t0;
+    const int steps_t = (rest + 4 * kThreads2 - 1) / (4 * kThreads2);
+    for (int t = 0; t < steps_t; ++t) {
+      const int e0 = t0 + (t * kThreads2 + tid) * 4;
+      float f[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) f[j] = e0 + j < row_end ? row[e0 + j] : 0.f;
+      fn(e0, f, e0 < row_end);
     }
   };
   auto composite = [](uint32_t key, int i) { return (uint64_t(key) << 32) | uint32_t(0xFFFFFFFFu - uint32_t(i)); };
-  const bool take_all = take >= row_end;
-  if (take_all) {
-    for_row([&](int i, float f, bool ok) {
-      const uint32_t pos = append_warp(&s_count, ok);
-      if (ok && pos < uint32_t(kMaxK)) cand[pos] = composite(order_key(f), i);
+  auto hist_add = [&](uint32_t bin) {
+    if (bin != 0xFFFFFFFFu) atomicAdd(&hist[bin], 1u);
+  };
+  // Append this lane's selected elements to cand / sec with one warp scan of
+  // the packed per-lane counts and one shared atomic per warp.
+  auto collect = [&](const uint32_t (&keys)[4], int e0, uint32_t gmask, uint32_t smask) {
+    const uint32_t mine = uint32_t(__popc(gmask)) | (uint32_t(__popc(smask)) << 16);
+    uint32_t incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+    if (total == 0) return;
+    unsigned long long base = 0;
+    if (lane == 31)
+      base = atomicAdd(&s_pack, (unsigned long long)(total & 0xFFFFu) | ((unsigned long long)(total >> 16) << 32));
+    base = __shfl_sync(0xffffffffu, base, 31);
+    uint32_t pg = uint32_t(base & 0xFFFFFFFFull) + ((incl - mine) & 0xFFFFu);
+    uint32_t ps = uint32_t(base >> 32) + ((incl - mine) >> 16);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (gmask >> j & 1u) {
+        if (pg < uint32_t(kMaxK)) cand[pg] = composite(keys[j], e0 + j);
+        ++pg;
+      }
+      if (smask >> j & 1u) {
+        if (ps < uint32_t(kSecCap)) sec[ps] = composite(keys[j], e0 + j);
+        ++ps;
+      }
+    }
+  };
+  // Suffix search over hist[0, nbins): the bin holding rank `rank` counting
+  // from the top; returns it in s_bstar, keys above it in s_above (plus
+  // `carry`), keys in it in s_in.
+  auto find_bin = [&](int nbins, uint32_t rank, uint32_t carry) {
+    uint32_t local[4], lsum = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      local[j] = 4 * tid + j < nbins ? hist[4 * tid + j] : 0u;
+      lsum += local[j];
+    }
+    uint32_t v = lsum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t n = __shfl_down_sync(0xffffffffu, v, o);
+      if (lane + o < 32) v += n;
+    }
+    if (lane == 0) warp_sum[wid] = v;
+    __syncthreads();
+    uint32_t higher = 0;
+    for (int j = wid + 1; j < kThreads2 / 32; ++j) higher += warp_sum[j];
+    uint32_t above = carry + higher + v - lsum;  // keys above bin 4 tid + 3
+#pragma unroll
+    for (int j = 3; j >= 0; --j) {
+      if (above < rank && above + local[j] >= rank) {
+        s_bstar = 4 * tid + j;
+        s_above = above;
+        s_in = local[j];
+      }
+      above += local[j];
+    }
+    __syncthreads();
+  };
+
+  if (take >= row_end) {
+    // Every valid element is taken (row_end <= k <= kMaxK).
+    for_row4([&](int e0, const float (&f)[4], bool ok) {
+      uint32_t keys[4], g = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        keys[j] = order_key(f[j]);
+        if (ok && e0 + j < row_end) g |= 1u << j;
+      }
+      collect(keys, e0, g, 0u);
     });
   } else {
-    // Radix levels of 12, 12 and 8 bits.  After each level the bin holding
-    // the k-th key becomes the prefix; refinement stops as soon as that bin
-    // fits the shared-memory stage (clustered logits need the 2nd level).
-    uint32_t prefix = 0, above_total = 0;
+    // 1. Levels over the row until the threshold bin fits the stage.
+    uint32_t prefix = 0, above_total = 0, in_bin = 0;
     int pbits = 0;
     const int level_bits[3] = {12, 12, 8};
     for (int level = 0; level < 3; ++level) {
@@ -270,120 +359,169 @@ __global__ void __launch_bounds__(kThreads2) topk2_kernel(const float* __restric
       const int shift = 32 - pbits - lb;
       for (int i = tid; i < kBins; i += kThreads2) hist[i] = 0;
       __syncthreads();
-      for_row([&](int, float f, bool ok) {
-        const uint32_t key = order_key(f);
-        if (ok && (pbits == 0 || (key >> (32 - pbits)) == prefix))
-          atomicAdd(&hist[(key >> shift) & ((1u << lb) - 1u)], 1u);
+      for_row4([&](int e0, const float (&f)[4], bool ok) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t key = order_key(f[j]);
+          const bool in = ok && e0 + j < row_end && (pbits == 0 || (key >> (32 - pbits)) == prefix);
+          hist_add(in ? (key >> shift) & ((1u << lb) - 1u) : 0xFFFFFFFFu);
+        }
       });
       __syncthreads();
-      // Suffix counts: thread t owns bins [4t, 4t+4).
-      uint32_t local[4], lsum = 0;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        local[j] = hist[4 * tid + j];
-        lsum += local[j];
-      }
-      uint32_t v = lsum;
-      const int lane = tid % 32, w = tid / 32;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t n = __shfl_down_sync(0xffffffffu, v, o);
-        if (lane + o < 32) v += n;
-      }
-      if (lane == 0) warp_sum[w] = v;
-      __syncthreads();
-      uint32_t higher = 0;
-      for (int j = w + 1; j < kThreads2 / 32; ++j) higher += warp_sum[j];
-      uint32_t above = above_total + higher + v - lsum;  // keys above bin 4t+3 (incl. earlier levels)
-#pragma unroll
-      for (int j = 3; j >= 0; --j) {
-        const uint32_t b = 4 * tid + j;
-        if (above < uint32_t(take) && above + local[j] >= uint32_t(take)) {
-          s_bstar = b;
-          s_above = above;
-          s_sec = local[j];  // keys in the threshold bin
-        }
-        above += local[j];
-      }
-      __syncthreads();
+      find_bin(1 << lb, uint32_t(take), above_total);
+      mark();
       prefix = (pbits == 0 ? 0u : (prefix << lb)) | s_bstar;
       pbits += lb;
       above_total = s_above;
-      const uint32_t in_bin = s_sec;
+      in_bin = s_in;
       __syncthreads();
       if (in_bin <= uint32_t(kSecCap) || pbits == 32) break;
     }
-    if (tid == 0) {
-      s_bstar = prefix;
-      s_sec = 0;
-    }
-    __syncthreads();
-    const int pshift = 32 - pbits;
-    const uint32_t bstar = s_bstar;
-    for_row([&](int i, float f, bool ok) {
-      const uint32_t key = order_key(f);
-      const uint32_t b = pshift >= 32 ? 0u : (key >> pshift);
-      const bool gt = ok && b > bstar, eq = ok && b == bstar;
-      const uint32_t pg = append_warp(&s_count, gt);
-      const uint32_t pe = append_warp(&s_sec, eq);
-      if (gt && pg < uint32_t(kMaxK)) cand[pg] = composite(key, i);
-      if (eq && pe < uint32_t(kSecCap)) sec[pe] = composite(key, i);
-    });
-    __syncthreads();
-    const uint32_t nsec = s_sec;
-    if (nsec > uint32_t(kSecCap)) {  // pathological: finished by the multi-pass kernel
+    if (in_bin > uint32_t(kSecCap)) {  // one value shared by too many keys: multi-pass kernel
       if (tid == 0) overflow[r] = 1;
       return;
     }
-    // sort the threshold-bin keys, take the first (take - above)
-    int n2 = 1;
-    while (n2 < int(nsec)) n2 <<= 1;
-    for (int i = nsec + tid; i < n2; i += kThreads2) sec[i] = 0ull;
+    // 2. Collect: higher bins to the result, the threshold bin to the stage.
+    const int pshift = 32 - pbits;
+    for_row4([&](int e0, const float (&f)[4], bool ok) {
+      uint32_t keys[4], g = 0, sm = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        keys[j] = order_key(f[j]);
+        const uint32_t b = pshift >= 32 ? 0u : (keys[j] >> pshift);
+        if (ok && e0 + j < row_end) {
+          if (b > prefix) g |= 1u << j;
+          else if (b == prefix) sm |= 1u << j;
+        }
+      }
+      collect(keys, e0, g, sm);
+    });
     __syncthreads();
-    for (int size = 2; size <= n2; size <<= 1) {
-      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+    mark();
+    const uint32_t above = uint32_t(s_pack & 0xFFFFFFFFull);  // == above_total
+    const uint32_t nsec = min(uint32_t(s_pack >> 32), uint32_t(kSecCap));
+    const uint32_t need = uint32_t(take) - above;
+    // 3. Exact last composite among the staged ones: levels over the bits
+    //    below the key prefix (composite bits [0, 64 - pbits)), 12 at a time,
+    //    until the threshold bin holds one composite.
+    uint64_t cprefix = 0;   // selected high bits of the composite below the key prefix
+    int cbits = pbits;      // composite bits fixed so far (from the top)
+    uint32_t crank = need;
+    while (cbits < 64) {
+      const int lb = min(12, 64 - cbits);
+      const int shift = 64 - cbits - lb;
+      for (int i = tid; i < (1 << lb); i += kThreads2) hist[i] = 0;
+      __syncthreads();
+      for (uint32_t i0 = 0; i0 < nsec; i0 += kThreads2) {
+        const uint32_t i = i0 + tid;
+        const uint64_t c = i < nsec ? sec[i] : 0ull;
+        const uint64_t hi = cbits >= 64 ? 0ull : (c >> (64 - cbits));
+        const uint64_t want = (uint64_t(prefix) << (cbits - pbits)) | cprefix;
+        hist_add(i < nsec && hi == want ? uint32_t(c >> shift) & ((1u << lb) - 1u) : 0xFFFFFFFFu);
+      }
+      __syncthreads();
+      find_bin(1 << lb, crank, 0u);
+      const uint32_t bsel = s_bstar, in = s_in, ab = s_above;
+      __syncthreads();
+      cprefix = (cprefix << lb) | bsel;
+      cbits += lb;
+      crank -= ab;
+      if (in == 1u) break;
+    }
+    mark();
+    // Staged composites whose top cbits exceed or equal the selected prefix
+    // are taken: exactly `need` of them.
+    const uint64_t want = (uint64_t(prefix) << (cbits - pbits)) | cprefix;
+    for (uint32_t i0 = 0; i0 < nsec; i0 += kThreads2) {
+      const uint32_t i = i0 + tid;
+      bool sel = false;
+      uint64_t c = 0;
+      if (i < nsec) {
+        c = sec[i];
+        sel = (c >> (64 - cbits)) >= want;
+      }
+      const uint32_t ballot = __ballot_sync(0xffffffffu, sel);
+      uint32_t base = 0;
+      if (lane == 0 && ballot) base = atomicAdd(reinterpret_cast<unsigned int*>(&s_pack), uint32_t(__popc(ballot)));
+      base = __shfl_sync(0xffffffffu, base, 0);
+      const uint32_t pos = base + __popc(ballot & ((1u << lane) - 1u));
+      if (sel && pos < uint32_t(kMaxK)) cand[pos] = c;
+    }
+  }
+  __syncthreads();
+  mark();
+  // 4. Order the results.
+  const int count = min(int(s_pack & 0xFFFFFFFFull), kMaxK);
+  if (count != take && tid == 0) record_error(err, kErrBadIndex);
+  // Bitonic sort of n2 = max(64, 2^ceil(log2 count)) composites (zero
+  // padding sorts last), descending.  Warp w holds elements [64 w, 64 w + 64)
+  // in registers, lane l elements 64 w + l and 64 w + l + 32: every stage of
+  // stride <= 32 is a register / shuffle exchange with no barrier; only the
+  // stages of stride >= 64 go through shared memory.
+  int n2 = 64;
+  while (n2 < count) n2 <<= 1;
+  for (int i = count + tid; i < n2; i += kThreads2) cand[i] = 0ull;
+  __syncthreads();
+  const bool active = wid * 64 < n2;
+  const int e0 = wid * 64 + lane;
+  uint64_t x0 = active ? cand[e0] : 0ull, x1 = active ? cand[e0 + 32] : 0ull;
+  // One compare-exchange stage of stride <= 32 for elements e and e + 32.
+  auto reg_stage = [&](int size, int stride) {
+    if (stride == 32) {
+      const bool desc = (e0 & size) == 0;  // lo = e0, hi = e0 + 32
+      if ((x0 < x1) == desc) {
+        const uint64_t t = x0;
+        x0 = x1;
+        x1 = t;
+      }
+      return;
+    }
+    auto exch = [&](uint64_t mine, int e) {
+      const uint64_t other = __shfl_xor_sync(0xffffffffu, mine, stride);
+      const bool is_lo = (e & stride) == 0;
+      const bool desc = ((e & ~stride) & size) == 0;
+      // lo keeps the larger (desc) / smaller (asc) of the pair, hi the other.
+      const bool keep_max = is_lo == desc;
+      return keep_max ? (mine > other ? mine : other) : (mine < other ? mine : other);
+    };
+    x0 = exch(x0, e0);
+    x1 = exch(x1, e0 + 32);
+  };
+  for (int size = 2; size <= n2; size <<= 1) {
+    int stride = size >> 1;
+    if (stride >= 64) {
+      if (active) {
+        cand[e0] = x0;
+        cand[e0 + 32] = x1;
+      }
+      __syncthreads();
+      for (; stride >= 64; stride >>= 1) {
         for (int i = tid; i < n2 / 2; i += kThreads2) {
-          const int lo = 2 * stride * (i / stride) + (i % stride);
+          const int lo = 2 * i - (i & (stride - 1));  // 2 stride (i / stride) + i % stride, stride = 2^m
           const int hi = lo + stride;
           const bool desc = ((lo & size) == 0);
-          const uint64_t a = sec[lo], bb = sec[hi];
+          const uint64_t a = cand[lo], bb = cand[hi];
           if ((a < bb) == desc) {
-            sec[lo] = bb;
-            sec[hi] = a;
+            cand[lo] = bb;
+            cand[hi] = a;
           }
         }
         __syncthreads();
       }
-    }
-    const uint32_t base = s_count;  // == s_above
-    const uint32_t need = uint32_t(take) - s_above;
-    for (uint32_t i = tid; i < need; i += kThreads2)
-      if (base + i < uint32_t(kMaxK)) cand[base + i] = sec[i];
-    __syncthreads();
-    if (tid == 0) s_count = base + need;
-  }
-  __syncthreads();
-  const int count = min(int(s_count), kMaxK);
-  if (count != take && tid == 0) record_error(err, kErrBadIndex);
-  int n2 = 1;
-  while (n2 < count) n2 <<= 1;
-  for (int i = count + tid; i < n2; i += kThreads2) cand[i] = 0ull;
-  __syncthreads();
-  for (int size = 2; size <= n2; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = tid; i < n2 / 2; i += kThreads2) {
-        const int lo = 2 * stride * (i / stride) + (i % stride);
-        const int hi = lo + stride;
-        const bool desc = ((lo & size) == 0);
-        const uint64_t a = cand[lo], bb = cand[hi];
-        if ((a < bb) == desc) {
-          cand[lo] = bb;
-          cand[hi] = a;
-        }
+      if (active) {
+        x0 = cand[e0];
+        x1 = cand[e0 + 32];
       }
-      __syncthreads();
     }
+    if (active)
+      for (; stride > 0; stride >>= 1) reg_stage(size, stride);
   }
+  if (active) {
+    cand[e0] = x0;
+    cand[e0 + 32] = x1;
+  }
+  __syncthreads();
+  mark();
   float* vout = values + int64_t(r) * k;
   int* iout = ids + int64_t(r) * k;
   for (int i = tid; i < k; i += kThreads2) {
@@ -398,10 +536,18 @@ __global__ void __launch_bounds__(kThreads2) topk2_kernel(const float* __restric
       iout[i] = -1;
     }
   }
+  if (tracing && tid == 0) g_topk_trace[15] = uint64_t(tp);
 }
 
 
 }  // namespace
+
+void set_topk_trace_row(int row) {
+  cuda_check(cudaMemcpyToSymbol(g_topk_trace_row, &row, sizeof(int)), "topk trace row");
+}
+void copy_topk_trace(unsigned long long* host) {
+  cuda_check(cudaMemcpyFromSymbol(host, g_topk_trace, sizeof(g_topk_trace)), "topk trace copy");
+}
 
 void launch_topk(const float* scores, int64_t ld, int R, int N, int k, float* values, int* ids,
                  int* err, cudaStream_t stream) {
@@ -417,7 +563,7 @@ void launch_topk_causal(const float* scores, int64_t ld, int R, int N, int k, in
     cuda_check(cudaGetLastError(), "topk launch");
     return;
   }
-  const size_t smem = size_t(kBins) * 4 + size_t(kMaxK) * 8 + size_t(8192) * 8;
+  const size_t smem = size_t(kBins) * 4 + size_t(kMaxK) * 8 + size_t(kSecCap) * 8;
   cuda_check(cudaFuncSetAttribute(topk2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
              "topk2 smem attribute");
   topk2_kernel<<<R, kThreads2, smem, stream>>>(scores, ld, N, k, causal_start, values, ids, overflow, err);

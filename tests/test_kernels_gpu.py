@@ -179,6 +179,27 @@ def test_topk_moderate_ties_two_pass():
     assert torch.equal(i.cpu(), ri) and torch.equal(v.cpu(), rv)
 
 
+@pytest.mark.parametrize("ld_pad", [0, 3])
+def test_topk_indexer_like_rows(ld_pad):
+    """Narrow-band logits (threshold decided inside the staged bin by the index
+    bits for equal values), unaligned row starts, short rows that take every
+    element, -inf entries."""
+    torch.manual_seed(15)
+    R, N = 40, 9000
+    base = torch.randn(R, N + ld_pad, device=DEV)
+    s = (10.0 + 0.01 * base).half().float()  # many exact duplicates near the threshold
+    s[:, 7] = -torch.inf
+    view = s[:, ld_pad:] if ld_pad else s
+    v, i = ops.exact_topk(view, 2048, causal_start=1000)
+    rows = torch.arange(R)[:, None]
+    cols = torch.arange(N)[None, :]
+    masked = view.cpu().masked_fill(cols > 1000 + rows, -torch.inf)
+    rv, ri = ref.exact_topk(masked, 2048)
+    assert torch.equal(i.cpu(), ri)
+    fin = torch.isfinite(rv)
+    assert torch.equal(v.cpu()[fin], rv[fin])
+
+
 # ------------------------------------------------------------ sparse MLA
 @pytest.mark.parametrize("impl", [0, 1], ids=["tcgen05", "mma_sync"])
 @pytest.mark.parametrize("T,K,P,splits", [(2, 2048, 5000, 1), (3, 256, 300, 1), (1, 2048, 9000, 16), (5, 100, 64, 4),
