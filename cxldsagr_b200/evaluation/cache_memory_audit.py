@@ -70,8 +70,8 @@ def model_cache_tensors(model, sessions=()) -> dict:
     if st is not None:
         for i, b in enumerate(st.buffers):
             out[f"staging.{i}"] = b
-    if getattr(model, "_logits_buf", None) is not None:
-        out["workspace.logits"] = model._logits_buf
+    for d, buf in (getattr(model, "_logits_buf", None) or {}).items():
+        out["workspace.logits" if d == model.device else f"workspace.logits.{d}"] = buf
     return out
 
 

@@ -6,6 +6,7 @@ prints ``{"length": ..., "next_token_id": ...}``.  ``--random-init`` runs the
 V3.2 architecture with random weights (no checkpoint needed).
 
     python -m cxldsagr_b200.models.deepseek_v32.infer --model ckpt/ --input-ids ids.json --history 65536
+    python -m cxldsagr_b200.models.deepseek_v32.infer --model ckpt/ --devices 0,1,2,3 ...   # layers over 4 GPUs
 """
 
 from __future__ import annotations
@@ -28,6 +29,8 @@ def main(argv=None):
     p.add_argument("--chunk-size", type=int, default=2048)
     p.add_argument("--num-layers", type=int, help="run only the first N checkpoint layers")
     p.add_argument("--device", default="cuda:0")
+    p.add_argument("--devices", help="comma-separated GPU indices: place the layers over these GPUs "
+                   "(contiguous runs by weight bytes; the reference's multi-GPU mode)")
     a = p.parse_args(argv)
     if (a.model is None) == (not a.random_init):
         p.error("give exactly one of --model or --random-init")
@@ -41,7 +44,8 @@ def main(argv=None):
     ids = json.loads(a.input_ids.read_text())
     if not 0 < a.history < len(ids):
         p.error("--history must leave a nonempty extension")
-    dev = torch.device(a.device)
+    devices = [torch.device("cuda", int(x)) for x in a.devices.split(",")] if a.devices else None
+    dev = devices[0] if devices else torch.device(a.device)
     if a.random_init:
         cfg = v32_config(a.num_layers or 3)
         src = StateDictSource(random_state_dict(cfg, layers=range(cfg.num_hidden_layers), device=dev), cfg)
@@ -53,7 +57,7 @@ def main(argv=None):
     cache = CacheConfig(method=method, capacity=len(ids), pool_tokens=a.slots if method != "hbm" else None,
                         host_tokens=a.host_arena_tokens, chunk_size=a.chunk_size,
                         candidate_tokens=len(ids) - a.history)
-    model = DeepSeekV32Model(cfg, src, device=dev, cache=cache, layers=layers)
+    model = DeepSeekV32Model(cfg, src, device=dev, cache=cache, layers=layers, devices=devices)
     tokens = prepare_token_ids(ids, device=dev, vocab_size=cfg.vocab_size, max_tokens=len(ids))
     model.prefill(tokens[: a.history])
     result = model.extend(tokens[a.history:])

@@ -81,7 +81,7 @@ class MoE:
 
     def _layout(self, rows: int, device):
         bucket = max(128, 1 << max(0, rows - 1).bit_length())
-        key = (bucket, self.w.experts.start, len(self.w.experts))
+        key = (bucket, self.w.experts.start, len(self.w.experts), str(device))
         lay = self._layouts.get(key)
         if lay is None:
             lay = ops.MoELayout(bucket, self.w.experts.start, len(self.w.experts), self.cfg.dim, device)
@@ -246,14 +246,18 @@ class ModelSession:
     """
 
     def __init__(self, model: "DeepSeekV32Model", capacity: int):
-        cc, dev, width = model.cache_cfg, model.device, model.cfg.qk_head_dim
+        cc, width = model.cache_cfg, model.cfg.qk_head_dim
         self.model = model
         self.capacity = capacity
-        self.pool_session = model.pool.allocate_session(capacity) if cc.offload else None
+        # One pool session per device pool (layer placement); pool_session is the first.
+        self.pool_sessions = [pool.allocate_session(capacity) for pool in model.pools] if cc.offload else []
+        self.pool_session = self.pool_sessions[0] if self.pool_sessions else None
         self.layers: list[LayerState] = []
         for i in range(len(model.layer_ids)):
+            dev = model.placement[i]
             if cc.offload:
-                kv = self.pool_session.layer(i)
+                g, local = model.block_pool[i]
+                kv = self.pool_sessions[g].layer(local)
             else:
                 kv = SparseTokenCache(capacity, width, device=dev, candidate_slots=cc.candidate_tokens)
             index = IndexerCache(capacity + cc.candidate_tokens, model.cfg.index_head_dim, device=dev)
@@ -283,8 +287,8 @@ class ModelSession:
     def release(self):
         if self.released:
             return
-        if self.pool_session is not None:
-            self.pool_session.release()
+        for ps in self.pool_sessions:
+            ps.release()
         self.layers.clear()
         self.released = True
 
@@ -294,7 +298,7 @@ class ModelSession:
         if self.pool_session is None:
             hbm += sum(layer.kv.records.numel() * layer.kv.records.element_size() for layer in self.layers)
         else:
-            hbm += self.pool_session.session_bytes().get("hbm", 0)
+            hbm += sum(ps.session_bytes().get("hbm", 0) for ps in self.pool_sessions)
         return {"hbm": hbm, "dram": 0}
 
 
@@ -317,13 +321,35 @@ class DeepSeekV32Model:
     def __init__(self, cfg: ModelConfig, source, *, device="cuda", cache: CacheConfig | None = None,
                  layers=None, pool: SharedSparseTokenPool | None = None, scope=None,
                  allocate_default_session: bool = True, replay: bool = False, allocate_pool: bool = True,
-                 parallel: ParallelContext | None = None):
+                 parallel: ParallelContext | None = None, devices=None, reserve_gib: float = 8.0):
+        """``devices``: place the layers over several devices of this process
+        (contiguous runs by weight bytes, see :mod:`...parallel.placement`);
+        the embedding lives on the first, final norm and LM head on the last."""
         self.cfg = cfg
-        self.device = torch.device(device)
+        self.device = torch.device(devices[0] if devices else device)
         self.cache_cfg = cache or CacheConfig(capacity=4096)
         self.layer_ids = list(range(cfg.num_hidden_layers) if layers is None else layers)
         self.scope = scope
-        self.par = parallel or single(device)
+        self.par = parallel or single(self.device)
+        if devices and len(devices) > 1:
+            from ...parallel.placement import device_budgets, layer_weight_bytes, plan_layer_devices
+
+            if self.par.world > 1:
+                raise ValueError("layer placement runs in one process; it does not combine with a process group")
+            devs = [torch.device(d) for d in devices]
+            sizes = [layer_weight_bytes(cfg, layer, fp8=cfg.weight_dtype == "fp8") for layer in self.layer_ids]
+            edge = cfg.vocab_size * cfg.dim * 2
+            self.placement = plan_layer_devices(sizes, devs,
+                                                device_budgets(devs, int(reserve_gib * 2**30), (edge, edge)))
+        else:
+            self.placement = [self.device] * len(self.layer_ids)
+        self.head_device = self.placement[-1] if self.placement else self.device
+        # Device pools: one per distinct device, holding that device's blocks in order.
+        self.pool_devices = list(dict.fromkeys(self.placement)) or [self.device]
+        self.block_pool = []
+        for dv in self.placement:
+            g = self.pool_devices.index(dv)
+            self.block_pool.append((g, sum(1 for x in self.block_pool if x[0] == g)))
         has_moe = any(cfg.is_moe_layer(layer) for layer in self.layer_ids)
         self.comm = make_comm(self.par, max_rows=self.cache_cfg.chunk_size,
                               moe=(cfg.n_routed_experts, cfg.dim, cfg.num_experts_per_tok) if has_moe else None)
@@ -332,21 +358,36 @@ class DeepSeekV32Model:
         self.replay_layout = ReplayLayout(tuple(self.layer_ids)) if replay else None
         cc = self.cache_cfg
         dev = self.device
+        hd = self.head_device
         self.embed_table = source.get_tensor("model.embed_tokens.weight").to(dev, torch.bfloat16).contiguous()
-        self.final_norm = source.get_tensor("model.norm.weight").to(dev, torch.float32).contiguous()
-        self.lm_head = source.get_tensor("lm_head.weight").to(dev, torch.bfloat16).contiguous()
-        self.freqs = ops.reference.rotary_frequencies(cfg, device=dev)
+        self.final_norm = source.get_tensor("model.norm.weight").to(hd, torch.float32).contiguous()
+        self.lm_head = source.get_tensor("lm_head.weight").to(hd, torch.bfloat16).contiguous()
+        self._freqs = {d: ops.reference.rotary_frequencies(cfg, device=d) for d in self.pool_devices}
+        self.freqs = self._freqs[self.pool_devices[0]]
+        if len(self.pool_devices) > 1 and (cc.method == "dense_prefetch" or pool is not None or replay):
+            raise ValueError("layer placement supports the hbm, serial_sparse and echo methods with own pools")
         width = cfg.qk_head_dim
-        self.pool = pool
+        self.pools: list[SharedSparseTokenPool] = []
+        self.pool = None
         self.session = None
-        if cc.offload and pool is None and allocate_pool:
+        if pool is not None:
+            self.attach_pool(pool)
+        elif cc.offload and allocate_pool:
             P = cc.pool_tokens or min(cc.capacity, 65536)
             host = cc.host_tokens or cc.capacity
-            self.attach_pool(self.make_pool(host, P))
+            if len(self.pool_devices) == 1:
+                self.attach_pool(self.make_pool(host, P))
+            else:
+                hp = (host + 63) // 64 * 64
+                self.pools = [SharedSparseTokenPool(hp, width, sum(1 for x in self.block_pool if x[0] == g), P,
+                                                    device=d, candidate_slots=cc.candidate_tokens)
+                              for g, d in enumerate(self.pool_devices)]
+                self.pool = self.pools[0]
         self.blocks: list[Block] = []
         par, comm = self.par, self.comm
         self._moe_workspace: dict = {}
         for i, layer in enumerate(self.layer_ids):
+            dev = self.placement[i]
             attn_w = load_attention(source, cfg, layer, device=dev)
             runner = AttentionRunner(cfg, attn_w, method=cc.method)
             if cfg.is_moe_layer(layer):
@@ -357,12 +398,13 @@ class DeepSeekV32Model:
                 mlp = DenseMLP(mw, comm, sharded=par.world > 1)
             post = source.get_tensor(f"model.layers.{layer}.post_attention_layernorm.weight").to(dev, torch.float32)
             self.blocks.append(Block(cfg, layer, runner, mlp, post.contiguous(), comm))
+        dev = self.device
         self.dense_staging = None
         if cc.method == "dense_prefetch":
             from ...cache.staging import DoubleBufferStaging
 
             self.dense_staging = DoubleBufferStaging(cc.capacity + cc.candidate_tokens, cfg.qk_head_dim, device=dev)
-        self._logits_buf = None
+        self._logits_buf = {}
         self.last_hidden = None
         self.poisoned = False
         self.session = self.new_session(cc.capacity) if allocate_default_session else None
@@ -377,7 +419,10 @@ class DeepSeekV32Model:
     def attach_pool(self, pool: SharedSparseTokenPool | None):
         if pool is not None and pool.num_layers != len(self.layer_ids):
             raise ValueError("the pool must have one layer per model block")
+        if pool is not None and len(self.pool_devices) > 1:
+            raise ValueError("a placed model builds one pool per device itself")
         self.pool = pool
+        self.pools = [pool] if pool is not None else []
 
     def new_session(self, capacity: int | None = None) -> ModelSession:
         return ModelSession(self, capacity or self.cache_cfg.capacity)
@@ -397,15 +442,16 @@ class DeepSeekV32Model:
     def _scope(self):
         return self.scope or (lambda _n: nullcontext())
 
-    def _ensure_logits_buf(self, rows, cols):
-        if not self.device.type == "cuda":
+    def _ensure_logits_buf(self, rows, cols, device=None):
+        device = device or self.device
+        if not device.type == "cuda":
             return None
         cols = (cols + 3) // 4 * 4
-        buf = self._logits_buf
+        buf = self._logits_buf.get(device)
         if buf is None or buf.shape[0] < rows or buf.shape[1] < cols:
             cap_cols = max(cols, (self.cache_cfg.capacity + self.cache_cfg.candidate_tokens + 3) // 4 * 4)
-            buf = torch.empty((max(rows, self.cache_cfg.chunk_size), cap_cols), dtype=torch.float32, device=self.device)
-            self._logits_buf = buf
+            buf = torch.empty((max(rows, self.cache_cfg.chunk_size), cap_cols), dtype=torch.float32, device=device)
+            self._logits_buf[device] = buf
         return buf
 
     # ------------------------------------------------------------- forward
@@ -419,11 +465,13 @@ class DeepSeekV32Model:
             c1 = min(T, c0 + chunk)
             pos = start + c0
             positions = torch.arange(pos, start + c1, device=self.device, dtype=torch.float32)
+            pos_on = {self.device: positions}
             rows = par.token_range(c1 - c0)
             with scope("embedding"):
                 hidden = ops.embed(ids[c0 + rows[0]:c0 + rows[1]], self.embed_table)
             residual = None
-            logits_buf = self._ensure_logits_buf(max(rows[1] - rows[0], 1), start + c1)
+            n_rows = max(rows[1] - rows[0], 1)
+            logits_buf = self._ensure_logits_buf(n_rows, start + c1)
             replay = self.replay_layout.begin_chunk() if self.replay_layout is not None else None
             dense = self.dense_staging is not None and session.pool_session is not None
             nxt = self._stage_history(session, 0, pos) if dense else None
@@ -439,9 +487,18 @@ class DeepSeekV32Model:
                     state.dense = self.dense_staging.buffers[cur.index]
                     if i + 1 < len(self.blocks):  # next layer's history streams in meanwhile
                         nxt = self._stage_history(session, i + 1, pos)
+                dv = self.placement[i]
                 try:
-                    hidden, residual = block.forward(state, hidden, residual, pos, positions, self.freqs,
-                                                     scope=scope, logits_buf=logits_buf, rows=rows)
+                    if dv != hidden.device:  # layer placement: hand the rows to the next device
+                        with scope("hidden_transfer"):
+                            hidden = hidden.to(dv, non_blocking=True)
+                            residual = residual.to(dv, non_blocking=True) if residual is not None else None
+                    if dv not in pos_on:
+                        pos_on[dv] = positions.to(dv)
+                    lb = logits_buf if dv == self.device else self._ensure_logits_buf(n_rows, start + c1, dv)
+                    with (torch.cuda.device(dv) if dv.type == "cuda" else nullcontext()):
+                        hidden, residual = block.forward(state, hidden, residual, pos, pos_on[dv], self._freqs[dv],
+                                                         scope=scope, logits_buf=lb, rows=rows)
                 finally:
                     if cur is not None:
                         state.dense = None
@@ -455,10 +512,11 @@ class DeepSeekV32Model:
             normed = None
             if out_h.shape[0]:
                 normed, _ = ops.residual_rms_norm(out_h[keep], out_r[keep], self.final_norm, cfg.norm_eps)
-            logits = torch.empty((1, self.lm_head.shape[0]), dtype=torch.float32, device=self.device)
+            hd = self.head_device
+            logits = torch.empty((1, self.lm_head.shape[0]), dtype=torch.float32, device=hd)
             if par.rank == owner:
                 last = normed[-1:]
-                logits = ops.linear(last, self.lm_head).float() if self.device.type != "cuda" else self._lm_head(last)
+                logits = ops.linear(last, self.lm_head).float() if hd.type != "cuda" else self._lm_head(last)
             if par.world > 1:
                 logits = self.comm.broadcast(logits.contiguous(), owner)
                 if want_hidden:
@@ -478,7 +536,7 @@ class DeepSeekV32Model:
                                    before=lambda: self.pool.wait_host(ps, layer))
 
     def _lm_head(self, last):
-        out = torch.empty((last.shape[0], self.lm_head.shape[0]), dtype=torch.float32, device=self.device)
+        out = torch.empty((last.shape[0], self.lm_head.shape[0]), dtype=torch.float32, device=self.head_device)
         V, D = self.lm_head.shape
         ops.lib().bf16_gemm(last.contiguous(), 0, D, 0, self.lm_head, 0, D, 0, out, 0, V, 0, last.shape[0], V, D, 1)
         return out
@@ -545,12 +603,13 @@ class DeepSeekV32Model:
         """Drop the HBM copies of a session's offloaded history (host copies and indexer keys stay):
         the next steps recall every selected row from DRAM."""
         session = session or self.session
-        if session.pool_session is None or self.pool is None:
+        if session.pool_session is None or not self.pools:
             return
-        self.pool.drain()
-        ids = session.pool_session.global_ids()
-        for i in range(len(self.layer_ids)):
-            self.pool.release_ids(i, ids)
+        for g, (pool, ps) in enumerate(zip(self.pools, session.pool_sessions)):
+            pool.drain()
+            ids = ps.global_ids()
+            for layer in range(pool.num_layers):
+                pool.release_ids(layer, ids)
 
     def reset(self, *, session: ModelSession | None = None):
         (session or self.session).reset()
@@ -577,6 +636,8 @@ class ExtendGraph:
     def __init__(self, model: DeepSeekV32Model, T: int, *, warmup: int = 2, session: ModelSession | None = None):
         if model.cache_cfg.method == "dense_prefetch":
             raise ValueError("the dense_prefetch method runs its extend eagerly")
+        if len(model.pool_devices) > 1:
+            raise ValueError("a model placed over several devices runs its extend eagerly")
         self.model, self.T = model, T
         self.session = session or model.session
         self.start = self.session.length

@@ -127,9 +127,8 @@ class DeepSeekServingBackend:
         out = {"hbm": 0, "dram": 0}
         if self.model.pool is not None:
             out = dict(self.model.pool.shared_bytes())
-        if self.model._logits_buf is not None:
-            key = "hbm" if self.model._logits_buf.is_cuda else "dram"
-            out[key] += self.model._logits_buf.numel() * 4
+        for buf in self.model._logits_buf.values():
+            out["hbm" if buf.is_cuda else "dram"] += buf.numel() * 4
         return out
 
     # ------------------------------------------------------------ sessions
