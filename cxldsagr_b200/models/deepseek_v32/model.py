@@ -366,23 +366,13 @@ class DeepSeekV32Model:
         self.freqs = self._freqs[self.pool_devices[0]]
         if len(self.pool_devices) > 1 and (cc.method == "dense_prefetch" or pool is not None or replay):
             raise ValueError("layer placement supports the hbm, serial_sparse and echo methods with own pools")
-        width = cfg.qk_head_dim
         self.pools: list[SharedSparseTokenPool] = []
         self.pool = None
         self.session = None
         if pool is not None:
             self.attach_pool(pool)
         elif cc.offload and allocate_pool:
-            P = cc.pool_tokens or min(cc.capacity, 65536)
-            host = cc.host_tokens or cc.capacity
-            if len(self.pool_devices) == 1:
-                self.attach_pool(self.make_pool(host, P))
-            else:
-                hp = (host + 63) // 64 * 64
-                self.pools = [SharedSparseTokenPool(hp, width, sum(1 for x in self.block_pool if x[0] == g), P,
-                                                    device=d, candidate_slots=cc.candidate_tokens)
-                              for g, d in enumerate(self.pool_devices)]
-                self.pool = self.pools[0]
+            self._build_pools()
         self.blocks: list[Block] = []
         par, comm = self.par, self.comm
         self._moe_workspace: dict = {}
@@ -398,18 +388,96 @@ class DeepSeekV32Model:
                 mlp = DenseMLP(mw, comm, sharded=par.world > 1)
             post = source.get_tensor(f"model.layers.{layer}.post_attention_layernorm.weight").to(dev, torch.float32)
             self.blocks.append(Block(cfg, layer, runner, mlp, post.contiguous(), comm))
-        dev = self.device
         self.dense_staging = None
-        if cc.method == "dense_prefetch":
-            from ...cache.staging import DoubleBufferStaging
-
-            self.dense_staging = DoubleBufferStaging(cc.capacity + cc.candidate_tokens, cfg.qk_head_dim, device=dev)
+        self._build_staging()
         self._logits_buf = {}
         self.last_hidden = None
         self.poisoned = False
         self.session = self.new_session(cc.capacity) if allocate_default_session else None
 
     # ------------------------------------------------------------- sessions
+    def _build_pools(self):
+        cc = self.cache_cfg
+        P = cc.pool_tokens or min(cc.capacity, 65536)
+        host = cc.host_tokens or cc.capacity
+        if len(self.pool_devices) == 1:
+            self.attach_pool(self.make_pool(host, P))
+            return
+        hp = (host + 63) // 64 * 64
+        self.pools = [SharedSparseTokenPool(hp, self.cfg.qk_head_dim, sum(1 for x in self.block_pool if x[0] == g), P,
+                                            device=d, candidate_slots=cc.candidate_tokens)
+                      for g, d in enumerate(self.pool_devices)]
+        self.pool = self.pools[0]
+
+    def _build_staging(self):
+        cc = self.cache_cfg
+        if cc.method == "dense_prefetch":
+            from ...cache.staging import DoubleBufferStaging
+
+            self.dense_staging = DoubleBufferStaging(cc.capacity + cc.candidate_tokens, self.cfg.qk_head_dim,
+                                                     device=self.device)
+
+    def set_cache_method(self, method: str, **overrides):
+        """Switch to another cache method with an independent, empty cache.
+
+        Reference: ``models/deepseek_v32/model.py:458-479``.  Every session of
+        this model is released and the model's own pools are closed; new pools
+        (offload methods) or staging buffers (``dense_prefetch``) are built
+        from the cache config with ``method`` and ``overrides`` (for example
+        ``pool_tokens``), and a new default session is opened.  Weights stay.
+        """
+        from dataclasses import replace
+
+        if method not in ("hbm", "echo", "serial_sparse", "dense_prefetch"):
+            raise ValueError("unsupported DeepSeek cache method")
+        cc = replace(self.cache_cfg, method=method, **overrides)
+        if method == "dense_prefetch" and (cc.pool_tokens or min(cc.capacity, 65536)) < cc.capacity:
+            raise ValueError("dense prefetch requires P >= session capacity")
+        if method == "dense_prefetch" and len(self.pool_devices) > 1:
+            raise ValueError("layer placement supports the hbm, serial_sparse and echo methods with own pools")
+        if self.session is not None:
+            self.session.release()
+            self.session = None
+        for pool in self.pools:
+            pool.close()
+        self.pools, self.pool, self.dense_staging = [], None, None
+        self.cache_cfg = cc
+        for block in self.blocks:
+            block.attention.method = method
+        if cc.offload:
+            self._build_pools()
+        self._build_staging()
+        self.session = self.new_session(cc.capacity)
+
+    def snapshot_prefix(self, *, session: ModelSession | None = None) -> dict:
+        """Snapshot a session's committed prefix (pool rows and maps, indexer lengths and hints).
+
+        Reference: ``models/deepseek_v32/model.py:945-962``.  Resident (``hbm``)
+        records keep their prefix untouched by later steps, so only lengths are
+        recorded for them; offload pools are snapshotted whole (the pool must be
+        quiescent).  ``restore_prefix`` rewinds the session to this point.
+        """
+        session = session or self.session
+        if session.failed or session.released:
+            raise RuntimeError("the session cannot be snapshotted")
+        return {"schema": "cxld-prefix-v1", "model": id(self), "session": id(session),
+                "method": self.cache_cfg.method, "length": session.length,
+                "pools": [pool.snapshot() for pool in self.pools] if session.pool_session is not None else [],
+                "index": [layer.index.snapshot() for layer in session.layers]}
+
+    def restore_prefix(self, state: dict, *, session: ModelSession | None = None):
+        session = session or self.session
+        if (state.get("schema") != "cxld-prefix-v1" or state["model"] != id(self) or state["session"] != id(session)
+                or state["method"] != self.cache_cfg.method or len(state["index"]) != len(session.layers)):
+            raise ValueError("prefix snapshot does not match this model's cache")
+        for pool, snap in zip(self.pools, state["pools"]):
+            pool.restore(snap)
+        for layer, idx in zip(session.layers, state["index"]):
+            if session.pool_session is None:
+                layer.kv.truncate(state["length"])
+            layer.index.restore(idx)
+        session.length = state["length"]
+
     def make_pool(self, host_tokens: int, pool_tokens: int) -> SharedSparseTokenPool:
         """A shared sparse-token pool for this model's layers (host rows rounded to 64-token pages)."""
         host = (host_tokens + 63) // 64 * 64

@@ -81,3 +81,43 @@ def test_offload_methods_match_resident(tiny, method):
     assert torch.equal(ref.prefill(hist).logits, off.prefill(hist).logits)
     assert torch.equal(ref.candidate(cand).logits, off.candidate(cand).logits)
     assert torch.equal(ref.extend(cand).logits, off.extend(cand).logits)
+
+
+@pytest.mark.parametrize("method", ["hbm", "serial_sparse"])
+def test_snapshot_restore_prefix(tiny, method):
+    """Rewinding to a snapshot and replaying the same extend gives the same logits."""
+    cfg, src = tiny
+    g = torch.Generator().manual_seed(7)
+    hist = torch.randint(0, cfg.vocab_size, (512,), generator=g)
+    a = torch.randint(0, cfg.vocab_size, (16,), generator=g)
+    b = torch.randint(0, cfg.vocab_size, (16,), generator=g)
+    kw = {} if method == "hbm" else {"pool_tokens": 256, "host_tokens": 1024 + 64}
+    m = _model(cfg, src, method, **kw)
+    m.prefill(hist)
+    snap = m.snapshot_prefix()
+    first = m.extend(a).logits
+    m.extend(b)
+    m.restore_prefix(snap)
+    assert m.length == 512
+    assert torch.equal(m.extend(a).logits, first)
+    other = _model(cfg, src, method, **kw)
+    with pytest.raises(ValueError):
+        other.restore_prefix(snap)
+
+
+def test_set_cache_method(tiny):
+    """Switching methods gives a fresh empty cache with the new method's results."""
+    cfg, src = tiny
+    g = torch.Generator().manual_seed(8)
+    hist = torch.randint(0, cfg.vocab_size, (512,), generator=g)
+    ref = _model(cfg, src, "hbm")
+    want = ref.prefill(hist).logits
+    m = _model(cfg, src, "hbm")
+    m.prefill(hist[:100])
+    m.set_cache_method("echo", pool_tokens=256, host_tokens=1024 + 64)
+    assert m.length == 0 and m.pool is not None
+    assert torch.equal(m.prefill(hist).logits, want)
+    m.set_cache_method("hbm")
+    assert m.pool is None and torch.equal(m.prefill(hist).logits, want)
+    with pytest.raises(ValueError):
+        m.set_cache_method("bogus")
