@@ -142,6 +142,9 @@ def numerical_comparison(actual: torch.Tensor, expected: torch.Tensor, *, atol: 
 
 def run_record(**extra) -> dict:
     """Everything a published number needs next to it."""
+    from .cpu_environment import cpu_environment
+
     return {"source": source_snapshot(), "backend": backend_provenance(), "native": loaded_native_artifacts(),
+            "cpu_environment": cpu_environment(),
             "environment": {k: v for k, v in os.environ.items() if k.startswith(("NCCL_", "CUDA_", "PYTORCH_"))},
             **extra}

@@ -74,3 +74,19 @@ def test_model_cache_inventory_and_audit_cli(tmp_path):
     res = serving_comparison.compare([serving_comparison.collect_run(str(log))] * 2)
     assert res["same_workload"] and res["runs"][0]["revisit_ms"]["mean"] == 1.0
     assert "| hbm |" in serving_comparison.markdown(res)
+
+
+def test_cpu_environment_audit():
+    from cxldsagr_b200.evaluation.cpu_environment import (cpu_environment, finish_cpu_environment,
+                                                          validate_cpu_environment_record)
+
+    meta = {"cpu_environment": cpu_environment()}
+    assert meta["cpu_environment"]["affinity"]
+    assert finish_cpu_environment(meta) == {"status": "recorded_and_equal"}
+    assert validate_cpu_environment_record(meta)["status"] == "recorded_and_equal"
+    changed = dict(meta, cpu_environment=dict(meta["cpu_environment"], torch_num_threads=-1))
+    with pytest.raises(ValueError):
+        finish_cpu_environment(changed)
+    assert changed["cpu_environment_audit"]["status"] == "rejected"
+    with pytest.raises(ValueError):
+        validate_cpu_environment_record({"cpu_environment_audit": {}})
