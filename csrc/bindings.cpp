@@ -4,6 +4,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "host/recall_dispatch.h"
 #include "kernels/launchers.h"
 
 namespace {
@@ -364,6 +365,67 @@ void pool_recall_select(Tensor& h2d, Tensor& d2h, Tensor& priority, Tensor& meta
   b200::launch_pool_select(a, -1, int(k_limit), nullptr, int(count_slot), stream());
 }
 
+b200::TensorDesc desc_of(const Tensor& t) {
+  b200::TensorDesc d;
+  d.defined = t.defined();
+  if (!d.defined) return d;
+  switch (t.scalar_type()) {
+    case torch::kInt32: d.dtype = b200::DType::I32; break;
+    case torch::kInt64: d.dtype = b200::DType::I64; break;
+    case torch::kUInt8: d.dtype = b200::DType::U8; break;
+    case torch::kBFloat16: d.dtype = b200::DType::BF16; break;
+    case torch::kFloat32: d.dtype = b200::DType::F32; break;
+    default: d.dtype = b200::DType::Other;
+  }
+  d.numel = t.numel();
+  d.ndim = int(t.dim());
+  d.rows = t.dim() ? t.size(0) : 0;
+  d.row_bytes = t.dim() == 2 ? t.stride(0) * int64_t(t.element_size()) : 0;
+  d.contiguous = t.is_contiguous();
+  d.device = t.is_cuda() ? int(t.get_device()) : -1;
+  d.pinned = !t.is_cuda() && t.is_pinned();
+  return d;
+}
+
+// One exact recall event (classify -> select -> gather), each stage validated
+// right before it is enqueued; see host/recall_dispatch.h.
+void pool_recall_dispatch(const Tensor& ids, int64_t hist_end, const Tensor& page_table, Tensor& h2d, Tensor& d2h,
+                          Tensor& priority, Tensor& meta, Tensor& mark, Tensor& miss_list, Tensor& victims,
+                          Tensor& stats, Tensor& select_stats, int64_t k_limit, int64_t count_slot, const Tensor& host,
+                          Tensor& records) {
+  b200::RecallDesc d;
+  d.ids = desc_of(ids); d.page_table = desc_of(page_table); d.h2d = desc_of(h2d); d.d2h = desc_of(d2h);
+  d.priority = desc_of(priority); d.meta = desc_of(meta); d.mark = desc_of(mark); d.miss_list = desc_of(miss_list);
+  d.victims = desc_of(victims); d.stats = desc_of(stats); d.select_stats = desc_of(select_stats);
+  d.host = desc_of(host); d.records = desc_of(records);
+  d.hist_end = hist_end; d.k_limit = k_limit; d.count_slot = count_slot;
+  c10::cuda::CUDAGuard g(h2d.device());
+  struct Stages {
+    const Tensor &ids, &page_table, &host;
+    Tensor &h2d, &d2h, &priority, &meta, &mark, &miss_list, &victims, &stats, &select_stats, &records;
+    int64_t hist_end, k_limit, count_slot;
+    void classify() {
+      auto a = pool_args(ids, hist_end, page_table, h2d, d2h, priority, meta, mark, miss_list, victims, stats);
+      b200::launch_pool_recall(a, stream());
+    }
+    void select() {
+      auto a = pool_args(c10::nullopt, 0, c10::nullopt, h2d, d2h, priority, meta, mark, miss_list, victims,
+                         select_stats);
+      b200::launch_pool_select(a, -1, int(k_limit), nullptr, int(count_slot), stream());
+    }
+    void gather() {
+      // meta word 2 holds the rows placed; its low 32 bits are the gather's device-side count.
+      const int* count = reinterpret_cast<const int*>(meta.data_ptr<int64_t>()) + 4;
+      const int row_bytes = int(records.stride(0) * records.element_size());
+      b200::launch_gather_rows(cptr<uint8_t>(host), ptr<uint8_t>(records), cptr<int64_t>(miss_list),
+                               cptr<int64_t>(victims), int(miss_list.numel()), count, row_bytes, host.size(0),
+                               records.size(0), err_ptr(records), stream());
+    }
+  } stages{ids, page_table, host, h2d, d2h, priority, meta, mark, miss_list, victims, stats, select_stats, records,
+           hist_end, k_limit, count_slot};
+  b200::run_recall(d, stages);
+}
+
 // offset[0] = mean of the finite logits of the last min(4, rows) rows over columns [0, cols).
 void echo_hint(const Tensor& logits, int64_t rows, int64_t cols, Tensor& offset) {
   c10::cuda::CUDAGuard g(logits.device());
@@ -611,6 +673,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("pool_recall", &pool_recall);
   m.def("pool_select", &pool_select);
   m.def("pool_recall_select", &pool_recall_select);
+  m.def("pool_recall_dispatch", &pool_recall_dispatch);
   m.def("pool_map", &pool_map);
   m.def("echo_predict", &echo_predict);
   m.def("echo_hint", &echo_hint);

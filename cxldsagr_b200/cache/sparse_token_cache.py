@@ -358,15 +358,14 @@ class SparseTokenCache:
         from .. import ops
 
         pool = self._pool.layers[self.layer_id]
-        lib = ops.lib()
-        lib.pool_recall(ids32, hist_end, self.session.page_table, pool.h2d, pool.d2h, pool.priority, pool.meta,
-                        pool.mark, pool.miss_list, pool.victims, stats)
-        self._pool.wait_host(self.session, self.layer_id)   # host rows written by earlier appends are complete
-        lib.pool_recall_select(pool.h2d, pool.d2h, pool.priority, pool.meta, pool.mark, pool.miss_list,
-                               pool.victims, self._dev if stats is self._scratch else stats, k_limit, count_slot)
-        # meta[2] now holds the rows placed; its low 32 bits are the gather's device-side count.
-        count = pool.meta.view(torch.int32)[4:5]
-        ops.gather_host_records(pool.host, pool.records, pool.miss_list, pool.victims, device_count=count)
+        # Host rows written by earlier appends must be complete before a slot they
+        # still back can be evicted (select) or a row is read back (gather).
+        self._pool.wait_host(self.session, self.layer_id)
+        # classify -> select -> gather in one native call (csrc/host/recall_dispatch.h).
+        ops.lib().pool_recall_dispatch(ids32, hist_end, self.session.page_table, pool.h2d, pool.d2h, pool.priority,
+                                       pool.meta, pool.mark, pool.miss_list, pool.victims, stats,
+                                       self._dev if stats is self._scratch else stats, k_limit, count_slot,
+                                       pool.host, pool.records)
         return pool
 
     def _ensure_native(self, indices: torch.Tensor) -> torch.Tensor:

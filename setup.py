@@ -7,6 +7,8 @@ own arch list when an explicit -gencode flag is present).
 import glob
 import os
 
+import pybind11
+
 from setuptools import Extension, setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
@@ -35,6 +37,14 @@ setup(
             name="cxldsagr_b200.serving._token_validation",
             sources=["csrc/host/token_validation.cpp"],
             extra_compile_args=["-O3", "-std=c++17", "-Wall", "-Wextra", "-Werror"],
+            language="c++",
+        ),
+        # Host-only CPU probe of the recall dispatch (validators, stage order, fault injection) for tests.
+        Extension(
+            name="cxldsagr_b200.cache._recall_dispatch_probe",
+            sources=["csrc/host/recall_dispatch_probe.cpp"],
+            include_dirs=[pybind11.get_include(), os.path.join(ROOT, "csrc", "host")],
+            extra_compile_args=["-O2", "-std=c++17", "-Wall", "-Wextra", "-Werror"],
             language="c++",
         ),
     ],
