@@ -142,9 +142,15 @@ def numerical_comparison(actual: torch.Tensor, expected: torch.Tensor, *, atol: 
 
 def run_record(**extra) -> dict:
     """Everything a published number needs next to it."""
+    from ..ops import native as _native
     from .cpu_environment import cpu_environment
 
+    try:
+        build = _native.native_info()
+        build = {k: v for k, v in build.items() if k != "sources"} | {"sources_sha256": build["sources"]["sha256"]}
+    except _native.NativeUnavailable as exc:
+        build = {"unavailable": str(exc)}
     return {"source": source_snapshot(), "backend": backend_provenance(), "native": loaded_native_artifacts(),
-            "cpu_environment": cpu_environment(),
+            "native_build": build, "cpu_environment": cpu_environment(),
             "environment": {k: v for k, v in os.environ.items() if k.startswith(("NCCL_", "CUDA_", "PYTORCH_"))},
             **extra}

@@ -572,7 +572,8 @@ class DeepSeekV32Model:
                         state.dense = None
                         cur.release()
             out_h, out_r = hidden, residual
-        with scope("final_norm_lm_head"):
+        hd = self.head_device
+        with scope("final_norm_lm_head"), (torch.cuda.device(hd) if hd.type == "cuda" else nullcontext()):
             n_last = c1 - c0
             owner = next(r for r in range(par.world) if par.world == 1 or
                          shard_range(n_last, par.world, r)[0] <= n_last - 1 < shard_range(n_last, par.world, r)[1])
@@ -580,7 +581,6 @@ class DeepSeekV32Model:
             normed = None
             if out_h.shape[0]:
                 normed, _ = ops.residual_rms_norm(out_h[keep], out_r[keep], self.final_norm, cfg.norm_eps)
-            hd = self.head_device
             logits = torch.empty((1, self.lm_head.shape[0]), dtype=torch.float32, device=hd)
             if par.rank == owner:
                 last = normed[-1:]

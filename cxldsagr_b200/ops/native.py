@@ -57,13 +57,27 @@ class _CountingLib:
 
 @functools.cache
 def lib():
+    from . import build_identity
+
     try:
         from .. import _C  # noqa: PLC0415
     except ImportError as exc:  # pragma: no cover - depends on the build
         raise NativeUnavailable(
             "the sm_100a extension is not built; run `python setup.py build_ext --inplace`"
         ) from exc
+    try:
+        build_identity.verify()
+    except RuntimeError as exc:
+        raise NativeUnavailable(str(exc)) from exc
     return _CountingLib(_C)
+
+
+def native_info() -> dict:
+    """Build record of the loaded extension (sources, flags, compiler, artifact digests), re-verified."""
+    from . import build_identity
+
+    lib()
+    return build_identity.verify()
 
 
 def launch_count() -> int:

@@ -21,6 +21,23 @@ NVCC_FLAGS = [
 ]
 SOURCES = ["csrc/bindings.cpp"] + sorted(glob.glob("csrc/kernels/*.cu"))
 
+_Base = BuildExtension.with_options(use_ninja=True)
+
+
+class BuildWithIdentity(_Base):
+    """Build, then record the sources / flags / artifact digests the loader checks."""
+
+    def run(self):
+        super().run()
+        import importlib.util
+
+        spec = importlib.util.spec_from_file_location(
+            "_build_identity", os.path.join(ROOT, "cxldsagr_b200", "ops", "build_identity.py"))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        mod.write_record(NVCC_FLAGS)
+
+
 setup(
     name="cxldsagr_b200",
     version="0.1.0",
@@ -48,5 +65,5 @@ setup(
             language="c++",
         ),
     ],
-    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+    cmdclass={"build_ext": BuildWithIdentity},
 )

@@ -90,3 +90,28 @@ def test_cpu_environment_audit():
     assert changed["cpu_environment_audit"]["status"] == "rejected"
     with pytest.raises(ValueError):
         validate_cpu_environment_record({"cpu_environment_audit": {}})
+
+
+def test_native_build_identity(tmp_path, monkeypatch):
+    """The loader refuses an extension whose sources changed since its build."""
+    import json as _json
+    import shutil
+
+    from cxldsagr_b200.ops import build_identity as bi
+
+    src = tmp_path / "csrc"
+    shutil.copytree(bi.ROOT / "csrc", src)
+    before = bi.sources_digest(tmp_path)
+    (src / "kernels" / "topk.cu").write_text((src / "kernels" / "topk.cu").read_text() + "\n// edit\n")
+    after = bi.sources_digest(tmp_path)
+    assert before["sha256"] != after["sha256"]
+    assert [k for k in before["files"] if before["files"][k] != after["files"][k]] == ["csrc/kernels/topk.cu"]
+    if bi.artifact_path() is None or not bi.RECORD.exists():
+        pytest.skip("extension not built here")
+    rec = _json.loads(bi.RECORD.read_text())
+    rec["sources"]["sha256"] = "0" * 64
+    fake = tmp_path / "_C.build.json"
+    fake.write_text(_json.dumps(rec))
+    monkeypatch.setattr(bi, "RECORD", fake)
+    with pytest.raises(RuntimeError, match="stale"):
+        bi.verify()

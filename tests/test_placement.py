@@ -71,3 +71,30 @@ def test_placement_rejects_unsupported_modes(tiny):
     cfg, src = tiny
     with pytest.raises(ValueError):
         _model(cfg, src, "dense_prefetch", devices=["cpu:0", "cpu:1"], pool_tokens=512, host_tokens=1024 + 64)
+
+
+@pytest.mark.gpu
+def test_placed_model_two_gpus():
+    """Layers over two GPUs match one GPU (same kernels, rows handed over between devices)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from cxldsagr_b200.config import v32_config
+
+    cfg = v32_config(2)
+    d0, d1 = torch.device("cuda", 0), torch.device("cuda", 1)
+    src = StateDictSource(random_state_dict(cfg, layers=[0, 1], seed=0, device=d0))
+    g = torch.Generator().manual_seed(0)
+    hist = torch.randint(0, cfg.vocab_size, (2048,), generator=g).to(d0)
+    ext = torch.randint(0, cfg.vocab_size, (16,), generator=g).to(d0)
+    outs = []
+    for devices in (None, [d0, d1]):
+        cache = CacheConfig(method="serial_sparse", capacity=2048 + 64, chunk_size=1024, candidate_tokens=16,
+                            pool_tokens=2048 + 64, host_tokens=2048 + 64)
+        m = DeepSeekV32Model(cfg, src, device=d0, cache=cache, devices=devices)
+        if devices:
+            assert m.placement == [d0, d1] and m.lm_head.device == d1
+        outs.append((m.prefill(hist).logits.to(d0), m.extend(ext).logits.to(d0)))
+        torch.cuda.synchronize(d0)
+        del m
+    torch.testing.assert_close(outs[0][0], outs[1][0], rtol=0, atol=0)
+    torch.testing.assert_close(outs[0][1], outs[1][1], rtol=0, atol=0)
