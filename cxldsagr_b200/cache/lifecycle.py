@@ -50,6 +50,18 @@ class ResourceLifecycle:
         if owner is not self.admission_owner:
             raise RuntimeError(f"{self.label} resources belong to another admission owner")
 
+    def check_active(self, session):
+        """Borrowed session caches mutate only inside their own session's operation.
+
+        Reference: ``models/deepseek_v32/cache/session.py:12-84`` (``ServingCacheGuard``).
+        """
+        if self.poisoned:
+            raise RuntimeError(f"{self.label} resources are poisoned")
+        if session not in self.sessions:
+            raise RuntimeError(f"{self.label}: the session is released or belongs to another generation")
+        if self.active_session is not session:
+            raise RuntimeError(f"{self.label}: session cache mutation requires the session's active operation")
+
     def bind_owner(self, owner):
         if self.admission_owner is not None and self.admission_owner is not owner:
             raise RuntimeError(f"{self.label} already has an admission owner")

@@ -118,7 +118,13 @@ class SparseTokenCache:
     def record_bytes(self) -> int:
         return self.width * self.records.element_size()
 
+    # Set by a serving backend for borrowed session caches: raises unless the
+    # owning session's own operation is active (see ResourceLifecycle.check_active).
+    access_check = None
+
     def _check(self):
+        if self.access_check is not None:
+            self.access_check()
         if self._pool is not None:
             self.session._check()
 
@@ -166,6 +172,8 @@ class SparseTokenCache:
         self._step_end = self.length + count
 
     def discard_transient(self):
+        if self.access_check is not None:
+            self.access_check()
         if self.transient_start is None:
             raise RuntimeError("no transient step is open")
         self.written = self.length = self.transient_start
@@ -322,6 +330,8 @@ class SparseTokenCache:
         Used by the indexer-fused prefetch method: ``logical`` are ids the
         predictor proved to be in the coming top-k.  Returns records copied.
         """
+        if self.access_check is not None:
+            self.access_check()
         if self._pool is None or not logical.numel():
             return 0
         if self.native:

@@ -18,6 +18,7 @@ and replayed per request, like the reference's full extend graph
 
 from __future__ import annotations
 
+import functools
 from contextlib import nullcontext
 from dataclasses import dataclass
 
@@ -283,6 +284,12 @@ class ModelSession:
             layer.kv.truncate(length)
             layer.index.truncate(length)
         self.length = length
+
+    def bind_serving(self, lifecycle):
+        """Guard this session's KV caches: mutation only inside the lifecycle's operation on this session."""
+        check = functools.partial(lifecycle.check_active, self)
+        for layer in self.layers:
+            layer.kv.access_check = check
 
     def release(self):
         if self.released:

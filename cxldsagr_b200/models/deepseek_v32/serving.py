@@ -172,6 +172,7 @@ class DeepSeekServingBackend:
         session.generation = self.lifecycle.generation
         self._sessions.add(id(session))
         self.lifecycle.register(session)
+        session.bind_serving(self.lifecycle)
         return session
 
     def _check_session(self, session):

@@ -186,3 +186,21 @@ def test_token_digest_is_little_endian_int64():
 
     ids = [1, 2, 2**40]
     assert token_digest(ids) == hashlib.sha256(struct.pack("<3q", *ids)).hexdigest()
+
+
+def test_borrowed_caches_mutate_only_inside_their_operation(tiny3):
+    """A backend session's KV caches refuse mutation outside the backend's operation on that session."""
+    backend = _backend(tiny3, "serial_sparse")
+    runtime = TokenRuntime(backend.runtime_driver(CapacityPolicy.byte_budget(CacheFootprint(1 << 30, 1 << 30))))
+    runtime.allocate_resources(runtime.plan_resources(CapacityPolicy.byte_budget(CacheFootprint(1 << 30, 1 << 30)),
+                                                      LIMITS))
+    s = runtime.create_session(runtime.plan_session(RequestShape(HIST, CAND), "u0"))
+    runtime.prefill(s, torch.randint(0, 150, (HIST,), generator=torch.Generator().manual_seed(1)))
+    model_session = next(iter(backend.lifecycle.sessions))
+    kv = model_session.layers[0].kv
+    with pytest.raises(RuntimeError, match="active operation"):
+        kv.begin_step(1)
+    with pytest.raises(RuntimeError, match="active operation"):
+        kv.truncate(0)
+    assert model_session.length == HIST
+    runtime.release_session(s)
