@@ -228,11 +228,14 @@ void topk(const Tensor& scores, int64_t N, int64_t k, int64_t causal_start, Tens
   TORCH_CHECK(values.is_contiguous() && ids.is_contiguous() && values.size(1) == k && ids.size(1) == k, "topk outputs");
   TORCH_CHECK(N <= scores.size(1), "topk: N exceeds scores width");
   c10::cuda::CUDAGuard g(scores.device());
+  // algo 0: histogram select, descending; 2: histogram select, ascending index order
+  // (rows finished by the multi-pass fallback stay descending); 1: multi-pass only.
+  const bool select = algo == 0 || algo == 2;
   Tensor overflow;
-  if (algo == 0) overflow = torch::zeros({scores.size(0)}, torch::dtype(torch::kInt32).device(scores.device()));
+  if (select) overflow = torch::zeros({scores.size(0)}, torch::dtype(torch::kInt32).device(scores.device()));
   b200::launch_topk_causal(cptr<float>(scores), scores.stride(0), scores.size(0), N, k, causal_start,
                            ptr<float>(values), ptr<int>(ids), err_ptr(scores), stream(),
-                           algo == 0 ? overflow.data_ptr<int>() : nullptr);
+                           select ? overflow.data_ptr<int>() : nullptr, algo == 2);
 }
 
 // ------------------------------------------------------------- attention

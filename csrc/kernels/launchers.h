@@ -209,7 +209,8 @@ void launch_topk(const float* scores, int64_t ld, int R, int N, int k, float* va
 // With `overflow` (R zeroed ints of caller scratch) the two-pass kernel runs
 // first and only rows it flags are redone by the multi-pass kernel.
 void launch_topk_causal(const float* scores, int64_t ld, int R, int N, int k, int causal_start,
-                        float* values, int* ids, int* err, cudaStream_t stream, int* overflow = nullptr);
+                        float* values, int* ids, int* err, cudaStream_t stream, int* overflow = nullptr,
+                        bool index_order = false);
 
 // --------------------------------------------------------------- sparse MLA
 struct MLAArgs {

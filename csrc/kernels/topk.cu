@@ -197,7 +197,9 @@ __global__ void __launch_bounds__(kThreads) topk_kernel(const float* __restrict_
 //     are distinct, so ties are settled by the smaller index with no special
 //     case, and the stage is never sorted;
 //  4. a bitonic sort of the take (<= 2048) results orders them (larger key,
-//     then smaller index).
+//     then smaller index); or, with index_order, the results are marked in a
+//     shared-memory bitmap of the row and written out by ascending index (a
+//     block scan of per-thread bit counts places them), which needs no sort.
 // Row passes read 4 floats per lane per step with two steps in flight, and
 // collect with one warp scan per step instead of a warp vote per element.
 // Rows whose threshold bin still exceeds kSecCap after 32 key bits (one
@@ -206,7 +208,7 @@ __global__ void __launch_bounds__(kThreads) topk_kernel(const float* __restrict_
 __global__ void __launch_bounds__(kThreads2) topk2_kernel(const float* __restrict__ scores, int64_t ld, int N,
                                                           int k, int causal_start, float* __restrict__ values,
                                                           int* __restrict__ ids, int* __restrict__ overflow,
-                                                          int* err) {
+                                                          int* err, bool index_order) {
   extern __shared__ uint8_t dyn[];
   uint32_t* hist = reinterpret_cast<uint32_t*>(dyn);                      // kBins
   uint64_t* cand = reinterpret_cast<uint64_t*>(dyn + kBins * 4);          // kMaxK
@@ -453,6 +455,56 @@ __global__ void __launch_bounds__(kThreads2) topk2_kernel(const float* __restric
   // 4. Order the results.
   const int count = min(int(s_pack & 0xFFFFFFFFull), kMaxK);
   if (count != take && tid == 0) record_error(err, kErrBadIndex);
+  float* vout = values + int64_t(r) * k;
+  int* iout = ids + int64_t(r) * k;
+  if (index_order && row_end <= kSecCap * 64) {
+    // Ascending-index output: mark the taken indices in a bitmap over the row
+    // (the stage is free now), give each thread a contiguous run of words,
+    // and place its indices after an exclusive scan of the per-thread counts.
+    uint32_t* bm = reinterpret_cast<uint32_t*>(sec);
+    const int words = (row_end + 31) / 32;
+    for (int i = tid; i < words; i += kThreads2) bm[i] = 0u;
+    __syncthreads();
+    for (int i = tid; i < count; i += kThreads2) {
+      const int idx = int(0xFFFFFFFFu - uint32_t(cand[i] & 0xFFFFFFFFull));
+      atomicOr(&bm[idx >> 5], 1u << (idx & 31));
+    }
+    __syncthreads();
+    const int per = (words + kThreads2 - 1) / kThreads2;
+    const int w0 = min(words, tid * per), w1 = min(words, w0 + per);
+    uint32_t mine = 0;
+    for (int w = w0; w < w1; ++w) mine += uint32_t(__popc(bm[w]));
+    uint32_t incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_sum[wid] = incl;
+    __syncthreads();
+    uint32_t pos = incl - mine;
+    for (int j = 0; j < wid; ++j) pos += warp_sum[j];
+    for (int w = w0; w < w1; ++w) {
+      uint32_t bits = bm[w];
+      while (bits) {
+        const int idx = w * 32 + __ffs(bits) - 1;
+        bits &= bits - 1u;
+        const float v = row[idx];
+        if (pos < uint32_t(k)) {
+          vout[pos] = v;
+          iout[pos] = (__float_as_uint(v) & 0x7FFFFFFFu) >= 0x7F800000u ? -1 : idx;
+        }
+        ++pos;
+      }
+    }
+    for (int i = count + tid; i < k; i += kThreads2) {
+      vout[i] = -INFINITY;
+      iout[i] = -1;
+    }
+    mark();
+    if (tracing && tid == 0) g_topk_trace[15] = uint64_t(tp);
+    return;
+  }
   // Bitonic sort of n2 = max(64, 2^ceil(log2 count)) composites (zero
   // padding sorts last), descending.  Warp w holds elements [64 w, 64 w + 64)
   // in registers, lane l elements 64 w + l and 64 w + l + 32: every stage of
@@ -522,8 +574,6 @@ __global__ void __launch_bounds__(kThreads2) topk2_kernel(const float* __restric
   }
   __syncthreads();
   mark();
-  float* vout = values + int64_t(r) * k;
-  int* iout = ids + int64_t(r) * k;
   for (int i = tid; i < k; i += kThreads2) {
     if (i < count) {
       const uint64_t c = cand[i];
@@ -555,7 +605,7 @@ void launch_topk(const float* scores, int64_t ld, int R, int N, int k, float* va
 }
 
 void launch_topk_causal(const float* scores, int64_t ld, int R, int N, int k, int causal_start,
-                        float* values, int* ids, int* err, cudaStream_t stream, int* overflow) {
+                        float* values, int* ids, int* err, cudaStream_t stream, int* overflow, bool index_order) {
   if (R <= 0) return;
   if (k < 1 || k > kMaxK) throw std::invalid_argument("topk: k must be in [1, 2048]");
   if (overflow == nullptr) {
@@ -566,7 +616,8 @@ void launch_topk_causal(const float* scores, int64_t ld, int R, int N, int k, in
   const size_t smem = size_t(kBins) * 4 + size_t(kMaxK) * 8 + size_t(kSecCap) * 8;
   cuda_check(cudaFuncSetAttribute(topk2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
              "topk2 smem attribute");
-  topk2_kernel<<<R, kThreads2, smem, stream>>>(scores, ld, N, k, causal_start, values, ids, overflow, err);
+  topk2_kernel<<<R, kThreads2, smem, stream>>>(scores, ld, N, k, causal_start, values, ids, overflow, err,
+                                                index_order);
   cuda_check(cudaGetLastError(), "topk2 launch");
   topk_kernel<<<R, kThreads, 0, stream>>>(scores, ld, N, k, causal_start, values, ids, err, overflow);
   cuda_check(cudaGetLastError(), "topk fallback launch");

@@ -105,14 +105,15 @@ def bench_indexer(Q=1024, N=65536, **_):
     return {"op": "indexer_logits", "Q": Q, "N": N, "ms": ms, "tflops": flops / ms / 1e9}
 
 
-def bench_topk(R=1024, N=65536, k=2048, clustered=False, **_):
+def bench_topk(R=1024, N=65536, k=2048, clustered=False, order="value", causal=False, **_):
     dev = "cuda"
     s = torch.randn(R, N, device=dev)
     if clustered:  # indexer-like: most logits within a narrow band
         s = 10.0 + 0.05 * s
-    ms = time_fn(lambda: ops.exact_topk(s, k))
-    return {"op": "topk", "R": R, "N": N, "k": k, "clustered": clustered, "ms": ms,
-            "read_gbs": R * N * 4 / ms / 1e6}
+    cs = N - R if causal else None
+    ms = time_fn(lambda: ops.exact_topk(s, k, causal_start=cs, order=order))
+    return {"op": "topk", "R": R, "N": N, "k": k, "clustered": clustered, "order": order, "causal": causal,
+            "ms": ms, "read_gbs": R * N * 4 / ms / 1e6}
 
 
 def _p2p_single():
@@ -168,6 +169,8 @@ def main():
     p.add_argument("--locality", type=float, default=0.0)
     p.add_argument("--R", type=int, default=1024)
     p.add_argument("--clustered", action="store_true")
+    p.add_argument("--order", default="value", choices=("value", "index"), help="topk: output order")
+    p.add_argument("--causal", action="store_true", help="topk: rows end at N - R + r (prefill chunk)")
     p.add_argument("--M", type=int, default=1024)
     p.add_argument("--N", type=int, default=36864)
     p.add_argument("--Kdim", type=int, default=7168)
@@ -181,7 +184,7 @@ def main():
         if name in ("ag_gemm", "rs_gemm"):
             kw = dict(M=a.M, N=a.N, Kdim=a.Kdim)
         if name == "topk":
-            kw = dict(R=a.R, clustered=a.clustered)
+            kw = dict(R=a.R, clustered=a.clustered, order=a.order, causal=a.causal)
         print(json.dumps(OPS[name](**kw)))
     torch.cuda.synchronize()
     ops.check_errors("cuda")

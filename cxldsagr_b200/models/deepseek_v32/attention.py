@@ -152,7 +152,9 @@ class AttentionRunner:
                 with scope("indexer_prefetch"):
                     self._predictive_prefetch(state, logits, pos, end)
             with scope("exact_topk"):
-                values, ids = ops.exact_topk(logits, cfg.index_topk, causal_start=qpos, n=end)
+                # The selection in ascending index order: the kernel skips its final
+                # sort, and attention only needs the set in a deterministic order.
+                values, ids = ops.exact_topk(logits, cfg.index_topk, causal_start=qpos, n=end, order="index")
             if self.method == "echo" and cache.offload:
                 with scope("prefetch_hint"):
                     self._update_hints(state, logits, values, pos, end)
@@ -223,7 +225,8 @@ class AttentionRunner:
         else:
             off[0] = ops.reference.prefetch_hint(logits[:, :end])
         if logits.shape[0] == 1 and end >= 32768:
-            off[1] = ops.reference.decode_hint(off[1], values[0, -1])
+            # kth score = the smallest selected one (the selection is index-ordered)
+            off[1] = ops.reference.decode_hint(off[1], values[0].min())
 
 
 def _order_bins(x: torch.Tensor) -> torch.Tensor:

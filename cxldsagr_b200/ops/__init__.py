@@ -211,12 +211,20 @@ def indexer_logits(q, k, weights, kscale, query_start: int, *, out=None):
     return out
 
 
-def exact_topk(scores, k: int, *, causal_start: int | None = None, n: int | None = None, algo: int = 0):
-    """Descending top-k (ties -> smaller index), -1 ids for non-finite/empty slots.
+def exact_topk(scores, k: int, *, causal_start: int | None = None, n: int | None = None, algo: int = 0,
+               order: str = "value"):
+    """Exact top-k (ties -> smaller index), -1 ids for non-finite/empty slots.
 
     ``causal_start`` restricts row r to columns [0, causal_start + r + 1).
     Output width is min(k, n) like the reference selection API.
+    ``order="value"`` lists the selection by descending value; ``order="index"``
+    lists the same selection by ascending index (padding last), which skips the
+    kernel's final sort -- for consumers that need the set in a deterministic
+    order, not its ranking (rows with one value shared by more than 6,144 keys
+    are finished by the multi-pass kernel and stay value-ordered).
     """
+    if order not in ("value", "index"):
+        raise ValueError("order must be 'value' or 'index'")
     n = scores.shape[1] if n is None else n
     count = min(k, n)
     if not _cuda(scores):
@@ -225,7 +233,14 @@ def exact_topk(scores, k: int, *, causal_start: int | None = None, n: int | None
             rows = torch.arange(s.shape[0])[:, None]
             cols = torch.arange(n)[None, :]
             s = s.masked_fill(cols > causal_start + rows, -torch.inf)
-        return reference.exact_topk(s, count)
+        values, ids = reference.exact_topk(s, count)
+        if order == "index":
+            key = torch.where(ids >= 0, ids.long(), torch.iinfo(torch.int64).max)
+            perm = key.argsort(dim=-1, stable=True)
+            values, ids = values.gather(1, perm).contiguous(), ids.gather(1, perm).contiguous()
+        return values, ids
+    if order == "index" and algo == 0:
+        algo = 2
     R = scores.shape[0]
     values = torch.empty((R, count), dtype=torch.float32, device=scores.device)
     ids = torch.empty((R, count), dtype=torch.int32, device=scores.device)

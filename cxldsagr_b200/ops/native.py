@@ -19,7 +19,7 @@ class NativeUnavailable(RuntimeError):
 # Entry points that launch more than one kernel per call.
 _MULTI_LAUNCH = {
     "sparse_mla": lambda args: 2 if len(args) > 6 and int(args[6]) > 1 else 1,  # + LSE combine
-    "topk": lambda args: 3 if len(args) > 6 and int(args[6]) == 0 else 1,       # zero + 2-pass + fallback
+    "topk": lambda args: 3 if len(args) > 6 and int(args[6]) in (0, 2) else 1,  # zero + select + fallback
 }
 
 

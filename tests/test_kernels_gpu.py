@@ -458,3 +458,25 @@ def test_echo_hint_matches_reference(rows, cols):
     ops.lib().echo_hint(logits, rows, cols, offset)
     want = ref.prefetch_hint(logits[:, :cols].cpu())
     assert abs(float(offset[0]) - float(want)) < 1e-4 * max(1.0, abs(float(want)))
+
+
+@pytest.mark.parametrize("R,N,k,cs,pad,ties", [(3, 100, 64, None, 0, False), (5, 5000, 2048, None, 0, False),
+                                               (300, 65536, 2048, None, 0, False), (40, 9000, 2048, 1000, 3, True),
+                                               (6, 3000, 2048, 1000, 0, True), (4, 1500, 2048, None, 0, False)])
+def test_topk_index_order(R, N, k, cs, pad, ties):
+    """order="index": the exact selection of the value-ordered kernel, listed by ascending index."""
+    torch.manual_seed(21)
+    base = torch.randn(R, N + pad, device=DEV)
+    s = (10.0 + 0.01 * base).half().float() if ties else base
+    view = s[:, pad:] if pad else s
+    v, i = ops.exact_topk(view, k, causal_start=cs, order="index")
+    rows = torch.arange(R)[:, None]
+    cols = torch.arange(N)[None, :]
+    masked = view.cpu() if cs is None else view.cpu().masked_fill(cols > cs + rows, -torch.inf)
+    rv, ri = ref.exact_topk(masked, k)
+    got = i.cpu()
+    assert torch.equal(torch.sort(got, dim=1).values, torch.sort(ri, dim=1).values)
+    valid = got >= 0
+    big = torch.where(valid, got, torch.iinfo(torch.int32).max)
+    assert torch.equal(big, torch.sort(big, dim=1).values)  # ascending, padding last
+    assert torch.equal(v.cpu()[valid], masked.gather(1, got.clamp_min(0).long())[valid])
