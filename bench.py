@@ -5,7 +5,7 @@ last-token LM head), 64K-token prefill then a 128-token extend, per B200.
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N   (N > 1)
     python bench.py --impl reference     (the reference arm)
 
-One step = one request: reset the KV caches, prefill 64 x 1024-token chunks,
+One step = one request: reset the KV caches, prefill 32 x 2048-token chunks,
 then the 128-token extend (replayed from a CUDA graph captured at 64K, like the
 reference's full extend graph).  With N GPUs every rank serves its own request
 (data-parallel requests, weak scaling); ``value`` is the box's prefill
@@ -44,7 +44,9 @@ def parse():
     p.add_argument("--method", default="hbm", choices=["hbm", "serial_sparse", "echo", "dense_prefetch"])
     p.add_argument("--history", type=int, default=65536)
     p.add_argument("--extend", type=int, default=128)
-    p.add_argument("--chunk", type=int, default=1024)
+    p.add_argument("--chunk", type=int, default=2048, help="prefill chunk tokens (the reference's default 2048)")
+    p.add_argument("--select-rows", type=int, default=None,
+                   help="rows per indexer + top-k round inside a chunk (0: whole chunk; default: the model's)")
     p.add_argument("--layers", type=int, default=3)
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--e2e-steps", type=int, default=2)
@@ -107,6 +109,9 @@ def main():
 
         par = ParallelContext(rank, world, dist.group.WORLD, dev, backend=args.comm)
     model = DeepSeekV32Model(cfg, src, device=dev, cache=cache, parallel=par)
+    if args.select_rows is not None:
+        for block in model.blocks:
+            block.attention.select_rows = args.select_rows
     del src
     torch.cuda.empty_cache()
 
@@ -252,6 +257,7 @@ def main():
                 "history": H,
                 "extend": A,
                 "chunk": args.chunk,
+                "select_rows": model.blocks[0].attention.select_rows,
                 "cache_method": args.method,
                 "pool_tokens": (H + A) if offload else None,
                 "extend_residency": "cold (HBM copies of the history dropped before the extend)" if offload else "resident",

@@ -212,7 +212,7 @@ def indexer_logits(q, k, weights, kscale, query_start: int, *, out=None):
 
 
 def exact_topk(scores, k: int, *, causal_start: int | None = None, n: int | None = None, algo: int = 0,
-               order: str = "value"):
+               order: str = "value", out=None):
     """Exact top-k (ties -> smaller index), -1 ids for non-finite/empty slots.
 
     ``causal_start`` restricts row r to columns [0, causal_start + r + 1).
@@ -242,8 +242,11 @@ def exact_topk(scores, k: int, *, causal_start: int | None = None, n: int | None
     if order == "index" and algo == 0:
         algo = 2
     R = scores.shape[0]
-    values = torch.empty((R, count), dtype=torch.float32, device=scores.device)
-    ids = torch.empty((R, count), dtype=torch.int32, device=scores.device)
+    if out is not None:  # caller-owned [R, count] outputs (row slices of a larger result)
+        values, ids = out
+    else:
+        values = torch.empty((R, count), dtype=torch.float32, device=scores.device)
+        ids = torch.empty((R, count), dtype=torch.int32, device=scores.device)
     lib().topk(scores, n, count, -1 if causal_start is None else causal_start, values, ids, algo)
     return values, ids
 

@@ -480,3 +480,27 @@ def test_topk_index_order(R, N, k, cs, pad, ties):
     big = torch.where(valid, got, torch.iinfo(torch.int32).max)
     assert torch.equal(big, torch.sort(big, dim=1).values)  # ascending, padding last
     assert torch.equal(v.cpu()[valid], masked.gather(1, got.clamp_min(0).long())[valid])
+
+
+@pytest.mark.parametrize("method", ["hbm", "serial_sparse"])
+def test_indexer_topk_rounds_match_whole_chunk(method):
+    """Running the indexer + top-k in L2-sized row rounds (an option) gives the whole-chunk result bit for bit."""
+    from cxldsagr_b200.checkpoint import StateDictSource, random_state_dict
+    from cxldsagr_b200.config import CacheConfig, v32_config
+    from cxldsagr_b200.models.deepseek_v32.model import DeepSeekV32Model
+
+    cfg = v32_config(1)
+    src = StateDictSource(random_state_dict(cfg, layers=[0], seed=0, device=DEV))
+    g = torch.Generator().manual_seed(3)
+    hist = torch.randint(0, cfg.vocab_size, (3000,), generator=g).to(DEV)
+    ext = torch.randint(0, cfg.vocab_size, (16,), generator=g).to(DEV)
+    outs = []
+    for rows in (0, 296):
+        kw = {} if method == "hbm" else {"pool_tokens": 3072 + 16, "host_tokens": 3072 + 16}
+        cache = CacheConfig(method=method, capacity=3072 + 16, chunk_size=1024, candidate_tokens=16, **kw)
+        m = DeepSeekV32Model(cfg, src, device=DEV, cache=cache)
+        m.blocks[0].attention.select_rows = rows
+        outs.append((m.prefill(hist).logits, m.extend(ext).logits, m.blocks[0].attention.last_indices.clone()))
+        del m
+    ops.check_errors(DEV)
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
