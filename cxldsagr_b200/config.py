@@ -209,7 +209,7 @@ class CacheConfig:
     host_tokens: int | None = None
     candidate_tokens: int = 0
     page_size: int = 64
-    chunk_size: int = 1024
+    chunk_size: int = 2048
 
     METHODS = ("hbm", "echo", "serial_sparse", "dense_prefetch")
 
