@@ -200,8 +200,9 @@ __global__ void __launch_bounds__(kThreads) topk_kernel(const float* __restrict_
 //     then smaller index); or, with index_order, the results are marked in a
 //     shared-memory bitmap of the row and written out by ascending index (a
 //     block scan of per-thread bit counts places them), which needs no sort.
-// Row passes read 4 floats per lane per step with two steps in flight, and
-// collect with one warp scan per step instead of a warp vote per element.
+// Row passes read 4 floats per lane per step with several steps in flight;
+// the collect pass appends with one shared atomic per lane that selected
+// anything (selections are sparse), with no warp collective per step.
 // Rows whose threshold bin still exceeds kSecCap after 32 key bits (one
 // value shared by > kSecCap keys) set *overflow and are finished by the
 // multi-pass kernel.
@@ -277,34 +278,29 @@ __global__ void __launch_bounds__(kThreads2) topk2_kernel(const float* __restric
   auto hist_add = [&](uint32_t bin) {
     if (bin != 0xFFFFFFFFu) atomicAdd(&hist[bin], 1u);
   };
-  // Append this lane's selected elements to cand / sec with one warp scan of
-  // the packed per-lane counts and one shared atomic per warp.
+  // Append this lane's selected elements (a few percent of the row) to cand /
+  // sec: one shared atomic per lane and list that has any, no warp collective,
+  // so the common all-below-threshold step costs only the comparisons.  The
+  // low / high words of s_pack count cand / sec entries.
+  unsigned int* cnt = reinterpret_cast<unsigned int*>(&s_pack);
   auto collect = [&](const uint32_t (&keys)[4], int e0, uint32_t gmask, uint32_t smask) {
-    const uint32_t mine = uint32_t(__popc(gmask)) | (uint32_t(__popc(smask)) << 16);
-    uint32_t incl = mine;
+    if (gmask) {
+      uint32_t pg = atomicAdd(&cnt[0], uint32_t(__popc(gmask)));
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
+      for (int j = 0; j < 4; ++j)
+        if (gmask >> j & 1u) {
+          if (pg < uint32_t(kMaxK)) cand[pg] = composite(keys[j], e0 + j);
+          ++pg;
+        }
     }
-    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
-    if (total == 0) return;
-    unsigned long long base = 0;
-    if (lane == 31)
-      base = atomicAdd(&s_pack, (unsigned long long)(total & 0xFFFFu) | ((unsigned long long)(total >> 16) << 32));
-    base = __shfl_sync(0xffffffffu, base, 31);
-    uint32_t pg = uint32_t(base & 0xFFFFFFFFull) + ((incl - mine) & 0xFFFFu);
-    uint32_t ps = uint32_t(base >> 32) + ((incl - mine) >> 16);
+    if (smask) {
+      uint32_t ps = atomicAdd(&cnt[1], uint32_t(__popc(smask)));
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (gmask >> j & 1u) {
-        if (pg < uint32_t(kMaxK)) cand[pg] = composite(keys[j], e0 + j);
-        ++pg;
-      }
-      if (smask >> j & 1u) {
-        if (ps < uint32_t(kSecCap)) sec[ps] = composite(keys[j], e0 + j);
-        ++ps;
-      }
+      for (int j = 0; j < 4; ++j)
+        if (smask >> j & 1u) {
+          if (ps < uint32_t(kSecCap)) sec[ps] = composite(keys[j], e0 + j);
+          ++ps;
+        }
     }
   };
   // Suffix search over hist[0, nbins): the bin holding rank `rank` counting
