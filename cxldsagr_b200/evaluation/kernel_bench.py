@@ -183,6 +183,8 @@ def main():
             kw = dict(M=a.M, N=a.N, K=a.Kdim, ue8m0=a.block_scaled)
         if name in ("ag_gemm", "rs_gemm"):
             kw = dict(M=a.M, N=a.N, Kdim=a.Kdim)
+        if name == "indexer":
+            kw = dict(Q=a.R)
         if name == "topk":
             kw = dict(R=a.R, clustered=a.clustered, order=a.order, causal=a.causal)
         print(json.dumps(OPS[name](**kw)))
