@@ -180,7 +180,8 @@ class AttentionRunner:
             self.last_indices = ids
             with scope("sparse_mla"):
                 if state.dense is not None:
-                    attn = ops.sparse_mla(q_proj, state.dense, ids, cfg.attention_scale, value_dim=cfg.kv_lora_rank)
+                    attn = ops.sparse_mla(q_proj, state.dense, ids, cfg.attention_scale, value_dim=cfg.kv_lora_rank,
+                                          splits=ops.mla_splits(q_proj.shape[0], ids.shape[1]))
                 else:
                     attn = self._consume(cache, q_proj, ids)
         return self._output(attn, T_loc, scope)
@@ -228,7 +229,8 @@ class AttentionRunner:
 
     def _consume(self, cache, q, ids):
         if not cache.offload:
-            return ops.sparse_mla(q, cache.records, ids, self.cfg.attention_scale, value_dim=self.cfg.kv_lora_rank)
+            return ops.sparse_mla(q, cache.records, ids, self.cfg.attention_scale, value_dim=self.cfg.kv_lora_rank,
+                                  splits=ops.mla_splits(q.shape[0], ids.shape[1]))
         try:
             physical = cache.ensure(ids)
         except WorkingSetTooLarge:
@@ -237,7 +239,8 @@ class AttentionRunner:
             cache.stats.capacity_splits += 1
             mid = len(q) // 2
             return torch.cat((self._consume(cache, q[:mid], ids[:mid]), self._consume(cache, q[mid:], ids[mid:])))
-        return ops.sparse_mla(q, cache.records, physical, self.cfg.attention_scale, value_dim=self.cfg.kv_lora_rank)
+        return ops.sparse_mla(q, cache.records, physical, self.cfg.attention_scale, value_dim=self.cfg.kv_lora_rank,
+                              splits=ops.mla_splits(q.shape[0], ids.shape[1]))
 
     # ------------------------------------------------------------ echo method
     def _predictive_prefetch(self, state, logits, pos, end):

@@ -332,6 +332,16 @@ def sparse_mla(q, kv, ids, scale, *, splits: int = 1, return_lse: bool = False, 
     return (out, lse) if return_lse else out
 
 
+def mla_splits(T: int, K: int = 2048, *, clusters: int = 74) -> int:
+    """Split-K factor for the 2-CTA sparse MLA: few queries (decode, short
+    extends) leave most of the 74 cluster slots (148 SMs) idle, so split each
+    query's selection until ~all are busy, keeping >= 64 keys (two tiles) per
+    split; 32 splits at most (the combine's limit)."""
+    if T >= clusters:
+        return 1
+    return max(1, min(32, clusters // max(T, 1), K // 64))
+
+
 def sparse_mla_decode(q, kv, ids, scale, splits: int = 16):
     """Single-query decode: split the selection over ``splits`` CTAs and LSE-merge."""
     return sparse_mla(q, kv, ids, scale, splits=splits)
