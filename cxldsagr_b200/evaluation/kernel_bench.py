@@ -41,10 +41,19 @@ def flush_l2(dev):
     _L2_FLUSH.zero_()
 
 
+GRAPH = False  # set by --graph: replay each op from a CUDA graph (no host launch cost in the timing)
+
+
 def time_fn(fn, *, warmup=3, iters=10, flush=True, dev="cuda"):
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
+    if GRAPH:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        torch.cuda.synchronize()
+        fn = graph.replay
     total = 0.0
     for _ in range(iters):
         if flush:
@@ -175,7 +184,10 @@ def main():
     p.add_argument("--N", type=int, default=36864)
     p.add_argument("--Kdim", type=int, default=7168)
     p.add_argument("--block-scaled", action="store_true", help="fp8_gemm: block-scaled (UE8M0) tensor-core path")
+    p.add_argument("--graph", action="store_true", help="time CUDA-graph replays (small, launch-bound ops)")
     a = p.parse_args()
+    global GRAPH
+    GRAPH = a.graph
     names = list(OPS) if a.op == "all" else a.op.split(",")
     for name in names:
         kw = dict(T=a.T, K=a.K, P=a.P, splits=a.splits, impl=a.impl, locality=a.locality)
