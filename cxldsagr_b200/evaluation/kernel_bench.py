@@ -67,7 +67,21 @@ def time_fn(fn, *, warmup=3, iters=10, flush=True, dev="cuda"):
     return total / iters
 
 
-def bench_sparse_mla(T=256, K=2048, P=65664, splits=1, impl=0, locality=0.0, **_):
+def mla_timeline(q, kv, ids, splits: int) -> dict:
+    """Phase clocks (SM cycles) of the first 2-CTA cluster of one tcgen05 MLA launch
+    (kernel debug bit 64): Q resident in TMEM, each tile's P stored, epilogue, exit."""
+    ops.sparse_mla(q, kv, ids, 0.1, splits=splits, impl=16 + 64)
+    torch.cuda.synchronize()
+    tr = ops.lib().sparse_mla_trace()
+    t0 = int(tr[0, 64, 0])
+    n = min(64, -(-ids.shape[1] // splits) // 32)
+    p_stored = [int(tr[0, i, 7]) - t0 for i in range(n)]
+    return {"q_in_tmem": int(tr[0, 64, 1]) - t0, "first_p": p_stored[0], "last_p": p_stored[-1],
+            "cycles_per_tile": (p_stored[-1] - p_stored[0]) / max(1, n - 1),
+            "epilogue_start": int(tr[0, 64, 2]) - t0, "exit": int(tr[0, 64, 3]) - t0, "tiles": n}
+
+
+def bench_sparse_mla(T=256, K=2048, P=65664, splits=1, impl=0, locality=0.0, trace=False, **_):
     dev = "cuda"
     g = torch.Generator(device=dev).manual_seed(0)
     q = (torch.randn(T, 128, 576, device=dev, generator=g) * 0.5).bfloat16()
@@ -78,12 +92,14 @@ def bench_sparse_mla(T=256, K=2048, P=65664, splits=1, impl=0, locality=0.0, **_
         mask = torch.rand(T, K, device=dev, generator=g) < locality
         ids = torch.where(mask, hot[None, :].expand(T, K), ids)
     ms = time_fn(lambda: ops.sparse_mla(q, kv, ids, 0.1, splits=splits, impl=impl))
+    timeline = mla_timeline(q, kv, ids, splits) if trace else None
     flops = 2.0 * T * 128 * K * (576 + 512)
     gather = T * K * 1152.0
     pk = _peaks()
     return {"op": "sparse_mla", "T": T, "K": K, "P": P, "splits": splits, "impl": impl, "ms": ms,
             "tflops": flops / ms / 1e9, "frac_bf16_peak": flops / ms / 1e9 / pk["bf16_tflops"],
-            "gather_gbs": gather / ms / 1e6, "peaks": pk["source"]}
+            "gather_gbs": gather / ms / 1e6, "peaks": pk["source"],
+            **({"timeline_cycles": timeline} if timeline else {})}
 
 
 def bench_fp8_gemm(M=1024, N=36864, K=7168, ue8m0=False, **_):
@@ -184,13 +200,14 @@ def main():
     p.add_argument("--N", type=int, default=36864)
     p.add_argument("--Kdim", type=int, default=7168)
     p.add_argument("--block-scaled", action="store_true", help="fp8_gemm: block-scaled (UE8M0) tensor-core path")
+    p.add_argument("--trace", action="store_true", help="sparse_mla: phase clocks of the first cluster")
     p.add_argument("--graph", action="store_true", help="time CUDA-graph replays (small, launch-bound ops)")
     a = p.parse_args()
     global GRAPH
     GRAPH = a.graph
     names = list(OPS) if a.op == "all" else a.op.split(",")
     for name in names:
-        kw = dict(T=a.T, K=a.K, P=a.P, splits=a.splits, impl=a.impl, locality=a.locality)
+        kw = dict(T=a.T, K=a.K, P=a.P, splits=a.splits, impl=a.impl, locality=a.locality, trace=a.trace)
         if name == "fp8_gemm":
             kw = dict(M=a.M, N=a.N, K=a.Kdim, ue8m0=a.block_scaled)
         if name in ("ag_gemm", "rs_gemm"):
