@@ -504,3 +504,26 @@ def test_indexer_topk_rounds_match_whole_chunk(method):
         del m
     ops.check_errors(DEV)
     assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
+def test_model_replay_is_deterministic():
+    """The same request twice (reset in between) gives bitwise equal logits: no
+    order-dependent atomics reach the results (top-k, MoE layout, split-K)."""
+    from cxldsagr_b200.checkpoint import StateDictSource, random_state_dict
+    from cxldsagr_b200.config import CacheConfig, v32_config
+    from cxldsagr_b200.models.deepseek_v32.model import DeepSeekV32Model
+
+    cfg = v32_config(1)
+    src = StateDictSource(random_state_dict(cfg, layers=[0], seed=1, device=DEV))
+    g = torch.Generator().manual_seed(4)
+    hist = torch.randint(0, cfg.vocab_size, (2500,), generator=g).to(DEV)
+    ext = torch.randint(0, cfg.vocab_size, (1,), generator=g).to(DEV)
+    cache = CacheConfig(method="serial_sparse", capacity=2560, chunk_size=1024, candidate_tokens=1,
+                        pool_tokens=2560, host_tokens=2560)
+    m = DeepSeekV32Model(cfg, src, device=DEV, cache=cache)
+    runs = []
+    for _ in range(2):
+        m.reset()
+        runs.append((m.prefill(hist).logits.clone(), m.extend(ext).logits.clone()))
+    ops.check_errors(DEV)
+    assert torch.equal(runs[0][0], runs[1][0]) and torch.equal(runs[0][1], runs[1][1])
