@@ -14,7 +14,7 @@
 // shared memory), N = 4 queries x 64 heads = 256 (B = the 4 queries' Q rows),
 // K = 128 -> a 128x256 FP32 accumulator in TMEM.  Both operands are naturally
 // K-major 128-byte rows, so TMA writes them with the 128-byte swizzle and the
-// MMA reads them unchanged.  Two accumulators (512 TMEM columns) let the 8
+// MMA reads them unchanged.  Two accumulators (512 TMEM columns) let the 16
 // epilogue warps reduce tile i while the tensor core computes tile i+1.
 //
 // Work unit = (query block of 4, chunk of key tiles); persistent CTAs walk the
@@ -31,7 +31,8 @@ constexpr int QB = 4;                 // queries per unit
 constexpr int BKV = 128;              // keys per tile
 constexpr int NQ = QB * kHeads;       // 256 MMA columns
 constexpr int kStages = 8;
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;
+constexpr int kQPW = QB * 4 / kEpiWarps;  // queries per epilogue warp (4 warps cover a lane quadrant each)
 constexpr int kThreads = 64 + kEpiWarps * 32;
 
 struct Smem {
@@ -40,7 +41,7 @@ struct Smem {
   uint64_t q_full[2], q_empty[2];
   uint64_t k_full[kStages], k_empty[kStages];
   uint64_t tmem_full[2], tmem_empty[2];
-  alignas(16) float w[kEpiWarps][2][kHeads];  // per-warp head weights of its 2 queries
+  alignas(16) float w[kEpiWarps][kQPW][kHeads];  // per-warp head weights of its queries
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -162,9 +163,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    const int ew = warp - 2;             // 0..7
+    const int ew = warp - 2;             // 0..kEpiWarps-1
     const int quad = warp & 3;           // TMEM lane quadrant
-    const int half = ew / 4;             // which 2 of the 4 queries
+    const int qgrp = ew / 4;             // which kQPW of the 4 queries
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     const int key_in_tile = quad * 32 + lane;
     uint32_t tcount = 0;
@@ -172,19 +173,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
       int qb, t0, t1;
       if (!sch.unit(u, qb, t0, t1)) continue;
-      // Each warp stages its own 2 queries' head weights (private slice:
+      // Each warp stages its own queries' head weights (private slice:
       // only __syncwarp ordering is needed, no cross-warp barrier).
       __syncwarp();
 #pragma unroll
-      for (int e = lane; e < 2 * kHeads; e += 32) {
+      for (int e = lane; e < kQPW * kHeads; e += 32) {
         const int j = e / kHeads, h = e % kHeads;
-        const int qc = min(qb * QB + half * 2 + j, sch.Q - 1);
+        const int qc = min(qb * QB + qgrp * kQPW + j, sch.Q - 1);
         s.w[ew][j][h] = __ldg(w + int64_t(qc) * kHeads + h);
       }
       __syncwarp();
-      int qidx[2];
+      int qidx[kQPW];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) qidx[j] = qb * QB + half * 2 + j;
+      for (int j = 0; j < kQPW; ++j) qidx[j] = qb * QB + qgrp * kQPW + j;
       for (int t = t0; t < t1; ++t, ++tcount) {
         const uint32_t buf = tcount & 1, bpar = (tcount >> 1) & 1;
         const int key = t * BKV + key_in_tile;
@@ -194,9 +195,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        float out[2];
+        float out[kQPW];
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
+        for (int j = 0; j < kQPW; ++j) {
           // Two packed FP32x2 accumulators (even / odd heads of each quad);
           // the ReLU stays scalar (there is no packed max).
           float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
@@ -204,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             uint32_t r[32];
-            tmem_ld32(tmem + lane_addr + buf * NQ + (half * 2 + j) * kHeads + c * 32, r);
+            tmem_ld32(tmem + lane_addr + buf * NQ + (qgrp * kQPW + j) * kHeads + c * 32, r);
             tmem_wait_ld();
 #pragma unroll
             for (int h4 = 0; h4 < 8; ++h4) {
@@ -222,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&s.tmem_empty[buf]);
         if (key < sch.N) {
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
+          for (int j = 0; j < kQPW; ++j) {
             if (qidx[j] < sch.Q) {
               const bool visible = key <= sch.query_start + qidx[j];
               logits[int64_t(qidx[j]) * ldl + key] = visible ? out[j] : -INFINITY;
