@@ -34,6 +34,24 @@ def _peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
+FP8_NOMINAL_TFLOPS = 4500.0  # dense FP8 nominal; no measured FP8 denominator exists
+
+
+def roofline(ms: float, *, flops: float = 0.0, nbytes: float = 0.0, fp8: bool = False) -> dict:
+    """Achieved / roofline time, where the roofline is the slower of FLOPs / peak
+    (measured BF16 GEMM; nominal 4.5 PF for FP8 work) and bytes / measured copy
+    bandwidth.  Values near 1 mean the kernel runs at the bound."""
+    pk = _peaks()
+    peak = FP8_NOMINAL_TFLOPS if fp8 else pk["bf16_tflops"]
+    t_compute = flops / (peak * 1e9) if flops else 0.0      # ms
+    t_memory = nbytes / (pk["hbm_gbs"] * 1e6) if nbytes else 0.0
+    bound = max(t_compute, t_memory)
+    return {"roofline_ms": bound, "frac_of_roofline": bound / ms if ms > 0 else None,
+            "bound": "compute" if t_compute >= t_memory else "memory",
+            "compute_peak": f"{peak:.0f} TFLOP/s ({'nominal FP8' if fp8 else pk['source'] + ' BF16'})",
+            "hbm_gbs": pk["hbm_gbs"]}
+
+
 def flush_l2(dev):
     global _L2_FLUSH
     if _L2_FLUSH is None:
@@ -99,6 +117,7 @@ def bench_sparse_mla(T=256, K=2048, P=65664, splits=1, impl=0, locality=0.0, tra
     return {"op": "sparse_mla", "T": T, "K": K, "P": P, "splits": splits, "impl": impl, "ms": ms,
             "tflops": flops / ms / 1e9, "frac_bf16_peak": flops / ms / 1e9 / pk["bf16_tflops"],
             "gather_gbs": gather / ms / 1e6, "peaks": pk["source"],
+            **roofline(ms, flops=flops, nbytes=gather + T * 128 * (576 + 512) * 2),
             **({"timeline_cycles": timeline} if timeline else {})}
 
 
@@ -113,7 +132,8 @@ def bench_fp8_gemm(M=1024, N=36864, K=7168, ue8m0=False, **_):
     ms = time_fn(lambda: ops.fp8_gemm(q, s_t, w, s, out=out, ue8m0=ue8m0))
     flops = 2.0 * M * N * K
     return {"op": "fp8_gemm", "M": M, "N": N, "K": K, "ue8m0": ue8m0, "ms": ms, "tflops": flops / ms / 1e9,
-            "bytes_gbs": (N * K + M * K + M * N * 2) / ms / 1e6}
+            "bytes_gbs": (N * K + M * K + M * N * 2) / ms / 1e6,
+            **roofline(ms, flops=flops, nbytes=N * K + M * K + M * N * 2, fp8=True)}
 
 
 def bench_indexer(Q=1024, N=65536, **_):
@@ -127,7 +147,8 @@ def bench_indexer(Q=1024, N=65536, **_):
     ms = time_fn(lambda: ops.lib().indexer_logits(q, k, w, ks, out, start))
     visible = Q * start + Q * (Q + 1) / 2
     flops = 2.0 * 64 * 128 * visible
-    return {"op": "indexer_logits", "Q": Q, "N": N, "ms": ms, "tflops": flops / ms / 1e9}
+    return {"op": "indexer_logits", "Q": Q, "N": N, "ms": ms, "tflops": flops / ms / 1e9,
+            **roofline(ms, flops=flops, nbytes=N * 132 + Q * 64 * 132 + visible * 4, fp8=True)}
 
 
 def bench_topk(R=1024, N=65536, k=2048, clustered=False, order="value", causal=False, **_):
@@ -138,7 +159,7 @@ def bench_topk(R=1024, N=65536, k=2048, clustered=False, order="value", causal=F
     cs = N - R if causal else None
     ms = time_fn(lambda: ops.exact_topk(s, k, causal_start=cs, order=order))
     return {"op": "topk", "R": R, "N": N, "k": k, "clustered": clustered, "order": order, "causal": causal,
-            "ms": ms, "read_gbs": R * N * 4 / ms / 1e6}
+            "ms": ms, "read_gbs": R * N * 4 / ms / 1e6, **roofline(ms, nbytes=R * N * 4 + R * k * 8)}
 
 
 def _p2p_single():
