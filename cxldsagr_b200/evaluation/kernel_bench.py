@@ -117,7 +117,8 @@ def bench_sparse_mla(T=256, K=2048, P=65664, splits=1, impl=0, locality=0.0, tra
     return {"op": "sparse_mla", "T": T, "K": K, "P": P, "splits": splits, "impl": impl, "ms": ms,
             "tflops": flops / ms / 1e9, "frac_bf16_peak": flops / ms / 1e9 / pk["bf16_tflops"],
             "gather_gbs": gather / ms / 1e6, "peaks": pk["source"],
-            **roofline(ms, flops=flops, nbytes=gather + T * 128 * (576 + 512) * 2),
+            # distinct KV rows (repeats across queries hit L2) + Q + O
+            **roofline(ms, flops=flops, nbytes=int(torch.unique(ids).numel()) * 1152 + T * 128 * (576 + 512) * 2),
             **({"timeline_cycles": timeline} if timeline else {})}
 
 
