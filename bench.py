@@ -67,6 +67,31 @@ def reference_arm():
     print(json.dumps({"impl": "reference", "metric": METRIC, "unavailable": reason}))
 
 
+def prefill_scope_flops(cfg, history: int, layers: int, topk: int = 2048) -> dict:
+    """Algorithmic FLOPs of the main prefill scopes (all chunks, all layers):
+    sparse MLA over min(topk, position + 1) keys per query (QK 576 + PV 512 per
+    head), the causal FP8 indexer (64 heads x 128), the dense MLP (gate/up +
+    down) and o_proj."""
+    H = cfg.n_heads
+    keys = sum(min(topk, p + 1) for p in range(min(history, topk))) + max(0, history - topk) * topk
+    return {
+        "sparse_mla": layers * 2.0 * H * keys * (cfg.qk_head_dim + cfg.kv_lora_rank),
+        "indexer": layers * 2.0 * cfg.index_n_heads * cfg.index_head_dim * history * (history + 1) / 2,
+        "dense_mlp": layers * 2.0 * history * cfg.dim * cfg.intermediate_size * 3,
+        "attention_output/o_proj": layers * 2.0 * history * H * cfg.v_head_dim * cfg.dim,
+    }
+
+
+def scope_rooflines(scopes: dict, flops: dict) -> dict:
+    """Achieved TFLOP/s per scope from a ``--profile`` summary."""
+    out = {}
+    for name, f in flops.items():
+        ms = scopes.get(name, {}).get("ms")
+        if ms:
+            out[name] = {"ms": round(ms, 3), "tflops": round(f / ms / 1e9, 1)}
+    return out
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -169,7 +194,9 @@ def main():
         model.extend(ext)
         extend_scopes = scope.summary()
         model.scope = None
-        print(json.dumps({"profile_prefill": prefill_scopes, "profile_extend_eager": extend_scopes}), file=sys.stderr)
+        rates = scope_rooflines(prefill_scopes, prefill_scope_flops(cfg, H, n_layers))
+        print(json.dumps({"profile_prefill": prefill_scopes, "profile_extend_eager": extend_scopes,
+                          "prefill_scope_tflops": rates}), file=sys.stderr)
 
     launches0 = launch_count()
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]

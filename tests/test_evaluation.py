@@ -115,3 +115,22 @@ def test_native_build_identity(tmp_path, monkeypatch):
     monkeypatch.setattr(bi, "RECORD", fake)
     with pytest.raises(RuntimeError, match="stale"):
         bi.verify()
+
+
+def test_bench_scope_flops():
+    """bench.py's per-scope FLOP model: causal indexer pairs, top-2048 MLA keys, achieved TFLOP/s."""
+    import importlib.util
+    from pathlib import Path
+
+    from cxldsagr_b200.config import v32_config
+
+    spec = importlib.util.spec_from_file_location("bench_mod", Path(__file__).resolve().parents[1] / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    cfg = v32_config(1)
+    f = bench.prefill_scope_flops(cfg, 4096, 1)
+    keys = sum(min(2048, p + 1) for p in range(2048)) + 2048 * 2048
+    assert f["sparse_mla"] == 2.0 * 128 * keys * (576 + 512)
+    assert f["indexer"] == 2.0 * 64 * 128 * 4096 * 4097 / 2
+    r = bench.scope_rooflines({"indexer": {"ms": 1.0}}, f)
+    assert r["indexer"]["tflops"] == round(f["indexer"] / 1e9, 1) and "sparse_mla" not in r
