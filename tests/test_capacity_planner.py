@@ -63,3 +63,17 @@ def test_allocator_tail():
     assert allocator_tail(0) == 0
     assert allocator_tail(512) == 0 and allocator_tail(513) == 511
     assert allocator_tail(3 << 20) == 1 << 20
+
+
+def test_capacity_cli(capsys):
+    import json
+
+    from cxldsagr_b200.models.deepseek_v32.capacity import main
+
+    main(["--num-layers", "3", "--history", "65536", "--candidate", "1280", "--fixed-p", "65536", "--dram-gib", "64"])
+    out = json.loads(capsys.readouterr().out)
+    assert out["feasible"] and out["max_full_sessions"] == out["max_host_arena_tokens"] // 65536
+    main(["--num-layers", "3", "--history", "65536", "--candidate", "1280", "--fixed-nh", "262144",
+          "--total-hbm-gib", "40", "--model-hbm-gib", "20"])
+    out = json.loads(capsys.readouterr().out)
+    assert out["useful_max_P"] <= 262144

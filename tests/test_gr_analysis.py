@@ -77,3 +77,13 @@ def test_load_titles(tmp_path):
     p.write_text(json.dumps({"meta": {"3": " "}}))
     with pytest.raises(ValueError):
         load_titles(p)
+
+
+def test_reconstruct_cli(tmp_path):
+    curves = tmp_path / "heat_curves.csv"
+    curves.write_text("dataset,field,user_fraction,traffic_fraction,relative_weight\n"
+                      "d,f,0.1,0.5,5\nd,f,1,1,1\n")
+    main(["reconstruct", "--curve-path", str(curves), "--dataset", "d", "--field", "f", "--users", "10",
+          "--visits", "100", "--output", str(tmp_path / "r")])
+    rows = (tmp_path / "r" / "histogram.csv").read_text().splitlines()
+    assert rows[0] == "visits_per_user,users" and len(rows) == 4
