@@ -134,3 +134,13 @@ def test_bench_scope_flops():
     assert f["indexer"] == 2.0 * 64 * 128 * 4096 * 4097 / 2
     r = bench.scope_rooflines({"indexer": {"ms": 1.0}}, f)
     assert r["indexer"]["tflops"] == round(f["indexer"] / 1e9, 1) and "sparse_mla" not in r
+
+
+def test_roofline_fraction():
+    from cxldsagr_b200.evaluation.kernel_bench import _peaks, roofline
+
+    pk = _peaks()
+    r = roofline(2.0, nbytes=pk["hbm_gbs"] * 1e6)            # 1 ms of copy bandwidth in 2 ms
+    assert r["bound"] == "memory" and abs(r["frac_of_roofline"] - 0.5) < 1e-9
+    r = roofline(1.0, flops=4500e9, fp8=True)                 # 1 ms at nominal FP8 in 1 ms
+    assert r["bound"] == "compute" and abs(r["frac_of_roofline"] - 1.0) < 1e-9
