@@ -32,6 +32,7 @@ struct P2PArgs {
   // Flag counters are cumulative over calls; the host tracks the totals.
   uint64_t arrive_target = 0;   // arrival count (incl. this call) to wait for before reading peer data
   uint64_t reuse_target = 0;    // reader-done count of the call two back on this parity (0: none)
+  uint64_t wait_ns = 2000000000ull;  // budget of each peer-flag wait (default 2 s)
   int grid = 0;                 // CTAs of the GEMM (identical on every rank)
   int reduce_grid = 0;          // CTAs of the reduce kernel (RS)
   // AG: this rank's shard and every rank's gather buffers ([2][M][K] fp8, [2][K/128][M] fp32)
@@ -54,6 +55,7 @@ struct EpArgs {
   int M_pad = 0;                 // grouped-layout row capacity per rank
   int parity = 0;
   uint64_t call = 0;             // 1-based call number of the EP op
+  uint64_t wait_ns = 2000000000ull;  // budget of each peer-flag wait (default 2 s)
   int* cnt[kMaxRanks] = {};      // [2][world][E] int32 per rank
   uint8_t* a[kMaxRanks] = {};    // [2][M_pad][D] fp8
   float* as[kMaxRanks] = {};     // [2][D/128][M_pad] fp32

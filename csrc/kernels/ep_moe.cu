@@ -44,7 +44,7 @@ __global__ void __launch_bounds__(1024) ep_count_kernel(const __grid_constant__ 
     // Reuse guard: every owner finished reading this parity's counts/rows two calls ago.
     if (p.call > 2)
       for (int q = 0; q < p.world && ok; ++q)
-        ok = wait_flag_ge(p.flags[p.rank] + kFlagEpReady + q, p.call - 2, err, kErrTimeoutPeerFlag);
+        ok = wait_flag_ge(p.flags[p.rank] + kFlagEpReady + q, p.call - 2, err, kErrTimeoutPeerFlag, nullptr, p.wait_ns);
     s_ok = ok;
   }
   __syncthreads();
@@ -107,7 +107,7 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const __grid_constant__
   if (threadIdx.x == 0) {
     int ok = 1;
     for (int s = 0; s < p.world && ok; ++s)
-      ok = wait_flag_ge(p.flags[p.rank] + kFlagEpCount + s, p.call, err, kErrTimeoutPeerFlag);
+      ok = wait_flag_ge(p.flags[p.rank] + kFlagEpCount + s, p.call, err, kErrTimeoutPeerFlag, nullptr, p.wait_ns);
     s_ok = ok;
   }
   __syncthreads();
@@ -169,10 +169,10 @@ __global__ void ep_signal_kernel(const __grid_constant__ EpArgs p, int kind) {
 __global__ void ep_wait_kernel(const __grid_constant__ EpArgs p, int* err) {
   if (threadIdx.x != 0) return;
   for (int s = 0; s < p.world; ++s)
-    if (!wait_flag_ge(p.flags[p.rank] + kFlagEpData + s, p.call, err, kErrTimeoutPeerFlag)) return;
+    if (!wait_flag_ge(p.flags[p.rank] + kFlagEpData + s, p.call, err, kErrTimeoutPeerFlag, nullptr, p.wait_ns)) return;
   if (p.call > 2)
     for (int s = 0; s < p.world; ++s)
-      if (!wait_flag_ge(p.flags[p.rank] + kFlagEpDone + s, p.call - 2, err, kErrTimeoutPeerFlag)) return;
+      if (!wait_flag_ge(p.flags[p.rank] + kFlagEpDone + s, p.call - 2, err, kErrTimeoutPeerFlag, nullptr, p.wait_ns)) return;
   fence_proxy_async_global();
 }
 
@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const __grid_constant__
   if (threadIdx.x == 0) {
     int ok = 1;
     for (int o = 0; o < p.world && ok; ++o)
-      ok = wait_flag_ge(p.flags[p.rank] + kFlagEpReady + o, p.call, err, kErrTimeoutPeerFlag);
+      ok = wait_flag_ge(p.flags[p.rank] + kFlagEpReady + o, p.call, err, kErrTimeoutPeerFlag, nullptr, p.wait_ns);
     s_ok = ok;
   }
   __syncthreads();

@@ -30,7 +30,8 @@ __global__ void __launch_bounds__(256) rs_reduce_kernel(const __grid_constant__ 
   if (threadIdx.x == 0) {
     int ok = 1;
     for (int src = 0; src < p.world && ok; ++src)
-      ok = wait_flag_ge(p.flags[p.rank] + kFlagRsArrive + src, p.arrive_target, err, kErrTimeoutPeerFlag);
+      ok = wait_flag_ge(p.flags[p.rank] + kFlagRsArrive + src, p.arrive_target, err, kErrTimeoutPeerFlag, nullptr,
+                        p.wait_ns);
     s_ok = ok;
   }
   __syncthreads();
@@ -82,7 +83,8 @@ __global__ void p2p_barrier_kernel(const __grid_constant__ P2PArgs p, int* err) 
   __threadfence_system();
   for (int q = 0; q < p.world; ++q) red_release_sys_add(p.flags[q] + kFlagBarrier + p.rank, 1);
   for (int q = 0; q < p.world; ++q)
-    if (!wait_flag_ge(p.flags[p.rank] + kFlagBarrier + q, p.arrive_target, err, kErrTimeoutPeerFlag)) return;
+    if (!wait_flag_ge(p.flags[p.rank] + kFlagBarrier + q, p.arrive_target, err, kErrTimeoutPeerFlag, nullptr, p.wait_ns))
+      return;
 }
 
 void check_p2p(const P2PArgs& p) {

@@ -1,7 +1,8 @@
 // Allocation-free entry point for the split-K sparse MLA decode (see
-// noalloc_mla.h for the contract).  It reuses the library's tcgen05 split-K
-// kernel and LSE combine unchanged; only the scratch comes from a fixed
+// noalloc_mla.h for the contract).  It reuses the library's cta_group::2
+// split-K kernel and LSE combine unchanged; only the scratch comes from a fixed
 // device array instead of a caller or allocator buffer.
+#include <atomic>
 #include <mutex>
 #include <stdexcept>
 
@@ -24,7 +25,9 @@ static __device__ int g_mla_error_word;
 struct DeviceScratch {
   float* scratch = nullptr;
   int* error_word = nullptr;
-  bool ready = false;
+  // Published with release order after the two pointers are written; a
+  // reader that sees true (acquire) also sees the pointers.
+  std::atomic<bool> ready{false};
 };
 
 constexpr int kMaxDevices = 64;
@@ -36,9 +39,9 @@ int setup_current_device(DeviceScratch** out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CXLD_NOALLOC_SETUP_FAILED;
   DeviceScratch& d = g_devices[dev];
-  if (!d.ready) {
+  if (!d.ready.load(std::memory_order_acquire)) {
     std::lock_guard<std::mutex> lock(g_setup_mutex);
-    if (!d.ready) {
+    if (!d.ready.load(std::memory_order_relaxed)) {
       void* scratch = nullptr;
       void* err = nullptr;
       if (cudaGetSymbolAddress(&scratch, g_mla_scratch) != cudaSuccess || scratch == nullptr)
@@ -47,7 +50,7 @@ int setup_current_device(DeviceScratch** out) {
         return CXLD_NOALLOC_SETUP_FAILED;
       d.scratch = static_cast<float*>(scratch);
       d.error_word = static_cast<int*>(err);
-      d.ready = true;
+      d.ready.store(true, std::memory_order_release);
     }
   }
   *out = &d;
@@ -77,11 +80,28 @@ extern "C" int cxld_sparse_mla_split_noalloc(const void* q, const void* kv, cons
   a.P = P;
   a.scale = scale;
   a.err = d->error_word;
+  // Each call reports only its own device errors: the word is cleared in
+  // stream order before the kernel runs (the kernel records the first error
+  // of the call and never clears it).
+  if (cudaMemsetAsync(d->error_word, 0, sizeof(int), stream) != cudaSuccess) return CXLD_NOALLOC_LAUNCH_FAILED;
   try {
-    b200::launch_sparse_mla_tc(a, splits, d->scratch, stream);
+    b200::launch_sparse_mla_2sm(a, splits, d->scratch, stream);
   } catch (const std::exception&) {
     return CXLD_NOALLOC_LAUNCH_FAILED;
   }
+  return CXLD_NOALLOC_OK;
+}
+
+extern "C" int cxld_sparse_mla_noalloc_error(int* device_code, cudaStream_t stream) {
+  if (device_code == nullptr) return CXLD_NOALLOC_BAD_ARGUMENT;
+  DeviceScratch* d = nullptr;
+  const int rc = setup_current_device(&d);
+  if (rc != CXLD_NOALLOC_OK) return rc;
+  // The copy is ordered after the work already on `stream`; the host value
+  // is settled once the stream has been synchronised.
+  if (cudaMemcpyAsync(device_code, d->error_word, sizeof(int), cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+    return CXLD_NOALLOC_LAUNCH_FAILED;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return CXLD_NOALLOC_LAUNCH_FAILED;
   return CXLD_NOALLOC_OK;
 }
 

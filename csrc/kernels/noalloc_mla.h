@@ -24,6 +24,12 @@
 //    them) race on the array and produce wrong results; serialise them.
 //  * Requests with splits * T above the maximum are rejected with
 //    CXLD_NOALLOC_TOO_LARGE and nothing is launched.
+//  * Device-side failures (a bounded wait that ran out, for instance) do not
+//    change the return code, which only covers argument checks and the
+//    launch.  The kernel records them in a device error word of the library
+//    that each call clears, in stream order, before its kernel runs; read it
+//    with cxld_sparse_mla_noalloc_error after the call (0 = no error, else a
+//    device error code).  The word is shared like the scratch array.
 //  * No cudaMalloc, cudaFree or allocating library routine is called.
 #pragma once
 #include <cuda_runtime.h>
@@ -48,6 +54,12 @@ extern "C" {
 __attribute__((visibility("default"))) int cxld_sparse_mla_split_noalloc(
     const void* q, const void* kv, const int* ids, int T, int K, int P, float scale, int splits,
     void* out, float* lse, cudaStream_t stream);
+
+// Device error code of the most recent call on `stream`'s device: waits for
+// the work already enqueued on `stream`, then stores the code in
+// *device_code (0 when the call's kernels recorded no error).  Returns a
+// CXLD_NOALLOC_* code for the read itself.
+__attribute__((visibility("default"))) int cxld_sparse_mla_noalloc_error(int* device_code, cudaStream_t stream);
 
 // Largest splits * T a call accepts.
 __attribute__((visibility("default"))) int cxld_sparse_mla_noalloc_max_rows(void);

@@ -48,9 +48,9 @@ class _CountingLib:
         if name == "fp8_gemm":
             multi = lambda args: _fp8_gemm_launches(self._mod, args)  # noqa: E731
 
-        def call(*args):
+        def call(*args, **kwargs):
             self.launches += multi(args) if multi else 1
-            return fn(*args)
+            return fn(*args, **kwargs)
 
         return call
 

@@ -5,8 +5,10 @@ reserved up front, allocator owned by another framework, no allocation in a
 latency-critical loop) call ``cxld_sparse_mla_split_noalloc`` through its C
 symbol; it takes its split-K scratch from a fixed array in the library.  This
 test calls that symbol with ctypes, twice in a row, and checks each result
-against the regular entry point (which gets the same scratch from the torch
-allocator).  The file name makes pytest collect it last.
+against the FP32 oracle and the regular entry point (which gets the same
+scratch from the torch allocator), that the call's device error word reads 0
+and that no device memory is allocated by the call.  The file name makes
+pytest collect it last.
 """
 
 import ctypes
@@ -16,6 +18,7 @@ import torch
 
 from cxldsagr_b200 import ops
 from cxldsagr_b200.config import v32_config
+from cxldsagr_b200.ops import reference as ref
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -32,7 +35,16 @@ def _symbol():
     lib.cxld_sparse_mla_noalloc_max_rows.restype = ctypes.c_int
     lib.cxld_noalloc_error_string.restype = ctypes.c_char_p
     lib.cxld_noalloc_error_string.argtypes = [ctypes.c_int]
+    lib.cxld_sparse_mla_noalloc_error.restype = ctypes.c_int
+    lib.cxld_sparse_mla_noalloc_error.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]
     return lib, fn
+
+
+def _device_error(lib, stream):
+    code = ctypes.c_int(-1)
+    rc = lib.cxld_sparse_mla_noalloc_error(ctypes.byref(code), stream)
+    assert rc == 0, lib.cxld_noalloc_error_string(rc).decode()
+    return code.value
 
 
 def _rel_err(a, b):
@@ -58,13 +70,24 @@ def test_noalloc_matches_regular_entry_point_twice():
         q, kv, ids = _case(seed, T, K, P)
         out = torch.empty(T, 128, 512, device=DEV, dtype=torch.bfloat16)
         lse = torch.empty(T, 128, device=DEV, dtype=torch.float32)
+        torch.cuda.synchronize()
+        allocated = torch.cuda.memory_allocated()
+        free_before = torch.cuda.mem_get_info()[0]
         rc = fn(q.data_ptr(), kv.data_ptr(), ids.data_ptr(), T, K, P, scale, splits, out.data_ptr(),
                 lse.data_ptr(), stream)
         assert rc == 0, lib.cxld_noalloc_error_string(rc).decode()
-        want, want_lse = ops.sparse_mla(q, kv, ids, scale, splits=splits, return_lse=True)
+        assert _device_error(lib, stream) == 0
         torch.cuda.synchronize()
-        assert _rel_err(out, want) < 2e-2
-        assert torch.allclose(lse, want_lse, atol=2e-2, rtol=1e-3)
+        assert torch.cuda.memory_allocated() == allocated
+        if seed > 0:  # the first call on a device may load the library's device image
+            assert torch.cuda.mem_get_info()[0] == free_before
+        want, want_lse = ref.sparse_mla_lse(q.cpu(), kv.cpu(), ids.cpu(), scale)
+        assert _rel_err(out.cpu(), want) < 2e-2
+        assert torch.allclose(lse.cpu(), want_lse.float(), atol=2e-2, rtol=1e-3)
+        got, got_lse = ops.sparse_mla(q, kv, ids, scale, splits=splits, return_lse=True)
+        torch.cuda.synchronize()
+        assert _rel_err(out, got) < 2e-2
+        assert torch.allclose(lse, got_lse, atol=2e-2, rtol=1e-3)
     ops.check_errors(DEV)
 
 
