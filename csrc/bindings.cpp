@@ -260,14 +260,30 @@ void sparse_mla(const Tensor& q, const Tensor& kv, const Tensor& ids, double sca
     TORCH_CHECK(size_t(scratch->numel()) * 4 >= b200::sparse_mla_scratch_bytes(a.T, a.H, splits), "sparse_mla: scratch too small");
     sp = ptr<float>(*scratch);
   }
-  if (impl == 0 || impl >= 16) b200::launch_sparse_mla_tc(a, int(splits), sp, stream(), impl >= 16 ? int(impl - 16) : 0);
-  else b200::launch_sparse_mla_split(a, int(splits), sp, stream());
+  // impl 0 / 2: the cta_group::2 kernel (default); 1: the mma.sync baseline;
+  // 3: probe; 4 / 16+: the DSMEM-exchange tcgen05 kernel; 32+: pair kernel debug bits.
+  if (impl == 0 || impl == 2 || (impl >= 32 && impl < 64)) {
+    b200::launch_sparse_mla_2sm(a, int(splits), sp, stream(), nullptr, impl >= 32 ? int(impl - 32) : 0);
+  } else if (impl == 3) {  // debug: raw first-tile scores of cluster 0 into `scratch` (splits must be 1)
+    TORCH_CHECK(splits == 1 && scratch && scratch->defined() && scratch->numel() >= 2 * 128 * 32, "sparse_mla: probe buffer");
+    b200::launch_sparse_mla_2sm(a, 1, nullptr, stream(), ptr<float>(*scratch));
+  } else if (impl == 4 || impl >= 16) {
+    b200::launch_sparse_mla_tc(a, int(splits), sp, stream(), impl >= 16 ? int(impl - 16) : 0);
+  } else {
+    b200::launch_sparse_mla_split(a, int(splits), sp, stream());
+  }
 }
 
 Tensor topk_trace(int64_t row) {
   Tensor t = torch::empty({16}, torch::kInt64);
   if (row >= -1) b200::set_topk_trace_row(int(row));
   b200::copy_topk_trace(reinterpret_cast<unsigned long long*>(t.data_ptr<int64_t>()));
+  return t;
+}
+
+Tensor sparse_mla_2sm_trace() {
+  Tensor t = torch::empty({4, 65, 16}, torch::kInt64);
+  b200::copy_sparse_mla_2sm_trace(reinterpret_cast<unsigned long long*>(t.data_ptr<int64_t>()));
   return t;
 }
 
@@ -617,9 +633,12 @@ void fp8_gemm_rs(const Tensor& a_q, const Tensor& a_s_t, const Tensor& w, const 
                            int(out.stride(0)), err_ptr(a_q), at::cuda::getCurrentCUDAStream());
 }
 
-void p2p_barrier(int64_t device, int64_t rank, int64_t world, int64_t call, const std::vector<int64_t>& flags) {
+void p2p_barrier(int64_t device, int64_t rank, int64_t world, int64_t call, const std::vector<int64_t>& flags,
+                 int64_t wait_ns) {
   c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
   auto p = make_p2p(rank, world, 1, call, call, 0, flags, {}, {}, {});
+  TORCH_CHECK(wait_ns > 0, "p2p_barrier: wait budget must be positive");
+  p.wait_ns = uint64_t(wait_ns);
   b200::launch_p2p_barrier(p, error_word_ref(int(device)).data_ptr<int>(), at::cuda::getCurrentCUDAStream());
 }
 
@@ -683,7 +702,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("echo_hint", &echo_hint);
   m.def("fp8_gemm_ag", &fp8_gemm_ag);
   m.def("fp8_gemm_rs", &fp8_gemm_rs);
-  m.def("p2p_barrier", &p2p_barrier);
+  m.def("p2p_barrier", &p2p_barrier, py::arg("device"), py::arg("rank"), py::arg("world"), py::arg("call"),
+        py::arg("flags"), py::arg("wait_ns") = int64_t(2000000000));
+  m.def("sparse_mla_2sm_trace", &sparse_mla_2sm_trace);
   m.def("moe_route", &moe_route);
   m.def("ep_dispatch", &ep_dispatch);
   m.def("ep_combine", &ep_combine);

@@ -230,6 +230,12 @@ size_t sparse_mla_scratch_bytes(int T, int H, int splits);
 void launch_sparse_mla_split(const MLAArgs& a, int splits, float* scratch, cudaStream_t stream);
 // tcgen05 version (2-CTA clusters exchanging partial S through DSMEM).
 void launch_sparse_mla_tc(const MLAArgs& a, int splits, float* scratch, cudaStream_t stream, int dbg = 0);
+// tcgen05 cta_group::2 version (64 heads per CTA, no partial-score exchange).
+// dbg_s (optional, 2 x 128 x 32 floats): raw scores of the first tile of cluster 0.
+// dbg bits: 1 skip the gather, 2 skip the MMAs, 8 record the per-tile timeline.
+void launch_sparse_mla_2sm(const MLAArgs& a, int splits, float* scratch, cudaStream_t stream,
+                           float* dbg_s = nullptr, int dbg = 0);
+void copy_sparse_mla_2sm_trace(unsigned long long* host);
 // Top-k debug timeline: clock64 at the phase boundaries of one row (-1 = off).
 void set_topk_trace_row(int row);
 void copy_topk_trace(unsigned long long* host);

@@ -86,17 +86,19 @@ def time_fn(fn, *, warmup=3, iters=10, flush=True, dev="cuda"):
 
 
 def mla_timeline(q, kv, ids, splits: int) -> dict:
-    """Phase clocks (SM cycles) of the first 2-CTA cluster of one tcgen05 MLA launch
-    (kernel debug bit 64): Q resident in TMEM, each tile's P stored, epilogue, exit."""
-    ops.sparse_mla(q, kv, ids, 0.1, splits=splits, impl=16 + 64)
+    """Phase clocks (SM cycles) of the first cluster of one cta_group::2 MLA launch
+    (kernel debug bit 8): Q landed, each tile's S read and P handed to PV, O ready, exit."""
+    ops.sparse_mla(q, kv, ids, 0.1, splits=splits, impl=32 + 8)
     torch.cuda.synchronize()
-    tr = ops.lib().sparse_mla_trace()
+    tr = ops.lib().sparse_mla_2sm_trace()
     t0 = int(tr[0, 64, 0])
-    n = min(64, -(-ids.shape[1] // splits) // 32)
-    p_stored = [int(tr[0, i, 7]) - t0 for i in range(n)]
-    return {"q_in_tmem": int(tr[0, 64, 1]) - t0, "first_p": p_stored[0], "last_p": p_stored[-1],
-            "cycles_per_tile": (p_stored[-1] - p_stored[0]) / max(1, n - 1),
-            "epilogue_start": int(tr[0, 64, 2]) - t0, "exit": int(tr[0, 64, 3]) - t0, "tiles": n}
+    n = min(64, -(-ids.shape[1] // splits) // 64)
+    p_handed = [int(tr[0, i, 5]) - t0 for i in range(n)]
+    s_read = [int(tr[0, i, 4]) - t0 for i in range(n)]
+    return {"q_landed": int(tr[0, 64, 1]) - t0, "first_s": s_read[0], "first_p": p_handed[0],
+            "last_p": p_handed[-1], "cycles_per_tile": (p_handed[-1] - p_handed[0]) / max(1, n - 1),
+            "softmax_cycles_per_tile": sum(p - r for p, r in zip(p_handed, s_read)) / n,
+            "o_ready": int(tr[0, 64, 2]) - t0, "exit": int(tr[0, 64, 3]) - t0, "tiles": n, "keys_per_tile": 64}
 
 
 def bench_sparse_mla(T=256, K=2048, P=65664, splits=1, impl=0, locality=0.0, trace=False, **_):

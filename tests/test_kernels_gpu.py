@@ -201,7 +201,7 @@ def test_topk_indexer_like_rows(ld_pad):
 
 
 # ------------------------------------------------------------ sparse MLA
-@pytest.mark.parametrize("impl", [0, 1], ids=["tcgen05", "mma_sync"])
+@pytest.mark.parametrize("impl", [0, 1, 4], ids=["tcgen05_pair", "mma_sync", "tcgen05_exchange"])
 @pytest.mark.parametrize("T,K,P,splits", [(2, 2048, 5000, 1), (3, 256, 300, 1), (1, 2048, 9000, 16), (5, 100, 64, 4),
                                           (300, 2048, 70000, 1)])
 def test_sparse_mla(T, K, P, splits, impl):
@@ -224,7 +224,7 @@ def test_sparse_mla(T, K, P, splits, impl):
     assert torch.allclose(lse.cpu(), wlse, atol=2e-2, rtol=1e-3)
 
 
-@pytest.mark.parametrize("impl", [0, 1])
+@pytest.mark.parametrize("impl", [0, 1, 4])
 def test_sparse_mla_all_padding_is_zero(impl):
     q = torch.randn(2, 128, 576, device=DEV).bfloat16()
     kv = torch.randn(10, 576, device=DEV).bfloat16()
@@ -527,3 +527,39 @@ def test_model_replay_is_deterministic():
         runs.append((m.prefill(hist).logits.clone(), m.extend(ext).logits.clone()))
     ops.check_errors(DEV)
     assert torch.equal(runs[0][0], runs[1][0]) and torch.equal(runs[0][1], runs[1][1])
+
+
+# ------------------------------------------------------- bounded failures
+def test_peer_flag_wait_times_out_and_reports():
+    """A flag barrier whose arrival target no rank reaches gives up after its
+    budget: the kernel returns, the error word holds the peer-flag timeout and
+    check_errors raises; the context stays usable."""
+    from cxldsagr_b200.ops import native
+
+    dev = torch.device(DEV, torch.cuda.current_device())
+    flags = torch.zeros(128, dtype=torch.int64, device=dev)  # one rank's flag block
+    ops.check_errors(dev)
+    # call=5: the barrier bumps its own slot to 1 and waits for 5 (never reached).
+    ops.lib().p2p_barrier(dev.index, 0, 1, 5, [flags.data_ptr()], wait_ns=10_000_000)
+    torch.cuda.synchronize()
+    assert int(native.error_word(dev).item()) == 5  # kErrTimeoutPeerFlag
+    with pytest.raises(native.DeviceError, match="peer"):
+        ops.check_errors(dev)
+    ops.check_errors(dev)  # reset by the raise above
+    assert torch.ones(4, device=dev).sum().item() == 4.0
+
+
+def test_kv_gather_rejects_out_of_range_rows():
+    """An out-of-range host row or pool slot is skipped and reported as a bad index."""
+    from cxldsagr_b200.ops import native
+
+    dev = torch.device(DEV, torch.cuda.current_device())
+    host = torch.randn(64, 576).bfloat16().pin_memory()
+    records = torch.zeros(32, 576, dtype=torch.bfloat16, device=dev)
+    ops.check_errors(dev)
+    ops.gather_host_records(host, records, torch.tensor([3, 64], device=dev), torch.tensor([1, 2], device=dev))
+    torch.cuda.synchronize()
+    with pytest.raises(native.DeviceError, match="index"):
+        ops.check_errors(dev)
+    assert torch.equal(records[1].cpu(), host[3])  # the valid row still landed
+    assert torch.count_nonzero(records[2]) == 0
