@@ -1,15 +1,16 @@
 """Single-request chunked inference over any model with a request cache.
 
-Behavioural parity with ``executor/model_executor.py:18-125`` of the
-reference: ``run_chunks`` feeds a token tensor through ``model(chunk, cache,
-...)`` in chunks of ``chunk_size`` and returns only the last chunk's output
-(hidden states of every token of that chunk, or logits through the model's
-``logits_to_keep`` option); :class:`ModelExecutor` adds the empty/nonempty
-cache rules of prefill and extend and the cache allocation hooks.
+Same job as the reference's ``executor/model_executor.py``: split a token
+tensor into chunks, feed each chunk through ``model(chunk, cache, ...)`` so
+the cache grows chunk by chunk, and hand back what the last chunk produced
+(the hidden states of all its tokens, or the logits of its last
+``logits_to_keep`` tokens).  :class:`ModelExecutor` adds the prefill
+(empty cache) / extend (nonempty cache) rules and the cache allocation hooks.
 """
 
 from __future__ import annotations
 
+from dataclasses import dataclass
 from typing import Any, Literal
 
 import torch
@@ -17,43 +18,68 @@ import torch
 Output = Literal["hidden", "logits"]
 
 
-def _check_chunk(chunk_size):
-    if isinstance(chunk_size, bool) or not isinstance(chunk_size, int) or chunk_size < 1:
-        raise ValueError("chunk_size must be a positive integer")
+def _is_count(value: Any, *, minimum: int) -> bool:
+    return isinstance(value, int) and not isinstance(value, bool) and value >= minimum
+
+
+@dataclass(frozen=True)
+class ChunkSchedule:
+    """Chunk boundaries of one request: tokens [start, start + size) per step."""
+
+    total: int
+    chunk_size: int
+
+    def __post_init__(self):
+        if not _is_count(self.chunk_size, minimum=1):
+            raise ValueError(f"chunk_size must be an int >= 1, got {self.chunk_size!r}")
+
+    def spans(self):
+        for start in range(0, self.total, self.chunk_size):
+            yield start, min(self.chunk_size, self.total - start)
+
+    @property
+    def steps(self) -> int:
+        return -(-self.total // self.chunk_size)
+
+
+def _check_request(ids: Any, output: str, logits_to_keep: Any) -> None:
+    if not (isinstance(ids, torch.Tensor) and ids.ndim == 1 and ids.numel() > 0 and ids.dtype == torch.long):
+        raise ValueError("ids: expected a nonempty 1-D tensor of dtype torch.long")
+    if output not in ("hidden", "logits"):
+        raise ValueError(f"output must be 'hidden' or 'logits', got {output!r}")
+    if not _is_count(logits_to_keep, minimum=0):
+        raise ValueError(f"logits_to_keep must be an int >= 0, got {logits_to_keep!r}")
+    if output == "hidden" and logits_to_keep:
+        raise ValueError("logits_to_keep applies to logits output only (hidden output returns the whole last chunk)")
+
+
+def _check_capacity(model: Any, cache: Any, new_tokens: int) -> None:
+    end = cache.length + new_tokens
+    if end > cache.max_seq_len:
+        raise ValueError(f"the request needs {end} cache rows, the cache holds {cache.max_seq_len}")
+    limit = model.config.max_position_embeddings
+    if end > limit:
+        raise ValueError(f"the request reaches position {end}, beyond max_position_embeddings = {limit}")
 
 
 def run_chunks(model: Any, ids: torch.Tensor, cache: Any, chunk_size: int, *, output: Output = "hidden",
                logits_to_keep: int = 0) -> torch.Tensor:
-    _check_chunk(chunk_size)
-    if not isinstance(ids, torch.Tensor) or ids.ndim != 1 or ids.numel() == 0 or ids.dtype != torch.long:
-        raise ValueError("ids must be a nonempty 1-D torch.long tensor")
-    if output not in ("hidden", "logits"):
-        raise ValueError("output must be 'hidden' or 'logits'")
-    if isinstance(logits_to_keep, bool) or not isinstance(logits_to_keep, int) or logits_to_keep < 0:
-        raise ValueError("logits_to_keep must be a nonnegative integer")
-    if output == "hidden" and logits_to_keep:
-        raise ValueError("hidden output returns all final-chunk features; do not set logits_to_keep")
-    end = cache.length + ids.numel()
-    if end > cache.max_seq_len:
-        raise ValueError("KV cache capacity exceeded by the complete input")
-    if end > model.config.max_position_embeddings:
-        raise ValueError("Input exceeds model.config.max_position_embeddings")
-    result = None
+    schedule = ChunkSchedule(ids.numel() if isinstance(ids, torch.Tensor) else 0, chunk_size)
+    _check_request(ids, output, logits_to_keep)
+    _check_capacity(model, cache, ids.numel())
+    kwargs = {"return_hidden": True} if output == "hidden" else {"logits_to_keep": logits_to_keep}
+    last = None
     with torch.inference_mode():
-        for start in range(0, ids.numel(), chunk_size):
-            chunk = ids[start:start + chunk_size]
-            if output == "hidden":
-                result = model(chunk, cache, return_hidden=True)
-            else:
-                result = model(chunk, cache, logits_to_keep=logits_to_keep)
-    return result
+        for start, size in schedule.spans():
+            last = model(ids.narrow(0, start, size), cache, **kwargs)
+    return last
 
 
 class ModelExecutor:
     """Prefill/extend token tensors against a model and a request-level cache."""
 
     def __init__(self, model: Any, *, cache_manager: Any = None, chunk_size: int = 1024):
-        _check_chunk(chunk_size)
+        ChunkSchedule(0, chunk_size)  # validates chunk_size
         self.model = model
         self.cache_manager = cache_manager if cache_manager is not None else getattr(model, "cache_manager", None)
         self.chunk_size = chunk_size
@@ -63,21 +89,23 @@ class ModelExecutor:
         return self.model.config.max_position_embeddings
 
     def allocate(self, max_seq_len: int) -> Any:
-        if self.cache_manager is not None:
-            return self.cache_manager.allocate(max_seq_len)
-        return self.model.new_cache(max_seq_len)
+        manager = self.cache_manager
+        return manager.allocate(max_seq_len) if manager is not None else self.model.new_cache(max_seq_len)
 
     def release(self, cache: Any) -> None:
         if self.cache_manager is not None:
             self.cache_manager.release(cache)
 
-    def prefill(self, ids, cache, *, output: Output = "hidden", logits_to_keep: int = 0):
-        if cache.length != 0:
-            raise ValueError("prefill requires an empty cache")
+    def _run(self, ids, cache, output, logits_to_keep):
         return run_chunks(self.model, ids, cache, self.chunk_size, output=output, logits_to_keep=logits_to_keep)
+
+    def prefill(self, ids, cache, *, output: Output = "hidden", logits_to_keep: int = 0):
+        if cache.length:
+            raise ValueError(f"prefill starts from an empty cache; this one holds {cache.length} tokens")
+        return self._run(ids, cache, output, logits_to_keep)
 
     def extend(self, ids, cache, *, output: Output = "hidden", logits_to_keep: int = 0):
         """Append one or more tokens (single-token decode included)."""
         if cache.length <= 0:
-            raise ValueError("extend requires a nonempty cache")
-        return run_chunks(self.model, ids, cache, self.chunk_size, output=output, logits_to_keep=logits_to_keep)
+            raise ValueError("extend continues a cache that already holds tokens; prefill first")
+        return self._run(ids, cache, output, logits_to_keep)

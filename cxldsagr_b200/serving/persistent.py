@@ -1,22 +1,25 @@
 """Serial GR service with bounded cross-request prefix reuse.
 
-Reference semantics (``serving/persistent.py:56-319``).  One request runs at
-a time; only each user's stable history survives between requests:
+The service the reference runs in ``serving/persistent.py`` (one request at
+a time; only each user's stable history survives between requests), built
+here as a small request pipeline:
 
-1. validate the request (user id, token ids, stable prefix length) and pack
-   the ids once (the prefix digest is the history identity);
-2. admit the user through the LRU :class:`PrefixSessionPool` (hit: reuse the
-   retained session; miss: evict least-recently-used users until the new
-   reservation fits, then prefill the prefix);
-3. run the candidate suffix (GPU-transient tails) and restore the session to
-   its history;
-4. report latency split into admission / prefix / extend / cleanup plus the
-   cache ledger.
+* ``_parse``     checks the request (user id, token ids, stable prefix) and
+                 packs the ids once; the prefix digest is the history identity;
+* ``_admit``     plans the session and leases it from the LRU
+                 :class:`PrefixSessionPool` (a hit reuses the retained
+                 session; a miss evicts least-recently-used users until the
+                 reservation fits);
+* ``_prefix``    builds the history on a miss;
+* ``_candidates`` runs the candidate suffix and cuts the session back to its
+                 history, auditing the cache ledger at both ends;
+* ``_report``    turns the request's clock marks and ledger into metrics.
 
-Latency covers input validation and transfer, admission and eviction, prefix
-construction on a miss, all candidate hidden states and the rollback.  Any
-failure discards the user's session (never reused after a failure).  Omitting
-both byte budgets selects fixed-pool admission (host pages / HBM tokens).
+A :class:`_Clock` synchronises the device before each mark, so the phases
+(admission / prefix / extend / cleanup) are device-complete wall times; the
+whole latency covers validation and the host-to-device copy too.  A failure
+anywhere in the leased part discards the user's session.  Omitting both byte
+budgets selects fixed-pool admission (host pages / HBM tokens).
 """
 
 from __future__ import annotations
@@ -67,48 +70,97 @@ class ServingResult:
     hidden: torch.Tensor
 
 
+@dataclass(frozen=True)
+class _Request:
+    uid: Any
+    ids: list
+    prefix: int
+
+    @property
+    def shape(self) -> RequestShape:
+        return RequestShape(self.prefix, len(self.ids) - self.prefix)
+
+
+class _Clock:
+    """Named perf_counter marks; each mark first waits for the device."""
+
+    def __init__(self, synchronize):
+        self._sync = synchronize
+        self.marks: dict[str, float] = {}
+
+    def mark(self, name: str, *, sync: bool = True) -> None:
+        if sync:
+            self._sync()
+        self.marks[name] = time.perf_counter()
+
+    def ms(self, begin: str, end: str) -> float:
+        return (self.marks[end] - self.marks[begin]) * 1e3
+
+
+@dataclass
+class _Candidates:
+    hidden: torch.Tensor
+    ledger_during: CacheFootprint | None = None  # measured bytes with the candidate tail present
+    ledger_after: CacheFootprint | None = None   # measured bytes after the cut
+
+
 class PersistentGRRunner:
     def __init__(self, backend: ServingBackend, *, hbm_budget_bytes: int | None = None,
                  dram_budget_bytes: int | None = None, resource_limits: Mapping[str, int] | None = None,
                  native_token_validation: bool = False):
+        if (hbm_budget_bytes is None) is not (dram_budget_bytes is None):
+            raise ValueError("give both cache byte budgets (HBM and DRAM) or neither (fixed pools)")
         self.backend = backend
         self.pool: PrefixSessionPool | None = None
         self.closed = True
         self._owner_bound = False
         self._closed_fully = False
         self._rollback_on_close = False
-        if (hbm_budget_bytes is None) != (dram_budget_bytes is None):
-            raise ValueError("provide both cache byte budgets or omit both for fixed pools")
         budget = None if hbm_budget_bytes is None else CacheFootprint(hbm_budget_bytes, dram_budget_bytes)
-        self.resource_mode = "fixed_pools" if budget is None else "budget"
-        limits = {"max_seq_len": backend.max_seq_len, "max_session_capacity": backend.max_seq_len,
-                  **(resource_limits or {})}
-        if any(type(v) is not int or v <= 0 for v in limits.values()):
-            raise ValueError("resource limits must be positive integers")
-        self.resource_limits = limits
-        policy = CapacityPolicy.fixed_pools() if budget is None else CapacityPolicy.byte_budget(budget)
+        self.resource_mode = "budget" if budget is not None else "fixed_pools"
+        self.resource_limits = self._limits(backend, resource_limits)
+        policy = CapacityPolicy.byte_budget(budget) if budget is not None else CapacityPolicy.fixed_pools()
         self.runtime = TokenRuntime(backend.runtime_driver(policy))
         self.driver = self.runtime.driver
-        self.resource_plan = self.runtime.plan_resources(policy, limits)
-        plan = self.resource_plan
-        if budget is not None and not plan.shared.fits(budget):
-            raise CacheBudgetExceeded(f"shared cache requires {plan.shared}, exceeds cache budget {budget}")
-        if budget is None:
-            if plan.host_pages == plan.hbm_tokens == 0:
-                raise ValueError("fixed-pools admission requires a shared backend with host pages or HBM tokens")
-            pages, tokens = self.driver.maximum_session_quota(plan)
-            if pages == tokens == 0:
-                raise ValueError("fixed-pools admission requires positive session host pages or HBM tokens")
-            if pages > plan.host_pages:
-                raise CacheBudgetExceeded("fixed host arena cannot hold one maximum-size session")
-            if tokens > plan.hbm_tokens:
-                raise CacheBudgetExceeded("fixed HBM pool cannot hold one maximum-size session")
+        self.resource_plan = self.runtime.plan_resources(policy, self.resource_limits)
+        self._check_plan(self.resource_plan, budget)
+        self._valid_ids = token_validation.prepare() if native_token_validation else token_validation.reference
         self.token_validation_identity = {"backend": "python_reference", "fallback_reason": None,
                                           "requested_native": native_token_validation}
-        self._valid_ids = token_validation.reference
         if native_token_validation:
-            self._valid_ids = token_validation.prepare()
             self.token_validation_identity.update(token_validation.runtime_info())
+        self._open(budget)
+        self.visits: Counter = Counter()
+        self.closed = False
+
+    # ------------------------------------------------------------ set-up
+    @staticmethod
+    def _limits(backend, extra: Mapping[str, int] | None) -> dict:
+        limits = {"max_seq_len": backend.max_seq_len, "max_session_capacity": backend.max_seq_len}
+        limits.update(extra or {})
+        bad = {k: v for k, v in limits.items() if type(v) is not int or v <= 0}
+        if bad:
+            raise ValueError(f"resource limits must be positive integers: {bad}")
+        return limits
+
+    def _check_plan(self, plan, budget) -> None:
+        if budget is not None:
+            if not plan.shared.fits(budget):
+                raise CacheBudgetExceeded(f"the shared cache alone needs {plan.shared}; budget is {budget}")
+            return
+        if plan.host_pages == 0 and plan.hbm_tokens == 0:
+            raise ValueError("fixed-pools admission needs a shared backend with host pages or HBM tokens")
+        pages, tokens = self.driver.maximum_session_quota(plan)
+        if pages == 0 and tokens == 0:
+            raise ValueError("fixed-pools admission needs sessions that take host pages or HBM tokens")
+        for need, have, what in ((pages, plan.host_pages, "host arena"), (tokens, plan.hbm_tokens, "HBM pool")):
+            if need > have:
+                raise CacheBudgetExceeded(f"the fixed {what} ({have}) is smaller than one maximum-size session "
+                                          f"({need})")
+
+    def _open(self, budget) -> None:
+        """Bind ownership, allocate and build the session pool; undo on failure."""
+        plan = self.resource_plan
         try:
             self.driver.bind_owner(self)
             self._owner_bound = True
@@ -119,115 +171,134 @@ class PersistentGRRunner:
                 measure_shared=lambda: self.runtime.shared_usage().as_mapping(),
                 host_page_capacity=plan.host_pages, hbm_token_capacity=plan.hbm_tokens)
             self.pool.audit()
-        except BaseException as init_error:
-            try:
-                self._close(rollback=True)
-            except BaseException as cleanup_error:  # noqa: BLE001 - keep both failures
-                raise BaseExceptionGroup("runner initialization cleanup failed; ownership retained",
-                                         [init_error, cleanup_error]) from None
+        except BaseException as failure:
+            self._undo(failure, "runner set-up failed and so did its cleanup (ownership kept)",
+                       lambda: self._close(rollback=True))
             raise
-        self.visits: Counter = Counter()
-        self.closed = False
 
-    # --------------------------------------------------------------- request
-    def _validate(self, request: Mapping):
+    @staticmethod
+    def _undo(failure: BaseException, message: str, cleanup) -> None:
+        """Run ``cleanup`` after ``failure``; if it fails too, raise both together."""
+        try:
+            cleanup()
+        except BaseException as second:  # noqa: BLE001 - report both failures
+            raise BaseExceptionGroup(message, [failure, second]) from None
+
+    # --------------------------------------------------------- one request
+    def _parse(self, request: Mapping) -> _Request:
         uid = request["user_id"]
         if isinstance(uid, bool) or not isinstance(uid, (str, int)):
-            raise TypeError("user_id must be an integer or string")
+            raise TypeError(f"user_id must be an int or a str, got {type(uid).__name__}")
         ids = request["input_ids"]
-        if not isinstance(ids, (list, tuple)) or not ids:
-            raise ValueError("input_ids must be a nonempty integer list")
+        if not isinstance(ids, (list, tuple)) or len(ids) == 0:
+            raise ValueError("input_ids must be a nonempty list of token ids")
         ids = list(ids)
         if not self._valid_ids(ids):
-            raise ValueError("input_ids must contain nonnegative integers")
+            raise ValueError("input_ids may only hold nonnegative integers")
         prefix = request["stable_prefix_tokens"]
-        if type(prefix) is not int or not 0 < prefix < len(ids):
-            raise ValueError("stable_prefix_tokens must leave a nonempty suffix")
-        self.resource_plan.limits.validate(RequestShape(prefix, len(ids) - prefix))
-        return uid, ids, prefix
+        if type(prefix) is not int or prefix <= 0 or prefix >= len(ids):
+            raise ValueError(f"stable_prefix_tokens={prefix!r} must be in [1, {len(ids) - 1}] (nonempty suffix)")
+        parsed = _Request(uid, ids, prefix)
+        self.resource_plan.limits.validate(parsed.shape)
+        return parsed
+
+    def _admit(self, req: _Request, signature):
+        plan = self.runtime.plan_session(req.shape, signature)
+        return self.pool.acquire(req.uid, signature, plan.retained_capacity, plan.reservation,
+                                 host_pages=plan.host_pages, hbm_tokens=plan.hbm_tokens, plan=plan)
+
+    def _prefix(self, lease, req: _Request, ids: torch.Tensor) -> None:
+        if lease.hit:
+            return
+        self.runtime.prefill(lease.session, ids[:req.prefix])
+        self.backend.synchronize()
+        self.pool.mark_ready(req.uid)
+
+    def _candidates(self, lease, req: _Request, ids: torch.Tensor, clock: _Clock) -> _Candidates:
+        out = _Candidates(hidden=None)
+
+        def on_stage(stage):
+            # The audit checks every session against its reservation; the
+            # ledger is what the caches hold at that point.
+            if stage == "executed":
+                clock.mark("extended", sync=False)   # the runtime synchronised already
+                self.pool.audit()
+                out.ledger_during = self._ledger()
+            else:
+                self.pool.audit()
+                out.ledger_after = self._ledger()
+                clock.mark("finished", sync=False)
+
+        out.hidden = self.runtime.candidate(lease.session, ids[req.prefix:], observer=on_stage).hidden
+        return out
 
     def execute(self, request: Mapping) -> ServingResult:
         if self.closed:
-            raise RuntimeError("runner has been closed")
-        self.backend.synchronize()
-        t0 = time.perf_counter()
-        uid, raw, prefix = self._validate(request)
-        signature, cpu_ids = _pack(raw, prefix)
+            raise RuntimeError("this runner is closed")
+        clock = _Clock(self.backend.synchronize)
+        clock.mark("start")
+        req = self._parse(request)
+        signature, cpu_ids = _pack(req.ids, req.prefix)
         ids = cpu_ids.to(device=self.backend.device)
         del cpu_ids
-        plan = self.runtime.plan_session(RequestShape(prefix, len(raw) - prefix), signature)
-        lease = self.pool.acquire(uid, signature, plan.retained_capacity, plan.reservation,
-                                  host_pages=plan.host_pages, hbm_tokens=plan.hbm_tokens, plan=plan)
-        session = lease.session
-        stamps = {}
+        lease = self._admit(req, signature)
         try:
-            self.backend.synchronize()
-            t_admit = time.perf_counter()
-            if not lease.hit:
-                self.runtime.prefill(session, ids[:prefix])
-                self.backend.synchronize()
-                self.pool.mark_ready(uid)
-            t_prefix = time.perf_counter()
-
-            def observe(stage):
-                if stage == "executed":
-                    stamps["extended"] = time.perf_counter()
-                    stamps["request_usage"] = self.pool.audit()
-                else:
-                    stamps["usage"] = self.pool.audit()
-                    stamps["finished"] = time.perf_counter()
-
-            result = self.runtime.candidate(session, ids[prefix:], observer=observe)
-        except BaseException as exec_error:
-            try:
-                self.pool.discard(uid)
-            except BaseException as cleanup_error:  # noqa: BLE001 - keep both failures
-                raise BaseExceptionGroup("request execution and session cleanup failed",
-                                         [exec_error, cleanup_error]) from None
+            clock.mark("admitted")
+            self._prefix(lease, req, ids)
+            clock.mark("prefixed", sync=False)
+            done = self._candidates(lease, req, ids, clock)
+        except BaseException as failure:
+            self._undo(failure, "the request failed and discarding its session failed too",
+                       lambda: self.pool.discard(req.uid))
             raise
-        diagnostics = self.driver.diagnostics(session)   # outside the timed interval
-        visit = self.visits[uid]
-        self.visits[uid] += 1
-        usage = self._usage(stamps["usage"])
-        req_usage = self._usage(stamps["request_usage"])
-        shared_now = self.pool.shared_bytes()
-        budget = self.pool.budget
-        metrics = {k: v for k, v in request.items() if k not in ("input_ids", "attention_mask", "prompt")}
-        metrics.update(
-            scheme=self.backend.scheme, user_id=uid, visit_index=visit, visit_number=visit + 1,
-            is_revisit=visit > 0,
-            prefix_hit_tier=(("hbm" if self.backend.scheme == "hbm" else "dram") if lease.hit else "miss"),
-            prefix_cache_hit=lease.hit, evicted_users=list(lease.evicted),
-            latency_ms=(stamps["finished"] - t0) * 1e3, admission_ms=(t_admit - t0) * 1e3,
-            prefix_ms=(t_prefix - t_admit) * 1e3, extend_ms=(stamps["extended"] - t_prefix) * 1e3,
-            cleanup_ms=(stamps["finished"] - stamps["extended"]) * 1e3,
-            stable_prefix_tokens=prefix, candidate_suffix_tokens=len(raw) - prefix,
-            resource_mode=self.resource_mode,
-            hbm_budget_bytes=None if budget is None else budget.hbm,
-            dram_budget_bytes=None if budget is None else budget.dram,
-            cache_hbm_bytes=usage.hbm, cache_dram_bytes=usage.dram,
-            request_cache_hbm_bytes=req_usage.hbm, request_cache_dram_bytes=req_usage.dram,
-            reserved_hbm_bytes=self.pool.reserved.hbm, reserved_dram_bytes=self.pool.reserved.dram,
-            shared_cache_hbm_bytes=shared_now.hbm, shared_cache_dram_bytes=shared_now.dram,
-            shared_reserved_hbm_bytes=self.pool.shared.hbm, shared_reserved_dram_bytes=self.pool.shared.dram,
-            session_reserved_hbm_bytes=self.pool.session_reserved.hbm,
-            session_reserved_dram_bytes=self.pool.session_reserved.dram,
-            cache_host_pages=self.pool.reserved_host_pages, host_page_capacity=self.pool.host_page_capacity,
-            session_host_pages=lease.entry.host_pages, cache_hbm_tokens=self.pool.reserved_hbm_tokens,
-            hbm_token_capacity=self.pool.hbm_token_capacity, session_hbm_tokens=lease.entry.hbm_tokens,
-            host_page_tokens=self.resource_plan.page_size,
-            cache_pool_scope=self.resource_plan.metadata.get("pool_scope", "session"),
-            cache_diagnostics=diagnostics, cached_users=len(self.pool),
-        )
-        return ServingResult(metrics, result.hidden)
+        return ServingResult(self._report(request, req, lease, clock, done), done.hidden)
 
-    def _usage(self, audit_report) -> CacheFootprint:
-        """Measured bytes summed over sessions + shared structures at an audit point."""
+    # -------------------------------------------------------------- report
+    def _ledger(self) -> CacheFootprint:
+        """Measured bytes of the shared structures plus every retained session."""
         total = self.pool.shared_bytes()
         for entry in self.pool._entries.values():
-            used = self.runtime.session_usage(entry.session).bytes
-            total = total + used
+            total = total + self.runtime.session_usage(entry.session).bytes
         return total
+
+    def _report(self, request: Mapping, req: _Request, lease, clock: _Clock, done: _Candidates) -> dict:
+        diagnostics = self.driver.diagnostics(lease.session)   # read after the timed part
+        visit = self.visits[req.uid]
+        self.visits[req.uid] += 1
+        pool, plan, budget = self.pool, self.resource_plan, self.pool.budget
+        after, during = done.ledger_after, done.ledger_during
+        shared = pool.shared_bytes()
+        hit_tier = ("hbm" if self.backend.scheme == "hbm" else "dram") if lease.hit else "miss"
+        timing = {
+            "latency_ms": clock.ms("start", "finished"), "admission_ms": clock.ms("start", "admitted"),
+            "prefix_ms": clock.ms("admitted", "prefixed"), "extend_ms": clock.ms("prefixed", "extended"),
+            "cleanup_ms": clock.ms("extended", "finished"),
+        }
+        visit_info = {
+            "scheme": self.backend.scheme, "user_id": req.uid, "visit_index": visit, "visit_number": visit + 1,
+            "is_revisit": visit > 0, "prefix_hit_tier": hit_tier, "prefix_cache_hit": lease.hit,
+            "evicted_users": list(lease.evicted), "stable_prefix_tokens": req.prefix,
+            "candidate_suffix_tokens": len(req.ids) - req.prefix,
+        }
+        ledger = {
+            "resource_mode": self.resource_mode,
+            "hbm_budget_bytes": budget.hbm if budget is not None else None,
+            "dram_budget_bytes": budget.dram if budget is not None else None,
+            "cache_hbm_bytes": after.hbm, "cache_dram_bytes": after.dram,
+            "request_cache_hbm_bytes": during.hbm, "request_cache_dram_bytes": during.dram,
+            "reserved_hbm_bytes": pool.reserved.hbm, "reserved_dram_bytes": pool.reserved.dram,
+            "shared_cache_hbm_bytes": shared.hbm, "shared_cache_dram_bytes": shared.dram,
+            "shared_reserved_hbm_bytes": pool.shared.hbm, "shared_reserved_dram_bytes": pool.shared.dram,
+            "session_reserved_hbm_bytes": pool.session_reserved.hbm,
+            "session_reserved_dram_bytes": pool.session_reserved.dram,
+            "cache_host_pages": pool.reserved_host_pages, "host_page_capacity": pool.host_page_capacity,
+            "session_host_pages": lease.entry.host_pages, "cache_hbm_tokens": pool.reserved_hbm_tokens,
+            "hbm_token_capacity": pool.hbm_token_capacity, "session_hbm_tokens": lease.entry.hbm_tokens,
+            "host_page_tokens": plan.page_size, "cache_pool_scope": plan.metadata.get("pool_scope", "session"),
+            "cache_diagnostics": diagnostics, "cached_users": len(pool),
+        }
+        passthrough = {k: v for k, v in request.items() if k not in ("input_ids", "attention_mask", "prompt")}
+        return {**passthrough, **visit_info, **timing, **ledger}
 
     def run(self, requests: Iterable[Mapping]) -> Iterator[ServingResult]:
         for request in requests:
@@ -258,5 +329,6 @@ class PersistentGRRunner:
             self.close()
         except BaseException as cleanup_error:
             if error is not None:
-                raise BaseExceptionGroup("runner body and close both failed", [error, cleanup_error]) from None
+                raise BaseExceptionGroup("the runner body and its close both failed", [error, cleanup_error]) \
+                    from None
             raise
