@@ -26,6 +26,9 @@ import time
 
 import torch
 
+# Recalled rows per layer of the reference's 64K + 128 cold extend on the real checkpoint
+# (experiments/deepseek_v32_mfu/report/shape_matrix/cache_metrics_samples.csv, H=65,536 A=128, layers 0-2).
+REFERENCE_RECALL_ROWS = (8909, 2875, 8007)
 # H200 published numbers per cache method (experiments/deepseek_v32_mfu/README.md:274-277):
 # full 64K prefill ms and full 128-token extend ms.
 BASELINE_MS = {"hbm": (644.938, 3.326), "echo": (648.375, 5.716), "serial_sparse": (640.701, 4.265),
@@ -57,6 +60,10 @@ def parse():
     p.add_argument("--comm", default="p2p", choices=["p2p", "torch"],
                    help="sp collectives: fused peer-memory kernels (p2p) or the NCCL baseline (torch)")
     p.add_argument("--full", action="store_true", help="the full 61-layer model (3 dense + 58 MoE layers)")
+    p.add_argument("--no-offload-methods", action="store_true",
+                   help="skip the per-method cold extends (serial_sparse / echo / dense_prefetch) of the hbm run")
+    p.add_argument("--no-sp", action="store_true",
+                   help="with N > 1 GPUs, skip the one-request sequence-parallel arms (fused and NCCL)")
     return p.parse_args()
 
 
@@ -90,6 +97,133 @@ def scope_rooflines(scopes: dict, flops: dict) -> dict:
         if ms:
             out[name] = {"ms": round(ms, 3), "tflops": round(f / ms / 1e9, 1)}
     return out
+
+
+def _events(n):
+    return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+
+
+def offload_extends(model, hist, ext, H: int, A: int, reps: int = 3) -> dict:
+    """Cold 128-token extends of the offload methods at P = NH = H + A.
+
+    For each method the model switches to that cache (empty pools), prefills
+    the history once, then repeats: drop the HBM copies of the history (DRAM
+    copies and indexer keys stay), time one extend (CUDA graph replay, eager
+    for dense_prefetch) with CUDA events, roll the candidates back.  Recalled
+    rows come from the pools' device counters.  ``matched`` drops only the
+    reference's per-layer recall counts of this extend (its real-checkpoint
+    selections are concentrated; random-init selections cover the history), so
+    the PCIe traffic matches the H200 measurement."""
+    stream = torch.cuda.current_stream()
+    out = {}
+    record_bytes = model.caches[0].row_bytes if hasattr(model.caches[0], "row_bytes") else 1152
+    runs = [("serial_sparse", None), ("echo", None), ("dense_prefetch", None),
+            ("serial_sparse", REFERENCE_RECALL_ROWS), ("echo", REFERENCE_RECALL_ROWS)]
+    for method, rows in runs:
+        if model.cache_cfg.method != method:
+            model.set_cache_method(method, pool_tokens=H + A, host_tokens=H + A)
+        model.reset()
+        p0, p1 = _events(2)
+        p0.record(stream)
+        model.prefill(hist)
+        p1.record(stream)
+        graph = None if method == "dense_prefetch" else model.capture_extend(A)
+        times, recalled = [], []
+        for r in range(reps):
+            model.clear_residency(rows_per_layer=rows, seed=r)
+            before = [c.stats.recalled_records + c.stats.prefetched_records for c in model.caches]
+            e0, e1 = _events(2)
+            e0.record(stream)
+            if graph is not None:
+                graph.replay(ext)
+                e1.record(stream)
+                graph.rollback()
+            else:
+                model.extend(ext)
+                e1.record(stream)
+                model.session.truncate(H)
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+            after = [c.stats.recalled_records + c.stats.prefetched_records for c in model.caches]
+            recalled.append(sum(a - b for a, b in zip(after, before)) / len(before))
+        del graph
+        key = method if rows is None else f"{method}_matched_recall"
+        rows_mean = sum(recalled) / len(recalled)
+        out[key] = {"cold_extend_ms": round(min(times), 4), "cold_extend_ms_mean": round(sum(times) / len(times), 4),
+                    "prefill_ms": round(p0.elapsed_time(p1), 3),
+                    "recalled_rows_per_layer": round(rows_mean, 1),
+                    "recalled_mb_per_layer": round(rows_mean * record_bytes / 1e6, 3),
+                    "extend_vs_baseline": round(BASELINE_MS[method][1] / min(times), 4)}
+        if rows is not None:
+            out[key]["dropped_rows_per_layer"] = list(rows)
+    model.set_cache_method("hbm")
+    return out
+
+
+def sp_arm(cfg, n_layers, args, dev, rank, world, comm: str) -> dict:
+    """One 64K request across all ranks: sequence-parallel attention,
+    column/row-parallel dense MLP (AG->GEMM, GEMM->RS), expert-parallel MoE,
+    with the fused peer-memory kernels (``p2p``) or the NCCL baseline
+    (``torch``).  Device time of the prefill, the extend and each collective
+    op (CUDA events), max over ranks."""
+    import torch.distributed as dist
+
+    from cxldsagr_b200.checkpoint import RandomSource
+    from cxldsagr_b200.config import CacheConfig
+    from cxldsagr_b200.models.deepseek_v32.model import DeepSeekV32Model
+    from cxldsagr_b200.parallel.comm import CollectiveTimer
+    from cxldsagr_b200.parallel.groups import ParallelContext
+
+    H, A = args.history, args.extend
+    par = ParallelContext(rank, world, dist.group.WORLD, dev, backend=comm)
+    src = RandomSource(cfg, layers=range(n_layers), seed=0, device=dev)
+    model = DeepSeekV32Model(cfg, src, device=dev, parallel=par,
+                             cache=CacheConfig(method="hbm", capacity=H + A, chunk_size=args.chunk, host_tokens=H + A,
+                                               candidate_tokens=A))
+    del src
+    g = torch.Generator().manual_seed(4321)
+    hist = torch.randint(0, cfg.vocab_size, (H,), generator=g).to(dev)
+    ext = torch.randint(0, cfg.vocab_size, (A,), generator=g).to(dev)
+    stream = torch.cuda.current_stream(dev)
+    timer = CollectiveTimer(dev)
+    for _ in range(max(1, args.warmup // 2)):
+        model.reset()
+        model.prefill(hist)
+        model.extend(ext)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    model.comm.timer = timer
+    steps = max(1, args.steps)
+    pre, extd = 0.0, 0.0
+    for _ in range(steps):
+        model.reset()
+        e = _events(3)
+        e[0].record(stream)
+        model.prefill(hist)
+        e[1].record(stream)
+        model.extend(ext)
+        e[2].record(stream)
+        torch.cuda.synchronize(dev)
+        pre += e[0].elapsed_time(e[1])
+        extd += e[1].elapsed_time(e[2])
+    model.comm.timer = None
+    coll = timer.summary()
+    names = sorted(coll)
+    vec = torch.tensor([pre / steps, extd / steps] + [coll[n]["ms"] / steps for n in names], dtype=torch.float64,
+                       device=dev)
+    dist.all_reduce(vec, op=dist.ReduceOp.MAX)
+    vals = vec.tolist()
+    calls = dict(getattr(model.comm, "fused_calls", {}))
+    if hasattr(model.comm, "close"):
+        model.comm.close()
+    del model
+    torch.cuda.empty_cache()
+    dist.barrier()
+    return {"prefill_ms": round(vals[0], 3), "extend_ms": round(vals[1], 4),
+            "prefill_tok_s": round(H / (vals[0] / 1e3), 1),
+            "collective_ms_per_step": {n: round(v, 3) for n, v in zip(names, vals[2:])},
+            "collective_calls_per_step": {n: coll[n]["calls"] // steps for n in names},
+            "fused_calls": calls}
 
 
 def main():
@@ -247,10 +381,39 @@ def main():
         del first, second
     e2e_s = sum(e2e_times) / max(1, len(e2e_times))
 
+    if graph is not None:
+        del graph
+        graph = None
+    # ---- the offload methods' cold extends (each rank measures its own request)
+    methods = None
+    if args.method == "hbm" and not sp and not args.full and not args.no_offload_methods:
+        methods = offload_extends(model, hist, ext, H, A)
+        if world > 1:
+            keys = sorted(methods)
+            vec = torch.tensor([methods[k]["cold_extend_ms"] for k in keys], dtype=torch.float64, device=dev)
+            dist.all_reduce(vec, op=dist.ReduceOp.MAX)
+            for k, v in zip(keys, vec.tolist()):
+                methods[k]["cold_extend_ms"] = round(v, 4)
+                methods[k]["extend_vs_baseline"] = round(BASELINE_MS[k.replace("_matched_recall", "")][1] / v, 4)
+    ops.check_errors(dev)
+
     stats = torch.tensor([prefill_ms, extend_ms, total_ms, e2e_s], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
     prefill_ms, extend_ms, total_ms, e2e_s = stats.tolist()
+    # ---- N > 1: the same request across the box (fused kernels, then the NCCL baseline)
+    sp_runs = None
+    if world > 1 and not sp and not args.full and not args.no_sp:
+        if hasattr(model.comm, "close"):
+            model.comm.close()
+        del model
+        torch.cuda.empty_cache()
+        sp_runs = {"parallelism": f"sp{world} attention + tp{world} dense MLP (+ ep{world} MoE layers)",
+                   "fused": sp_arm(cfg, n_layers, args, dev, rank, world, "p2p"),
+                   "nccl": sp_arm(cfg, n_layers, args, dev, rank, world, "torch")}
+        sp_runs["fused_vs_nccl_prefill"] = round(sp_runs["nccl"]["prefill_ms"] / sp_runs["fused"]["prefill_ms"], 4)
+        sp_runs["fused_vs_nccl_extend"] = round(sp_runs["nccl"]["extend_ms"] / sp_runs["fused"]["extend_ms"], 4)
+        model = None
     requests = 1 if sp else world
     base_prefill_ms, base_extend_ms = BASELINE_MS[args.method]
     base_tok_s = H / (base_prefill_ms / 1e3)
@@ -274,7 +437,7 @@ def main():
             "higher_is_better": True,
             "scaling": "strong" if sp else "weak",
             "vs_baseline": round(prefill_tok_s / (requests * base_tok_s), 4),
-            "dtype": "bf16",
+            "dtype": "fp8-block linears (e4m3, 128x128 scales), bf16 attention/KV",
             "data": "synthetic (uniform random token ids; random-init weights of the DeepSeek-V3.2 "
                     "architecture, FP8 128x128 block-scaled linears)",
             "config": {
@@ -296,6 +459,8 @@ def main():
             "extend_ms": round(extend_ms, 4),
             "extend_vs_baseline": round(base_extend_ms / extend_ms, 4),
             "extend_recalled_rows_per_layer": recall_rows,
+            "offload_methods": methods,
+            "sp": sp_runs,
             "clocks": clocks,
             "e2e": {
                 "value": round(requests * H / e2e_s, 1),
@@ -308,9 +473,7 @@ def main():
             "gpu_launches": int(launches),
         }
         print(json.dumps(out))
-    if graph is not None:
-        del graph
-    if hasattr(model.comm, "close"):
+    if model is not None and hasattr(model.comm, "close"):
         model.comm.close()
     if world > 1:
         dist.barrier()

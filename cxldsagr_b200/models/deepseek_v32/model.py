@@ -674,17 +674,31 @@ class DeepSeekV32Model:
     def truncate(self, length: int, *, session: ModelSession | None = None):
         (session or self.session).truncate(length)
 
-    def clear_residency(self, *, session: ModelSession | None = None):
+    def clear_residency(self, *, session: ModelSession | None = None, rows_per_layer=None, seed: int = 0):
         """Drop the HBM copies of a session's offloaded history (host copies and indexer keys stay):
-        the next steps recall every selected row from DRAM."""
+        the next steps recall every selected row from DRAM.
+
+        ``rows_per_layer`` (one count per layer, in model layer order) drops
+        only that many randomly chosen history rows of each layer instead of
+        all of them, so a following extend recalls at most that many rows per
+        layer; it pins the DRAM traffic of an extend to a given recall count."""
         session = session or self.session
         if session.pool_session is None or not self.pools:
             return
-        for g, (pool, ps) in enumerate(zip(self.pools, session.pool_sessions)):
+        gen = torch.Generator().manual_seed(seed)
+        first = 0
+        for pool, ps in zip(self.pools, session.pool_sessions):
             pool.drain()
             ids = ps.global_ids()
             for layer in range(pool.num_layers):
-                pool.release_ids(layer, ids)
+                drop = ids
+                if rows_per_layer is not None:
+                    hist = ids[: session.length]  # logical order: the committed history comes first
+                    count = min(int(rows_per_layer[first + layer]), hist.numel())
+                    pick = torch.randperm(hist.numel(), generator=gen)[:count].to(ids.device)
+                    drop = hist[pick]
+                pool.release_ids(layer, drop)
+            first += pool.num_layers
 
     def reset(self, *, session: ModelSession | None = None):
         (session or self.session).reset()

@@ -18,6 +18,9 @@ per op.
 
 from __future__ import annotations
 
+from collections import defaultdict
+from contextlib import contextmanager
+
 import torch
 
 from .. import ops
@@ -25,9 +28,57 @@ from . import collectives as C
 from .groups import ParallelContext
 
 
+class CollectiveTimer:
+    """Device time of each communication op (CUDA events on the current stream).
+
+    Attach one to :attr:`Comm.timer`; every ``ag_linear`` / ``linear_rs`` /
+    expert-parallel exchange then records a start and end event.  A fused op
+    that falls back to the baseline implementation is timed once (only the
+    outermost call counts).  :meth:`summary` synchronises and returns
+    ``{op: {"calls": n, "ms": total}}``.
+    """
+
+    def __init__(self, device: torch.device):
+        self.device = torch.device(device)
+        self._spans: dict[str, list] = defaultdict(list)
+        self._depth = 0
+
+    @contextmanager
+    def span(self, name: str):
+        if self._depth or self.device.type != "cuda":
+            yield
+            return
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        self._depth += 1
+        start.record()
+        try:
+            yield
+        finally:
+            end.record()
+            self._depth -= 1
+            self._spans[name].append((start, end))
+
+    def summary(self, *, reset: bool = True) -> dict:
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        out = {name: {"calls": len(ev), "ms": sum(a.elapsed_time(b) for a, b in ev)} for name, ev in self._spans.items()}
+        if reset:
+            self._spans.clear()
+        return out
+
+
+@contextmanager
+def _no_span():
+    yield
+
+
 class Comm:
     def __init__(self, ctx: ParallelContext):
         self.ctx = ctx
+        self.timer: CollectiveTimer | None = None
+
+    def _span(self, name: str):
+        return self.timer.span(name) if self.timer is not None else _no_span()
 
     @property
     def world(self) -> int:
@@ -44,16 +95,18 @@ class Comm:
         return C.all_gather_rows(self.ctx, normed, total, 0)
 
     def ag_linear(self, lin, normed, quantized, total: int) -> torch.Tensor:
-        g = self.gather(normed, quantized, total)
-        return lin(quantized=g) if isinstance(g, tuple) else lin(g)
+        with self._span("ag_gemm"):
+            g = self.gather(normed, quantized, total)
+            return lin(quantized=g) if isinstance(g, tuple) else lin(g)
 
     # ------------------------------------------------------------------ RS
     def linear_rs(self, lin, h, quantized) -> torch.Tensor:
         """Row-parallel linear over all rows, reduced and scattered to the row owners."""
-        partial = lin(h, quantized=quantized)
-        if self.world == 1:
-            return partial
-        return C.reduce_scatter_rows(self.ctx, partial, out_dtype=torch.bfloat16)
+        with self._span("gemm_rs"):
+            partial = lin(h, quantized=quantized)
+            if self.world == 1:
+                return partial
+            return C.reduce_scatter_rows(self.ctx, partial, out_dtype=torch.bfloat16)
 
     # -------------------------------------------------------------- EP a2a
     def dispatch(self, rows: torch.Tensor, scales_rows, dest: torch.Tensor, experts: torch.Tensor):
@@ -64,15 +117,17 @@ class Comm:
         ``experts`` [N] global expert id per row.  Returns the received rows,
         scales, expert ids and the per-source counts.
         """
-        counts = torch.bincount(dest, minlength=self.world).tolist()
-        recv, rc = C.all_to_all_rows(self.ctx, rows, counts)
-        rs = C.all_to_all_back(self.ctx, scales_rows, counts, rc) if scales_rows is not None else None
-        re = C.all_to_all_back(self.ctx, experts.to(torch.int32), counts, rc)
-        return recv, rs, re, counts, rc
+        with self._span("ep_dispatch"):
+            counts = torch.bincount(dest, minlength=self.world).tolist()
+            recv, rc = C.all_to_all_rows(self.ctx, rows, counts)
+            rs = C.all_to_all_back(self.ctx, scales_rows, counts, rc) if scales_rows is not None else None
+            re = C.all_to_all_back(self.ctx, experts.to(torch.int32), counts, rc)
+            return recv, rs, re, counts, rc
 
     def combine(self, out_rows: torch.Tensor, send_counts, recv_counts) -> torch.Tensor:
         """Return expert outputs to the rows' source ranks (inverse of :meth:`dispatch`)."""
-        return C.all_to_all_back(self.ctx, out_rows, recv_counts, send_counts)
+        with self._span("ep_combine"):
+            return C.all_to_all_back(self.ctx, out_rows, recv_counts, send_counts)
 
     # ---------------------------------------------------------------- misc
     def gather_rows(self, x, total: int):

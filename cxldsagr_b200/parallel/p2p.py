@@ -161,8 +161,9 @@ class P2PComm(Comm):
         out = torch.empty((total, N), dtype=torch.bfloat16, device=q.device)
         grid = self.lib().fp8_gemm_ag_grid(total, N)
         call, arrive, reuse = self.ag.next(grid, grid)
-        self.lib().fp8_gemm_ag(q.contiguous(), s_t.contiguous(), lin.weight, lin.scales, out, self.ctx.rank,
-                               self.world, call, arrive, reuse, self.flag_ptrs, self.g_ptrs, self.gs_ptrs)
+        with self._span("ag_gemm"):
+            self.lib().fp8_gemm_ag(q.contiguous(), s_t.contiguous(), lin.weight, lin.scales, out, self.ctx.rank,
+                                   self.world, call, arrive, reuse, self.flag_ptrs, self.g_ptrs, self.gs_ptrs)
         self.fused_calls["ag"] += 1
         return out
 
@@ -185,8 +186,9 @@ class P2PComm(Comm):
         rgrid = self.lib().rs_reduce_grid(S, N)
         call, arrive, reuse = self.rs.next(num_n * mblocks, rgrid)
         out = torch.empty((S, N), dtype=torch.bfloat16, device=q.device)
-        self.lib().fp8_gemm_rs(q, s_t, lin.weight, lin.scales, None, out, r, self.world, call, arrive, reuse,
-                               self.flag_ptrs, self.rb_ptrs)
+        with self._span("gemm_rs"):
+            self.lib().fp8_gemm_rs(q, s_t, lin.weight, lin.scales, None, out, r, self.world, call, arrive, reuse,
+                                   self.flag_ptrs, self.rb_ptrs)
         self.fused_calls["rs"] += 1
         return out
 
@@ -214,13 +216,16 @@ class P2PComm(Comm):
         p = self.ep_ptrs
         pos = torch.full((T * topk,), -1, dtype=torch.int32, device=q.device)
         ids32 = ids.to(torch.int32).contiguous()
-        self.lib().ep_dispatch(ids32, q.contiguous(), s_t, self.ep_cursor, pos, self.ep_block_expert, self.ctx.rank,
-                               self.world, E, self.ep_mpad, call, self.flag_ptrs, p["cnt"], p["a"], p["as"], p["y"])
+        with self._span("ep_dispatch"):
+            self.lib().ep_dispatch(ids32, q.contiguous(), s_t, self.ep_cursor, pos, self.ep_block_expert, self.ctx.rank,
+                                   self.world, E, self.ep_mpad, call, self.flag_ptrs, p["cnt"], p["a"], p["as"],
+                                   p["y"])
         a, a_s, y = self._ep_views(parity)
         experts_fn(a, a_s, self.ep_block_expert, y)
         out = torch.empty((T, D), dtype=torch.bfloat16, device=q.device)
-        self.lib().ep_combine(ids32, pos, weights.contiguous(), out, self.ctx.rank, self.world, E, self.ep_mpad, call,
-                              self.flag_ptrs, p["cnt"], p["a"], p["as"], p["y"])
+        with self._span("ep_combine"):
+            self.lib().ep_combine(ids32, pos, weights.contiguous(), out, self.ctx.rank, self.world, E, self.ep_mpad,
+                                  call, self.flag_ptrs, p["cnt"], p["a"], p["as"], p["y"])
         self.fused_calls["ep"] = self.fused_calls.get("ep", 0) + 1
         return out
 
