@@ -271,6 +271,7 @@ def main():
     if args.select_rows is not None:
         for block in model.blocks:
             block.attention.select_rows = args.select_rows
+    select_rows = model.blocks[0].attention.select_rows
     del src
     torch.cuda.empty_cache()
 
@@ -447,7 +448,7 @@ def main():
                 "history": H,
                 "extend": A,
                 "chunk": args.chunk,
-                "select_rows": model.blocks[0].attention.select_rows,
+                "select_rows": select_rows,
                 "cache_method": args.method,
                 "pool_tokens": (H + A) if offload else None,
                 "extend_residency": "cold (HBM copies of the history dropped before the extend)" if offload else "resident",

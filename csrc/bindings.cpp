@@ -194,12 +194,13 @@ void linear_f32(const Tensor& x, const Tensor& W, Tensor& out) {
                           ptr<float>(out), stream());
 }
 
-void embed(const Tensor& ids, const Tensor& table, Tensor& out) {
+void embed(const Tensor& ids, const Tensor& table, Tensor& out, int64_t row0, int64_t vocab_total) {
   CHECK_CUDA(ids); CHECK_DTYPE(ids, torch::kInt64); CHECK_DTYPE(table, torch::kBFloat16); CHECK_DTYPE(out, torch::kBFloat16);
   TORCH_CHECK(table.is_contiguous() && out.is_contiguous() && ids.is_contiguous(), "embed layout");
   c10::cuda::CUDAGuard g(ids.device());
-  b200::launch_embed(cptr<int64_t>(ids), ids.numel(), cptr<__nv_bfloat16>(table), table.size(0), table.size(1),
-                     ptr<__nv_bfloat16>(out), err_ptr(ids), stream());
+  const int64_t total = vocab_total > 0 ? vocab_total : table.size(0);
+  b200::launch_embed(cptr<int64_t>(ids), ids.numel(), cptr<__nv_bfloat16>(table), table.size(0), row0, total,
+                     table.size(1), ptr<__nv_bfloat16>(out), err_ptr(ids), stream());
 }
 
 // ------------------------------------------------------------- indexer
@@ -684,7 +685,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("index_k", &index_k);
   m.def("index_q", &index_q);
   m.def("linear_f32", &linear_f32);
-  m.def("embed", &embed);
+  m.def("embed", &embed, py::arg("ids"), py::arg("table"), py::arg("out"), py::arg("row0") = int64_t(0),
+        py::arg("vocab_total") = int64_t(0));
   m.def("indexer_logits", &indexer_logits);
   m.def("topk", &topk);
   m.def("sparse_mla", &sparse_mla);

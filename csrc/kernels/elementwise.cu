@@ -392,17 +392,26 @@ __global__ void __launch_bounds__(256) linear_f32_kernel(const __nv_bfloat16* __
 }
 
 // ----------------------------------------------------------------- embed
+// Vocabulary-sharded tables: `table` holds rows [row0, row0 + rows) of a
+// vocab_total-row embedding; ids outside the shard give zero rows (the shards'
+// outputs are summed across ranks afterwards), ids outside the whole
+// vocabulary are reported.
 __global__ void embed_kernel(const int64_t* __restrict__ ids, int T,
-                             const __nv_bfloat16* __restrict__ table, int64_t vocab, int D,
-                             __nv_bfloat16* __restrict__ out, int* err) {
+                             const __nv_bfloat16* __restrict__ table, int64_t rows, int64_t row0,
+                             int64_t vocab_total, int D, __nv_bfloat16* __restrict__ out, int* err) {
   const int t = blockIdx.x;
   int64_t id = ids[t];
-  if (id < 0 || id >= vocab) {
+  if (id < 0 || id >= vocab_total) {
     if (threadIdx.x == 0) record_error(err, kErrBadIndex);
-    id = 0;
+    id = row0;
   }
-  const uint4* src = reinterpret_cast<const uint4*>(table + id * D);
+  const int64_t local = id - row0;
   uint4* dst = reinterpret_cast<uint4*>(out + int64_t(t) * D);
+  if (local < 0 || local >= rows) {
+    for (int i = threadIdx.x; i < D / 8; i += blockDim.x) dst[i] = make_uint4(0u, 0u, 0u, 0u);
+    return;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(table + local * D);
   for (int i = threadIdx.x; i < D / 8; i += blockDim.x) dst[i] = src[i];
 }
 
@@ -481,11 +490,12 @@ void launch_linear_f32(const __nv_bfloat16* x, int64_t ldx, const float* W, int 
   cuda_check(cudaGetLastError(), "linear_f32 launch");
 }
 
-void launch_embed(const int64_t* ids, int T, const __nv_bfloat16* table, int64_t vocab, int D,
-                  __nv_bfloat16* out, int* err, cudaStream_t stream) {
+void launch_embed(const int64_t* ids, int T, const __nv_bfloat16* table, int64_t rows, int64_t row0,
+                  int64_t vocab_total, int D, __nv_bfloat16* out, int* err, cudaStream_t stream) {
   if (T <= 0) return;
   if (D % 8) throw std::invalid_argument("embed: D must be a multiple of 8");
-  embed_kernel<<<T, 256, 0, stream>>>(ids, T, table, vocab, D, out, err);
+  if (row0 < 0 || row0 + rows > vocab_total) throw std::invalid_argument("embed: shard outside the vocabulary");
+  embed_kernel<<<T, 256, 0, stream>>>(ids, T, table, rows, row0, vocab_total, D, out, err);
   cuda_check(cudaGetLastError(), "embed launch");
 }
 

@@ -182,8 +182,10 @@ void launch_index_q(const __nv_bfloat16* q, int64_t ldq, int T, int H, int D, in
 void launch_linear_f32(const __nv_bfloat16* x, int64_t ldx, const float* W, int T, int H, int K,
                        float* out, cudaStream_t stream);
 
-void launch_embed(const int64_t* ids, int T, const __nv_bfloat16* table, int64_t vocab, int D,
-                  __nv_bfloat16* out, int* err, cudaStream_t stream);
+// table holds rows [row0, row0 + rows) of a vocab_total-row table (shard
+// rows outside it embed as zeros).
+void launch_embed(const int64_t* ids, int T, const __nv_bfloat16* table, int64_t rows, int64_t row0,
+                  int64_t vocab_total, int D, __nv_bfloat16* out, int* err, cudaStream_t stream);
 
 // ------------------------------------------------------------- indexer
 // logits[q, t] = kscale[t] * sum_h relu(Q[q,h,:] . K[t,:]) * w[q,h]; -inf for

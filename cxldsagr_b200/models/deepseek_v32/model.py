@@ -366,9 +366,20 @@ class DeepSeekV32Model:
         cc = self.cache_cfg
         dev = self.device
         hd = self.head_device
-        self.embed_table = source.get_tensor("model.embed_tokens.weight").to(dev, torch.bfloat16).contiguous()
+        # One request across ranks (world > 1): the embedding table and the LM
+        # head are split by vocabulary rows, rank r keeping rows vocab_rows.
+        self.vocab_parallel = self.par.world > 1 and getattr(self.par, "vocab_parallel", True)
+        V = cfg.vocab_size
+        self.vocab_rows = shard_range(V, self.par.world, self.par.rank) if self.vocab_parallel else (0, V)
+        v0, v1 = self.vocab_rows
+
+        def vocab_shard(name, device, dtype):
+            full = source.get_tensor(name)
+            return (full[v0:v1] if self.vocab_parallel else full).to(device, dtype).contiguous()
+
+        self.embed_table = vocab_shard("model.embed_tokens.weight", dev, torch.bfloat16)
         self.final_norm = source.get_tensor("model.norm.weight").to(hd, torch.float32).contiguous()
-        self.lm_head = source.get_tensor("lm_head.weight").to(hd, torch.bfloat16).contiguous()
+        self.lm_head = vocab_shard("lm_head.weight", hd, torch.bfloat16)
         self._freqs = {d: ops.reference.rotary_frequencies(cfg, device=d) for d in self.pool_devices}
         self.freqs = self._freqs[self.pool_devices[0]]
         if len(self.pool_devices) > 1 and (cc.method == "dense_prefetch" or pool is not None or replay):
@@ -543,7 +554,14 @@ class DeepSeekV32Model:
             pos_on = {self.device: positions}
             rows = par.token_range(c1 - c0)
             with scope("embedding"):
-                hidden = ops.embed(ids[c0 + rows[0]:c0 + rows[1]], self.embed_table)
+                if self.vocab_parallel:
+                    # Every rank embeds the whole chunk from its vocabulary rows
+                    # (zeros elsewhere); the sum lands on each row's owner.
+                    partial = ops.embed(ids[c0:c1], self.embed_table, row0=self.vocab_rows[0],
+                                        vocab_total=cfg.vocab_size)
+                    hidden = self.comm.reduce_rows(partial)
+                else:
+                    hidden = ops.embed(ids[c0 + rows[0]:c0 + rows[1]], self.embed_table)
             residual = None
             n_rows = max(rows[1] - rows[0], 1)
             logits_buf = self._ensure_logits_buf(n_rows, start + c1)
@@ -588,16 +606,24 @@ class DeepSeekV32Model:
             normed = None
             if out_h.shape[0]:
                 normed, _ = ops.residual_rms_norm(out_h[keep], out_r[keep], self.final_norm, cfg.norm_eps)
-            logits = torch.empty((1, self.lm_head.shape[0]), dtype=torch.float32, device=hd)
-            if par.rank == owner:
-                last = normed[-1:]
-                logits = ops.linear(last, self.lm_head).float() if hd.type != "cuda" else self._lm_head(last)
-            if par.world > 1:
-                logits = self.comm.broadcast(logits.contiguous(), owner)
-                if want_hidden:
-                    local = normed if normed is not None else torch.empty((0, cfg.dim), dtype=torch.bfloat16,
-                                                                         device=self.device)
-                    normed = self.comm.gather_rows(local, n_last)
+            head = (lambda x: ops.linear(x, self.lm_head).float()) if hd.type != "cuda" else self._lm_head
+            if self.vocab_parallel:
+                # The owner's last row goes to every rank; each computes the
+                # logits of its vocabulary rows, then the shards are gathered.
+                last = normed[-1:].contiguous() if par.rank == owner else torch.empty(
+                    (1, cfg.dim), dtype=torch.bfloat16, device=hd)
+                last = self.comm.broadcast(last, owner)
+                logits = self.comm.gather_cols(head(last).contiguous(), cfg.vocab_size)
+            else:
+                logits = torch.empty((1, self.lm_head.shape[0]), dtype=torch.float32, device=hd)
+                if par.rank == owner:
+                    logits = head(normed[-1:])
+                if par.world > 1:
+                    logits = self.comm.broadcast(logits.contiguous(), owner)
+            if par.world > 1 and want_hidden:
+                local = normed if normed is not None else torch.empty((0, cfg.dim), dtype=torch.bfloat16,
+                                                                     device=self.device)
+                normed = self.comm.gather_rows(local, n_last)
         self.last_hidden = normed if want_hidden else None
         return logits
 

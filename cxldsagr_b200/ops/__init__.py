@@ -362,11 +362,15 @@ def gather_host_records(host, records, host_ids, slots, *, device_count=None):
     return records
 
 
-def embed(ids, table):
+def embed(ids, table, *, row0: int = 0, vocab_total: int | None = None):
+    """Embedding rows of ``ids``.  ``table`` may be a vocabulary shard holding
+    rows [row0, row0 + len(table)) of a ``vocab_total``-row table; ids outside
+    the shard give zero rows (sum the shards' outputs across ranks)."""
+    total = table.shape[0] if vocab_total is None else vocab_total
     if not table.is_cuda:
-        return table[ids.long()].bfloat16()
+        return reference.embed_shard(ids, table, row0, total)
     out = torch.empty((ids.numel(), table.shape[1]), dtype=torch.bfloat16, device=table.device)
-    lib().embed(ids.long().contiguous(), table, out)
+    lib().embed(ids.long().contiguous(), table, out, row0, total)
     return out
 
 

@@ -58,6 +58,18 @@ def silu_mul(gate, up):
 
 
 # ------------------------------------------------------------------ rope
+def embed_shard(ids: torch.Tensor, table: torch.Tensor, row0: int, vocab_total: int) -> torch.Tensor:
+    """Rows of a vocabulary shard (rows [row0, row0 + len(table))); ids outside the shard give zeros."""
+    ids = ids.long().reshape(-1)
+    if ((ids < 0) | (ids >= vocab_total)).any():
+        raise IndexError("token id outside the vocabulary")
+    local = ids - row0
+    inside = (local >= 0) & (local < table.shape[0])
+    out = torch.zeros((ids.numel(), table.shape[1]), dtype=torch.bfloat16, device=table.device)
+    out[inside] = table[local[inside]].bfloat16()
+    return out
+
+
 def rotary_frequencies(cfg, device="cpu") -> torch.Tensor:
     """YaRN-corrected inverse frequencies, length rope_dim / 2."""
     dim = cfg.qk_rope_head_dim

@@ -130,6 +130,20 @@ class Comm:
             return C.all_to_all_back(self.ctx, out_rows, recv_counts, send_counts)
 
     # ---------------------------------------------------------------- misc
+    def reduce_rows(self, x: torch.Tensor) -> torch.Tensor:
+        """Sum [T, D] over ranks and keep this rank's rows (vocabulary-parallel embedding)."""
+        if self.world == 1:
+            return x
+        with self._span("embed_rs"):
+            return C.reduce_scatter_rows(self.ctx, x, out_dtype=x.dtype)
+
+    def gather_cols(self, x: torch.Tensor, total: int) -> torch.Tensor:
+        """Concatenate every rank's column shard of [R, total] (vocabulary-parallel LM head)."""
+        if self.world == 1:
+            return x
+        with self._span("lm_head_gather"):
+            return C.all_gather_rows(self.ctx, x, total, 1)
+
     def gather_rows(self, x, total: int):
         return x if self.world == 1 else C.all_gather_rows(self.ctx, x, total, 0)
 

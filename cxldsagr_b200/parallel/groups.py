@@ -48,6 +48,7 @@ class ParallelContext:
     device: torch.device
     backend: str = "torch"          # "torch" (NCCL/gloo collectives) or "p2p" (fused peer-memory kernels)
     ep: bool = True                 # experts sharded across the group
+    vocab_parallel: bool = True     # embedding table and LM head split by vocabulary rows
 
     @property
     def is_parallel(self) -> bool:

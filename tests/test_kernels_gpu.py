@@ -563,3 +563,19 @@ def test_kv_gather_rejects_out_of_range_rows():
         ops.check_errors(dev)
     assert torch.equal(records[1].cpu(), host[3])  # the valid row still landed
     assert torch.count_nonzero(records[2]) == 0
+
+
+def test_embed_vocab_shard_matches_reference():
+    """A vocabulary shard embeds its own rows and zeros elsewhere; shards sum to the full table's rows."""
+    torch.manual_seed(3)
+    V, D = 1000, 256
+    table = torch.randn(V, D).bfloat16()
+    ids = torch.randint(0, V, (77,))
+    total = torch.zeros(77, D, dtype=torch.float32)
+    for r0, r1 in ((0, 334), (334, 667), (667, 1000)):
+        got = ops.embed(ids.to(DEV), table[r0:r1].to(DEV), row0=r0, vocab_total=V)
+        want = ref.embed_shard(ids, table[r0:r1], r0, V)
+        assert torch.equal(got.cpu(), want)
+        total += got.float().cpu()
+    assert torch.equal(total.bfloat16(), table[ids])
+    ops.check_errors(DEV)

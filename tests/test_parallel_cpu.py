@@ -122,3 +122,15 @@ def test_sequence_expert_parallel_matches_single(world, method):
         for got, want in ((a, single[0]), (b, single[1])):
             assert (got - want).abs().max() < 0.15 and corr(got, want) > 0.995
         assert corr(h, single[2]) > 0.99
+
+
+def test_embed_shards_sum_to_full_table():
+    from cxldsagr_b200 import ops
+
+    torch.manual_seed(0)
+    table = torch.randn(50, 16)
+    ids = torch.randint(0, 50, (30,))
+    parts = [ops.embed(ids, table[a:b], row0=a, vocab_total=50) for a, b in ((0, 17), (17, 34), (34, 50))]
+    assert torch.equal(sum(p.float() for p in parts).bfloat16(), table[ids].bfloat16())
+    with pytest.raises(IndexError):
+        ops.embed(torch.tensor([50]), table[:10], row0=0, vocab_total=50)
