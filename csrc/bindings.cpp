@@ -294,8 +294,8 @@ Tensor sparse_mla_trace() {
   return t;
 }
 
-int64_t fp8_gemm_splits(int64_t M, int64_t N, int64_t K) {
-  return b200::plan_fp8_gemm(int(M), int(N), int(K), 8).splits;
+int64_t fp8_gemm_splits(int64_t M, int64_t N, int64_t K, bool ue8m0) {
+  return b200::fp8_gemm_launch_splits(int(M), int(N), int(K), 8, ue8m0);
 }
 
 int64_t sparse_mla_scratch_bytes(int64_t T, int64_t H, int64_t splits) {
@@ -693,7 +693,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sparse_mla_scratch_bytes", &sparse_mla_scratch_bytes);
   m.def("sparse_mla_trace", &sparse_mla_trace);
   m.def("topk_trace", &topk_trace);
-  m.def("fp8_gemm_splits", &fp8_gemm_splits);
+  m.def("fp8_gemm_splits", &fp8_gemm_splits, py::arg("M"), py::arg("N"), py::arg("K"), py::arg("ue8m0") = false);
   m.def("gather_rows", &gather_rows);
   m.def("pool_recall", &pool_recall);
   m.def("pool_select", &pool_select);
@@ -704,6 +704,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("echo_hint", &echo_hint);
   m.def("fp8_gemm_ag", &fp8_gemm_ag);
   m.def("fp8_gemm_rs", &fp8_gemm_rs);
+  m.def("set_fp8_gemm_pair_tiles", &b200::set_fp8_gemm_pair_tiles);
   m.def("p2p_barrier", &p2p_barrier, py::arg("device"), py::arg("rank"), py::arg("world"), py::arg("call"),
         py::arg("flags"), py::arg("wait_ns") = int64_t(2000000000));
   m.def("sparse_mla_2sm_trace", &sparse_mla_2sm_trace);

@@ -41,7 +41,75 @@ void launch_fp8_gemm_t(const FP8GemmArgs& a, int splits, cudaStream_t stream) {
   }
 }
 
+// Pair tiles (256 x BN on a 2-CTA cluster); see gemm_fp8.cuh.
+template <int BN, int STAGES>
+void launch_fp8_gemm_pair_t(const FP8GemmArgs& a, int splits, cudaStream_t stream) {
+  const CUtensorMap ta = make_tma_2d(a.A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.M, a.K, a.lda, BK, BM);
+  const CUtensorMap tb = make_tma_2d(a.B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.N, a.K, a.ldb, BK, BN / 2);
+  const int tiles = ((a.M + 2 * BM - 1) / (2 * BM)) * ((a.N + BN - 1) / BN);
+  const int clusters = std::min(tiles * splits, sm_count() / 2);
+  const size_t smem = smem_bytes<BN, STAGES, kModePlain, false, true>();
+  auto kern = fp8_gemm_kernel<BN, STAGES, kModePlain, false, true>;
+  cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+             "fp8 pair gemm smem attribute");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cuda_check(cudaLaunchKernelEx(&cfg, kern, ta, tb, a.sfa, a.lda_s, a.sfb, a.out, a.ldo, a.residual, a.ldr, a.M,
+                                a.N, a.K, splits, a.partial, a.err, P2PArgs{}, GroupArgs{}),
+             "fp8 pair gemm launch");
+  if (splits > 1) {
+    const int64_t n = int64_t(a.M) * a.N;
+    splitk_reduce_kernel<<<int((n + 255) / 256), 256, 0, stream>>>(a.partial, splits, a.M, a.N, a.out, a.ldo,
+                                                                   a.residual, a.ldr);
+    cuda_check(cudaGetLastError(), "fp8 gemm split-k reduce launch");
+  }
+}
+
+// Off by default: on B200 the pair tiles measured ~10% slower than 128-row
+// tiles for every prefill shape (the per-K-block promotion, not the operand
+// feed, limits the promotion path).
+bool g_pair_tiles = false;
+
 }  // namespace
+
+void set_fp8_gemm_pair_tiles(bool enabled) { g_pair_tiles = enabled; }
+
+// Pair-tile plan: the same wave-quantisation cost with 256-row tiles on the
+// 74 SM pairs.
+static FP8GemmPlan plan_fp8_gemm_pair(int M, int N, int K, int max_splits) {
+  const int clusters = sm_count() / 2;
+  const int num_kb = (K + BK - 1) / BK;
+  const int64_t mt = (M + 2 * BM - 1) / (2 * BM);
+  FP8GemmPlan best{};
+  double best_cost = -1.0;
+  const int widths[3] = {256, 224, 128};
+  for (int bn : widths) {
+    if (bn == 224 && N % 224) continue;
+    const int64_t tiles = mt * ((N + bn - 1) / bn);
+    for (int sp = 1; sp <= (bn == 128 ? max_splits : 1); ++sp) {
+      if (sp > 1 && num_kb / sp < 8) break;
+      const int64_t waves = (tiles * sp + clusters - 1) / clusters;
+      const double reduce = sp > 1 ? (2.0 + double(sp) * M * N * 4.8e-6) * 128.0 : 0.0;
+      const double cost = double(waves) * ((num_kb + sp - 1) / sp) * bn * 2 + reduce;
+      if (best_cost < 0 || cost < best_cost * 0.999) {
+        best_cost = cost;
+        best.bn = bn;
+        best.splits = sp;
+      }
+    }
+  }
+  return best;
+}
 
 FP8GemmPlan plan_fp8_gemm(int M, int N, int K, int max_splits) {
   // Tile width BN in {256, 224, 128} and an optional K split, chosen by a
@@ -76,12 +144,25 @@ FP8GemmPlan plan_fp8_gemm(int M, int N, int K, int max_splits) {
 
 size_t fp8_gemm_scratch_bytes(int M, int N, int K, int max_splits) {
   const FP8GemmPlan p = plan_fp8_gemm(M, N, K, max_splits);
-  return p.splits > 1 ? size_t(p.splits) * M * N * sizeof(float) : 0;
+  const FP8GemmPlan pp = plan_fp8_gemm_pair(M, N, K, max_splits);
+  return size_t(std::max(p.splits, pp.splits) > 1 ? std::max(p.splits, pp.splits) : 0) * M * N * sizeof(float);
+}
+
+int fp8_gemm_launch_splits(int M, int N, int K, int max_splits, bool ue8m0) {
+  if (!ue8m0 && g_pair_tiles && M >= 2 * BM) return plan_fp8_gemm_pair(M, N, K, max_splits).splits;
+  return ue8m0 ? 1 : plan_fp8_gemm(M, N, K, max_splits).splits;
 }
 
 void launch_fp8_gemm(const FP8GemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return;
   if (a.K % 16) throw std::invalid_argument("fp8 gemm: K must be a multiple of 16");
+  if (!a.ue8m0 && g_pair_tiles && a.M >= 2 * BM) {
+    const FP8GemmPlan pp = plan_fp8_gemm_pair(a.M, a.N, a.K, a.partial ? a.max_splits : 1);
+    if (pp.bn == 256) launch_fp8_gemm_pair_t<256, 6>(a, 1, stream);
+    else if (pp.bn == 224) launch_fp8_gemm_pair_t<224, 6>(a, 1, stream);
+    else launch_fp8_gemm_pair_t<128, 8>(a, pp.splits, stream);
+    return;
+  }
   FP8GemmPlan p = plan_fp8_gemm(a.M, a.N, a.K, a.partial ? a.max_splits : 1);
   if (a.ue8m0) {
     if (p.bn == 256) launch_fp8_gemm_t<256, 4, true>(a, 1, stream);

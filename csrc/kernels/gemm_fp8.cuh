@@ -23,6 +23,19 @@
 //              Two TMEM buffers let the tensor core run the next K block
 //              meanwhile.
 //
+// Pair tiles (template PAIR, plain mode, promotion path): a 2-CTA cluster
+// computes a 256 x BN tile with tcgen05.mma.cta_group::2 (M = 256: each CTA
+// holds 128 rows of A and of the accumulator, and loads half of the tile's B
+// rows, which the pair's tensor cores share).  Both CTAs' TMA loads complete
+// on CTA 0's stage barrier (cta_group::2 TMA form, no multicast); CTA 0's
+// single thread issues the MMAs and commits their completion to the stage,
+// accumulator barriers of both CTAs; each CTA's epilogue promotes its own
+// 128 rows and releases the accumulator on CTA 0's barrier.  Halving the B
+// operand per CTA halves the shared-memory operand feed per MMA.  Measured on
+// B200 (M = 1024-2048, the prefill linears): ~10% slower than 128-row tiles,
+// because the per-K-block promotion, which pair tiles do not shorten, is the
+// limiter of this path; so pair tiles are opt-in (set_fp8_gemm_pair_tiles).
+//
 // Communication modes (template MODE, peer pointers in P2PArgs):
 //   AG (all-gather -> GEMM): A is the chunk gathered from every rank's row
 //      shard.  At kernel start the epilogue warps of every CTA (idle until the
@@ -85,10 +98,10 @@ constexpr int kSfSlotCols = 12;     // TMEM columns per scale slot: SFA 4 + SFB 
 constexpr int kSfSlots = 4;
 constexpr uint32_t kSfCol0 = 512 - kSfSlots * kSfSlotCols;
 
-template <int BN, int STAGES, bool BS = false>
+template <int BN, int STAGES, bool BS = false, int BROWS = BN>
 struct GemmSmem {
   alignas(1024) uint8_t a[STAGES][BM * BK];
-  alignas(1024) uint8_t b[STAGES][BN * BK];
+  alignas(1024) uint8_t b[STAGES][BROWS * BK];  // B rows this CTA loads (BN, or BN / 2 for pair tiles)
   alignas(128) uint8_t sf[BS ? STAGES : 1][BS ? 3 * kSfChunk : 16];  // SFA, SFB rows 0-127, SFB rows 128-255
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
@@ -118,10 +131,38 @@ __device__ __forceinline__ bool ag_wait_rows(const P2PArgs& p, int m0, int M, ui
   return true;
 }
 
+// 2-D tiled TMA load into this CTA's shared memory whose completion is
+// counted on the mbarrier at shared::cluster address `bar` (CTA 0 of the
+// pair): the cta_group::2 form of a plain (non-multicast) load.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* desc, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(desc), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_f8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void commit_pair_at(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync_pair() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // UE8M0 code of a power-of-two FP32 scale: its biased exponent.
 __device__ __forceinline__ uint32_t ue8m0_byte(float v) { return (__float_as_uint(v) >> 23) & 0xFFu; }
 
-template <int BN, int STAGES, int MODE, bool BS = false>
+template <int BN, int STAGES, int MODE, bool BS = false, bool PAIR = false>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                     const __grid_constant__ CUtensorMap tma_b, const float* __restrict__ sfa,
@@ -129,12 +170,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     int ldo, const __nv_bfloat16* __restrict__ residual, int ldr, int M, int N,
                     int K, int splits, float* __restrict__ partial, int* err,
                     const __grid_constant__ P2PArgs p2p, const __grid_constant__ GroupArgs grp) {
+  static_assert(!PAIR || (MODE == kModePlain && !BS), "pair tiles: plain mode, promotion path");
+  constexpr int BROWS = PAIR ? BN / 2 : BN;  // B rows loaded by this CTA
+  constexpr int TM = PAIR ? 2 * BM : BM;     // rows of a tile
   extern __shared__ uint8_t smem_raw[];
-  auto& s = *reinterpret_cast<GemmSmem<BN, STAGES, BS>*>(
+  auto& s = *reinterpret_cast<GemmSmem<BN, STAGES, BS, BROWS>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int num_m = (M + BM - 1) / BM;
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0u;
+  const int cta0 = PAIR ? int(blockIdx.x >> 1) : int(blockIdx.x);  // first work unit of this CTA (or pair)
+  const int cstride = PAIR ? int(gridDim.x >> 1) : int(gridDim.x);  // work units advance by this
+  const int row_off = int(crank) * BM;                               // this CTA's rows inside a tile
+  const int num_m = (M + TM - 1) / TM;
   const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (K + BK - 1) / BK;
@@ -142,7 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Work unit = (tile, K split); split-major so concurrent CTAs share a K range.
   const int num_units = num_tiles * splits;
   const int kps = (num_kb + splits - 1) / splits;
-  const int rot = MODE == kModeRS ? ((p2p.rank + 1) % p2p.world) * p2p.S / BM % num_m : 0;
+  const int rot = MODE == kModeRS ? ((p2p.rank + 1) % p2p.world) * p2p.S / TM % num_m : 0;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -151,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.tmem_full[i], 1);
-      mbar_init(&s.tmem_empty[i], kEpiWarps);
+      mbar_init(&s.tmem_empty[i], kEpiWarps * (PAIR ? 2 : 1));  // pair: both CTAs' epilogues release on CTA 0
     }
     s.abort_flag = 0;
     fence_barrier_init();
@@ -162,8 +210,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kTmemCols = BS ? 512 : (2 * BN <= 256 ? 256 : 512);
   constexpr int kAccBufs = (!BS || 2 * BN <= int(kSfCol0)) ? 2 : 1;
   if (warp == 1) {
-    tmem_alloc(&s.tmem_base, kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s.tmem_base)),
+                   "r"(kTmemCols)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      tmem_alloc(&s.tmem_base, kTmemCols);
+      tmem_relinquish();
+    }
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tma_a);
@@ -171,6 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_pair();  // both CTAs' barriers exist before any remote arrive
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
   volatile int* abort_flag = &s.abort_flag;
@@ -310,9 +366,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       uint32_t ready = 0;  // AG: shards known to have arrived
       bool ok = true;
-      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      for (int u = cta0; u < num_units && ok; u += cstride) {
         const int tile = u % num_tiles, sp = u / num_tiles;
-        const int m0 = tile_m_block(tile, num_m, rot) * BM;
+        const int m0 = tile_m_block(tile, num_m, rot) * TM + row_off;
         int n0 = (tile / num_m) * BN;
         const int kb0 = sp * kps, kb1 = min(num_kb, kb0 + kps);
         if constexpr (MODE == kModeAG) {
@@ -332,17 +388,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&s.full[stage], BM * BK + BN * BK);
-          tma_load_2d(s.a[stage], &tma_a, &s.full[stage], kb * BK, m0);
-          tma_load_2d(s.b[stage], &tma_b, &s.full[stage], kb * BK, n0);
+          if constexpr (PAIR) {
+            // Both CTAs' loads complete on CTA 0's barrier, which expects the pair's bytes.
+            if (crank == 0) mbar_arrive_expect_tx(&s.full[stage], 2 * (BM * BK + BROWS * BK));
+            const uint32_t fb = mapa_shared(smem_u32(&s.full[stage]), 0);
+            tma_load_2d_pair(s.a[stage], &tma_a, fb, kb * BK, m0);
+            tma_load_2d_pair(s.b[stage], &tma_b, fb, kb * BK, n0 + int(crank) * BROWS);
+          } else {
+            mbar_arrive_expect_tx(&s.full[stage], BM * BK + BN * BK);
+            tma_load_2d(s.a[stage], &tma_a, &s.full[stage], kb * BK, m0);
+            tma_load_2d(s.b[stage], &tma_b, &s.full[stage], kb * BK, n0);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
-      if (!ok) {
-        // Drain copies already in flight before the CTA releases its smem.
+      if (!ok && (!PAIR || crank == 0)) {
+        // Drain copies already in flight before the CTA releases its smem
+        // (pair: CTA 0's barriers count both CTAs' loads).
         for (int i = 0; i < STAGES; ++i) mbar_wait(&s.full[i], 0, nullptr, 0, nullptr, 100000000ull);
       }
     }
@@ -400,13 +465,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (elect_one()) {
-      const uint32_t idesc = umma_idesc(BM, BN, 0, 0);
+    if (elect_one() && (!PAIR || crank == 0)) {
+      const uint32_t idesc = umma_idesc(TM, BN, 0, 0);
+      auto wait_bar = [&](uint64_t* bar, uint32_t par, int code) {
+        return PAIR ? mbar_wait_cluster(bar, par, err, code, abort_flag) : mbar_wait(bar, par, err, code, abort_flag);
+      };
+      auto commit_both = [&](uint64_t* bar) {
+        if constexpr (PAIR) {
+          commit_pair_at(smem_u32(bar));
+          commit_pair_at(mapa_shared(smem_u32(bar), 1));
+        } else {
+          mma_commit(bar);
+        }
+      };
       int stage = 0;
       uint32_t phase = 0;
       uint32_t kcount = 0;  // global K-block counter -> TMEM buffer + parity
       bool ok = true;
-      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      for (int u = cta0; u < num_units && ok; u += cstride) {
         const int sp = u / num_tiles;
         const int kb0 = sp * kps, kb1 = min(num_kb, kb0 + kps);
         if constexpr (MODE == kModeGrouped) {
@@ -415,12 +491,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = kb0; kb < kb1; ++kb, ++kcount) {
           const uint32_t buf = kcount & 1;
           const uint32_t bpar = (kcount >> 1) & 1;
-          if (!mbar_wait(&s.tmem_empty[buf], bpar ^ 1, err, kErrTimeoutTmemEmpty, abort_flag)) {
+          if (!wait_bar(&s.tmem_empty[buf], bpar ^ 1, kErrTimeoutTmemEmpty)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          if (!mbar_wait(&s.full[stage], phase, err, kErrTimeoutTmaFull, abort_flag)) {
+          if (!wait_bar(&s.full[stage], phase, kErrTimeoutTmaFull)) {
             ok = false;
             break;
           }
@@ -430,10 +506,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < BK / 32; ++k) {
             // +32 bytes along K inside the swizzled 128-byte row.
-            mma_f8_ss(tmem + buf * BN, adesc + (k * 32 >> 4), bdesc + (k * 32 >> 4), idesc, k > 0);
+            if constexpr (PAIR)
+              mma_f8_pair(tmem + buf * BN, adesc + (k * 32 >> 4), bdesc + (k * 32 >> 4), idesc, k > 0);
+            else
+              mma_f8_ss(tmem + buf * BN, adesc + (k * 32 >> 4), bdesc + (k * 32 >> 4), idesc, k > 0);
           }
-          mma_commit(&s.empty[stage]);
-          mma_commit(&s.tmem_full[buf]);
+          commit_both(&s.empty[stage]);
+          commit_both(&s.tmem_full[buf]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -452,7 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     // RS staging tile [BM][BN + 8] bf16 after the pipeline buffers (dynamic smem).
     __nv_bfloat16* stage =
-        reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(&s) + sizeof(GemmSmem<BN, STAGES, BS>));
+        reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(&s) + sizeof(GemmSmem<BN, STAGES, BS, BROWS>));
 
     if constexpr (MODE == kModeAG) {
       // Push this rank's shard (rows [rank*S, rank*S+S) of the gathered A) and
@@ -497,10 +576,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t tcount = 0;  // BS: tiles finished (accumulator buffer + parity)
     uint32_t ready = 0;
     int owner_ok = -1;  // RS: owner whose reuse guard this thread already passed
-    for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+    // Pair tiles: CTA 1's epilogue warps release the accumulator on CTA 0.
+    auto release_acc = [&](uint64_t* bar) {
+      if (PAIR && crank == 1) mbar_arrive_remote(mapa_shared(smem_u32(bar), 0));
+      else mbar_arrive(bar);
+    };
+    for (int u = cta0; u < num_units && ok; u += cstride) {
       const int tile = u % num_tiles, sp = u / num_tiles;
       const int kb0 = sp * kps, kb1 = min(num_kb, kb0 + kps);
-      const int m0 = tile_m_block(tile, num_m, rot) * BM;
+      const int m0 = tile_m_block(tile, num_m, rot) * TM + row_off;
       const int n0 = (tile / num_m) * BN + chalf * CPW;  // first column of this warp
       const int row = m0 + row_in_tile;
       const float* sfb_u = sfb;
@@ -571,7 +655,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&s.tmem_empty[buf]);
+          if (lane == 0) release_acc(&s.tmem_empty[buf]);
         }
       }
       // RS threads always reach the per-tile named barrier below (a thread that
@@ -690,9 +774,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_pair();  // no CTA leaves while its peer may still signal it
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    if constexpr (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    else
+      tmem_dealloc(tmem, kTmemCols);
   }
   if constexpr (MODE == kModeAG) {
     // Every load of this CTA has been consumed: tell each rank its data here may be overwritten.
@@ -703,9 +791,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int BN, int STAGES, int MODE = kModePlain, bool BS = false>
+template <int BN, int STAGES, int MODE = kModePlain, bool BS = false, bool PAIR = false>
 inline size_t smem_bytes() {
-  return sizeof(GemmSmem<BN, STAGES, BS>) + 1024 + (MODE == kModeRS ? size_t(BM) * (BN + 8) * 2 : 0);
+  return sizeof(GemmSmem<BN, STAGES, BS, PAIR ? BN / 2 : BN>) + 1024 +
+         (MODE == kModeRS ? size_t(BM) * (BN + 8) * 2 : 0);
 }
 
 }  // namespace gemm_fp8

@@ -34,6 +34,10 @@ struct FP8GemmPlan {
   int splits;
 };
 FP8GemmPlan plan_fp8_gemm(int M, int N, int K, int max_splits);
+// Pair (256-row, 2-CTA) tiles for the plain promotion path when M >= 256 (default off).
+void set_fp8_gemm_pair_tiles(bool enabled);
+// K splits launch_fp8_gemm uses for this shape (1 = no split-K reduce launch).
+int fp8_gemm_launch_splits(int M, int N, int K, int max_splits, bool ue8m0);
 size_t fp8_gemm_scratch_bytes(int M, int N, int K, int max_splits);
 void launch_fp8_gemm(const FP8GemmArgs& a, cudaStream_t stream);
 

@@ -116,6 +116,29 @@ def test_fp8_gemm_residual(M, N, K):
     assert rel_err(got.cpu(), want) < 2e-2
 
 
+@pytest.mark.parametrize("M,N,K", [(256, 7168, 2048), (300, 2304, 7168), (1000, 7168, 4096), (2048, 2048, 1024),
+                                   (512, 18432, 2048), (384, 640, 512)])
+def test_fp8_gemm_pair_tiles_match_single(M, N, K):
+    """256-row pair tiles (2-CTA cta_group::2) against the FP32 oracle and the 128-row kernel:
+    every tile width, an M that is not a multiple of 256, a residual."""
+    torch.manual_seed(8)
+    x = torch.randn(M, K, device=DEV).bfloat16()
+    w, s = quantize_weight_blocks(torch.randn(N, K, device=DEV) * 0.02, pow2_scales=False)
+    res = torch.randn(M, N, device=DEV).bfloat16()
+    ops.lib().set_fp8_gemm_pair_tiles(True)
+    try:
+        got = ops.fp8_linear(x, w, s, residual=res)
+    finally:
+        ops.lib().set_fp8_gemm_pair_tiles(False)
+    want = ref.fp8_linear(x.cpu(), w.cpu(), s.cpu()).float() + res.cpu().float()
+    assert rel_err(got.cpu(), want) < 2e-2
+    single = ops.fp8_linear(x, w, s, residual=res)
+    torch.cuda.synchronize()
+    # Same per-128-K promotion order per output: the two kernels agree to BF16 rounding.
+    assert rel_err(got.cpu(), single.cpu().float()) < 5e-3
+    ops.check_errors(DEV)
+
+
 @pytest.mark.parametrize("G,M,N,K", [(1, 1, 1000, 7168), (4, 130, 512, 128), (3, 64, 128, 512)])
 def test_bf16_bmm(G, M, N, K):
     torch.manual_seed(6)
