@@ -113,15 +113,17 @@ def offload_extends(model, hist, ext, H: int, A: int, reps: int = 3) -> dict:
     rows come from the pools' device counters.  ``matched`` drops only the
     reference's per-layer recall counts of this extend (its real-checkpoint
     selections are concentrated; random-init selections cover the history), so
-    the PCIe traffic matches the H200 measurement."""
+    the PCIe traffic matches the H200 measurement.  ``*_fp8_records`` repeat the
+    runs with 656-byte FP8 KV records in the DRAM arena (1152-byte BF16 otherwise)."""
     stream = torch.cuda.current_stream()
     out = {}
-    record_bytes = model.caches[0].row_bytes if hasattr(model.caches[0], "row_bytes") else 1152
-    runs = [("serial_sparse", None), ("echo", None), ("dense_prefetch", None),
-            ("serial_sparse", REFERENCE_RECALL_ROWS), ("echo", REFERENCE_RECALL_ROWS)]
-    for method, rows in runs:
-        if model.cache_cfg.method != method:
-            model.set_cache_method(method, pool_tokens=H + A, host_tokens=H + A)
+    runs = [(m, rows, fmt) for fmt in ("bf16", "fp8")
+            for m, rows in (("serial_sparse", None), ("echo", None), ("dense_prefetch", None),
+                            ("serial_sparse", REFERENCE_RECALL_ROWS), ("echo", REFERENCE_RECALL_ROWS))]
+    for method, rows, fmt in runs:
+        if model.cache_cfg.method != method or model.cache_cfg.kv_format != fmt:
+            model.set_cache_method(method, pool_tokens=H + A, host_tokens=H + A, kv_format=fmt)
+        record_bytes = model.caches[0].record_bytes
         model.reset()
         p0, p1 = _events(2)
         p0.record(stream)
@@ -147,7 +149,7 @@ def offload_extends(model, hist, ext, H: int, A: int, reps: int = 3) -> dict:
             after = [c.stats.recalled_records + c.stats.prefetched_records for c in model.caches]
             recalled.append(sum(a - b for a, b in zip(after, before)) / len(before))
         del graph
-        key = method if rows is None else f"{method}_matched_recall"
+        key = (method if rows is None else f"{method}_matched_recall") + ("_fp8_records" if fmt == "fp8" else "")
         rows_mean = sum(recalled) / len(recalled)
         out[key] = {"cold_extend_ms": round(min(times), 4), "cold_extend_ms_mean": round(sum(times) / len(times), 4),
                     "prefill_ms": round(p0.elapsed_time(p1), 3),
@@ -156,7 +158,8 @@ def offload_extends(model, hist, ext, H: int, A: int, reps: int = 3) -> dict:
                     "extend_vs_baseline": round(BASELINE_MS[method][1] / min(times), 4)}
         if rows is not None:
             out[key]["dropped_rows_per_layer"] = list(rows)
-    model.set_cache_method("hbm")
+        out[key]["record_bytes"] = record_bytes
+    model.set_cache_method("hbm", kv_format="bf16")
     return out
 
 
@@ -395,7 +398,8 @@ def main():
             dist.all_reduce(vec, op=dist.ReduceOp.MAX)
             for k, v in zip(keys, vec.tolist()):
                 methods[k]["cold_extend_ms"] = round(v, 4)
-                methods[k]["extend_vs_baseline"] = round(BASELINE_MS[k.replace("_matched_recall", "")][1] / v, 4)
+                base = k.replace("_fp8_records", "").replace("_matched_recall", "")
+                methods[k]["extend_vs_baseline"] = round(BASELINE_MS[base][1] / v, 4)
     ops.check_errors(dev)
 
     stats = torch.tensor([prefill_ms, extend_ms, total_ms, e2e_s], dtype=torch.float64, device=dev)

@@ -157,14 +157,36 @@ void mla_q_rope(const Tensor& q, int64_t ldq, int64_t T, int64_t H, int64_t nope
 }
 
 void kv_finish(const Tensor& kv, int64_t L, int64_t R, const Tensor& norm_w, double eps, const Tensor& freqs,
-               const Tensor& positions, Tensor& out, const c10::optional<Tensor>& dst_row) {
+               const Tensor& positions, Tensor& out, const c10::optional<Tensor>& dst_row,
+               const c10::optional<Tensor>& packed) {
   CHECK_CUDA(kv); CHECK_DTYPE(kv, torch::kBFloat16); CHECK_DTYPE(out, torch::kBFloat16); CHECK_LAST_CONTIG(kv);
   c10::cuda::CUDAGuard g(kv.device());
   const int64_t* dr = nullptr;
   if (dst_row && dst_row->defined()) { CHECK_DTYPE((*dst_row), torch::kInt64); dr = cptr<int64_t>(*dst_row); }
+  uint8_t* pk = nullptr;
+  if (packed && packed->defined()) {
+    CHECK_DTYPE((*packed), torch::kUInt8);
+    TORCH_CHECK(packed->is_contiguous() && packed->dim() == 2 && packed->size(1) == 656 && packed->size(0) >= kv.size(0),
+                "kv_finish: packed records [>= T, 656] uint8");
+    pk = ptr<uint8_t>(*packed);
+  }
   b200::launch_kv_finish(cptr<__nv_bfloat16>(kv), kv.stride(0), kv.size(0), L, R, cptr<float>(norm_w), float(eps),
                          cptr<float>(freqs), cptr<float>(positions), ptr<__nv_bfloat16>(out), out.stride(0), dr,
-                         out.size(0), err_ptr(kv), stream());
+                         out.size(0), err_ptr(kv), stream(), pk);
+}
+
+// records[slots[i]] = dequant(packed[i]) for i < min(n, device_count).
+void dequant_kv_rows(const Tensor& packed, Tensor& records, const c10::optional<Tensor>& slots, int64_t n,
+                     const c10::optional<Tensor>& device_count) {
+  CHECK_CUDA(packed); CHECK_DTYPE(packed, torch::kUInt8); CHECK_DTYPE(records, torch::kBFloat16);
+  TORCH_CHECK(packed.is_contiguous() && packed.size(1) == 656 && packed.size(0) >= n, "dequant_kv_rows: packed [n, 656]");
+  TORCH_CHECK(records.is_contiguous() && records.size(1) == 576, "dequant_kv_rows: records [*, 576]");
+  c10::cuda::CUDAGuard g(packed.device());
+  const int64_t* sl = nullptr;
+  if (slots && slots->defined()) { CHECK_DTYPE((*slots), torch::kInt64); sl = cptr<int64_t>(*slots); }
+  b200::launch_dequant_kv_rows(cptr<uint8_t>(packed), ptr<__nv_bfloat16>(records), sl, int(n),
+                               (device_count && device_count->defined()) ? cptr<int>(*device_count) : nullptr,
+                               records.size(0), err_ptr(records), stream());
 }
 
 void index_k(const Tensor& k, int64_t R, const Tensor& ln_w, const Tensor& ln_b, double eps, const Tensor& freqs,
@@ -303,16 +325,18 @@ int64_t sparse_mla_scratch_bytes(int64_t T, int64_t H, int64_t splits) {
 }
 
 // ------------------------------------------------------------ transfer
-void gather_rows(const Tensor& host, Tensor& records, const Tensor& host_ids, const Tensor& slots, int64_t n,
-                 const c10::optional<Tensor>& device_count) {
+void gather_rows(const Tensor& host, Tensor& records, const Tensor& host_ids, const c10::optional<Tensor>& slots,
+                 int64_t n, const c10::optional<Tensor>& device_count) {
   TORCH_CHECK(host.is_pinned(), "gather_rows: host must be pinned");
-  CHECK_CUDA(records); CHECK_DTYPE(host_ids, torch::kInt64); CHECK_DTYPE(slots, torch::kInt64);
+  CHECK_CUDA(records); CHECK_DTYPE(host_ids, torch::kInt64);
+  const bool have_slots = slots && slots->defined();
+  if (have_slots) CHECK_DTYPE((*slots), torch::kInt64);
   TORCH_CHECK(host.is_contiguous() && records.is_contiguous() && host.stride(0) * host.element_size() == records.stride(0) * records.element_size(),
               "gather_rows: matching contiguous rows");
   c10::cuda::CUDAGuard g(records.device());
   const int row_bytes = records.stride(0) * records.element_size();
-  b200::launch_gather_rows(cptr<uint8_t>(host), ptr<uint8_t>(records), cptr<int64_t>(host_ids), cptr<int64_t>(slots),
-                           int(n), (device_count && device_count->defined()) ? cptr<int>(*device_count) : nullptr,
+  b200::launch_gather_rows(cptr<uint8_t>(host), ptr<uint8_t>(records), cptr<int64_t>(host_ids),
+                           have_slots ? cptr<int64_t>(*slots) : nullptr, int(n), (device_count && device_count->defined()) ? cptr<int>(*device_count) : nullptr,
                            row_bytes, host.size(0), records.size(0), err_ptr(records), stream());
 }
 
@@ -413,17 +437,22 @@ b200::TensorDesc desc_of(const Tensor& t) {
 void pool_recall_dispatch(const Tensor& ids, int64_t hist_end, const Tensor& page_table, Tensor& h2d, Tensor& d2h,
                           Tensor& priority, Tensor& meta, Tensor& mark, Tensor& miss_list, Tensor& victims,
                           Tensor& stats, Tensor& select_stats, int64_t k_limit, int64_t count_slot, const Tensor& host,
-                          Tensor& records) {
+                          Tensor& records, const c10::optional<Tensor>& fp8_scratch) {
   b200::RecallDesc d;
   d.ids = desc_of(ids); d.page_table = desc_of(page_table); d.h2d = desc_of(h2d); d.d2h = desc_of(d2h);
   d.priority = desc_of(priority); d.meta = desc_of(meta); d.mark = desc_of(mark); d.miss_list = desc_of(miss_list);
   d.victims = desc_of(victims); d.stats = desc_of(stats); d.select_stats = desc_of(select_stats);
   d.host = desc_of(host); d.records = desc_of(records);
   d.hist_end = hist_end; d.k_limit = k_limit; d.count_slot = count_slot;
+  d.fp8_host = fp8_scratch && fp8_scratch->defined();
   c10::cuda::CUDAGuard g(h2d.device());
+  Tensor scratch = (fp8_scratch && fp8_scratch->defined()) ? *fp8_scratch : Tensor();
+  if (scratch.defined())
+    TORCH_CHECK(scratch.scalar_type() == torch::kUInt8 && scratch.size(1) == 656 && scratch.size(0) >= miss_list.numel() &&
+                host.size(1) * host.element_size() == 656, "pool_recall_dispatch: FP8 scratch [>= P+1, 656]");
   struct Stages {
     const Tensor &ids, &page_table, &host;
-    Tensor &h2d, &d2h, &priority, &meta, &mark, &miss_list, &victims, &stats, &select_stats, &records;
+    Tensor &h2d, &d2h, &priority, &meta, &mark, &miss_list, &victims, &stats, &select_stats, &records, &scratch;
     int64_t hist_end, k_limit, count_slot;
     void classify() {
       auto a = pool_args(ids, hist_end, page_table, h2d, d2h, priority, meta, mark, miss_list, victims, stats);
@@ -437,13 +466,23 @@ void pool_recall_dispatch(const Tensor& ids, int64_t hist_end, const Tensor& pag
     void gather() {
       // meta word 2 holds the rows placed; its low 32 bits are the gather's device-side count.
       const int* count = reinterpret_cast<const int*>(meta.data_ptr<int64_t>()) + 4;
+      if (scratch.defined()) {
+        // FP8 host records: the 656-byte rows cross PCIe into a dense scratch,
+        // then are dequantized into their pool slots.
+        b200::launch_gather_rows(cptr<uint8_t>(host), ptr<uint8_t>(scratch), cptr<int64_t>(miss_list), nullptr,
+                                 int(miss_list.numel()), count, 656, host.size(0), scratch.size(0), err_ptr(records),
+                                 stream());
+        b200::launch_dequant_kv_rows(cptr<uint8_t>(scratch), ptr<__nv_bfloat16>(records), cptr<int64_t>(victims),
+                                     int(miss_list.numel()), count, records.size(0), err_ptr(records), stream());
+        return;
+      }
       const int row_bytes = int(records.stride(0) * records.element_size());
       b200::launch_gather_rows(cptr<uint8_t>(host), ptr<uint8_t>(records), cptr<int64_t>(miss_list),
                                cptr<int64_t>(victims), int(miss_list.numel()), count, row_bytes, host.size(0),
                                records.size(0), err_ptr(records), stream());
     }
   } stages{ids, page_table, host, h2d, d2h, priority, meta, mark, miss_list, victims, stats, select_stats, records,
-           hist_end, k_limit, count_slot};
+           scratch, hist_end, k_limit, count_slot};
   b200::run_recall(d, stages);
 }
 
@@ -681,7 +720,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quant_act", &quant_act);
   m.def("silu_mul_quant", &silu_mul_quant);
   m.def("mla_q_rope", &mla_q_rope);
-  m.def("kv_finish", &kv_finish);
+  m.def("kv_finish", &kv_finish, py::arg("kv"), py::arg("L"), py::arg("R"), py::arg("norm_w"), py::arg("eps"),
+        py::arg("freqs"), py::arg("positions"), py::arg("out"), py::arg("dst_row"), py::arg("packed") = py::none());
   m.def("index_k", &index_k);
   m.def("index_q", &index_q);
   m.def("linear_f32", &linear_f32);
@@ -698,7 +738,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("pool_recall", &pool_recall);
   m.def("pool_select", &pool_select);
   m.def("pool_recall_select", &pool_recall_select);
-  m.def("pool_recall_dispatch", &pool_recall_dispatch);
+  m.def("pool_recall_dispatch", &pool_recall_dispatch, py::arg("ids"), py::arg("hist_end"), py::arg("page_table"),
+        py::arg("h2d"), py::arg("d2h"), py::arg("priority"), py::arg("meta"), py::arg("mark"), py::arg("miss_list"),
+        py::arg("victims"), py::arg("stats"), py::arg("select_stats"), py::arg("k_limit"), py::arg("count_slot"),
+        py::arg("host"), py::arg("records"), py::arg("fp8_scratch") = py::none());
+  m.def("dequant_kv_rows", &dequant_kv_rows);
   m.def("pool_map", &pool_map);
   m.def("echo_predict", &echo_predict);
   m.def("echo_hint", &echo_hint);

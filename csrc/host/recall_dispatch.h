@@ -39,6 +39,8 @@ struct TensorDesc {
 struct RecallDesc {
   TensorDesc ids, page_table, h2d, d2h, priority, meta, mark, miss_list, victims, stats, select_stats, host, records;
   int64_t hist_end = 0, k_limit = -1, count_slot = 0;
+  // Host rows are 656-byte FP8 records dequantized into 1152-byte BF16 device rows.
+  bool fp8_host = false;
 };
 
 // Stage numbers used in errors and traces.
@@ -96,8 +98,12 @@ inline void validate_gather(const RecallDesc& a) {
   require(a.records.defined && a.records.device == a.h2d.device, kStageGather, "device records must be on the pool device");
   require(a.host.ndim == 2 && a.records.ndim == 2 && a.host.contiguous && a.records.contiguous, kStageGather,
           "records must be contiguous 2-D");
-  require(a.host.dtype == a.records.dtype && a.host.row_bytes == a.records.row_bytes && a.host.row_bytes > 0,
-          kStageGather, "host and device records must have one dtype and row width");
+  if (a.fp8_host)
+    require(a.host.row_bytes == 656 && a.records.row_bytes == 1152, kStageGather,
+            "FP8 host records are 656 bytes and dequantize into 1152-byte device rows");
+  else
+    require(a.host.dtype == a.records.dtype && a.host.row_bytes == a.records.row_bytes && a.host.row_bytes > 0,
+            kStageGather, "host and device records must have one dtype and row width");
   require(a.host.rows >= a.h2d.numel, kStageGather, "host arena shorter than the host_to_device map");
   require(a.records.rows >= a.d2h.numel, kStageGather, "device records shorter than the slot maps");
 }

@@ -228,13 +228,22 @@ __global__ void mla_q_rope_kernel(const __nv_bfloat16* __restrict__ q, int64_t l
 }
 
 // One CTA (128 threads) per token: RMSNorm of the latent, interleaved RoPE of k_pe.
+//
+// FP8 records (packed != nullptr, L = 512, R = 64): the BF16-rounded latent is
+// quantized per 128-dim block to E4M3 with scale s = amax / 448 (FP32), and
+// the record row receives the exact dequantized values bf16(float(q) * s), so a
+// row recalled from its packed form (dequant_kv_rows) is bitwise the resident
+// one.  packed[t] is the 656-byte record: 512 E4M3 bytes, 4 FP32 scales,
+// 64 BF16 RoPE values.
 __global__ void kv_finish_kernel(const __nv_bfloat16* __restrict__ kv, int64_t ldkv, int T, int L,
                                  int R, const float* __restrict__ norm_w, float eps,
                                  const float* __restrict__ freqs,
                                  const float* __restrict__ positions,
                                  __nv_bfloat16* __restrict__ out, int64_t ldo,
-                                 const int64_t* __restrict__ dst_row, int64_t out_rows, int* err) {
+                                 const int64_t* __restrict__ dst_row, int64_t out_rows,
+                                 uint8_t* __restrict__ packed, int* err) {
   __shared__ float red[4];
+  __shared__ float bmax[4][4];
   const int t = blockIdx.x;
   const __nv_bfloat16* src = kv + t * ldkv;
   const int64_t drow = dst_row ? dst_row[t] : int64_t(t);
@@ -254,15 +263,50 @@ __global__ void kv_finish_kernel(const __nv_bfloat16* __restrict__ kv, int64_t l
   float tot = 0.f;
   for (int i = 0; i < blockDim.x / 32; ++i) tot += red[i];
   const float inv = rsqrtf(tot / L + eps);
-  for (int i = threadIdx.x; i < L; i += blockDim.x)
-    dst[i] = __float2bfloat16_rn(__bfloat162float(src[i]) * inv * norm_w[i]);
+  if (packed == nullptr) {
+    for (int i = threadIdx.x; i < L; i += blockDim.x)
+      dst[i] = __float2bfloat16_rn(__bfloat162float(src[i]) * inv * norm_w[i]);
+  } else {
+    // Thread j owns dim j of each 128-dim block k (L = 4 x 128, blockDim = 128).
+    float x[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      x[k] = __bfloat162float(__float2bfloat16_rn(__bfloat162float(src[128 * k + threadIdx.x]) * inv *
+                                                  norm_w[128 * k + threadIdx.x]));
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float m = fabsf(x[k]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (threadIdx.x % 32 == 0) bmax[k][threadIdx.x / 32] = m;
+    }
+    __syncthreads();
+    uint8_t* prow = packed + int64_t(t) * 656;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float amax = fmaxf(fmaxf(bmax[k][0], bmax[k][1]), fmaxf(bmax[k][2], bmax[k][3]));
+      const float sc = amax / 448.f;
+      const __nv_fp8_storage_t q =
+          sc > 0.f ? __nv_cvt_float_to_fp8(x[k] / sc, __NV_SATFINITE, __NV_E4M3) : __nv_fp8_storage_t(0);
+      const float deq = __half2float(__half(__nv_cvt_fp8_to_halfraw(q, __NV_E4M3))) * sc;
+      dst[128 * k + threadIdx.x] = __float2bfloat16_rn(deq);
+      prow[128 * k + threadIdx.x] = q;
+      if (threadIdx.x == 0) reinterpret_cast<float*>(prow + 512)[k] = sc;
+    }
+  }
   for (int i = threadIdx.x; i < R / 2; i += blockDim.x) {
     const float a = __bfloat162float(src[L + 2 * i]);
     const float b = __bfloat162float(src[L + 2 * i + 1]);
     float c, s;
     rope_angle(freqs, positions, t, i, c, s);
-    dst[L + 2 * i] = __float2bfloat16_rn(a * c - b * s);
-    dst[L + 2 * i + 1] = __float2bfloat16_rn(b * c + a * s);
+    const __nv_bfloat16 r0 = __float2bfloat16_rn(a * c - b * s), r1 = __float2bfloat16_rn(b * c + a * s);
+    dst[L + 2 * i] = r0;
+    dst[L + 2 * i + 1] = r1;
+    if (packed != nullptr) {
+      __nv_bfloat16* pr = reinterpret_cast<__nv_bfloat16*>(packed + int64_t(t) * 656 + 528);
+      pr[2 * i] = r0;
+      pr[2 * i + 1] = r1;
+    }
   }
 }
 
@@ -456,10 +500,12 @@ void launch_mla_q_rope(const __nv_bfloat16* q, int64_t ldq, int T, int H, int no
 void launch_kv_finish(const __nv_bfloat16* kv, int64_t ldkv, int T, int L, int R,
                       const float* norm_w, float eps, const float* freqs,
                       const float* positions, __nv_bfloat16* out, int64_t ldo,
-                      const int64_t* dst_row, int64_t out_rows, int* err, cudaStream_t stream) {
+                      const int64_t* dst_row, int64_t out_rows, int* err, cudaStream_t stream,
+                      uint8_t* packed) {
   if (T <= 0) return;
+  if (packed && (L != 512 || R != 64)) throw std::invalid_argument("kv_finish: FP8 records need L = 512, R = 64");
   kv_finish_kernel<<<T, 128, 0, stream>>>(kv, ldkv, T, L, R, norm_w, eps, freqs, positions, out, ldo, dst_row,
-                                          out_rows, err);
+                                          out_rows, packed, err);
   cuda_check(cudaGetLastError(), "kv_finish launch");
 }
 

@@ -166,7 +166,12 @@ void launch_mla_q_rope(const __nv_bfloat16* q, int64_t ldq, int T, int H, int no
 void launch_kv_finish(const __nv_bfloat16* kv, int64_t ldkv, int T, int L, int R,
                       const float* norm_w, float eps, const float* freqs,
                       const float* positions, __nv_bfloat16* out, int64_t ldo,
-                      const int64_t* dst_row, int64_t out_rows, int* err, cudaStream_t stream);
+                      const int64_t* dst_row, int64_t out_rows, int* err, cudaStream_t stream,
+                      uint8_t* packed = nullptr);
+// records[slots[i]] (BF16 [*, 576]) = dequantized packed[i] (656-byte FP8 records),
+// i < min(n, *device_count); slots == nullptr: identity.
+void launch_dequant_kv_rows(const uint8_t* packed, __nv_bfloat16* records, const int64_t* slots, int n,
+                            const int* device_count, int64_t pool_rows, int* err, cudaStream_t stream);
 
 // Indexer key: k = bf16(layernorm(x) * w + b); rope split-half on the first R
 // dims; quantise the 128-d row (UE8M0) -> k_q [t], k_scale [t].

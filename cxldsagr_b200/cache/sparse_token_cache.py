@@ -21,6 +21,7 @@ from dataclasses import dataclass, asdict
 
 import torch
 
+from ..ops.reference import fp8_record_bytes
 from .sparse_token_pool import MISSING, PAGE_SIZE, SharedSparseTokenPool, SparseTokenSession, _device
 
 
@@ -49,19 +50,27 @@ _SELECTED, _RESIDENT, _EVICTED, _RECALLED, _PREFETCHED = 0, 1, 2, 3, 5
 
 class SparseTokenCache:
     def __init__(self, capacity: int, width: int, *, device="cuda", dtype=torch.bfloat16,
-                 slots: int | None = None, candidate_slots: int = 0):
-        """Standalone cache: resident (``slots`` None) or a private pool of ``slots`` rows."""
+                 slots: int | None = None, candidate_slots: int = 0, kv_format: str = "bf16",
+                 latent_dim: int | None = None):
+        """Standalone cache: resident (``slots`` None) or a private pool of ``slots`` rows.
+
+        ``kv_format="fp8"``: rows are FP8-quantized once on write (the resident
+        rows hold the dequantized values, a pool's host arena the 656-byte records)."""
         if capacity < 1 or width < 1:
             raise ValueError("capacity and width must be positive")
         self._init_stats(device)
         if slots is not None:
             host = ((capacity + PAGE_SIZE - 1) // PAGE_SIZE) * PAGE_SIZE
             pool = SharedSparseTokenPool(host, width, 1, slots, device=device, dtype=dtype,
-                                         candidate_slots=candidate_slots)
+                                         candidate_slots=candidate_slots, kv_format=kv_format, latent_dim=latent_dim)
             session = pool.allocate_session(capacity)
             self._bind(session, 0)
             session._layers[0] = self
             return
+        if kv_format not in ("bf16", "fp8"):
+            raise ValueError("kv_format must be 'bf16' or 'fp8'")
+        self.kv_format = kv_format
+        self.latent_dim = SharedSparseTokenPool._split(width, latent_dim)[0] if kv_format == "fp8" else None
         self._pool = None
         self.session = None
         self.layer_id = 0
@@ -105,6 +114,7 @@ class SparseTokenCache:
     def _bind(self, session, layer):
         pool = session.pool
         self._pool, self.session, self.layer_id = pool, session, layer
+        self.kv_format, self.latent_dim = pool.kv_format, pool.latent_dim
         self.capacity, self.width, self.slots = session.capacity, pool.width, pool.slots
         self.candidate_slots = pool.candidate_slots
         self.device, self.offload = pool.device, True
@@ -116,7 +126,16 @@ class SparseTokenCache:
     # ---------------------------------------------------------------- helpers
     @property
     def record_bytes(self) -> int:
+        """Bytes of one record as it crosses PCIe (656 for FP8 records)."""
+        if self.kv_format == "fp8":
+            return fp8_record_bytes(self.latent_dim, self.width - self.latent_dim)
         return self.width * self.records.element_size()
+
+    def packed_rows(self, count: int):
+        """A fresh [count, record bytes] uint8 buffer for kv_finish's FP8 records (None for BF16 caches)."""
+        if self.kv_format != "fp8":
+            return None
+        return torch.empty((count, self.record_bytes), dtype=torch.uint8, device=self.device)
 
     # Set by a serving backend for borrowed session caches: raises unless the
     # owning session's own operation is active (see ResourceLifecycle.check_active).
@@ -256,11 +275,15 @@ class SparseTokenCache:
             self._pool.stamp(self.layer_id, chosen)
         return chosen
 
-    def finish_append(self, rows: torch.Tensor):
-        """Complete an append whose records were written into ``records[rows]``."""
+    def finish_append(self, rows: torch.Tensor, packed: torch.Tensor | None = None):
+        """Complete an append whose records were written into ``records[rows]``
+        (``packed``: their 656-byte FP8 records, required for FP8 caches)."""
         start, count = self.written, rows.numel()
+        if self.kv_format == "fp8" and packed is None:
+            raise ValueError("an FP8 cache append needs the packed records")
         if self._pool is not None and self.transient_start is None:
-            self._pool.write_host(self.session, self.layer_id, start, self.records[rows])
+            source = packed[:count] if self.kv_format == "fp8" else self.records[rows]
+            self._pool.write_host(self.session, self.layer_id, start, source)
             self._stats.device_to_host_bytes += count * self.record_bytes
         if self.transient_start is not None:
             self._stats.transient_written_records += count
@@ -272,9 +295,14 @@ class SparseTokenCache:
         if records.ndim != 2 or records.shape[1] != self.width or not len(records):
             raise ValueError("invalid appended records")
         rows = self.destination_rows(len(records))
+        packed = None
         with self.operation():
+            if self.kv_format == "fp8":
+                from .. import ops
+
+                records, packed = ops.fp8_kv_records(records.to(self.records.dtype), self.latent_dim)
             self.records[rows] = records.to(self.records.dtype)
-        return self.finish_append(rows)
+        return self.finish_append(rows, packed)
 
     # ----------------------------------------------------------------- recall
     def ensure(self, indices: torch.Tensor) -> torch.Tensor:
@@ -309,7 +337,8 @@ class SparseTokenCache:
                 self._dev[_EVICTED] += self._pool.evict(self.layer_id, chosen)
                 from .. import ops
 
-                ops.gather_host_records(pool.host, pool.records, missing, chosen)
+                ops.gather_host_records(pool.host, pool.records, missing, chosen, fp8_scratch=self._pool.fp8_scratch,
+                                        latent_dim=self._pool.latent_dim)
                 pool.h2d[missing] = chosen.int()
                 pool.d2h[chosen] = missing
                 self._dev[_RECALLED] += int(missing.numel())
@@ -353,7 +382,8 @@ class SparseTokenCache:
             self._dev[_EVICTED] += self._pool.evict(self.layer_id, chosen)
             from .. import ops
 
-            ops.gather_host_records(pool.host, pool.records, missing, chosen)
+            ops.gather_host_records(pool.host, pool.records, missing, chosen, fp8_scratch=self._pool.fp8_scratch,
+                                        latent_dim=self._pool.latent_dim)
             pool.h2d[missing] = chosen.int()
             pool.d2h[chosen] = missing
             self._pool.stamp(self.layer_id, chosen)
@@ -375,7 +405,7 @@ class SparseTokenCache:
         ops.lib().pool_recall_dispatch(ids32, hist_end, self.session.page_table, pool.h2d, pool.d2h, pool.priority,
                                        pool.meta, pool.mark, pool.miss_list, pool.victims, stats,
                                        self._dev if stats is self._scratch else stats, k_limit, count_slot,
-                                       pool.host, pool.records)
+                                       pool.host, pool.records, self._pool.fp8_scratch)
         return pool
 
     def _ensure_native(self, indices: torch.Tensor) -> torch.Tensor:

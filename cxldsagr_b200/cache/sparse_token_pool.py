@@ -2,7 +2,8 @@
 
 Layout per layer (reference semantics: ``cache/sparse_token_pool.py:98-906``):
 
-* ``host``     [NH, W]    pinned DRAM arena, owned by sessions in 64-token pages;
+* ``host``     [NH, W]    pinned DRAM arena, owned by sessions in 64-token pages
+  (``kv_format="fp8"``: [NH, 656] uint8, the packed FP8 records);
 * ``records``  [P+1+C, W] HBM pool: slot 0 is a never-allocated padding
   sentinel, slots 1..P hold history records, the C tail slots hold a
   session's transient candidate records (no host pages, no maps);
@@ -28,6 +29,7 @@ from dataclasses import dataclass, field
 
 import torch
 
+from ..ops.reference import fp8_record_bytes
 from .host_allocation import allocate_host_tensor, pinned_allocation_bytes, tensor_bytes
 
 PAGE_SIZE = 64
@@ -103,22 +105,41 @@ class SharedSparseTokenPool:
 
     @classmethod
     def estimate_shared_bytes(cls, host_capacity, width, layers, slots, *, dtype=torch.bfloat16,
-                              device="cuda", candidate_slots=0) -> dict:
+                              device="cuda", candidate_slots=0, kv_format="bf16", latent_dim=None) -> dict:
         """Exact persistent bytes of the pool ({"hbm", "dram"}) before allocating it."""
         cls._validate(host_capacity, width, layers, slots, candidate_slots)
         size = torch.empty((), dtype=dtype).element_size()
-        host = host_capacity * width * size
+        fp8_row = fp8_record_bytes(*cls._split(width, latent_dim)) if kv_format == "fp8" else 0
+        host_row = fp8_row if kv_format == "fp8" else width * size
+        host = host_capacity * host_row
         if torch.device(device).type == "cuda":
             host = pinned_allocation_bytes(host)
         per_layer = ((slots + 1 + candidate_slots) * width * size + host_capacity * 8 + (slots + 1) * 32 + 64)
+        if kv_format == "fp8":
+            per_layer += (slots + 1) * fp8_row  # recall scratch
         hbm = layers * per_layer
         if torch.device(device).type == "cpu":
             return {"hbm": 0, "dram": hbm + layers * host}
         return {"hbm": hbm, "dram": layers * host}
 
+    @staticmethod
+    def _split(width: int, latent_dim: int | None) -> tuple[int, int]:
+        """(latent, rope) widths of a KV row (V3.2: 512 + 64)."""
+        L = latent_dim if latent_dim is not None else (512 if width == 576 else None)
+        if L is None or not 0 < L < width:
+            raise ValueError("FP8 records need the latent width of the KV row")
+        return L, width - L
+
     def __init__(self, host_capacity, width, layers, slots, *, device="cuda", dtype=torch.bfloat16,
-                 candidate_slots=0, max_inflight_writes=2):
+                 candidate_slots=0, max_inflight_writes=2, kv_format="bf16", latent_dim=None):
         self._validate(host_capacity, width, layers, slots, candidate_slots)
+        if kv_format not in ("bf16", "fp8"):
+            raise ValueError("kv_format must be 'bf16' or 'fp8'")
+        if kv_format == "fp8" and dtype != torch.bfloat16:
+            raise ValueError("FP8 records cover BF16 MLA KV rows")
+        self.kv_format = kv_format
+        self.latent_dim = self._split(width, latent_dim)[0] if kv_format == "fp8" else None
+        host_row = fp8_record_bytes(self.latent_dim, width - self.latent_dim) if kv_format == "fp8" else 0
         self.device = _device(device)
         self.host_capacity, self.width, self.num_layers, self.slots = host_capacity, width, layers, slots
         self.candidate_slots = candidate_slots
@@ -129,8 +150,10 @@ class SharedSparseTokenPool:
         for _ in range(layers):
             priority = torch.full((slots + 1,), -1, dtype=torch.int64, device=self.device)
             priority[0] = MISSING
+            host_shape, host_dtype = ((host_capacity, host_row), torch.uint8) if kv_format == "fp8" else \
+                ((host_capacity, width), dtype)
             self.layers.append(LayerPool(
-                host=allocate_host_tensor((host_capacity, width), dtype=dtype, pin_memory=pin),
+                host=allocate_host_tensor(host_shape, dtype=host_dtype, pin_memory=pin),
                 records=torch.zeros((slots + 1 + candidate_slots, width), dtype=dtype, device=self.device),
                 h2d=torch.full((host_capacity,), MISSING, dtype=torch.int32, device=self.device),
                 d2h=torch.full((slots + 1,), MISSING, dtype=torch.int64, device=self.device),
@@ -140,6 +163,10 @@ class SharedSparseTokenPool:
                 miss_list=torch.zeros(slots + 1, dtype=torch.int64, device=self.device),
                 victims=torch.zeros(slots + 1, dtype=torch.int64, device=self.device),
             ))
+        # FP8 host records cross PCIe into this dense scratch and are dequantized
+        # into their slots (one recall event at a time per pool).
+        self.fp8_scratch = (torch.zeros((slots + 1, host_row), dtype=torch.uint8, device=self.device)
+                            if kv_format == "fp8" else None)
         self._free_pages = list(range(host_capacity // PAGE_SIZE - 1, -1, -1))
         self._sessions: dict[int, SparseTokenSession] = {}
         self._next_owner = 0
@@ -163,6 +190,8 @@ class SharedSparseTokenPool:
         for layer in self.layers:
             ts += [layer.host, layer.records, layer.h2d, layer.d2h, layer.priority, layer.meta, layer.mark,
                    layer.miss_list, layer.victims]
+        if self.fp8_scratch is not None:
+            ts.append(self.fp8_scratch)
         return tensor_bytes(ts)
 
     def _check(self):

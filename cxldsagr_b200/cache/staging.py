@@ -6,6 +6,10 @@ buffer (l + 1) % 2 with layer l+1's history from pinned host memory.  A
 lease hands out a buffer; ``prefetch`` enqueues the host->device copy on
 the staging stream and records a ready event; ``wait_ready`` makes the
 compute stream wait for it (no host synchronisation).
+
+FP8 records (``fp8_records=True``): the host arena holds 656-byte records;
+the copy engine fills a packed staging buffer and ``wait_ready`` dequantizes
+the staged rows into the BF16 buffer on the compute stream.
 """
 
 from __future__ import annotations
@@ -26,19 +30,24 @@ class StagingLease:
     def buffer(self) -> torch.Tensor:
         return self.staging.buffers[self.index][: self.rows]
 
+    def _target(self) -> torch.Tensor:
+        st = self.staging
+        return st.packed[self.index] if st.packed is not None else st.buffers[self.index]
+
     def prefetch(self, host: torch.Tensor, rows: int):
         st = self.staging
         if rows > st.buffers[self.index].shape[0]:
             raise ValueError("history exceeds the staging buffer")
         self.rows = rows
+        target = self._target()
         if st.stream is None:
-            st.buffers[self.index][:rows].copy_(host[:rows])
+            target[:rows].copy_(host[:rows])
             return self
         # The buffer may still be read by the layer that used it two steps ago.
         if st.consumed[self.index] is not None:
             st.stream.wait_event(st.consumed[self.index])
         with torch.cuda.stream(st.stream):
-            st.buffers[self.index][:rows].copy_(host[:rows], non_blocking=True)
+            target[:rows].copy_(host[:rows], non_blocking=True)
             self.event = torch.cuda.Event()
             self.event.record(st.stream)
         return self
@@ -53,7 +62,7 @@ class StagingLease:
         if rows > st.buffers[self.index].shape[0]:
             raise ValueError("history exceeds the staging buffer")
         self.rows = rows
-        buf = st.buffers[self.index]
+        buf = self._target()
         if st.stream is None:
             for lo, n, h in runs:
                 buf[lo:lo + n].copy_(host[h:h + n])
@@ -70,8 +79,14 @@ class StagingLease:
         return self
 
     def wait_ready(self) -> torch.Tensor:
+        st = self.staging
         if self.event is not None:
-            torch.cuda.current_stream(self.staging.device).wait_event(self.event)
+            torch.cuda.current_stream(st.device).wait_event(self.event)
+        if st.packed is not None and self.rows:
+            from .. import ops
+
+            ops.dequant_kv_rows(st.packed[self.index], st.buffers[self.index], count=self.rows,
+                                latent_dim=st.latent_dim)
         return self.buffer
 
     def release(self):
@@ -83,9 +98,16 @@ class StagingLease:
 
 
 class DoubleBufferStaging:
-    def __init__(self, rows: int, width: int, *, device="cuda", dtype=torch.bfloat16):
+    def __init__(self, rows: int, width: int, *, device="cuda", dtype=torch.bfloat16, fp8_records: bool = False,
+                 latent_dim: int = 512):
+        from ..ops.reference import fp8_record_bytes
+
         self.device = torch.device(device)
+        self.latent_dim = latent_dim
         self.buffers = [torch.zeros((rows, width), dtype=dtype, device=self.device) for _ in range(2)]
+        rb = fp8_record_bytes(latent_dim, width - latent_dim)
+        self.packed = ([torch.zeros((rows, rb), dtype=torch.uint8, device=self.device) for _ in range(2)]
+                       if fp8_records else None)
         self.stream = torch.cuda.Stream(device=self.device) if self.device.type == "cuda" else None
         self.consumed = [None, None]
         self._next = 0
@@ -96,4 +118,4 @@ class DoubleBufferStaging:
         return lease
 
     def nbytes(self) -> int:
-        return sum(b.numel() * b.element_size() for b in self.buffers)
+        return sum(b.numel() * b.element_size() for b in self.buffers + (self.packed or []))

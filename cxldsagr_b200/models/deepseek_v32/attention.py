@@ -95,10 +95,12 @@ class AttentionRunner:
         with scope("kv_record"):
             with scope("slots"):
                 dst = state.kv.destination_rows(T)
+            packed = state.kv.packed_rows(T)  # FP8 caches: the 656-byte records of this chunk
             with scope("finish"):
-                ops.kv_finish(kv, L, rope, w.kv_norm, cfg.norm_eps, freqs, positions, state.kv.records, dst)
+                ops.kv_finish(kv, L, rope, w.kv_norm, cfg.norm_eps, freqs, positions, state.kv.records, dst,
+                              packed=packed)
             with scope("host_write"):
-                state.kv.finish_append(dst)
+                state.kv.finish_append(dst, packed)
             state.last_rows = dst
             if state.dense is not None:
                 # The staged history plus this chunk's records (logical row = staged row).

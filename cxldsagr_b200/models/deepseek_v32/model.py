@@ -260,7 +260,8 @@ class ModelSession:
                 g, local = model.block_pool[i]
                 kv = self.pool_sessions[g].layer(local)
             else:
-                kv = SparseTokenCache(capacity, width, device=dev, candidate_slots=cc.candidate_tokens)
+                kv = SparseTokenCache(capacity, width, device=dev, candidate_slots=cc.candidate_tokens,
+                                      kv_format=cc.kv_format, latent_dim=model.cfg.kv_lora_rank)
             index = IndexerCache(capacity + cc.candidate_tokens, model.cfg.index_head_dim, device=dev)
             self.layers.append(LayerState(kv, index))
         self.length = 0
@@ -423,7 +424,8 @@ class DeepSeekV32Model:
             return
         hp = (host + 63) // 64 * 64
         self.pools = [SharedSparseTokenPool(hp, self.cfg.qk_head_dim, sum(1 for x in self.block_pool if x[0] == g), P,
-                                            device=d, candidate_slots=cc.candidate_tokens)
+                                            device=d, candidate_slots=cc.candidate_tokens, kv_format=cc.kv_format,
+                                            latent_dim=self.cfg.kv_lora_rank)
                       for g, d in enumerate(self.pool_devices)]
         self.pool = self.pools[0]
 
@@ -433,7 +435,8 @@ class DeepSeekV32Model:
             from ...cache.staging import DoubleBufferStaging
 
             self.dense_staging = DoubleBufferStaging(cc.capacity + cc.candidate_tokens, self.cfg.qk_head_dim,
-                                                     device=self.device)
+                                                     device=self.device, fp8_records=cc.kv_format == "fp8",
+                                                     latent_dim=self.cfg.kv_lora_rank)
 
     def set_cache_method(self, method: str, **overrides):
         """Switch to another cache method with an independent, empty cache.
@@ -500,7 +503,8 @@ class DeepSeekV32Model:
         """A shared sparse-token pool for this model's layers (host rows rounded to 64-token pages)."""
         host = (host_tokens + 63) // 64 * 64
         return SharedSparseTokenPool(host, self.cfg.qk_head_dim, len(self.layer_ids), pool_tokens,
-                                     device=self.device, candidate_slots=self.cache_cfg.candidate_tokens)
+                                     device=self.device, candidate_slots=self.cache_cfg.candidate_tokens,
+                                     kv_format=self.cache_cfg.kv_format, latent_dim=self.cfg.kv_lora_rank)
 
     def attach_pool(self, pool: SharedSparseTokenPool | None):
         if pool is not None and pool.num_layers != len(self.layer_ids):

@@ -351,8 +351,21 @@ def sparse_mla_decode(q, kv, ids, scale, splits: int = 16):
 
 
 # -------------------------------------------------------------- transfer
-def gather_host_records(host, records, host_ids, slots, *, device_count=None):
-    """records[slots[i]] = host[host_ids[i]] (SM gather from pinned host memory on CUDA)."""
+def gather_host_records(host, records, host_ids, slots, *, device_count=None, fp8_scratch=None, latent_dim=512):
+    """records[slots[i]] = host[host_ids[i]] (SM gather from pinned host memory on CUDA).
+
+    ``fp8_scratch`` ([>= n, 656] uint8 on the device): the host holds 656-byte
+    FP8 records; they cross PCIe into the scratch and are dequantized into
+    ``records[slots]``."""
+    if fp8_scratch is not None:
+        n = host_ids.numel()
+        if not records.is_cuda:
+            records[slots.long()] = reference.fp8_kv_unpack(host[host_ids.long()], latent_dim).to(records.dtype)
+            return records
+        if n:
+            lib().gather_rows(host, fp8_scratch, host_ids.long().contiguous(), None, n, device_count)
+            lib().dequant_kv_rows(fp8_scratch, records, slots.long().contiguous(), n, device_count)
+        return records
     if not records.is_cuda:
         records[slots.long()] = host[host_ids.long()].to(records.dtype)
         return records
@@ -396,14 +409,43 @@ def mla_q_rope(b, H, nope, rope, freqs, positions, q_proj, latent):
     lib().mla_q_rope(b, b.stride(0), T, H, nope, rope, freqs, positions, q_proj, q_proj.stride(0), q_proj.stride(1), latent)
 
 
-def kv_finish(kv, L, R, norm_w, eps, freqs, positions, records, rows):
-    """records[rows] = [rmsnorm(kv[:, :L]) || interleaved-RoPE(kv[:, L:L+R])]."""
+def kv_finish(kv, L, R, norm_w, eps, freqs, positions, records, rows, *, packed=None):
+    """records[rows] = [rmsnorm(kv[:, :L]) || interleaved-RoPE(kv[:, L:L+R])].
+
+    ``packed`` ([>= T, 656] uint8): FP8 records.  The latent is quantized per
+    128 dims (E4M3, FP32 scale amax / 448), ``packed[:T]`` receives the 656-byte
+    records and ``records[rows]`` their exact dequantized values."""
     if not _cuda(kv):
         lat = reference.rms_norm(kv[:, :L], norm_w, eps)
-        pe = reference.apply_rope(kv[:, L:L + R], _angles(freqs, positions), interleaved=True)
-        records[rows.long()] = torch.cat((lat, pe), -1).to(records.dtype)
+        pe = reference.apply_rope(kv[:, L:L + R], _angles(freqs, positions), interleaved=True).bfloat16()
+        if packed is not None:
+            q, scale, lat = reference.fp8_kv_quantize(lat.bfloat16())
+            packed[: kv.shape[0]] = reference.fp8_kv_pack(q, scale, pe)
+        records[rows.long()] = torch.cat((lat.to(records.dtype), pe.to(records.dtype)), -1)
         return
-    lib().kv_finish(kv, L, R, norm_w, eps, freqs, positions, records, rows.long())
+    lib().kv_finish(kv, L, R, norm_w, eps, freqs, positions, records, rows.long(), packed)
+
+
+def fp8_kv_records(rows: torch.Tensor, latent_dim: int = 512):
+    """(dequantized BF16 rows, packed FP8 records) of BF16 KV rows [T, L + R]: the
+    generic append path (records that did not come from kv_finish); same
+    arithmetic as kv_finish's FP8 path, in torch ops on either device."""
+    q, scale, lat = reference.fp8_kv_quantize(rows[:, :latent_dim])
+    pe = rows[:, latent_dim:].bfloat16()
+    return torch.cat((lat, pe), -1), reference.fp8_kv_pack(q, scale, pe)
+
+
+def dequant_kv_rows(packed, records, slots=None, *, count=None, device_count=None, latent_dim: int = 512):
+    """records[slots[i]] = BF16 row of the packed FP8 record packed[i] (i < count)."""
+    n = packed.shape[0] if count is None else count
+    if not _cuda(records):
+        rows = reference.fp8_kv_unpack(packed[:n], latent_dim)
+        idx = torch.arange(n) if slots is None else slots[:n].long()
+        records[idx] = rows.to(records.dtype)
+        return records
+    if n:
+        lib().dequant_kv_rows(packed, records, None if slots is None else slots.long().contiguous(), n, device_count)
+    return records
 
 
 def index_k(ik, R, ln_w, ln_b, eps, freqs, positions, k_out, s_out):

@@ -58,6 +58,57 @@ def silu_mul(gate, up):
 
 
 # ------------------------------------------------------------------ rope
+# ------------------------------------------------------------ FP8 KV records
+FP8_RECORD_BYTES = 656  # V3.2 (L = 512, R = 64): 512 E4M3 latent + 4 FP32 block scales + 64 BF16 RoPE
+
+
+def _fp8_blocks(L: int) -> int:
+    """Latent quantization blocks: 128 dims each (one block when L < 128)."""
+    if L < 128:
+        return 1
+    if L % 128:
+        raise ValueError("FP8 KV records need a latent width that is a multiple of 128 (or below 128)")
+    return L // 128
+
+
+def fp8_record_bytes(L: int, R: int) -> int:
+    return L + 4 * _fp8_blocks(L) + 2 * R
+
+
+def fp8_kv_quantize(latent: torch.Tensor):
+    """Per-block E4M3 quantization of BF16-valued latents [T, L] (128-dim blocks):
+    scale = amax / 448 (FP32), q = e4m3(x / scale); returns (q [T, L], scales
+    [T, blocks], dequantized BF16 rows bf16(float(q) * scale))."""
+    T, L = latent.shape
+    nb = _fp8_blocks(L)
+    x = latent.float().reshape(T, nb, L // nb)
+    scale = x.abs().amax(-1) / 448.0
+    safe = torch.where(scale > 0, scale, torch.ones_like(scale))
+    q = torch.where(scale[..., None] > 0, x / safe[..., None], torch.zeros_like(x)).to(torch.float8_e4m3fn)
+    deq = (q.float() * scale[..., None]).bfloat16()
+    return q.reshape(T, L), scale, deq.reshape(T, L)
+
+
+def fp8_kv_pack(q: torch.Tensor, scale: torch.Tensor, rope: torch.Tensor) -> torch.Tensor:
+    """Packed records: [L E4M3 | blocks FP32 scales | R BF16 RoPE] (656 bytes for V3.2)."""
+    T = q.shape[0]
+    return torch.cat((q.contiguous().view(torch.uint8).reshape(T, -1),
+                      scale.float().contiguous().view(torch.uint8).reshape(T, -1),
+                      rope.bfloat16().contiguous().view(torch.uint8).reshape(T, -1)), -1)
+
+
+def fp8_kv_unpack(packed: torch.Tensor, L: int = 512) -> torch.Tensor:
+    """Packed records -> BF16 rows [T, L + R] (bitwise the rows kv_finish stored)."""
+    T = packed.shape[0]
+    nb = _fp8_blocks(L)
+    p = packed.contiguous()
+    q = p[:, :L].contiguous().view(torch.float8_e4m3fn).reshape(T, nb, L // nb)
+    scale = p[:, L:L + 4 * nb].contiguous().view(torch.float32).reshape(T, nb)
+    rope = p[:, L + 4 * nb:].contiguous().view(torch.bfloat16).reshape(T, -1)
+    lat = (q.float() * scale[..., None]).bfloat16().reshape(T, L)
+    return torch.cat((lat, rope), -1)
+
+
 def embed_shard(ids: torch.Tensor, table: torch.Tensor, row0: int, vocab_total: int) -> torch.Tensor:
     """Rows of a vocabulary shard (rows [row0, row0 + len(table))); ids outside the shard give zeros."""
     ids = ids.long().reshape(-1)

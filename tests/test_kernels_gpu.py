@@ -602,3 +602,90 @@ def test_embed_vocab_shard_matches_reference():
         total += got.float().cpu()
     assert torch.equal(total.bfloat16(), table[ids])
     ops.check_errors(DEV)
+
+
+# ------------------------------------------------------- FP8 KV records
+def test_kv_finish_fp8_records_match_reference():
+    """kv_finish's FP8 path: packed 656-byte records and dequantized rows equal
+    the CPU oracle bit for bit; dequant_kv_rows reproduces the rows from the records."""
+    torch.manual_seed(30)
+    cfg = v32_config()
+    T, L, R = 70, 512, 64
+    kv = (torch.randn(T, L + R, device=DEV) * 2).bfloat16()
+    kv[5, :128] = 0  # an all-zero latent block (scale 0)
+    norm_w = torch.rand(L, device=DEV) + 0.5
+    freqs = ref.rotary_frequencies(cfg, device=DEV)
+    pos = torch.arange(100, 100 + T, device=DEV, dtype=torch.float32)
+    rows = torch.randperm(200, device=DEV)[:T]
+    recs = torch.zeros(200, L + R, dtype=torch.bfloat16, device=DEV)
+    packed = torch.zeros(T, 656, dtype=torch.uint8, device=DEV)
+    ops.kv_finish(kv, L, R, norm_w, cfg.norm_eps, freqs, pos, recs, rows, packed=packed)
+    want_recs = torch.zeros(200, L + R, dtype=torch.bfloat16)
+    want_packed = torch.zeros(T, 656, dtype=torch.uint8)
+    ops.kv_finish(kv.cpu(), L, R, norm_w.cpu(), cfg.norm_eps, freqs.cpu(), pos.cpu(), want_recs, rows.cpu(),
+                  packed=want_packed)
+    torch.cuda.synchronize()
+    assert torch.equal(packed.cpu(), want_packed)
+    assert torch.equal(recs.cpu(), want_recs)
+    out = torch.zeros(300, L + R, dtype=torch.bfloat16, device=DEV)
+    slots = torch.randperm(300, device=DEV)[:T]
+    ops.dequant_kv_rows(packed, out, slots)
+    torch.cuda.synchronize()
+    assert torch.equal(out[slots].cpu(), recs[rows].cpu())
+    ops.check_errors(DEV)
+
+
+@pytest.mark.parametrize("slots", [96, 256])
+def test_native_pool_recall_fp8_records(slots):
+    """FP8 host records: recalls through the native dispatch (gather into the
+    scratch + dequant) give the resident rows bit for bit under eviction."""
+    from cxldsagr_b200.cache.sparse_token_cache import SparseTokenCache
+
+    torch.manual_seed(31)
+    width, cap = 576, 640
+    res = SparseTokenCache(cap, width, device=DEV, kv_format="fp8")
+    off = SparseTokenCache(cap, width, device=DEV, slots=slots, kv_format="fp8")
+    assert off.native and off.record_bytes == 656
+    for step in range(8):
+        recs = (torch.randn(64, width, device=DEV) * 3).bfloat16()
+        for c in (res, off):
+            c.begin_step(64)
+            c.append(recs)
+            c.commit()
+        ids = torch.randint(-1, res.length, (8, 12), device=DEV, dtype=torch.int32)
+        a, b = res.ensure(ids), off.ensure(ids)
+        valid = ids >= 0
+        assert torch.equal(res.records[a[valid].long()], off.records[b[valid].long()])
+    ops.check_errors(DEV)
+    st = off.stats
+    assert st.recalled_records > 0 and st.host_to_device_bytes == (st.recalled_records + st.prefetched_records) * 656
+
+
+@pytest.mark.parametrize("method", ["serial_sparse", "echo", "dense_prefetch"])
+def test_model_fp8_records_offload_matches_resident(method):
+    """One V3.2 layer with FP8 KV records: every offload method (finite pool,
+    656-byte host records) gives the resident model's logits bit for bit."""
+    from cxldsagr_b200.checkpoint import StateDictSource, random_state_dict
+    from cxldsagr_b200.config import CacheConfig
+    from cxldsagr_b200.models.deepseek_v32.model import DeepSeekV32Model
+
+    cfg = v32_config(1)
+    src = StateDictSource(random_state_dict(cfg, layers=[0], seed=2, device=DEV))
+    g = torch.Generator().manual_seed(5)
+    hist = torch.randint(0, cfg.vocab_size, (3000,), generator=g).to(DEV)
+    ext = torch.randint(0, cfg.vocab_size, (16,), generator=g).to(DEV)
+    out = {}
+    for m_name in ("hbm", method):
+        # P = NH: every history row recalled after clear_residency (a smaller
+        # pool would split the selection into rounds, a different schedule).
+        kw = {} if m_name == "hbm" else {"pool_tokens": 3072 + 16, "host_tokens": 3072 + 16}
+        cache = CacheConfig(method=m_name, capacity=3072 + 16, chunk_size=1024, candidate_tokens=16, kv_format="fp8",
+                            **kw)
+        m = DeepSeekV32Model(cfg, src, device=DEV, cache=cache)
+        a = m.prefill(hist).logits.clone()
+        if m_name != "hbm":
+            m.clear_residency()
+        out[m_name] = (a, m.extend(ext).logits.clone())
+        del m
+    ops.check_errors(DEV)
+    assert torch.equal(out["hbm"][0], out[method][0]) and torch.equal(out["hbm"][1], out[method][1])

@@ -131,3 +131,47 @@ def test_mla_split_policy():
     assert ops.mla_splits(74) == 1 and ops.mla_splits(2048) == 1
     assert ops.mla_splits(1, K=512) == 2
     assert all(2048 // ops.mla_splits(T) >= 256 for T in range(1, 200))
+
+
+@pytest.mark.parametrize("method", ["serial_sparse", "echo", "dense_prefetch"])
+def test_fp8_records_resident_vs_offload_identical(tiny, method):
+    """FP8 KV records: the resident rows hold the dequantized values, the host
+    arena the packed records; recalls (or whole-history staging) reproduce the
+    resident rows bitwise, so logits match exactly."""
+    cfg, src = tiny
+    g = torch.Generator().manual_seed(2)
+    hist = torch.randint(0, cfg.vocab_size, (1024,), generator=g)
+    cand = torch.randint(0, cfg.vocab_size, (16,), generator=g)
+    ref = _model(cfg, src, "hbm", kv_format="fp8")
+    pool = 1024 + 64 if method == "dense_prefetch" else 256
+    off = _model(cfg, src, method, pool_tokens=pool, host_tokens=1024 + 64, kv_format="fp8")
+    assert torch.equal(ref.prefill(hist).logits, off.prefill(hist).logits)
+    assert torch.equal(ref.extend(cand).logits, off.extend(cand).logits)
+    if method != "dense_prefetch":
+        assert sum(c.stats.recalled_records for c in off.caches) > 0
+        host = off.pool.layers[0].host
+        assert host.dtype == torch.uint8 and host.shape[1] == off.caches[0].record_bytes
+    # FP8 records change the values (quantization), so BF16 and FP8 models differ.
+    bf16 = _model(cfg, src, "hbm")
+    ref.reset()
+    assert not torch.equal(bf16.prefill(hist).logits, ref.prefill(hist).logits)
+
+
+def test_fp8_record_pack_roundtrip():
+    from cxldsagr_b200.ops import reference as R
+
+    torch.manual_seed(0)
+    for L, Rd in ((512, 64), (64, 16)):
+        rows = (torch.randn(33, L + Rd) * 3).bfloat16()
+        rows[3, :L] = 0  # an all-zero latent block keeps scale 0
+        q, s, deq = R.fp8_kv_quantize(rows[:, :L])
+        packed = R.fp8_kv_pack(q, s, rows[:, L:])
+        assert packed.shape[1] == R.fp8_record_bytes(L, Rd)
+        back = R.fp8_kv_unpack(packed, L)
+        assert torch.equal(back[:, :L], deq) and torch.equal(back[:, L:], rows[:, L:])
+        assert torch.count_nonzero(back[3, :L]) == 0
+        # within E4M3's relative precision of each block's scale
+        err = (back[:, :L].float() - rows[:, :L].float()).abs().reshape(33, -1, min(L, 128)).amax(-1)
+        amax = rows[:, :L].float().abs().reshape(33, -1, min(L, 128)).amax(-1)
+        assert bool((err <= amax * 0.07 + 1e-6).all())
+    assert R.fp8_record_bytes(512, 64) == R.FP8_RECORD_BYTES == 656
