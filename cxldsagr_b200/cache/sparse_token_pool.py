@@ -114,10 +114,9 @@ class SharedSparseTokenPool:
         host = host_capacity * host_row
         if torch.device(device).type == "cuda":
             host = pinned_allocation_bytes(host)
-        per_layer = ((slots + 1 + candidate_slots) * width * size + host_capacity * 8 + (slots + 1) * 32 + 64)
-        if kv_format == "fp8":
-            per_layer += (slots + 1) * fp8_row  # recall scratch
-        hbm = layers * per_layer
+        per_layer = ((slots + 1 + candidate_slots) * width * size + host_capacity * 8 + (slots + 1) * 32
+                     + POOL_META_WORDS * 8)
+        hbm = layers * per_layer + ((slots + 1) * fp8_row if kv_format == "fp8" else 0)  # + one recall scratch
         if torch.device(device).type == "cpu":
             return {"hbm": 0, "dram": hbm + layers * host}
         return {"hbm": hbm, "dram": layers * host}

@@ -24,7 +24,9 @@ import torch
 
 from ...cache.capacity import CacheBudgetExceeded, CacheFootprint, ResourcePlan
 from ...cache.host_allocation import pinned_allocation_bytes
+from ...cache.sparse_token_pool import POOL_META_WORDS
 from ...config import ModelConfig
+from ...ops.reference import fp8_record_bytes
 
 PAGE = 64
 CACHE_POLICY_REVISION = "b200-v1"
@@ -46,10 +48,18 @@ class ServingResourceConfig:
     host_arena_tokens: int | None = None
     extend_chunk_size: int | None = None
     device: str = "cuda"
+    kv_format: str = "bf16"
 
     @property
     def width(self) -> int:
         return self.cfg.kv_lora_rank + self.cfg.qk_rope_head_dim
+
+    @property
+    def host_row_bytes(self) -> int:
+        """Bytes of one KV record in the pinned-DRAM arena (656 for V3.2 FP8 records)."""
+        if self.kv_format == "fp8":
+            return fp8_record_bytes(self.cfg.kv_lora_rank, self.cfg.qk_rope_head_dim)
+        return self.width * 2
 
     @property
     def offload(self) -> bool:
@@ -82,11 +92,13 @@ def shared_pool_bytes(config: ServingResourceConfig, host_tokens: int, candidate
     """Bytes of the per-layer shared pool (exactly the tensors SharedSparseTokenPool allocates)."""
     L, P, w = config.num_layers, config.slots, config.width
     rows = (P + 1 + candidate) * w * 2
-    maps = host_tokens * 8 + (P + 1) * 8 * 4 + 64   # h2d + marks, d2h + priority + miss list + victims, meta
-    host = pinned_allocation_bytes(host_tokens * w * 2) if config.on_gpu else host_tokens * w * 2
+    maps = host_tokens * 8 + (P + 1) * 8 * 4 + POOL_META_WORDS * 8   # h2d + marks, d2h + priority + miss list + victims, meta
+    hb = config.host_row_bytes
+    host = pinned_allocation_bytes(host_tokens * hb) if config.on_gpu else host_tokens * hb
+    scratch = (P + 1) * hb if config.kv_format == "fp8" else 0   # one FP8 recall scratch per pool
     if config.on_gpu:
-        return CacheFootprint(L * (rows + maps), L * host)
-    return CacheFootprint(0, L * (rows + maps + host))
+        return CacheFootprint(L * (rows + maps) + scratch, L * host)
+    return CacheFootprint(0, L * (rows + maps + host) + scratch)
 
 
 def session_bytes(config: ServingResourceConfig, capacity: int, candidate: int) -> CacheFootprint:
@@ -159,7 +171,7 @@ def plan_serving_resources(config: ServingResourceConfig, budget: CacheFootprint
         if tokens < minimum or not fits(tokens):
             raise CacheBudgetExceeded("configured host arena plus one session exceeds budgets")
     else:
-        per_token = config.num_layers * config.width * 2
+        per_token = config.num_layers * config.host_row_bytes
         upper = max(minimum, (budget.dram // max(per_token, 1)) // PAGE * PAGE)
         if not fits(minimum):
             raise CacheBudgetExceeded("shared pool, workspace and one session do not fit budgets")

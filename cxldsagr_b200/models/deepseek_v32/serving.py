@@ -41,7 +41,8 @@ class DeepSeekServingBackend:
     def __init__(self, model_path=None, *, source=None, cfg: ModelConfig | None = None, scheme: str = "hbm",
                  device="cuda:0", num_layers: int = 3, chunk_size: int = 2048, extend_chunk_size: int | None = None,
                  sparse_pool_tokens: int = 32768, host_arena_tokens: int | None = None,
-                 workspace_query_tokens: int | None = None, candidate_tokens: int | None = None, scope=None):
+                 workspace_query_tokens: int | None = None, candidate_tokens: int | None = None, scope=None,
+                 kv_format: str = "bf16"):
         if scheme not in SCHEMES:
             raise ValueError(f"scheme must be one of {SCHEMES}")
         if chunk_size < 1 or (scheme != "hbm" and sparse_pool_tokens < chunk_size):
@@ -78,6 +79,7 @@ class DeepSeekServingBackend:
         self.extend_chunk_size = extend_chunk_size
         self.slots = sparse_pool_tokens
         self.host_arena_tokens = host_arena_tokens
+        self.kv_format = kv_format
         self.workspace_query_tokens = workspace_query_tokens or max(chunk_size, extend_chunk_size or 0)
         self.candidate_tokens = candidate_tokens or self.workspace_query_tokens
         self.lifecycle = ResourceLifecycle("DeepSeek", drain=self.synchronize)
@@ -86,7 +88,7 @@ class DeepSeekServingBackend:
         self.parameter_counts = replay_parameter_count(source, num_layers) if num_layers >= 3 else None
         cache = CacheConfig(method=scheme, capacity=self.max_seq_len, pool_tokens=sparse_pool_tokens,
                             host_tokens=host_arena_tokens, candidate_tokens=self.candidate_tokens,
-                            chunk_size=chunk_size)
+                            chunk_size=chunk_size, kv_format=kv_format)
         self.model = DeepSeekV32Model(cfg, source, device=self.device, cache=cache, layers=layers,
                                       replay=num_layers >= 3, allocate_default_session=False,
                                       allocate_pool=False, scope=scope)
@@ -107,7 +109,7 @@ class DeepSeekServingBackend:
             scheme=self.scheme, cfg=self.cfg, num_layers=self.num_layers, max_seq_len=self.max_seq_len,
             slots=self.slots, chunk_size=self.chunk_size, workspace_query_tokens=self.workspace_query_tokens,
             host_arena_tokens=self.host_arena_tokens, extend_chunk_size=self.extend_chunk_size,
-            device=str(self.device))
+            device=str(self.device), kv_format=self.kv_format)
 
     def plan_resources(self, budget: CacheFootprint | None, limits) -> ResourcePlan:
         return planning.plan_serving_resources(self._planning_config(), budget, limits)

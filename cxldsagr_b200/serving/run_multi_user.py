@@ -54,6 +54,8 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--workspace-query-tokens", type=int)
     p.add_argument("--extend-chunk-size", type=int)
     p.add_argument("--native-token-validation", action="store_true")
+    p.add_argument("--kv-format", choices=("bf16", "fp8"), default="bf16",
+                   help="KV records: bf16 (1152 bytes) or fp8 (656-byte records in DRAM, dequantized rows in HBM)")
     p.add_argument("--device", default="cuda:0")
     return p
 
@@ -123,7 +125,7 @@ def build_backend(args):
     common = dict(scheme=args.scheme, device=device, num_layers=args.num_layers, chunk_size=args.chunk_size,
                   sparse_pool_tokens=args.sparse_pool_tokens, host_arena_tokens=args.host_arena_tokens,
                   workspace_query_tokens=args.workspace_query_tokens, extend_chunk_size=args.extend_chunk_size,
-                  candidate_tokens=args.candidate_tokens)
+                  candidate_tokens=args.candidate_tokens, kv_format=args.kv_format)
     if args.random_init:
         cfg = v32_config(3)
         src = StateDictSource(random_state_dict(cfg, layers=range(3), seed=args.seed, device=device), cfg)

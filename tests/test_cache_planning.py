@@ -250,3 +250,15 @@ def test_host_backing_window_and_recall():
     c.begin(2)
     c.rollback()
     assert c.length == 12
+
+
+def test_fp8_pool_estimate_matches_allocation():
+    """The FP8 pool's byte estimate (656-byte host rows + one recall scratch) equals what it allocates."""
+    from cxldsagr_b200.cache.sparse_token_pool import SharedSparseTokenPool
+
+    est = SharedSparseTokenPool.estimate_shared_bytes(1024, 576, 3, 256, device="cpu", candidate_slots=16,
+                                                      kv_format="fp8")
+    pool = SharedSparseTokenPool(1024, 576, 3, 256, device="cpu", candidate_slots=16, kv_format="fp8")
+    got = pool.shared_bytes()
+    assert pool.layers[0].host.shape == (1024, 656)
+    assert est["hbm"] + est["dram"] == got["hbm"] + got["dram"]
