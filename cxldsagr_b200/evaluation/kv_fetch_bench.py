@@ -18,6 +18,13 @@ the max time over ranks and the summed bandwidth)::
 
     python -m cxldsagr_b200.evaluation.kv_fetch_bench --context 65536 --hit 0.5
     torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m cxldsagr_b200.evaluation.kv_fetch_bench ...
+
+``--cp`` (with torchrun): one context shared by all ranks; the indexer and
+top-k are split by keys (every rank scores all queries against its key shard,
+the (score, id) lists are all-gathered and merged, ``parallel.cp_indexer``),
+and each rank then fetches and attends for its share of the queries.
+``--kv-format fp8``: 656-byte FP8 records in pinned DRAM (1,152-byte BF16
+otherwise).
 """
 
 from __future__ import annotations
@@ -30,6 +37,8 @@ import torch
 
 from .. import ops
 from ..cache.sparse_token_cache import SparseTokenCache
+from ..parallel import cp_indexer
+from ..parallel.groups import ParallelContext, shard_range
 
 WIDTH = 576
 TOPK = 2048
@@ -56,9 +65,10 @@ def pcie_h2d_gbs(dev, nbytes=256 << 20, reps=5) -> float:
 class Layer:
     """A context of N records in a pool of N slots, backed by pinned host memory."""
 
-    def __init__(self, N: int, Q: int, dev, seed: int):
+    def __init__(self, N: int, Q: int, dev, seed: int, kv_format: str = "bf16", cp=None):
         g = torch.Generator(device=dev).manual_seed(seed)
-        self.cache = SparseTokenCache(N, WIDTH, device=dev, slots=N)
+        self.cache = SparseTokenCache(N, WIDTH, device=dev, slots=N, kv_format=kv_format)
+        self.cp = cp  # ParallelContext for the context-parallel selection, or None
         for s in range(0, N, 8192):
             n = min(8192, N - s)
             self.cache.begin_step(n)
@@ -69,15 +79,23 @@ class Layer:
         self.w = torch.randn(Q, 64, device=dev, generator=g)
         self.ks = torch.rand(N, device=dev, generator=g)
         self.qa = (torch.randn(Q, 128, WIDTH, device=dev, generator=g) * 0.5).bfloat16()
-        self.logits = torch.empty(Q, N, device=dev)
         self.N, self.Q = N, Q
+        self.rows = (0, Q) if cp is None else shard_range(Q, cp.world, cp.rank)
+        self.logits = torch.empty(Q, N, device=dev) if cp is None else None
         self.ids = None
 
     def select(self):
-        ops.lib().indexer_logits(self.q8, self.k8, self.w, self.ks, self.logits, self.N - self.Q)
+        if self.cp is None:
+            ops.lib().indexer_logits(self.q8, self.k8, self.w, self.ks, self.logits, self.N - self.Q)
 
     def topk(self):
-        _, self.ids = ops.exact_topk(self.logits, TOPK, causal_start=self.N - self.Q, n=self.N)
+        if self.cp is None:
+            _, self.ids = ops.exact_topk(self.logits, TOPK, causal_start=self.N - self.Q, n=self.N)
+            return
+        k0, k1 = cp_indexer.key_shard(self.N, self.cp.world, self.cp.rank)
+        _, ids = cp_indexer.cp_exact_topk(self.cp, self.q8, self.k8[k0:k1], self.w, self.ks[k0:k1], k0,
+                                          self.N - self.Q, TOPK)
+        self.ids = ids[self.rows[0]:self.rows[1]].contiguous()
 
     def set_residency(self, hit: float, gen: torch.Generator):
         """Drop every HBM copy, then make a random ``hit`` fraction of the selected rows resident."""
@@ -94,14 +112,14 @@ class Layer:
         return self.cache.ensure(self.ids)
 
     def mla(self, phys):
-        return ops.sparse_mla(self.qa, self.cache.records, phys, 0.0723)
+        return ops.sparse_mla(self.qa[self.rows[0]:self.rows[1]], self.cache.records, phys, 0.0723)
 
     def recalled(self) -> int:
         return int(self.cache.stats.recalled_records)
 
 
-def run(N: int, Q: int, hit: float, reps: int, dev) -> dict:
-    a, b = Layer(N, Q, dev, 1), Layer(N, Q, dev, 2)
+def run(N: int, Q: int, hit: float, reps: int, dev, kv_format: str = "bf16", cp=None) -> dict:
+    a, b = Layer(N, Q, dev, 1, kv_format, cp), Layer(N, Q, dev, 2, kv_format, cp)
     for L in (a, b):
         L.select()
         L.topk()
@@ -153,7 +171,7 @@ def run(N: int, Q: int, hit: float, reps: int, dev) -> dict:
     med = {k: sorted(v)[len(v) // 2] for k, v in phases.items()}
     uniq, recalled, _ = rows[len(rows) // 2]
     return {"ms": med, "selected_unique_rows": uniq, "recalled_rows": recalled,
-            "fetch_bytes": recalled * WIDTH * 2}
+            "fetch_bytes": recalled * a.cache.record_bytes, "record_bytes": a.cache.record_bytes}
 
 
 def main(argv=None):
@@ -162,6 +180,8 @@ def main(argv=None):
     p.add_argument("--queries", type=int, default=128)
     p.add_argument("--hit", type=float, default=0.0)
     p.add_argument("--reps", type=int, default=5)
+    p.add_argument("--kv-format", choices=("bf16", "fp8"), default="bf16")
+    p.add_argument("--cp", action="store_true", help="one shared context, indexer split by keys across ranks")
     a = p.parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -171,22 +191,29 @@ def main(argv=None):
         import torch.distributed as dist
 
         dist.init_process_group("nccl", device_id=dev)
+    cp = None
+    if a.cp:
+        import torch.distributed as dist
+
+        cp = ParallelContext(rank, world, dist.group.WORLD if world > 1 else None, dev)
     pcie = pcie_h2d_gbs(dev)
-    r = run(a.context, a.queries, a.hit, a.reps, dev)
+    r = run(a.context, a.queries, a.hit, a.reps, dev, a.kv_format, cp)
     fetch_gbs = r["fetch_bytes"] / (r["ms"]["fetch"] * 1e-3) / 1e9 if r["ms"]["fetch"] > 0 else 0.0
     if world > 1:
         import torch.distributed as dist
 
-        t = torch.tensor([r["ms"]["fetch"], r["ms"]["serial"], r["ms"]["overlapped"]], device=dev)
+        names = ("indexer", "topk", "fetch", "mla", "serial", "overlapped")
+        t = torch.tensor([r["ms"][k] for k in names], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         bw = torch.tensor([fetch_gbs, pcie], device=dev)
         dist.all_reduce(bw)
-        r["ms"]["fetch"], r["ms"]["serial"], r["ms"]["overlapped"] = t.tolist()
+        r["ms"] = dict(zip(names, t.tolist()))
         fetch_gbs, pcie = bw.tolist()
         dist.destroy_process_group()
     if rank == 0:
         out = {"op": "kv_fetch", "gpus": world, "context": a.context, "queries": a.queries, "topk": TOPK,
-               "hit": a.hit, "record_bytes": WIDTH * 2, **r, "fetch_gbs": fetch_gbs, "pcie_h2d_gbs": pcie,
+               "hit": a.hit, "kv_format": a.kv_format, "context_parallel_selection": a.cp,
+               **r, "fetch_gbs": fetch_gbs, "pcie_h2d_gbs": pcie,
                "fetch_frac_of_pcie": fetch_gbs / pcie if pcie else None,
                "timing": "CUDA events, median of reps after 2 warm-up steps; max over ranks"}
         print(json.dumps(out))

@@ -147,6 +147,21 @@ class AttentionRunner:
                 return torch.empty((0, cfg.dim), dtype=torch.bfloat16, device=normed.device)
             qpos = pos + r0
             keys, kscales = state.index.visible(end)
+            if comm is not None and comm.world > 1 and getattr(comm.ctx, "cp_indexer", False) and \
+                    self.method != "echo":
+                # Context-parallel selection: every rank scores all of the chunk's
+                # queries against its key shard, the (score, id) lists are merged.
+                with scope("indexer_cp"):
+                    ids = self._cp_select(comm, q_idx, weights, keys, kscales, pos, end, T, r0, r1)
+                self.last_indices = ids
+                with scope("sparse_mla"):
+                    if state.dense is not None:
+                        attn = ops.sparse_mla(q_proj, state.dense, ids, cfg.attention_scale,
+                                              value_dim=cfg.kv_lora_rank,
+                                              splits=ops.mla_splits(q_proj.shape[0], ids.shape[1]))
+                    else:
+                        attn = self._consume(cache, q_proj, ids)
+                return self._output(attn, T_loc, scope)
             rounds = self._select_rounds(T_loc, end, normed.is_cuda)
             if rounds is not None:
                 ids = self._select_in_rounds(rounds, q_idx, keys, weights, kscales, logits_buf, qpos, end, scope)
@@ -187,6 +202,24 @@ class AttentionRunner:
                 else:
                     attn = self._consume(cache, q_proj, ids)
         return self._output(attn, T_loc, scope)
+
+    def _cp_select(self, comm, q_idx, weights, keys, kscales, pos: int, end: int, T: int, r0: int, r1: int):
+        """Exact top-k of this rank's query rows [r0, r1) with the indexer split by keys.
+
+        The chunk's indexer queries and head weights are all-gathered; rank r
+        scores all T queries against keys [k0, k1) of the visible ``end`` keys
+        (``parallel.cp_indexer``), every rank's (score, id) lists are
+        all-gathered and merged.  The selection equals the single-device one,
+        ties included; ids come in descending-score order."""
+        from ...parallel import cp_indexer as cp
+
+        ctx = comm.ctx
+        H, D = q_idx.shape[1], q_idx.shape[2]
+        q_all = comm.gather_rows(q_idx.reshape(q_idx.shape[0], H * D), T).reshape(T, H, D)
+        w_all = comm.gather_rows(weights.contiguous(), T)
+        k0, k1 = cp.key_shard(end, ctx.world, ctx.rank)
+        values, ids = cp.cp_exact_topk(ctx, q_all, keys[k0:k1], w_all, kscales[k0:k1], k0, pos, self.cfg.index_topk)
+        return ids[r0:r1].contiguous()
 
     def _output(self, attn, T_loc, scope):
         with scope("attention_output"):

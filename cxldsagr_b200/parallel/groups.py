@@ -49,6 +49,7 @@ class ParallelContext:
     backend: str = "torch"          # "torch" (NCCL/gloo collectives) or "p2p" (fused peer-memory kernels)
     ep: bool = True                 # experts sharded across the group
     vocab_parallel: bool = True     # embedding table and LM head split by vocabulary rows
+    cp_indexer: bool = False        # indexer split by keys across ranks (every query scored on every rank's shard)
 
     @property
     def is_parallel(self) -> bool:

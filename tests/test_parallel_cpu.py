@@ -86,13 +86,14 @@ def _tiny_cfg():
                        topk_group=2, num_experts_per_tok=4)
 
 
-def _run_model(rank, world, T_hist, T_cand, method):
+def _run_model(rank, world, T_hist, T_cand, method, cp=False):
     from cxldsagr_b200.checkpoint import StateDictSource, random_state_dict
     from cxldsagr_b200.config import CacheConfig
     from cxldsagr_b200.models.deepseek_v32.model import DeepSeekV32Model
     from cxldsagr_b200.parallel.groups import init_distributed
 
     ctx = init_distributed(backend="gloo", timeout_s=120)
+    ctx.cp_indexer = cp
     cfg = _tiny_cfg()
     src = StateDictSource(random_state_dict(cfg, seed=0))
     cache = CacheConfig(method=method, capacity=T_hist + T_cand, chunk_size=128, candidate_tokens=T_cand,
@@ -106,10 +107,12 @@ def _run_model(rank, world, T_hist, T_cand, method):
     return a.numpy().copy(), b.logits.numpy().copy(), b.hidden.float().numpy().copy()
 
 
-@pytest.mark.parametrize("world,method", [(2, "hbm"), (4, "serial_sparse")])
-def test_sequence_expert_parallel_matches_single(world, method):
+@pytest.mark.parametrize("world,method,cp", [(2, "hbm", False), (4, "serial_sparse", False), (2, "hbm", True),
+                                            (4, "serial_sparse", True)])
+def test_sequence_expert_parallel_matches_single(world, method, cp):
+    """cp: the indexer split by keys across ranks (context-parallel selection)."""
     single = [torch.from_numpy(x) for x in _spawn(_run_model, 1, 300, 24, method)[0][1]]
-    par = _spawn(_run_model, world, 300, 24, method)
+    par = _spawn(_run_model, world, 300, 24, method, cp)
     def corr(x, y):
         return torch.corrcoef(torch.stack([x.flatten().double(), y.flatten().double()]))[0, 1].item()
 
