@@ -144,3 +144,14 @@ def test_roofline_fraction():
     assert r["bound"] == "memory" and abs(r["frac_of_roofline"] - 0.5) < 1e-9
     r = roofline(1.0, flops=4500e9, fp8=True)                 # 1 ms at nominal FP8 in 1 ms
     assert r["bound"] == "compute" and abs(r["frac_of_roofline"] - 1.0) < 1e-9
+
+
+def test_shape_matrix_table_and_reference_cells():
+    from cxldsagr_b200.evaluation import shape_matrix as sm
+
+    rows = [{"history": 16384, "extend": 128, "method": "hbm", "prefill_ms": 100.0, "extend_ms": 1.5,
+             "h200_extend_ms": sm.REFERENCE_H200[(16384, 128)]["hbm"][1], "extend_speedup_vs_h200": 1.75}]
+    text = sm.table(rows)
+    assert "| 16384 | 128 | hbm | 100.0 | 1.500 | 2.623 | 1.75x |" in text
+    assert set(sm.REFERENCE_H200[(65536, 128)]) == set(sm.METHODS)
+    assert sm._ints("4096,16384") == [4096, 16384]
