@@ -233,6 +233,7 @@ void indexer_logits(const Tensor& q, const Tensor& k, const Tensor& w, const Ten
   TORCH_CHECK(q.dim() == 3 && q.size(1) == 64 && q.size(2) == 128 && q.is_contiguous(), "indexer: q [Q,64,128]");
   TORCH_CHECK(k.dim() == 2 && k.size(1) == 128 && k.is_contiguous(), "indexer: k [N,128]");
   TORCH_CHECK(w.is_contiguous() && w.size(0) == q.size(0) && w.size(1) == 64, "indexer: w [Q,64]");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0, "indexer: w must be 16-byte aligned");
   TORCH_CHECK(kscale.numel() >= k.size(0), "indexer: kscale");
   TORCH_CHECK(logits.size(0) >= q.size(0) && logits.size(1) >= k.size(0) && logits.stride(1) == 1, "indexer: logits");
   // Rows past the last key see every key (a key shard before the queries).
@@ -645,7 +646,7 @@ void fp8_gemm_ag(const Tensor& q_local, const Tensor& s_local_t, const Tensor& w
   TORCH_CHECK(out.size(0) == world * S && out.size(1) == N && out.is_contiguous(), "ag: out shape");
   c10::cuda::CUDAGuard guard(q_local.device());
   auto p = make_p2p(rank, world, S, call, arrive_target, reuse_target, flags, g, gs, {});
-  p.grid = b200::fp8_gemm_ag_grid(int(world * S), int(N));
+  p.grid = b200::fp8_gemm_ag_grid(int(world * S), int(N), int(K));
   p.a_local = reinterpret_cast<const uint8_t*>(q_local.data_ptr());
   p.sfa_local = s_local_t.data_ptr<float>();
   b200::launch_fp8_gemm_ag(p, reinterpret_cast<const uint8_t*>(w.data_ptr()), int(w.stride(0)), w_s.data_ptr<float>(),
@@ -759,7 +760,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_gather", &moe_gather);
   m.def("moe_combine", &moe_combine);
   m.def("fp8_gemm_grouped", &fp8_gemm_grouped);
-  m.def("fp8_gemm_ag_grid", [](int64_t M, int64_t N) { return int64_t(b200::fp8_gemm_ag_grid(int(M), int(N))); });
+  m.def("fp8_gemm_ag_grid", [](int64_t M, int64_t N, int64_t K) {
+    return int64_t(b200::fp8_gemm_ag_grid(int(M), int(N), int(K)));
+  });
+  m.def("fp8_gemm_p2p_bn", [](int64_t M, int64_t N, int64_t K) {
+    return int64_t(b200::fp8_gemm_p2p_bn(int(M), int(N), int(K)));
+  });
   m.def("rs_reduce_grid", [](int64_t S, int64_t N) { return int64_t(b200::rs_reduce_grid(int(S), int(N))); });
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_free", &symm_free);

@@ -97,8 +97,13 @@ void check_p2p(const P2PArgs& p) {
 
 }  // namespace
 
-int fp8_gemm_ag_grid(int M, int N) {
-  const int tiles = ((M + BM - 1) / BM) * ((N + 127) / 128);
+// Tile width of the fused AG / RS GEMMs: the plain planner's choice without
+// split-K (256, 224 or 128 columns).
+int fp8_gemm_p2p_bn(int M, int N, int K) { return plan_fp8_gemm(M, N, K, 1).bn; }
+
+int fp8_gemm_ag_grid(int M, int N, int K) {
+  const int bn = fp8_gemm_p2p_bn(M, N, K);
+  const int tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
   return std::min(tiles, sm_count());
 }
 
@@ -112,11 +117,22 @@ void launch_fp8_gemm_ag(P2PArgs p, const uint8_t* B, int ldb, const float* sfb, 
   const int kb = K / 128;
   const uint8_t* g_local = p.g[p.rank] + size_t(p.parity) * M * K;
   const float* gs_local = p.gs[p.rank] + size_t(p.parity) * kb * M;
+  const int bn = fp8_gemm_p2p_bn(M, N, K);
   const CUtensorMap ta = make_tma_2d(g_local, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, BK, BM);
-  const CUtensorMap tb = make_tma_2d(B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, ldb, BK, 128);
-  if (p.grid != fp8_gemm_ag_grid(M, N)) throw std::invalid_argument("ag gemm: grid differs from the planned grid");
-  const size_t smem = smem_bytes<128, 6>();
-  auto kern = fp8_gemm_kernel<128, 6, kModeAG>;
+  const CUtensorMap tb = make_tma_2d(B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, ldb, BK, bn);
+  if (p.grid != fp8_gemm_ag_grid(M, N, K)) throw std::invalid_argument("ag gemm: grid differs from the planned grid");
+  size_t smem = 0;
+  decltype(&fp8_gemm_kernel<128, 6, kModeAG>) kern = nullptr;
+  if (bn == 256) {
+    smem = smem_bytes<256, 4>();
+    kern = fp8_gemm_kernel<256, 4, kModeAG>;
+  } else if (bn == 224) {
+    smem = smem_bytes<224, 4>();
+    kern = fp8_gemm_kernel<224, 4, kModeAG>;
+  } else {
+    smem = smem_bytes<128, 6>();
+    kern = fp8_gemm_kernel<128, 6, kModeAG>;
+  }
   cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)), "ag gemm smem");
   // Cooperative launch: CTAs of this grid wait for each other's pushes of the
   // local shard, so all of them must be resident at once (1 CTA per SM, grid <= SMs).
@@ -152,18 +168,30 @@ void launch_fp8_gemm_rs(P2PArgs p, const uint8_t* A, int lda, const float* sfa, 
   if (N % 8 || K % 16) throw std::invalid_argument("rs gemm: N must be a multiple of 8, K of 16");
   for (int q = 0; q < p.world; ++q)
     if (!p.rb[q]) throw std::invalid_argument("rs gemm: missing receive buffer pointer");
+  const int bn = fp8_gemm_p2p_bn(M, N, K);
   const CUtensorMap ta = make_tma_2d(A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, lda, BK, BM);
-  const CUtensorMap tb = make_tma_2d(B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, ldb, BK, 128);
-  const int tiles = ((M + BM - 1) / BM) * ((N + 127) / 128);
+  const CUtensorMap tb = make_tma_2d(B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, ldb, BK, bn);
+  const int tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
   p.grid = std::min(tiles, sm_count());
   if (p.reduce_grid != rs_reduce_grid(p.S, N)) throw std::invalid_argument("rs gemm: reduce grid differs from plan");
-  const size_t smem = smem_bytes<128, 5, kModeRS>();
-  auto kern = fp8_gemm_kernel<128, 5, kModeRS>;
+  // The RS epilogue stages a BM x (BN + 8) BF16 tile after the pipeline buffers.
+  size_t smem = 0;
+  decltype(&fp8_gemm_kernel<128, 5, kModeRS>) kern = nullptr;
+  if (bn == 256) {
+    smem = smem_bytes<256, 3, kModeRS>();
+    kern = fp8_gemm_kernel<256, 3, kModeRS>;
+  } else if (bn == 224) {
+    smem = smem_bytes<224, 3, kModeRS>();
+    kern = fp8_gemm_kernel<224, 3, kModeRS>;
+  } else {
+    smem = smem_bytes<128, 5, kModeRS>();
+    kern = fp8_gemm_kernel<128, 5, kModeRS>;
+  }
   cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)), "rs gemm smem");
   kern<<<p.grid, kThreads, smem, stream>>>(ta, tb, sfa, lda_s, sfb, nullptr, 0, nullptr, 0, M, N, K, 1, nullptr,
                                            err, p, GroupArgs{});
   cuda_check(cudaGetLastError(), "rs gemm launch");
-  rs_reduce_kernel<<<p.reduce_grid, 256, 0, stream>>>(p, N, (N + 127) / 128, residual, ldr, out, ldo, err);
+  rs_reduce_kernel<<<p.reduce_grid, 256, 0, stream>>>(p, N, (N + bn - 1) / bn, residual, ldr, out, ldo, err);
   cuda_check(cudaGetLastError(), "rs reduce launch");
 }
 

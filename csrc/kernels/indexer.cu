@@ -32,7 +32,7 @@ constexpr int BKV = 128;              // keys per tile
 constexpr int NQ = QB * kHeads;       // 256 MMA columns
 constexpr int kStages = 8;
 constexpr int kEpiWarps = 16;
-constexpr int kQPW = QB * 4 / kEpiWarps;  // queries per epilogue warp (4 warps cover a lane quadrant each)
+static_assert(QB * 4 == kEpiWarps, "one query per epilogue warp (4 warps cover a lane quadrant each)");
 constexpr int kThreads = 64 + kEpiWarps * 32;
 
 struct Smem {
@@ -41,7 +41,6 @@ struct Smem {
   uint64_t q_full[2], q_empty[2];
   uint64_t k_full[kStages], k_empty[kStages];
   uint64_t tmem_full[2], tmem_empty[2];
-  alignas(16) float w[kEpiWarps][kQPW][kHeads];  // per-warp head weights of its queries
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -165,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     const int ew = warp - 2;             // 0..kEpiWarps-1
     const int quad = warp & 3;           // TMEM lane quadrant
-    const int qgrp = ew / 4;             // which kQPW of the 4 queries
+    const int qgrp = ew / 4;             // which of the 4 queries
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     const int key_in_tile = quad * 32 + lane;
     uint32_t tcount = 0;
@@ -173,19 +172,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
       int qb, t0, t1;
       if (!sch.unit(u, qb, t0, t1)) continue;
-      // Each warp stages its own queries' head weights (private slice:
-      // only __syncwarp ordering is needed, no cross-warp barrier).
-      __syncwarp();
+      // This warp's query's 64 head weights live in registers for the whole
+      // unit (up to 16 tiles): reading them from shared memory on every tile
+      // cost 256 B per thread per tile, which bounded the epilogue at the
+      // shared-memory read bandwidth.
+      const int qidx = qb * QB + qgrp;
+      float wr[kHeads];
+      {
+        const float4* wq = reinterpret_cast<const float4*>(w + int64_t(min(qidx, sch.Q - 1)) * kHeads);
 #pragma unroll
-      for (int e = lane; e < kQPW * kHeads; e += 32) {
-        const int j = e / kHeads, h = e % kHeads;
-        const int qc = min(qb * QB + qgrp * kQPW + j, sch.Q - 1);
-        s.w[ew][j][h] = __ldg(w + int64_t(qc) * kHeads + h);
+        for (int h4 = 0; h4 < kHeads / 4; ++h4) {
+          const float4 v = __ldg(wq + h4);
+          wr[4 * h4 + 0] = v.x;
+          wr[4 * h4 + 1] = v.y;
+          wr[4 * h4 + 2] = v.z;
+          wr[4 * h4 + 3] = v.w;
+        }
       }
-      __syncwarp();
-      int qidx[kQPW];
-#pragma unroll
-      for (int j = 0; j < kQPW; ++j) qidx[j] = qb * QB + qgrp * kQPW + j;
       for (int t = t0; t < t1; ++t, ++tcount) {
         const uint32_t buf = tcount & 1, bpar = (tcount >> 1) & 1;
         const int key = t * BKV + key_in_tile;
@@ -195,41 +198,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        float out[kQPW];
+        // Two packed FP32x2 accumulators (heads h = 4i, 4i+1 and 4i+2, 4i+3);
+        // the ReLU stays scalar (there is no packed max).
+        float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
 #pragma unroll
-        for (int j = 0; j < kQPW; ++j) {
-          // Two packed FP32x2 accumulators (even / odd heads of each quad);
-          // the ReLU stays scalar (there is no packed max).
-          float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
-          const float4* wv = reinterpret_cast<const float4*>(s.w[ew][j]);
+        for (int c = 0; c < kHeads / 16; ++c) {
+          uint32_t r[16];
+          tmem_ld16(tmem + lane_addr + buf * NQ + qgrp * kHeads + c * 16, r);
+          tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tmem + lane_addr + buf * NQ + (qgrp * kQPW + j) * kHeads + c * 32, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int h4 = 0; h4 < 8; ++h4) {
-              const float4 ww = wv[c * 8 + h4];
-              fma_f32x2(a0, a1, fmaxf(__uint_as_float(r[4 * h4 + 0]), 0.f), fmaxf(__uint_as_float(r[4 * h4 + 1]), 0.f),
-                        ww.x, ww.y);
-              fma_f32x2(b0, b1, fmaxf(__uint_as_float(r[4 * h4 + 2]), 0.f), fmaxf(__uint_as_float(r[4 * h4 + 3]), 0.f),
-                        ww.z, ww.w);
-            }
+          for (int h4 = 0; h4 < 4; ++h4) {
+            const int h = c * 16 + 4 * h4;
+            fma_f32x2(a0, a1, fmaxf(__uint_as_float(r[4 * h4 + 0]), 0.f), fmaxf(__uint_as_float(r[4 * h4 + 1]), 0.f),
+                      wr[h], wr[h + 1]);
+            fma_f32x2(b0, b1, fmaxf(__uint_as_float(r[4 * h4 + 2]), 0.f), fmaxf(__uint_as_float(r[4 * h4 + 3]), 0.f),
+                      wr[h + 2], wr[h + 3]);
           }
-          out[j] = ((a0 + a1) + (b0 + b1)) * ks;
         }
+        const float out = ((a0 + a1) + (b0 + b1)) * ks;
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.tmem_empty[buf]);
-        if (key < sch.N) {
-#pragma unroll
-          for (int j = 0; j < kQPW; ++j) {
-            if (qidx[j] < sch.Q) {
-              const bool visible = key <= sch.query_start + qidx[j];
-              logits[int64_t(qidx[j]) * ldl + key] = visible ? out[j] : -INFINITY;
-            }
-          }
-        }
+        if (key < sch.N && qidx < sch.Q)
+          logits[int64_t(qidx) * ldl + key] = key <= sch.query_start + qidx ? out : -INFINITY;
       }
     }
   }

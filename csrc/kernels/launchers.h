@@ -45,7 +45,8 @@ void launch_fp8_gemm(const FP8GemmArgs& a, cudaStream_t stream);
 // AG: out[M, N] = (all-gather of every rank's [S, K] shard) . B^T; p.a_local / p.sfa_local
 //     are this rank's shard; M = world * S.
 // RS: this rank's rows [rank*S, rank*S+S) of sum over ranks of A . B^T (+ residual).
-int fp8_gemm_ag_grid(int M, int N);
+int fp8_gemm_p2p_bn(int M, int N, int K);
+int fp8_gemm_ag_grid(int M, int N, int K);
 int rs_reduce_grid(int S, int N);
 void launch_fp8_gemm_ag(P2PArgs p, const uint8_t* B, int ldb, const float* sfb, __nv_bfloat16* out, int ldo,
                         int M, int N, int K, int* err, cudaStream_t stream);

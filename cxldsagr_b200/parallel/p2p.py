@@ -159,7 +159,7 @@ class P2PComm(Comm):
         q, s_t = quantized
         N = lin.weight.shape[0]
         out = torch.empty((total, N), dtype=torch.bfloat16, device=q.device)
-        grid = self.lib().fp8_gemm_ag_grid(total, N)
+        grid = self.lib().fp8_gemm_ag_grid(total, N, q.shape[1])
         call, arrive, reuse = self.ag.next(grid, grid)
         with self._span("ag_gemm"):
             self.lib().fp8_gemm_ag(q.contiguous(), s_t.contiguous(), lin.weight, lin.scales, out, self.ctx.rank,
@@ -181,7 +181,8 @@ class P2PComm(Comm):
         N = lin.weight.shape[0]
         S = total // self.world
         r = self.ctx.rank
-        num_n = (N + 127) // 128
+        bn = self.lib().fp8_gemm_p2p_bn(total, N, q.shape[1])  # the kernel's tile width
+        num_n = (N + bn - 1) // bn
         mblocks = (r * S + S - 1) // 128 - (r * S) // 128 + 1
         rgrid = self.lib().rs_reduce_grid(S, N)
         call, arrive, reuse = self.rs.next(num_n * mblocks, rgrid)
