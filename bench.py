@@ -48,6 +48,8 @@ def parse():
     p.add_argument("--history", type=int, default=65536)
     p.add_argument("--extend", type=int, default=128)
     p.add_argument("--chunk", type=int, default=2048, help="prefill chunk tokens (the reference's default 2048)")
+    p.add_argument("--no-fused-select", action="store_true",
+                   help="indexer logits + separate exact top-k instead of the fused selection")
     p.add_argument("--select-rows", type=int, default=None,
                    help="rows per indexer + top-k round inside a chunk (0: whole chunk; default: the model's)")
     p.add_argument("--layers", type=int, default=3)
@@ -274,6 +276,9 @@ def main():
     if args.select_rows is not None:
         for block in model.blocks:
             block.attention.select_rows = args.select_rows
+    if args.no_fused_select:
+        for block in model.blocks:
+            block.attention.fused_select = False
     select_rows = model.blocks[0].attention.select_rows
     del src
     torch.cuda.empty_cache()
@@ -452,7 +457,7 @@ def main():
                 "history": H,
                 "extend": A,
                 "chunk": args.chunk,
-                "select_rows": select_rows,
+                "select_rows": select_rows, "fused_select": not args.no_fused_select,
                 "cache_method": args.method,
                 "pool_tokens": (H + A) if offload else None,
                 "extend_residency": "cold (HBM copies of the history dropped before the extend)" if offload else "resident",

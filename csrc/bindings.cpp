@@ -246,6 +246,48 @@ void indexer_logits(const Tensor& q, const Tensor& k, const Tensor& w, const Ten
   b200::launch_indexer_logits(a, stream());
 }
 
+// Fused exact selection: ids/values [Q, width] equal to topk(indexer_logits(...))
+// with the causal rule, without full logits in HBM (logits = the fallback
+// buffer, written only for rows the candidate lists cannot finish).
+void indexer_select(const Tensor& q, const Tensor& k, const Tensor& w, const Tensor& kscale, Tensor& logits,
+                    int64_t query_start, int64_t topk, Tensor& values, Tensor& ids, bool index_order,
+                    int64_t sample_stride, int64_t cand_cap) {
+  CHECK_CUDA(q); CHECK_DTYPE(q, torch::kFloat8_e4m3fn); CHECK_DTYPE(k, torch::kFloat8_e4m3fn);
+  CHECK_DTYPE(w, torch::kFloat32); CHECK_DTYPE(kscale, torch::kFloat32); CHECK_DTYPE(logits, torch::kFloat32);
+  CHECK_DTYPE(values, torch::kFloat32); CHECK_DTYPE(ids, torch::kInt32);
+  TORCH_CHECK(q.dim() == 3 && q.size(1) == 64 && q.size(2) == 128 && q.is_contiguous(), "indexer_select: q [Q,64,128]");
+  TORCH_CHECK(k.dim() == 2 && k.size(1) == 128 && k.is_contiguous(), "indexer_select: k [N,128]");
+  TORCH_CHECK(w.is_contiguous() && w.size(0) == q.size(0) && w.size(1) == 64, "indexer_select: w [Q,64]");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0, "indexer_select: w must be 16-byte aligned");
+  TORCH_CHECK(kscale.numel() >= k.size(0), "indexer_select: kscale");
+  TORCH_CHECK(logits.size(0) >= q.size(0) && logits.size(1) >= k.size(0) && logits.stride(1) == 1,
+              "indexer_select: fallback logits [>=Q, >=N]");
+  TORCH_CHECK(values.is_contiguous() && ids.is_contiguous() && values.size(0) == q.size(0) &&
+                  ids.size(0) == q.size(0) && values.size(1) == ids.size(1),
+              "indexer_select: outputs [Q, width]");
+  TORCH_CHECK(query_start >= 0, "indexer_select: query_start");
+  c10::cuda::CUDAGuard g(q.device());
+  const int64_t Q = q.size(0), N = k.size(0);
+  auto f32 = torch::dtype(torch::kFloat32).device(q.device());
+  auto i32 = torch::dtype(torch::kInt32).device(q.device());
+  const int64_t ns = (N + sample_stride - 1) / sample_stride;
+  Tensor slog = torch::empty({Q, std::max<int64_t>(4, (ns + 3) / 4 * 4)}, f32);
+  Tensor thresh = torch::empty({Q}, f32);
+  Tensor cand = torch::empty({Q, cand_cap}, torch::dtype(torch::kInt64).device(q.device()));
+  Tensor small = torch::empty({3, Q}, i32);  // counts, flags, overflow
+  b200::IndexerSelectArgs a{};
+  a.idx.q = cptr<uint8_t>(q); a.idx.k = cptr<uint8_t>(k); a.idx.w = cptr<float>(w);
+  a.idx.kscale = cptr<float>(kscale); a.idx.logits = ptr<float>(logits); a.idx.ldl = logits.stride(0);
+  a.idx.Q = int(Q); a.idx.N = int(N); a.idx.query_start = int(query_start); a.idx.n_cols = int(logits.size(1));
+  a.idx.err = err_ptr(q);
+  a.k = int(topk); a.width = int(ids.size(1)); a.sample_stride = int(sample_stride); a.cand_cap = int(cand_cap);
+  a.sample_logits = slog.data_ptr<float>(); a.ld_sample = slog.stride(0); a.thresh = thresh.data_ptr<float>();
+  a.cand = reinterpret_cast<uint64_t*>(cand.data_ptr<int64_t>());
+  a.cand_count = small[0].data_ptr<int>(); a.flags = small[1].data_ptr<int>(); a.overflow = small[2].data_ptr<int>();
+  a.values = ptr<float>(values); a.ids = ptr<int>(ids); a.index_order = index_order;
+  b200::launch_indexer_select(a, stream());
+}
+
 void topk(const Tensor& scores, int64_t N, int64_t k, int64_t causal_start, Tensor& values, Tensor& ids,
           int64_t algo) {
   CHECK_CUDA(scores); CHECK_DTYPE(scores, torch::kFloat32); CHECK_DTYPE(values, torch::kFloat32);
@@ -729,6 +771,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed", &embed, py::arg("ids"), py::arg("table"), py::arg("out"), py::arg("row0") = int64_t(0),
         py::arg("vocab_total") = int64_t(0));
   m.def("indexer_logits", &indexer_logits);
+  m.def("indexer_select", &indexer_select, py::arg("q"), py::arg("k"), py::arg("w"), py::arg("kscale"),
+        py::arg("logits"), py::arg("query_start"), py::arg("topk"), py::arg("values"), py::arg("ids"),
+        py::arg("index_order") = true, py::arg("sample_stride") = 16, py::arg("cand_cap") = 8192);
   m.def("topk", &topk);
   m.def("sparse_mla", &sparse_mla);
   m.def("sparse_mla_scratch_bytes", &sparse_mla_scratch_bytes);

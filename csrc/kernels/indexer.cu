@@ -20,6 +20,7 @@
 // Work unit = (query block of 4, chunk of key tiles); persistent CTAs walk the
 // units chunk-major so concurrently running CTAs share K tiles through L2.
 #include "../common/ptx.cuh"
+#include "../common/select.cuh"
 #include "launchers.h"
 
 namespace b200 {
@@ -47,13 +48,25 @@ struct Smem {
 
 struct Schedule {
   int Q, N, query_start, num_qb, num_tiles_total, chunk_tiles, num_chunks;
+  int stride;                // key j of this launch is key j * stride of the cache (sampling pass)
+  const int* row_flags;      // when set, only query blocks with a flagged row run
   __device__ __forceinline__ int units() const { return num_qb * num_chunks; }
-  // Returns false when the unit lies entirely past the query block's causal end.
+  // Returns false when the unit lies entirely past the query block's causal
+  // end, or (with row_flags) when none of the block's rows is flagged.
   __device__ __forceinline__ bool unit(int u, int& qb, int& t0, int& t1) const {
     qb = u % num_qb;
     const int chunk = u / num_qb;
+    if (row_flags != nullptr) {
+      bool any = false;
+#pragma unroll
+      for (int i = 0; i < QB; ++i) {
+        const int q = qb * QB + i;
+        any |= q < Q && row_flags[q] != 0;
+      }
+      if (!any) return false;
+    }
     const int q_last = min(Q - 1, qb * QB + QB - 1);
-    const int end = min(N, query_start + q_last + 1);  // exclusive visible end of the block
+    const int end = min(N, (query_start + q_last) / stride + 1);  // exclusive visible end of the block
     const int tiles = (end + BKV - 1) / BKV;
     t0 = chunk * chunk_tiles;
     t1 = min(tiles, t0 + chunk_tiles);
@@ -61,11 +74,24 @@ struct Schedule {
   }
 };
 
+// Output of one launch: FP32 logits rows (ldl pitch), or, in selection mode,
+// every visible logit >= thresh[q] appended to row q's candidate list as a
+// selection composite (cand_count[q] counts them; entries past cand_cap are
+// counted but not stored).
+struct IndexerOut {
+  float* logits;
+  int64_t ldl;
+  bool select;
+  const float* thresh;       // nullable in selection mode: every visible logit is a candidate
+  uint64_t* cand;            // [Q, cand_cap]
+  int* cand_count;           // [Q], zeroed before the launch
+  int cand_cap;
+};
+
 __global__ void __launch_bounds__(kThreads, 1)
     indexer_kernel(const __grid_constant__ CUtensorMap tma_q,
                    const __grid_constant__ CUtensorMap tma_k, const float* __restrict__ w,
-                   const float* __restrict__ kscale, float* __restrict__ logits, int64_t ldl,
-                   Schedule sch, int* err) {
+                   const float* __restrict__ kscale, IndexerOut o, Schedule sch, int* err) {
   extern __shared__ uint8_t smem_raw[];
   auto& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x / 32;
@@ -189,10 +215,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           wr[4 * h4 + 3] = v.w;
         }
       }
+      const float thresh = (o.select && o.thresh != nullptr) ? __ldg(o.thresh + min(qidx, sch.Q - 1)) : -INFINITY;
+      const int last_key = sch.query_start + qidx;  // causal: cache key index <= last_key is visible
       for (int t = t0; t < t1; ++t, ++tcount) {
         const uint32_t buf = tcount & 1, bpar = (tcount >> 1) & 1;
         const int key = t * BKV + key_in_tile;
-        const float ks = key < sch.N ? __ldg(kscale + key) : 0.f;
+        const int cache_key = key * sch.stride;
+        const float ks = key < sch.N ? __ldg(kscale + cache_key) : 0.f;
         if (!mbar_wait(&s.tmem_full[buf], bpar, err, kErrTimeoutTmemFull, abort_flag)) {
           ok = false;
           break;
@@ -219,8 +248,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.tmem_empty[buf]);
-        if (key < sch.N && qidx < sch.Q)
-          logits[int64_t(qidx) * ldl + key] = key <= sch.query_start + qidx ? out : -INFINITY;
+        const bool valid = key < sch.N && qidx < sch.Q;
+        if (!o.select) {
+          if (valid) o.logits[int64_t(qidx) * o.ldl + key] = cache_key <= last_key ? out : -INFINITY;
+        } else {
+          // All 32 lanes hold the same query: one counter update per warp.
+          const bool take = valid && cache_key <= last_key && out >= thresh;
+          const uint32_t m = __ballot_sync(0xffffffffu, take);
+          if (m != 0u) {
+            uint32_t base = 0;
+            if (lane == 0) base = atomicAdd(reinterpret_cast<unsigned int*>(o.cand_count + qidx), uint32_t(__popc(m)));
+            base = __shfl_sync(0xffffffffu, base, 0);
+            const uint32_t pos = base + uint32_t(__popc(m & ((1u << lane) - 1u)));
+            if (take && pos < uint32_t(o.cand_cap))
+              o.cand[int64_t(qidx) * o.cand_cap + pos] = select_composite(out, key);
+          }
+        }
       }
     }
   }
@@ -237,15 +280,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 void launch_indexer_logits(const IndexerArgs& a, cudaStream_t stream) {
   if (a.Q <= 0 || a.N <= 0) return;
+  const int stride = std::max(1, a.key_stride);
+  if (a.select && stride != 1) throw std::invalid_argument("indexer: selection mode reads every key");
+  const int n = (a.N + stride - 1) / stride;  // keys this launch reads
   const CUtensorMap tq = make_tma_2d(a.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, int64_t(a.Q) * kHeads,
                                      kDim, kDim, kDim, NQ);
-  const CUtensorMap tk = make_tma_2d(a.k, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.N, kDim, kDim, kDim, BKV);
+  const CUtensorMap tk = make_tma_2d(a.k, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, n, kDim, int64_t(kDim) * stride, kDim,
+                                     BKV);
   Schedule sch;
   sch.Q = a.Q;
-  sch.N = a.N;
+  sch.N = n;
   sch.query_start = a.query_start;
+  sch.stride = stride;
+  sch.row_flags = a.row_flags;
   sch.num_qb = (a.Q + QB - 1) / QB;
-  const int end = std::min(a.N, a.query_start + a.Q);
+  const int end = std::min(n, (a.query_start + a.Q - 1) / stride + 1);
   sch.num_tiles_total = (end + BKV - 1) / BKV;
   // Enough units to fill every SM about twice, at most 16 tiles per unit.
   const int sms = sm_count();
@@ -255,10 +304,18 @@ void launch_indexer_logits(const IndexerArgs& a, cudaStream_t stream) {
   sch.num_chunks = (sch.num_tiles_total + chunk - 1) / chunk;
   const int units = sch.num_qb * sch.num_chunks;
   const int grid = std::min(units, sms);
+  IndexerOut o{};
+  o.logits = a.logits;
+  o.ldl = a.ldl;
+  o.select = a.select;
+  o.thresh = a.thresh;
+  o.cand = a.cand;
+  o.cand_count = a.cand_count;
+  o.cand_cap = a.cand_cap;
   const size_t smem = sizeof(Smem) + 1024;
   cuda_check(cudaFuncSetAttribute(indexer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
              "indexer smem attribute");
-  indexer_kernel<<<grid, kThreads, smem, stream>>>(tq, tk, a.w, a.kscale, a.logits, a.ldl, sch, a.err);
+  indexer_kernel<<<grid, kThreads, smem, stream>>>(tq, tk, a.w, a.kscale, o, sch, a.err);
   cuda_check(cudaGetLastError(), "indexer launch");
 }
 

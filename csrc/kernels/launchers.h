@@ -209,8 +209,39 @@ struct IndexerArgs {
   int64_t ldl;
   int Q, N, query_start, n_cols;
   int* err;
+  // Sampling pass: read cache keys 0, s, 2s, ... (logits column j = key j*s).
+  int key_stride = 1;
+  // Only query blocks holding a flagged row run (fallback rows of a selection).
+  const int* row_flags = nullptr;
+  // Selection mode: instead of logits, append every visible logit >= thresh[q]
+  // (all visible ones when thresh is null) as a composite to row q's list.
+  bool select = false;
+  const float* thresh = nullptr;
+  uint64_t* cand = nullptr;
+  int* cand_count = nullptr;
+  int cand_cap = 0;
 };
 void launch_indexer_logits(const IndexerArgs& a, cudaStream_t stream);
+
+// Fused exact selection (indexer + top-k without full logits in HBM).
+struct IndexerSelectArgs {
+  IndexerArgs idx;       // q, k, w, kscale, Q, N, query_start, err; logits = the fallback buffer
+  int k;                 // top-k (<= 2048)
+  int width;             // output row width (>= min(k, visible keys))
+  int sample_stride;     // threshold sampling stride (e.g. 16)
+  int cand_cap;          // candidate capacity per row
+  float* sample_logits;  // [Q, ceil(N / sample_stride)] scratch
+  int64_t ld_sample;
+  float* thresh;         // [Q]
+  uint64_t* cand;        // [Q, cand_cap]
+  int* cand_count;       // [Q]
+  int* flags;            // [Q]: rows the candidate list could not finish
+  int* overflow;         // [Q]: rows the two-pass top-k sends to the multi-pass kernel
+  float* values;         // [Q, width]
+  int* ids;              // [Q, width]
+  bool index_order;
+};
+void launch_indexer_select(const IndexerSelectArgs& a, cudaStream_t stream);
 
 // -------------------------------------------------------------- top-k
 // Exact descending top-k per row of FP32 scores [R, N] (row pitch ld), ties to
@@ -222,7 +253,7 @@ void launch_topk(const float* scores, int64_t ld, int R, int N, int k, float* va
 // first and only rows it flags are redone by the multi-pass kernel.
 void launch_topk_causal(const float* scores, int64_t ld, int R, int N, int k, int causal_start,
                         float* values, int* ids, int* err, cudaStream_t stream, int* overflow = nullptr,
-                        bool index_order = false);
+                        bool index_order = false, const int* only_rows = nullptr);
 
 // --------------------------------------------------------------- sparse MLA
 struct MLAArgs {

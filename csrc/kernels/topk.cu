@@ -14,6 +14,7 @@
 // first keys == T; a bitonic sort of (key, ~index) in shared memory orders the
 // result.  No scratch memory outside shared memory is used.
 #include "../common/ptx.cuh"
+#include "../common/select.cuh"
 #include "launchers.h"
 
 namespace b200 {
@@ -30,16 +31,6 @@ constexpr int kSecCap = 6144;     // threshold-bin candidates staged in shared m
 __device__ int g_topk_trace_row = -1;
 __device__ unsigned long long g_topk_trace[16];
 
-__device__ __forceinline__ uint32_t order_key(float f) {
-  const uint32_t u = __float_as_uint(f);
-  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0u;  // NaN sorts below everything
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
-__device__ __forceinline__ float key_value(uint32_t k) {
-  const uint32_t u = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
-  return __uint_as_float(u);
-}
 
 __global__ void __launch_bounds__(kThreads) topk_kernel(const float* __restrict__ scores, int64_t ld,
                                                         int N, int k, int causal_start,
@@ -209,7 +200,10 @@ __global__ void __launch_bounds__(kThreads) topk_kernel(const float* __restrict_
 __global__ void __launch_bounds__(kThreads2) topk2_kernel(const float* __restrict__ scores, int64_t ld, int N,
                                                           int k, int causal_start, float* __restrict__ values,
                                                           int* __restrict__ ids, int* __restrict__ overflow,
-                                                          int* err, bool index_order) {
+                                                          int* err, bool index_order,
+                                                          const int* __restrict__ only_rows) {
+  // With only_rows set, rows not flagged there are left as they are.
+  if (only_rows && !only_rows[blockIdx.x]) return;
   extern __shared__ uint8_t dyn[];
   uint32_t* hist = reinterpret_cast<uint32_t*>(dyn);                      // kBins
   uint64_t* cand = reinterpret_cast<uint64_t*>(dyn + kBins * 4);          // kMaxK
@@ -601,7 +595,8 @@ void launch_topk(const float* scores, int64_t ld, int R, int N, int k, float* va
 }
 
 void launch_topk_causal(const float* scores, int64_t ld, int R, int N, int k, int causal_start,
-                        float* values, int* ids, int* err, cudaStream_t stream, int* overflow, bool index_order) {
+                        float* values, int* ids, int* err, cudaStream_t stream, int* overflow, bool index_order,
+                        const int* only_rows) {
   if (R <= 0) return;
   if (k < 1 || k > kMaxK) throw std::invalid_argument("topk: k must be in [1, 2048]");
   if (overflow == nullptr) {
@@ -613,7 +608,7 @@ void launch_topk_causal(const float* scores, int64_t ld, int R, int N, int k, in
   cuda_check(cudaFuncSetAttribute(topk2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
              "topk2 smem attribute");
   topk2_kernel<<<R, kThreads2, smem, stream>>>(scores, ld, N, k, causal_start, values, ids, overflow, err,
-                                                index_order);
+                                                index_order, only_rows);
   cuda_check(cudaGetLastError(), "topk2 launch");
   topk_kernel<<<R, kThreads, 0, stream>>>(scores, ld, N, k, causal_start, values, ids, err, overflow);
   cuda_check(cudaGetLastError(), "topk fallback launch");

@@ -1,0 +1,286 @@
+// Fused exact indexer selection: the top-k of every query's indexer logits
+// without writing the full FP32 logits to HBM.
+//
+//   1. Sampling pass: the indexer scores every 16th cache key (a strided
+//      tensor map over the same key rows), [Q, N/16] FP32.
+//   2. Threshold: per query, the sampled value of rank ceil(2k * ns / n_vis)
+//      (ns sampled and n_vis visible keys), expected to leave ~2k keys of the
+//      full row at or above it.  Rows with n_vis <= cap take every key.
+//   3. Selection pass: the indexer scores every visible key and appends the
+//      ones >= the threshold to the row's candidate list as (value, index)
+//      composites; nothing else leaves the SM.
+//   4. Candidate top-k: per row, the exact rank-k composite among the
+//      candidates by 12-bit radix levels, then the selection sorted by index
+//      (or by value).  Exact whenever count >= min(k, n_vis) and count <= cap:
+//      every key below the threshold is below every candidate, so the top-k of
+//      the row lies inside the list.
+//   5. Fallback, for rows where 4 did not hold (a threshold estimate off by a
+//      factor of two, e.g. a row of equal values): the indexer writes those
+//      rows' full logits and the two-pass / multi-pass top-k redoes them.
+//      Both launches are always made and return at once when no row is
+//      flagged, so the sequence needs no host synchronisation (CUDA graphs).
+//
+// The result equals exact_topk over the full logits row, ties included
+// (larger value first, then smaller index; -1 ids for non-finite values and
+// padding).  Reference behaviour: the fused ECHO indexer and exact top-k,
+// operators/deepseek_v32/indexer/csrc/echo_logits.cuh:48-590 and
+// operators/deepseek_v32/indexer/selection.py:62-113.
+#include "../common/ptx.cuh"
+#include "../common/select.cuh"
+#include "launchers.h"
+
+namespace b200 {
+namespace {
+
+constexpr int kThrThreads = 256;
+constexpr int kCandThreads = 512;
+constexpr int kMaxK = 2048;
+constexpr int kLevelBits = 12;
+
+// Block-wide search over hist[0, nbins) (bins ascending in value): the bin
+// holding the element of rank `rank` counted from the top (1-based).  Writes
+// the bin, the count strictly above it and the count inside it.  Every thread
+// owns BPT consecutive bins.
+template <int THREADS, int BPT>
+__device__ void find_rank_bin(const uint32_t* hist, int nbins, uint32_t rank, uint32_t* warp_sum, uint32_t& bin,
+                              uint32_t& above, uint32_t& in, uint32_t* s_out) {
+  const int tid = threadIdx.x, lane = tid % 32, wid = tid / 32;
+  uint32_t local[BPT], lsum = 0;
+#pragma unroll
+  for (int j = 0; j < BPT; ++j) {
+    const int b = BPT * tid + j;
+    local[j] = b < nbins ? hist[b] : 0u;
+    lsum += local[j];
+  }
+  // Inclusive suffix sum of lsum within the warp (higher lanes own higher bins).
+  uint32_t v = lsum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t n = __shfl_down_sync(0xffffffffu, v, o);
+    if (lane + o < 32) v += n;
+  }
+  if (lane == 0) warp_sum[wid] = v;
+  __syncthreads();
+  uint32_t acc = v - lsum;  // bins of higher lanes in this warp
+  for (int w = wid + 1; w < THREADS / 32; ++w) acc += warp_sum[w];
+#pragma unroll
+  for (int j = BPT - 1; j >= 0; --j) {
+    if (acc < rank && acc + local[j] >= rank) {
+      s_out[0] = uint32_t(BPT * tid + j);
+      s_out[1] = acc;
+      s_out[2] = local[j];
+    }
+    acc += local[j];
+  }
+  __syncthreads();
+  bin = s_out[0];
+  above = s_out[1];
+  in = s_out[2];
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kThrThreads) select_threshold_kernel(const float* __restrict__ slog, int64_t lds,
+                                                                      int N, int Ns, int stride, int query_start,
+                                                                      int k, int cap, float* __restrict__ thresh) {
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t warp_sum[kThrThreads / 32];
+  __shared__ uint32_t s_out[3];
+  const int q = blockIdx.x, tid = threadIdx.x;
+  const int n_vis = min(N, query_start + q + 1);
+  if (n_vis <= cap) {
+    if (tid == 0) thresh[q] = -INFINITY;
+    return;
+  }
+  const int ns = min(Ns, (query_start + q) / stride + 1);
+  int r = int((int64_t(2) * k * ns + n_vis - 1) / n_vis);
+  r = max(1, min(r, ns));
+  const float* row = slog + int64_t(q) * lds;
+  uint32_t prefix = 0, rem = uint32_t(r);
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    hist[tid] = 0u;
+    __syncthreads();
+    for (int j = tid; j < ns; j += kThrThreads) {
+      const uint32_t key = order_key(row[j]);
+      if (pass == 0 || (key >> (shift + 8)) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    uint32_t bin, above, in;
+    find_rank_bin<kThrThreads, 1>(hist, 256, rem, warp_sum, bin, above, in, s_out);
+    prefix = (prefix << 8) | bin;
+    rem -= above;
+  }
+  if (tid == 0) thresh[q] = key_value(prefix);
+}
+
+__global__ void __launch_bounds__(kCandThreads) topk_candidates_kernel(
+    const uint64_t* __restrict__ cand, const int* __restrict__ cand_count, int cap, int N, int query_start, int k,
+    int width, float* __restrict__ values, int* __restrict__ ids, int* __restrict__ flags, int* __restrict__ overflow,
+    bool index_order) {
+  extern __shared__ uint8_t dyn[];
+  uint64_t* buf = reinterpret_cast<uint64_t*>(dyn);             // cap candidates
+  uint32_t* hist = reinterpret_cast<uint32_t*>(buf + cap);      // 4096 bins, later the selection
+  uint64_t* sel = reinterpret_cast<uint64_t*>(hist);            // kMaxK
+  __shared__ uint32_t warp_sum[kCandThreads / 32];
+  __shared__ uint32_t s_out[3];
+  __shared__ uint32_t s_cnt;
+  const int q = blockIdx.x, tid = threadIdx.x, lane = tid % 32;
+  const int n_vis = min(N, query_start + q + 1);
+  const int take = min(k, n_vis);
+  const int c = cand_count[q];
+  const bool bad = c > cap || c < take;
+  if (tid == 0) {
+    overflow[q] = 0;
+    flags[q] = bad ? 1 : 0;
+    s_cnt = 0u;
+  }
+  if (bad) return;
+  const uint64_t* src = cand + int64_t(q) * cap;
+  for (int i = tid; i < c; i += kCandThreads) buf[i] = src[i];
+  __syncthreads();
+
+  // Exact rank-`take` composite: 12-bit levels from the top until its bin
+  // holds one composite (composites are distinct).
+  uint64_t want = 0;
+  int cbits = 0;
+  if (take < c) {
+    uint32_t crank = uint32_t(take);
+    while (cbits < 64) {
+      const int lb = min(kLevelBits, 64 - cbits);
+      const int shift = 64 - cbits - lb;
+      for (int i = tid; i < (1 << lb); i += kCandThreads) hist[i] = 0u;
+      __syncthreads();
+      for (int i = tid; i < c; i += kCandThreads) {
+        const uint64_t x = buf[i];
+        if (cbits == 0 || (x >> (64 - cbits)) == want)
+          atomicAdd(&hist[uint32_t(x >> shift) & ((1u << lb) - 1u)], 1u);
+      }
+      __syncthreads();
+      uint32_t bin, above, in;
+      find_rank_bin<kCandThreads, (1 << kLevelBits) / kCandThreads>(hist, 1 << lb, crank, warp_sum, bin, above, in,
+                                                                    s_out);
+      want = (want << lb) | bin;
+      cbits += lb;
+      crank -= above;
+      if (in == 1u) break;
+    }
+  }
+  __syncthreads();
+  // Compact the selection (exactly `take` composites) into sel[], keyed for
+  // an ascending sort: (index, value key) for index order, ~composite for
+  // value order.
+  for (int i0 = 0; i0 < c; i0 += kCandThreads) {
+    const int i = i0 + tid;
+    bool s = false;
+    uint64_t x = 0;
+    if (i < c) {
+      x = buf[i];
+      s = cbits == 0 || (x >> (64 - cbits)) >= want;
+    }
+    const uint32_t m = __ballot_sync(0xffffffffu, s);
+    uint32_t base = 0;
+    if (lane == 0 && m) base = atomicAdd(&s_cnt, uint32_t(__popc(m)));
+    base = __shfl_sync(0xffffffffu, base, 0);
+    const uint32_t pos = base + uint32_t(__popc(m & ((1u << lane) - 1u)));
+    if (s && pos < uint32_t(kMaxK))
+      sel[pos] = index_order ? (uint64_t(uint32_t(composite_index(x))) << 32) | uint32_t(x >> 32) : ~x;
+  }
+  __syncthreads();
+  const int count = min(int(s_cnt), kMaxK);
+  // Bitonic sort, ascending, of n2 = 2^ceil(log2 count) keys (padding ~0 last).
+  int n2 = 1;
+  while (n2 < count) n2 <<= 1;
+  for (int i = count + tid; i < n2; i += kCandThreads) sel[i] = ~0ull;
+  __syncthreads();
+  for (int size = 2; size <= n2; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = tid; i < n2 / 2; i += kCandThreads) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool asc = (lo & size) == 0;
+        const uint64_t a = sel[lo], b = sel[hi];
+        if ((a > b) == asc) {
+          sel[lo] = b;
+          sel[hi] = a;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  float* vout = values + int64_t(q) * width;
+  int* iout = ids + int64_t(q) * width;
+  for (int i = tid; i < width; i += kCandThreads) {
+    if (i < count) {
+      const uint64_t x = sel[i];
+      float v;
+      int idx;
+      if (index_order) {
+        idx = int(x >> 32);
+        v = key_value(uint32_t(x));
+      } else {
+        v = composite_value(~x);
+        idx = composite_index(~x);
+      }
+      vout[i] = v;
+      iout[i] = (__float_as_uint(v) & 0x7FFFFFFFu) >= 0x7F800000u ? -1 : idx;
+    } else {
+      vout[i] = -INFINITY;
+      iout[i] = -1;
+    }
+  }
+}
+
+}  // namespace
+
+size_t indexer_select_cand_smem(int cap) { return size_t(cap) * 8 + size_t(1 << kLevelBits) * 4; }
+
+void launch_indexer_select(const IndexerSelectArgs& a, cudaStream_t stream) {
+  const IndexerArgs& x = a.idx;
+  if (x.Q <= 0 || x.N <= 0) return;
+  if (a.k < 1 || a.k > kMaxK) throw std::invalid_argument("indexer select: k must be in [1, 2048]");
+  if (a.cand_cap < 2 * a.k) throw std::invalid_argument("indexer select: candidate capacity must be >= 2k");
+  if (a.sample_stride < 2) throw std::invalid_argument("indexer select: sample stride must be >= 2");
+  const int n_end = std::min(x.N, x.query_start + x.Q);  // keys visible to the last row
+  if (a.width < std::min(a.k, n_end)) throw std::invalid_argument("indexer select: output width < min(k, keys)");
+  const bool sample = n_end > a.cand_cap;
+  if (sample) {
+    IndexerArgs s = x;
+    s.logits = a.sample_logits;
+    s.ldl = a.ld_sample;
+    s.key_stride = a.sample_stride;
+    s.select = false;
+    s.row_flags = nullptr;
+    launch_indexer_logits(s, stream);
+    const int ns = (x.N + a.sample_stride - 1) / a.sample_stride;
+    select_threshold_kernel<<<x.Q, kThrThreads, 0, stream>>>(a.sample_logits, a.ld_sample, x.N, ns, a.sample_stride,
+                                                              x.query_start, a.k, a.cand_cap, a.thresh);
+    cuda_check(cudaGetLastError(), "indexer select threshold launch");
+  }
+  cuda_check(cudaMemsetAsync(a.cand_count, 0, size_t(x.Q) * sizeof(int), stream), "indexer select count reset");
+  IndexerArgs m = x;
+  m.key_stride = 1;
+  m.row_flags = nullptr;
+  m.select = true;
+  m.thresh = sample ? a.thresh : nullptr;
+  m.cand = a.cand;
+  m.cand_count = a.cand_count;
+  m.cand_cap = a.cand_cap;
+  launch_indexer_logits(m, stream);
+  const size_t smem = indexer_select_cand_smem(a.cand_cap);
+  cuda_check(cudaFuncSetAttribute(topk_candidates_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+             "indexer select candidates smem");
+  topk_candidates_kernel<<<x.Q, kCandThreads, smem, stream>>>(a.cand, a.cand_count, a.cand_cap, x.N, x.query_start,
+                                                              a.k, a.width, a.values, a.ids, a.flags, a.overflow,
+                                                              a.index_order);
+  cuda_check(cudaGetLastError(), "indexer select candidates launch");
+  // Fallback for flagged rows (no work when none is flagged).
+  IndexerArgs f = x;
+  f.key_stride = 1;
+  f.select = false;
+  f.row_flags = a.flags;
+  launch_indexer_logits(f, stream);
+  launch_topk_causal(x.logits, x.ldl, x.Q, n_end, a.width, x.query_start, a.values, a.ids, x.err, stream, a.overflow,
+                     a.index_order, a.flags);
+}
+
+}  // namespace b200

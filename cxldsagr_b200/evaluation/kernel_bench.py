@@ -154,6 +154,33 @@ def bench_indexer(Q=1024, N=65536, **_):
             **roofline(ms, flops=flops, nbytes=N * 132 + Q * 64 * 132 + visible * 4, fp8=True)}
 
 
+def bench_indexer_select(Q=1024, N=65536, k=2048, **_):
+    """Fused selection (ops.indexer_select) against indexer logits + exact top-k
+    (index order), the same causal rows; the outputs are checked equal."""
+    dev = "cuda"
+    q = (torch.randn(Q, 64, 128, device=dev) * 2).to(torch.float8_e4m3fn)
+    kk = (torch.randn(N, 128, device=dev) * 2).to(torch.float8_e4m3fn)
+    w = torch.randn(Q, 64, device=dev)
+    ks = torch.rand(N, device=dev) + 0.05
+    out = torch.empty(Q, N, device=dev)
+    start = N - Q
+
+    def separate():
+        ops.lib().indexer_logits(q, kk, w, ks, out, start)
+        return ops.exact_topk(out, k, causal_start=start, n=N, order="index")
+
+    def fused():
+        return ops.indexer_select(q, kk, w, ks, start, k, logits_buf=out, order="index")
+
+    ref_ids = separate()[1]
+    got_ids = fused()[1]
+    equal = bool(torch.equal(ref_ids, got_ids))
+    ms_sep = time_fn(separate)
+    ms_fused = time_fn(fused)
+    return {"op": "indexer_select", "Q": Q, "N": N, "k": k, "ms": ms_fused, "separate_ms": ms_sep,
+            "speedup": ms_sep / ms_fused, "ids_equal": equal}
+
+
 def bench_topk(R=1024, N=65536, k=2048, clustered=False, order="value", causal=False, **_):
     dev = "cuda"
     s = torch.randn(R, N, device=dev)
@@ -203,7 +230,8 @@ def bench_rs_gemm(M=1024, N=7168, Kdim=2304, **_):
             "tflops": flops / ms / 1e9}
 
 
-OPS = {"sparse_mla": bench_sparse_mla, "fp8_gemm": bench_fp8_gemm, "indexer": bench_indexer, "topk": bench_topk,
+OPS = {"sparse_mla": bench_sparse_mla, "fp8_gemm": bench_fp8_gemm, "indexer": bench_indexer,
+       "indexer_select": bench_indexer_select, "topk": bench_topk,
        "ag_gemm": bench_ag_gemm, "rs_gemm": bench_rs_gemm}
 
 
@@ -236,7 +264,7 @@ def main():
             kw = dict(M=a.M, N=a.N, K=a.Kdim, ue8m0=a.block_scaled)
         if name in ("ag_gemm", "rs_gemm"):
             kw = dict(M=a.M, N=a.N, Kdim=a.Kdim)
-        if name == "indexer":
+        if name in ("indexer", "indexer_select"):
             kw = dict(Q=a.R)
         if name == "topk":
             kw = dict(R=a.R, clustered=a.clustered, order=a.order, causal=a.causal)

@@ -59,6 +59,9 @@ class AttentionRunner:
         # 296-row rounds and 574.5 ms with 148-row rounds (smaller launches
         # cost more than the L2 residency saves).
         self.select_rows = 0
+        # CUDA, methods other than echo (whose predictor reads the full logits):
+        # indexer + top-k as one fused selection (ops.indexer_select).
+        self.fused_select = True
         self.last_indices = None
         self.head_scale = cfg.index_n_heads ** -0.5 * cfg.index_head_dim ** -0.5
         (self.qa0, self.qa_n), (self.kv0, self.kv_n), (self.ik0, self.ik_n) = weights.spans_a
@@ -153,6 +156,23 @@ class AttentionRunner:
                 # queries against its key shard, the (score, id) lists are merged.
                 with scope("indexer_cp"):
                     ids = self._cp_select(comm, q_idx, weights, keys, kscales, pos, end, T, r0, r1)
+                self.last_indices = ids
+                with scope("sparse_mla"):
+                    if state.dense is not None:
+                        attn = ops.sparse_mla(q_proj, state.dense, ids, cfg.attention_scale,
+                                              value_dim=cfg.kv_lora_rank,
+                                              splits=ops.mla_splits(q_proj.shape[0], ids.shape[1]))
+                    else:
+                        attn = self._consume(cache, q_proj, ids)
+                return self._output(attn, T_loc, scope)
+            if normed.is_cuda and self.fused_select and self.method != "echo":
+                # Fused exact selection: no full logits in HBM (sampled threshold,
+                # candidate lists, candidate top-k; flagged rows redone in full).
+                with scope("indexer_select"):
+                    lb = logits_buf if (logits_buf is not None and logits_buf.shape[0] >= T_loc
+                                        and logits_buf.shape[1] >= end) else None
+                    _, ids = ops.indexer_select(q_idx, keys, weights, kscales, qpos, cfg.index_topk,
+                                                logits_buf=lb, order="index")
                 self.last_indices = ids
                 with scope("sparse_mla"):
                     if state.dense is not None:

@@ -211,6 +211,35 @@ def indexer_logits(q, k, weights, kscale, query_start: int, *, out=None):
     return out
 
 
+def indexer_select(q, keys, weights, kscale, query_start: int, k: int, *, logits_buf=None, order: str = "index",
+                   sample_stride: int = 16, cand_cap: int = 8192):
+    """Fused indexer + exact top-k: ``exact_topk(indexer_logits(...), k, causal_start=query_start,
+    n=len(keys), order=order)`` without the full FP32 logits in HBM.
+
+    On CUDA a 1/``sample_stride`` sampling pass of the indexer sets a per-row
+    threshold, the selection pass keeps only logits at or above it (at most
+    ``cand_cap`` per row) and an exact top-k runs over those candidates; rows
+    whose candidates cannot decide the top-k are redone from full logits in
+    ``logits_buf`` (allocated when not given).  Returns (values, ids), width
+    min(k, len(keys)).
+    """
+    if order not in ("value", "index"):
+        raise ValueError("order must be 'value' or 'index'")
+    N = keys.shape[0]
+    if not _cuda(q):
+        logits = reference.indexer_logits(q, keys, weights, kscale, query_start)
+        return exact_topk(logits, k, causal_start=query_start, n=N, order=order)
+    Q = q.shape[0]
+    width = min(k, N)
+    if logits_buf is None or logits_buf.shape[0] < Q or logits_buf.shape[1] < N:
+        logits_buf = torch.empty((Q, max(4, (N + 3) // 4 * 4)), dtype=torch.float32, device=q.device)
+    values = torch.empty((Q, width), dtype=torch.float32, device=q.device)
+    ids = torch.empty((Q, width), dtype=torch.int32, device=q.device)
+    lib().indexer_select(q, keys, weights, kscale, logits_buf, query_start, k, values, ids, order == "index",
+                         sample_stride, max(cand_cap, 2 * k))
+    return values, ids
+
+
 def exact_topk(scores, k: int, *, causal_start: int | None = None, n: int | None = None, algo: int = 0,
                order: str = "value", out=None):
     """Exact top-k (ties -> smaller index), -1 ids for non-finite/empty slots.

@@ -165,6 +165,51 @@ def test_indexer_logits(Q, N, start):
     assert rel_err(got.cpu()[fin], want[fin]) < 1e-4
 
 
+# ------------------------------------------------- fused indexer selection
+@pytest.mark.parametrize("order", ["index", "value"])
+@pytest.mark.parametrize("Q,N,start", [(7, 300, 200), (64, 20000, 19936), (130, 12000, 0), (256, 65536, 65280),
+                                       (1, 70000, 69999), (40, 9000, 3000)])
+def test_indexer_select_matches_logits_topk(Q, N, start, order):
+    """The fused selection (sampled threshold, candidate lists, candidate top-k,
+    fallback) equals exact_topk over the kernel's full logits, bit for bit."""
+    torch.manual_seed(31)
+    N = max(N, start + Q)
+    q = (torch.randn(Q, 64, 128, device=DEV) * 2).to(torch.float8_e4m3fn)
+    k = (torch.randn(N, 128, device=DEV) * 2).to(torch.float8_e4m3fn)
+    w = torch.randn(Q, 64, device=DEV)
+    ks = torch.rand(N, device=DEV) + 0.1
+    logits = ops.indexer_logits(q, k, w, ks, start)
+    rv, ri = ops.exact_topk(logits, 2048, causal_start=start, n=N, order=order)
+    v, i = ops.indexer_select(q, k, w, ks, start, 2048, order=order)
+    ops.check_errors(DEV)
+    assert torch.equal(i, ri)
+    assert torch.equal(v, rv)
+
+
+@pytest.mark.parametrize("kind", ["equal_keys", "banded"])
+def test_indexer_select_fallback_rows(kind):
+    """Rows the candidate lists cannot decide (one value shared by every key:
+    the threshold keeps them all and overflows the list) are redone from full
+    logits; the result still equals the plain path."""
+    torch.manual_seed(32)
+    Q, N, start = 48, 30000, 29952
+    q = (torch.randn(Q, 64, 128, device=DEV) * 2).to(torch.float8_e4m3fn)
+    if kind == "equal_keys":
+        k = (torch.randn(1, 128, device=DEV) * 2).expand(N, 128).contiguous().to(torch.float8_e4m3fn)
+        ks = torch.full((N,), 0.5, device=DEV)
+    else:  # few distinct keys: large tie groups around the threshold
+        k = (torch.randn(7, 128, device=DEV) * 2)[torch.randint(0, 7, (N,), device=DEV)].to(torch.float8_e4m3fn)
+        ks = torch.full((N,), 0.5, device=DEV)
+    w = torch.randn(Q, 64, device=DEV)
+    w[: Q // 2] = w[: Q // 2].abs()
+    logits = ops.indexer_logits(q, k, w, ks, start)
+    rv, ri = ops.exact_topk(logits, 2048, causal_start=start, n=N, order="index")
+    v, i = ops.indexer_select(q, k, w, ks, start, 2048, order="index")
+    ops.check_errors(DEV)
+    assert torch.equal(i, ri)
+    assert torch.equal(v, rv)
+
+
 # ----------------------------------------------------------------- topk
 @pytest.mark.parametrize("algo", [0, 1], ids=["two_pass", "multi_pass"])
 @pytest.mark.parametrize("R,N,k", [(3, 100, 64), (5, 5000, 2048), (2, 70000, 2048), (4, 1500, 2048), (300, 65536, 2048)])
