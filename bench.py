@@ -213,9 +213,34 @@ def sp_arm(cfg, n_layers, args, dev, rank, world, comm: str) -> dict:
         extd += e[1].elapsed_time(e[2])
     model.comm.timer = None
     coll = timer.summary()
+    # The extend again, captured in one CUDA graph per rank (replays in lockstep).
+    graph_ms = -1.0
+    if not args.no_graph:
+        model.reset()
+        model.prefill(hist)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        graph = model.capture_extend(A)
+        for _ in range(2):
+            graph.replay(ext)
+            graph.rollback()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        tot = 0.0
+        for _ in range(steps):
+            e = _events(2)
+            e[0].record(stream)
+            graph.replay(ext)
+            e[1].record(stream)
+            torch.cuda.synchronize(dev)
+            tot += e[0].elapsed_time(e[1])
+            graph.rollback()
+        graph_ms = tot / steps
+        del graph  # before the process group goes away (it may hold NCCL calls)
+        torch.cuda.synchronize(dev)
     names = sorted(coll)
-    vec = torch.tensor([pre / steps, extd / steps] + [coll[n]["ms"] / steps for n in names], dtype=torch.float64,
-                       device=dev)
+    vec = torch.tensor([pre / steps, extd / steps, graph_ms] + [coll[n]["ms"] / steps for n in names],
+                       dtype=torch.float64, device=dev)
     dist.all_reduce(vec, op=dist.ReduceOp.MAX)
     vals = vec.tolist()
     calls = dict(getattr(model.comm, "fused_calls", {}))
@@ -225,8 +250,9 @@ def sp_arm(cfg, n_layers, args, dev, rank, world, comm: str) -> dict:
     torch.cuda.empty_cache()
     dist.barrier()
     return {"prefill_ms": round(vals[0], 3), "extend_ms": round(vals[1], 4),
+            "graph_extend_ms": round(vals[2], 4) if vals[2] >= 0 else None,
             "prefill_tok_s": round(H / (vals[0] / 1e3), 1),
-            "collective_ms_per_step": {n: round(v, 3) for n, v in zip(names, vals[2:])},
+            "collective_ms_per_step": {n: round(v, 3) for n, v in zip(names, vals[3:])},
             "collective_calls_per_step": {n: coll[n]["calls"] // steps for n in names},
             "fused_calls": calls}
 

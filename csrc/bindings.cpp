@@ -251,7 +251,7 @@ void indexer_logits(const Tensor& q, const Tensor& k, const Tensor& w, const Ten
 // buffer, written only for rows the candidate lists cannot finish).
 void indexer_select(const Tensor& q, const Tensor& k, const Tensor& w, const Tensor& kscale, Tensor& logits,
                     int64_t query_start, int64_t topk, Tensor& values, Tensor& ids, bool index_order,
-                    int64_t sample_stride, int64_t cand_cap) {
+                    int64_t sample_stride, int64_t cand_cap, const c10::optional<Tensor>& diag) {
   CHECK_CUDA(q); CHECK_DTYPE(q, torch::kFloat8_e4m3fn); CHECK_DTYPE(k, torch::kFloat8_e4m3fn);
   CHECK_DTYPE(w, torch::kFloat32); CHECK_DTYPE(kscale, torch::kFloat32); CHECK_DTYPE(logits, torch::kFloat32);
   CHECK_DTYPE(values, torch::kFloat32); CHECK_DTYPE(ids, torch::kInt32);
@@ -274,7 +274,8 @@ void indexer_select(const Tensor& q, const Tensor& k, const Tensor& w, const Ten
   Tensor slog = torch::empty({Q, std::max<int64_t>(4, (ns + 3) / 4 * 4)}, f32);
   Tensor thresh = torch::empty({Q}, f32);
   Tensor cand = torch::empty({Q, cand_cap}, torch::dtype(torch::kInt64).device(q.device()));
-  Tensor small = torch::empty({3, Q}, i32);  // counts, flags, overflow
+  Tensor counts = torch::empty({Q + 1}, i32);  // per-row counts, then the any-row-flagged word
+  Tensor small = torch::empty({2, Q}, i32);    // flags, overflow
   b200::IndexerSelectArgs a{};
   a.idx.q = cptr<uint8_t>(q); a.idx.k = cptr<uint8_t>(k); a.idx.w = cptr<float>(w);
   a.idx.kscale = cptr<float>(kscale); a.idx.logits = ptr<float>(logits); a.idx.ldl = logits.stride(0);
@@ -283,9 +284,18 @@ void indexer_select(const Tensor& q, const Tensor& k, const Tensor& w, const Ten
   a.k = int(topk); a.width = int(ids.size(1)); a.sample_stride = int(sample_stride); a.cand_cap = int(cand_cap);
   a.sample_logits = slog.data_ptr<float>(); a.ld_sample = slog.stride(0); a.thresh = thresh.data_ptr<float>();
   a.cand = reinterpret_cast<uint64_t*>(cand.data_ptr<int64_t>());
-  a.cand_count = small[0].data_ptr<int>(); a.flags = small[1].data_ptr<int>(); a.overflow = small[2].data_ptr<int>();
+  a.cand_count = counts.data_ptr<int>(); a.any_flag = a.cand_count + Q;
+  a.flags = small[0].data_ptr<int>(); a.overflow = small[1].data_ptr<int>();
   a.values = ptr<float>(values); a.ids = ptr<int>(ids); a.index_order = index_order;
   b200::launch_indexer_select(a, stream());
+  if (diag) {  // [rows redone from full logits, candidates kept, most candidates of a row]
+    TORCH_CHECK(diag->dtype() == torch::kInt64 && diag->numel() >= 3, "indexer_select: diag int64 [3]");
+    Tensor d = *diag;
+    Tensor c = counts.narrow(0, 0, Q);
+    d.select(0, 0).copy_(small[0].sum());
+    d.select(0, 1).copy_(c.to(torch::kInt64).sum());
+    d.select(0, 2).copy_(c.max());
+  }
 }
 
 void topk(const Tensor& scores, int64_t N, int64_t k, int64_t causal_start, Tensor& values, Tensor& ids,
@@ -679,15 +689,28 @@ b200::P2PArgs make_p2p(int64_t rank, int64_t world, int64_t S, int64_t call, int
   return p;
 }
 
+// Device-resident op state (epoch != 0): the call's number, parity and flag
+// targets come from the op-state block; the host passes only its increments.
+void set_epoch(b200::P2PArgs& p, int64_t epoch, int64_t arrive_inc, int64_t done_inc) {
+  if (epoch == 0) return;
+  TORCH_CHECK(epoch % 8 == 0, "p2p: op-state block must be 8-byte aligned");
+  TORCH_CHECK(arrive_inc > 0 && done_inc >= 0, "p2p: op-state increments");
+  p.epoch = reinterpret_cast<uint64_t*>(epoch);
+  p.arrive_inc = uint32_t(arrive_inc);
+  p.done_inc = uint32_t(done_inc);
+}
+
 // AG-GEMM: q_local [S, K] fp8, s_local_t [K/128, S] fp32 -> out [world*S, N] bf16.
 void fp8_gemm_ag(const Tensor& q_local, const Tensor& s_local_t, const Tensor& w, const Tensor& w_s, Tensor& out,
                  int64_t rank, int64_t world, int64_t call, int64_t arrive_target, int64_t reuse_target,
-                 const std::vector<int64_t>& flags, const std::vector<int64_t>& g, const std::vector<int64_t>& gs) {
+                 const std::vector<int64_t>& flags, const std::vector<int64_t>& g, const std::vector<int64_t>& gs,
+                 int64_t epoch, int64_t arrive_inc, int64_t done_inc) {
   const int64_t S = q_local.size(0), K = q_local.size(1), N = w.size(0);
   TORCH_CHECK(q_local.is_contiguous() && s_local_t.is_contiguous() && s_local_t.size(1) == S, "ag: layout");
   TORCH_CHECK(out.size(0) == world * S && out.size(1) == N && out.is_contiguous(), "ag: out shape");
   c10::cuda::CUDAGuard guard(q_local.device());
   auto p = make_p2p(rank, world, S, call, arrive_target, reuse_target, flags, g, gs, {});
+  set_epoch(p, epoch, arrive_inc, done_inc);
   p.grid = b200::fp8_gemm_ag_grid(int(world * S), int(N), int(K));
   p.a_local = reinterpret_cast<const uint8_t*>(q_local.data_ptr());
   p.sfa_local = s_local_t.data_ptr<float>();
@@ -700,13 +723,14 @@ void fp8_gemm_ag(const Tensor& q_local, const Tensor& s_local_t, const Tensor& w
 void fp8_gemm_rs(const Tensor& a_q, const Tensor& a_s_t, const Tensor& w, const Tensor& w_s,
                  const c10::optional<Tensor>& residual, Tensor& out, int64_t rank, int64_t world, int64_t call,
                  int64_t arrive_target, int64_t reuse_target, const std::vector<int64_t>& flags,
-                 const std::vector<int64_t>& rb) {
+                 const std::vector<int64_t>& rb, int64_t epoch, int64_t arrive_inc, int64_t done_inc) {
   const int64_t M = a_q.size(0), K = a_q.size(1), N = w.size(0);
   TORCH_CHECK(M % world == 0, "rs: rows must split evenly");
   const int64_t S = M / world;
   TORCH_CHECK(out.size(0) == S && out.size(1) == N && out.is_contiguous(), "rs: out shape");
   c10::cuda::CUDAGuard guard(a_q.device());
   auto p = make_p2p(rank, world, S, call, arrive_target, reuse_target, flags, {}, {}, rb);
+  set_epoch(p, epoch, arrive_inc, done_inc);
   p.reduce_grid = b200::rs_reduce_grid(int(S), int(N));
   const __nv_bfloat16* res = residual ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr;
   b200::launch_fp8_gemm_rs(p, reinterpret_cast<const uint8_t*>(a_q.data_ptr()), int(a_q.stride(0)),
@@ -717,9 +741,10 @@ void fp8_gemm_rs(const Tensor& a_q, const Tensor& a_s_t, const Tensor& w, const 
 }
 
 void p2p_barrier(int64_t device, int64_t rank, int64_t world, int64_t call, const std::vector<int64_t>& flags,
-                 int64_t wait_ns) {
+                 int64_t wait_ns, int64_t epoch) {
   c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
-  auto p = make_p2p(rank, world, 1, call, call, 0, flags, {}, {}, {});
+  auto p = make_p2p(rank, world, 1, call, std::max<int64_t>(call, 1), 0, flags, {}, {}, {});
+  set_epoch(p, epoch, 1, 0);
   TORCH_CHECK(wait_ns > 0, "p2p_barrier: wait budget must be positive");
   p.wait_ns = uint64_t(wait_ns);
   b200::launch_p2p_barrier(p, error_word_ref(int(device)).data_ptr<int>(), at::cuda::getCurrentCUDAStream());
@@ -773,7 +798,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("indexer_logits", &indexer_logits);
   m.def("indexer_select", &indexer_select, py::arg("q"), py::arg("k"), py::arg("w"), py::arg("kscale"),
         py::arg("logits"), py::arg("query_start"), py::arg("topk"), py::arg("values"), py::arg("ids"),
-        py::arg("index_order") = true, py::arg("sample_stride") = 16, py::arg("cand_cap") = 8192);
+        py::arg("index_order") = true, py::arg("sample_stride") = 32, py::arg("cand_cap") = 8192,
+        py::arg("diag") = py::none());
   m.def("topk", &topk);
   m.def("sparse_mla", &sparse_mla);
   m.def("sparse_mla_scratch_bytes", &sparse_mla_scratch_bytes);
@@ -792,11 +818,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("pool_map", &pool_map);
   m.def("echo_predict", &echo_predict);
   m.def("echo_hint", &echo_hint);
-  m.def("fp8_gemm_ag", &fp8_gemm_ag);
-  m.def("fp8_gemm_rs", &fp8_gemm_rs);
+  m.def("fp8_gemm_ag", &fp8_gemm_ag, py::arg("q_local"), py::arg("s_local_t"), py::arg("w"), py::arg("w_s"),
+        py::arg("out"), py::arg("rank"), py::arg("world"), py::arg("call"), py::arg("arrive_target"),
+        py::arg("reuse_target"), py::arg("flags"), py::arg("g"), py::arg("gs"), py::arg("epoch") = int64_t(0),
+        py::arg("arrive_inc") = int64_t(0), py::arg("done_inc") = int64_t(0));
+  m.def("fp8_gemm_rs", &fp8_gemm_rs, py::arg("a_q"), py::arg("a_s_t"), py::arg("w"), py::arg("w_s"),
+        py::arg("residual"), py::arg("out"), py::arg("rank"), py::arg("world"), py::arg("call"),
+        py::arg("arrive_target"), py::arg("reuse_target"), py::arg("flags"), py::arg("rb"),
+        py::arg("epoch") = int64_t(0), py::arg("arrive_inc") = int64_t(0), py::arg("done_inc") = int64_t(0));
   m.def("set_fp8_gemm_pair_tiles", &b200::set_fp8_gemm_pair_tiles);
   m.def("p2p_barrier", &p2p_barrier, py::arg("device"), py::arg("rank"), py::arg("world"), py::arg("call"),
-        py::arg("flags"), py::arg("wait_ns") = int64_t(2000000000));
+        py::arg("flags"), py::arg("wait_ns") = int64_t(2000000000), py::arg("epoch") = int64_t(0));
   m.def("sparse_mla_2sm_trace", &sparse_mla_2sm_trace);
   m.def("moe_route", &moe_route);
   m.def("ep_dispatch", &ep_dispatch);

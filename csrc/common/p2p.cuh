@@ -58,4 +58,41 @@ __device__ __forceinline__ bool wait_flag_ge(const uint64_t* flag, uint64_t targ
   }
 }
 
+// Number, parity and flag targets of the running call: from the kernel
+// arguments (host-counted mode) or from the device op-state block.
+struct P2PCall {
+  int parity;
+  uint64_t arrive_target;
+  uint64_t reuse_target;
+};
+
+__device__ __forceinline__ P2PCall p2p_call(const P2PArgs& p) {
+  if (p.epoch == nullptr) return P2PCall{p.parity, p.arrive_target, p.reuse_target};
+  const uint64_t calls = __ldcg(p.epoch + kEpochCalls) + 1;
+  P2PCall c;
+  c.parity = int(calls & 1u);
+  c.arrive_target = __ldcg(p.epoch + kEpochArrive) + p.arrive_inc;
+  c.reuse_target = calls >= 3 ? __ldcg(p.epoch + kEpochDone + (calls - 2) % 4) : 0ull;
+  return c;
+}
+
+// Thread 0 of every CTA of the call's last kernel, after the CTA's work: the
+// last CTA to get here advances the op state (every CTA has read it by then).
+__device__ __forceinline__ void p2p_epoch_finish(const P2PArgs& p) {
+  if (p.epoch == nullptr) return;
+  __threadfence();
+  const unsigned long long n = gridDim.x * gridDim.y * gridDim.z;
+  const unsigned long long prev =
+      atomicAdd(reinterpret_cast<unsigned long long*>(p.epoch + kEpochFinish), 1ull);
+  if (prev + 1 != n) return;
+  __threadfence();
+  volatile uint64_t* e = p.epoch;
+  const uint64_t calls = e[kEpochCalls] + 1;
+  e[kEpochDone + calls % 4] = e[kEpochDone + (calls - 1) % 4] + p.done_inc;
+  e[kEpochArrive] = e[kEpochArrive] + p.arrive_inc;
+  e[kEpochCalls] = calls;
+  e[kEpochFinish] = 0;
+  __threadfence();
+}
+
 }  // namespace b200

@@ -23,6 +23,18 @@ constexpr int kFlagEpReady = 80;    // + owner: owner's expert outputs are ready
 constexpr int kFlagEpDone = 88;     // + src: src finished reading this rank's expert outputs
 constexpr int kFlagSlots = 128;
 
+// Device-resident op state (CUDA-graph replays): one block of kEpochSlots u64
+// per op kind in this rank's local memory.  A call reads its number, parity
+// and flag targets from the block at launch; the last CTA of the call's last
+// kernel advances it, so eager calls and graph replays stay in step with the
+// peers without host counters.
+constexpr int kEpochCalls = 0;      // calls completed
+constexpr int kEpochArrive = 1;     // cumulative arrival count per source
+constexpr int kEpochDone = 2;       // ring of 4: cumulative reader-done count after call c at [2 + c % 4]
+constexpr int kEpochFinish = 6;     // CTAs of the running call that finished (reset by the last one)
+constexpr int kEpochSlots = 8;
+constexpr int kEpochAg = 0, kEpochRs = 1, kEpochBarrier = 2, kEpochKinds = 3;
+
 // Peer pointers and flag targets of one fused call (passed by value as a kernel argument).
 struct P2PArgs {
   int rank = 0;
@@ -43,6 +55,11 @@ struct P2PArgs {
   // RS: every rank's receive slots ([2][world][S][N] bf16)
   __nv_bfloat16* rb[kMaxRanks] = {};
   uint64_t* flags[kMaxRanks] = {};  // every rank's flag block
+  // Device-resident mode: when set, parity / arrive_target / reuse_target
+  // above are ignored and come from this op-state block (kEpochSlots u64).
+  uint64_t* epoch = nullptr;
+  uint32_t arrive_inc = 0;      // arrival count this call adds per source
+  uint32_t done_inc = 0;        // reader-done count this call adds per source
 };
 
 // Expert-parallel dispatch / combine over the symmetric heap.

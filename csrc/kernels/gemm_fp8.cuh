@@ -119,13 +119,13 @@ __device__ __forceinline__ int tile_m_block(int tile, int num_m, int rot) {
 }
 
 // AG: wait until every shard overlapping rows [m0, m0 + BM) has arrived here.
-__device__ __forceinline__ bool ag_wait_rows(const P2PArgs& p, int m0, int M, uint32_t& ready, int* err,
-                                             volatile int* abort_flag) {
+__device__ __forceinline__ bool ag_wait_rows(const P2PArgs& p, uint64_t arrive_target, int m0, int M,
+                                             uint32_t& ready, int* err, volatile int* abort_flag) {
   const int s0 = m0 / p.S, s1 = min(M - 1, m0 + BM - 1) / p.S;
   for (int s = s0; s <= s1; ++s) {
     if (ready & (1u << s)) continue;
     const uint64_t* f = p.flags[p.rank] + kFlagAgArrive + s;
-    if (!wait_flag_ge(f, p.arrive_target, err, kErrTimeoutPeerFlag, abort_flag)) return false;
+    if (!wait_flag_ge(f, arrive_target, err, kErrTimeoutPeerFlag, abort_flag, p.wait_ns)) return false;
     ready |= 1u << s;
   }
   return true;
@@ -191,6 +191,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_units = num_tiles * splits;
   const int kps = (num_kb + splits - 1) / splits;
   const int rot = MODE == kModeRS ? ((p2p.rank + 1) % p2p.world) * p2p.S / TM % num_m : 0;
+  // AG / RS: this call's parity and flag targets (kernel arguments or the device op state).
+  const P2PCall pc = (MODE == kModeAG || MODE == kModeRS) ? p2p_call(p2p) : P2PCall{0, 0ull, 0ull};
+  // AG: A (tensor map rows) and its scales cover both parity halves of the gather buffer.
+  const int a_row0 = MODE == kModeAG ? pc.parity * M : 0;
+  const float* sfa_k = MODE == kModeAG ? sfa + size_t(pc.parity) * num_kb * lda_s : sfa;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -372,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int n0 = (tile / num_m) * BN;
         const int kb0 = sp * kps, kb1 = min(num_kb, kb0 + kps);
         if constexpr (MODE == kModeAG) {
-          if (!ag_wait_rows(p2p, m0, M, ready, err, abort_flag)) {
+          if (!ag_wait_rows(p2p, pc.arrive_target, m0, M, ready, err, abort_flag)) {
             ok = false;
             break;
           }
@@ -396,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d_pair(s.b[stage], &tma_b, fb, kb * BK, n0 + int(crank) * BROWS);
           } else {
             mbar_arrive_expect_tx(&s.full[stage], BM * BK + BN * BK);
-            tma_load_2d(s.a[stage], &tma_a, &s.full[stage], kb * BK, m0);
+            tma_load_2d(s.a[stage], &tma_a, &s.full[stage], kb * BK, a_row0 + m0);
             tma_load_2d(s.b[stage], &tma_b, &s.full[stage], kb * BK, n0);
           }
           if (++stage == STAGES) {
@@ -537,10 +542,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Push this rank's shard (rows [rank*S, rank*S+S) of the gathered A) and
       // its scales into every rank's gather buffer (this call's parity half).
       const int et = threadIdx.x - 64;
-      if (et == 0 && p2p.reuse_target > 0) {
+      if (et == 0 && pc.reuse_target > 0) {
         // Reuse guard: rank q finished reading this parity two calls ago.
         for (int q = 0; q < p2p.world && ok; ++q)
-          ok = wait_flag_ge(p2p.flags[p2p.rank] + kFlagAgDone + q, p2p.reuse_target, err, kErrTimeoutPeerFlag,
+          ok = wait_flag_ge(p2p.flags[p2p.rank] + kFlagAgDone + q, pc.reuse_target, err, kErrTimeoutPeerFlag,
                             abort_flag);
       }
       named_barrier(kEpiBarrier, kEpiWarps * 32);
@@ -550,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t gt = int64_t(blockIdx.x) * kEpiWarps * 32 + et;
         const int vec_per_row = K / 16;
         const int64_t nvec = int64_t(p2p.S) * vec_per_row;
-        const int64_t row_base = int64_t(p2p.parity) * M + int64_t(p2p.rank) * p2p.S;
+        const int64_t row_base = int64_t(pc.parity) * M + int64_t(p2p.rank) * p2p.S;
         for (int64_t v = gt; v < nvec; v += stride) {
           const int64_t r = v / vec_per_row, c = v % vec_per_row;
           const uint4 val = *reinterpret_cast<const uint4*>(p2p.a_local + r * K + c * 16);
@@ -562,7 +567,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int64_t kb = i / p2p.S, j = i % p2p.S;
           const float val = p2p.sfa_local[kb * p2p.S + j];
           for (int q = 0; q < p2p.world; ++q)
-            p2p.gs[q][(int64_t(p2p.parity) * num_kb + kb) * M + int64_t(p2p.rank) * p2p.S + j] = val;
+            p2p.gs[q][(int64_t(pc.parity) * num_kb + kb) * M + int64_t(p2p.rank) * p2p.S + j] = val;
         }
       }
       named_barrier(kEpiBarrier, kEpiWarps * 32);
@@ -595,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if constexpr (MODE == kModeAG) {
         // Scales of peer rows were written by peers: acquire before reading them.
-        if (!ag_wait_rows(p2p, m0, M, ready, err, abort_flag)) {
+        if (!ag_wait_rows(p2p, pc.arrive_target, m0, M, ready, err, abort_flag)) {
           ok = false;
           break;
         }
@@ -632,7 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t bpar = (kcount >> 1) & 1;
           float sa = 0.f;
           if (row < M) {
-            const float* sp_ = sfa + static_cast<size_t>(kb) * lda_s + row;
+            const float* sp_ = sfa_k + static_cast<size_t>(kb) * lda_s + row;
             sa = MODE == kModeAG ? __ldcg(sp_) : __ldg(sp_);
           }
           // A warp's CPW (<= 128) columns touch at most two 128-wide weight scale blocks.
@@ -699,16 +704,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int grow = m0 + r;
           if (grow >= M || tn0 + c >= N) continue;
           const int owner = grow / p2p.S;
-          if (owner != owner_ok && p2p.reuse_target > 0) {
+          if (owner != owner_ok && pc.reuse_target > 0) {
             // Reuse guard: the owner's reduce of two calls ago has read this parity.
-            if (!wait_flag_ge(p2p.flags[p2p.rank] + kFlagRsDone + owner, p2p.reuse_target, err,
+            if (!wait_flag_ge(p2p.flags[p2p.rank] + kFlagRsDone + owner, pc.reuse_target, err,
                               kErrTimeoutPeerFlag, abort_flag)) {
               ok = false;
               break;
             }
           }
           owner_ok = owner;
-          const int64_t slot = (int64_t(p2p.parity) * p2p.world + p2p.rank) * p2p.S + (grow - owner * p2p.S);
+          const int64_t slot = (int64_t(pc.parity) * p2p.world + p2p.rank) * p2p.S + (grow - owner * p2p.S);
           *reinterpret_cast<uint4*>(p2p.rb[owner] + slot * N + tn0 + c) =
               *reinterpret_cast<const uint4*>(stage + r * (BN + 8) + c);
         }
@@ -788,6 +793,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __threadfence_system();
       for (int q = 0; q < p2p.world; ++q) red_release_sys_add(p2p.flags[q] + kFlagAgDone + p2p.rank, 1);
     }
+    if (threadIdx.x == 0) p2p_epoch_finish(p2p);
   }
 }
 

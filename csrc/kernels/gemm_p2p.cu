@@ -27,19 +27,23 @@ __global__ void __launch_bounds__(256) rs_reduce_kernel(const __grid_constant__ 
                                                          const __nv_bfloat16* __restrict__ residual, int ldr,
                                                          __nv_bfloat16* __restrict__ out, int ldo, int* err) {
   __shared__ int s_ok;
+  const P2PCall pc = p2p_call(p);
   if (threadIdx.x == 0) {
     int ok = 1;
     for (int src = 0; src < p.world && ok; ++src)
-      ok = wait_flag_ge(p.flags[p.rank] + kFlagRsArrive + src, p.arrive_target, err, kErrTimeoutPeerFlag, nullptr,
+      ok = wait_flag_ge(p.flags[p.rank] + kFlagRsArrive + src, pc.arrive_target, err, kErrTimeoutPeerFlag, nullptr,
                         p.wait_ns);
     s_ok = ok;
   }
   __syncthreads();
-  if (!s_ok) return;
+  if (!s_ok) {
+    if (threadIdx.x == 0) p2p_epoch_finish(p);
+    return;
+  }
   const int vec_per_row = N / 8;
   const int64_t nvec = int64_t(p.S) * vec_per_row;
   const int64_t slot_elems = int64_t(p.S) * N;
-  const __nv_bfloat16* base = p.rb[p.rank] + int64_t(p.parity) * p.world * slot_elems;
+  const __nv_bfloat16* base = p.rb[p.rank] + int64_t(pc.parity) * p.world * slot_elems;
   for (int64_t v = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; v < nvec; v += int64_t(gridDim.x) * blockDim.x) {
     const int64_t r = v / vec_per_row, c = (v % vec_per_row) * 8;
     float acc[8];
@@ -74,23 +78,28 @@ __global__ void __launch_bounds__(256) rs_reduce_kernel(const __grid_constant__ 
   if (threadIdx.x == 0) {
     __threadfence_system();
     for (int src = 0; src < p.world; ++src) red_release_sys_add(p.flags[src] + kFlagRsDone + p.rank, 1);
+    p2p_epoch_finish(p);  // the reduce is the call's last kernel
   }
 }
 
 // All ranks: bump my slot on every rank, then wait until every rank's slot here reached the target.
 __global__ void p2p_barrier_kernel(const __grid_constant__ P2PArgs p, int* err) {
   if (threadIdx.x != 0) return;
+  const P2PCall pc = p2p_call(p);
   __threadfence_system();
   for (int q = 0; q < p.world; ++q) red_release_sys_add(p.flags[q] + kFlagBarrier + p.rank, 1);
   for (int q = 0; q < p.world; ++q)
-    if (!wait_flag_ge(p.flags[p.rank] + kFlagBarrier + q, p.arrive_target, err, kErrTimeoutPeerFlag, nullptr, p.wait_ns))
-      return;
+    if (!wait_flag_ge(p.flags[p.rank] + kFlagBarrier + q, pc.arrive_target, err, kErrTimeoutPeerFlag, nullptr,
+                      p.wait_ns))
+      break;
+  p2p_epoch_finish(p);
 }
 
 void check_p2p(const P2PArgs& p) {
   if (p.world < 1 || p.world > kMaxRanks || p.rank < 0 || p.rank >= p.world)
     throw std::invalid_argument("p2p: rank/world out of range");
-  if (p.arrive_target < 1) throw std::invalid_argument("p2p: arrival target must be positive");
+  if (p.epoch == nullptr && p.arrive_target < 1) throw std::invalid_argument("p2p: arrival target must be positive");
+  if (p.epoch != nullptr && p.arrive_inc < 1) throw std::invalid_argument("p2p: arrival increment must be positive");
   for (int q = 0; q < p.world; ++q)
     if (!p.flags[q]) throw std::invalid_argument("p2p: missing peer flag pointer");
 }
@@ -115,10 +124,13 @@ void launch_fp8_gemm_ag(P2PArgs p, const uint8_t* B, int ldb, const float* sfb, 
   for (int q = 0; q < p.world; ++q)
     if (!p.g[q] || !p.gs[q]) throw std::invalid_argument("ag gemm: missing gather buffer pointer");
   const int kb = K / 128;
-  const uint8_t* g_local = p.g[p.rank] + size_t(p.parity) * M * K;
-  const float* gs_local = p.gs[p.rank] + size_t(p.parity) * kb * M;
+  // Both parity halves ([2][M][K] and [2][K/128][M]): the kernel offsets by
+  // the call's parity, which the device op state may decide.
+  const uint8_t* g_local = p.g[p.rank];
+  const float* gs_local = p.gs[p.rank];
+  (void)kb;
   const int bn = fp8_gemm_p2p_bn(M, N, K);
-  const CUtensorMap ta = make_tma_2d(g_local, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, BK, BM);
+  const CUtensorMap ta = make_tma_2d(g_local, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, int64_t(2) * M, K, K, BK, BM);
   const CUtensorMap tb = make_tma_2d(B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, ldb, BK, bn);
   if (p.grid != fp8_gemm_ag_grid(M, N, K)) throw std::invalid_argument("ag gemm: grid differs from the planned grid");
   size_t smem = 0;

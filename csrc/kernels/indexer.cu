@@ -35,6 +35,7 @@ constexpr int kStages = 8;
 constexpr int kEpiWarps = 16;
 static_assert(QB * 4 == kEpiWarps, "one query per epilogue warp (4 warps cover a lane quadrant each)");
 constexpr int kThreads = 64 + kEpiWarps * 32;
+constexpr int kStageCap = 128;        // candidates a warp stages before one counter update
 
 struct Smem {
   alignas(1024) uint8_t q[2][NQ * kDim];         // 2 x 32 KB
@@ -42,6 +43,7 @@ struct Smem {
   uint64_t q_full[2], q_empty[2];
   uint64_t k_full[kStages], k_empty[kStages];
   uint64_t tmem_full[2], tmem_empty[2];
+  uint64_t stage[kEpiWarps][kStageCap];          // selection mode: each warp's pending candidates
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -50,6 +52,7 @@ struct Schedule {
   int Q, N, query_start, num_qb, num_tiles_total, chunk_tiles, num_chunks;
   int stride;                // key j of this launch is key j * stride of the cache (sampling pass)
   const int* row_flags;      // when set, only query blocks with a flagged row run
+  const int* any_flag;       // when set and zero, no row is flagged: the launch returns at once
   __device__ __forceinline__ int units() const { return num_qb * num_chunks; }
   // Returns false when the unit lies entirely past the query block's causal
   // end, or (with row_flags) when none of the block's rows is flagged.
@@ -88,10 +91,19 @@ struct IndexerOut {
   int cand_cap;
 };
 
+// relu(x) * 2^-64 on the FMA pipe (saturating multiply clamps to [0, 1]).
+__device__ __forceinline__ float relu_scaled(float x) {
+  float y;
+  asm("mul.rn.sat.f32 %0, %1, 0f1F800000;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <bool SELECT>
 __global__ void __launch_bounds__(kThreads, 1)
     indexer_kernel(const __grid_constant__ CUtensorMap tma_q,
                    const __grid_constant__ CUtensorMap tma_k, const float* __restrict__ w,
                    const float* __restrict__ kscale, IndexerOut o, Schedule sch, int* err) {
+  if (sch.any_flag != nullptr && __ldcg(sch.any_flag) == 0) return;  // uniform: nothing to redo
   extern __shared__ uint8_t smem_raw[];
   auto& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x / 32;
@@ -195,6 +207,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int key_in_tile = quad * 32 + lane;
     uint32_t tcount = 0;
     bool ok = true;
+    uint32_t fill = 0;  // selection mode: candidates in this warp's stage (warp-uniform)
+    // One counter update per batch; the batch's slots past the capacity are
+    // counted but not stored (the row then goes to the fallback).
+    auto flush = [&](int q, uint32_t cnt) {
+      __syncwarp();
+      uint32_t base = 0;
+      if (lane == 0) base = atomicAdd(reinterpret_cast<unsigned int*>(o.cand_count + q), cnt);
+      base = __shfl_sync(0xffffffffu, base, 0);
+      for (uint32_t i = lane; i < cnt; i += 32)
+        if (base + i < uint32_t(o.cand_cap)) o.cand[int64_t(q) * o.cand_cap + base + i] = s.stage[ew][i];
+      __syncwarp();
+    };
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
       int qb, t0, t1;
       if (!sch.unit(u, qb, t0, t1)) continue;
@@ -203,6 +227,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // cost 256 B per thread per tile, which bounded the epilogue at the
       // shared-memory read bandwidth.
       const int qidx = qb * QB + qgrp;
+      // Heads 4i+2, 4i+3 hold w * 2^64 and take their ReLU on the FMA pipe:
+      // mul.sat(x, 2^-64) = relu(x) * 2^-64 exactly (an E4M3 x E4M3 dot
+      // product is 0 or a multiple of 2^-18 below 2^25, so the scaled value is
+      // a normal float below 1), and the product with w * 2^64 rounds exactly
+      // like relu(x) * w.  Heads 4i, 4i+1 use max(x, 0) on the ALU pipe.  The
+      // split halves the ALU work that bounded the epilogue.
       float wr[kHeads];
       {
         const float4* wq = reinterpret_cast<const float4*>(w + int64_t(min(qidx, sch.Q - 1)) * kHeads);
@@ -211,11 +241,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float4 v = __ldg(wq + h4);
           wr[4 * h4 + 0] = v.x;
           wr[4 * h4 + 1] = v.y;
-          wr[4 * h4 + 2] = v.z;
-          wr[4 * h4 + 3] = v.w;
+          wr[4 * h4 + 2] = v.z * 18446744073709551616.0f;  // 2^64
+          wr[4 * h4 + 3] = v.w * 18446744073709551616.0f;
         }
       }
-      const float thresh = (o.select && o.thresh != nullptr) ? __ldg(o.thresh + min(qidx, sch.Q - 1)) : -INFINITY;
+      const float thresh = (SELECT && o.thresh != nullptr) ? __ldg(o.thresh + min(qidx, sch.Q - 1)) : -INFINITY;
       const int last_key = sch.query_start + qidx;  // causal: cache key index <= last_key is visible
       for (int t = t0; t < t1; ++t, ++tcount) {
         const uint32_t buf = tcount & 1, bpar = (tcount >> 1) & 1;
@@ -227,8 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        // Two packed FP32x2 accumulators (heads h = 4i, 4i+1 and 4i+2, 4i+3);
-        // the ReLU stays scalar (there is no packed max).
+        // Two packed FP32x2 accumulators (heads h = 4i, 4i+1 and 4i+2, 4i+3).
         float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
 #pragma unroll
         for (int c = 0; c < kHeads / 16; ++c) {
@@ -240,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int h = c * 16 + 4 * h4;
             fma_f32x2(a0, a1, fmaxf(__uint_as_float(r[4 * h4 + 0]), 0.f), fmaxf(__uint_as_float(r[4 * h4 + 1]), 0.f),
                       wr[h], wr[h + 1]);
-            fma_f32x2(b0, b1, fmaxf(__uint_as_float(r[4 * h4 + 2]), 0.f), fmaxf(__uint_as_float(r[4 * h4 + 3]), 0.f),
+            fma_f32x2(b0, b1, relu_scaled(__uint_as_float(r[4 * h4 + 2])), relu_scaled(__uint_as_float(r[4 * h4 + 3])),
                       wr[h + 2], wr[h + 3]);
           }
         }
@@ -249,21 +278,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.tmem_empty[buf]);
         const bool valid = key < sch.N && qidx < sch.Q;
-        if (!o.select) {
+        if constexpr (!SELECT) {
           if (valid) o.logits[int64_t(qidx) * o.ldl + key] = cache_key <= last_key ? out : -INFINITY;
         } else {
-          // All 32 lanes hold the same query: one counter update per warp.
+          // All 32 lanes hold the same query; candidates collect in the warp's
+          // shared-memory stage and reach the row's list in batches.
           const bool take = valid && cache_key <= last_key && out >= thresh;
           const uint32_t m = __ballot_sync(0xffffffffu, take);
-          if (m != 0u) {
-            uint32_t base = 0;
-            if (lane == 0) base = atomicAdd(reinterpret_cast<unsigned int*>(o.cand_count + qidx), uint32_t(__popc(m)));
-            base = __shfl_sync(0xffffffffu, base, 0);
-            const uint32_t pos = base + uint32_t(__popc(m & ((1u << lane) - 1u)));
-            if (take && pos < uint32_t(o.cand_cap))
-              o.cand[int64_t(qidx) * o.cand_cap + pos] = select_composite(out, key);
+          const uint32_t n = uint32_t(__popc(m));
+          if (fill + n > uint32_t(kStageCap)) {
+            flush(qidx, fill);
+            fill = 0;
           }
+          if (take) s.stage[ew][fill + uint32_t(__popc(m & ((1u << lane) - 1u)))] = select_composite(out, key);
+          fill += n;
         }
+      }
+      if (SELECT && fill > 0) {
+        flush(qidx, fill);
+        fill = 0;
       }
     }
   }
@@ -293,6 +326,7 @@ void launch_indexer_logits(const IndexerArgs& a, cudaStream_t stream) {
   sch.query_start = a.query_start;
   sch.stride = stride;
   sch.row_flags = a.row_flags;
+  sch.any_flag = a.row_flags != nullptr ? a.any_flag : nullptr;
   sch.num_qb = (a.Q + QB - 1) / QB;
   const int end = std::min(n, (a.query_start + a.Q - 1) / stride + 1);
   sch.num_tiles_total = (end + BKV - 1) / BKV;
@@ -313,9 +347,10 @@ void launch_indexer_logits(const IndexerArgs& a, cudaStream_t stream) {
   o.cand_count = a.cand_count;
   o.cand_cap = a.cand_cap;
   const size_t smem = sizeof(Smem) + 1024;
-  cuda_check(cudaFuncSetAttribute(indexer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+  auto kern = a.select ? indexer_kernel<true> : indexer_kernel<false>;
+  cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
              "indexer smem attribute");
-  indexer_kernel<<<grid, kThreads, smem, stream>>>(tq, tk, a.w, a.kscale, o, sch, a.err);
+  kern<<<grid, kThreads, smem, stream>>>(tq, tk, a.w, a.kscale, o, sch, a.err);
   cuda_check(cudaGetLastError(), "indexer launch");
 }
 

@@ -213,6 +213,7 @@ struct IndexerArgs {
   int key_stride = 1;
   // Only query blocks holding a flagged row run (fallback rows of a selection).
   const int* row_flags = nullptr;
+  const int* any_flag = nullptr;  // with row_flags: nonzero when some row is flagged
   // Selection mode: instead of logits, append every visible logit >= thresh[q]
   // (all visible ones when thresh is null) as a composite to row q's list.
   bool select = false;
@@ -236,6 +237,7 @@ struct IndexerSelectArgs {
   uint64_t* cand;        // [Q, cand_cap]
   int* cand_count;       // [Q]
   int* flags;            // [Q]: rows the candidate list could not finish
+  int* any_flag;         // [1]: set when some row is flagged (reset with the counts)
   int* overflow;         // [Q]: rows the two-pass top-k sends to the multi-pass kernel
   float* values;         // [Q, width]
   int* ids;              // [Q, width]

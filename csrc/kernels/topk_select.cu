@@ -1,8 +1,8 @@
 // Fused exact indexer selection: the top-k of every query's indexer logits
 // without writing the full FP32 logits to HBM.
 //
-//   1. Sampling pass: the indexer scores every 16th cache key (a strided
-//      tensor map over the same key rows), [Q, N/16] FP32.
+//   1. Sampling pass: the indexer scores every 32nd cache key (a strided
+//      tensor map over the same key rows), [Q, N/32] FP32.
 //   2. Threshold: per query, the sampled value of rank ceil(2k * ns / n_vis)
 //      (ns sampled and n_vis visible keys), expected to leave ~2k keys of the
 //      full row at or above it.  Rows with n_vis <= cap take every key.
@@ -79,11 +79,40 @@ __device__ void find_rank_bin(const uint32_t* hist, int nbins, uint32_t rank, ui
   __syncthreads();
 }
 
+// Block-wide min and max of one value per thread (64-bit keys).
+template <int THREADS>
+__device__ void block_min_max(uint64_t lo, uint64_t hi, uint64_t* red, uint64_t& out_lo, uint64_t& out_hi) {
+  const int lane = threadIdx.x % 32, wid = threadIdx.x / 32;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t a = __shfl_xor_sync(0xffffffffu, lo, o), b = __shfl_xor_sync(0xffffffffu, hi, o);
+    lo = a < lo ? a : lo;
+    hi = b > hi ? b : hi;
+  }
+  if (lane == 0) {
+    red[2 * wid] = lo;
+    red[2 * wid + 1] = hi;
+  }
+  __syncthreads();
+  out_lo = red[0];
+  out_hi = red[1];
+  for (int w = 1; w < THREADS / 32; ++w) {
+    out_lo = red[2 * w] < out_lo ? red[2 * w] : out_lo;
+    out_hi = red[2 * w + 1] > out_hi ? red[2 * w + 1] : out_hi;
+  }
+  __syncthreads();
+}
+
+// Per row: a threshold at or below the sampled value of rank r.  The levels
+// start below the bits every visible sample shares (no atomic contention on
+// a few hot bins) and stop after 16 bits: the lower edge of the bin holding
+// rank r is the threshold, so at least r samples are >= it.
 __global__ void __launch_bounds__(kThrThreads) select_threshold_kernel(const float* __restrict__ slog, int64_t lds,
                                                                       int N, int Ns, int stride, int query_start,
                                                                       int k, int cap, float* __restrict__ thresh) {
   __shared__ uint32_t hist[256];
   __shared__ uint32_t warp_sum[kThrThreads / 32];
+  __shared__ uint64_t red[2 * (kThrThreads / 32)];
   __shared__ uint32_t s_out[3];
   const int q = blockIdx.x, tid = threadIdx.x;
   const int n_vis = min(N, query_start + q + 1);
@@ -95,36 +124,57 @@ __global__ void __launch_bounds__(kThrThreads) select_threshold_kernel(const flo
   int r = int((int64_t(2) * k * ns + n_vis - 1) / n_vis);
   r = max(1, min(r, ns));
   const float* row = slog + int64_t(q) * lds;
-  uint32_t prefix = 0, rem = uint32_t(r);
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
+  uint64_t lo = ~0ull, hi = 0;
+  for (int j = tid; j < ns; j += kThrThreads) {
+    const uint64_t key = order_key(row[j]);
+    lo = key < lo ? key : lo;
+    hi = key > hi ? key : hi;
+  }
+  uint64_t klo, khi;
+  block_min_max<kThrThreads>(lo, hi, red, klo, khi);
+  int pbits = klo == khi ? 32 : __clz(uint32_t(klo ^ khi));
+  uint32_t prefix = pbits == 0 ? 0u : uint32_t(klo) >> (32 - pbits);
+  uint32_t rem = uint32_t(r);
+  for (int level = 0; level < 2 && pbits < 32; ++level) {
+    const int lb = min(8, 32 - pbits);
+    const int shift = 32 - pbits - lb;
     hist[tid] = 0u;
     __syncthreads();
     for (int j = tid; j < ns; j += kThrThreads) {
       const uint32_t key = order_key(row[j]);
-      if (pass == 0 || (key >> (shift + 8)) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      if (pbits == 0 || (key >> (32 - pbits)) == prefix) atomicAdd(&hist[(key >> shift) & ((1u << lb) - 1u)], 1u);
     }
     __syncthreads();
     uint32_t bin, above, in;
-    find_rank_bin<kThrThreads, 1>(hist, 256, rem, warp_sum, bin, above, in, s_out);
-    prefix = (prefix << 8) | bin;
+    find_rank_bin<kThrThreads, 1>(hist, 1 << lb, rem, warp_sum, bin, above, in, s_out);
+    prefix = (prefix << lb) | bin;
+    pbits += lb;
     rem -= above;
   }
-  if (tid == 0) thresh[q] = key_value(prefix);
+  if (tid == 0) {
+    const uint32_t edge = pbits >= 32 ? prefix : prefix << (32 - pbits);
+    // Keys below -inf's are NaN patterns: no finite threshold below them.
+    thresh[q] = edge <= order_key(-INFINITY) ? -INFINITY : key_value(edge);
+  }
 }
+
+constexpr int kBitmapKeys = 131072;  // index-order output by bitmap up to this many visible keys
 
 __global__ void __launch_bounds__(kCandThreads) topk_candidates_kernel(
     const uint64_t* __restrict__ cand, const int* __restrict__ cand_count, int cap, int N, int query_start, int k,
     int width, float* __restrict__ values, int* __restrict__ ids, int* __restrict__ flags, int* __restrict__ overflow,
-    bool index_order) {
+    int* __restrict__ any_flag, bool index_order) {
   extern __shared__ uint8_t dyn[];
   uint64_t* buf = reinterpret_cast<uint64_t*>(dyn);             // cap candidates
-  uint32_t* hist = reinterpret_cast<uint32_t*>(buf + cap);      // 4096 bins, later the selection
-  uint64_t* sel = reinterpret_cast<uint64_t*>(hist);            // kMaxK
+  uint32_t* hist = reinterpret_cast<uint32_t*>(buf + cap);      // 4096 bins during the levels, then:
+  uint64_t* sel = reinterpret_cast<uint64_t*>(hist);            //   kMaxK sort keys (sort path), or
+  uint32_t* bm = hist;                                          //   the selection bitmap (kBitmapKeys bits)
+  uint32_t* wpre = hist + kBitmapKeys / 32;                     //   and its per-word exclusive prefix
   __shared__ uint32_t warp_sum[kCandThreads / 32];
+  __shared__ uint64_t red[2 * (kCandThreads / 32)];
   __shared__ uint32_t s_out[3];
   __shared__ uint32_t s_cnt;
-  const int q = blockIdx.x, tid = threadIdx.x, lane = tid % 32;
+  const int q = blockIdx.x, tid = threadIdx.x, lane = tid % 32, wid = tid / 32;
   const int n_vis = min(N, query_start + q + 1);
   const int take = min(k, n_vis);
   const int c = cand_count[q];
@@ -132,18 +182,28 @@ __global__ void __launch_bounds__(kCandThreads) topk_candidates_kernel(
   if (tid == 0) {
     overflow[q] = 0;
     flags[q] = bad ? 1 : 0;
+    if (bad) atomicOr(any_flag, 1);
     s_cnt = 0u;
   }
   if (bad) return;
   const uint64_t* src = cand + int64_t(q) * cap;
-  for (int i = tid; i < c; i += kCandThreads) buf[i] = src[i];
-  __syncthreads();
+  uint64_t lo = ~0ull, hi = 0;
+  for (int i = tid; i < c; i += kCandThreads) {
+    const uint64_t x = src[i];
+    buf[i] = x;
+    lo = x < lo ? x : lo;
+    hi = x > hi ? x : hi;
+  }
+  uint64_t clo, chi;
+  block_min_max<kCandThreads>(lo, hi, red, clo, chi);  // includes the barrier after the stores
 
-  // Exact rank-`take` composite: 12-bit levels from the top until its bin
-  // holds one composite (composites are distinct).
-  uint64_t want = 0;
+  // Exact rank-`take` composite: 12-bit levels below the bits all candidates
+  // share, until its bin holds one composite (composites are distinct).
   int cbits = 0;
+  uint64_t want = 0;
   if (take < c) {
+    cbits = __clzll(clo ^ chi);  // clo != chi: c >= 2 distinct composites
+    want = cbits == 0 ? 0ull : clo >> (64 - cbits);
     uint32_t crank = uint32_t(take);
     while (cbits < 64) {
       const int lb = min(kLevelBits, 64 - cbits);
@@ -166,28 +226,89 @@ __global__ void __launch_bounds__(kCandThreads) topk_candidates_kernel(
     }
   }
   __syncthreads();
-  // Compact the selection (exactly `take` composites) into sel[], keyed for
-  // an ascending sort: (index, value key) for index order, ~composite for
-  // value order.
+  auto selected = [&](uint64_t x) { return cbits == 0 || (x >> (64 - cbits)) >= want; };
+  float* vout = values + int64_t(q) * width;
+  int* iout = ids + int64_t(q) * width;
+  auto emit = [&](int pos, float v, int idx) {
+    if (pos < width) {
+      vout[pos] = v;
+      iout[pos] = (__float_as_uint(v) & 0x7FFFFFFFu) >= 0x7F800000u ? -1 : idx;
+    }
+  };
+  if (index_order && n_vis <= kBitmapKeys) {
+    // Ascending index order without a sort: mark the selection in a bitmap,
+    // scan the per-word counts, and place each selected composite at
+    // (selected indices below it).
+    const int words = (n_vis + 31) / 32;
+    for (int i = tid; i < words; i += kCandThreads) bm[i] = 0u;
+    __syncthreads();
+    for (int i = tid; i < c; i += kCandThreads) {
+      const uint64_t x = buf[i];
+      if (selected(x)) {
+        const int idx = composite_index(x);
+        atomicOr(&bm[idx >> 5], 1u << (idx & 31));
+      }
+    }
+    __syncthreads();
+    constexpr int WPT = kBitmapKeys / 32 / kCandThreads;  // words per thread
+    uint32_t cnt[WPT], mine = 0;
+#pragma unroll
+    for (int j = 0; j < WPT; ++j) {
+      const int wi = tid * WPT + j;
+      cnt[j] = wi < words ? uint32_t(__popc(bm[wi])) : 0u;
+      mine += cnt[j];
+    }
+    uint32_t incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_sum[wid] = incl;
+    __syncthreads();
+    uint32_t base = incl - mine;
+    for (int w = 0; w < wid; ++w) base += warp_sum[w];
+#pragma unroll
+    for (int j = 0; j < WPT; ++j) {
+      const int wi = tid * WPT + j;
+      if (wi < words) wpre[wi] = base;
+      base += cnt[j];
+    }
+    __syncthreads();
+    for (int i = tid; i < c; i += kCandThreads) {
+      const uint64_t x = buf[i];
+      if (selected(x)) {
+        const int idx = composite_index(x);
+        const int pos = int(wpre[idx >> 5]) + __popc(bm[idx >> 5] & ((1u << (idx & 31)) - 1u));
+        emit(pos, composite_value(x), idx);
+      }
+    }
+    for (int i = take + tid; i < width; i += kCandThreads) {
+      vout[i] = -INFINITY;
+      iout[i] = -1;
+    }
+    return;
+  }
+  // Sort path: compact the selection (exactly `take` composites) keyed for an
+  // ascending sort -- (index, value key) for index order, ~composite for value order.
   for (int i0 = 0; i0 < c; i0 += kCandThreads) {
     const int i = i0 + tid;
-    bool s = false;
+    bool sl = false;
     uint64_t x = 0;
     if (i < c) {
       x = buf[i];
-      s = cbits == 0 || (x >> (64 - cbits)) >= want;
+      sl = selected(x);
     }
-    const uint32_t m = __ballot_sync(0xffffffffu, s);
-    uint32_t base = 0;
-    if (lane == 0 && m) base = atomicAdd(&s_cnt, uint32_t(__popc(m)));
-    base = __shfl_sync(0xffffffffu, base, 0);
-    const uint32_t pos = base + uint32_t(__popc(m & ((1u << lane) - 1u)));
-    if (s && pos < uint32_t(kMaxK))
+    const uint32_t m = __ballot_sync(0xffffffffu, sl);
+    uint32_t b = 0;
+    if (lane == 0 && m) b = atomicAdd(&s_cnt, uint32_t(__popc(m)));
+    b = __shfl_sync(0xffffffffu, b, 0);
+    const uint32_t pos = b + uint32_t(__popc(m & ((1u << lane) - 1u)));
+    if (sl && pos < uint32_t(kMaxK))
       sel[pos] = index_order ? (uint64_t(uint32_t(composite_index(x))) << 32) | uint32_t(x >> 32) : ~x;
   }
   __syncthreads();
   const int count = min(int(s_cnt), kMaxK);
-  // Bitonic sort, ascending, of n2 = 2^ceil(log2 count) keys (padding ~0 last).
   int n2 = 1;
   while (n2 < count) n2 <<= 1;
   for (int i = count + tid; i < n2; i += kCandThreads) sel[i] = ~0ull;
@@ -195,34 +316,23 @@ __global__ void __launch_bounds__(kCandThreads) topk_candidates_kernel(
   for (int size = 2; size <= n2; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
       for (int i = tid; i < n2 / 2; i += kCandThreads) {
-        const int lo = 2 * i - (i & (stride - 1));
-        const int hi = lo + stride;
-        const bool asc = (lo & size) == 0;
-        const uint64_t a = sel[lo], b = sel[hi];
+        const int lo_i = 2 * i - (i & (stride - 1));
+        const int hi_i = lo_i + stride;
+        const bool asc = (lo_i & size) == 0;
+        const uint64_t a = sel[lo_i], b = sel[hi_i];
         if ((a > b) == asc) {
-          sel[lo] = b;
-          sel[hi] = a;
+          sel[lo_i] = b;
+          sel[hi_i] = a;
         }
       }
       __syncthreads();
     }
   }
-  float* vout = values + int64_t(q) * width;
-  int* iout = ids + int64_t(q) * width;
   for (int i = tid; i < width; i += kCandThreads) {
     if (i < count) {
       const uint64_t x = sel[i];
-      float v;
-      int idx;
-      if (index_order) {
-        idx = int(x >> 32);
-        v = key_value(uint32_t(x));
-      } else {
-        v = composite_value(~x);
-        idx = composite_index(~x);
-      }
-      vout[i] = v;
-      iout[i] = (__float_as_uint(v) & 0x7FFFFFFFu) >= 0x7F800000u ? -1 : idx;
+      if (index_order) emit(i, key_value(uint32_t(x)), int(x >> 32));
+      else emit(i, composite_value(~x), composite_index(~x));
     } else {
       vout[i] = -INFINITY;
       iout[i] = -1;
@@ -232,7 +342,9 @@ __global__ void __launch_bounds__(kCandThreads) topk_candidates_kernel(
 
 }  // namespace
 
-size_t indexer_select_cand_smem(int cap) { return size_t(cap) * 8 + size_t(1 << kLevelBits) * 4; }
+// Candidates, then 2 x kBitmapKeys / 32 words (bitmap + prefix; also holds
+// the 4096-bin histogram and the kMaxK sort keys).
+size_t indexer_select_cand_smem(int cap) { return size_t(cap) * 8 + size_t(kBitmapKeys / 32) * 4 * 2; }
 
 void launch_indexer_select(const IndexerSelectArgs& a, cudaStream_t stream) {
   const IndexerArgs& x = a.idx;
@@ -256,7 +368,9 @@ void launch_indexer_select(const IndexerSelectArgs& a, cudaStream_t stream) {
                                                               x.query_start, a.k, a.cand_cap, a.thresh);
     cuda_check(cudaGetLastError(), "indexer select threshold launch");
   }
-  cuda_check(cudaMemsetAsync(a.cand_count, 0, size_t(x.Q) * sizeof(int), stream), "indexer select count reset");
+  // Counts and the any-row-flagged word (contiguous: any_flag == cand_count + Q).
+  if (a.any_flag != a.cand_count + x.Q) throw std::invalid_argument("indexer select: any_flag must follow the counts");
+  cuda_check(cudaMemsetAsync(a.cand_count, 0, size_t(x.Q + 1) * sizeof(int), stream), "indexer select count reset");
   IndexerArgs m = x;
   m.key_stride = 1;
   m.row_flags = nullptr;
@@ -271,13 +385,14 @@ void launch_indexer_select(const IndexerSelectArgs& a, cudaStream_t stream) {
              "indexer select candidates smem");
   topk_candidates_kernel<<<x.Q, kCandThreads, smem, stream>>>(a.cand, a.cand_count, a.cand_cap, x.N, x.query_start,
                                                               a.k, a.width, a.values, a.ids, a.flags, a.overflow,
-                                                              a.index_order);
+                                                              a.any_flag, a.index_order);
   cuda_check(cudaGetLastError(), "indexer select candidates launch");
   // Fallback for flagged rows (no work when none is flagged).
   IndexerArgs f = x;
   f.key_stride = 1;
   f.select = false;
   f.row_flags = a.flags;
+  f.any_flag = a.any_flag;
   launch_indexer_logits(f, stream);
   launch_topk_causal(x.logits, x.ldl, x.Q, n_end, a.width, x.query_start, a.values, a.ids, x.err, stream, a.overflow,
                      a.index_order, a.flags);

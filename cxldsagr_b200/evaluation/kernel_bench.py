@@ -173,12 +173,15 @@ def bench_indexer_select(Q=1024, N=65536, k=2048, **_):
         return ops.indexer_select(q, kk, w, ks, start, k, logits_buf=out, order="index")
 
     ref_ids = separate()[1]
-    got_ids = fused()[1]
+    diag = torch.zeros(3, dtype=torch.int64, device=dev)
+    got_ids = ops.indexer_select(q, kk, w, ks, start, k, logits_buf=out, order="index", diag=diag)[1]
     equal = bool(torch.equal(ref_ids, got_ids))
+    redone, kept, most = (int(x) for x in diag.tolist())
     ms_sep = time_fn(separate)
     ms_fused = time_fn(fused)
     return {"op": "indexer_select", "Q": Q, "N": N, "k": k, "ms": ms_fused, "separate_ms": ms_sep,
-            "speedup": ms_sep / ms_fused, "ids_equal": equal}
+            "speedup": ms_sep / ms_fused, "ids_equal": equal, "rows_redone": redone,
+            "candidates_per_row": kept / Q, "max_candidates": most}
 
 
 def bench_topk(R=1024, N=65536, k=2048, clustered=False, order="value", causal=False, **_):

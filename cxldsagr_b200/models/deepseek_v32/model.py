@@ -757,6 +757,10 @@ class ExtendGraph:
             raise ValueError("the dense_prefetch method runs its extend eagerly")
         if len(model.pool_devices) > 1:
             raise ValueError("a model placed over several devices runs its extend eagerly")
+        comm = getattr(model, "comm", None)
+        if comm is not None and getattr(comm, "moe", None) is not None and comm.world > 1:
+            # Its dispatch / combine number their calls on the host, which a replay would repeat.
+            raise ValueError("the expert-parallel exchange runs its extend eagerly")
         self.model, self.T = model, T
         self.session = session or model.session
         self.start = self.session.length

@@ -212,7 +212,7 @@ def indexer_logits(q, k, weights, kscale, query_start: int, *, out=None):
 
 
 def indexer_select(q, keys, weights, kscale, query_start: int, k: int, *, logits_buf=None, order: str = "index",
-                   sample_stride: int = 16, cand_cap: int = 8192):
+                   sample_stride: int = 32, cand_cap: int = 8192, diag=None):
     """Fused indexer + exact top-k: ``exact_topk(indexer_logits(...), k, causal_start=query_start,
     n=len(keys), order=order)`` without the full FP32 logits in HBM.
 
@@ -221,7 +221,8 @@ def indexer_select(q, keys, weights, kscale, query_start: int, k: int, *, logits
     ``cand_cap`` per row) and an exact top-k runs over those candidates; rows
     whose candidates cannot decide the top-k are redone from full logits in
     ``logits_buf`` (allocated when not given).  Returns (values, ids), width
-    min(k, len(keys)).
+    min(k, len(keys)).  ``diag`` (int64 [3], CUDA) receives the rows redone
+    from full logits, the candidates kept and the largest per-row count.
     """
     if order not in ("value", "index"):
         raise ValueError("order must be 'value' or 'index'")
@@ -236,7 +237,7 @@ def indexer_select(q, keys, weights, kscale, query_start: int, k: int, *, logits
     values = torch.empty((Q, width), dtype=torch.float32, device=q.device)
     ids = torch.empty((Q, width), dtype=torch.int32, device=q.device)
     lib().indexer_select(q, keys, weights, kscale, logits_buf, query_start, k, values, ids, order == "index",
-                         sample_stride, max(cand_cap, 2 * k))
+                         sample_stride, max(cand_cap, 2 * k), diag)
     return values, ids
 
 

@@ -45,7 +45,8 @@ class CollectiveTimer:
 
     @contextmanager
     def span(self, name: str):
-        if self._depth or self.device.type != "cuda":
+        # Not timed inside a CUDA-graph capture (replays are timed as a whole).
+        if self._depth or self.device.type != "cuda" or torch.cuda.is_current_stream_capturing():
             yield
             return
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -12,8 +12,13 @@
   (BF16 weights, rows that do not split evenly, buffers too small) fall back
   to the NCCL baseline of the parent class.
 
-Flag counters are cumulative; the host keeps, per op kind, the running
-totals that every rank computes identically (same calls, same shapes).
+Flag counters are cumulative.  For the fused GEMMs and the barrier, each
+rank keeps its op state (calls, arrival and reader-done totals per kind) in a
+small block of its own device memory: a call reads its number, parity and
+flag targets from it at launch and its last CTA advances it, so the host only
+passes the per-call increments, which every rank computes identically from
+the shapes.  The same launches therefore replay correctly from a CUDA graph.
+The expert-parallel exchange keeps host-side call numbers.
 """
 
 from __future__ import annotations
@@ -78,20 +83,8 @@ class SymmetricHeap:
         self.closed = True
 
 
-class _Counter:
-    """Cumulative targets of one op kind: arrivals incl. this call, reuse = total two calls back."""
-
-    def __init__(self):
-        self.calls = 0
-        self.arrive = 0
-        self.done_history = [0]   # cumulative reader-done counts after each call
-
-    def next(self, arrive_inc: int, done_inc: int) -> tuple[int, int, int]:
-        self.calls += 1
-        self.arrive += arrive_inc
-        reuse = self.done_history[self.calls - 2] if self.calls >= 3 else 0
-        self.done_history.append(self.done_history[-1] + done_inc)
-        return self.calls, self.arrive, reuse
+EPOCH_SLOTS = 8                      # u64 per op kind (csrc/common/p2p_args.h kEpochSlots)
+EPOCH_AG, EPOCH_RS, EPOCH_BARRIER = 0, 1, 2
 
 
 class P2PComm(Comm):
@@ -134,15 +127,19 @@ class P2PComm(Comm):
             self.ep_block_expert = torch.full((self.ep_blocks,), -1, dtype=torch.int32, device=dev)
         self.flag_ptrs = self.heap.ptrs(self.off_flags)
         self.g_ptrs, self.gs_ptrs, self.rb_ptrs = (self.heap.ptrs(o) for o in (self.off_g, self.off_gs, self.off_rb))
-        self.ag = _Counter()
-        self.rs = _Counter()
+        # Device-resident op state of the AG, RS and barrier kinds (local memory).
+        self.epoch = torch.zeros(3 * EPOCH_SLOTS, dtype=torch.int64, device=ctx.device)
         self.barriers = 0
         self.fused_calls = {"ag": 0, "rs": 0}
         self.barrier()  # every peer mapped its neighbours' heaps before any kernel writes to them
 
     def barrier(self):
         self.barriers += 1
-        self.lib().p2p_barrier(self.ctx.device.index, self.ctx.rank, self.world, self.barriers, self.flag_ptrs)
+        self.lib().p2p_barrier(self.ctx.device.index, self.ctx.rank, self.world, 0, self.flag_ptrs,
+                               epoch=self._epoch(EPOCH_BARRIER))
+
+    def _epoch(self, kind: int) -> int:
+        return self.epoch.data_ptr() + kind * EPOCH_SLOTS * 8
 
     @staticmethod
     def lib():
@@ -160,10 +157,11 @@ class P2PComm(Comm):
         N = lin.weight.shape[0]
         out = torch.empty((total, N), dtype=torch.bfloat16, device=q.device)
         grid = self.lib().fp8_gemm_ag_grid(total, N, q.shape[1])
-        call, arrive, reuse = self.ag.next(grid, grid)
         with self._span("ag_gemm"):
+            # Every CTA of every rank pushes (arrival) and reads (done) once per call.
             self.lib().fp8_gemm_ag(q.contiguous(), s_t.contiguous(), lin.weight, lin.scales, out, self.ctx.rank,
-                                   self.world, call, arrive, reuse, self.flag_ptrs, self.g_ptrs, self.gs_ptrs)
+                                   self.world, 0, 0, 0, self.flag_ptrs, self.g_ptrs, self.gs_ptrs,
+                                   epoch=self._epoch(EPOCH_AG), arrive_inc=grid, done_inc=grid)
         self.fused_calls["ag"] += 1
         return out
 
@@ -185,11 +183,12 @@ class P2PComm(Comm):
         num_n = (N + bn - 1) // bn
         mblocks = (r * S + S - 1) // 128 - (r * S) // 128 + 1
         rgrid = self.lib().rs_reduce_grid(S, N)
-        call, arrive, reuse = self.rs.next(num_n * mblocks, rgrid)
         out = torch.empty((S, N), dtype=torch.bfloat16, device=q.device)
         with self._span("gemm_rs"):
-            self.lib().fp8_gemm_rs(q, s_t, lin.weight, lin.scales, None, out, r, self.world, call, arrive, reuse,
-                                   self.flag_ptrs, self.rb_ptrs)
+            # Arrivals per source: the tiles covering this rank's rows; done: the owner's reduce CTAs.
+            self.lib().fp8_gemm_rs(q, s_t, lin.weight, lin.scales, None, out, r, self.world, 0, 0, 0,
+                                   self.flag_ptrs, self.rb_ptrs, epoch=self._epoch(EPOCH_RS),
+                                   arrive_inc=num_n * mblocks, done_inc=rgrid)
         self.fused_calls["rs"] += 1
         return out
 

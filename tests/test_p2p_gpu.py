@@ -212,3 +212,52 @@ def test_model_fused_backend_matches_nccl(world):
         # own: the prefill logits agree to BF16 accumulation-order noise.
         assert rep["prefill_corr"] > 0.999
         assert rep["prefill_maxdiff"] <= 5e-2 * rep["prefill_scale"]
+
+
+def _sp_extend_graph(rank, world):
+    """A sequence-parallel extend (AG-GEMM / GEMM-RS, vocabulary-parallel
+    embedding and LM head) captured in one CUDA graph per rank: replays give
+    the eager extend's logits bit for bit, for the fused peer-memory backend
+    (call state in device memory) and for the NCCL baseline."""
+    from cxldsagr_b200.checkpoint import StateDictSource, random_state_dict
+    from cxldsagr_b200.config import CacheConfig, v32_config
+    from cxldsagr_b200.models.deepseek_v32.model import DeepSeekV32Model
+    from cxldsagr_b200.ops.native import check_errors
+    from cxldsagr_b200.parallel.groups import ParallelContext, init_distributed
+
+    base = init_distributed(timeout_s=60, comm="torch")
+    dev = base.device
+    cfg = v32_config(1)
+    src = StateDictSource(random_state_dict(cfg, layers=[0], seed=0, device=dev), cfg)
+    cache = CacheConfig(capacity=2048 + 64, chunk_size=1024, candidate_tokens=64)
+    g = torch.Generator(device=dev).manual_seed(6)
+    ids = torch.randint(0, cfg.vocab_size, (2048 + 64,), generator=g, device=dev)
+    out = {}
+    for backend in ("p2p", "torch"):
+        ctx = base if backend == "torch" else ParallelContext(base.rank, base.world, base.group, dev, backend="p2p")
+        m = DeepSeekV32Model(cfg, src, device=dev, cache=cache, layers=[0], parallel=ctx)
+        m.prefill(ids[:2048])
+        eager = m.extend(ids[2048:]).logits.float().cpu()
+        m.session.truncate(2048)
+        graph = m.capture_extend(64)
+        reps = []
+        for _ in range(3):
+            reps.append(graph.replay(ids[2048:]).float().cpu())
+            graph.rollback()
+        torch.cuda.synchronize()
+        check_errors(dev)
+        del graph
+        out[backend] = all(torch.equal(r, eager) for r in reps)
+        if hasattr(m.comm, "close"):
+            m.comm.close()
+        del m
+    return out
+
+
+@pytest.mark.parametrize("world", [2])
+def test_sp_extend_cuda_graph(world):
+    _need(world)
+    reports = _spawn(_sp_extend_graph, world)
+    for rank, rep in reports.items():
+        print(rank, rep)
+        assert rep["p2p"] and rep["torch"]
