@@ -1,19 +1,46 @@
-"""Cache memory audit: measured storage against the admission plan.
+"""Cache memory audit: fixed cache storage and per-scope transient device memory
+against the admission plan.
 
-Reference: ``evaluation/cache_memory_audit.py:47-887``.  The ledger that admits
-users (``cache.prefix_pool``) reserves bytes from a plan; this audit walks the
-tensors that actually hold cache state (shared pool, sessions, staging,
-workspace), groups them by category and device tier, counts each storage
-once, and reports any category whose measured bytes exceed its reservation.
-The pinned-host allocator rounds up to powers of two, so DRAM is measured as
-charged bytes (``cache.host_allocation.pinned_allocation_bytes``).
+Reference behaviour: ``evaluation/cache_memory_audit.py:47-887`` (an
+allocator-event audit of the cache paths with a workspace allowance per
+transaction).  Three measurements, none of them part of a latency sample:
+
+* **Fixed storage** (:func:`storage_inventory`): the tensors that hold cache
+  state (shared pool, sessions, staging, workspace buffers), grouped by
+  category and tier, each storage counted once.  With a CUDA allocator
+  snapshot the allocator block behind every storage is charged as well, so
+  rounding padding shows; pinned host storage is charged at the caching host
+  allocator's power-of-two size.
+* **Transient memory per scope** (:class:`ScopeMemoryTracker`): installed as a
+  model's ``scope`` hook, it reads the CUDA caching allocator's counters at
+  every scope boundary (host side, no device synchronisation) and records per
+  scope name the peak bytes above the bytes live at entry (nested scopes
+  included), the bytes still live at exit (retained) and the bytes allocated.
+  Peak counters are reset at each boundary and folded into the enclosing
+  scope, so nested scopes do not hide each other's peaks.
+* **Allowance** (:class:`WorkspaceAllowance`): the transient bytes one chunk
+  of one layer may take per component, computed from the buffers this
+  framework's kernels use (fused selection: sampled logits, thresholds,
+  candidate lists, counts, outputs; full-logits selection; MLA output and
+  split-K partials; FP8 recall scratch; pool metadata lists).
+  :func:`audit_scopes` compares the tracker's peaks with it.
+
+What this does not see: memory outside the PyTorch caching allocator (the
+symmetric heap's ``cudaMalloc``, CUDA graph private pools' reuse), CPU malloc
+overhead, and allocator fragmentation beyond block rounding.
+
+CLI::
+
+    python -m cxldsagr_b200.evaluation.cache_memory_audit run.jsonl     # serving log: per-request bytes vs budget
+    python -m cxldsagr_b200.evaluation.cache_memory_audit model --history 16384 --extend 128 --method serial_sparse
 """
 
 from __future__ import annotations
 
 import argparse
 import json
-from dataclasses import dataclass, field
+from contextlib import contextmanager
+from dataclasses import asdict, dataclass, field
 
 import torch
 
@@ -21,6 +48,17 @@ from ..cache.capacity import CacheFootprint
 from ..cache.host_allocation import pinned_allocation_bytes
 
 CATEGORIES = ("shared_pool", "session", "staging", "workspace", "other")
+
+# Scope names of the attention path and the allowance component they draw on.
+SCOPE_COMPONENTS = {
+    "indexer_select": "selection",
+    "indexer": "selection",
+    "exact_topk": "selection",
+    "indexer_cp": "selection",
+    "indexer_prefetch": "selection",
+    "prefetch_hint": "selection",
+    "sparse_mla": "attention",
+}
 
 
 def scope_category(name: str) -> str:
@@ -30,23 +68,44 @@ def scope_category(name: str) -> str:
     return "other"
 
 
-def storage_inventory(tensors: dict) -> dict:
-    """{category: {"hbm": bytes, "dram": bytes}} over distinct storages (aliases counted once)."""
+# ------------------------------------------------------------ fixed storage
+def allocator_blocks(snapshot) -> dict:
+    """(device, address) -> allocator block bytes of every active allocation in a
+    ``torch.cuda.memory_snapshot()``."""
+    blocks = {}
+    for seg in snapshot or ():
+        addr = seg["address"]
+        for blk in seg["blocks"]:
+            start = blk.get("address", addr)
+            if blk["state"] == "active_allocated":
+                blocks[(f"cuda:{seg['device']}", start)] = blk["size"]
+            addr = start + blk["size"]
+    return blocks
+
+
+def storage_inventory(tensors: dict, *, snapshot=None) -> dict:
+    """{category: {"hbm", "hbm_allocator", "dram"}} over distinct storages (aliases counted once).
+
+    ``hbm_allocator`` charges the caching allocator's block for each CUDA
+    storage when a snapshot is given (else the storage size)."""
+    blocks = allocator_blocks(snapshot) if snapshot is not None else {}
     seen = set()
-    out = {c: {"hbm": 0, "dram": 0} for c in CATEGORIES}
+    out = {c: {"hbm": 0, "hbm_allocator": 0, "dram": 0} for c in CATEGORIES}
     for name, t in tensors.items():
         if t is None:
             continue
         st = t.untyped_storage()
         key = (str(t.device), st.data_ptr())
-        if key in seen:
+        if key in seen or st.nbytes() == 0:
             continue
         seen.add(key)
         n = st.nbytes()
+        row = out[scope_category(name)]
         if t.device.type == "cuda":
-            out[scope_category(name)]["hbm"] += n
+            row["hbm"] += n
+            row["hbm_allocator"] += max(n, blocks.get(key, n))
         else:
-            out[scope_category(name)]["dram"] += pinned_allocation_bytes(n) if t.is_pinned() else n
+            row["dram"] += pinned_allocation_bytes(n) if t.is_pinned() else n
     return out
 
 
@@ -87,9 +146,10 @@ class CacheMemoryAudit:
             res = self.reservations.get(cat)
             if res is None:
                 continue
-            if not CacheFootprint(used["hbm"], used["dram"]).fits(res):
+            hbm = max(used["hbm"], used.get("hbm_allocator", 0))
+            if not CacheFootprint(hbm, used["dram"]).fits(res):
                 violations.append({"category": cat, "used": used, "reserved": {"hbm": res.hbm, "dram": res.dram}})
-        total = {"hbm": sum(v["hbm"] for v in inventory.values()), "dram": sum(v["dram"] for v in inventory.values())}
+        total = {t: sum(v.get(t, 0) for v in inventory.values()) for t in ("hbm", "hbm_allocator", "dram")}
         return {"inventory": inventory, "total": total, "violations": violations, "ok": not violations}
 
 
@@ -102,13 +162,144 @@ def cuda_allocator_snapshot(device=None) -> dict:
                                      "reserved_bytes.all.current", "reserved_bytes.all.peak")}
 
 
-def main(argv=None):
-    p = argparse.ArgumentParser(description="Audit a serving run's JSONL output: per-request cache bytes vs budget.")
-    p.add_argument("jsonl", help="output of python -m cxldsagr_b200.serving.run_multi_user")
-    a = p.parse_args(argv)
+# ------------------------------------------------------------ allowances
+def _c4(n: int) -> int:
+    return max(4, (n + 3) // 4 * 4)
+
+
+@dataclass(frozen=True)
+class WorkspaceAllowance:
+    """Transient device bytes one chunk of one layer may hold, per component.
+
+    The components are additive admission terms; scopes are attribution only
+    (a scope's peak is compared with the component it draws on)."""
+
+    selection: int      # indexer + exact top-k working set
+    attention: int      # MLA query projection, output, split-K partials, recall scratch
+    metadata: int       # pool classify / map lists of one step
+
+    @property
+    def total(self) -> int:
+        return self.selection + self.attention + self.metadata
+
+    @classmethod
+    def for_chunk(cls, cfg, *, queries: int, context: int, method: str = "hbm", kv_format: str = "bf16",
+                  fused_select: bool = True, logits_preallocated: bool = True, cand_cap: int = 8192,
+                  sample_stride: int = 32, splits: int = 1, offload: bool = False) -> "WorkspaceAllowance":
+        if min(queries, context) < 1:
+            raise ValueError("queries and context must be positive")
+        k = cfg.index_topk
+        width = min(k, context)
+        out_ids = queries * width * 8                      # values FP32 + ids int32
+        if fused_select and method != "echo":
+            sel = (queries * _c4(-(-context // sample_stride)) * 4   # sampled logits
+                   + queries * 4                                     # thresholds
+                   + queries * max(cand_cap, 2 * k) * 8              # candidate composites
+                   + (queries + 1) * 4 + 2 * queries * 4             # counts + any-flag, flags, overflow
+                   + out_ids)
+        else:
+            sel = out_ids + queries * 4                              # outputs + two-pass overflow words
+            if method == "echo":
+                sel += context * 4                                   # predicted-row list
+        if not logits_preallocated:
+            sel += queries * _c4(context) * 4                        # [Q, N] FP32 logits (or fallback rows)
+        H, D = cfg.n_heads, cfg.kv_lora_rank
+        qk = D + cfg.qk_rope_head_dim
+        att = queries * H * qk * 2 + queries * H * D * 2             # absorbed query, latent output (BF16)
+        if splits > 1:
+            att += splits * queries * H * (D + 1) * 4                # FP32 partial outputs + LSE
+        meta = 0
+        if offload:
+            rows = queries * width
+            att += rows * 4                                          # physical slot ids
+            if kv_format == "fp8":
+                att += min(rows, context) * 656                      # 656-byte records gathered before dequant
+            meta = 3 * rows * 4                                      # classify / select / map lists
+        return cls(int(sel), int(att), int(meta))
+
+
+# ------------------------------------------------------------ transient tracker
+@dataclass
+class ScopeMemory:
+    calls: int = 0
+    peak_transient: int = 0     # max over calls: peak live bytes above the bytes live at entry
+    retained: int = 0           # sum over calls: bytes still live at exit beyond entry
+    allocated: int = 0          # sum over calls: bytes handed out inside the scope
+
+
+class ScopeMemoryTracker:
+    """Per-scope allocator accounting from the caching allocator's counters.
+
+    ``stats_fn`` returns a dict with ``allocated_bytes.all.current``,
+    ``allocated_bytes.all.peak`` and ``allocated_bytes.all.allocated``;
+    ``reset_fn`` sets the peak to the current value (defaults: the CUDA
+    allocator of ``device``).  Use :meth:`scope` as the model's scope hook."""
+
+    CUR, PEAK, CUM = "allocated_bytes.all.current", "allocated_bytes.all.peak", "allocated_bytes.all.allocated"
+
+    def __init__(self, device=None, *, stats_fn=None, reset_fn=None):
+        self.stats_fn = stats_fn or (lambda: torch.cuda.memory_stats(device))
+        self.reset_fn = reset_fn or (lambda: torch.cuda.reset_peak_memory_stats(device))
+        self._stack: list[list] = []     # [name, entry_current, running_peak, entry_cumulative]
+        self.rows: dict[str, ScopeMemory] = {}
+
+    def _enter(self, name: str):
+        s = self.stats_fn()
+        if self._stack:
+            top = self._stack[-1]
+            top[2] = max(top[2], s[self.PEAK])
+        self.reset_fn()
+        self._stack.append([name, s[self.CUR], s[self.CUR], s[self.CUM]])
+
+    def _exit(self):
+        s = self.stats_fn()
+        name, entry, peak, cum = self._stack.pop()
+        peak = max(peak, s[self.PEAK])
+        row = self.rows.setdefault(name, ScopeMemory())
+        row.calls += 1
+        row.peak_transient = max(row.peak_transient, peak - entry)
+        row.retained += s[self.CUR] - entry
+        row.allocated += s[self.CUM] - cum
+        if self._stack:
+            self._stack[-1][2] = max(self._stack[-1][2], peak)
+        self.reset_fn()
+
+    @contextmanager
+    def scope(self, name: str):
+        self._enter(name)
+        try:
+            yield
+        finally:
+            self._exit()
+
+    def __call__(self, name: str):
+        return self.scope(name)
+
+    def summary(self) -> dict:
+        return {n: asdict(r) for n, r in sorted(self.rows.items())}
+
+
+def audit_scopes(rows: dict, allowance: WorkspaceAllowance, *, mapping=None) -> dict:
+    """Compare each mapped scope's peak transient with its allowance component."""
+    mapping = SCOPE_COMPONENTS if mapping is None else mapping
+    limits = asdict(allowance)
+    checked, violations = {}, []
+    for name, row in rows.items():
+        comp = mapping.get(name)
+        if comp is None:
+            continue
+        peak = row["peak_transient"] if isinstance(row, dict) else row.peak_transient
+        checked[name] = {"component": comp, "peak_transient": peak, "allowance": limits[comp]}
+        if peak > limits[comp]:
+            violations.append(name)
+    return {"checked": checked, "violations": violations, "ok": not violations, "allowance": limits}
+
+
+# ------------------------------------------------------------ CLI
+def audit_serving_log(path: str) -> int:
     worst, n = {"hbm": 0, "dram": 0}, 0
     violations = []
-    with open(a.jsonl) as f:
+    with open(path) as f:
         for line in f:
             row = json.loads(line)
             if row.get("status") != "completed":
@@ -124,6 +315,72 @@ def main(argv=None):
     print(json.dumps({"requests": n, "peak_request_cache_bytes": worst, "violations": violations,
                       "ok": not violations}))
     return 0 if not violations else 1
+
+
+def audit_model(a) -> int:
+    """Prefill + extend of a random-init V3.2 model under the tracker (CUDA)."""
+    from ..checkpoint import RandomSource
+    from ..config import CacheConfig, v32_config
+    from ..models.deepseek_v32.model import DeepSeekV32Model
+
+    dev = torch.device(a.device)
+    cfg = v32_config(layers=a.layers)
+    H, A = a.history, a.extend
+    offload = a.method in ("serial_sparse", "echo")
+    cache = CacheConfig(method=a.method, capacity=H + A, chunk_size=a.chunk, candidate_tokens=A,
+                        pool_tokens=(H + A) if offload else None, host_tokens=H + A, kv_format=a.kv_format)
+    model = DeepSeekV32Model(cfg, RandomSource(cfg, layers=range(a.layers), seed=0, device=dev), device=dev,
+                             cache=cache)
+    g = torch.Generator().manual_seed(11)
+    hist = torch.randint(0, cfg.vocab_size, (H,), generator=g).to(dev)
+    ext = torch.randint(0, cfg.vocab_size, (A,), generator=g).to(dev)
+    model.prefill(hist)            # warm-up: kernels, cached buffers
+    model.reset()
+    torch.cuda.synchronize(dev)
+    report = {}
+    for phase, fn, queries, context in (("prefill", lambda: model.prefill(hist), min(a.chunk, H), H),
+                                        ("extend", lambda: model.extend(ext), A, H + A)):
+        tracker = ScopeMemoryTracker(dev)
+        model.scope = tracker
+        fn()
+        model.scope = None
+        torch.cuda.synchronize(dev)
+        from ..ops import mla_splits
+
+        allowance = WorkspaceAllowance.for_chunk(cfg, queries=queries, context=context, method=a.method,
+                                                 kv_format=a.kv_format, offload=offload,
+                                                 splits=mla_splits(queries, min(cfg.index_topk, context)))
+        rows = tracker.summary()
+        report[phase] = {"scopes": rows, "audit": audit_scopes(rows, allowance)}
+    inv = storage_inventory(model_cache_tensors(model, [model.session]), snapshot=torch.cuda.memory_snapshot())
+    report["fixed"] = CacheMemoryAudit().check(inv)
+    report["allocator"] = cuda_allocator_snapshot(dev)
+    report["config"] = {"history": H, "extend": A, "method": a.method, "layers": a.layers, "chunk": a.chunk,
+                        "kv_format": a.kv_format}
+    ok = report["prefill"]["audit"]["ok"] and report["extend"]["audit"]["ok"]
+    report["ok"] = ok
+    print(json.dumps(report))
+    return 0 if ok else 1
+
+
+def main(argv=None):
+    import sys
+
+    argv = list(sys.argv[1:] if argv is None else argv)
+    if argv and argv[0] == "model":
+        p = argparse.ArgumentParser(prog="cache_memory_audit model",
+                                    description="per-scope transient memory of a model step vs the allowance")
+        p.add_argument("--history", type=int, default=16384)
+        p.add_argument("--extend", type=int, default=128)
+        p.add_argument("--chunk", type=int, default=2048)
+        p.add_argument("--layers", type=int, default=3)
+        p.add_argument("--method", default="hbm", choices=("hbm", "serial_sparse", "echo", "dense_prefetch"))
+        p.add_argument("--kv-format", choices=("bf16", "fp8"), default="bf16")
+        p.add_argument("--device", default="cuda:0")
+        return audit_model(p.parse_args(argv[1:]))
+    p = argparse.ArgumentParser(description="Audit a serving run's JSONL output: per-request cache bytes vs budget.")
+    p.add_argument("jsonl", help="output of python -m cxldsagr_b200.serving.run_multi_user")
+    return audit_serving_log(p.parse_args(argv).jsonl)
 
 
 if __name__ == "__main__":

@@ -14,11 +14,20 @@ measurement.  Times are CUDA events on the launching stream, minimum over
 ``--reps`` replays after the capture's warm-up.
 
     python -m cxldsagr_b200.evaluation.shape_matrix --histories 16384,65536 --extends 128,1024
+
+Check and bench are separate runs (the reference's receipt workflow,
+``evaluation/motivation_validation.py:36-231``): ``--mode check`` runs every
+cell once, requires each method's cold-extend logits to equal the resident
+``hbm`` logits bit for bit, and writes a check receipt bound to the source
+tree, the loaded native build and the matrix configuration; ``--mode bench``
+(the default when ``--receipt`` is given) refuses to time anything unless
+that receipt matches, and publishes no numbers from an unchecked build.
 """
 
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 
 import torch
@@ -40,6 +49,42 @@ METHODS = ("hbm", "serial_sparse", "echo", "dense_prefetch")
 
 def _ints(text: str) -> list[int]:
     return [int(x) for x in text.split(",") if x]
+
+
+def check_history(H: int, extends: list[int], methods, *, layers: int, kv_format: str, dev) -> dict:
+    """One cold extend per (method, A): logits digests and bitwise equality with hbm."""
+    from ..checkpoint import RandomSource
+    from ..config import CacheConfig, v32_config
+    from ..models.deepseek_v32.model import DeepSeekV32Model
+    cfg = v32_config(layers=layers)
+    cap = H + max(extends)
+    src = RandomSource(cfg, layers=range(layers), seed=0, device=dev)
+    model = DeepSeekV32Model(cfg, src, device=dev,
+                             cache=CacheConfig(method="hbm", capacity=cap, chunk_size=2048, candidate_tokens=max(extends),
+                                               host_tokens=cap, kv_format=kv_format))
+    del src
+    g = torch.Generator().manual_seed(H)
+    hist = torch.randint(0, cfg.vocab_size, (H,), generator=g).to(dev)
+    cands = {A: torch.randint(0, cfg.vocab_size, (A,), generator=g).to(dev) for A in extends}
+    out, ref = {}, {}
+    for method in ("hbm",) + tuple(m for m in methods if m != "hbm"):
+        if method != model.cache_cfg.method:
+            model.set_cache_method(method, pool_tokens=cap, host_tokens=cap, kv_format=kv_format)
+        model.reset()
+        model.prefill(hist)
+        for A in extends:
+            model.clear_residency()
+            logits = model.extend(cands[A]).logits.float().cpu()
+            model.session.truncate(H)
+            if method == "hbm":
+                ref[A] = logits
+            key = f"H{H}/A{A}/{method}"
+            out[key] = {"logits_sha256": hashlib.sha256(logits.numpy().tobytes()).hexdigest(),
+                        "equal_to_hbm": bool(torch.equal(logits, ref[A])),
+                        "finite": bool(torch.isfinite(logits).all())}
+    del model
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_history(H: int, extends: list[int], methods, *, layers: int, kv_format: str, reps: int, dev) -> list[dict]:
@@ -119,13 +164,39 @@ def main(argv=None):
     p.add_argument("--kv-format", choices=("bf16", "fp8"), default="bf16")
     p.add_argument("--reps", type=int, default=3)
     p.add_argument("--device", default="cuda:0")
+    p.add_argument("--mode", choices=("check", "bench"), default=None,
+                   help="check: bitwise method agreement + receipt; bench: timing, requires a check receipt")
+    p.add_argument("--receipt", default=None, help="receipt path (written by check, required by bench)")
     a = p.parse_args(argv)
-    dev = torch.device(a.device)
-    torch.cuda.set_device(dev)
     methods = [m for m in a.methods.split(",") if m]
     for m in methods:
         if m not in METHODS:
             raise SystemExit(f"unknown method {m}")
+    from . import validation
+
+    mode = a.mode or ("bench" if a.receipt else None)
+    ident = {"harness": "shape_matrix", "histories": _ints(a.histories), "extends": _ints(a.extends),
+             "methods": methods, "layers": a.layers, "kv_format": a.kv_format}
+    if mode == "bench":
+        if not a.receipt:
+            raise SystemExit("--mode bench needs the --receipt of a check run")
+        validation.require_receipt(a.receipt, "check", ident)   # before any device work
+    dev = torch.device(a.device)
+    torch.cuda.set_device(dev)
+    if mode == "check":
+        if not a.receipt:
+            raise SystemExit("--mode check needs --receipt PATH to write")
+        evidence = {}
+        for H in _ints(a.histories):
+            evidence.update(check_history(H, _ints(a.extends), methods, layers=a.layers, kv_format=a.kv_format,
+                                          dev=dev))
+        bad = [k for k, v in evidence.items() if not (v["equal_to_hbm"] and v["finite"])]
+        if bad:
+            print(json.dumps({"check": "failed", "cells": bad}))
+            return 1
+        validation.write_receipt(a.receipt, "check", ident, evidence)
+        print(json.dumps({"check": "passed", "cells": len(evidence), "receipt": a.receipt}))
+        return 0
     rows = []
     for H in _ints(a.histories):
         rows += run_history(H, _ints(a.extends), methods, layers=a.layers, kv_format=a.kv_format, reps=a.reps,
@@ -133,7 +204,8 @@ def main(argv=None):
         for r in rows[-len(methods) * len(_ints(a.extends)):]:
             print(json.dumps(r), flush=True)
     print(table(rows))
+    return 0
 
 
 if __name__ == "__main__":
-    main()
+    raise SystemExit(main())

@@ -49,6 +49,84 @@ def test_storage_inventory_counts_storages_once():
     assert not rep["ok"] and rep["violations"][0]["category"] == "session"
 
 
+class _FakeAllocator:
+    """Caching-allocator counters driven by the test (current, peak, cumulative)."""
+
+    def __init__(self):
+        self.cur = self.peak = self.cum = 0
+
+    def alloc(self, n):
+        self.cur += n
+        self.cum += n
+        self.peak = max(self.peak, self.cur)
+
+    def free(self, n):
+        self.cur -= n
+
+    def stats(self):
+        return {"allocated_bytes.all.current": self.cur, "allocated_bytes.all.peak": self.peak,
+                "allocated_bytes.all.allocated": self.cum}
+
+    def reset(self):
+        self.peak = self.cur
+
+
+def test_scope_memory_tracker_nested_peaks():
+    fa = _FakeAllocator()
+    tr = audit.ScopeMemoryTracker(stats_fn=fa.stats, reset_fn=fa.reset)
+    fa.alloc(1000)                      # live before any scope
+    with tr("attention"):
+        fa.alloc(100)
+        with tr("indexer_select"):
+            fa.alloc(500)
+            fa.free(500)
+        fa.alloc(50)                    # retained by attention
+        with tr("sparse_mla"):
+            fa.alloc(200)
+            fa.free(200)
+        fa.free(100)
+    with tr("indexer_select"):
+        fa.alloc(700)
+        fa.free(700)
+    rows = tr.summary()
+    assert rows["indexer_select"] == {"calls": 2, "peak_transient": 700, "retained": 0, "allocated": 1200}
+    assert rows["sparse_mla"]["peak_transient"] == 200
+    # the child's peak (1000 + 100 + 500) counts for the enclosing scope
+    assert rows["attention"]["peak_transient"] == 600 and rows["attention"]["retained"] == 50
+    al = audit.WorkspaceAllowance(selection=600, attention=10_000, metadata=0)
+    rep = audit.audit_scopes(rows, al)
+    assert rep["violations"] == ["indexer_select"] and not rep["ok"]
+    assert rep["checked"]["sparse_mla"]["component"] == "attention"
+
+
+def test_workspace_allowance_terms():
+    from cxldsagr_b200.config import v32_config
+
+    cfg = v32_config(1)
+    fused = audit.WorkspaceAllowance.for_chunk(cfg, queries=2048, context=65536)
+    plain = audit.WorkspaceAllowance.for_chunk(cfg, queries=2048, context=65536, fused_select=False)
+    cands = 2048 * 8192 * 8
+    assert fused.selection - plain.selection >= cands                  # candidate lists dominate
+    assert fused.selection < cands + 2048 * 65536 * 4 // 8             # far below a logits buffer
+    no_buf = audit.WorkspaceAllowance.for_chunk(cfg, queries=2048, context=65536, logits_preallocated=False)
+    assert no_buf.selection - fused.selection == 2048 * 65536 * 4
+    split = audit.WorkspaceAllowance.for_chunk(cfg, queries=1, context=65536, splits=8)
+    one = audit.WorkspaceAllowance.for_chunk(cfg, queries=1, context=65536)
+    assert split.attention - one.attention == 8 * 128 * 513 * 4
+    fp8 = audit.WorkspaceAllowance.for_chunk(cfg, queries=128, context=65664, offload=True, kv_format="fp8")
+    bf16 = audit.WorkspaceAllowance.for_chunk(cfg, queries=128, context=65664, offload=True)
+    assert fp8.attention - bf16.attention == 65664 * 656 and fp8.metadata == 3 * 128 * 2048 * 4
+    with pytest.raises(ValueError):
+        audit.WorkspaceAllowance.for_chunk(cfg, queries=0, context=10)
+
+
+def test_allocator_blocks_charge_padding():
+    snap = [{"device": 0, "address": 4096, "blocks": [
+        {"size": 512, "state": "active_allocated"}, {"size": 1536, "state": "inactive"},
+        {"size": 2048, "state": "active_allocated"}]}]
+    assert audit.allocator_blocks(snap) == {("cuda:0", 4096): 512, ("cuda:0", 6144): 2048}
+
+
 def test_model_cache_inventory_and_audit_cli(tmp_path):
     from cxldsagr_b200.checkpoint import StateDictSource, random_state_dict
     from cxldsagr_b200.config import CacheConfig, tiny_config
@@ -155,3 +233,19 @@ def test_shape_matrix_table_and_reference_cells():
     assert "| 16384 | 128 | hbm | 100.0 | 1.500 | 2.623 | 1.75x |" in text
     assert set(sm.REFERENCE_H200[(65536, 128)]) == set(sm.METHODS)
     assert sm._ints("4096,16384") == [4096, 16384]
+
+
+def test_shape_matrix_bench_requires_matching_check_receipt(tmp_path):
+    from cxldsagr_b200.evaluation import shape_matrix as sm
+    from cxldsagr_b200.evaluation import validation as val
+
+    args = ["--histories", "4096", "--extends", "128", "--methods", "hbm,serial_sparse", "--layers", "1"]
+    with pytest.raises(SystemExit):
+        sm.main(args + ["--mode", "bench"])
+    with pytest.raises(FileNotFoundError):
+        sm.main(args + ["--mode", "bench", "--receipt", str(tmp_path / "none.json")])
+    other = {"harness": "shape_matrix", "histories": [4096], "extends": [128], "methods": ["hbm"], "layers": 1,
+             "kv_format": "bf16"}
+    val.write_receipt(tmp_path / "r.json", "check", other, {"H4096/A128/hbm": {"equal_to_hbm": True}})
+    with pytest.raises(ValueError):  # receipt of another method list
+        sm.main(args + ["--receipt", str(tmp_path / "r.json")])

@@ -734,3 +734,23 @@ def test_model_fp8_records_offload_matches_resident(method):
         del m
     ops.check_errors(DEV)
     assert torch.equal(out["hbm"][0], out[method][0]) and torch.equal(out["hbm"][1], out[method][1])
+
+
+@pytest.mark.parametrize("method,kv_format", [("hbm", "bf16"), ("serial_sparse", "fp8")])
+def test_cache_memory_audit_model(method, kv_format, capsys):
+    """Per-scope transient memory of a real prefill + extend stays inside the
+    workspace allowance of the selection and attention paths."""
+    import argparse
+    import json
+
+    from cxldsagr_b200.evaluation import cache_memory_audit as audit
+
+    a = argparse.Namespace(history=4096, extend=64, chunk=2048, layers=1, method=method, kv_format=kv_format,
+                           device=DEV)
+    rc = audit.audit_model(a)
+    rep = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    for phase in ("prefill", "extend"):
+        checked = rep[phase]["audit"]["checked"]
+        assert "sparse_mla" in checked and ("indexer_select" in checked or "indexer" in checked), checked
+    assert rc == 0, {p: rep[p]["audit"] for p in ("prefill", "extend")}
+    assert rep["fixed"]["total"]["hbm"] > 0
