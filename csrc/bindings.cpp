@@ -622,7 +622,8 @@ void fp8_gemm_grouped(const Tensor& a, const Tensor& a_s, const Tensor& w, const
 
 b200::EpArgs make_ep(int64_t rank, int64_t world, int64_t E, int64_t D, int64_t topk, int64_t T, int64_t M_pad,
                      int64_t call, const std::vector<int64_t>& flags, const std::vector<int64_t>& cnt,
-                     const std::vector<int64_t>& a, const std::vector<int64_t>& as, const std::vector<int64_t>& y) {
+                     const std::vector<int64_t>& a, const std::vector<int64_t>& as, const std::vector<int64_t>& y,
+                     const std::vector<int64_t>& rsrc) {
   if (world < 1 || world > b200::kMaxRanks || int64_t(flags.size()) != world) throw std::invalid_argument("ep: bad world");
   b200::EpArgs p;
   p.rank = int(rank);
@@ -641,6 +642,7 @@ b200::EpArgs make_ep(int64_t rank, int64_t world, int64_t E, int64_t D, int64_t 
     p.a[q] = reinterpret_cast<uint8_t*>(a[q]);
     p.as[q] = reinterpret_cast<float*>(as[q]);
     p.y[q] = reinterpret_cast<__nv_bfloat16*>(y[q]);
+    if (!rsrc.empty()) p.rsrc[q] = reinterpret_cast<int*>(rsrc[q]);
   }
   return p;
 }
@@ -648,25 +650,55 @@ b200::EpArgs make_ep(int64_t rank, int64_t world, int64_t E, int64_t D, int64_t 
 void ep_dispatch(const Tensor& ids, const Tensor& q, const Tensor& s_t, Tensor& cursor, Tensor& pos_out,
                  Tensor& block_expert, int64_t rank, int64_t world, int64_t E, int64_t M_pad, int64_t call,
                  const std::vector<int64_t>& flags, const std::vector<int64_t>& cnt, const std::vector<int64_t>& a,
-                 const std::vector<int64_t>& as, const std::vector<int64_t>& y) {
+                 const std::vector<int64_t>& as, const std::vector<int64_t>& y, const std::vector<int64_t>& rsrc,
+                 const c10::optional<Tensor>& block_valid) {
   c10::cuda::CUDAGuard guard(q.device());
   TORCH_CHECK(ids.dtype() == torch::kInt32 && ids.is_contiguous() && q.is_contiguous(), "ep_dispatch: layouts");
-  auto p = make_ep(rank, world, E, q.size(1), ids.size(1), ids.size(0), M_pad, call, flags, cnt, a, as, y);
+  if (block_valid) TORCH_CHECK(block_valid->numel() == block_expert.numel(), "ep_dispatch: block_valid size");
+  auto p = make_ep(rank, world, E, q.size(1), ids.size(1), ids.size(0), M_pad, call, flags, cnt, a, as, y, rsrc);
   b200::launch_ep_dispatch(p, ids.data_ptr<int>(), reinterpret_cast<const uint8_t*>(q.data_ptr()), s_t.data_ptr<float>(),
                            int(s_t.stride(0)), cursor.data_ptr<int>(), pos_out.data_ptr<int>(),
                            block_expert.data_ptr<int>(), int(block_expert.numel()), err_ptr(q),
-                           at::cuda::getCurrentCUDAStream());
+                           at::cuda::getCurrentCUDAStream(), block_valid ? block_valid->data_ptr<int>() : nullptr);
 }
 
 void ep_combine(const Tensor& ids, const Tensor& pos, const Tensor& w, Tensor& out, int64_t rank, int64_t world,
                 int64_t E, int64_t M_pad, int64_t call, const std::vector<int64_t>& flags,
                 const std::vector<int64_t>& cnt, const std::vector<int64_t>& a, const std::vector<int64_t>& as,
-                const std::vector<int64_t>& y) {
+                const std::vector<int64_t>& y, const std::vector<int64_t>& rsrc, bool push) {
   c10::cuda::CUDAGuard guard(out.device());
-  auto p = make_ep(rank, world, E, out.size(1), ids.size(1), ids.size(0), M_pad, call, flags, cnt, a, as, y);
+  auto p = make_ep(rank, world, E, out.size(1), ids.size(1), ids.size(0), M_pad, call, flags, cnt, a, as, y, rsrc);
   b200::launch_ep_combine(p, ids.data_ptr<int>(), pos.data_ptr<int>(), w.data_ptr<float>(),
                           reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), err_ptr(out),
-                          at::cuda::getCurrentCUDAStream());
+                          at::cuda::getCurrentCUDAStream(), push);
+}
+
+// Down projection of the expert-parallel MoE that pushes every row to its
+// source rank's receive slot (call parity half) and raises the ready flags.
+void fp8_gemm_grouped_push(const Tensor& a, const Tensor& a_s, const Tensor& w, const Tensor& w_s,
+                           const Tensor& block_expert, const Tensor& block_valid, int64_t row_src,
+                           const std::vector<int64_t>& dst, const std::vector<int64_t>& flags, Tensor& finish,
+                           int64_t rank, int64_t world) {
+  c10::cuda::CUDAGuard guard(a.device());
+  TORCH_CHECK(w.dim() == 3 && w.is_contiguous() && w_s.is_contiguous(), "grouped push: stacked expert weights");
+  TORCH_CHECK(int64_t(dst.size()) == world && int64_t(flags.size()) == world, "grouped push: peer lists");
+  TORCH_CHECK(block_valid.numel() * 128 >= a.size(0) && finish.dtype() == torch::kInt32, "grouped push: tables");
+  b200::EpPushArgs push;
+  push.row_src = reinterpret_cast<const int*>(row_src);
+  push.block_valid = block_valid.data_ptr<int>();
+  push.finish = reinterpret_cast<unsigned int*>(finish.data_ptr<int>());
+  push.ld = int(w.size(1));
+  push.rank = int(rank);
+  push.world = int(world);
+  for (int q = 0; q < world; ++q) {
+    push.dst[q] = reinterpret_cast<__nv_bfloat16*>(dst[q]);
+    push.flags[q] = reinterpret_cast<uint64_t*>(flags[q]);
+  }
+  b200::launch_fp8_gemm_grouped(reinterpret_cast<const uint8_t*>(a.data_ptr()), a_s.data_ptr<float>(),
+                                int(a_s.stride(0)), reinterpret_cast<const uint8_t*>(w.data_ptr()),
+                                w_s.data_ptr<float>(), block_expert.data_ptr<int>(), int(a.size(0)), int(w.size(1)),
+                                int(a.size(1)), int(w.size(0)), nullptr, int(w.size(1)), err_ptr(a),
+                                at::cuda::getCurrentCUDAStream(), &push);
 }
 
 b200::P2PArgs make_p2p(int64_t rank, int64_t world, int64_t S, int64_t call, int64_t arrive_target,
@@ -827,6 +859,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("arrive_target"), py::arg("reuse_target"), py::arg("flags"), py::arg("rb"),
         py::arg("epoch") = int64_t(0), py::arg("arrive_inc") = int64_t(0), py::arg("done_inc") = int64_t(0));
   m.def("set_fp8_gemm_pair_tiles", &b200::set_fp8_gemm_pair_tiles);
+  m.def("set_decode_gemv", &b200::set_decode_gemv);
   m.def("p2p_barrier", &p2p_barrier, py::arg("device"), py::arg("rank"), py::arg("world"), py::arg("call"),
         py::arg("flags"), py::arg("wait_ns") = int64_t(2000000000), py::arg("epoch") = int64_t(0));
   m.def("sparse_mla_2sm_trace", &sparse_mla_2sm_trace);
@@ -837,6 +870,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_gather", &moe_gather);
   m.def("moe_combine", &moe_combine);
   m.def("fp8_gemm_grouped", &fp8_gemm_grouped);
+  m.def("fp8_gemm_grouped_push", &fp8_gemm_grouped_push);
   m.def("fp8_gemm_ag_grid", [](int64_t M, int64_t N, int64_t K) {
     return int64_t(b200::fp8_gemm_ag_grid(int(M), int(N), int(K)));
   });

@@ -76,7 +76,9 @@ struct EpArgs {
   int* cnt[kMaxRanks] = {};      // [2][world][E] int32 per rank
   uint8_t* a[kMaxRanks] = {};    // [2][M_pad][D] fp8
   float* as[kMaxRanks] = {};     // [2][D/128][M_pad] fp32
-  __nv_bfloat16* y[kMaxRanks] = {};  // [2][M_pad][D] bf16
+  __nv_bfloat16* y[kMaxRanks] = {};  // [2][M_pad][D] bf16: pull mode the owner's expert outputs,
+                                     // push mode this rank's receive slots (row = t * topk + k)
+  int* rsrc[kMaxRanks] = {};     // [2][M_pad] int32: (source << 24) | source row of each grouped row
   uint64_t* flags[kMaxRanks] = {};
 };
 

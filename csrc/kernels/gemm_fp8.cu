@@ -79,8 +79,11 @@ void launch_fp8_gemm_pair_t(const FP8GemmArgs& a, int splits, cudaStream_t strea
 // tiles for every prefill shape (the per-K-block promotion, not the operand
 // feed, limits the promotion path).
 bool g_pair_tiles = false;
+bool g_decode_gemv = true;
 
 }  // namespace
+
+void set_decode_gemv(bool enabled) { g_decode_gemv = enabled; }
 
 void set_fp8_gemm_pair_tiles(bool enabled) { g_pair_tiles = enabled; }
 
@@ -156,6 +159,12 @@ int fp8_gemm_launch_splits(int M, int N, int K, int max_splits, bool ue8m0) {
 void launch_fp8_gemm(const FP8GemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return;
   if (a.K % 16) throw std::invalid_argument("fp8 gemm: K must be a multiple of 16");
+  if (g_decode_gemv && gemv_fits(a.M, a.K, a.lda, a.ldb, a.A, a.B)) {
+    // A few rows: the tile kernel's 128-row MMA would stream the weights with
+    // mostly empty tiles; the GEMV streams them at HBM rate on the CUDA cores.
+    launch_fp8_gemv(a, stream);
+    return;
+  }
   if (!a.ue8m0 && g_pair_tiles && a.M >= 2 * BM) {
     const FP8GemmPlan pp = plan_fp8_gemm_pair(a.M, a.N, a.K, a.partial ? a.max_splits : 1);
     if (pp.bn == 256) launch_fp8_gemm_pair_t<256, 6>(a, 1, stream);

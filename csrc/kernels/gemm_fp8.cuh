@@ -65,6 +65,17 @@ constexpr int kModePlain = 0, kModeAG = 1, kModeRS = 2, kModeGrouped = 3;
 struct GroupArgs {
   const int* mblock_expert = nullptr;
   int64_t sfb_expert_stride = 0;   // floats per expert in sfb
+  // Expert-parallel push (down projection): grouped row m goes to rank
+  // (row_src[m] >> 24)'s receive slot (row_src[m] & 0xFFFFFF) instead of out;
+  // rows of block b at or past block_valid[b] are padding.  After its last
+  // tile the kernel's last CTA raises kFlagEpReady + rank on every rank.
+  const int* row_src = nullptr;
+  const int* block_valid = nullptr;
+  __nv_bfloat16* push_dst[kMaxRanks] = {};
+  int push_ld = 0;
+  int rank = 0, world = 0;
+  uint64_t* ready_flags[kMaxRanks] = {};
+  unsigned int* finish = nullptr;  // CTA finish counter (local memory, reset by the last CTA)
 };
 
 __device__ __forceinline__ int unit_expert(const GroupArgs& g, int mb) {
@@ -721,8 +732,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         __nv_bfloat16* orow = nullptr;
         const __nv_bfloat16* rrow = nullptr;
         if (ok && row < M && n0 < N) {
-          orow = out + static_cast<size_t>(row) * ldo + n0;
-          rrow = residual ? residual + static_cast<size_t>(row) * ldr + n0 : nullptr;
+          if constexpr (MODE == kModeGrouped) {
+            if (grp.row_src != nullptr) {
+              // Push the row to its source rank's receive slot (NVLink store).
+              const int mb = row / BM;
+              if (row - mb * BM < __ldg(grp.block_valid + mb)) {
+                const int code = __ldg(grp.row_src + row);
+                orow = grp.push_dst[code >> 24] + static_cast<size_t>(code & 0xFFFFFF) * grp.push_ld + n0;
+              }
+            } else {
+              orow = out + static_cast<size_t>(row) * ldo + n0;
+            }
+          } else {
+            orow = out + static_cast<size_t>(row) * ldo + n0;
+            rrow = residual ? residual + static_cast<size_t>(row) * ldr + n0 : nullptr;
+          }
         }
         if (orow != nullptr) {
           const int ncols = min(CPW, N - n0);
@@ -786,6 +810,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
     else
       tmem_dealloc(tmem, kTmemCols);
+  }
+  if constexpr (MODE == kModeGrouped) {
+    if (grp.finish != nullptr && threadIdx.x == 0) {
+      // Every pushed row of this CTA is stored (barrier above); the last CTA
+      // tells every source that this owner's outputs have landed.
+      __threadfence_system();
+      const unsigned int prev = atomicAdd(grp.finish, 1u);
+      if (prev + 1 == gridDim.x) {
+        __threadfence_system();
+        for (int q = 0; q < grp.world; ++q) red_release_sys_add(grp.ready_flags[q] + kFlagEpReady + grp.rank, 1);
+        *grp.finish = 0u;
+      }
+    }
   }
   if constexpr (MODE == kModeAG) {
     // Every load of this CTA has been consumed: tell each rank its data here may be overwritten.

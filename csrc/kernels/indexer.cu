@@ -91,13 +91,6 @@ struct IndexerOut {
   int cand_cap;
 };
 
-// relu(x) * 2^-64 on the FMA pipe (saturating multiply clamps to [0, 1]).
-__device__ __forceinline__ float relu_scaled(float x) {
-  float y;
-  asm("mul.rn.sat.f32 %0, %1, 0f1F800000;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 template <bool SELECT>
 __global__ void __launch_bounds__(kThreads, 1)
     indexer_kernel(const __grid_constant__ CUtensorMap tma_q,
@@ -208,6 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t tcount = 0;
     bool ok = true;
     uint32_t fill = 0;  // selection mode: candidates in this warp's stage (warp-uniform)
+    const uint32_t lane_lt = (1u << lane) - 1u;
     // One counter update per batch; the batch's slots past the capacity are
     // counted but not stored (the row then goes to the fallback).
     auto flush = [&](int q, uint32_t cnt) {
@@ -215,8 +209,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t base = 0;
       if (lane == 0) base = atomicAdd(reinterpret_cast<unsigned int*>(o.cand_count + q), cnt);
       base = __shfl_sync(0xffffffffu, base, 0);
-      for (uint32_t i = lane; i < cnt; i += 32)
-        if (base + i < uint32_t(o.cand_cap)) o.cand[int64_t(q) * o.cand_cap + base + i] = s.stage[ew][i];
+      for (uint32_t i = lane; i < cnt; i += 32) {
+        const uint64_t x = s.stage[ew][i];
+        if (base + i < uint32_t(o.cand_cap))
+          o.cand[int64_t(q) * o.cand_cap + base + i] = select_composite(__uint_as_float(uint32_t(x >> 32)), int(uint32_t(x)));
+      }
       __syncwarp();
     };
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
@@ -227,12 +224,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       // cost 256 B per thread per tile, which bounded the epilogue at the
       // shared-memory read bandwidth.
       const int qidx = qb * QB + qgrp;
-      // Heads 4i+2, 4i+3 hold w * 2^64 and take their ReLU on the FMA pipe:
-      // mul.sat(x, 2^-64) = relu(x) * 2^-64 exactly (an E4M3 x E4M3 dot
-      // product is 0 or a multiple of 2^-18 below 2^25, so the scaled value is
-      // a normal float below 1), and the product with w * 2^64 rounds exactly
-      // like relu(x) * w.  Heads 4i, 4i+1 use max(x, 0) on the ALU pipe.  The
-      // split halves the ALU work that bounded the epilogue.
       float wr[kHeads];
       {
         const float4* wq = reinterpret_cast<const float4*>(w + int64_t(min(qidx, sch.Q - 1)) * kHeads);
@@ -241,8 +232,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float4 v = __ldg(wq + h4);
           wr[4 * h4 + 0] = v.x;
           wr[4 * h4 + 1] = v.y;
-          wr[4 * h4 + 2] = v.z * 18446744073709551616.0f;  // 2^64
-          wr[4 * h4 + 3] = v.w * 18446744073709551616.0f;
+          wr[4 * h4 + 2] = v.z;
+          wr[4 * h4 + 3] = v.w;
         }
       }
       const float thresh = (SELECT && o.thresh != nullptr) ? __ldg(o.thresh + min(qidx, sch.Q - 1)) : -INFINITY;
@@ -258,6 +249,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         // Two packed FP32x2 accumulators (heads h = 4i, 4i+1 and 4i+2, 4i+3).
+        // The ReLU (max on the ALU pipe, 64 per key and query) bounds the
+        // epilogue; moving half of it to the FMA pipe (x + |x|, or a
+        // saturating multiply by 2^-64) measured slower.
         float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
 #pragma unroll
         for (int c = 0; c < kHeads / 16; ++c) {
@@ -269,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int h = c * 16 + 4 * h4;
             fma_f32x2(a0, a1, fmaxf(__uint_as_float(r[4 * h4 + 0]), 0.f), fmaxf(__uint_as_float(r[4 * h4 + 1]), 0.f),
                       wr[h], wr[h + 1]);
-            fma_f32x2(b0, b1, relu_scaled(__uint_as_float(r[4 * h4 + 2])), relu_scaled(__uint_as_float(r[4 * h4 + 3])),
+            fma_f32x2(b0, b1, fmaxf(__uint_as_float(r[4 * h4 + 2]), 0.f), fmaxf(__uint_as_float(r[4 * h4 + 3]), 0.f),
                       wr[h + 2], wr[h + 3]);
           }
         }
@@ -290,7 +284,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             flush(qidx, fill);
             fill = 0;
           }
-          if (take) s.stage[ew][fill + uint32_t(__popc(m & ((1u << lane) - 1u)))] = select_composite(out, key);
+          if (take)  // raw (value, key): the composite is formed at the flush, for candidates only
+            s.stage[ew][fill + uint32_t(__popc(m & lane_lt))] =
+                (uint64_t(__float_as_uint(out)) << 32) | uint32_t(key);
           fill += n;
         }
       }

@@ -36,10 +36,19 @@ struct FP8GemmPlan {
 FP8GemmPlan plan_fp8_gemm(int M, int N, int K, int max_splits);
 // Pair (256-row, 2-CTA) tiles for the plain promotion path when M >= 256 (default off).
 void set_fp8_gemm_pair_tiles(bool enabled);
+// Decode-size FP8 linears (<= kGemvMaxRows rows) on the GEMV (default on).
+void set_decode_gemv(bool enabled);
 // K splits launch_fp8_gemm uses for this shape (1 = no split-K reduce launch).
 int fp8_gemm_launch_splits(int M, int N, int K, int max_splits, bool ue8m0);
 size_t fp8_gemm_scratch_bytes(int M, int N, int K, int max_splits);
 void launch_fp8_gemm(const FP8GemmArgs& a, cudaStream_t stream);
+
+// Decode-size linears (1 to kGemvMaxRows rows) on the CUDA cores, weight-streaming.
+constexpr int kGemvMaxRows = 8;
+bool gemv_fits(int M, int K, int64_t lda_bytes, int64_t ldw_bytes, const void* a, const void* w);
+void launch_fp8_gemv(const FP8GemmArgs& a, cudaStream_t stream);
+void launch_bf16_gemv(const __nv_bfloat16* x, int ldx, const __nv_bfloat16* w, int ldw, __nv_bfloat16* out, int ldo,
+                      int M, int N, int K, cudaStream_t stream);
 
 // Communication-fused FP8 GEMMs over NVLink peer memory (P2PArgs in common/p2p_args.h).
 // AG: out[M, N] = (all-gather of every rank's [S, K] shard) . B^T; p.a_local / p.sfa_local
@@ -64,15 +73,27 @@ void launch_moe_gather(const uint8_t* q, const float* s_t, int ld_st, int R, int
                        uint8_t* a, float* a_s, int ld_as, cudaStream_t stream);
 void launch_moe_combine(const __nv_bfloat16* y, int D, const int* row_pos, const float* w, int T, int topk,
                         __nv_bfloat16* out, cudaStream_t stream);
+// Expert-parallel push of the down projection's rows (see GroupArgs in gemm_fp8.cuh).
+struct EpPushArgs {
+  const int* row_src = nullptr;       // this rank's [M_pad] (source << 24 | source row), call parity half
+  const int* block_valid = nullptr;   // [M_pad / 128] valid rows per block
+  __nv_bfloat16* dst[kMaxRanks] = {}; // every rank's receive slots, call parity half
+  uint64_t* flags[kMaxRanks] = {};    // every rank's flag block
+  unsigned int* finish = nullptr;     // local CTA counter, zero between calls
+  int ld = 0, rank = 0, world = 0;
+};
 void launch_fp8_gemm_grouped(const uint8_t* A, const float* sfa, int lda_s, const uint8_t* B, const float* sfb,
                              const int* block_expert, int M_pad, int N, int K, int E, __nv_bfloat16* out, int ldo,
-                             int* err, cudaStream_t stream);
-// Expert-parallel dispatch (counts exchange + scatter into owners' grouped layouts + wait) and
-// combine (ready signal + pull of expert outputs + weighted k-order sum + done signal).
+                             int* err, cudaStream_t stream, const EpPushArgs* push = nullptr);
+// Expert-parallel dispatch (counts exchange + scatter into owners' grouped layouts and row-source
+// tables + wait) and combine (weighted k-order sum of the expert outputs + done signal).
 void launch_ep_dispatch(const EpArgs& p, const int* ids, const uint8_t* q, const float* s_t, int ld_st, int* cursor,
-                        int* pos_out, int* block_expert, int max_blocks, int* err, cudaStream_t stream);
+                        int* pos_out, int* block_expert, int max_blocks, int* err, cudaStream_t stream,
+                        int* block_valid = nullptr);
+// push: the owners' down GEMMs stored the rows here and raised the ready flags;
+// otherwise the owners' outputs are pulled over NVLink.
 void launch_ep_combine(const EpArgs& p, const int* ids, const int* pos, const float* w, __nv_bfloat16* out, int* err,
-                       cudaStream_t stream);
+                       cudaStream_t stream, bool push = false);
 // Shared sparse-token pool metadata on the device (csrc/kernels/pool_meta.cu).
 struct PoolRecallArgs {
   const int* ids = nullptr;      // selected logical rows (-1 = padding)

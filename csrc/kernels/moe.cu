@@ -221,7 +221,7 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int D, c
 template <int BN, int STAGES>
 void launch_grouped_t(const uint8_t* A, const float* sfa, int lda_s, const uint8_t* B, const float* sfb,
                       const int* block_expert, int M_pad, int N, int K, int E, __nv_bfloat16* out, int ldo, int* err,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, const GroupArgs* push = nullptr) {
   const CUtensorMap ta = make_tma_2d(A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M_pad, K, K, BK, BM);
   const CUtensorMap tb = make_tma_2d(B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, int64_t(E) * N, K, K, BK, BN);
   const int tiles = (M_pad / BM) * ((N + BN - 1) / BN);
@@ -229,7 +229,7 @@ void launch_grouped_t(const uint8_t* A, const float* sfa, int lda_s, const uint8
   const size_t smem = smem_bytes<BN, STAGES>();
   auto kern = fp8_gemm_kernel<BN, STAGES, kModeGrouped>;
   cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)), "grouped smem");
-  GroupArgs g;
+  GroupArgs g = push != nullptr ? *push : GroupArgs{};
   g.mblock_expert = block_expert;
   g.sfb_expert_stride = int64_t((N + 127) / 128) * (K / 128);
   kern<<<grid, kThreads, smem, stream>>>(ta, tb, sfa, lda_s, sfb, out, ldo, nullptr, 0, M_pad, N, K, 1, nullptr,
@@ -276,14 +276,35 @@ void launch_moe_combine(const __nv_bfloat16* y, int D, const int* row_pos, const
 
 void launch_fp8_gemm_grouped(const uint8_t* A, const float* sfa, int lda_s, const uint8_t* B, const float* sfb,
                              const int* block_expert, int M_pad, int N, int K, int E, __nv_bfloat16* out, int ldo,
-                             int* err, cudaStream_t stream) {
+                             int* err, cudaStream_t stream, const EpPushArgs* push) {
   if (M_pad % BM || K % 128) throw std::invalid_argument("grouped gemm: M_pad and K must be multiples of 128");
-  if (M_pad == 0) return;
+  if (M_pad == 0) {
+    if (push != nullptr) throw std::invalid_argument("grouped gemm push: empty layout would never signal");
+    return;
+  }
+  GroupArgs g;
+  const GroupArgs* gp = nullptr;
+  if (push != nullptr) {
+    if (push->world < 1 || push->world > kMaxRanks || !push->row_src || !push->block_valid || !push->finish)
+      throw std::invalid_argument("grouped gemm push: bad arguments");
+    g.row_src = push->row_src;
+    g.block_valid = push->block_valid;
+    g.push_ld = push->ld;
+    g.rank = push->rank;
+    g.world = push->world;
+    g.finish = push->finish;
+    for (int q = 0; q < push->world; ++q) {
+      if (!push->dst[q] || !push->flags[q]) throw std::invalid_argument("grouped gemm push: null peer");
+      g.push_dst[q] = push->dst[q];
+      g.ready_flags[q] = push->flags[q];
+    }
+    gp = &g;
+  }
   if (N % 224 == 0 && N % 256 != 0) launch_grouped_t<224, 4>(A, sfa, lda_s, B, sfb, block_expert, M_pad, N, K, E,
-                                                              out, ldo, err, stream);
+                                                              out, ldo, err, stream, gp);
   else if (N >= 256) launch_grouped_t<256, 4>(A, sfa, lda_s, B, sfb, block_expert, M_pad, N, K, E, out, ldo, err,
-                                              stream);
-  else launch_grouped_t<128, 6>(A, sfa, lda_s, B, sfb, block_expert, M_pad, N, K, E, out, ldo, err, stream);
+                                              stream, gp);
+  else launch_grouped_t<128, 6>(A, sfa, lda_s, B, sfb, block_expert, M_pad, N, K, E, out, ldo, err, stream, gp);
 }
 
 }  // namespace b200

@@ -167,6 +167,11 @@ def _c4(n: int) -> int:
     return max(4, (n + 3) // 4 * 4)
 
 
+def _blk(n: int) -> int:
+    """Bytes the CUDA caching allocator hands out for an n-byte request (512-byte rounding)."""
+    return (n + 511) // 512 * 512
+
+
 @dataclass(frozen=True)
 class WorkspaceAllowance:
     """Transient device bytes one chunk of one layer may hold, per component.
@@ -190,31 +195,31 @@ class WorkspaceAllowance:
             raise ValueError("queries and context must be positive")
         k = cfg.index_topk
         width = min(k, context)
-        out_ids = queries * width * 8                      # values FP32 + ids int32
+        out_ids = _blk(queries * width * 4) * 2            # values FP32 + ids int32
         if fused_select and method != "echo":
-            sel = (queries * _c4(-(-context // sample_stride)) * 4   # sampled logits
-                   + queries * 4                                     # thresholds
-                   + queries * max(cand_cap, 2 * k) * 8              # candidate composites
-                   + (queries + 1) * 4 + 2 * queries * 4             # counts + any-flag, flags, overflow
+            sel = (_blk(queries * _c4(-(-context // sample_stride)) * 4)   # sampled logits
+                   + _blk(queries * 4)                                     # thresholds
+                   + _blk(queries * max(cand_cap, 2 * k) * 8)              # candidate composites
+                   + _blk((queries + 1) * 4) + _blk(2 * queries * 4)       # counts + any-flag, flags + overflow
                    + out_ids)
         else:
-            sel = out_ids + queries * 4                              # outputs + two-pass overflow words
+            sel = out_ids + _blk(queries * 4)                        # outputs + two-pass overflow words
             if method == "echo":
-                sel += context * 4                                   # predicted-row list
+                sel += _blk(context * 4)                             # predicted-row list
         if not logits_preallocated:
-            sel += queries * _c4(context) * 4                        # [Q, N] FP32 logits (or fallback rows)
+            sel += _blk(queries * _c4(context) * 4)                  # [Q, N] FP32 logits (or fallback rows)
         H, D = cfg.n_heads, cfg.kv_lora_rank
         qk = D + cfg.qk_rope_head_dim
-        att = queries * H * qk * 2 + queries * H * D * 2             # absorbed query, latent output (BF16)
+        att = _blk(queries * H * qk * 2) + _blk(queries * H * D * 2)  # absorbed query, latent output (BF16)
         if splits > 1:
-            att += splits * queries * H * (D + 1) * 4                # FP32 partial outputs + LSE
+            att += _blk(splits * queries * H * D * 4) + _blk(splits * queries * H * 4)  # FP32 partials + LSE
         meta = 0
         if offload:
             rows = queries * width
-            att += rows * 4                                          # physical slot ids
+            att += _blk(rows * 4)                                    # physical slot ids
             if kv_format == "fp8":
-                att += min(rows, context) * 656                      # 656-byte records gathered before dequant
-            meta = 3 * rows * 4                                      # classify / select / map lists
+                att += _blk(min(rows, context) * 656)                # 656-byte records gathered before dequant
+            meta = 3 * _blk(rows * 4)                                # classify / select / map lists
         return cls(int(sel), int(att), int(meta))
 
 

@@ -139,6 +139,43 @@ def bench_fp8_gemm(M=1024, N=36864, K=7168, ue8m0=False, **_):
             **roofline(ms, flops=flops, nbytes=N * K + M * K + M * N * 2, fp8=True)}
 
 
+def bench_decode_gemms(M=1, **_):
+    """The projections of one DeepSeek-V3.2 layer and the LM head at decode row
+    counts: weight bytes streamed per call against the measured copy
+    bandwidth (power-of-two block scales; both FP8 paths)."""
+    from ..config import v32_config
+
+    cfg = v32_config(1)
+    dev = "cuda"
+    shapes = {  # name: (N, K)
+        "fused_a": (cfg.q_lora_rank + 640 + cfg.index_head_dim, cfg.dim),
+        "fused_b": (cfg.n_heads * (cfg.qk_nope_head_dim + cfg.qk_rope_head_dim)
+                    + cfg.index_n_heads * cfg.index_head_dim, cfg.q_lora_rank),
+        "o_proj": (cfg.dim, cfg.n_heads * cfg.v_head_dim),
+        "gate_up": (2 * cfg.intermediate_size, cfg.dim),
+        "down": (cfg.dim, cfg.intermediate_size),
+    }
+    hbm = _peaks()["hbm_gbs"]
+    rows = []
+    for name, (N, K) in shapes.items():
+        x = torch.randn(M, K, device=dev).bfloat16()
+        w, s = quantize_weight_blocks(torch.randn(N, K, device=dev) * 0.02)
+        q, s_t = ops.quantize_act(x)
+        out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        for ue in (False, True):
+            ms = time_fn(lambda: ops.fp8_gemm(q, s_t, w, s, out=out, ue8m0=ue))
+            rows.append({"gemm": name, "N": N, "K": K, "ue8m0": ue, "us": round(ms * 1e3, 2),
+                         "weight_gbs": round(N * K / ms / 1e6, 1), "frac_hbm": round(N * K / ms / 1e6 / hbm, 3)})
+        del w, s
+    N, K = cfg.vocab_size, cfg.dim
+    x = torch.randn(M, K, device=dev).bfloat16()
+    head = (torch.randn(N, K, device=dev) * 0.02).bfloat16()
+    ms = time_fn(lambda: ops.linear(x, head))
+    rows.append({"gemm": "lm_head_bf16", "N": N, "K": K, "us": round(ms * 1e3, 2),
+                 "weight_gbs": round(N * K * 2 / ms / 1e6, 1), "frac_hbm": round(N * K * 2 / ms / 1e6 / hbm, 3)})
+    return {"op": "decode_gemms", "M": M, "graph": GRAPH, "rows": rows}
+
+
 def bench_indexer(Q=1024, N=65536, **_):
     dev = "cuda"
     q = (torch.randn(Q, 64, 128, device=dev) * 2).to(torch.float8_e4m3fn)
@@ -234,7 +271,7 @@ def bench_rs_gemm(M=1024, N=7168, Kdim=2304, **_):
 
 
 OPS = {"sparse_mla": bench_sparse_mla, "fp8_gemm": bench_fp8_gemm, "indexer": bench_indexer,
-       "indexer_select": bench_indexer_select, "topk": bench_topk,
+       "indexer_select": bench_indexer_select, "topk": bench_topk, "decode_gemms": bench_decode_gemms,
        "ag_gemm": bench_ag_gemm, "rs_gemm": bench_rs_gemm}
 
 
@@ -269,6 +306,8 @@ def main():
             kw = dict(M=a.M, N=a.N, Kdim=a.Kdim)
         if name in ("indexer", "indexer_select"):
             kw = dict(Q=a.R)
+        if name == "decode_gemms":
+            kw = dict(M=a.M)
         if name == "topk":
             kw = dict(R=a.R, clustered=a.clustered, order=a.order, causal=a.causal)
         print(json.dumps(OPS[name](**kw)))

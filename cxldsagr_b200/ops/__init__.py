@@ -326,8 +326,26 @@ class MoELayout:
         return self.row_pos[: self.rows]
 
 
+class EpPushTarget:
+    """Destination of an expert-parallel down projection that pushes its rows
+    to their source ranks (``out=`` of :func:`fp8_gemm_grouped`): the owner's
+    row-source table and block validity, every rank's receive slots and flag
+    block (call parity half), and a local CTA finish counter."""
+
+    def __init__(self, row_src: int, block_valid, dst: list, flags: list, finish, rank: int, world: int):
+        self.row_src, self.block_valid, self.dst, self.flags = row_src, block_valid, dst, flags
+        self.finish, self.rank, self.world = finish, rank, world
+
+
 def fp8_gemm_grouped(a, a_s, w, w_s, block_expert, out=None):
-    """Grouped FP8 GEMM over a padded layout: out[m] = a[m] . w[expert(m // 128)]^T."""
+    """Grouped FP8 GEMM over a padded layout: out[m] = a[m] . w[expert(m // 128)]^T.
+
+    With ``out`` an :class:`EpPushTarget` the rows go to their source ranks
+    over NVLink instead (returns None)."""
+    if isinstance(out, EpPushTarget):
+        lib().fp8_gemm_grouped_push(a, a_s, w, w_s, block_expert, out.block_valid, out.row_src, out.dst, out.flags,
+                                    out.finish, out.rank, out.world)
+        return None
     if out is None:
         out = torch.empty((a.shape[0], w.shape[1]), dtype=torch.bfloat16, device=a.device)
     lib().fp8_gemm_grouped(a, a_s, w, w_s, block_expert, out)

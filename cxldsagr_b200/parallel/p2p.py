@@ -109,7 +109,7 @@ class P2PComm(Comm):
             # Worst case: every routed row of the chunk lands on one owner, plus per-expert padding.
             self.ep_mpad = (max_rows * topk + (E // W) * 127 + 127) // 128 * 128
             self.ep_shapes = {"cnt": 2 * W * E * 4, "a": 2 * self.ep_mpad * D, "as": 2 * (D // 128) * self.ep_mpad * 4,
-                              "y": 2 * self.ep_mpad * D * 2}
+                              "y": 2 * self.ep_mpad * D * 2, "rsrc": 2 * self.ep_mpad * 4}
             ep_bytes = sum(self.ep_shapes.values()) + 4 * ALIGN
         self.heap = SymmetricHeap(ctx, flags + g_bytes + gs_bytes + rb_bytes + ep_bytes + 4 * ALIGN)
         self.off_flags = self.heap.region(flags)
@@ -125,6 +125,11 @@ class P2PComm(Comm):
             self.ep_blocks = self.ep_mpad // 128
             self.ep_cursor = torch.zeros(E, dtype=torch.int32, device=dev)
             self.ep_block_expert = torch.full((self.ep_blocks,), -1, dtype=torch.int32, device=dev)
+            self.ep_block_valid = torch.zeros(self.ep_blocks, dtype=torch.int32, device=dev)
+            self.ep_finish = torch.zeros(1, dtype=torch.int32, device=dev)
+        # Push mode: the owners' down GEMMs store rows into the sources' receive
+        # slots (fused combine); pull mode: sources load the owners' outputs.
+        self.ep_push = True
         self.flag_ptrs = self.heap.ptrs(self.off_flags)
         self.g_ptrs, self.gs_ptrs, self.rb_ptrs = (self.heap.ptrs(o) for o in (self.off_g, self.off_gs, self.off_rb))
         # Device-resident op state of the AG, RS and barrier kinds (local memory).
@@ -219,13 +224,19 @@ class P2PComm(Comm):
         with self._span("ep_dispatch"):
             self.lib().ep_dispatch(ids32, q.contiguous(), s_t, self.ep_cursor, pos, self.ep_block_expert, self.ctx.rank,
                                    self.world, E, self.ep_mpad, call, self.flag_ptrs, p["cnt"], p["a"], p["as"],
-                                   p["y"])
+                                   p["y"], p["rsrc"], self.ep_block_valid)
         a, a_s, y = self._ep_views(parity)
+        if self.ep_push:
+            # Receive slots and row-source tables of this call's parity half.
+            y_bytes = self.ep_mpad * D * 2
+            y = ops.EpPushTarget(p["rsrc"][self.ctx.rank] + parity * self.ep_mpad * 4, self.ep_block_valid,
+                                 [b + parity * y_bytes for b in p["y"]], self.flag_ptrs, self.ep_finish,
+                                 self.ctx.rank, self.world)
         experts_fn(a, a_s, self.ep_block_expert, y)
         out = torch.empty((T, D), dtype=torch.bfloat16, device=q.device)
         with self._span("ep_combine"):
             self.lib().ep_combine(ids32, pos, weights.contiguous(), out, self.ctx.rank, self.world, E, self.ep_mpad,
-                                  call, self.flag_ptrs, p["cnt"], p["a"], p["as"], p["y"])
+                                  call, self.flag_ptrs, p["cnt"], p["a"], p["as"], p["y"], p["rsrc"], self.ep_push)
         self.fused_calls["ep"] = self.fused_calls.get("ep", 0) + 1
         return out
 

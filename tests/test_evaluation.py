@@ -112,10 +112,10 @@ def test_workspace_allowance_terms():
     assert no_buf.selection - fused.selection == 2048 * 65536 * 4
     split = audit.WorkspaceAllowance.for_chunk(cfg, queries=1, context=65536, splits=8)
     one = audit.WorkspaceAllowance.for_chunk(cfg, queries=1, context=65536)
-    assert split.attention - one.attention == 8 * 128 * 513 * 4
+    assert split.attention - one.attention == 8 * 128 * 512 * 4 + 8 * 128 * 4
     fp8 = audit.WorkspaceAllowance.for_chunk(cfg, queries=128, context=65664, offload=True, kv_format="fp8")
     bf16 = audit.WorkspaceAllowance.for_chunk(cfg, queries=128, context=65664, offload=True)
-    assert fp8.attention - bf16.attention == 65664 * 656 and fp8.metadata == 3 * 128 * 2048 * 4
+    assert fp8.attention - bf16.attention == (65664 * 656 + 511) // 512 * 512 and fp8.metadata == 3 * 128 * 2048 * 4
     with pytest.raises(ValueError):
         audit.WorkspaceAllowance.for_chunk(cfg, queries=0, context=10)
 

@@ -754,3 +754,35 @@ def test_cache_memory_audit_model(method, kv_format, capsys):
         assert "sparse_mla" in checked and ("indexer_select" in checked or "indexer" in checked), checked
     assert rc == 0, {p: rep[p]["audit"] for p in ("prefill", "extend")}
     assert rep["fixed"]["total"]["hbm"] > 0
+
+
+@pytest.mark.parametrize("M", [1, 3, 8])
+@pytest.mark.parametrize("N,K", [(2304, 7168), (7168, 16384), (1000, 1536)])
+def test_decode_gemv_fp8(M, N, K):
+    """Decode-size FP8 linears run on the weight-streaming GEMV: FP32-oracle
+    accuracy, and agreement with the tensor-core tile kernel."""
+    torch.manual_seed(41)
+    x = torch.randn(M, K, device=DEV).bfloat16()
+    w, s = quantize_weight_blocks(torch.randn(N, K, device=DEV) * 0.02)
+    q, s_t = ops.quantize_act(x)
+    res = torch.randn(M, N, device=DEV).bfloat16()
+    got = ops.fp8_gemm(q, s_t, w, s, residual=res)
+    ops.lib().set_decode_gemv(False)
+    try:
+        tiles = ops.fp8_gemm(q, s_t, w, s, residual=res)
+    finally:
+        ops.lib().set_decode_gemv(True)
+    a = ref.dequantize_act(q.cpu(), s_t.t().cpu())
+    want = a @ ref.dequantize_weight(w.cpu(), s.cpu()).T + res.float().cpu()
+    assert rel_err(got.float().cpu(), want) < 1e-2
+    assert rel_err(got.float().cpu(), tiles.float().cpu()) < 1e-2
+
+
+@pytest.mark.parametrize("M", [1, 2, 8])
+def test_decode_gemv_bf16(M):
+    torch.manual_seed(42)
+    x = torch.randn(M, 7168, device=DEV).bfloat16()
+    w = (torch.randn(4100, 7168, device=DEV) * 0.02).bfloat16()
+    got = ops.linear(x, w)
+    want = x.float().cpu() @ w.float().cpu().T
+    assert rel_err(got.float().cpu(), want) < 1e-2

@@ -261,3 +261,52 @@ def test_sp_extend_cuda_graph(world):
     for rank, rep in reports.items():
         print(rank, rep)
         assert rep["p2p"] and rep["torch"]
+
+
+def _ep_push_vs_pull(rank, world):
+    """The expert-parallel combine fused into the down projection (owners push
+    rows to the sources' receive slots) equals the pull combine bit for bit."""
+    from cxldsagr_b200.checkpoint import StateDictSource, random_state_dict
+    from cxldsagr_b200.config import CacheConfig, v32_config
+    from cxldsagr_b200.models.deepseek_v32.model import DeepSeekV32Model
+    from cxldsagr_b200.ops.native import check_errors
+    from cxldsagr_b200.parallel.groups import ParallelContext, init_distributed
+
+    base = init_distributed(timeout_s=60, comm="torch")
+    dev = base.device
+    cfg = v32_config(4, n_routed_experts=16, n_group=8, topk_group=4, num_experts_per_tok=4,
+                     moe_intermediate_size=512)
+    layers = [0, 3]
+    per = cfg.n_routed_experts // world
+    src = StateDictSource(random_state_dict(cfg, layers=layers, seed=0, device=dev,
+                                            experts=range(rank * per, (rank + 1) * per)), cfg)
+    cache = CacheConfig(capacity=2048 + 64, chunk_size=1024, candidate_tokens=64)
+    ctx = ParallelContext(base.rank, base.world, base.group, dev, backend="p2p")
+    m = DeepSeekV32Model(cfg, src, device=dev, cache=cache, layers=layers, parallel=ctx)
+    g = torch.Generator(device=dev).manual_seed(7)
+    ids = torch.randint(0, cfg.vocab_size, (2048 + 64,), generator=g, device=dev)
+    out = {}
+    for push in (True, False, True):
+        m.comm.ep_push = push
+        m.reset()
+        a = m.prefill(ids[:2048]).logits.float().cpu()
+        b = m.extend(ids[2048:]).logits.float().cpu()
+        torch.cuda.synchronize()
+        check_errors(dev)
+        out.setdefault(push, []).append((a, b))
+    calls = dict(m.comm.fused_calls)
+    m.comm.close()
+    pull = out[False][0]
+    return {"calls": calls,
+            "equal": all(torch.equal(x[0], pull[0]) and torch.equal(x[1], pull[1]) for x in out[True]),
+            "finite": bool(torch.isfinite(pull[1]).all())}
+
+
+@pytest.mark.parametrize("world", [2])
+def test_ep_push_combine_matches_pull(world):
+    _need(world)
+    reports = _spawn(_ep_push_vs_pull, world)
+    for rank, rep in reports.items():
+        print(rank, rep)
+        assert rep["finite"] and rep["calls"].get("ep", 0) > 0
+        assert rep["equal"]
