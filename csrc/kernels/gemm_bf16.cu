@@ -203,12 +203,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 void launch_bf16_gemm(const BF16GemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0 || a.batch <= 0) return;
-  if (a.batch == 1 && !a.out_fp32 && a.M <= kGemvMaxRows && a.K % 8 == 0 && (a.lda * 2) % 16 == 0 &&
-      (a.ldb * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(a.A) & 15) == 0 &&
-      (reinterpret_cast<uintptr_t>(a.B) & 15) == 0) {
+  if (decode_gemv_enabled() && a.batch == 1 && a.M <= kGemvMaxRows && a.K % 8 == 0 && (a.lda * 2) % 16 == 0 && (a.ldb * 2) % 16 == 0 &&
+      (reinterpret_cast<uintptr_t>(a.A) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.B) & 15) == 0) {
     // Decode rows (the LM head of a one-token step): stream the weights once.
-    launch_bf16_gemv(a.A, int(a.lda), a.B, int(a.ldb), static_cast<__nv_bfloat16*>(a.out), int(a.ldo), a.M, a.N, a.K,
-                     stream);
+    launch_bf16_gemv(a.A, int(a.lda), a.B, int(a.ldb), a.out, a.out_fp32, int(a.ldo), a.M, a.N, a.K, stream);
     return;
   }
   constexpr int BN = 128, STAGES = 6;

@@ -84,6 +84,7 @@ bool g_decode_gemv = true;
 }  // namespace
 
 void set_decode_gemv(bool enabled) { g_decode_gemv = enabled; }
+bool decode_gemv_enabled() { return g_decode_gemv; }
 
 void set_fp8_gemm_pair_tiles(bool enabled) { g_pair_tiles = enabled; }
 

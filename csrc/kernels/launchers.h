@@ -36,19 +36,22 @@ struct FP8GemmPlan {
 FP8GemmPlan plan_fp8_gemm(int M, int N, int K, int max_splits);
 // Pair (256-row, 2-CTA) tiles for the plain promotion path when M >= 256 (default off).
 void set_fp8_gemm_pair_tiles(bool enabled);
-// Decode-size FP8 linears (<= kGemvMaxRows rows) on the GEMV (default on).
+// Decode-size FP8 / BF16 linears (<= kGemvMaxRows rows) on the GEMV (default on).
 void set_decode_gemv(bool enabled);
+bool decode_gemv_enabled();
 // K splits launch_fp8_gemm uses for this shape (1 = no split-K reduce launch).
 int fp8_gemm_launch_splits(int M, int N, int K, int max_splits, bool ue8m0);
 size_t fp8_gemm_scratch_bytes(int M, int N, int K, int max_splits);
 void launch_fp8_gemm(const FP8GemmArgs& a, cudaStream_t stream);
 
-// Decode-size linears (1 to kGemvMaxRows rows) on the CUDA cores, weight-streaming.
-constexpr int kGemvMaxRows = 8;
+// Decode-size linears on the CUDA cores, weight-streaming: FP8 at one row,
+// BF16 (the LM head) up to four rows; more rows run on the tile kernels.
+constexpr int kGemvMaxRowsFp8 = 1;
+constexpr int kGemvMaxRows = 4;
 bool gemv_fits(int M, int K, int64_t lda_bytes, int64_t ldw_bytes, const void* a, const void* w);
 void launch_fp8_gemv(const FP8GemmArgs& a, cudaStream_t stream);
-void launch_bf16_gemv(const __nv_bfloat16* x, int ldx, const __nv_bfloat16* w, int ldw, __nv_bfloat16* out, int ldo,
-                      int M, int N, int K, cudaStream_t stream);
+void launch_bf16_gemv(const __nv_bfloat16* x, int ldx, const __nv_bfloat16* w, int ldw, void* out, bool out_fp32,
+                      int ldo, int M, int N, int K, cudaStream_t stream);
 
 // Communication-fused FP8 GEMMs over NVLink peer memory (P2PArgs in common/p2p_args.h).
 // AG: out[M, N] = (all-gather of every rank's [S, K] shard) . B^T; p.a_local / p.sfa_local

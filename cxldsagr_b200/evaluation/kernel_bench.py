@@ -141,39 +141,53 @@ def bench_fp8_gemm(M=1024, N=36864, K=7168, ue8m0=False, **_):
 
 def bench_decode_gemms(M=1, **_):
     """The projections of one DeepSeek-V3.2 layer and the LM head at decode row
-    counts: weight bytes streamed per call against the measured copy
-    bandwidth (power-of-two block scales; both FP8 paths)."""
+    counts 1, 2, 4, 8 (up to ``M``): weight bytes streamed per call on the
+    GEMV and on the tensor-core tile kernels, against the measured copy
+    bandwidth (power-of-two block scales)."""
     from ..config import v32_config
 
     cfg = v32_config(1)
     dev = "cuda"
-    shapes = {  # name: (N, K)
-        "fused_a": (cfg.q_lora_rank + 640 + cfg.index_head_dim, cfg.dim),
+    shapes = {  # name: (N, K, fp8)
+        "fused_a": (cfg.q_lora_rank + 640 + cfg.index_head_dim, cfg.dim, True),
         "fused_b": (cfg.n_heads * (cfg.qk_nope_head_dim + cfg.qk_rope_head_dim)
-                    + cfg.index_n_heads * cfg.index_head_dim, cfg.q_lora_rank),
-        "o_proj": (cfg.dim, cfg.n_heads * cfg.v_head_dim),
-        "gate_up": (2 * cfg.intermediate_size, cfg.dim),
-        "down": (cfg.dim, cfg.intermediate_size),
+                    + cfg.index_n_heads * cfg.index_head_dim, cfg.q_lora_rank, True),
+        "o_proj": (cfg.dim, cfg.n_heads * cfg.v_head_dim, True),
+        "gate_up": (2 * cfg.intermediate_size, cfg.dim, True),
+        "down": (cfg.dim, cfg.intermediate_size, True),
+        "lm_head_bf16": (cfg.vocab_size, cfg.dim, False),
     }
     hbm = _peaks()["hbm_gbs"]
     rows = []
-    for name, (N, K) in shapes.items():
-        x = torch.randn(M, K, device=dev).bfloat16()
-        w, s = quantize_weight_blocks(torch.randn(N, K, device=dev) * 0.02)
-        q, s_t = ops.quantize_act(x)
-        out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
-        for ue in (False, True):
-            ms = time_fn(lambda: ops.fp8_gemm(q, s_t, w, s, out=out, ue8m0=ue))
-            rows.append({"gemm": name, "N": N, "K": K, "ue8m0": ue, "us": round(ms * 1e3, 2),
-                         "weight_gbs": round(N * K / ms / 1e6, 1), "frac_hbm": round(N * K / ms / 1e6 / hbm, 3)})
-        del w, s
-    N, K = cfg.vocab_size, cfg.dim
-    x = torch.randn(M, K, device=dev).bfloat16()
-    head = (torch.randn(N, K, device=dev) * 0.02).bfloat16()
-    ms = time_fn(lambda: ops.linear(x, head))
-    rows.append({"gemm": "lm_head_bf16", "N": N, "K": K, "us": round(ms * 1e3, 2),
-                 "weight_gbs": round(N * K * 2 / ms / 1e6, 1), "frac_hbm": round(N * K * 2 / ms / 1e6 / hbm, 3)})
-    return {"op": "decode_gemms", "M": M, "graph": GRAPH, "rows": rows}
+    for name, (N, K, fp8) in shapes.items():
+        if fp8:
+            w, s = quantize_weight_blocks(torch.randn(N, K, device=dev) * 0.02)
+            nbytes = N * K
+        else:
+            w = (torch.randn(N, K, device=dev) * 0.02).bfloat16()
+            nbytes = 2 * N * K
+        for m in (1, 2, 4, 8):
+            if m > max(M, 1):
+                break
+            x = torch.randn(m, K, device=dev).bfloat16()
+            if fp8:
+                q, s_t = ops.quantize_act(x)
+                out = torch.empty(m, N, device=dev, dtype=torch.bfloat16)
+                fn = lambda: ops.fp8_gemm(q, s_t, w, s, out=out)  # noqa: E731
+            else:
+                fn = lambda: ops.linear(x, w)  # noqa: E731
+            row = {"gemm": name, "M": m, "N": N, "K": K}
+            for label, on in (("gemv", True), ("tiles", False)):
+                ops.lib().set_decode_gemv(on)
+                try:
+                    ms = time_fn(fn)
+                finally:
+                    ops.lib().set_decode_gemv(True)
+                row[f"{label}_us"] = round(ms * 1e3, 2)
+                row[f"{label}_frac_hbm"] = round(nbytes / ms / 1e6 / hbm, 3)
+            rows.append(row)
+        del w
+    return {"op": "decode_gemms", "graph": GRAPH, "rows": rows}
 
 
 def bench_indexer(Q=1024, N=65536, **_):

@@ -786,3 +786,14 @@ def test_decode_gemv_bf16(M):
     got = ops.linear(x, w)
     want = x.float().cpu() @ w.float().cpu().T
     assert rel_err(got.float().cpu(), want) < 1e-2
+
+
+def test_decode_gemv_bf16_fp32_out():
+    """The LM head's FP32-output BF16 GEMM at one row (the decode head) uses the GEMV."""
+    torch.manual_seed(43)
+    x = torch.randn(1, 7168, device=DEV).bfloat16()
+    w = (torch.randn(3000, 7168, device=DEV) * 0.02).bfloat16()
+    out = torch.empty(1, 3000, device=DEV, dtype=torch.float32)
+    ops.lib().bf16_gemm(x, 0, 7168, 0, w, 0, 7168, 0, out, 0, 3000, 0, 1, 3000, 7168, 1)
+    want = x.float().cpu() @ w.float().cpu().T
+    assert rel_err(out.cpu(), want) < 1e-3
