@@ -220,22 +220,31 @@ def sp_arm(cfg, n_layers, args, dev, rank, world, comm: str) -> dict:
         model.prefill(hist)
         torch.cuda.synchronize(dev)
         dist.barrier()
-        graph = model.capture_extend(A)
-        for _ in range(2):
-            graph.replay(ext)
-            graph.rollback()
-        torch.cuda.synchronize(dev)
-        dist.barrier()
-        tot = 0.0
-        for _ in range(steps):
-            e = _events(2)
-            e[0].record(stream)
-            graph.replay(ext)
-            e[1].record(stream)
+        graph, err = None, ""
+        try:
+            graph = model.capture_extend(A)
+        except (RuntimeError, ValueError) as exc:  # same code on every rank: all fail alike
+            err = str(exc)
+        ok = torch.tensor([0 if graph is None else 1], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if ok.item():
+            for _ in range(2):
+                graph.replay(ext)
+                graph.rollback()
             torch.cuda.synchronize(dev)
-            tot += e[0].elapsed_time(e[1])
-            graph.rollback()
-        graph_ms = tot / steps
+            dist.barrier()
+            tot = 0.0
+            for _ in range(steps):
+                e = _events(2)
+                e[0].record(stream)
+                graph.replay(ext)
+                e[1].record(stream)
+                torch.cuda.synchronize(dev)
+                tot += e[0].elapsed_time(e[1])
+                graph.rollback()
+            graph_ms = tot / steps
+        elif rank == 0:
+            print(f"sp extend graph unavailable: {err[:200]}", file=sys.stderr)
         del graph  # before the process group goes away (it may hold NCCL calls)
         torch.cuda.synchronize(dev)
     names = sorted(coll)

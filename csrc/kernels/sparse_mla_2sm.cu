@@ -603,17 +603,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (have_o) tc_fence_after();
     if (tt == 0) trace(kTraceTiles, 2);
     const int head = HC * int(crank) + hrow;
+    // Two chunks per TMEM round trip: both loads are in flight before the
+    // wait, so the output stores of a pair overlap the next pair's loads.
 #pragma unroll 1
-    for (int c = 0; c < 8; ++c) {
-      uint32_t r[32];
+    for (int c2 = 0; c2 < 8; c2 += 2) {
+      uint32_t rr[2][32];
       if (have_o) {
-        tmem_ld32(tmem + lane_addr + c * 32, r);
+        tmem_ld32(tmem + lane_addr + c2 * 32, rr[0]);
+        tmem_ld32(tmem + lane_addr + (c2 + 1) * 32, rr[1]);
         tmem_wait_ld();
-        tmem_regs_ready(r);
+        tmem_regs_ready(rr[0]);
+        tmem_regs_ready(rr[1]);
       } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) r[j] = 0u;
+        for (int j = 0; j < 32; ++j) rr[0][j] = rr[1][j] = 0u;
       }
+#pragma unroll
+    for (int ci = 0; ci < 2; ++ci) {
+      const int c = c2 + ci;
+      const uint32_t (&r)[32] = rr[ci];
       // Columns [32c, 32c+32): value half c / 4, dims 256 (c/4) + 128 kh + 32 (c%4).
       const int dim0 = 256 * (c >> 2) + 128 * kh + 32 * (c & 3);
       if (splits == 1) {
@@ -635,6 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               make_float4(__uint_as_float(r[j]) * inv, __uint_as_float(r[j + 1]) * inv,
                           __uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
       }
+    }
     }
     if (kh == 0) {
       if (splits == 1) {

@@ -383,14 +383,15 @@ def sparse_mla(q, kv, ids, scale, *, splits: int = 1, return_lse: bool = False, 
 def mla_splits(T: int, K: int = 2048, *, clusters: int = 74) -> int:
     """Split-K factor for the 2-CTA sparse MLA: few queries (decode, short
     extends) leave most of the 74 cluster slots (148 SMs) idle, so split each
-    query's selection over more clusters, keeping >= 256 keys (eight 32-key
-    tiles) per split: each split reloads the query and pays its pipeline fill.
-    Measured on B200 at K = 2048: T = 1 takes 96.8 / 42.1 / 45.7 / 62.3 us with
-    1 / 8 / 16 / 32 splits; T = 16 takes 94.8 / 52.0 us with 1 / 4 splits;
-    T = 128 is faster unsplit (0.188 vs 0.318 ms with 4)."""
+    query's selection over more clusters, keeping >= 512 keys (eight 64-key
+    pair tiles) per split: each split reloads the query (5K cycles), pays its
+    pipeline fill and writes a 256 KB FP32 partial (10K cycles), and the LSE
+    combine reads every split.  Measured on B200 at K = 2048, cold L2, CUDA
+    graph replays: T = 1 takes 57.6 / 32.9 / 37.0 / 41.2 / 59.3 us with
+    1 / 4 / 8 / 16 / 32 splits; T = 128 is faster unsplit."""
     if T >= clusters:
         return 1
-    return max(1, min(32, clusters // max(T, 1), K // 256))
+    return max(1, min(32, clusters // max(T, 1), K // 512))
 
 
 def sparse_mla_decode(q, kv, ids, scale, splits: int = 16):
