@@ -312,7 +312,7 @@ void copy_topk_trace(unsigned long long* host);
 void copy_sparse_mla_trace(unsigned long long* host);
 // out[t,h,:] = sum_s exp(lse_s - lse) * part_o[s,t,h,:]; lse = logsumexp_s lse_s.
 void launch_mla_combine(const float* part_o, const float* part_lse, int splits, int T, int H,
-                        __nv_bfloat16* out, float* lse, cudaStream_t stream);
+                        __nv_bfloat16* out, float* lse, cudaStream_t stream, bool head_minor = false);
 
 // ----------------------------------------------------------- KV transfer
 // records[slots[i]] = host[host_ids[i]] for i < n (width bytes per row), SM

@@ -300,6 +300,45 @@ __global__ void mla_combine_kernel(const float* __restrict__ part_o, const float
   if (lse_out && threadIdx.x == 0) lse_out[th] = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
 }
 
+// Same merge over head-minor partials [split][t][dim][head] (the 2-CTA
+// kernel's layout): block (t, 8-dim group), thread h = head; reads of a dim
+// across heads are contiguous.
+__global__ void mla_combine_hm_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
+                                      int splits, int T, int H, __nv_bfloat16* __restrict__ out,
+                                      float* __restrict__ lse_out) {
+  const int t = blockIdx.x, d0 = blockIdx.y * 8;
+  for (int h = threadIdx.x; h < H; h += blockDim.x) {
+    const int64_t th = int64_t(t) * H + h;
+    float mx = -INFINITY;
+    for (int sidx = 0; sidx < splits; ++sidx) mx = fmaxf(mx, part_lse[int64_t(sidx) * T * H + th]);
+    float wsum = 0.f;
+    float wts[32];
+    for (int sidx = 0; sidx < splits && sidx < 32; ++sidx) {
+      const float l = part_lse[int64_t(sidx) * T * H + th];
+      wts[sidx] = (mx == -INFINITY) ? 0.f : expf(l - mx);
+      wsum += wts[sidx];
+    }
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int sidx = 0; sidx < splits && sidx < 32; ++sidx) {
+      if (wts[sidx] > 0.f) {
+        const float* p = part_o + ((int64_t(sidx) * T + t) * DV + d0) * H + h;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += wts[sidx] * p[int64_t(j) * H];
+      }
+    }
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = wsum > 0.f ? acc[j] / wsum : 0.f;
+    uint4 o;
+    o.x = pack_bf16(v[0], v[1]);
+    o.y = pack_bf16(v[2], v[3]);
+    o.z = pack_bf16(v[4], v[5]);
+    o.w = pack_bf16(v[6], v[7]);
+    *reinterpret_cast<uint4*>(out + th * DV + d0) = o;
+    if (lse_out && blockIdx.y == 0) lse_out[th] = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
+  }
+}
+
 }  // namespace
 
 size_t sparse_mla_scratch_bytes(int T, int H, int splits) {
@@ -325,8 +364,11 @@ void launch_sparse_mla_split(const MLAArgs& a, int splits, float* scratch, cudaS
 }
 
 void launch_mla_combine(const float* part_o, const float* part_lse, int splits, int T, int H,
-                        __nv_bfloat16* out, float* lse, cudaStream_t stream) {
-  mla_combine_kernel<<<T * H, 128, 0, stream>>>(part_o, part_lse, splits, T, H, out, lse);
+                        __nv_bfloat16* out, float* lse, cudaStream_t stream, bool head_minor) {
+  if (head_minor)
+    mla_combine_hm_kernel<<<dim3(T, DV / 8), 128, 0, stream>>>(part_o, part_lse, splits, T, H, out, lse);
+  else
+    mla_combine_kernel<<<T * H, 128, 0, stream>>>(part_o, part_lse, splits, T, H, out, lse);
   cuda_check(cudaGetLastError(), "mla_combine launch");
 }
 

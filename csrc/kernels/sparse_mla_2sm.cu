@@ -636,12 +636,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<uint4*>(o + j) = v;
         }
       } else {
-        float* o = part_o + ((int64_t(split) * T + t) * H + head) * DV + dim0;
+        // Head-minor partials [split][t][dim][head]: the 32 lanes of a warp
+        // hold 32 consecutive heads, so each store writes one 128-byte line
+        // (a head-major row per lane made every store 32 separate segments).
+        float* o = part_o + ((int64_t(split) * T + t) * DV + dim0) * H + head;
 #pragma unroll
-        for (int j = 0; j < 32; j += 4)
-          *reinterpret_cast<float4*>(o + j) =
-              make_float4(__uint_as_float(r[j]) * inv, __uint_as_float(r[j + 1]) * inv,
-                          __uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
+        for (int j = 0; j < 32; ++j) o[int64_t(j) * H] = __uint_as_float(r[j]) * inv;
       }
     }
     }
@@ -706,7 +706,7 @@ void launch_sparse_mla_2sm(const MLAArgs& a, int splits, float* scratch, cudaStr
   cuda_check(cudaLaunchKernelEx(&cfg, sparse_mla_pair_kernel, a.q, reinterpret_cast<const uint8_t*>(a.kv), a.ids,
                                 a.T, a.K, a.P, scale_log2, splits, a.out, part_o, part_lse, a.lse, a.err, dbg_s, dbg),
              "sparse_mla_2sm launch");
-  if (splits > 1) launch_mla_combine(part_o, part_lse, splits, a.T, a.H, a.out, a.lse, stream);
+  if (splits > 1) launch_mla_combine(part_o, part_lse, splits, a.T, a.H, a.out, a.lse, stream, true);
 }
 
 }  // namespace b200

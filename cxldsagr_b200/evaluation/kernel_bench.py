@@ -98,6 +98,15 @@ def mla_timeline(q, kv, ids, splits: int) -> dict:
     return {"q_landed": int(tr[0, 64, 1]) - t0, "first_s": s_read[0], "first_p": p_handed[0],
             "last_p": p_handed[-1], "cycles_per_tile": (p_handed[-1] - p_handed[0]) / max(1, n - 1),
             "softmax_cycles_per_tile": sum(p - r for p, r in zip(p_handed, s_read)) / n,
+            # Softmax phases per tile (mean over tiles, SM cycles): S read -> maxima exchanged
+            # (named barrier) -> exponentials and P packed -> P buffer free (PV two tiles back)
+            # -> P stored and handed to PV; and the wait for the next S.
+            "softmax_phases": {
+                "max_exchange": sum(int(tr[0, i, 8]) - int(tr[0, i, 4]) for i in range(n)) / n,
+                "exp_pack": sum(int(tr[0, i, 9]) - int(tr[0, i, 8]) for i in range(n)) / n,
+                "p_buffer_wait": sum(int(tr[0, i, 10]) - int(tr[0, i, 9]) for i in range(n)) / n,
+                "p_store_hand": sum(int(tr[0, i, 5]) - int(tr[0, i, 10]) for i in range(n)) / n,
+                "next_s_wait": sum(int(tr[0, i + 1, 4]) - int(tr[0, i, 5]) for i in range(n - 1)) / max(1, n - 1)},
             "o_ready": int(tr[0, 64, 2]) - t0, "exit": int(tr[0, 64, 3]) - t0, "tiles": n, "keys_per_tile": 64}
 
 

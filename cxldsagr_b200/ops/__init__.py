@@ -383,15 +383,15 @@ def sparse_mla(q, kv, ids, scale, *, splits: int = 1, return_lse: bool = False, 
 def mla_splits(T: int, K: int = 2048, *, clusters: int = 74) -> int:
     """Split-K factor for the 2-CTA sparse MLA: few queries (decode, short
     extends) leave most of the 74 cluster slots (148 SMs) idle, so split each
-    query's selection over more clusters, keeping >= 512 keys (eight 64-key
-    pair tiles) per split: each split reloads the query (5K cycles), pays its
-    pipeline fill and writes a 256 KB FP32 partial (10K cycles), and the LSE
-    combine reads every split.  Measured on B200 at K = 2048, cold L2, CUDA
-    graph replays: T = 1 takes 57.6 / 32.9 / 37.0 / 41.2 / 59.3 us with
-    1 / 4 / 8 / 16 / 32 splits; T = 128 is faster unsplit."""
+    query's selection over more clusters, keeping >= 256 keys (four 64-key
+    pair tiles) per split: each split reloads the query (~5K cycles), pays its
+    pipeline fill and writes a 256 KB FP32 partial (head-minor, ~4.4K
+    cycles), and the LSE combine reads every split.  Measured on B200 at
+    K = 2048, cold L2, CUDA graph replays: T = 1 takes 39.5 / 29.5 / 24.9 us
+    with 2 / 4 / 8 splits; T = 128 is faster unsplit."""
     if T >= clusters:
         return 1
-    return max(1, min(32, clusters // max(T, 1), K // 512))
+    return max(1, min(32, clusters // max(T, 1), K // 256))
 
 
 def sparse_mla_decode(q, kv, ids, scale, splits: int = 16):

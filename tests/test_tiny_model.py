@@ -127,10 +127,10 @@ def test_mla_split_policy():
     """Few queries split the selection (>= 256 keys per split, <= 32 splits); 74+ run unsplit."""
     from cxldsagr_b200 import ops
 
-    assert ops.mla_splits(1) == 4 and ops.mla_splits(16) == 4 and ops.mla_splits(37) == 2
+    assert ops.mla_splits(1) == 8 and ops.mla_splits(16) == 4 and ops.mla_splits(37) == 2
     assert ops.mla_splits(74) == 1 and ops.mla_splits(2048) == 1
-    assert ops.mla_splits(1, K=512) == 1 and ops.mla_splits(1, K=1024) == 2
-    assert all(2048 // ops.mla_splits(T) >= 512 for T in range(1, 200))
+    assert ops.mla_splits(1, K=512) == 2 and ops.mla_splits(1, K=1024) == 4
+    assert all(2048 // ops.mla_splits(T) >= 256 for T in range(1, 200))
 
 
 @pytest.mark.parametrize("method", ["serial_sparse", "echo", "dense_prefetch"])
