@@ -337,13 +337,15 @@ void sparse_mla(const Tensor& q, const Tensor& kv, const Tensor& ids, double sca
     sp = ptr<float>(*scratch);
   }
   // impl 0 / 2: the cta_group::2 kernel (default); 1: the mma.sync baseline;
-  // 3: probe; 4 / 16+: the DSMEM-exchange tcgen05 kernel; 32+: pair kernel debug bits.
-  if (impl == 0 || impl == 2 || (impl >= 32 && impl < 64)) {
-    b200::launch_sparse_mla_2sm(a, int(splits), sp, stream(), nullptr, impl >= 32 ? int(impl - 32) : 0);
+  // 3: probe; 4 / 16-31: the DSMEM-exchange tcgen05 kernel; 32-63 and 128-255:
+  // pair kernel with debug bits impl - 32 / impl - 128 (bit 64: cp.async gathers).
+  if (impl == 0 || impl == 2 || (impl >= 32 && impl < 64) || (impl >= 128 && impl < 256)) {
+    const int dbg = impl >= 128 ? int(impl - 128) : impl >= 32 ? int(impl - 32) : 0;
+    b200::launch_sparse_mla_2sm(a, int(splits), sp, stream(), nullptr, dbg);
   } else if (impl == 3) {  // debug: raw first-tile scores of cluster 0 into `scratch` (splits must be 1)
     TORCH_CHECK(splits == 1 && scratch && scratch->defined() && scratch->numel() >= 2 * 128 * 32, "sparse_mla: probe buffer");
     b200::launch_sparse_mla_2sm(a, 1, nullptr, stream(), ptr<float>(*scratch));
-  } else if (impl == 4 || impl >= 16) {
+  } else if (impl == 4 || (impl >= 16 && impl < 32)) {
     b200::launch_sparse_mla_tc(a, int(splits), sp, stream(), impl >= 16 ? int(impl - 16) : 0);
   } else {
     b200::launch_sparse_mla_split(a, int(splits), sp, stream());

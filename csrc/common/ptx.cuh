@@ -131,6 +131,19 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* desc, uint64_
       : "memory");
 }
 
+// Row gather: rows y0..y3 of a 2-D tensor map whose box is (box_cols x 1),
+// starting at column c0, land as four consecutive box rows at dst.  c0 * the
+// element size must be a multiple of 16 bytes; rows past the tensor's extent
+// read the fill value (zero).
+__device__ __forceinline__ void tma_gather4_2d(uint32_t dst, const void* desc, uint64_t* bar, int c0, int y0,
+                                               int y1, int y2, int y3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(smem_u32(bar)), "r"(c0), "r"(y0), "r"(y1), "r"(y2), "r"(y3)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d(void* dst, const void* desc, uint64_t* bar, int c0,
                                             int c1, int c2) {
   asm volatile(

@@ -35,7 +35,9 @@
 // tile's full records for QK into a 2-stage ring that QK releases; warps
 // 8-11 gather the value dims into a 2-stage ring that PV releases (cp.async,
 // 16 bytes per lane, written in the 128-byte swizzled layout; padding rows
-// zero-filled); warp 12 allocates the pair's TMEM and, in CTA 0, issues every
+// zero-filled).  Debug bit 64 replaces the record gathers by TMA row gathers
+// (tile::gather4, four keys x one 64-dim chunk per instruction, issued by
+// one thread per ring): correct, but slower; warp 12 allocates the pair's TMEM and, in CTA 0, issues every
 // MMA from one thread (QK runs up to four tiles ahead of the softmax through
 // four S buffers); in CTA 1 it relays "rows landed" to CTA 0's barriers;
 // warps 13-15 only complete the register warpgroup.
@@ -195,6 +197,7 @@ __device__ unsigned long long g_pair_trace[4][kTraceTiles + 1][16];
 
 __global__ void __launch_bounds__(kThreads, 1)
     sparse_mla_pair_kernel(const __nv_bfloat16* __restrict__ q, const uint8_t* __restrict__ kv_rows,
+                           const __grid_constant__ CUtensorMap tma_kv, int use_tma,
                            const int* __restrict__ ids, int T, int K, int P, float scale_log2, int splits,
                            __nv_bfloat16* __restrict__ out, float* __restrict__ part_o,
                            float* __restrict__ part_lse, float* __restrict__ lse_out, int* err,
@@ -244,10 +247,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     const uint32_t relay = crank == 0 ? 1u : 0u;  // CTA 0's landing barriers also wait for CTA 1's relay
     mbar_init(&s.q_full, kOwnWarps + relay);
+    // TMA gathers: one issuing thread arrives (with the byte count) per stage.
+    const uint32_t gather_arrivals = use_tma ? 1u : uint32_t(kOwnWarps);
     for (int i = 0; i < STAGES; ++i) {
-      mbar_init(&s.own_full[i], kOwnWarps + relay);
+      mbar_init(&s.own_full[i], gather_arrivals + relay);
       mbar_init(&s.own_empty[i], 1);
-      mbar_init(&s.pv_full[i], kPvWarps + relay);
+      mbar_init(&s.pv_full[i], (use_tma ? 1u : uint32_t(kPvWarps)) + relay);
       mbar_init(&s.pv_empty[i], 1);
     }
     for (int i = 0; i < SBUF; ++i) {
@@ -293,6 +298,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.q_full);
     }
+    if (use_tma) {
+      // One thread of warp 0 gathers the tile's 32 records of this CTA with
+      // TMA row gathers (4 keys x one 64-dim chunk each, 128-byte swizzle:
+      // the layout the cp.async path writes); padding keys read zeros.
+      if (ow == 0) {
+        int next = load_id(k_begin + BNC * int(crank) + lane);
+        int issued = 0;
+        for (int i = 0; i < ntiles; ++i) {
+          const int st = i % STAGES;
+          const int my = next >= 0 ? next : P;  // row P lies past the tensor: zero fill
+          next = load_id(k_begin + (i + 1) * BN + BNC * int(crank) + lane);
+          const bool got = lane == 0 && mbar_wait(&s.own_empty[st], ((i / STAGES) & 1) ^ 1, err,
+                                                  kErrTimeoutSmemEmpty, abort_flag);
+          if (!__shfl_sync(0xffffffffu, got, 0)) break;
+          if (lane == 0) mbar_arrive_expect_tx(&s.own_full[st], BNC * D * 2);
+          __syncwarp();
+#pragma unroll 1
+          for (int g = 0; g < BNC / 4; ++g) {
+            // Every lane takes part in the shuffles; lane 0 issues.
+            const int y0 = __shfl_sync(0xffffffffu, my, 4 * g), y1 = __shfl_sync(0xffffffffu, my, 4 * g + 1);
+            const int y2 = __shfl_sync(0xffffffffu, my, 4 * g + 2), y3 = __shfl_sync(0xffffffffu, my, 4 * g + 3);
+            if (lane == 0) {
+#pragma unroll
+              for (int c = 0; c < kChunks; ++c)
+                tma_gather4_2d(own_chunk(st, c) + 4 * g * 128, &tma_kv, &s.own_full[st], 64 * c, y0, y1, y2, y3);
+            }
+          }
+          if (lane == 0) trace(i, 0);
+          issued = i + 1;
+        }
+        // An aborted CTA waits (bounded) for its last gathers before it exits.
+        if (lane == 0 && issued < ntiles && issued > 0)
+          mbar_wait(&s.own_full[(issued - 1) % STAGES], ((issued - 1) / STAGES) & 1, nullptr, 0, nullptr,
+                    1000000ull);
+      }
+    } else {
     // Warp ow gathers this CTA's keys ow, ow + 4, ... of every tile (lane j holds the id of key ow + 4j).
     const int nkeys = (BNC - ow + kOwnWarps - 1) / kOwnWarps;
     auto key_id = [&](int i) {
@@ -325,11 +366,53 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ow == 0 && lane == 0) trace(i, 0);
     }
     cp_async_wait_all();  // no copy may land after an aborted CTA has exited
+    }
   } else if (warp >= kPvWarp0 && warp < kPvWarp0 + kPvWarps) {
     // ------------------------------------------------------- value dims
     regs_dec<kRegsOther>();
     const int pw = warp - kPvWarp0;
     const int pv_chunk0 = 2 * int(crank);  // first value chunk of this CTA in each half
+    if (use_tma) {
+      // One thread of warp 0 gathers this CTA's value chunks of the tile's
+      // 64 keys (two per value half) with TMA row gathers.
+      if (pw == 0) {
+        int next0 = load_id(k_begin + lane), next1 = load_id(k_begin + BNC + lane);
+        int issued = 0;
+        for (int i = 0; i < ntiles; ++i) {
+          const int st = i % STAGES;
+          const int my0 = next0 >= 0 ? next0 : P, my1 = next1 >= 0 ? next1 : P;
+          next0 = load_id(k_begin + (i + 1) * BN + lane);
+          next1 = load_id(k_begin + (i + 1) * BN + BNC + lane);
+          const bool got = lane == 0 && mbar_wait(&s.pv_empty[st], ((i / STAGES) & 1) ^ 1, err,
+                                                  kErrTimeoutSmemEmpty, abort_flag);
+          if (!__shfl_sync(0xffffffffu, got, 0)) break;
+          if (lane == 0) mbar_arrive_expect_tx(&s.pv_full[st], BN * 4 * 128);
+          __syncwarp();
+#pragma unroll 1
+          for (int kh = 0; kh < 2; ++kh) {
+            const int my = kh == 0 ? my0 : my1;
+#pragma unroll 1
+            for (int g = 0; g < BNC / 4; ++g) {
+              const int y0 = __shfl_sync(0xffffffffu, my, 4 * g), y1 = __shfl_sync(0xffffffffu, my, 4 * g + 1);
+              const int y2 = __shfl_sync(0xffffffffu, my, 4 * g + 2), y3 = __shfl_sync(0xffffffffu, my, 4 * g + 3);
+              if (lane == 0) {
+#pragma unroll
+                for (int v = 0; v < 2; ++v)
+#pragma unroll
+                  for (int qc = 0; qc < 2; ++qc)
+                    tma_gather4_2d(pv_chunk(st, kh, v, qc) + 4 * g * 128, &tma_kv, &s.pv_full[st],
+                                   64 * (4 * v + pv_chunk0 + qc), y0, y1, y2, y3);
+              }
+            }
+          }
+          if (lane == 0) trace(i, 1);
+          issued = i + 1;
+        }
+        if (lane == 0 && issued < ntiles && issued > 0)
+          mbar_wait(&s.pv_full[(issued - 1) % STAGES], ((issued - 1) / STAGES) & 1, nullptr, 0, nullptr,
+                    1000000ull);
+      }
+    } else {
     // Warp pw gathers tile keys pw, pw + 4, ... (lane j holds the id of key pw + 4j).
     const int nkeys = (BN - pw + kPvWarps - 1) / kPvWarps;
     auto key_id = [&](int i) { return lane < nkeys ? load_id(k_begin + i * BN + pw + kPvWarps * lane) : -1; };
@@ -357,6 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (pw == 0 && lane == 0) trace(i, 1);
     }
     cp_async_wait_all();
+    }
   } else if (warp >= kMmaWarp) {
     regs_dec<kRegsOther>();
     if (warp != kMmaWarp) {
@@ -703,8 +787,18 @@ void launch_sparse_mla_2sm(const MLAArgs& a, int splits, float* scratch, cudaStr
   const float scale_log2 = a.scale * 1.4426950408889634f;
   float* part_o = splits > 1 ? scratch : nullptr;
   float* part_lse = splits > 1 ? scratch + size_t(splits) * a.T * a.H * DV : nullptr;
-  cuda_check(cudaLaunchKernelEx(&cfg, sparse_mla_pair_kernel, a.q, reinterpret_cast<const uint8_t*>(a.kv), a.ids,
-                                a.T, a.K, a.P, scale_log2, splits, a.out, part_o, part_lse, a.lse, a.err, dbg_s, dbg),
+  // Gather map over the KV rows: boxes of one row x 64 dims (128 bytes, the
+  // swizzle span); row P and beyond read zeros (padding keys).  Debug bit 64
+  // selects the TMA row gathers; the cp.async gather warps are the default
+  // (measured on B200, T = 1024 x top-2048: 0.754 ms with cp.async, 2.15 ms
+  // with TMA gather4: one thread issuing 136 gathers of 512 bytes per tile
+  // left the softmax waiting ~6K cycles per tile for S).
+  const int use_tma = (dbg & 64) ? 1 : 0;
+  const CUtensorMap tkv = make_tma_2d(a.kv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, uint64_t(std::max(a.P, 1)), D,
+                                      uint64_t(D) * 2, 64, 1);
+  cuda_check(cudaLaunchKernelEx(&cfg, sparse_mla_pair_kernel, a.q, reinterpret_cast<const uint8_t*>(a.kv), tkv,
+                                use_tma, a.ids, a.T, a.K, a.P, scale_log2, splits, a.out, part_o, part_lse, a.lse,
+                                a.err, dbg_s, dbg),
              "sparse_mla_2sm launch");
   if (splits > 1) launch_mla_combine(part_o, part_lse, splits, a.T, a.H, a.out, a.lse, stream, true);
 }
