@@ -106,6 +106,15 @@ def loaded_native_artifacts(maps_path: str = "/proc/self/maps", roots=(ROOT,)) -
     return out
 
 
+def built_native_artifacts(root: Path = ROOT) -> dict:
+    """The repository's built shared objects on disk: {path: sha256} (what a run
+    will load, independent of which of them this process has loaded yet)."""
+    out = {}
+    for p in sorted((root / "cxldsagr_b200").rglob("*.so")):
+        out[str(p.relative_to(root))] = digest(p)
+    return out
+
+
 def verify_native_artifacts(expected: dict, *, allow_additions: bool = False) -> None:
     got = loaded_native_artifacts()
     for path, d in expected.items():

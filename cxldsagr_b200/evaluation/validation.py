@@ -13,13 +13,15 @@ from __future__ import annotations
 import json
 from pathlib import Path
 
-from .provenance import identity_digest, loaded_native_artifacts, source_snapshot
+from .provenance import built_native_artifacts, identity_digest, source_snapshot
 
 
 def run_identity(config: dict) -> dict:
-    """The part of a run that must match between check, bench and profile."""
+    """The part of a run that must match between check, bench and profile: the
+    configuration, the source tree and the built native artifacts on disk (a
+    check and a bench of the same build agree whatever each has loaded so far)."""
     snap = source_snapshot()
-    return {"config": config, "source_tree": snap["tree_sha256"], "native": loaded_native_artifacts()}
+    return {"config": config, "source_tree": snap["tree_sha256"], "native": built_native_artifacts()}
 
 
 def write_receipt(path: Path, kind: str, config: dict, evidence: dict | None = None) -> dict:
