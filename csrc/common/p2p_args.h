@@ -3,6 +3,7 @@
 // symmetric heap.  Plain data (no device code), shared by kernels and bindings.
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_bf16.h>
 
 namespace b200 {
@@ -50,6 +51,10 @@ struct P2PArgs {
   // AG: this rank's shard and every rank's gather buffers ([2][M][K] fp8, [2][K/128][M] fp32)
   const uint8_t* a_local = nullptr;
   const float* sfa_local = nullptr;  // [K/128, S]
+  // AG: tensor map over a_local ([S, K], box BK x BM); tiles inside this
+  // rank's rows read it directly and never wait for a push.
+  CUtensorMap tma_local;
+  int local_map = 0;
   uint8_t* g[kMaxRanks] = {};
   float* gs[kMaxRanks] = {};
   // RS: every rank's receive slots ([2][world][S][N] bf16)

@@ -201,7 +201,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Work unit = (tile, K split); split-major so concurrent CTAs share a K range.
   const int num_units = num_tiles * splits;
   const int kps = (num_kb + splits - 1) / splits;
-  const int rot = MODE == kModeRS ? ((p2p.rank + 1) % p2p.world) * p2p.S / TM % num_m : 0;
+  // RS rotates the m blocks so ranks start on different owners; AG starts on
+  // this rank's own rows (their tiles need no peer data).
+  const int rot = MODE == kModeRS   ? ((p2p.rank + 1) % p2p.world) * p2p.S / TM % num_m
+                  : MODE == kModeAG ? (p2p.rank * p2p.S / TM) % num_m
+                                    : 0;
+  const int own_lo = p2p.rank * p2p.S, own_hi = own_lo + p2p.S;  // AG: this rank's rows
+  auto own_tile = [&](int m0) { return MODE == kModeAG && p2p.local_map && m0 >= own_lo && m0 + BM <= own_hi; };
   // AG / RS: this call's parity and flag targets (kernel arguments or the device op state).
   const P2PCall pc = (MODE == kModeAG || MODE == kModeRS) ? p2p_call(p2p) : P2PCall{0, 0ull, 0ull};
   // AG: A (tensor map rows) and its scales cover both parity halves of the gather buffer.
@@ -388,11 +394,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         int n0 = (tile / num_m) * BN;
         const int kb0 = sp * kps, kb1 = min(num_kb, kb0 + kps);
         if constexpr (MODE == kModeAG) {
-          if (!ag_wait_rows(p2p, pc.arrive_target, m0, M, ready, err, abort_flag)) {
-            ok = false;
-            break;
+          if (!own_tile(m0)) {
+            if (!ag_wait_rows(p2p, pc.arrive_target, m0, M, ready, err, abort_flag)) {
+              ok = false;
+              break;
+            }
+            fence_proxy_async_global();
           }
-          fence_proxy_async_global();
         }
         if constexpr (MODE == kModeGrouped) {
           const int e = unit_expert(grp, m0 / BM);
@@ -412,7 +420,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d_pair(s.b[stage], &tma_b, fb, kb * BK, n0 + int(crank) * BROWS);
           } else {
             mbar_arrive_expect_tx(&s.full[stage], BM * BK + BN * BK);
-            tma_load_2d(s.a[stage], &tma_a, &s.full[stage], kb * BK, a_row0 + m0);
+            if (own_tile(m0))
+              tma_load_2d(s.a[stage], &p2p.tma_local, &s.full[stage], kb * BK, m0 - own_lo);
+            else
+              tma_load_2d(s.a[stage], &tma_a, &s.full[stage], kb * BK, a_row0 + m0);
             tma_load_2d(s.b[stage], &tma_b, &s.full[stage], kb * BK, n0);
           }
           if (++stage == STAGES) {
@@ -609,9 +620,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (e < 0) continue;
         sfb_u = sfb + e * grp.sfb_expert_stride;
       }
+      const bool own_rows = own_tile(m0);
       if constexpr (MODE == kModeAG) {
         // Scales of peer rows were written by peers: acquire before reading them.
-        if (!ag_wait_rows(p2p, pc.arrive_target, m0, M, ready, err, abort_flag)) {
+        if (!own_rows && !ag_wait_rows(p2p, pc.arrive_target, m0, M, ready, err, abort_flag)) {
           ok = false;
           break;
         }
@@ -648,8 +660,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t bpar = (kcount >> 1) & 1;
           float sa = 0.f;
           if (row < M) {
-            const float* sp_ = sfa_k + static_cast<size_t>(kb) * lda_s + row;
-            sa = MODE == kModeAG ? __ldcg(sp_) : __ldg(sp_);
+            if (own_rows) {
+              sa = __ldg(p2p.sfa_local + static_cast<size_t>(kb) * p2p.S + (row - own_lo));
+            } else {
+              const float* sp_ = sfa_k + static_cast<size_t>(kb) * lda_s + row;
+              sa = MODE == kModeAG ? __ldcg(sp_) : __ldg(sp_);
+            }
           }
           // A warp's CPW (<= 128) columns touch at most two 128-wide weight scale blocks.
           const int nb0 = n0 / 128, nb1 = (n0 + CPW - 1) / 128;

@@ -131,6 +131,11 @@ void launch_fp8_gemm_ag(P2PArgs p, const uint8_t* B, int ldb, const float* sfb, 
   (void)kb;
   const int bn = fp8_gemm_p2p_bn(M, N, K);
   const CUtensorMap ta = make_tma_2d(g_local, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, int64_t(2) * M, K, K, BK, BM);
+  // This rank's own rows straight from its input (no wait for the push).
+  if (p.a_local != nullptr && p.sfa_local != nullptr) {
+    p.tma_local = make_tma_2d(p.a_local, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.S, K, K, BK, BM);
+    p.local_map = 1;
+  }
   const CUtensorMap tb = make_tma_2d(B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, ldb, BK, bn);
   if (p.grid != fp8_gemm_ag_grid(M, N, K)) throw std::invalid_argument("ag gemm: grid differs from the planned grid");
   size_t smem = 0;

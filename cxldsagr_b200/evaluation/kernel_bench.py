@@ -272,11 +272,14 @@ def bench_ag_gemm(M=1024, N=2304, Kdim=7168, **_):
     lin = Linear(w, s)
     x = torch.randn(M, Kdim, device=dev).bfloat16()
     qx = ops.quantize_act(x)
+    got, want = comm.ag_linear(lin, x, qx, M), lin(quantized=qx)
+    ops.check_errors(dev)
+    err = ((got.float() - want.float()).abs().max() / want.float().abs().max()).item()
     ms = time_fn(lambda: comm.ag_linear(lin, x, qx, M))
     ref = time_fn(lambda: lin(quantized=qx))
     flops = 2.0 * M * N * Kdim
     return {"op": "ag_gemm(world=1)", "M": M, "N": N, "K": Kdim, "ms": ms, "plain_gemm_ms": ref,
-            "tflops": flops / ms / 1e9}
+            "tflops": flops / ms / 1e9, "max_rel_diff_vs_plain": err}
 
 
 def bench_rs_gemm(M=1024, N=7168, Kdim=2304, **_):

@@ -797,3 +797,27 @@ def test_decode_gemv_bf16_fp32_out():
     ops.lib().bf16_gemm(x, 0, 7168, 0, w, 0, 7168, 0, out, 0, 3000, 0, 1, 3000, 7168, 1)
     want = x.float().cpu() @ w.float().cpu().T
     assert rel_err(out.cpu(), want) < 1e-3
+
+
+def test_ag_gemm_world1_matches_plain_gemm():
+    """The AG-GEMM on one rank (its own rows come straight from the local input)
+    against the plain FP8 GEMM of the same rows."""
+    from cxldsagr_b200.models.deepseek_v32.weights import Linear
+    from cxldsagr_b200.parallel.groups import single
+    from cxldsagr_b200.parallel.p2p import P2PComm
+
+    torch.manual_seed(44)
+    comm = P2PComm(single("cuda"))
+    try:
+        w, s = quantize_weight_blocks(torch.randn(2304, 7168, device=DEV) * 0.02)
+        lin = Linear(w, s)
+        for M in (1024, 256):
+            x = torch.randn(M, 7168, device=DEV).bfloat16()
+            qx = ops.quantize_act(x)
+            for _ in range(3):  # both parity halves and the reuse guard
+                got = comm.ag_linear(lin, x, qx, M)
+            want = lin(quantized=qx)
+            ops.check_errors(DEV)
+            assert rel_err(got.float().cpu(), want.float().cpu()) < 1e-2
+    finally:
+        comm.close()
