@@ -203,10 +203,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 void launch_bf16_gemm(const BF16GemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0 || a.batch <= 0) return;
-  if (decode_gemv_enabled() && a.batch == 1 && a.M <= kGemvMaxRows && a.K % 8 == 0 && (a.lda * 2) % 16 == 0 && (a.ldb * 2) % 16 == 0 &&
-      (reinterpret_cast<uintptr_t>(a.A) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.B) & 15) == 0) {
-    // Decode rows (the LM head of a one-token step): stream the weights once.
-    launch_bf16_gemv(a.A, int(a.lda), a.B, int(a.ldb), a.out, a.out_fp32, int(a.ldo), a.M, a.N, a.K, stream);
+  const bool al16 = (reinterpret_cast<uintptr_t>(a.A) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.B) & 15) == 0 &&
+                   (a.lda * 2) % 16 == 0 && (a.ldb * 2) % 16 == 0 &&
+                   (a.batch == 1 || ((a.a_batch * 2) % 16 == 0 && (a.b_batch * 2) % 16 == 0));
+  if (decode_gemv_enabled() && a.M <= kGemvMaxRows && a.K % 8 == 0 && al16 && a.batch <= 65535) {
+    // Decode rows (the LM head, the per-head absorb / expand of a one-token
+    // step): stream the weights once.
+    launch_bf16_gemv(a.A, int(a.lda), a.B, int(a.ldb), a.out, a.out_fp32, int(a.ldo), a.M, a.N, a.K, stream,
+                     a.batch, a.batch > 1 ? a.a_batch : 0, a.batch > 1 ? a.b_batch : 0,
+                     a.batch > 1 ? a.o_batch : 0);
     return;
   }
   constexpr int BN = 128, STAGES = 6;

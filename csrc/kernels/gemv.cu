@@ -149,9 +149,14 @@ template <int MR, bool OUT_F32>
 __global__ void __launch_bounds__(kGemvThreads) bf16_gemv_kernel(const __nv_bfloat16* __restrict__ X, int ldx,
                                                                  const __nv_bfloat16* __restrict__ W, int ldw,
                                                                  void* __restrict__ out, int ldo, int N, int K,
-                                                                 int ks) {
+                                                                 int ks, int64_t xb, int64_t wb, int64_t ob) {
   __shared__ float red[kGemvWarps * kNR * MR];
   const GemvLayout L(ks);
+  // Batch blockIdx.y (the per-head absorb / expand products): element strides.
+  X += blockIdx.y * xb;
+  W += blockIdx.y * wb;
+  out = OUT_F32 ? static_cast<void*>(static_cast<float*>(out) + blockIdx.y * ob)
+                : static_cast<void*>(static_cast<__nv_bfloat16*>(out) + blockIdx.y * ob);
   const int lane = threadIdx.x % 32;
   float acc[kNR][MR];
 #pragma unroll
@@ -193,10 +198,10 @@ __global__ void __launch_bounds__(kGemvThreads) bf16_gemv_kernel(const __nv_bflo
 
 // K split per row group: enough warps in flight to cover the weight stream's
 // latency on narrow layers (N / 2 warps alone leave most SMs idle), none on wide ones.
-int gemv_k_split(int N) {
+int gemv_k_split(int N, int batch = 1) {
   const int want = sm_count() * 48;  // warps
   int ks = 1;
-  while (ks < kGemvWarps && int64_t(N / kNR) * ks < want) ks *= 2;
+  while (ks < kGemvWarps && int64_t(N / kNR) * batch * ks < want) ks *= 2;
   return ks;
 }
 
@@ -236,18 +241,20 @@ void launch_fp8_gemv(const FP8GemmArgs& a, cudaStream_t stream) {
 }
 
 void launch_bf16_gemv(const __nv_bfloat16* x, int ldx, const __nv_bfloat16* w, int ldw, void* out, bool out_fp32,
-                      int ldo, int M, int N, int K, cudaStream_t stream) {
+                      int ldo, int M, int N, int K, cudaStream_t stream, int batch, int64_t xb, int64_t wb,
+                      int64_t ob) {
   if (K % 8) throw std::invalid_argument("bf16 gemv: K must be a multiple of 8");
-  const int ks = gemv_k_split(N);
+  if (batch < 1 || batch > 65535) throw std::invalid_argument("bf16 gemv: batch out of range");
+  const int ks = gemv_k_split(N, batch);
   const int rows_per_cta = kNR * (kGemvWarps / ks);
-  const int grid = (N + rows_per_cta - 1) / rows_per_cta;
+  const dim3 grid((N + rows_per_cta - 1) / rows_per_cta, batch);
   dispatch_rows(M, [&](auto mr) {
     if (out_fp32)
       bf16_gemv_kernel<decltype(mr)::value, true>
-          <<<grid, kGemvThreads, 0, stream>>>(x, ldx, w, ldw, out, ldo, N, K, ks);
+          <<<grid, kGemvThreads, 0, stream>>>(x, ldx, w, ldw, out, ldo, N, K, ks, xb, wb, ob);
     else
       bf16_gemv_kernel<decltype(mr)::value, false>
-          <<<grid, kGemvThreads, 0, stream>>>(x, ldx, w, ldw, out, ldo, N, K, ks);
+          <<<grid, kGemvThreads, 0, stream>>>(x, ldx, w, ldw, out, ldo, N, K, ks, xb, wb, ob);
   });
   cuda_check(cudaGetLastError(), "bf16 gemv launch");
 }

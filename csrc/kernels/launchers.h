@@ -51,7 +51,8 @@ constexpr int kGemvMaxRows = 4;
 bool gemv_fits(int M, int K, int64_t lda_bytes, int64_t ldw_bytes, const void* a, const void* w);
 void launch_fp8_gemv(const FP8GemmArgs& a, cudaStream_t stream);
 void launch_bf16_gemv(const __nv_bfloat16* x, int ldx, const __nv_bfloat16* w, int ldw, void* out, bool out_fp32,
-                      int ldo, int M, int N, int K, cudaStream_t stream);
+                      int ldo, int M, int N, int K, cudaStream_t stream, int batch = 1, int64_t xb = 0,
+                      int64_t wb = 0, int64_t ob = 0);
 
 // Communication-fused FP8 GEMMs over NVLink peer memory (P2PArgs in common/p2p_args.h).
 // AG: out[M, N] = (all-gather of every rank's [S, K] shard) . B^T; p.a_local / p.sfa_local

@@ -168,7 +168,7 @@ def _c4(n: int) -> int:
 
 
 def _blk(n: int) -> int:
-    """Bytes the CUDA caching allocator hands out for an n-byte request (512-byte rounding)."""
+    """An n-byte request rounded to the caching allocator's 512-byte granule (at least the bytes requested)."""
     return (n + 511) // 512 * 512
 
 
@@ -235,14 +235,18 @@ class ScopeMemory:
 class ScopeMemoryTracker:
     """Per-scope allocator accounting from the caching allocator's counters.
 
-    ``stats_fn`` returns a dict with ``allocated_bytes.all.current``,
-    ``allocated_bytes.all.peak`` and ``allocated_bytes.all.allocated``;
-    ``reset_fn`` sets the peak to the current value (defaults: the CUDA
-    allocator of ``device``).  Use :meth:`scope` as the model's scope hook."""
+    ``stats_fn`` returns a dict with ``<counter>.all.current``, ``.peak`` and
+    ``.allocated``; ``reset_fn`` sets the peak to the current value (defaults:
+    the CUDA allocator of ``device``).  Use :meth:`scope` as the model's scope
+    hook.  The default counter, ``requested_bytes``, counts the bytes the code
+    asked for; ``allocated_bytes`` counts the caching allocator's blocks, which
+    add its slack: sizes round up to 512 bytes, and a request served from a
+    cached block of the large pool takes the whole block when the remainder
+    would be under 1 MiB, so the same step can charge different bytes
+    depending on what the cache held."""
 
-    CUR, PEAK, CUM = "allocated_bytes.all.current", "allocated_bytes.all.peak", "allocated_bytes.all.allocated"
-
-    def __init__(self, device=None, *, stats_fn=None, reset_fn=None):
+    def __init__(self, device=None, *, stats_fn=None, reset_fn=None, counter: str = "requested_bytes"):
+        self.CUR, self.PEAK, self.CUM = (f"{counter}.all.current", f"{counter}.all.peak", f"{counter}.all.allocated")
         self.stats_fn = stats_fn or (lambda: torch.cuda.memory_stats(device))
         self.reset_fn = reset_fn or (lambda: torch.cuda.reset_peak_memory_stats(device))
         self._stack: list[list] = []     # [name, entry_current, running_peak, entry_cumulative]

@@ -64,8 +64,8 @@ class _FakeAllocator:
         self.cur -= n
 
     def stats(self):
-        return {"allocated_bytes.all.current": self.cur, "allocated_bytes.all.peak": self.peak,
-                "allocated_bytes.all.allocated": self.cum}
+        return {f"{c}.all.{k}": v for c in ("allocated_bytes", "requested_bytes")
+                for k, v in (("current", self.cur), ("peak", self.peak), ("allocated", self.cum))}
 
     def reset(self):
         self.peak = self.cur
