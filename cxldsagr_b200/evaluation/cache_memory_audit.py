@@ -230,6 +230,7 @@ class ScopeMemory:
     peak_transient: int = 0     # max over calls: peak live bytes above the bytes live at entry
     retained: int = 0           # sum over calls: bytes still live at exit beyond entry
     allocated: int = 0          # sum over calls: bytes handed out inside the scope
+    block_peak_transient: int = 0   # peak_transient in allocator blocks (requests plus the cache's slack)
 
 
 class ScopeMemoryTracker:
@@ -247,30 +248,40 @@ class ScopeMemoryTracker:
 
     def __init__(self, device=None, *, stats_fn=None, reset_fn=None, counter: str = "requested_bytes"):
         self.CUR, self.PEAK, self.CUM = (f"{counter}.all.current", f"{counter}.all.peak", f"{counter}.all.allocated")
+        self.BCUR, self.BPEAK = "allocated_bytes.all.current", "allocated_bytes.all.peak"
         self.stats_fn = stats_fn or (lambda: torch.cuda.memory_stats(device))
         self.reset_fn = reset_fn or (lambda: torch.cuda.reset_peak_memory_stats(device))
-        self._stack: list[list] = []     # [name, entry_current, running_peak, entry_cumulative]
+        # [name, entry_current, running_peak, entry_cumulative, block_entry, block_running_peak]
+        self._stack: list[list] = []
         self.rows: dict[str, ScopeMemory] = {}
+
+    def _block(self, s: dict, key: str) -> int:
+        return s.get(key, 0)
 
     def _enter(self, name: str):
         s = self.stats_fn()
         if self._stack:
             top = self._stack[-1]
             top[2] = max(top[2], s[self.PEAK])
+            top[5] = max(top[5], self._block(s, self.BPEAK))
         self.reset_fn()
-        self._stack.append([name, s[self.CUR], s[self.CUR], s[self.CUM]])
+        b = self._block(s, self.BCUR)
+        self._stack.append([name, s[self.CUR], s[self.CUR], s[self.CUM], b, b])
 
     def _exit(self):
         s = self.stats_fn()
-        name, entry, peak, cum = self._stack.pop()
+        name, entry, peak, cum, bentry, bpeak = self._stack.pop()
         peak = max(peak, s[self.PEAK])
+        bpeak = max(bpeak, self._block(s, self.BPEAK))
         row = self.rows.setdefault(name, ScopeMemory())
         row.calls += 1
         row.peak_transient = max(row.peak_transient, peak - entry)
+        row.block_peak_transient = max(row.block_peak_transient, bpeak - bentry)
         row.retained += s[self.CUR] - entry
         row.allocated += s[self.CUM] - cum
         if self._stack:
             self._stack[-1][2] = max(self._stack[-1][2], peak)
+            self._stack[-1][5] = max(self._stack[-1][5], bpeak)
         self.reset_fn()
 
     @contextmanager
@@ -297,8 +308,10 @@ def audit_scopes(rows: dict, allowance: WorkspaceAllowance, *, mapping=None) -> 
         comp = mapping.get(name)
         if comp is None:
             continue
-        peak = row["peak_transient"] if isinstance(row, dict) else row.peak_transient
-        checked[name] = {"component": comp, "peak_transient": peak, "allowance": limits[comp]}
+        r = row if isinstance(row, dict) else asdict(row)
+        peak = r["peak_transient"]
+        checked[name] = {"component": comp, "peak_transient": peak, "allowance": limits[comp],
+                         "block_peak_transient": r.get("block_peak_transient", peak)}
         if peak > limits[comp]:
             violations.append(name)
     return {"checked": checked, "violations": violations, "ok": not violations, "allowance": limits}

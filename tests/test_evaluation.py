@@ -89,7 +89,8 @@ def test_scope_memory_tracker_nested_peaks():
         fa.alloc(700)
         fa.free(700)
     rows = tr.summary()
-    assert rows["indexer_select"] == {"calls": 2, "peak_transient": 700, "retained": 0, "allocated": 1200}
+    assert rows["indexer_select"] == {"calls": 2, "peak_transient": 700, "retained": 0, "allocated": 1200,
+                                      "block_peak_transient": 700}
     assert rows["sparse_mla"]["peak_transient"] == 200
     # the child's peak (1000 + 100 + 500) counts for the enclosing scope
     assert rows["attention"]["peak_transient"] == 600 and rows["attention"]["retained"] == 50
