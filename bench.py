@@ -56,6 +56,11 @@ def parse():
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--e2e-steps", type=int, default=2)
     p.add_argument("--profile", action="store_true", help="print a per-scope device-time breakdown to stderr")
+    p.add_argument("--cuda-profiler-extend", action="store_true",
+                   help="after warm-up, bracket one extend (graph replay) with cudaProfilerStart/Stop, so that "
+                        "ncu --profile-from-start off captures only the extend's kernels")
+    p.add_argument("--no-pdl", action="store_true",
+                   help="launch every kernel in plain stream order (no programmatic dependent launch)")
     p.add_argument("--parallel", default="dp", choices=["dp", "sp"],
                    help="dp: every rank serves its own request (weak scaling); sp: one request across all ranks "
                         "(sequence-parallel attention, column/row-parallel dense MLP, expert-parallel MoE)")
@@ -314,6 +319,8 @@ def main():
     if args.no_fused_select:
         for block in model.blocks:
             block.attention.fused_select = False
+    if args.no_pdl:
+        ops.lib().set_pdl(False)
     select_rows = model.blocks[0].attention.select_rows
     del src
     torch.cuda.empty_cache()
@@ -360,6 +367,21 @@ def main():
         step()
     barrier()
     ops.check_errors(dev)
+    if args.cuda_profiler_extend:
+        model.reset()
+        model.prefill(hist)
+        if offload:
+            model.clear_residency()
+        torch.cuda.synchronize(dev)
+        torch.cuda.profiler.start()
+        if graph is not None:
+            graph.replay(ext)
+        else:
+            model.extend(ext)
+        torch.cuda.synchronize(dev)
+        torch.cuda.profiler.stop()
+        if graph is not None:
+            graph.rollback()
     if args.profile:
         from cxldsagr_b200.utils.tracing import EventScope
 
@@ -493,6 +515,7 @@ def main():
                 "extend": A,
                 "chunk": args.chunk,
                 "select_rows": select_rows, "fused_select": not args.no_fused_select,
+                "pdl": not args.no_pdl,
                 "cache_method": args.method,
                 "pool_tokens": (H + A) if offload else None,
                 "extend_residency": "cold (HBM copies of the history dropped before the extend)" if offload else "resident",

@@ -216,6 +216,15 @@ void linear_f32(const Tensor& x, const Tensor& W, Tensor& out) {
                           ptr<float>(out), stream());
 }
 
+void l2_prefetch(const Tensor& t, int64_t bytes) {
+  CHECK_CUDA(t);
+  TORCH_CHECK(t.is_contiguous(), "l2_prefetch: contiguous tensor");
+  const int64_t total = t.numel() * t.element_size();
+  const int64_t n = bytes < 0 ? total : std::min(bytes, total);
+  c10::cuda::CUDAGuard g(t.device());
+  b200::launch_l2_prefetch(t.data_ptr(), n / 16 * 16, stream());
+}
+
 void embed(const Tensor& ids, const Tensor& table, Tensor& out, int64_t row0, int64_t vocab_total) {
   CHECK_CUDA(ids); CHECK_DTYPE(ids, torch::kInt64); CHECK_DTYPE(table, torch::kBFloat16); CHECK_DTYPE(out, torch::kBFloat16);
   TORCH_CHECK(table.is_contiguous() && out.is_contiguous() && ids.is_contiguous(), "embed layout");
@@ -827,6 +836,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("index_k", &index_k);
   m.def("index_q", &index_q);
   m.def("linear_f32", &linear_f32);
+  m.def("l2_prefetch", &l2_prefetch, py::arg("t"), py::arg("bytes") = int64_t(-1));
+  m.def("set_pdl", [](bool on) { b200::pdl_flag() = on; },
+        "programmatic dependent launch of the decode-path kernels (default on)");
+  m.def("pdl_enabled", []() { return b200::pdl_flag(); });
   m.def("embed", &embed, py::arg("ids"), py::arg("table"), py::arg("out"), py::arg("row0") = int64_t(0),
         py::arg("vocab_total") = int64_t(0));
   m.def("indexer_logits", &indexer_logits);

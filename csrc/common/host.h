@@ -7,12 +7,40 @@
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 namespace b200 {
 
 inline void cuda_check(cudaError_t e, const char* what) {
   if (e != cudaSuccess)
     throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// Programmatic dependent launch (PDL).  A kernel launched through launch_pdl
+// may start while the previous kernel of the stream is still running; it
+// must call pdl_wait() (griddepcontrol.wait: the previous grid has completed
+// and its writes are visible) in every CTA before it reads or writes anything
+// that kernel touches, and may do independent work (reading weights, barrier
+// setup) before.  Kernels call pdl_trigger() early so that their successor
+// can be scheduled onto SMs they leave free.  Off: plain stream order.
+inline bool& pdl_flag() {
+  static bool on = true;
+  return on;
+}
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       const char* what, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_flag() ? 1 : 0;
+  cuda_check(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), what);
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,

@@ -78,11 +78,25 @@ constexpr int kNormMaxChunks = 4;  // D <= 256 * 8 * 4 = 8192
 
 __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(NormArgs a) {
   __shared__ float red[kNormThreads / 32];
-  __shared__ alignas(16) __nv_bfloat16 srow[8192];
   const int row = blockIdx.x;
+  const int nchunk = a.D / 8;
+  // The norm weight does not depend on the previous kernel: load it before
+  // waiting on that kernel (programmatic dependent launch).
+  float w[kNormMaxChunks][8];
+#pragma unroll
+  for (int c = 0; c < kNormMaxChunks; ++c) {
+    const int idx = threadIdx.x + c * kNormThreads;
+    if (idx < nchunk) {
+      const float4 w0 = *reinterpret_cast<const float4*>(a.weight + idx * 8);
+      const float4 w1 = *reinterpret_cast<const float4*>(a.weight + idx * 8 + 4);
+      w[c][0] = w0.x; w[c][1] = w0.y; w[c][2] = w0.z; w[c][3] = w0.w;
+      w[c][4] = w1.x; w[c][5] = w1.y; w[c][6] = w1.z; w[c][7] = w1.w;
+    }
+  }
+  pdl_trigger();
+  pdl_wait();
   const __nv_bfloat16* x = a.x + row * a.ldx;
   const __nv_bfloat16* r = a.residual ? a.residual + row * a.ldr : nullptr;
-  const int nchunk = a.D / 8;
   float v[kNormMaxChunks][8];
   float ss = 0.f;
 #pragma unroll
@@ -118,33 +132,66 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(NormArgs a) {
   const float inv = rsqrtf(total / a.D + a.eps);
 #pragma unroll
   for (int c = 0; c < kNormMaxChunks; ++c) {
+    if (c * kNormThreads >= nchunk) break;  // uniform over the CTA
     const int idx = threadIdx.x + c * kNormThreads;
-    if (idx < nchunk) {
-      const float4 w0 = *reinterpret_cast<const float4*>(a.weight + idx * 8);
-      const float4 w1 = *reinterpret_cast<const float4*>(a.weight + idx * 8 + 4);
-      const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-      uint4 ov;
-      uint32_t* ow = reinterpret_cast<uint32_t*>(&ov);
+    const bool have = idx < nchunk;
+    uint4 ov = make_uint4(0, 0, 0, 0);
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&ov);
+    if (have) {
 #pragma unroll
       for (int t = 0; t < 4; ++t)
-        ow[t] = pack_bf16(v[c][2 * t] * inv * w[2 * t], v[c][2 * t + 1] * inv * w[2 * t + 1]);
+        ow[t] = pack_bf16(v[c][2 * t] * inv * w[c][2 * t], v[c][2 * t + 1] * inv * w[c][2 * t + 1]);
       if (a.out) *reinterpret_cast<uint4*>(a.out + row * a.ldo + idx * 8) = ov;
-      if (a.q) *reinterpret_cast<uint4*>(srow + idx * 8) = ov;
     }
-  }
-  if (a.q) {
-    __syncthreads();
-    // 1x128 groups: one warp per group, 4 elements per lane.
-    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    for (int g = warp; g < a.D / 128; g += kNormThreads / 32) {
-      const __nv_bfloat16* src = srow + g * 128 + lane * 4;
-      float f[4];
+    if (a.q) {
+      // 1x128 groups straight from registers: a group is 16 consecutive
+      // chunks, i.e. one half-warp (nchunk is a multiple of 16).
+      float f[8];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) f[t] = __bfloat162float(src[t]);
-      const float sc = quant_group_warp(f, a.q + row * a.ldq + g * 128);
-      if (lane == 0) a.sfa_t[static_cast<int64_t>(g) * a.lda_s + row] = sc;
+      for (int t = 0; t < 4; ++t) {
+        f[2 * t] = bf16_lo(ow[t]);
+        f[2 * t + 1] = bf16_hi(ow[t]);
+      }
+      float amax = 0.f;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) amax = fmaxf(amax, fabsf(f[t]));
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      amax = fmaxf(amax, 1e-4f);
+      const float scale = ue8m0_ceil(__fdiv_rn(amax, kFp8Max));
+      const float rs = __frcp_rn(scale);  // exact: scale is a power of two
+      if (have) {
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          lo |= static_cast<uint32_t>(to_e4m3(fminf(fmaxf(f[t] * rs, -kFp8Max), kFp8Max))) << (8 * t);
+          hi |= static_cast<uint32_t>(to_e4m3(fminf(fmaxf(f[4 + t] * rs, -kFp8Max), kFp8Max))) << (8 * t);
+        }
+        *reinterpret_cast<uint2*>(a.q + row * a.ldq + idx * 8) = make_uint2(lo, hi);
+        if (idx % 16 == 0) a.sfa_t[static_cast<int64_t>(idx / 16) * a.lda_s + row] = scale;
+      }
     }
   }
+}
+
+// ------------------------------------------------------------- L2 prefetch
+// Pulls a read-only range (a weight the stream reads soon) into L2 with bulk
+// prefetches of up to 64 KB each, so that a latency-bound stretch of kernels
+// (selection and sparse MLA at decode sizes) hides the DRAM time of the next
+// bandwidth-bound one.  The range must not be written by a kernel in flight.
+// The kernel waits on its predecessor before it exits, so that programmatic
+// dependents of it still see every earlier kernel complete.
+__global__ void l2_prefetch_kernel(const uint8_t* __restrict__ p, int64_t bytes) {
+  pdl_trigger();
+  constexpr int64_t kChunk = 1 << 16;
+  const int64_t n = (bytes + kChunk - 1) / kChunk;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t off = i * kChunk;
+    const uint32_t sz = uint32_t(min(kChunk, bytes - off));
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p + off)), "r"(sz)
+                 : "memory");
+  }
+  pdl_wait();
 }
 
 // ----------------------------------------------------------- quant_act
@@ -152,6 +199,8 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(NormArgs a) {
 __global__ void quant_act_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int rows,
                                  int D, uint8_t* __restrict__ q, int64_t ldq,
                                  float* __restrict__ sfa_t, int lda_s) {
+  pdl_trigger();
+  pdl_wait();
   const int groups = D / 128;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
@@ -169,6 +218,8 @@ __global__ void silu_mul_quant_kernel(const __nv_bfloat16* __restrict__ packed, 
                                       int rows, int I, __nv_bfloat16* __restrict__ h,
                                       uint8_t* __restrict__ q, float* __restrict__ sfa_t,
                                       int lda_s) {
+  pdl_trigger();
+  pdl_wait();
   const int groups = I / 128;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
@@ -211,6 +262,8 @@ __global__ void mla_q_rope_kernel(const __nv_bfloat16* __restrict__ q, int64_t l
                                   const float* __restrict__ positions,
                                   __nv_bfloat16* __restrict__ out, int64_t ldo_tok,
                                   int64_t ldo_head, int out_offset) {
+  pdl_trigger();
+  pdl_wait();
   const int half = rope / 2;
   const int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
   if (idx >= int64_t(T) * H * half) return;
@@ -244,6 +297,8 @@ __global__ void kv_finish_kernel(const __nv_bfloat16* __restrict__ kv, int64_t l
                                  uint8_t* __restrict__ packed, int* err) {
   __shared__ float red[4];
   __shared__ float bmax[4][4];
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
   const __nv_bfloat16* src = kv + t * ldkv;
   const int64_t drow = dst_row ? dst_row[t] : int64_t(t);
@@ -317,6 +372,8 @@ __global__ void index_k_kernel(const __nv_bfloat16* __restrict__ k, int64_t ldk,
                                const float* __restrict__ freqs,
                                const float* __restrict__ positions, uint8_t* __restrict__ k_q,
                                float* __restrict__ k_scale) {
+  pdl_trigger();
+  pdl_wait();
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (t >= T) return;
@@ -369,6 +426,8 @@ __global__ void index_q_kernel(const __nv_bfloat16* __restrict__ q, int64_t ldq,
                                const float* __restrict__ positions, uint8_t* __restrict__ q_q,
                                float* __restrict__ q_scale, const float* __restrict__ w_raw,
                                int w_split, float head_scale, float* __restrict__ weights) {
+  pdl_trigger();
+  pdl_wait();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (gw >= T * H) return;
@@ -407,6 +466,8 @@ __global__ void __launch_bounds__(256) linear_f32_kernel(const __nv_bfloat16* __
                                                          float* __restrict__ out) {
   __shared__ float xs[16][65];
   __shared__ float ws[64][65];
+  pdl_trigger();
+  pdl_wait();
   const int t0 = blockIdx.x * 16, h0 = blockIdx.y * 64;
   const int tx = threadIdx.x % 64, ty = threadIdx.x / 64;  // ty in [0,4)
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -443,6 +504,8 @@ __global__ void __launch_bounds__(256) linear_f32_kernel(const __nv_bfloat16* __
 __global__ void embed_kernel(const int64_t* __restrict__ ids, int T,
                              const __nv_bfloat16* __restrict__ table, int64_t rows, int64_t row0,
                              int64_t vocab_total, int D, __nv_bfloat16* __restrict__ out, int* err) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
   int64_t id = ids[t];
   if (id < 0 || id >= vocab_total) {
@@ -464,8 +527,18 @@ __global__ void embed_kernel(const int64_t* __restrict__ ids, int T,
 void launch_rms_norm(const NormArgs& a, cudaStream_t stream) {
   if (a.rows <= 0) return;
   if (a.D % 128 || a.D > 8192) throw std::invalid_argument("rms_norm: D must be a multiple of 128 and <= 8192");
-  rms_norm_kernel<<<a.rows, kNormThreads, 0, stream>>>(a);
+  launch_pdl(rms_norm_kernel, dim3(a.rows), dim3(kNormThreads), 0, stream, "rms_norm_kernel", a);
   cuda_check(cudaGetLastError(), "rms_norm launch");
+}
+
+void launch_l2_prefetch(const void* p, int64_t bytes, cudaStream_t stream) {
+  if ((reinterpret_cast<uintptr_t>(p) & 15) || bytes % 16)
+    throw std::invalid_argument("l2_prefetch: 16-byte aligned start and size");
+  if (bytes <= 0) return;
+  const int64_t chunks = (bytes + (1 << 16) - 1) >> 16;
+  const int blocks = int(std::min<int64_t>(32, (chunks + 63) / 64));
+  launch_pdl(l2_prefetch_kernel, dim3(blocks), dim3(64), 0, stream, "l2_prefetch launch",
+             reinterpret_cast<const uint8_t*>(p), bytes);
 }
 
 void launch_quant_act(const __nv_bfloat16* x, int64_t ldx, int rows, int D, uint8_t* q,
@@ -473,7 +546,7 @@ void launch_quant_act(const __nv_bfloat16* x, int64_t ldx, int rows, int D, uint
   if (rows <= 0) return;
   if (D % 128) throw std::invalid_argument("quant_act: D must be a multiple of 128");
   const int64_t warps = int64_t(rows) * (D / 128);
-  quant_act_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(x, ldx, rows, D, q, ldq, sfa_t, lda_s);
+  launch_pdl(quant_act_kernel, dim3((warps * 32 + 255) / 256), dim3(256), 0, stream, "quant_act_kernel", x, ldx, rows, D, q, ldq, sfa_t, lda_s);
   cuda_check(cudaGetLastError(), "quant_act launch");
 }
 
@@ -483,7 +556,7 @@ void launch_silu_mul_quant(const __nv_bfloat16* packed, int64_t ldp, int rows, i
   if (rows <= 0) return;
   if (I % 128) throw std::invalid_argument("silu_mul: I must be a multiple of 128");
   const int64_t warps = int64_t(rows) * (I / 128);
-  silu_mul_quant_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(packed, ldp, rows, I, h, q, sfa_t, lda_s);
+  launch_pdl(silu_mul_quant_kernel, dim3((warps * 32 + 255) / 256), dim3(256), 0, stream, "silu_mul_quant_kernel", packed, ldp, rows, I, h, q, sfa_t, lda_s);
   cuda_check(cudaGetLastError(), "silu_mul launch");
 }
 
@@ -492,7 +565,7 @@ void launch_mla_q_rope(const __nv_bfloat16* q, int64_t ldq, int T, int H, int no
                        int64_t ldo_tok, int64_t ldo_head, int out_offset, cudaStream_t stream) {
   const int64_t n = int64_t(T) * H * (rope / 2);
   if (n <= 0) return;
-  mla_q_rope_kernel<<<(n + 255) / 256, 256, 0, stream>>>(q, ldq, T, H, nope, rope, freqs, positions,
+  launch_pdl(mla_q_rope_kernel, dim3((n + 255) / 256), dim3(256), 0, stream, "mla_q_rope_kernel", q, ldq, T, H, nope, rope, freqs, positions,
                                                           out, ldo_tok, ldo_head, out_offset);
   cuda_check(cudaGetLastError(), "mla_q_rope launch");
 }
@@ -504,7 +577,7 @@ void launch_kv_finish(const __nv_bfloat16* kv, int64_t ldkv, int T, int L, int R
                       uint8_t* packed) {
   if (T <= 0) return;
   if (packed && (L != 512 || R != 64)) throw std::invalid_argument("kv_finish: FP8 records need L = 512, R = 64");
-  kv_finish_kernel<<<T, 128, 0, stream>>>(kv, ldkv, T, L, R, norm_w, eps, freqs, positions, out, ldo, dst_row,
+  launch_pdl(kv_finish_kernel, dim3(T), dim3(128), 0, stream, "kv_finish_kernel", kv, ldkv, T, L, R, norm_w, eps, freqs, positions, out, ldo, dst_row,
                                           out_rows, packed, err);
   cuda_check(cudaGetLastError(), "kv_finish launch");
 }
@@ -514,7 +587,7 @@ void launch_index_k(const __nv_bfloat16* k, int64_t ldk, int T, int D, int R,
                     const float* positions, uint8_t* k_q, float* k_scale, cudaStream_t stream) {
   if (T <= 0) return;
   if (D != 128) throw std::invalid_argument("index_k: head dim must be 128");
-  index_k_kernel<<<(T + 7) / 8, 256, 0, stream>>>(k, ldk, T, D, R, ln_w, ln_b, eps, freqs, positions, k_q, k_scale);
+  launch_pdl(index_k_kernel, dim3((T + 7) / 8), dim3(256), 0, stream, "index_k_kernel", k, ldk, T, D, R, ln_w, ln_b, eps, freqs, positions, k_q, k_scale);
   cuda_check(cudaGetLastError(), "index_k launch");
 }
 
@@ -524,7 +597,7 @@ void launch_index_q(const __nv_bfloat16* q, int64_t ldq, int T, int H, int D, in
   if (T <= 0) return;
   if (D != 128) throw std::invalid_argument("index_q: head dim must be 128");
   const int64_t warps = int64_t(T) * H;
-  index_q_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(q, ldq, T, H, D, R, freqs, positions, q_q, q_scale, w_raw, w_split, head_scale, weights);
+  launch_pdl(index_q_kernel, dim3((warps * 32 + 255) / 256), dim3(256), 0, stream, "index_q_kernel", q, ldq, T, H, D, R, freqs, positions, q_q, q_scale, w_raw, w_split, head_scale, weights);
   cuda_check(cudaGetLastError(), "index_q launch");
 }
 
@@ -532,7 +605,7 @@ void launch_linear_f32(const __nv_bfloat16* x, int64_t ldx, const float* W, int 
                        float* out, cudaStream_t stream) {
   if (T <= 0) return;
   dim3 grid((T + 15) / 16, (H + 63) / 64);
-  linear_f32_kernel<<<grid, 256, 0, stream>>>(x, ldx, W, T, H, K, out);
+  launch_pdl(linear_f32_kernel, dim3(grid), dim3(256), 0, stream, "linear_f32_kernel", x, ldx, W, T, H, K, out);
   cuda_check(cudaGetLastError(), "linear_f32 launch");
 }
 
@@ -541,7 +614,7 @@ void launch_embed(const int64_t* ids, int T, const __nv_bfloat16* table, int64_t
   if (T <= 0) return;
   if (D % 8) throw std::invalid_argument("embed: D must be a multiple of 8");
   if (row0 < 0 || row0 + rows > vocab_total) throw std::invalid_argument("embed: shard outside the vocabulary");
-  embed_kernel<<<T, 256, 0, stream>>>(ids, T, table, rows, row0, vocab_total, D, out, err);
+  launch_pdl(embed_kernel, dim3(T), dim3(256), 0, stream, "embed_kernel", ids, T, table, rows, row0, vocab_total, D, out, err);
   cuda_check(cudaGetLastError(), "embed launch");
 }
 

@@ -24,6 +24,7 @@ namespace {
 constexpr int kGemvThreads = 256;
 constexpr int kGemvWarps = kGemvThreads / 32;
 constexpr int kNR = 2;  // weight rows per warp
+constexpr int kPrefetchSteps = 4;  // warp steps of weights pulled into L2 before the dependency wait
 
 __device__ __forceinline__ void fp8x16_to_f32(const uint4& v, float (&f)[16]) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -109,6 +110,18 @@ __global__ void __launch_bounds__(kGemvThreads) fp8_gemv_kernel(const uint8_t* _
   for (int r = 0; r < kNR; ++r)
 #pragma unroll
     for (int m = 0; m < MR; ++m) acc[r][m] = 0.f;
+  // The weights do not depend on the previous kernel: start pulling this
+  // warp's first steps into L2 before waiting on it.
+  if (L.n0 < N)
+#pragma unroll
+    for (int u = 0; u < kPrefetchSteps; ++u) {
+      const int k0 = (L.kpart * 32 + lane) * 16 + u * L.ks * 512;
+#pragma unroll
+      for (int r = 0; r < kNR; ++r)
+        if (L.n0 + r < N && k0 < K) prefetch_l2(W + int64_t(L.n0 + r) * ldw + k0);
+    }
+  pdl_trigger();
+  pdl_wait();
   if (L.n0 < N) {
     for (int k0 = (L.kpart * 32 + lane) * 16; k0 < K; k0 += L.ks * 512) {
       const int kb = k0 / 128;
@@ -163,6 +176,16 @@ __global__ void __launch_bounds__(kGemvThreads) bf16_gemv_kernel(const __nv_bflo
   for (int r = 0; r < kNR; ++r)
 #pragma unroll
     for (int m = 0; m < MR; ++m) acc[r][m] = 0.f;
+  if (L.n0 < N)
+#pragma unroll
+    for (int u = 0; u < kPrefetchSteps; ++u) {
+      const int k0 = (L.kpart * 32 + lane) * 8 + u * L.ks * 256;
+#pragma unroll
+      for (int r = 0; r < kNR; ++r)
+        if (L.n0 + r < N && k0 < K) prefetch_l2(W + int64_t(L.n0 + r) * ldw + k0);
+    }
+  pdl_trigger();
+  pdl_wait();
   if (L.n0 < N) {
     for (int k0 = (L.kpart * 32 + lane) * 8; k0 < K; k0 += L.ks * 256) {
       uint4 wv[kNR];
@@ -233,7 +256,7 @@ void launch_fp8_gemv(const FP8GemmArgs& a, cudaStream_t stream) {
   const int rows_per_cta = kNR * (kGemvWarps / ks);
   const int grid = (a.N + rows_per_cta - 1) / rows_per_cta;
   dispatch_rows(a.M, [&](auto mr) {
-    fp8_gemv_kernel<decltype(mr)::value><<<grid, kGemvThreads, 0, stream>>>(
+    launch_pdl(fp8_gemv_kernel<decltype(mr)::value>, dim3(grid), dim3(kGemvThreads), 0, stream, "fp8_gemv_kernel", 
         a.A, a.lda, a.sfa, a.lda_s, a.B, a.ldb, a.sfb, (a.K + 127) / 128, a.out, a.ldo, a.residual, a.ldr, a.N, a.K,
         ks);
   });
@@ -250,11 +273,9 @@ void launch_bf16_gemv(const __nv_bfloat16* x, int ldx, const __nv_bfloat16* w, i
   const dim3 grid((N + rows_per_cta - 1) / rows_per_cta, batch);
   dispatch_rows(M, [&](auto mr) {
     if (out_fp32)
-      bf16_gemv_kernel<decltype(mr)::value, true>
-          <<<grid, kGemvThreads, 0, stream>>>(x, ldx, w, ldw, out, ldo, N, K, ks, xb, wb, ob);
+      launch_pdl(bf16_gemv_kernel<decltype(mr)::value, true>, dim3(grid), dim3(kGemvThreads), 0, stream, "bf16_gemv_kernel", x, ldx, w, ldw, out, ldo, N, K, ks, xb, wb, ob);
     else
-      bf16_gemv_kernel<decltype(mr)::value, false>
-          <<<grid, kGemvThreads, 0, stream>>>(x, ldx, w, ldw, out, ldo, N, K, ks, xb, wb, ob);
+      launch_pdl(bf16_gemv_kernel<decltype(mr)::value, false>, dim3(grid), dim3(kGemvThreads), 0, stream, "bf16_gemv_kernel", x, ldx, w, ldw, out, ldo, N, K, ks, xb, wb, ob);
   });
   cuda_check(cudaGetLastError(), "bf16 gemv launch");
 }

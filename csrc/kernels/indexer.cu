@@ -96,6 +96,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     indexer_kernel(const __grid_constant__ CUtensorMap tma_q,
                    const __grid_constant__ CUtensorMap tma_k, const float* __restrict__ w,
                    const float* __restrict__ kscale, IndexerOut o, Schedule sch, int* err) {
+  pdl_trigger();
+  pdl_wait();
   if (sch.any_flag != nullptr && __ldcg(sch.any_flag) == 0) return;  // uniform: nothing to redo
   extern __shared__ uint8_t smem_raw[];
   auto& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -346,7 +348,7 @@ void launch_indexer_logits(const IndexerArgs& a, cudaStream_t stream) {
   auto kern = a.select ? indexer_kernel<true> : indexer_kernel<false>;
   cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
              "indexer smem attribute");
-  kern<<<grid, kThreads, smem, stream>>>(tq, tk, a.w, a.kscale, o, sch, a.err);
+  launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, "indexer launch", tq, tk, a.w, a.kscale, o, sch, a.err);
   cuda_check(cudaGetLastError(), "indexer launch");
 }
 

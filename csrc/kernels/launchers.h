@@ -219,6 +219,8 @@ void launch_linear_f32(const __nv_bfloat16* x, int64_t ldx, const float* W, int 
 
 // table holds rows [row0, row0 + rows) of a vocab_total-row table (shard
 // rows outside it embed as zeros).
+// Bulk L2 prefetch of a read-only range (16-byte aligned start and size).
+void launch_l2_prefetch(const void* p, int64_t bytes, cudaStream_t stream);
 void launch_embed(const int64_t* ids, int T, const __nv_bfloat16* table, int64_t rows, int64_t row0,
                   int64_t vocab_total, int D, __nv_bfloat16* out, int* err, cudaStream_t stream);
 

@@ -281,6 +281,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 __global__ void mla_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
                                    int splits, int T, int H, __nv_bfloat16* __restrict__ out,
                                    float* __restrict__ lse_out) {
+  pdl_trigger();
+  pdl_wait();
   const int th = blockIdx.x;  // t * H + h
   float mx = -INFINITY;
   for (int sidx = 0; sidx < splits; ++sidx) mx = fmaxf(mx, part_lse[int64_t(sidx) * T * H + th]);
@@ -306,6 +308,8 @@ __global__ void mla_combine_kernel(const float* __restrict__ part_o, const float
 __global__ void mla_combine_hm_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
                                       int splits, int T, int H, __nv_bfloat16* __restrict__ out,
                                       float* __restrict__ lse_out) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x, d0 = blockIdx.y * 8;
   for (int h = threadIdx.x; h < H; h += blockDim.x) {
     const int64_t th = int64_t(t) * H + h;
@@ -366,9 +370,11 @@ void launch_sparse_mla_split(const MLAArgs& a, int splits, float* scratch, cudaS
 void launch_mla_combine(const float* part_o, const float* part_lse, int splits, int T, int H,
                         __nv_bfloat16* out, float* lse, cudaStream_t stream, bool head_minor) {
   if (head_minor)
-    mla_combine_hm_kernel<<<dim3(T, DV / 8), 128, 0, stream>>>(part_o, part_lse, splits, T, H, out, lse);
+    launch_pdl(mla_combine_hm_kernel, dim3(T, DV / 8), dim3(128), 0, stream, "mla_combine_hm_kernel", part_o,
+               part_lse, splits, T, H, out, lse);
   else
-    mla_combine_kernel<<<T * H, 128, 0, stream>>>(part_o, part_lse, splits, T, H, out, lse);
+    launch_pdl(mla_combine_kernel, dim3(T * H), dim3(128), 0, stream, "mla_combine_kernel", part_o, part_lse, splits,
+               T, H, out, lse);
   cuda_check(cudaGetLastError(), "mla_combine launch");
 }
 

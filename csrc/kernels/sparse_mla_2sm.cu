@@ -203,6 +203,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                            float* __restrict__ part_lse, float* __restrict__ lse_out, int* err,
                            float* __restrict__ dbg_s, int dbg) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+  pdl_trigger();
+  pdl_wait();
   uint8_t* base = smem_raw;
   const uint32_t sbase = smem_u32(base);
   if (sbase & 1023u) {  // uniform over the cluster: every CTA has the same layout
@@ -777,13 +779,15 @@ void launch_sparse_mla_2sm(const MLAArgs& a, int splits, float* scratch, cudaStr
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // the kernel starts with pdl_wait()
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_flag() ? 2 : 1;
   const float scale_log2 = a.scale * 1.4426950408889634f;
   float* part_o = splits > 1 ? scratch : nullptr;
   float* part_lse = splits > 1 ? scratch + size_t(splits) * a.T * a.H * DV : nullptr;

@@ -37,6 +37,8 @@ __global__ void __launch_bounds__(kThreads) topk_kernel(const float* __restrict_
                                                         float* __restrict__ values,
                                                         int* __restrict__ ids, int* err,
                                                         const int* __restrict__ only_rows) {
+  pdl_trigger();
+  pdl_wait();
   // With only_rows set, rows not flagged there were finished by topk2_kernel.
   if (only_rows && !only_rows[blockIdx.x]) return;
   __shared__ uint32_t hist[256];
@@ -202,6 +204,8 @@ __global__ void __launch_bounds__(kThreads2) topk2_kernel(const float* __restric
                                                           int* __restrict__ ids, int* __restrict__ overflow,
                                                           int* err, bool index_order,
                                                           const int* __restrict__ only_rows) {
+  pdl_trigger();
+  pdl_wait();
   // With only_rows set, rows not flagged there are left as they are.
   if (only_rows && !only_rows[blockIdx.x]) return;
   extern __shared__ uint8_t dyn[];
@@ -600,17 +604,17 @@ void launch_topk_causal(const float* scores, int64_t ld, int R, int N, int k, in
   if (R <= 0) return;
   if (k < 1 || k > kMaxK) throw std::invalid_argument("topk: k must be in [1, 2048]");
   if (overflow == nullptr) {
-    topk_kernel<<<R, kThreads, 0, stream>>>(scores, ld, N, k, causal_start, values, ids, err, nullptr);
+    launch_pdl(topk_kernel, dim3(R), dim3(kThreads), 0, stream, "topk_kernel", scores, ld, N, k, causal_start, values, ids, err, nullptr);
     cuda_check(cudaGetLastError(), "topk launch");
     return;
   }
   const size_t smem = size_t(kBins) * 4 + size_t(kMaxK) * 8 + size_t(kSecCap) * 8;
   cuda_check(cudaFuncSetAttribute(topk2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
              "topk2 smem attribute");
-  topk2_kernel<<<R, kThreads2, smem, stream>>>(scores, ld, N, k, causal_start, values, ids, overflow, err,
+  launch_pdl(topk2_kernel, dim3(R), dim3(kThreads2), smem, stream, "topk2_kernel", scores, ld, N, k, causal_start, values, ids, overflow, err,
                                                 index_order, only_rows);
   cuda_check(cudaGetLastError(), "topk2 launch");
-  topk_kernel<<<R, kThreads, 0, stream>>>(scores, ld, N, k, causal_start, values, ids, err, overflow);
+  launch_pdl(topk_kernel, dim3(R), dim3(kThreads), 0, stream, "topk_kernel", scores, ld, N, k, causal_start, values, ids, err, overflow);
   cuda_check(cudaGetLastError(), "topk fallback launch");
 }
 

@@ -114,6 +114,8 @@ __global__ void __launch_bounds__(kThrThreads) select_threshold_kernel(const flo
   __shared__ uint32_t warp_sum[kThrThreads / 32];
   __shared__ uint64_t red[2 * (kThrThreads / 32)];
   __shared__ uint32_t s_out[3];
+  pdl_trigger();
+  pdl_wait();
   const int q = blockIdx.x, tid = threadIdx.x;
   const int n_vis = min(N, query_start + q + 1);
   if (n_vis <= cap) {
@@ -165,6 +167,8 @@ __global__ void __launch_bounds__(kCandThreads) topk_candidates_kernel(
     int width, float* __restrict__ values, int* __restrict__ ids, int* __restrict__ flags, int* __restrict__ overflow,
     int* __restrict__ any_flag, bool index_order) {
   extern __shared__ uint8_t dyn[];
+  pdl_trigger();
+  pdl_wait();
   uint64_t* buf = reinterpret_cast<uint64_t*>(dyn);             // cap candidates
   uint32_t* hist = reinterpret_cast<uint32_t*>(buf + cap);      // 4096 bins during the levels, then:
   uint64_t* sel = reinterpret_cast<uint64_t*>(hist);            //   kMaxK sort keys (sort path), or
@@ -364,7 +368,7 @@ void launch_indexer_select(const IndexerSelectArgs& a, cudaStream_t stream) {
     s.row_flags = nullptr;
     launch_indexer_logits(s, stream);
     const int ns = (x.N + a.sample_stride - 1) / a.sample_stride;
-    select_threshold_kernel<<<x.Q, kThrThreads, 0, stream>>>(a.sample_logits, a.ld_sample, x.N, ns, a.sample_stride,
+    launch_pdl(select_threshold_kernel, dim3(x.Q), dim3(kThrThreads), 0, stream, "select_threshold_kernel", a.sample_logits, a.ld_sample, x.N, ns, a.sample_stride,
                                                               x.query_start, a.k, a.cand_cap, a.thresh);
     cuda_check(cudaGetLastError(), "indexer select threshold launch");
   }
@@ -383,7 +387,7 @@ void launch_indexer_select(const IndexerSelectArgs& a, cudaStream_t stream) {
   const size_t smem = indexer_select_cand_smem(a.cand_cap);
   cuda_check(cudaFuncSetAttribute(topk_candidates_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
              "indexer select candidates smem");
-  topk_candidates_kernel<<<x.Q, kCandThreads, smem, stream>>>(a.cand, a.cand_count, a.cand_cap, x.N, x.query_start,
+  launch_pdl(topk_candidates_kernel, dim3(x.Q), dim3(kCandThreads), smem, stream, "topk_candidates_kernel", a.cand, a.cand_count, a.cand_cap, x.N, x.query_start,
                                                               a.k, a.width, a.values, a.ids, a.flags, a.overflow,
                                                               a.any_flag, a.index_order);
   cuda_check(cudaGetLastError(), "indexer select candidates launch");

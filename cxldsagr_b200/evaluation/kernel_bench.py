@@ -296,9 +296,27 @@ def bench_rs_gemm(M=1024, N=7168, Kdim=2304, **_):
             "tflops": flops / ms / 1e9}
 
 
+def bench_copy_curve(**_):
+    """Device-to-device copy time against size (L2 flushed before each call): the
+    size-dependent floor of any kernel that streams that many bytes once
+    (launch, ramp-up and tail included), to set the decode linears against."""
+    dev = "cuda"
+    hbm = _peaks()["hbm_gbs"]
+    rows = []
+    for mb in (8, 16, 32, 64, 128, 256):
+        n = mb << 20
+        src = torch.empty(n, dtype=torch.uint8, device=dev).fill_(1)
+        dst = torch.empty_like(src)
+        ms = time_fn(lambda: dst.copy_(src))
+        rows.append({"read_mb": mb, "us": round(ms * 1e3, 2), "read_gbs": round(n / ms / 1e6, 1),
+                     "rw_frac_of_measured": round(2 * n / ms / 1e6 / hbm, 3)})
+        del src, dst
+    return {"op": "copy_curve", "graph": GRAPH, "rows": rows}
+
+
 OPS = {"sparse_mla": bench_sparse_mla, "fp8_gemm": bench_fp8_gemm, "indexer": bench_indexer,
        "indexer_select": bench_indexer_select, "topk": bench_topk, "decode_gemms": bench_decode_gemms,
-       "ag_gemm": bench_ag_gemm, "rs_gemm": bench_rs_gemm}
+       "ag_gemm": bench_ag_gemm, "rs_gemm": bench_rs_gemm, "copy_curve": bench_copy_curve}
 
 
 def main():

@@ -62,6 +62,12 @@ class AttentionRunner:
         # CUDA, methods other than echo (whose predictor reads the full logits):
         # indexer + top-k as one fused selection (ops.indexer_select).
         self.fused_select = True
+        # Chunks of at most this many query rows prefetch the output-side
+        # weights into L2 during selection + MLA.  Off (0): measured on B200,
+        # 1-token extend at 64K, 1.034-1.042 ms with it and 1.039 ms without.
+        self.prefetch_rows = 0
+        self._side = None
+        self._prefetch_done = None
         self.last_indices = None
         self.head_scale = cfg.index_n_heads ** -0.5 * cfg.index_head_dim ** -0.5
         (self.qa0, self.qa_n), (self.kv0, self.kv_n), (self.ik0, self.ik_n) = weights.spans_a
@@ -148,6 +154,22 @@ class AttentionRunner:
                                                       comm=comm, rows=(r0, r1))
             if T_loc == 0:
                 return torch.empty((0, cfg.dim), dtype=torch.bfloat16, device=normed.device)
+            self._prefetch_done = None
+            if normed.is_cuda and T_loc <= self.prefetch_rows:
+                # Decode sizes: selection and sparse MLA below are latency-bound and
+                # leave HBM idle, so the output projection's weights (and the value
+                # expansion's) are pulled into L2 meanwhile, on a side stream that
+                # the output joins (the prefetch kernel ends only when its bulk
+                # prefetches have, so in stream order it would hold up the selection).
+                cur = torch.cuda.current_stream(normed.device)
+                if self._side is None:
+                    self._side = torch.cuda.Stream(device=normed.device)
+                self._side.wait_stream(cur)
+                with torch.cuda.stream(self._side):
+                    ops.l2_prefetch(self.w.wv_b)
+                    ops.l2_prefetch(self.w.wo.weight)
+                self._prefetch_done = torch.cuda.Event()
+                self._prefetch_done.record(self._side)
             qpos = pos + r0
             keys, kscales = state.index.visible(end)
             if comm is not None and comm.world > 1 and getattr(comm.ctx, "cp_indexer", False) and \
@@ -242,6 +264,9 @@ class AttentionRunner:
         return ids[r0:r1].contiguous()
 
     def _output(self, attn, T_loc, scope):
+        if self._prefetch_done is not None:
+            torch.cuda.current_stream(attn.device).wait_event(self._prefetch_done)
+            self._prefetch_done = None
         with scope("attention_output"):
             with scope("expand"):
                 v = ops.mla_expand(attn, self.w.wv_b)

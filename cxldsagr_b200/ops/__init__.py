@@ -424,6 +424,12 @@ def gather_host_records(host, records, host_ids, slots, *, device_count=None, fp
     return records
 
 
+def l2_prefetch(t, nbytes: int | None = None):
+    """Start pulling ``t`` (contiguous, not written while in flight) into L2; no-op off CUDA."""
+    if _cuda(t):
+        lib().l2_prefetch(t, -1 if nbytes is None else int(nbytes))
+
+
 def embed(ids, table, *, row0: int = 0, vocab_total: int | None = None):
     """Embedding rows of ``ids``.  ``table`` may be a vocabulary shard holding
     rows [row0, row0 + len(table)) of a ``vocab_total``-row table; ids outside

@@ -43,10 +43,11 @@ def test_rms_norm(rows, D):
     assert rel_err(n.cpu(), wn) < 1e-2
 
 
-def test_norm_quant_matches_quantize():
+@pytest.mark.parametrize("rows,D", [(64, 7168), (1, 7168), (3, 1536), (5, 512)])
+def test_norm_quant_matches_quantize(rows, D):
     torch.manual_seed(1)
-    x = torch.randn(64, 7168, device=DEV).bfloat16()
-    w = torch.rand(7168, device=DEV) + 0.5
+    x = torch.randn(rows, D, device=DEV).bfloat16()
+    w = torch.rand(D, device=DEV) + 0.5
     n, _, q, s_t = ops.norm_quant(x, None, w, 1e-6)
     q2, s2 = ops.quantize_act(n)
     assert torch.equal(q.view(torch.uint8), q2.view(torch.uint8))
@@ -777,6 +778,42 @@ def test_decode_gemv_fp8(M, N, K):
     want = a @ ref.dequantize_weight(w.cpu(), s.cpu()).T + res.float().cpu()
     assert rel_err(got.float().cpu(), want) < 1e-2
     assert rel_err(got.float().cpu(), tiles.float().cpu()) < 1e-2
+
+
+def test_l2_prefetch_leaves_data():
+    """The bulk L2 prefetch runs on ragged sizes and changes nothing it touches."""
+    x = torch.randint(0, 255, (3 * (1 << 16) + 48,), dtype=torch.uint8, device=DEV)
+    before = x.clone()
+    ops.l2_prefetch(x)
+    ops.l2_prefetch(x, 1000)
+    torch.cuda.synchronize()
+    ops.check_errors(torch.device(DEV))
+    assert torch.equal(x, before)
+
+
+def test_pdl_switch_same_bits():
+    """Programmatic dependent launch changes launch overlap only: a decode-size
+    norm -> GEMV -> norm chain gives the same bits with it on and off."""
+    torch.manual_seed(45)
+    D, N = 7168, 2304
+    x = torch.randn(1, D, device=DEV).bfloat16()
+    res = torch.randn(1, D, device=DEV).bfloat16()
+    nw = torch.rand(D, device=DEV) + 0.5
+    w, s = quantize_weight_blocks(torch.randn(N, D, device=DEV) * 0.02)
+
+    def chain():
+        normed, summed, q, s_t = ops.norm_quant(x, res, nw, 1e-6)
+        y = ops.fp8_gemm(q, s_t, w, s)
+        return normed, summed, q.view(torch.uint8), s_t, y
+
+    on = chain()
+    ops.lib().set_pdl(False)
+    try:
+        off = chain()
+    finally:
+        ops.lib().set_pdl(True)
+    for a, b in zip(on, off):
+        assert torch.equal(a, b)
 
 
 @pytest.mark.parametrize("M", [1, 2, 8])
