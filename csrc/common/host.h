@@ -22,7 +22,10 @@ inline void cuda_check(cudaError_t e, const char* what) {
 // and its writes are visible) in every CTA before it reads or writes anything
 // that kernel touches, and may do independent work (reading weights, barrier
 // setup) before.  Kernels call pdl_trigger() early so that their successor
-// can be scheduled onto SMs they leave free.  Off: plain stream order.
+// can be scheduled onto SMs they leave free.  Rule for tensor memory: a
+// kernel that allocates TMEM triggers only after its allocation, so a
+// successor that allocates before its own wait can never hold TMEM that an
+// unfinished predecessor still needs.  Off: plain stream order.
 inline bool& pdl_flag() {
   static bool on = true;
   return on;

@@ -69,6 +69,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
   volatile int* abort_flag = &s.abort_flag;
+  pdl_trigger();  // programmatic dependent launch: set-up above overlapped the previous kernel
+  pdl_wait();
 
   if (warp == 0) {
     if (elect_one()) {
@@ -234,8 +236,8 @@ void launch_bf16_gemm(const BF16GemmArgs& a, cudaStream_t stream) {
   auto kern = bf16_gemm_kernel<BN, STAGES>;
   cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
              "bf16 gemm smem attribute");
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, a.out, a.out_fp32 ? 1 : 0, a.ldo, a.o_batch, a.M,
-                                         a.N, a.K, a.batch, a_inner ? 1 : 0, b_inner ? 1 : 0, a.err);
+  launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, "bf16 gemm launch", ta, tb, a.out, a.out_fp32 ? 1 : 0,
+             a.ldo, a.o_batch, a.M, a.N, a.K, a.batch, a_inner ? 1 : 0, b_inner ? 1 : 0, a.err);
   cuda_check(cudaGetLastError(), "bf16 gemm launch");
 }
 

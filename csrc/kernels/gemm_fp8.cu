@@ -10,6 +10,8 @@ using namespace gemm_fp8;
 __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N,
                                      __nv_bfloat16* __restrict__ out, int ldo,
                                      const __nv_bfloat16* __restrict__ residual, int ldr) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
   if (i >= int64_t(M) * N) return;
   const int m = int(i / N), n = int(i % N);
@@ -29,13 +31,12 @@ void launch_fp8_gemm_t(const FP8GemmArgs& a, int splits, cudaStream_t stream) {
   auto kern = fp8_gemm_kernel<BN, STAGES, kModePlain, BS>;
   cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
              "fp8 gemm smem attribute");
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, a.sfa, a.lda_s, a.sfb, a.out, a.ldo, a.residual,
-                                         a.ldr, a.M, a.N, a.K, splits, a.partial, a.err, P2PArgs{},
-                                         GroupArgs{});
+  launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, "fp8 gemm launch", ta, tb, a.sfa, a.lda_s, a.sfb,
+             a.out, a.ldo, a.residual, a.ldr, a.M, a.N, a.K, splits, a.partial, a.err, P2PArgs{}, GroupArgs{});
   cuda_check(cudaGetLastError(), "fp8 gemm launch");
   if (splits > 1) {
     const int64_t n = int64_t(a.M) * a.N;
-    splitk_reduce_kernel<<<int((n + 255) / 256), 256, 0, stream>>>(a.partial, splits, a.M, a.N, a.out, a.ldo,
+    launch_pdl(splitk_reduce_kernel, dim3(int((n + 255) / 256)), dim3(256), 0, stream, "splitk_reduce_kernel", a.partial, splits, a.M, a.N, a.out, a.ldo,
                                                                    a.residual, a.ldr);
     cuda_check(cudaGetLastError(), "fp8 gemm split-k reduce launch");
   }
@@ -69,7 +70,7 @@ void launch_fp8_gemm_pair_t(const FP8GemmArgs& a, int splits, cudaStream_t strea
              "fp8 pair gemm launch");
   if (splits > 1) {
     const int64_t n = int64_t(a.M) * a.N;
-    splitk_reduce_kernel<<<int((n + 255) / 256), 256, 0, stream>>>(a.partial, splits, a.M, a.N, a.out, a.ldo,
+    launch_pdl(splitk_reduce_kernel, dim3(int((n + 255) / 256)), dim3(256), 0, stream, "splitk_reduce_kernel", a.partial, splits, a.M, a.N, a.out, a.ldo,
                                                                    a.residual, a.ldr);
     cuda_check(cudaGetLastError(), "fp8 gemm split-k reduce launch");
   }

@@ -252,6 +252,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
   volatile int* abort_flag = &s.abort_flag;
+  // Programmatic dependent launch (plain mode): the set-up above overlapped
+  // the previous kernel; nothing below runs before it has completed.
+  pdl_trigger();
+  pdl_wait();
 
   if (warp == 0 && BS) {
     // Whole warp: lane 0 issues the TMA loads, every lane writes 16 bytes of

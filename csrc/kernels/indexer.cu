@@ -96,7 +96,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     indexer_kernel(const __grid_constant__ CUtensorMap tma_q,
                    const __grid_constant__ CUtensorMap tma_k, const float* __restrict__ w,
                    const float* __restrict__ kscale, IndexerOut o, Schedule sch, int* err) {
-  pdl_trigger();
+  // Programmatic dependent launch: wait for the previous kernel first; let the
+  // next one start only after this CTA holds its TMEM (below).
   pdl_wait();
   if (sch.any_flag != nullptr && __ldcg(sch.any_flag) == 0) return;  // uniform: nothing to redo
   extern __shared__ uint8_t smem_raw[];
@@ -125,6 +126,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_trigger();
   const uint32_t tmem = s.tmem_base;
   volatile int* abort_flag = &s.abort_flag;
   const int units = sch.units();

@@ -203,7 +203,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                            float* __restrict__ part_lse, float* __restrict__ lse_out, int* err,
                            float* __restrict__ dbg_s, int dbg) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  pdl_trigger();
+  // Programmatic dependent launch: wait for the previous kernel first; let the
+  // next one start only after this CTA holds its TMEM (below), so a successor
+  // that allocates TMEM before its own wait can never take it from this one.
   pdl_wait();
   uint8_t* base = smem_raw;
   const uint32_t sbase = smem_u32(base);
@@ -276,6 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   cluster_sync_all();  // both CTAs' barriers initialised before any remote arrive
+  pdl_trigger();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
   volatile int* abort_flag = &s.abort_flag;
