@@ -115,8 +115,8 @@ def offload_extends(model, hist, ext, H: int, A: int, reps: int = 3) -> dict:
 
     For each method the model switches to that cache (empty pools), prefills
     the history once, then repeats: drop the HBM copies of the history (DRAM
-    copies and indexer keys stay), time one extend (CUDA graph replay, eager
-    for dense_prefetch) with CUDA events, roll the candidates back.  Recalled
+    copies and indexer keys stay), time one extend (CUDA graph replay) with
+    CUDA events, roll the candidates back.  Recalled
     rows come from the pools' device counters.  ``matched`` drops only the
     reference's per-layer recall counts of this extend (its real-checkpoint
     selections are concentrated; random-init selections cover the history), so
@@ -136,7 +136,7 @@ def offload_extends(model, hist, ext, H: int, A: int, reps: int = 3) -> dict:
         p0.record(stream)
         model.prefill(hist)
         p1.record(stream)
-        graph = None if method == "dense_prefetch" else model.capture_extend(A)
+        graph = model.capture_extend(A)
         times, recalled = [], []
         for r in range(reps):
             model.clear_residency(rows_per_layer=rows, seed=r)
@@ -345,7 +345,7 @@ def main():
             model.clear_residency()
         if events:
             events[1].record(stream)
-        if not args.no_graph and args.method != "dense_prefetch" and not sp:
+        if not args.no_graph and not sp:
             if graph is None:
                 graph = model.capture_extend(A)
             graph.replay(ext)
@@ -521,7 +521,7 @@ def main():
                 "extend_residency": "cold (HBM copies of the history dropped before the extend)" if offload else "resident",
                 "parallelism": parallelism,
                 "l2": "no flush: per-step weight stream (3.7 GB) exceeds L2",
-                "extend_graph": not args.no_graph and args.method != "dense_prefetch" and not sp,
+                "extend_graph": not args.no_graph and not sp,
             },
             "prefill_ms": round(prefill_ms, 3),
             "extend_ms": round(extend_ms, 4),

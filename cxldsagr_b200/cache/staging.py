@@ -43,9 +43,7 @@ class StagingLease:
         if st.stream is None:
             target[:rows].copy_(host[:rows])
             return self
-        # The buffer may still be read by the layer that used it two steps ago.
-        if st.consumed[self.index] is not None:
-            st.stream.wait_event(st.consumed[self.index])
+        st.order_after_use(self.index)
         with torch.cuda.stream(st.stream):
             target[:rows].copy_(host[:rows], non_blocking=True)
             self.event = torch.cuda.Event()
@@ -67,8 +65,7 @@ class StagingLease:
             for lo, n, h in runs:
                 buf[lo:lo + n].copy_(host[h:h + n])
             return self
-        if st.consumed[self.index] is not None:
-            st.stream.wait_event(st.consumed[self.index])
+        st.order_after_use(self.index)
         with torch.cuda.stream(st.stream):
             if before is not None:
                 before()
@@ -111,6 +108,25 @@ class DoubleBufferStaging:
         self.stream = torch.cuda.Stream(device=self.device) if self.device.type == "cuda" else None
         self.consumed = [None, None]
         self._next = 0
+
+    def order_after_use(self, index: int):
+        """Order the staging stream after the last reader of buffer ``index``.
+
+        Eagerly: its consumed event (the layer that used it two steps ago),
+        or, with none recorded (first use, or after a capture, whose graph may
+        still be reading it), everything enqueued on the compute stream.
+        Inside a CUDA-graph capture: the compute stream's work so far, which
+        also brings the staging stream into the capture (events recorded
+        before the capture cannot be waited on inside it)."""
+        cur = torch.cuda.current_stream(self.device)
+        if torch.cuda.is_current_stream_capturing() or self.consumed[index] is None:
+            self.stream.wait_stream(cur)
+        else:
+            self.stream.wait_event(self.consumed[index])
+
+    def end_capture(self):
+        """Forget the consumed events recorded inside a capture (they never ran eagerly)."""
+        self.consumed = [None, None]
 
     def lease(self) -> StagingLease:
         lease = StagingLease(self, self._next)

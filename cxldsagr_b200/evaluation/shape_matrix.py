@@ -7,7 +7,7 @@ For each H the model (DeepSeek-V3.2 layers 0-2 + embedding, final norm and
 last-token LM head, random-init weights of the real shapes, uniform-random
 token ids) is built once; for each method it switches to that cache (P = NH =
 H + max A), prefills the H-token history once (timed), then for each A
-captures the A-token extend in a CUDA graph (eager for dense_prefetch) and
+captures the A-token extend in a CUDA graph (every method) and
 times cold replays: before each replay the HBM copies of the history are
 dropped (DRAM copies and indexer keys stay), as in the reference's cold
 measurement.  Times are CUDA events on the launching stream, minimum over
@@ -117,7 +117,7 @@ def run_history(H: int, extends: list[int], methods, *, layers: int, kv_format: 
         torch.cuda.synchronize(dev)
         prefill_ms = e0.elapsed_time(e1)
         for A in extends:
-            graph = None if method == "dense_prefetch" else model.capture_extend(A)
+            graph = model.capture_extend(A)
             times = []
             for _ in range(reps):
                 model.clear_residency()

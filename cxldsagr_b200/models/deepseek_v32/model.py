@@ -748,13 +748,13 @@ class ExtendGraph:
     methods (serial_sparse, echo) are captured too: their pool metadata,
     predictor, recall and host write-back run on the device with no host
     decision inside the step, so every replay acts on the pool state of its
-    own time.  (dense_prefetch stages through a second stream with host-side
-    lease state and is not captured.)
+    own time.  dense_prefetch is captured with its staging stream: the
+    whole-layer history copies from pinned host pages (one per contiguous
+    run, fixed at the captured history length) become copy nodes of the graph
+    ordered after the compute that last read their buffer.
     """
 
     def __init__(self, model: DeepSeekV32Model, T: int, *, warmup: int = 2, session: ModelSession | None = None):
-        if model.cache_cfg.method == "dense_prefetch":
-            raise ValueError("the dense_prefetch method runs its extend eagerly")
         if len(model.pool_devices) > 1:
             raise ValueError("a model placed over several devices runs its extend eagerly")
         comm = getattr(model, "comm", None)
@@ -789,6 +789,8 @@ class ExtendGraph:
                 pool.join_writes()
         if pool is not None:
             pool.end_capture()
+        if getattr(model, "dense_staging", None) is not None:
+            model.dense_staging.end_capture()
         self.launches_per_replay = launch_count() - n0
         model._graph_launches = self.launches_per_replay
         self._rewind()

@@ -737,6 +737,37 @@ def test_model_fp8_records_offload_matches_resident(method):
     assert torch.equal(out["hbm"][0], out[method][0]) and torch.equal(out["hbm"][1], out[method][1])
 
 
+@pytest.mark.parametrize("method,kv_format", [("hbm", "bf16"), ("serial_sparse", "fp8"), ("dense_prefetch", "bf16"),
+                                              ("dense_prefetch", "fp8")])
+def test_extend_graph_matches_eager(method, kv_format):
+    """A captured extend (dense_prefetch included: its staging copies become
+    graph nodes) gives the eager extend's logits bit for bit, on two replays."""
+    from cxldsagr_b200.checkpoint import StateDictSource, random_state_dict
+    from cxldsagr_b200.config import CacheConfig
+    from cxldsagr_b200.models.deepseek_v32.model import DeepSeekV32Model
+
+    cfg = v32_config(1)
+    src = StateDictSource(random_state_dict(cfg, layers=[0], seed=3, device=DEV))
+    g = torch.Generator().manual_seed(6)
+    H, A = 3000, 16
+    hist = torch.randint(0, cfg.vocab_size, (H,), generator=g).to(DEV)
+    ext = torch.randint(0, cfg.vocab_size, (A,), generator=g).to(DEV)
+    kw = {} if method == "hbm" else {"pool_tokens": H + A, "host_tokens": H + A}
+    cache = CacheConfig(method=method, capacity=H + A, chunk_size=1024, candidate_tokens=A, kv_format=kv_format, **kw)
+    m = DeepSeekV32Model(cfg, src, device=DEV, cache=cache)
+    m.prefill(hist)
+    eager = m.extend(ext).logits.clone()
+    m.session.truncate(H)
+    graph = m.capture_extend(A)
+    for _ in range(2):
+        got = graph.replay(ext).clone()
+        graph.rollback()
+        torch.cuda.synchronize()
+        assert torch.equal(got, eager)
+    del graph
+    ops.check_errors(DEV)
+
+
 @pytest.mark.parametrize("method,kv_format", [("hbm", "bf16"), ("serial_sparse", "fp8")])
 def test_cache_memory_audit_model(method, kv_format, capsys):
     """Per-scope transient memory of a real prefill + extend stays inside the
