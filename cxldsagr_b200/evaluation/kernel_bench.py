@@ -133,19 +133,64 @@ def bench_sparse_mla(T=256, K=2048, P=65664, splits=1, impl=0, locality=0.0, tra
             **({"timeline_cycles": timeline} if timeline else {})}
 
 
-def bench_fp8_gemm(M=1024, N=36864, K=7168, ue8m0=False, **_):
+def bench_fp8_gemm(M=1024, N=36864, K=7168, ue8m0=False, pair=False, **_):
     """Power-of-two block scales (the checkpoint convention); ``ue8m0`` picks the
-    block-scaled tensor-core path, otherwise the per-K-block FP32 promotion."""
+    block-scaled tensor-core path, otherwise the per-K-block FP32 promotion;
+    ``pair`` the 2-CTA 256-row tiles."""
     dev = "cuda"
     x = torch.randn(M, K, device=dev).bfloat16()
     w, s = quantize_weight_blocks(torch.randn(N, K, device=dev) * 0.02)
     q, s_t = ops.quantize_act(x)
     out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
-    ms = time_fn(lambda: ops.fp8_gemm(q, s_t, w, s, out=out, ue8m0=ue8m0))
+    ops.lib().set_fp8_gemm_pair_tiles(pair)
+    try:
+        ms = time_fn(lambda: ops.fp8_gemm(q, s_t, w, s, out=out, ue8m0=ue8m0))
+    finally:
+        ops.lib().set_fp8_gemm_pair_tiles(False)
     flops = 2.0 * M * N * K
-    return {"op": "fp8_gemm", "M": M, "N": N, "K": K, "ue8m0": ue8m0, "ms": ms, "tflops": flops / ms / 1e9,
+    return {"op": "fp8_gemm", "M": M, "N": N, "K": K, "ue8m0": ue8m0, "pair": pair, "ms": ms,
+            "tflops": flops / ms / 1e9,
             "bytes_gbs": (N * K + M * K + M * N * 2) / ms / 1e6,
             **roofline(ms, flops=flops, nbytes=N * K + M * K + M * N * 2, fp8=True)}
+
+
+def bench_gemm_paths(M=2048, **_):
+    """Prefill-chunk FP8 linears of one V3.2 layer on each tile path: 128-row
+    tiles with FP32 promotion (default), 128-row block-scaled (UE8M0) tiles,
+    and 2-CTA 256-row tiles (promotion).  TFLOP/s per path."""
+    from ..config import v32_config
+
+    cfg = v32_config(1)
+    dev = "cuda"
+    shapes = {
+        "fused_a": (cfg.q_lora_rank + 640 + cfg.index_head_dim, cfg.dim),
+        "fused_b": (cfg.n_heads * (cfg.qk_nope_head_dim + cfg.qk_rope_head_dim)
+                    + cfg.index_n_heads * cfg.index_head_dim, cfg.q_lora_rank),
+        "o_proj": (cfg.dim, cfg.n_heads * cfg.v_head_dim),
+        "gate_up": (2 * cfg.intermediate_size, cfg.dim),
+        "down": (cfg.dim, cfg.intermediate_size),
+    }
+    rows = []
+    for name, (N, K) in shapes.items():
+        x = torch.randn(M, K, device=dev).bfloat16()
+        w, s = quantize_weight_blocks(torch.randn(N, K, device=dev) * 0.02)
+        q, s_t = ops.quantize_act(x)
+        out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        ref_out = ops.fp8_gemm(q, s_t, w, s)
+        row = {"gemm": name, "M": M, "N": N, "K": K}
+        for label, bs, pair in (("promote", False, False), ("block_scaled", True, False), ("pair", False, True)):
+            ops.lib().set_fp8_gemm_pair_tiles(pair)
+            try:
+                ms = time_fn(lambda: ops.fp8_gemm(q, s_t, w, s, out=out, ue8m0=bs))
+                ops.fp8_gemm(q, s_t, w, s, out=out, ue8m0=bs)
+                diff = (out.float() - ref_out.float()).abs().max().item()
+            finally:
+                ops.lib().set_fp8_gemm_pair_tiles(False)
+            row[f"{label}_us"] = round(ms * 1e3, 1)
+            row[f"{label}_tflops"] = round(2.0 * M * N * K / ms / 1e9, 1)
+            row[f"{label}_maxdiff"] = diff
+        rows.append(row)
+    return {"op": "gemm_paths", "rows": rows}
 
 
 def bench_decode_gemms(M=1, **_):
@@ -316,7 +361,8 @@ def bench_copy_curve(**_):
 
 OPS = {"sparse_mla": bench_sparse_mla, "fp8_gemm": bench_fp8_gemm, "indexer": bench_indexer,
        "indexer_select": bench_indexer_select, "topk": bench_topk, "decode_gemms": bench_decode_gemms,
-       "ag_gemm": bench_ag_gemm, "rs_gemm": bench_rs_gemm, "copy_curve": bench_copy_curve}
+       "ag_gemm": bench_ag_gemm, "rs_gemm": bench_rs_gemm, "copy_curve": bench_copy_curve,
+       "gemm_paths": bench_gemm_paths}
 
 
 def main():
@@ -336,6 +382,7 @@ def main():
     p.add_argument("--N", type=int, default=36864)
     p.add_argument("--Kdim", type=int, default=7168)
     p.add_argument("--block-scaled", action="store_true", help="fp8_gemm: block-scaled (UE8M0) tensor-core path")
+    p.add_argument("--pair", action="store_true", help="fp8_gemm: 2-CTA 256-row tiles")
     p.add_argument("--trace", action="store_true", help="sparse_mla: phase clocks of the first cluster")
     p.add_argument("--graph", action="store_true", help="time CUDA-graph replays (small, launch-bound ops)")
     a = p.parse_args()
@@ -345,12 +392,12 @@ def main():
     for name in names:
         kw = dict(T=a.T, K=a.K, P=a.P, splits=a.splits, impl=a.impl, locality=a.locality, trace=a.trace)
         if name == "fp8_gemm":
-            kw = dict(M=a.M, N=a.N, K=a.Kdim, ue8m0=a.block_scaled)
+            kw = dict(M=a.M, N=a.N, K=a.Kdim, ue8m0=a.block_scaled, pair=a.pair)
         if name in ("ag_gemm", "rs_gemm"):
             kw = dict(M=a.M, N=a.N, Kdim=a.Kdim)
         if name in ("indexer", "indexer_select"):
             kw = dict(Q=a.R)
-        if name == "decode_gemms":
+        if name in ("decode_gemms", "gemm_paths"):
             kw = dict(M=a.M)
         if name == "topk":
             kw = dict(R=a.R, clustered=a.clustered, order=a.order, causal=a.causal)
