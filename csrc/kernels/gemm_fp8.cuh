@@ -686,12 +686,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld16(tmem + lane_addr + buf * BN + chalf * CPW + c * 16, r);
             tmem_wait_ld();
             const float scale = sa * ((n0 + c * 16) / 128 == nb0 ? sb0 : sb1);
-            // Packed FP32x2 FMAs (each lane an ordinary fmaf): half the
-            // promotion's FMA instructions, same bits.
 #pragma unroll
-            for (int j = 0; j < 16; j += 2)
-              fma_f32x2(acc[c * 16 + j], acc[c * 16 + j + 1], __uint_as_float(r[j]), __uint_as_float(r[j + 1]), scale,
-                        scale);
+            for (int j = 0; j < 16; ++j) acc[c * 16 + j] = fmaf(__uint_as_float(r[j]), scale, acc[c * 16 + j]);
           }
           tc_fence_before();
           __syncwarp();

@@ -91,7 +91,7 @@ struct IndexerOut {
   int cand_cap;
 };
 
-template <bool SELECT>
+template <bool SELECT, bool SINGLE>
 __global__ void __launch_bounds__(kThreads, 1)
     indexer_kernel(const __grid_constant__ CUtensorMap tma_q,
                    const __grid_constant__ CUtensorMap tma_k, const float* __restrict__ w,
@@ -161,7 +161,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      const uint32_t idesc = umma_idesc(BKV, NQ, 0, 0);
+      // Single-query launches: one MMA of N = 64 (the query's heads) per key
+      // tile, four tiles side by side in one accumulator, so the 16 epilogue
+      // warps score four tiles at once instead of one query's 4 warps
+      // scoring one tile while 12 idle.
+      constexpr bool single = SINGLE;
+      const uint32_t idesc = single ? umma_idesc(BKV, kHeads, 0, 0) : umma_idesc(BKV, NQ, 0, 0);
       int stage = 0;
       uint32_t phase = 0;
       uint32_t ucount = 0, tcount = 0;
@@ -174,23 +179,53 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&s.q_full[qbuf], qpar, err, kErrTimeoutTmaFull, abort_flag)) break;
         tc_fence_after();
         const uint64_t bdesc = umma_desc_sw128(smem_u32(s.q[qbuf]));
-        for (int t = t0; t < t1; ++t, ++tcount) {
-          const uint32_t buf = tcount & 1, bpar = (tcount >> 1) & 1;
-          if (!mbar_wait(&s.tmem_empty[buf], bpar ^ 1, err, kErrTimeoutTmemEmpty, abort_flag) ||
-              !mbar_wait(&s.k_full[stage], phase, err, kErrTimeoutTmaFull, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t adesc = umma_desc_sw128(smem_u32(s.k[stage]));
+        if constexpr (!SINGLE) {
+          for (int t = t0; t < t1; ++t, ++tcount) {
+            const uint32_t buf = tcount & 1, bpar = (tcount >> 1) & 1;
+            if (!mbar_wait(&s.tmem_empty[buf], bpar ^ 1, err, kErrTimeoutTmemEmpty, abort_flag) ||
+                !mbar_wait(&s.k_full[stage], phase, err, kErrTimeoutTmaFull, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t adesc = umma_desc_sw128(smem_u32(s.k[stage]));
 #pragma unroll
-          for (int k = 0; k < kDim / 32; ++k)
-            mma_f8_ss(tmem + buf * NQ, adesc + (k * 32 >> 4), bdesc + (k * 32 >> 4), idesc, k > 0);
-          mma_commit(&s.k_empty[stage]);
-          mma_commit(&s.tmem_full[buf]);
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1;
+            for (int k = 0; k < kDim / 32; ++k)
+              mma_f8_ss(tmem + buf * NQ, adesc + (k * 32 >> 4), bdesc + (k * 32 >> 4), idesc, k > 0);
+            mma_commit(&s.k_empty[stage]);
+            mma_commit(&s.tmem_full[buf]);
+            if (++stage == kStages) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+        } else {
+          for (int t = t0; t < t1 && ok; ++tcount) {
+            const int ng = single ? min(QB, t1 - t) : 1;  // key tiles in this accumulator
+            const uint32_t buf = tcount & 1, bpar = (tcount >> 1) & 1;
+            if (!mbar_wait(&s.tmem_empty[buf], bpar ^ 1, err, kErrTimeoutTmemEmpty, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            for (int g = 0; g < ng; ++g, ++t) {
+              if (!mbar_wait(&s.k_full[stage], phase, err, kErrTimeoutTmaFull, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint64_t adesc = umma_desc_sw128(smem_u32(s.k[stage]));
+#pragma unroll
+              for (int k = 0; k < kDim / 32; ++k)
+                mma_f8_ss(tmem + buf * NQ + g * kHeads, adesc + (k * 32 >> 4), bdesc + (k * 32 >> 4), idesc, k > 0);
+              mma_commit(&s.k_empty[stage]);
+              if (++stage == kStages) {
+                stage = 0;
+                phase ^= 1;
+              }
+            }
+            if (!ok) break;
+            mma_commit(&s.tmem_full[buf]);
           }
         }
         if (ok) mma_commit(&s.q_empty[qbuf]);
@@ -227,7 +262,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // unit (up to 16 tiles): reading them from shared memory on every tile
       // cost 256 B per thread per tile, which bounded the epilogue at the
       // shared-memory read bandwidth.
-      const int qidx = qb * QB + qgrp;
+      constexpr bool single = SINGLE;
+      const int qidx = single ? qb * QB : qb * QB + qgrp;
       float wr[kHeads];
       {
         const float4* wq = reinterpret_cast<const float4*>(w + int64_t(min(qidx, sch.Q - 1)) * kHeads);
@@ -242,16 +278,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float thresh = (SELECT && o.thresh != nullptr) ? __ldg(o.thresh + min(qidx, sch.Q - 1)) : -INFINITY;
       const int last_key = sch.query_start + qidx;  // causal: cache key index <= last_key is visible
-      for (int t = t0; t < t1; ++t, ++tcount) {
+      // Single-query launches: this warp scores key tile t + qgrp of the
+      // accumulator's (up to) four; otherwise tile t for query qgrp.
+      for (int t = t0; t < t1; t += (single ? min(QB, t1 - t) : 1), ++tcount) {
+        const int tt = single ? t + qgrp : t;
+        const bool have = !single || qgrp < t1 - t;  // warp-uniform
         const uint32_t buf = tcount & 1, bpar = (tcount >> 1) & 1;
-        const int key = t * BKV + key_in_tile;
+        const int key = tt * BKV + key_in_tile;
         const int cache_key = key * sch.stride;
-        const float ks = key < sch.N ? __ldg(kscale + cache_key) : 0.f;
+        const float ks = have && key < sch.N ? __ldg(kscale + cache_key) : 0.f;
         if (!mbar_wait(&s.tmem_full[buf], bpar, err, kErrTimeoutTmemFull, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        if (single && !have) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.tmem_empty[buf]);
+          continue;
+        }
         // Two packed FP32x2 accumulators (heads h = 4i, 4i+1 and 4i+2, 4i+3).
         // The ReLU (max on the ALU pipe, 64 per key and query) bounds the
         // epilogue; moving half of it to the FMA pipe (x + |x|, or a
@@ -334,6 +380,12 @@ void launch_indexer_logits(const IndexerArgs& a, cudaStream_t stream) {
   const int sms = sm_count();
   int64_t work = int64_t(sch.num_qb) * sch.num_tiles_total;
   int chunk = int(std::max<int64_t>(1, std::min<int64_t>(16, work / (2 * sms))));
+  const bool single = a.Q == 1;  // kernel variant: the 4 column groups of an accumulator hold 4 key tiles
+  if (single) {
+    // Whole accumulators of four key tiles, about one unit per SM.
+    const int per = (sch.num_tiles_total + sms - 1) / sms;
+    chunk = std::max(QB, (per + QB - 1) / QB * QB);
+  }
   sch.chunk_tiles = chunk;
   sch.num_chunks = (sch.num_tiles_total + chunk - 1) / chunk;
   const int units = sch.num_qb * sch.num_chunks;
@@ -347,7 +399,8 @@ void launch_indexer_logits(const IndexerArgs& a, cudaStream_t stream) {
   o.cand_count = a.cand_count;
   o.cand_cap = a.cand_cap;
   const size_t smem = sizeof(Smem) + 1024;
-  auto kern = a.select ? indexer_kernel<true> : indexer_kernel<false>;
+  auto kern = a.select ? (single ? indexer_kernel<true, true> : indexer_kernel<true, false>)
+                        : (single ? indexer_kernel<false, true> : indexer_kernel<false, false>);
   cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
              "indexer smem attribute");
   launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, "indexer launch", tq, tk, a.w, a.kscale, o, sch, a.err);

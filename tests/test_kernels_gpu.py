@@ -151,7 +151,8 @@ def test_bf16_bmm(G, M, N, K):
 
 
 # ------------------------------------------------------------- indexer
-@pytest.mark.parametrize("Q,N,start", [(1, 700, 699), (7, 300, 200), (64, 4096, 4032), (130, 2000, 0)])
+@pytest.mark.parametrize("Q,N,start", [(1, 700, 699), (1, 130, 129), (1, 65537, 65536), (7, 300, 200),
+                                       (64, 4096, 4032), (130, 2000, 0)])
 def test_indexer_logits(Q, N, start):
     torch.manual_seed(7)
     N = max(N, start + Q)
@@ -164,6 +165,11 @@ def test_indexer_logits(Q, N, start):
     fin = torch.isfinite(want)
     assert torch.equal(torch.isfinite(got.cpu()), fin)
     assert rel_err(got.cpu()[fin], want[fin]) < 1e-4
+    if Q == 1 and start > 0:
+        # The single-query layout (four key tiles per accumulator) gives the
+        # same bits as the query's row of a multi-query launch.
+        pair = ops.indexer_logits(torch.cat([q, q]), k, torch.cat([w, w]), ks, start - 1)
+        assert torch.equal(pair[1, :start + 1], got[0, :start + 1])
 
 
 # ------------------------------------------------- fused indexer selection
@@ -187,13 +193,16 @@ def test_indexer_select_matches_logits_topk(Q, N, start, order):
     assert torch.equal(v, rv)
 
 
+@pytest.mark.parametrize("Q", [48, 1])
 @pytest.mark.parametrize("kind", ["equal_keys", "banded"])
-def test_indexer_select_fallback_rows(kind):
+def test_indexer_select_fallback_rows(kind, Q):
     """Rows the candidate lists cannot decide (one value shared by every key:
     the threshold keeps them all and overflows the list) are redone from full
-    logits; the result still equals the plain path."""
+    logits; the result still equals the plain path (one query: the
+    single-query indexer layout in every pass)."""
     torch.manual_seed(32)
-    Q, N, start = 48, 30000, 29952
+    N = 30000
+    start = N - Q
     q = (torch.randn(Q, 64, 128, device=DEV) * 2).to(torch.float8_e4m3fn)
     if kind == "equal_keys":
         k = (torch.randn(1, 128, device=DEV) * 2).expand(N, 128).contiguous().to(torch.float8_e4m3fn)
