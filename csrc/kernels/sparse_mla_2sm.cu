@@ -18,11 +18,13 @@
 //    cross between the CTAs.
 //  * PV (two MMAs of N = 256 value dims, K = the tile's 64 keys): B is split by
 //    N again, so CTA c supplies value dims [256v+128c, 256v+128c+128) (v = 0,
-//    1) of all 64 keys; it gathers those 256 dims of every key of the tile
-//    into a separate region (the pair's shared descriptors need identical
-//    offsets in both CTAs, so the QK copy cannot be reused).  Gather bytes per
-//    key are 1152 + 2 x 512; the gather reaches ~11 TB/s from L2 with eight
-//    cp.async warps and three or more stages in flight per SM.
+//    1) of all 64 keys.  For its own 32 keys those dims are already in the
+//    tile's record chunks 4v+2c, 4v+2c+1.  For the peer's keys it gathers
+//    them into its own record chunks 4v+2(1-c), 4v+2(1-c)+1, which held QK-only
+//    dims of its own keys and are free once the tile's QK is done; so one
+//    descriptor offset serves both CTAs and a CTA gathers 1152 + 512 bytes
+//    per key pair member instead of 1152 + 1024.  A record stage is held from
+//    its gather to the tile's PV (3 stages).
 //  * Softmax: thread t of warps 0-3 owns TMEM lane t: head 64c + (t & 63),
 //    keys [32 (t >> 6), +32) of each tile.  The two threads of a head trade
 //    their tile maxima through shared memory, keep the same lazily rescaled
@@ -32,19 +34,20 @@
 //
 // Roles per CTA (16 warps, registers rebalanced with setmaxnreg): warps 0-3
 // softmax + epilogue (232 registers); warps 4-7 gather the Q rows and the
-// tile's full records for QK into a 2-stage ring that QK releases; warps
-// 8-11 gather the value dims into a 2-stage ring that PV releases (cp.async,
+// tile's full records into a 3-stage ring that PV releases; warps 8-11
+// gather the peer keys' value dims once QK is done with the tile (cp.async,
 // 16 bytes per lane, written in the 128-byte swizzled layout; padding rows
 // zero-filled).  Debug bit 64 replaces the record gathers by TMA row gathers
 // (tile::gather4, four keys x one 64-dim chunk per instruction, issued by
-// one thread per ring): correct, but slower; warp 12 allocates the pair's TMEM and, in CTA 0, issues every
+// one thread): correct, but slower; warp 12 allocates the pair's TMEM and, in CTA 0, issues every
 // MMA from one thread (QK runs up to four tiles ahead of the softmax through
 // four S buffers); in CTA 1 it relays "rows landed" to CTA 0's barriers;
 // warps 13-15 only complete the register warpgroup.
 //
-// Measured on B200 (T = 1024 queries x top-2048, per-tile clock64 timeline):
-// 0.82 ms (710 TFLOP/s); the softmax chain (~1.8K cycles per 64-key tile on
-// one warp per SM sub-partition) sets the pace.  Splitting the softmax over
+// Measured on B200 (T = 1024 queries x top-2048): 0.738 ms (792 TFLOP/s;
+// 0.758 ms with a separate value-dim ring that gathered all 64 keys' value
+// dims).  Per 64-key tile (clock64 timeline, T = 256) the softmax spends
+// ~2.4K cycles, ~0.8K of them waiting for the next tile's S (its records).  Splitting the softmax over
 // two warpgroups halved its exponent work but left fewer gather warps (an SM
 // moves ~40 bytes per clock of cp.async gathers) and measured slower (0.92 -
 // 0.94 ms with 3 or 5 value-gather warps).
@@ -62,7 +65,7 @@ constexpr int H = 128;
 constexpr int HC = 64;                    // heads per CTA
 constexpr int BN = 64;                    // keys per tile (pair)
 constexpr int BNC = 32;                   // keys per tile per CTA (QK's B split)
-constexpr int STAGES = 2;                 // depth of each gather ring
+constexpr int STAGES = 3;                 // depth of the record ring (a stage is held from gather to PV)
 constexpr int SBUF = 4;                   // S buffers in TMEM
 constexpr int kChunks = D / 64;           // 64-dim (128-byte) chunks of a record
 constexpr int kQChunkBytes = HC * 128;    // 8 KB
@@ -87,8 +90,7 @@ constexpr uint32_t kTmemS = 256;
 // Shared-memory layout (offsets from a 1024-byte aligned base).
 constexpr int kOffQ = 0;                                             // [9][8 KB]
 constexpr int kOffOwn = kOffQ + kChunks * kQChunkBytes;              // [STAGES][9][4 KB]
-constexpr int kOffPv = kOffOwn + STAGES * kChunks * kKeyChunkBytes;  // [STAGES][key half][v][chunk][4 KB]
-constexpr int kOffP = kOffPv + STAGES * 8 * kKeyChunkBytes;          // [2][8 KB]
+constexpr int kOffP = kOffOwn + STAGES * kChunks * kKeyChunkBytes;   // [2][8 KB]
 constexpr int kOffSmall = kOffP + 2 * kPBytes;
 
 struct Small {
@@ -97,9 +99,9 @@ struct Small {
   float red[2][kSoftmaxThreads];
   uint64_t q_full;            // Q rows landed (CTA 0: + CTA 1's relay)
   uint64_t own_full[STAGES];  // QK records landed (CTA 0: + relay)
-  uint64_t own_empty[STAGES]; // QK of the stage's tile done (commit)
-  uint64_t pv_full[STAGES];   // value dims landed (CTA 0: + relay)
-  uint64_t pv_empty[STAGES];  // PV of the stage's tile done (commit)
+  uint64_t qk_done[STAGES];   // QK of the stage's tile done (commit): its peer-slot chunks may be overwritten
+  uint64_t pv_full[STAGES];   // the peer keys' value dims landed (CTA 0: + relay)
+  uint64_t own_empty[STAGES]; // PV of the stage's tile done (commit): the stage may be refilled
   uint64_t s_full[SBUF];      // QK done (commit)
   uint64_t s_empty[SBUF];     // CTA 0: both CTAs' softmax warps read S
   uint64_t p_full[2];         // CTA 0: both CTAs' softmax warps wrote P
@@ -236,10 +238,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) trace(kTraceTiles, 0);
 
   auto own_chunk = [&](int st, int j) { return sbase + kOffOwn + (st * kChunks + j) * kKeyChunkBytes; };
-  // Value-dim region: keys of key half kh (CTA kh's keys), value half v, chunk qc (of the CTA's two).
-  auto pv_chunk = [&](int st, int kh, int v, int qc) {
-    return sbase + kOffPv + (((st * 2 + kh) * 2 + v) * 2 + qc) * kKeyChunkBytes;
-  };
+  // PV's B operand (value dims, MN-major) of key half kh and value half v:
+  // record chunks 4v + 2kh and 4v + 2kh + 1 of the stage.  In CTA kh they hold
+  // its own keys' dims [256v + 128kh, +128) (its N half of PV) from the QK
+  // gather; in the other CTA they held its own keys' QK-only dims, which QK
+  // has finished with, and receive the peer keys' value dims of its N half.
+  // One descriptor offset thus serves both CTAs, and each CTA gathers value
+  // dims for the peer's 32 keys only (16 KB per tile instead of 32 KB).
+  auto pv_region = [&](int st, int kh, int v) { return own_chunk(st, 4 * v + 2 * kh); };
   const uint32_t p_buf[2] = {sbase + kOffP, sbase + kOffP + kPBytes};
   // Valid (in-range, non-padding) id of selection entry jj of this split, else -1.
   auto load_id = [&](int jj) {
@@ -255,9 +261,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t gather_arrivals = use_tma ? 1u : uint32_t(kOwnWarps);
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&s.own_full[i], gather_arrivals + relay);
+      mbar_init(&s.qk_done[i], 1);
+      mbar_init(&s.pv_full[i], uint32_t(kPvWarps) + relay);
       mbar_init(&s.own_empty[i], 1);
-      mbar_init(&s.pv_full[i], (use_tma ? 1u : uint32_t(kPvWarps)) + relay);
-      mbar_init(&s.pv_empty[i], 1);
     }
     for (int i = 0; i < SBUF; ++i) {
       mbar_init(&s.s_full[i], 1);
@@ -377,65 +383,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     regs_dec<kRegsOther>();
     const int pw = warp - kPvWarp0;
     const int pv_chunk0 = 2 * int(crank);  // first value chunk of this CTA in each half
-    if (use_tma) {
-      // One thread of warp 0 gathers this CTA's value chunks of the tile's
-      // 64 keys (two per value half) with TMA row gathers.
-      if (pw == 0) {
-        int next0 = load_id(k_begin + lane), next1 = load_id(k_begin + BNC + lane);
-        int issued = 0;
-        for (int i = 0; i < ntiles; ++i) {
-          const int st = i % STAGES;
-          const int my0 = next0 >= 0 ? next0 : P, my1 = next1 >= 0 ? next1 : P;
-          next0 = load_id(k_begin + (i + 1) * BN + lane);
-          next1 = load_id(k_begin + (i + 1) * BN + BNC + lane);
-          const bool got = lane == 0 && mbar_wait(&s.pv_empty[st], ((i / STAGES) & 1) ^ 1, err,
-                                                  kErrTimeoutSmemEmpty, abort_flag);
-          if (!__shfl_sync(0xffffffffu, got, 0)) break;
-          if (lane == 0) mbar_arrive_expect_tx(&s.pv_full[st], BN * 4 * 128);
-          __syncwarp();
-#pragma unroll 1
-          for (int kh = 0; kh < 2; ++kh) {
-            const int my = kh == 0 ? my0 : my1;
-#pragma unroll 1
-            for (int g = 0; g < BNC / 4; ++g) {
-              const int y0 = __shfl_sync(0xffffffffu, my, 4 * g), y1 = __shfl_sync(0xffffffffu, my, 4 * g + 1);
-              const int y2 = __shfl_sync(0xffffffffu, my, 4 * g + 2), y3 = __shfl_sync(0xffffffffu, my, 4 * g + 3);
-              if (lane == 0) {
-#pragma unroll
-                for (int v = 0; v < 2; ++v)
-#pragma unroll
-                  for (int qc = 0; qc < 2; ++qc)
-                    tma_gather4_2d(pv_chunk(st, kh, v, qc) + 4 * g * 128, &tma_kv, &s.pv_full[st],
-                                   64 * (4 * v + pv_chunk0 + qc), y0, y1, y2, y3);
-              }
-            }
-          }
-          if (lane == 0) trace(i, 1);
-          issued = i + 1;
-        }
-        if (lane == 0 && issued < ntiles && issued > 0)
-          mbar_wait(&s.pv_full[(issued - 1) % STAGES], ((issued - 1) / STAGES) & 1, nullptr, 0, nullptr,
-                    1000000ull);
-      }
-    } else {
-    // Warp pw gathers tile keys pw, pw + 4, ... (lane j holds the id of key pw + 4j).
-    const int nkeys = (BN - pw + kPvWarps - 1) / kPvWarps;
-    auto key_id = [&](int i) { return lane < nkeys ? load_id(k_begin + i * BN + pw + kPvWarps * lane) : -1; };
+    const int peer_half = 1 - int(crank);   // key half of the peer's keys
+    // Warp pw gathers the peer's keys pw, pw + 4, ... of each tile (lane j
+    // holds the id of key pw + 4j of that half), once QK is done with the
+    // chunks they land in.
+    const int nkeys = (BNC - pw + kPvWarps - 1) / kPvWarps;
+    auto key_id = [&](int i) {
+      return lane < nkeys ? load_id(k_begin + i * BN + BNC * peer_half + pw + kPvWarps * lane) : -1;
+    };
     int next_id = key_id(0);
     for (int i = 0; i < ntiles; ++i) {
       const int st = i % STAGES;
       const int my_id = next_id;
       next_id = key_id(i + 1);
-      if (!mbar_wait(&s.pv_empty[st], ((i / STAGES) & 1) ^ 1, err, kErrTimeoutSmemEmpty, abort_flag)) break;
+      if (!mbar_wait(&s.qk_done[st], (i / STAGES) & 1, err, kErrTimeoutSmemEmpty, abort_flag)) break;
       if (!(dbg & 1)) {
         const int v = lane >> 4, qc = (lane >> 3) & 1, u = lane & 7;
         const int src_unit = (4 * v + pv_chunk0 + qc) * 8 + u;
 #pragma unroll 2
         for (int k = 0; k < nkeys; ++k) {
-          const int r = pw + kPvWarps * k;
-          const int kh = r >> 5, rk = r & 31;
+          const int rk = pw + kPvWarps * k;
           const int id = __shfl_sync(0xffffffffu, my_id, k);
-          const uint32_t dst = pv_chunk(st, kh, v, qc) + rk * 128 + ((u ^ (rk & 7)) << 4);
+          const uint32_t dst = pv_region(st, peer_half, v) + qc * kKeyChunkBytes + rk * 128 + ((u ^ (rk & 7)) << 4);
           cp_async16_zfill(dst, id >= 0 ? kv_rows + int64_t(id) * (D * 2) + src_unit * 16 : kv_rows, id >= 0);
         }
       }
@@ -445,7 +414,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (pw == 0 && lane == 0) trace(i, 1);
     }
     cp_async_wait_all();
-    }
   } else if (warp >= kMmaWarp) {
     regs_dec<kRegsOther>();
     if (warp != kMmaWarp) {
@@ -499,8 +467,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         commit_pair(smem_u32(&s.s_full[b]));
         commit_pair(peer(&s.s_full[b]));
-        commit_pair(smem_u32(&s.own_empty[st]));
-        commit_pair(peer(&s.own_empty[st]));
+        commit_pair(smem_u32(&s.qk_done[st]));
+        commit_pair(peer(&s.qk_done[st]));
         trace(i, 2);
       };
       auto issue_pv = [&](int i) {
@@ -513,14 +481,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             // Keys [16k, 16k+16): key half k/2, row offset 16 (k%2) in its region.
-            const uint64_t vdesc = umma_desc_sw128_mn(pv_chunk(st, k >> 1, v, 0) + (k & 1) * 16 * 128, kKeyChunkBytes);
+            const uint64_t vdesc = umma_desc_sw128_mn(pv_region(st, k >> 1, v) + (k & 1) * 16 * 128, kKeyChunkBytes);
             mma_pair_ss(tmem + v * 128, pdesc + ((k * 32) >> 4), vdesc, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
           }
         }
         commit_pair(smem_u32(&s.p_empty[b]));
         commit_pair(peer(&s.p_empty[b]));
-        commit_pair(smem_u32(&s.pv_empty[st]));
-        commit_pair(peer(&s.pv_empty[st]));
+        commit_pair(smem_u32(&s.own_empty[st]));
+        commit_pair(peer(&s.own_empty[st]));
         trace(i, 3);
       };
       int nq = 0, np = 0;
