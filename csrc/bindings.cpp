@@ -875,6 +875,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("epoch") = int64_t(0), py::arg("arrive_inc") = int64_t(0), py::arg("done_inc") = int64_t(0));
   m.def("set_fp8_gemm_pair_tiles", &b200::set_fp8_gemm_pair_tiles);
   m.def("set_decode_gemv", &b200::set_decode_gemv);
+  m.def("set_gemv_k_split", &b200::set_gemv_k_split);
   m.def("p2p_barrier", &p2p_barrier, py::arg("device"), py::arg("rank"), py::arg("world"), py::arg("call"),
         py::arg("flags"), py::arg("wait_ns") = int64_t(2000000000), py::arg("epoch") = int64_t(0));
   m.def("sparse_mla_2sm_trace", &sparse_mla_2sm_trace);

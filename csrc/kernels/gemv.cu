@@ -220,8 +220,17 @@ __global__ void __launch_bounds__(kGemvThreads) bf16_gemv_kernel(const __nv_bflo
 }
 
 // K split per row group: enough warps in flight to cover the weight stream's
-// latency on narrow layers (N / 2 warps alone leave most SMs idle), none on wide ones.
-int gemv_k_split(int N, int batch = 1) {
+// latency on narrow layers (N / 2 warps alone leave most SMs idle), none on
+// wide ones; rows of 16 KB or more split 8 ways, so that a warp's serial run
+// of steps stays short (measured on B200, one row, graph replays: o_proj
+// 7168 x 16384 38.9 -> 36.1 us, MLP down 7168 x 18432 41.1 -> 38.8 us;
+// wide layers with shorter rows, e.g. gate/up 36864 x 7168, are fastest
+// unsplit).
+int g_gemv_ks_override = 0;  // measurement hook: a fixed K split (0 = the heuristic)
+
+int gemv_k_split(int N, int batch = 1, int64_t row_bytes = 0) {
+  if (g_gemv_ks_override > 0) return g_gemv_ks_override;
+  if (row_bytes >= 16384) return kGemvWarps;
   const int want = sm_count() * 48;  // warps
   int ks = 1;
   while (ks < kGemvWarps && int64_t(N / kNR) * batch * ks < want) ks *= 2;
@@ -245,6 +254,11 @@ void dispatch_rows(int M, F&& f) {
 
 }  // namespace
 
+void set_gemv_k_split(int ks) {
+  if (ks != 0 && ks != 1 && ks != 2 && ks != 4 && ks != 8) throw std::invalid_argument("gemv K split: 0, 1, 2, 4 or 8");
+  g_gemv_ks_override = ks;
+}
+
 bool gemv_fits(int M, int K, int64_t lda_bytes, int64_t ldw_bytes, const void* a, const void* w) {
   const auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   return M >= 1 && M <= kGemvMaxRowsFp8 && K % 128 == 0 && lda_bytes % 16 == 0 && ldw_bytes % 16 == 0 && al(a) &&
@@ -252,7 +266,7 @@ bool gemv_fits(int M, int K, int64_t lda_bytes, int64_t ldw_bytes, const void* a
 }
 
 void launch_fp8_gemv(const FP8GemmArgs& a, cudaStream_t stream) {
-  const int ks = gemv_k_split(a.N);
+  const int ks = gemv_k_split(a.N, 1, a.K);  // FP8: one byte per element
   const int rows_per_cta = kNR * (kGemvWarps / ks);
   const int grid = (a.N + rows_per_cta - 1) / rows_per_cta;
   dispatch_rows(a.M, [&](auto mr) {

@@ -38,6 +38,7 @@ FP8GemmPlan plan_fp8_gemm(int M, int N, int K, int max_splits);
 void set_fp8_gemm_pair_tiles(bool enabled);
 // Decode-size FP8 / BF16 linears (<= kGemvMaxRows rows) on the GEMV (default on).
 void set_decode_gemv(bool enabled);
+void set_gemv_k_split(int ks);  // 0 = heuristic; 1/2/4/8 fixed (measurement)
 bool decode_gemv_enabled();
 // K splits launch_fp8_gemm uses for this shape (1 = no split-K reduce launch).
 int fp8_gemm_launch_splits(int M, int N, int K, int max_splits, bool ue8m0);

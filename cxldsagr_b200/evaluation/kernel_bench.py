@@ -193,6 +193,34 @@ def bench_gemm_paths(M=2048, **_):
     return {"op": "gemm_paths", "rows": rows}
 
 
+def bench_gemv_ksplit(**_):
+    """One-row GEMV of each V3.2 linear with the K split fixed at 1/2/4/8 warps
+    per row group (and the heuristic's choice), CUDA-graph replays."""
+    from ..config import v32_config
+
+    cfg = v32_config(1)
+    dev = "cuda"
+    shapes = {"fused_a": (cfg.q_lora_rank + 640 + cfg.index_head_dim, cfg.dim),
+              "fused_b": (cfg.n_heads * (cfg.qk_nope_head_dim + cfg.qk_rope_head_dim)
+                          + cfg.index_n_heads * cfg.index_head_dim, cfg.q_lora_rank),
+              "o_proj": (cfg.dim, cfg.n_heads * cfg.v_head_dim), "gate_up": (2 * cfg.intermediate_size, cfg.dim),
+              "down": (cfg.dim, cfg.intermediate_size)}
+    rows = []
+    for name, (N, K) in shapes.items():
+        w, s = quantize_weight_blocks(torch.randn(N, K, device=dev) * 0.02)
+        q, s_t = ops.quantize_act(torch.randn(1, K, device=dev).bfloat16())
+        out = torch.empty(1, N, device=dev, dtype=torch.bfloat16)
+        row = {"gemm": name, "N": N, "K": K}
+        for ks in (0, 1, 2, 4, 8):
+            ops.lib().set_gemv_k_split(ks)
+            try:
+                row[f"ks{ks}_us"] = round(time_fn(lambda: ops.fp8_gemm(q, s_t, w, s, out=out)) * 1e3, 2)
+            finally:
+                ops.lib().set_gemv_k_split(0)
+        rows.append(row)
+    return {"op": "gemv_ksplit", "graph": GRAPH, "rows": rows}
+
+
 def bench_decode_gemms(M=1, **_):
     """The projections of one DeepSeek-V3.2 layer and the LM head at decode row
     counts 1, 2, 4, 8 (up to ``M``): weight bytes streamed per call on the
@@ -362,7 +390,7 @@ def bench_copy_curve(**_):
 OPS = {"sparse_mla": bench_sparse_mla, "fp8_gemm": bench_fp8_gemm, "indexer": bench_indexer,
        "indexer_select": bench_indexer_select, "topk": bench_topk, "decode_gemms": bench_decode_gemms,
        "ag_gemm": bench_ag_gemm, "rs_gemm": bench_rs_gemm, "copy_curve": bench_copy_curve,
-       "gemm_paths": bench_gemm_paths}
+       "gemm_paths": bench_gemm_paths, "gemv_ksplit": bench_gemv_ksplit}
 
 
 def main():

@@ -27,7 +27,7 @@ def _fp8_gemm_launches(mod, args):
     q, w = args[0], args[2]
     ue8m0 = bool(args[6]) if len(args) > 6 else False
     return 2 if mod.fp8_gemm_splits(q.shape[0], w.shape[0], q.shape[1], ue8m0) > 1 else 1  # + split-K reduce
-_NO_LAUNCH = {"error_word", "sparse_mla_scratch_bytes", "fp8_gemm_splits", "set_decode_gemv", "set_pdl",
+_NO_LAUNCH = {"error_word", "sparse_mla_scratch_bytes", "fp8_gemm_splits", "set_decode_gemv", "set_gemv_k_split", "set_pdl",
               "pdl_enabled"}
 
 
