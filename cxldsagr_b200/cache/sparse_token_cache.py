@@ -252,11 +252,13 @@ class SparseTokenCache:
         if self._step_end is None or self.written + count > self._step_end:
             raise ValueError("append exceeds the open step")
         start = self.written
+        from .. import ops
+
         if self._pool is None:
-            return torch.arange(start, start + count, device=self.device)
+            return ops.arange_cached(start, start + count, device=self.device)
         if self.transient_start is not None:
             first = self.slots + 1 + start - self.transient_start
-            return torch.arange(first, first + count, device=self.device)
+            return ops.arange_cached(first, first + count, device=self.device)
         if count > self.slots:
             raise WorkingSetTooLarge("new KV batch exceeds the shared pool")
         with self.operation():

@@ -554,7 +554,7 @@ class DeepSeekV32Model:
         for c0 in range(0, T, chunk):
             c1 = min(T, c0 + chunk)
             pos = start + c0
-            positions = torch.arange(pos, start + c1, device=self.device, dtype=torch.float32)
+            positions = ops.arange_cached(pos, start + c1, device=self.device, dtype=torch.float32)
             pos_on = {self.device: positions}
             rows = par.token_range(c1 - c0)
             with scope("embedding"):

@@ -424,6 +424,34 @@ def gather_host_records(host, records, host_ids, slots, *, device_count=None, fp
     return records
 
 
+_ARANGE_CACHE: dict = {}
+_ARANGE_MAX_LEN, _ARANGE_MAX_ENTRIES = 256, 64
+
+
+def arange_cached(start: int, end: int, *, device, dtype=torch.int64):
+    """``torch.arange(start, end)`` for short CUDA ranges, kept on the device.
+
+    Decode and extend steps ask for the same small index ranges (token
+    positions, the rows a chunk's records go to) on every call; a captured
+    CUDA graph then reads the kept tensor instead of running an arange kernel
+    in each replay.  Callers must not write to the result.  Entries are never
+    freed (a graph may still read them), so at most 64 ranges of at most 256
+    elements are kept; other requests, and misses inside a stream capture,
+    get a fresh ``torch.arange``."""
+    device = torch.device(device)
+    if device.type != "cuda" or end - start > _ARANGE_MAX_LEN:
+        return torch.arange(start, end, device=device, dtype=dtype)
+    key = (device, start, end, dtype)
+    t = _ARANGE_CACHE.get(key)
+    if t is None:
+        if len(_ARANGE_CACHE) >= _ARANGE_MAX_ENTRIES or torch.cuda.is_current_stream_capturing():
+            return torch.arange(start, end, device=device, dtype=dtype)
+        t = torch.arange(start, end, device=device, dtype=dtype)
+        torch.cuda.current_stream(device).synchronize()  # ready for any stream that reads it later
+        _ARANGE_CACHE[key] = t
+    return t
+
+
 def l2_prefetch(t, nbytes: int | None = None):
     """Start pulling ``t`` (contiguous, not written while in flight) into L2; no-op off CUDA."""
     if _cuda(t):
