@@ -208,6 +208,22 @@ void index_q(const Tensor& q, int64_t ldq, int64_t T, int64_t H, int64_t D, int6
                        float(head_scale), ptr<float>(weights), stream());
 }
 
+// mla_q_rope(q, ...) and index_q(iq, ...) of one chunk in one launch.
+void q_rope_index_q(const Tensor& q, int64_t ldq, int64_t T, int64_t H, int64_t nope, int64_t rope, Tensor& out,
+                    int64_t ldo_tok, int64_t ldo_head, int64_t out_offset, const Tensor& iq, int64_t ldiq,
+                    int64_t IH, int64_t D, int64_t R, Tensor& q_q, Tensor& q_scale, const Tensor& w_raw,
+                    double head_scale, Tensor& weights, const Tensor& freqs, const Tensor& positions) {
+  CHECK_CUDA(q); CHECK_DTYPE(q, torch::kBFloat16); CHECK_DTYPE(out, torch::kBFloat16);
+  CHECK_DTYPE(iq, torch::kBFloat16); CHECK_DTYPE(q_q, torch::kFloat8_e4m3fn);
+  c10::cuda::CUDAGuard g(q.device());
+  TORCH_CHECK(w_raw.is_contiguous() && (w_raw.size(-1) == IH || w_raw.size(-1) == 2 * IH), "q_rope_index_q: w_raw");
+  b200::launch_q_rope_index_q(cptr<__nv_bfloat16>(q), ldq, T, H, nope, rope, ptr<__nv_bfloat16>(out), ldo_tok,
+                              ldo_head, out_offset, cptr<__nv_bfloat16>(iq), ldiq, IH, D, R, ptr<uint8_t>(q_q),
+                              ptr<float>(q_scale), cptr<float>(w_raw), w_raw.size(-1) == 2 * IH ? 1 : 0,
+                              float(head_scale), ptr<float>(weights), cptr<float>(freqs), cptr<float>(positions),
+                              stream());
+}
+
 void linear_f32(const Tensor& x, const Tensor& W, Tensor& out) {
   CHECK_CUDA(x); CHECK_DTYPE(x, torch::kBFloat16); CHECK_DTYPE(W, torch::kFloat32); CHECK_DTYPE(out, torch::kFloat32);
   CHECK_LAST_CONTIG(x); TORCH_CHECK(W.is_contiguous() && out.is_contiguous(), "linear_f32 layout");
@@ -835,6 +851,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("freqs"), py::arg("positions"), py::arg("out"), py::arg("dst_row"), py::arg("packed") = py::none());
   m.def("index_k", &index_k);
   m.def("index_q", &index_q);
+  m.def("q_rope_index_q", &q_rope_index_q);
   m.def("linear_f32", &linear_f32);
   m.def("l2_prefetch", &l2_prefetch, py::arg("t"), py::arg("bytes") = int64_t(-1));
   m.def("set_pdl", [](bool on) { b200::pdl_flag() = on; },

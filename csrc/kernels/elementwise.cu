@@ -257,15 +257,12 @@ __device__ __forceinline__ void rope_angle(const float* freqs, const float* posi
 }
 
 // One thread per (t, h, pair).  Interleaved pairs (2i, 2i+1).
-__global__ void mla_q_rope_kernel(const __nv_bfloat16* __restrict__ q, int64_t ldq, int T, int H,
-                                  int nope, int rope, const float* __restrict__ freqs,
-                                  const float* __restrict__ positions,
-                                  __nv_bfloat16* __restrict__ out, int64_t ldo_tok,
-                                  int64_t ldo_head, int out_offset) {
-  pdl_trigger();
-  pdl_wait();
+__device__ __forceinline__ void mla_q_rope_body(int64_t block, const __nv_bfloat16* __restrict__ q, int64_t ldq,
+                                                int T, int H, int nope, int rope, const float* __restrict__ freqs,
+                                                const float* __restrict__ positions, __nv_bfloat16* __restrict__ out,
+                                                int64_t ldo_tok, int64_t ldo_head, int out_offset) {
   const int half = rope / 2;
-  const int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
+  const int64_t idx = block * int64_t(blockDim.x) + threadIdx.x;
   if (idx >= int64_t(T) * H * half) return;
   const int i = idx % half;
   const int h = (idx / half) % H;
@@ -278,6 +275,16 @@ __global__ void mla_q_rope_kernel(const __nv_bfloat16* __restrict__ q, int64_t l
   __nv_bfloat16* dst = out + t * ldo_tok + h * ldo_head + out_offset;
   dst[2 * i] = __float2bfloat16_rn(a * c - b * s);
   dst[2 * i + 1] = __float2bfloat16_rn(b * c + a * s);
+}
+
+__global__ void mla_q_rope_kernel(const __nv_bfloat16* __restrict__ q, int64_t ldq, int T, int H,
+                                  int nope, int rope, const float* __restrict__ freqs,
+                                  const float* __restrict__ positions,
+                                  __nv_bfloat16* __restrict__ out, int64_t ldo_tok,
+                                  int64_t ldo_head, int out_offset) {
+  pdl_trigger();
+  pdl_wait();
+  mla_q_rope_body(blockIdx.x, q, ldq, T, H, nope, rope, freqs, positions, out, ldo_tok, ldo_head, out_offset);
 }
 
 // One CTA (128 threads) per token: RMSNorm of the latent, interleaved RoPE of k_pe.
@@ -421,14 +428,12 @@ __global__ void index_k_kernel(const __nv_bfloat16* __restrict__ k, int64_t ldk,
 }
 
 // One warp per (t, h).
-__global__ void index_q_kernel(const __nv_bfloat16* __restrict__ q, int64_t ldq, int T, int H,
-                               int D, int R, const float* __restrict__ freqs,
-                               const float* __restrict__ positions, uint8_t* __restrict__ q_q,
-                               float* __restrict__ q_scale, const float* __restrict__ w_raw,
-                               int w_split, float head_scale, float* __restrict__ weights) {
-  pdl_trigger();
-  pdl_wait();
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+__device__ __forceinline__ void index_q_body(int64_t block, const __nv_bfloat16* __restrict__ q, int64_t ldq, int T,
+                                             int H, int D, int R, const float* __restrict__ freqs,
+                                             const float* __restrict__ positions, uint8_t* __restrict__ q_q,
+                                             float* __restrict__ q_scale, const float* __restrict__ w_raw,
+                                             int w_split, float head_scale, float* __restrict__ weights) {
+  const int gw = int((block * blockDim.x + threadIdx.x) / 32);
   const int lane = threadIdx.x % 32;
   if (gw >= T * H) return;
   const int t = gw / H, h = gw % H;
@@ -456,6 +461,50 @@ __global__ void index_q_kernel(const __nv_bfloat16* __restrict__ q, int64_t ldq,
                               : w_raw[int64_t(t) * H + h];
     weights[t * H + h] = raw * head_scale * sc;
   }
+}
+
+__global__ void index_q_kernel(const __nv_bfloat16* __restrict__ q, int64_t ldq, int T, int H,
+                               int D, int R, const float* __restrict__ freqs,
+                               const float* __restrict__ positions, uint8_t* __restrict__ q_q,
+                               float* __restrict__ q_scale, const float* __restrict__ w_raw,
+                               int w_split, float head_scale, float* __restrict__ weights) {
+  pdl_trigger();
+  pdl_wait();
+  index_q_body(blockIdx.x, q, ldq, T, H, D, R, freqs, positions, q_q, q_scale, w_raw, w_split, head_scale, weights);
+}
+
+// The two query-side steps after the q_b projection in one launch (they read
+// the same projection output and write disjoint outputs): blocks [0, nrope)
+// rotate the MLA query's RoPE dims, the rest quantize the indexer query.
+struct QRopeArgs {
+  const __nv_bfloat16* q;
+  int64_t ldq;
+  int T, H, nope, rope;
+  __nv_bfloat16* out;
+  int64_t ldo_tok, ldo_head;
+  int out_offset;
+};
+struct IndexQArgs {
+  const __nv_bfloat16* q;
+  int64_t ldq;
+  int T, H, D, R;
+  uint8_t* q_q;
+  float* q_scale;
+  const float* w_raw;
+  int w_split;
+  float head_scale;
+  float* weights;
+};
+__global__ void q_rope_index_q_kernel(QRopeArgs r, IndexQArgs x, const float* __restrict__ freqs,
+                                      const float* __restrict__ positions, int nrope) {
+  pdl_trigger();
+  pdl_wait();
+  if (int(blockIdx.x) < nrope)
+    mla_q_rope_body(blockIdx.x, r.q, r.ldq, r.T, r.H, r.nope, r.rope, freqs, positions, r.out, r.ldo_tok, r.ldo_head,
+                    r.out_offset);
+  else
+    index_q_body(int64_t(blockIdx.x) - nrope, x.q, x.ldq, x.T, x.H, x.D, x.R, freqs, positions, x.q_q, x.q_scale,
+                 x.w_raw, x.w_split, x.head_scale, x.weights);
 }
 
 // ------------------------------------------------- FP32 head-weight linear
@@ -599,6 +648,22 @@ void launch_index_q(const __nv_bfloat16* q, int64_t ldq, int T, int H, int D, in
   const int64_t warps = int64_t(T) * H;
   launch_pdl(index_q_kernel, dim3((warps * 32 + 255) / 256), dim3(256), 0, stream, "index_q_kernel", q, ldq, T, H, D, R, freqs, positions, q_q, q_scale, w_raw, w_split, head_scale, weights);
   cuda_check(cudaGetLastError(), "index_q launch");
+}
+
+void launch_q_rope_index_q(const __nv_bfloat16* q, int64_t ldq, int T, int H, int nope, int rope,
+                           __nv_bfloat16* out, int64_t ldo_tok, int64_t ldo_head, int out_offset,
+                           const __nv_bfloat16* iq, int64_t ldiq, int IH, int D, int R, uint8_t* q_q, float* q_scale,
+                           const float* w_raw, int w_split, float head_scale, float* weights, const float* freqs,
+                           const float* positions, cudaStream_t stream) {
+  if (T <= 0) return;
+  if (D != 128) throw std::invalid_argument("index_q: head dim must be 128");
+  const int64_t nr = int64_t(T) * H * (rope / 2);
+  const int nrope = int((nr + 255) / 256);
+  const int nidx = int((int64_t(T) * IH * 32 + 255) / 256);
+  const QRopeArgs r{q, ldq, T, H, nope, rope, out, ldo_tok, ldo_head, out_offset};
+  const IndexQArgs x{iq, ldiq, T, IH, D, R, q_q, q_scale, w_raw, w_split, head_scale, weights};
+  launch_pdl(q_rope_index_q_kernel, dim3(nrope + nidx), dim3(256), 0, stream, "q_rope_index_q launch", r, x, freqs,
+             positions, nrope);
 }
 
 void launch_linear_f32(const __nv_bfloat16* x, int64_t ldx, const float* W, int T, int H, int K,

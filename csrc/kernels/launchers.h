@@ -220,6 +220,12 @@ void launch_linear_f32(const __nv_bfloat16* x, int64_t ldx, const float* W, int 
 
 // table holds rows [row0, row0 + rows) of a vocab_total-row table (shard
 // rows outside it embed as zeros).
+// mla_q_rope and index_q of the same chunk in one launch (same semantics as the two).
+void launch_q_rope_index_q(const __nv_bfloat16* q, int64_t ldq, int T, int H, int nope, int rope,
+                           __nv_bfloat16* out, int64_t ldo_tok, int64_t ldo_head, int out_offset,
+                           const __nv_bfloat16* iq, int64_t ldiq, int IH, int D, int R, uint8_t* q_q, float* q_scale,
+                           const float* w_raw, int w_split, float head_scale, float* weights, const float* freqs,
+                           const float* positions, cudaStream_t stream);
 // Bulk L2 prefetch of a read-only range (16-byte aligned start and size).
 void launch_l2_prefetch(const void* p, int64_t bytes, cudaStream_t stream);
 void launch_embed(const int64_t* ids, int T, const __nv_bfloat16* table, int64_t rows, int64_t row0,

@@ -127,14 +127,14 @@ class AttentionRunner:
         q_proj = torch.empty((T_loc, H, cfg.qk_head_dim), dtype=torch.bfloat16, device=normed.device)
         with scope("absorb"):
             ops.mla_absorb(b, H, nope, rope, w.wk_b_t, q_proj)
-        with scope("q_rope"):
-            ops.mla_q_rope(b, H, nope, rope, freqs, q_pos, q_proj, L)
         with scope("index_weights_f32"):
             w_raw = ops.linear_split(normed, w.index_head_split) if normed.is_cuda else ops.linear_f32(normed, w.index_head)
         iq = b[:, self.iq0:self.iq0 + self.iq_n]
-        with scope("index_q"):
-            q_idx, weights = ops.index_q(iq, cfg.index_n_heads, cfg.index_head_dim, rope, freqs, q_pos,
-                                         w_raw, self.head_scale)
+        with scope("q_rope_index_q"):
+            # MLA query RoPE and the indexer query (RoPE + FP8 + head weights): one launch.
+            q_idx, weights = ops.mla_q_rope_index_q(b, H, nope, rope, freqs, q_pos, q_proj, L, iq,
+                                                    cfg.index_n_heads, cfg.index_head_dim, rope, w_raw,
+                                                    self.head_scale)
         return q_proj, q_idx, weights
 
     # ---------------------------------------------------------------- forward

@@ -562,6 +562,20 @@ def index_q(iq, heads, dim, R, freqs, positions, w_raw, head_scale):
     return qq, w
 
 
+def mla_q_rope_index_q(b, H, nope, rope, freqs, positions, q_proj, latent, iq, heads, dim, R, w_raw, head_scale):
+    """:func:`mla_q_rope` then :func:`index_q` (returns its (q, weights)); one launch on CUDA."""
+    if not _cuda(b):
+        mla_q_rope(b, H, nope, rope, freqs, positions, q_proj, latent)
+        return index_q(iq, heads, dim, R, freqs, positions, w_raw, head_scale)
+    T = iq.shape[0]
+    qq = torch.empty((T, heads, dim), dtype=FP8, device=iq.device)
+    qs = torch.empty((T, heads), dtype=torch.float32, device=iq.device)
+    w = torch.empty((T, heads), dtype=torch.float32, device=iq.device)
+    lib().q_rope_index_q(b, b.stride(0), T, H, nope, rope, q_proj, q_proj.stride(0), q_proj.stride(1), latent,
+                         iq, iq.stride(0), heads, dim, R, qq, qs, w_raw.contiguous(), head_scale, w, freqs, positions)
+    return qq, w
+
+
 def mla_absorb(b, H, nope, rope, wk_b_t, q_proj):
     """q_proj[:, h, :L] = b_nope[:, h] @ wk_b_t[h]^T  (W_UK absorption, BF16 GEMM per head)."""
     T = q_proj.shape[0]

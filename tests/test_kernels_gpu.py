@@ -820,6 +820,30 @@ def test_decode_gemv_fp8(M, N, K):
     assert rel_err(got.float().cpu(), tiles.float().cpu()) < 1e-2
 
 
+def test_q_rope_index_q_fused_matches_separate():
+    """The one-launch MLA query RoPE + indexer query gives the bits of the two
+    separate kernels (decode and prefill row counts)."""
+    cfg = v32_config(1)
+    H, nope, rope, L = cfg.n_heads, cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.kv_lora_rank
+    IH, ID = cfg.index_n_heads, cfg.index_head_dim
+    freqs = torch.rand(rope // 2, device=DEV) * 0.1
+    for T in (1, 37, 300):
+        torch.manual_seed(46 + T)
+        b = torch.randn(T, H * (nope + rope) + IH * ID, device=DEV).bfloat16()
+        pos = torch.arange(1000, 1000 + T, device=DEV, dtype=torch.float32)
+        w_raw = torch.randn(T, 2 * IH, device=DEV)
+        iq = b[:, H * (nope + rope):]
+        q1 = torch.zeros(T, H, L + rope, device=DEV).bfloat16()
+        q2 = torch.zeros_like(q1)
+        ops.mla_q_rope(b, H, nope, rope, freqs, pos, q1, L)
+        qa, wa = ops.index_q(iq, IH, ID, rope, freqs, pos, w_raw, 0.01)
+        qb, wb = ops.mla_q_rope_index_q(b, H, nope, rope, freqs, pos, q2, L, iq, IH, ID, rope, w_raw, 0.01)
+        ops.check_errors(torch.device(DEV))
+        assert torch.equal(q1, q2)
+        assert torch.equal(qa.view(torch.uint8), qb.view(torch.uint8))
+        assert torch.equal(wa, wb)
+
+
 def test_l2_prefetch_leaves_data():
     """The bulk L2 prefetch runs on ragged sizes and changes nothing it touches."""
     x = torch.randint(0, 255, (3 * (1 << 16) + 48,), dtype=torch.uint8, device=DEV)

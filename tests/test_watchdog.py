@@ -30,6 +30,7 @@ def _reported(rank, world):
     wd = RankWatchdog.for_group(interval_s=0.1, timeout_s=5.0, prefix="t1")
     dist.barrier()
     wd.check()  # everyone healthy
+    dist.barrier()  # every rank has checked before rank 1 reports
     if rank == 1:
         try:
             raise ValueError("step failed on rank 1")
