@@ -197,6 +197,30 @@ void index_k(const Tensor& k, int64_t R, const Tensor& ln_w, const Tensor& ln_b,
                        float(eps), cptr<float>(freqs), cptr<float>(positions), ptr<uint8_t>(k_q), ptr<float>(k_scale), stream());
 }
 
+// kv_finish(kv, ...) and index_k(k, ...) of one chunk in one launch.
+void kv_finish_index_k(const Tensor& kv, int64_t L, int64_t R, const Tensor& norm_w, double eps, Tensor& out,
+                       const Tensor& dst_row, const c10::optional<Tensor>& packed, const Tensor& k, int64_t RK,
+                       const Tensor& ln_w, const Tensor& ln_b, double ln_eps, Tensor& k_q, Tensor& k_scale,
+                       const Tensor& freqs, const Tensor& positions) {
+  CHECK_CUDA(kv); CHECK_DTYPE(kv, torch::kBFloat16); CHECK_DTYPE(out, torch::kBFloat16); CHECK_LAST_CONTIG(kv);
+  CHECK_DTYPE(k, torch::kBFloat16); CHECK_DTYPE(k_q, torch::kFloat8_e4m3fn); CHECK_LAST_CONTIG(k);
+  CHECK_DTYPE(dst_row, torch::kInt64);
+  TORCH_CHECK(k.size(0) == kv.size(0), "kv_finish_index_k: kv and k rows differ");
+  c10::cuda::CUDAGuard g(kv.device());
+  uint8_t* pk = nullptr;
+  if (packed && packed->defined()) {
+    CHECK_DTYPE((*packed), torch::kUInt8);
+    TORCH_CHECK(packed->is_contiguous() && packed->dim() == 2 && packed->size(1) == 656 && packed->size(0) >= kv.size(0),
+                "kv_finish: packed records [>= T, 656] uint8");
+    pk = ptr<uint8_t>(*packed);
+  }
+  b200::launch_kv_finish_index_k(cptr<__nv_bfloat16>(kv), kv.stride(0), kv.size(0), L, R, cptr<float>(norm_w),
+                                 float(eps), ptr<__nv_bfloat16>(out), out.stride(0), cptr<int64_t>(dst_row),
+                                 out.size(0), err_ptr(kv), pk, cptr<__nv_bfloat16>(k), k.stride(0), k.size(1), RK,
+                                 cptr<float>(ln_w), cptr<float>(ln_b), float(ln_eps), ptr<uint8_t>(k_q),
+                                 ptr<float>(k_scale), cptr<float>(freqs), cptr<float>(positions), stream());
+}
+
 void index_q(const Tensor& q, int64_t ldq, int64_t T, int64_t H, int64_t D, int64_t R, const Tensor& freqs,
              const Tensor& positions, Tensor& q_q, Tensor& q_scale, const Tensor& w_raw, double head_scale,
              Tensor& weights) {
@@ -852,6 +876,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("index_k", &index_k);
   m.def("index_q", &index_q);
   m.def("q_rope_index_q", &q_rope_index_q);
+  m.def("kv_finish_index_k", &kv_finish_index_k);
   m.def("linear_f32", &linear_f32);
   m.def("l2_prefetch", &l2_prefetch, py::arg("t"), py::arg("bytes") = int64_t(-1));
   m.def("set_pdl", [](bool on) { b200::pdl_flag() = on; },

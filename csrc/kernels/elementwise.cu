@@ -295,18 +295,15 @@ __global__ void mla_q_rope_kernel(const __nv_bfloat16* __restrict__ q, int64_t l
 // row recalled from its packed form (dequant_kv_rows) is bitwise the resident
 // one.  packed[t] is the 656-byte record: 512 E4M3 bytes, 4 FP32 scales,
 // 64 BF16 RoPE values.
-__global__ void kv_finish_kernel(const __nv_bfloat16* __restrict__ kv, int64_t ldkv, int T, int L,
-                                 int R, const float* __restrict__ norm_w, float eps,
-                                 const float* __restrict__ freqs,
-                                 const float* __restrict__ positions,
-                                 __nv_bfloat16* __restrict__ out, int64_t ldo,
-                                 const int64_t* __restrict__ dst_row, int64_t out_rows,
-                                 uint8_t* __restrict__ packed, int* err) {
+__device__ __forceinline__ void kv_finish_body(int t, const __nv_bfloat16* __restrict__ kv, int64_t ldkv, int T,
+                                               int L, int R, const float* __restrict__ norm_w, float eps,
+                                               const float* __restrict__ freqs,
+                                               const float* __restrict__ positions,
+                                               __nv_bfloat16* __restrict__ out, int64_t ldo,
+                                               const int64_t* __restrict__ dst_row, int64_t out_rows,
+                                               uint8_t* __restrict__ packed, int* err) {
   __shared__ float red[4];
   __shared__ float bmax[4][4];
-  pdl_trigger();
-  pdl_wait();
-  const int t = blockIdx.x;
   const __nv_bfloat16* src = kv + t * ldkv;
   const int64_t drow = dst_row ? dst_row[t] : int64_t(t);
   if (drow < 0 || drow >= out_rows) {  // never write outside the record table
@@ -372,19 +369,30 @@ __global__ void kv_finish_kernel(const __nv_bfloat16* __restrict__ kv, int64_t l
   }
 }
 
-// One warp per token (D = 128: 4 elements per lane).
-__global__ void index_k_kernel(const __nv_bfloat16* __restrict__ k, int64_t ldk, int T, int D,
-                               int R, const float* __restrict__ ln_w,
-                               const float* __restrict__ ln_b, float eps,
-                               const float* __restrict__ freqs,
-                               const float* __restrict__ positions, uint8_t* __restrict__ k_q,
-                               float* __restrict__ k_scale) {
+__global__ void kv_finish_kernel(const __nv_bfloat16* __restrict__ kv, int64_t ldkv, int T, int L,
+                                 int R, const float* __restrict__ norm_w, float eps,
+                                 const float* __restrict__ freqs,
+                                 const float* __restrict__ positions,
+                                 __nv_bfloat16* __restrict__ out, int64_t ldo,
+                                 const int64_t* __restrict__ dst_row, int64_t out_rows,
+                                 uint8_t* __restrict__ packed, int* err) {
   pdl_trigger();
   pdl_wait();
-  const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  kv_finish_body(blockIdx.x, kv, ldkv, T, L, R, norm_w, eps, freqs, positions, out, ldo, dst_row, out_rows, packed,
+                 err);
+}
+
+// One warp per token (D = 128: 4 elements per lane).
+__device__ __forceinline__ void index_k_body(int64_t block, const __nv_bfloat16* __restrict__ k, int64_t ldk, int T,
+                                             int D, int R, const float* __restrict__ ln_w,
+                                             const float* __restrict__ ln_b, float eps,
+                                             const float* __restrict__ freqs,
+                                             const float* __restrict__ positions, uint8_t* __restrict__ k_q,
+                                             float* __restrict__ k_scale) {
+  __shared__ float buf[8][128];  // one row per warp (up to 8 warps)
+  const int t = int((block * blockDim.x + threadIdx.x) / 32);
   const int lane = threadIdx.x % 32;
   if (t >= T) return;
-  __shared__ float buf[8][128];
   float* row = buf[threadIdx.x / 32];
   const __nv_bfloat16* src = k + t * ldk;
   float v[4];
@@ -425,6 +433,56 @@ __global__ void index_k_kernel(const __nv_bfloat16* __restrict__ k, int64_t ldk,
   }
   const float sc = quant_group_warp(out, k_q + int64_t(t) * D);
   if (lane == 0) k_scale[t] = sc;
+}
+
+__global__ void index_k_kernel(const __nv_bfloat16* __restrict__ k, int64_t ldk, int T, int D,
+                               int R, const float* __restrict__ ln_w,
+                               const float* __restrict__ ln_b, float eps,
+                               const float* __restrict__ freqs,
+                               const float* __restrict__ positions, uint8_t* __restrict__ k_q,
+                               float* __restrict__ k_scale) {
+  pdl_trigger();
+  pdl_wait();
+  index_k_body(blockIdx.x, k, ldk, T, D, R, ln_w, ln_b, eps, freqs, positions, k_q, k_scale);
+}
+
+// The two key-side steps after the fused_a projection in one launch (128
+// threads): blocks [0, T) finish the KV records, the rest (four tokens each)
+// build the indexer keys.
+struct KvFinishArgs {
+  const __nv_bfloat16* kv;
+  int64_t ldkv;
+  int L, R;
+  const float* norm_w;
+  float eps;
+  __nv_bfloat16* out;
+  int64_t ldo;
+  const int64_t* dst_row;
+  int64_t out_rows;
+  uint8_t* packed;
+  int* err;
+};
+struct IndexKArgs {
+  const __nv_bfloat16* k;
+  int64_t ldk;
+  int D, R;
+  const float* ln_w;
+  const float* ln_b;
+  float eps;
+  uint8_t* k_q;
+  float* k_scale;
+};
+__global__ void __launch_bounds__(128) kv_finish_index_k_kernel(KvFinishArgs a, IndexKArgs b,
+                                                                const float* __restrict__ freqs,
+                                                                const float* __restrict__ positions, int T) {
+  pdl_trigger();
+  pdl_wait();
+  if (int(blockIdx.x) < T)
+    kv_finish_body(blockIdx.x, a.kv, a.ldkv, T, a.L, a.R, a.norm_w, a.eps, freqs, positions, a.out, a.ldo, a.dst_row,
+                   a.out_rows, a.packed, a.err);
+  else
+    index_k_body(int64_t(blockIdx.x) - T, b.k, b.ldk, T, b.D, b.R, b.ln_w, b.ln_b, b.eps, freqs, positions, b.k_q,
+                 b.k_scale);
 }
 
 // One warp per (t, h).
@@ -638,6 +696,20 @@ void launch_index_k(const __nv_bfloat16* k, int64_t ldk, int T, int D, int R,
   if (D != 128) throw std::invalid_argument("index_k: head dim must be 128");
   launch_pdl(index_k_kernel, dim3((T + 7) / 8), dim3(256), 0, stream, "index_k_kernel", k, ldk, T, D, R, ln_w, ln_b, eps, freqs, positions, k_q, k_scale);
   cuda_check(cudaGetLastError(), "index_k launch");
+}
+
+void launch_kv_finish_index_k(const __nv_bfloat16* kv, int64_t ldkv, int T, int L, int R, const float* norm_w,
+                              float eps, __nv_bfloat16* out, int64_t ldo, const int64_t* dst_row, int64_t out_rows,
+                              int* err, uint8_t* packed, const __nv_bfloat16* k, int64_t ldk, int D, int RK,
+                              const float* ln_w, const float* ln_b, float ln_eps, uint8_t* k_q, float* k_scale,
+                              const float* freqs, const float* positions, cudaStream_t stream) {
+  if (T <= 0) return;
+  if (packed && (L != 512 || R != 64)) throw std::invalid_argument("kv_finish: FP8 records need L = 512, R = 64");
+  if (D != 128) throw std::invalid_argument("index_k: head dim must be 128");
+  const KvFinishArgs a{kv, ldkv, L, R, norm_w, eps, out, ldo, dst_row, out_rows, packed, err};
+  const IndexKArgs b{k, ldk, D, RK, ln_w, ln_b, ln_eps, k_q, k_scale};
+  launch_pdl(kv_finish_index_k_kernel, dim3(T + (T + 3) / 4), dim3(128), 0, stream, "kv_finish_index_k launch", a, b,
+             freqs, positions, T);
 }
 
 void launch_index_q(const __nv_bfloat16* q, int64_t ldq, int T, int H, int D, int R,

@@ -220,6 +220,12 @@ void launch_linear_f32(const __nv_bfloat16* x, int64_t ldx, const float* W, int 
 
 // table holds rows [row0, row0 + rows) of a vocab_total-row table (shard
 // rows outside it embed as zeros).
+// kv_finish and index_k of the same chunk in one launch (same semantics as the two).
+void launch_kv_finish_index_k(const __nv_bfloat16* kv, int64_t ldkv, int T, int L, int R, const float* norm_w,
+                              float eps, __nv_bfloat16* out, int64_t ldo, const int64_t* dst_row, int64_t out_rows,
+                              int* err, uint8_t* packed, const __nv_bfloat16* k, int64_t ldk, int D, int RK,
+                              const float* ln_w, const float* ln_b, float ln_eps, uint8_t* k_q, float* k_scale,
+                              const float* freqs, const float* positions, cudaStream_t stream);
 // mla_q_rope and index_q of the same chunk in one launch (same semantics as the two).
 void launch_q_rope_index_q(const __nv_bfloat16* q, int64_t ldq, int T, int H, int nope, int rope,
                            __nv_bfloat16* out, int64_t ldo_tok, int64_t ldo_head, int out_offset,

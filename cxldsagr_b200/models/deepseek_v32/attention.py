@@ -105,18 +105,18 @@ class AttentionRunner:
             with scope("slots"):
                 dst = state.kv.destination_rows(T)
             packed = state.kv.packed_rows(T)  # FP8 caches: the 656-byte records of this chunk
+            k_rows, s_rows = state.index.rows(pos, T)
             with scope("finish"):
-                ops.kv_finish(kv, L, rope, w.kv_norm, cfg.norm_eps, freqs, positions, state.kv.records, dst,
-                              packed=packed)
+                # KV records and the indexer keys of the chunk: one launch.
+                ops.kv_finish_index_k(kv, L, rope, w.kv_norm, cfg.norm_eps, freqs, positions, state.kv.records, dst,
+                                      ik, w.index_norm_w, w.index_norm_b, cfg.norm_eps, k_rows, s_rows,
+                                      packed=packed)
             with scope("host_write"):
                 state.kv.finish_append(dst, packed)
             state.last_rows = dst
             if state.dense is not None:
                 # The staged history plus this chunk's records (logical row = staged row).
                 state.dense[pos:pos + T] = state.kv.records[dst]
-        with scope("index_k"):
-            k_rows, s_rows = state.index.rows(pos, T)
-            ops.index_k(ik, rope, w.index_norm_w, w.index_norm_b, cfg.norm_eps, freqs, positions, k_rows, s_rows)
         if T_loc == 0:
             return None, None, None
         q_pos = positions[r0:r1]

@@ -543,6 +543,17 @@ def index_k(ik, R, ln_w, ln_b, eps, freqs, positions, k_out, s_out):
     lib().index_k(ik, R, ln_w, ln_b, eps, freqs, positions, k_out, s_out)
 
 
+def kv_finish_index_k(kv, L, R, norm_w, eps, freqs, positions, records, rows, ik, ln_w, ln_b, ln_eps, k_out, s_out,
+                      *, packed=None):
+    """:func:`kv_finish` then :func:`index_k` (both read the fused_a output); one launch on CUDA."""
+    if not _cuda(kv):
+        kv_finish(kv, L, R, norm_w, eps, freqs, positions, records, rows, packed=packed)
+        index_k(ik, R, ln_w, ln_b, ln_eps, freqs, positions, k_out, s_out)
+        return
+    lib().kv_finish_index_k(kv, L, R, norm_w, eps, records, rows.long(), packed, ik, R, ln_w, ln_b, ln_eps, k_out,
+                            s_out, freqs, positions)
+
+
 def index_q(iq, heads, dim, R, freqs, positions, w_raw, head_scale):
     """Indexer query: split-half RoPE + per-head UE8M0 FP8; weights = raw * head_scale * q_scale.
 

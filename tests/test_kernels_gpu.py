@@ -820,6 +820,39 @@ def test_decode_gemv_fp8(M, N, K):
     assert rel_err(got.float().cpu(), tiles.float().cpu()) < 1e-2
 
 
+@pytest.mark.parametrize("fp8", [False, True])
+def test_kv_finish_index_k_fused_matches_separate(fp8):
+    """The one-launch KV record finish + indexer key gives the bits of the two
+    separate kernels (BF16 and FP8 records, decode and prefill row counts)."""
+    cfg = v32_config(1)
+    L, R = cfg.kv_lora_rank, cfg.qk_rope_head_dim
+    freqs = torch.rand(R // 2, device=DEV) * 0.1
+    nw = torch.rand(L, device=DEV) + 0.5
+    lw, lb = torch.rand(128, device=DEV) + 0.5, torch.randn(128, device=DEV) * 0.1
+    for T in (1, 5, 300):
+        torch.manual_seed(47 + T)
+        a = torch.randn(T, 2304, device=DEV).bfloat16()
+        kv, ik = a[:, 1536:1536 + L + R], a[:, 1536 + L + R:1536 + L + R + 128]
+        pos = torch.arange(2000, 2000 + T, device=DEV, dtype=torch.float32)
+        rows = torch.randperm(512, device=DEV)[:T]
+        outs = []
+        for fused in (False, True):
+            rec = torch.zeros(512, L + R, device=DEV).bfloat16()
+            packed = torch.zeros(T, 656, dtype=torch.uint8, device=DEV) if fp8 else None
+            kq = torch.zeros(T, 128, device=DEV).to(torch.float8_e4m3fn)
+            ks = torch.zeros(T, device=DEV)
+            if fused:
+                ops.kv_finish_index_k(kv, L, R, nw, 1e-6, freqs, pos, rec, rows, ik, lw, lb, 1e-6, kq, ks,
+                                      packed=packed)
+            else:
+                ops.kv_finish(kv, L, R, nw, 1e-6, freqs, pos, rec, rows, packed=packed)
+                ops.index_k(ik, R, lw, lb, 1e-6, freqs, pos, kq, ks)
+            outs.append((rec, packed, kq.view(torch.uint8), ks))
+        ops.check_errors(torch.device(DEV))
+        for x, y in zip(outs[0], outs[1]):
+            assert (x is None and y is None) or torch.equal(x, y)
+
+
 def test_q_rope_index_q_fused_matches_separate():
     """The one-launch MLA query RoPE + indexer query gives the bits of the two
     separate kernels (decode and prefill row counts)."""
